@@ -1,0 +1,403 @@
+// speculative.h and medusa.h over the fl_engine (include/speculative.h,
+// include/medusa.h state the rules; the reference declares the functions in
+// fast_llm/include/speculative.h:78-185 and medusa.h:84-229 without
+// defining them).
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "fl_common.cuh"
+#include "fl_runtime.h"
+#include "medusa.h"
+#include "speculative.h"
+
+using namespace fl;
+
+namespace {
+
+// Hidden extension of draft_tree_t: the vocabulary size recorded by
+// draft_tokens so verify_tokens can walk [(K+1), vocab] logits.
+struct TreeImpl {
+    draft_tree_t pub;
+    int vocab;
+};
+
+struct CacheImpl {
+    draft_kv_cache_t pub;
+    int num_heads, head_dim;
+};
+
+std::mutex g_bind_mu;
+std::map<const void*, fl_engine_t*> g_bind;  // draft / Medusa model -> engine
+
+void bind(const void* m, fl_engine_t* e) {
+    std::lock_guard<std::mutex> lk(g_bind_mu);
+    g_bind[m] = e;
+}
+fl_engine_t* bound(const void* m) {
+    std::lock_guard<std::mutex> lk(g_bind_mu);
+    auto it = g_bind.find(m);
+    return it == g_bind.end() ? nullptr : it->second;
+}
+void unbind(const void* m) {
+    std::lock_guard<std::mutex> lk(g_bind_mu);
+    g_bind.erase(m);
+}
+
+bool parse_synthetic(const char* path, uint64_t* seed) {
+    if (!path || strncmp(path, "synthetic:", 10) != 0) return false;
+    char* end = nullptr;
+    unsigned long long v = strtoull(path + 10, &end, 10);
+    if (!end || *end != '\0' || end == path + 10) return false;
+    *seed = v;
+    return true;
+}
+
+void free_tensor_array(dequantized_tensor_t* arr, int n) {
+    if (!arr) return;
+    for (int i = 0; i < n; i++) {
+        release_tensor(&arr[i]);
+        free(arr[i].weights);
+        free(arr[i].scales);
+        free(arr[i].scales_f16);
+    }
+    free(arr);
+}
+
+int synth_tensor(dequantized_tensor_t* t, uint64_t seed, uint32_t id, int rows, int cols) {
+    release_tensor(t);
+    free(t->weights);
+    free(t->scales);
+    free(t->scales_f16);
+    t->weights = (int8_t*)malloc((size_t)rows * cols);
+    t->scales_f16 = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)rows * (cols / 32));
+    t->scales = nullptr;
+    if (!t->weights || !t->scales_f16) return set_error(FL_E_NOMEM, "synthetic tensor: host allocation");
+    t->rows = rows;
+    t->cols = cols;
+    t->original_bits = 4;
+    t->scale_block = 32;
+    return fl_synth_q4_0_i8(seed, id, rows, cols, 0.02f, t->weights, t->scales_f16);
+}
+
+// Pushes a draft model's host tensors into the engine's draft stack.
+int load_draft_into(fl_engine_t* e, const draft_model_t* dm) {
+    const dequantized_tensor_t* arrs[7] = {dm->w_q_proj, dm->w_k_proj, dm->w_v_proj, dm->w_o_proj,
+                                           dm->w_gate, dm->w_up, dm->w_down};
+    for (int l = 0; l < dm->num_layers; l++)
+        for (int p = 0; p < 7; p++) {
+            const dequantized_tensor_t* t = arrs[p] ? &arrs[p][l] : nullptr;
+            if (!t || !t->weights) continue;  // keep what the engine holds
+            if (t->scale_block != 32 || !t->scales_f16)
+                return set_error(FL_E_UNSUPPORTED, "draft tensors must be in block mode (scale_block 32)");
+            FL_CHECK(fl_engine_load_linear(e, 1, l, p, t->weights, t->scales_f16, t->rows, t->cols));
+        }
+    const dequantized_tensor_t* lm = dm->w_lm_head;
+    if (lm && lm->weights) {
+        if (lm->scale_block != 32 || !lm->scales_f16)
+            return set_error(FL_E_UNSUPPORTED, "LM head must be in block mode (scale_block 32)");
+        FL_CHECK(fl_engine_load_linear(e, 3, 0, 1, lm->weights, lm->scales_f16, lm->rows, lm->cols));
+    }
+    return FL_OK;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ speculative.h
+
+FL_API draft_model_t* draft_model_create(int num_layers, int hidden_size, int intermediate_size, int vocab_size) {
+    if (num_layers <= 0 || hidden_size <= 0 || intermediate_size <= 0 || vocab_size <= 0) return nullptr;
+    draft_model_t* m = (draft_model_t*)calloc(1, sizeof(draft_model_t));
+    if (!m) return nullptr;
+    m->num_layers = num_layers;
+    m->hidden_size = hidden_size;
+    m->intermediate_size = intermediate_size;
+    m->vocab_size = vocab_size;
+    dequantized_tensor_t** arrs[7] = {&m->w_q_proj, &m->w_k_proj, &m->w_v_proj, &m->w_o_proj,
+                                      &m->w_gate, &m->w_up, &m->w_down};
+    for (auto a : arrs) {
+        *a = (dequantized_tensor_t*)calloc(num_layers, sizeof(dequantized_tensor_t));
+        if (!*a) { draft_model_free(m); return nullptr; }
+    }
+    m->w_lm_head = (dequantized_tensor_t*)calloc(1, sizeof(dequantized_tensor_t));
+    if (!m->w_lm_head) { draft_model_free(m); return nullptr; }
+    return m;
+}
+
+FL_API int draft_model_load(draft_model_t* m, const char* path) {
+    uint64_t seed = 0;
+    if (!m || !parse_synthetic(path, &seed)) {
+        set_error(FL_E_UNSUPPORTED, "draft_model_load: only \"synthetic:<seed>\" sources are supported");
+        return -1;
+    }
+    const int d = m->hidden_size, F = m->intermediate_size;
+    const int shapes[7][2] = {{d, d}, {d, d}, {d, d}, {d, d}, {F, d}, {F, d}, {d, F}};
+    dequantized_tensor_t* arrs[7] = {m->w_q_proj, m->w_k_proj, m->w_v_proj, m->w_o_proj, m->w_gate, m->w_up, m->w_down};
+    for (int l = 0; l < m->num_layers; l++)
+        for (int p = 0; p < 7; p++)
+            if (synth_tensor(&arrs[p][l], seed, FL_TENSOR_ID(1, l, p), shapes[p][0], shapes[p][1]) != FL_OK) return -1;
+    if (synth_tensor(m->w_lm_head, seed, FL_TENSOR_ID(3, 0, 1), m->vocab_size, d) != FL_OK) return -1;
+    return 0;
+}
+
+FL_API void draft_model_free(draft_model_t* m) {
+    if (!m) return;
+    unbind(m);
+    free_tensor_array(m->w_q_proj, m->num_layers);
+    free_tensor_array(m->w_k_proj, m->num_layers);
+    free_tensor_array(m->w_v_proj, m->num_layers);
+    free_tensor_array(m->w_o_proj, m->num_layers);
+    free_tensor_array(m->w_gate, m->num_layers);
+    free_tensor_array(m->w_up, m->num_layers);
+    free_tensor_array(m->w_down, m->num_layers);
+    free_tensor_array(m->w_lm_head, 1);
+    free(m);
+}
+
+FL_API draft_kv_cache_t* draft_kv_cache_create(int max_len, int num_heads, int head_dim) {
+    if (max_len <= 0 || num_heads <= 0 || head_dim <= 0) return nullptr;
+    CacheImpl* c = (CacheImpl*)calloc(1, sizeof(CacheImpl));
+    if (!c) return nullptr;
+    c->pub.max_len = max_len;
+    c->num_heads = num_heads;
+    c->head_dim = head_dim;
+    return &c->pub;
+}
+
+FL_API void draft_kv_cache_reset(draft_kv_cache_t* c) {
+    if (c) c->cache_len = 0;
+}
+
+FL_API void draft_kv_cache_free(draft_kv_cache_t* c) { free(c); }
+
+FL_API draft_tree_t* draft_tree_create(int max_tokens) {
+    if (max_tokens <= 0) return nullptr;
+    TreeImpl* t = (TreeImpl*)calloc(1, sizeof(TreeImpl));
+    if (!t) return nullptr;
+    t->pub.tokens = (int*)calloc(max_tokens, sizeof(int));
+    t->pub.probs = (float*)calloc(max_tokens, sizeof(float));
+    t->pub.max_tokens = max_tokens;
+    if (!t->pub.tokens || !t->pub.probs) {
+        free(t->pub.tokens);
+        free(t->pub.probs);
+        free(t);
+        return nullptr;
+    }
+    return &t->pub;
+}
+
+FL_API void draft_tree_free(draft_tree_t* t) {
+    if (!t) return;
+    free(t->tokens);
+    free(t->probs);
+    free(t);
+}
+
+// Sets the vocabulary a tree's logits rows use (trees from draft_tree_create).
+FL_API int fl_draft_tree_set_vocab(draft_tree_t* t, int vocab) {
+    if (!t || vocab <= 0) return set_error(FL_E_INVAL, "tree/vocab");
+    ((TreeImpl*)t)->vocab = vocab;
+    return FL_OK;
+}
+
+FL_API int verify_tokens(const float* target_hidden, const draft_tree_t* tree, int* accepted_tokens,
+                         int* num_accepted, const speculative_config_t* config) {
+    if (!target_hidden || !tree || !accepted_tokens || !num_accepted || !config) return -1;
+    const int V = ((const TreeImpl*)tree)->vocab;
+    if (V <= 0) {
+        set_error(FL_E_STATE, "verify_tokens: tree vocabulary unknown (draft_tokens or fl_draft_tree_set_vocab)");
+        return -1;
+    }
+    if (config->temperature > 0.0f) {
+        set_error(FL_E_UNSUPPORTED, "verify_tokens: host rejection sampling needs the draft distributions; "
+                                    "use the engine's sampled decode");
+        return -1;
+    }
+    const int K = tree->num_tokens;
+    const int cap = config->max_accepted < 0 ? K : (config->max_accepted < K ? config->max_accepted : K);
+    auto argmax = [&](int r) {
+        const float* l = target_hidden + (size_t)r * V;
+        int bi = 0;
+        for (int i = 1; i < V; i++)
+            if (l[i] > l[bi]) bi = i;
+        return bi;
+    };
+    int a = 0;
+    while (a < cap && tree->tokens[a] == argmax(a)) {
+        accepted_tokens[a] = tree->tokens[a];
+        a++;
+    }
+    accepted_tokens[a] = argmax(a);
+    *num_accepted = a;
+    return a;
+}
+
+FL_API int draft_tokens(draft_model_t* model, draft_kv_cache_t* cache, const float* hidden_state, int current_token,
+                        draft_tree_t* tree, const speculative_config_t* config) {
+    if (!model || !cache || !hidden_state || !tree || !config) return -1;
+    fl_engine_t* e = bound(model);
+    if (!e) {
+        set_error(FL_E_STATE, "draft_tokens: draft not bound to an engine (speculative_generate or fl_engine_bind_draft)");
+        return -1;
+    }
+    const int K = config->num_draft_tokens < tree->max_tokens ? config->num_draft_tokens : tree->max_tokens;
+    if (K <= 0) return -1;
+    if (fl_engine_draft_chain(e, hidden_state, current_token, cache->cache_len, K, tree->tokens, tree->probs) != FL_OK)
+        return -1;
+    tree->num_tokens = K;
+    ((TreeImpl*)tree)->vocab = model->vocab_size;
+    cache->cache_len += 1;
+    return K;
+}
+
+FL_API int fl_engine_bind_draft(fl_engine_t* e, draft_model_t* dm) {
+    if (!e || !dm) return set_error(FL_E_INVAL, "bind_draft: NULL");
+    FL_CHECK(load_draft_into(e, dm));
+    bind(dm, e);
+    return FL_OK;
+}
+
+FL_API int speculative_decode_step(draft_model_t* draft, draft_kv_cache_t* draft_cache, void* target_model,
+                                   void (*target_forward)(void*, const float*, float*, int),
+                                   const float* current_hidden, int current_token, int* output_tokens,
+                                   int* num_output, const speculative_config_t* config) {
+    if (!draft || !draft_cache || !target_model || !current_hidden || !output_tokens || !num_output || !config)
+        return -1;
+    if (target_forward != fl_cuda_target_forward) {
+        set_error(FL_E_UNSUPPORTED, "speculative_decode_step: target_forward must be fl_cuda_target_forward");
+        return -1;
+    }
+    fl_engine_t* e = (fl_engine_t*)target_model;
+    if (!bound(draft) && fl_engine_bind_draft(e, draft) != FL_OK) return -1;
+    const int K = config->num_draft_tokens;
+    if (K <= 0 || K > 7) return -1;
+    draft_tree_t* tree = draft_tree_create(K);
+    if (!tree) return -1;
+    const int pos0 = fl_engine_position(e);
+    int rc = draft_tokens(draft, draft_cache, current_hidden, current_token, tree, config);
+    if (rc < 0) { draft_tree_free(tree); return -1; }
+    std::vector<float> in(K + 1), logits((size_t)(K + 1) * draft->vocab_size);
+    in[0] = (float)current_token;
+    for (int i = 0; i < K; i++) in[i + 1] = (float)tree->tokens[i];
+    target_forward(target_model, in.data(), logits.data(), K + 1);
+    if (fl_engine_position(e) != pos0 + K + 1) { draft_tree_free(tree); return -1; }
+    speculative_config_t greedy = *config;
+    greedy.temperature = 0.0f;
+    int a = 0;
+    rc = verify_tokens(logits.data(), tree, output_tokens, &a, &greedy);
+    draft_tree_free(tree);
+    if (rc < 0) return -1;
+    // keep the verified prefix in the base cache; the bonus token is next
+    if (fl_engine_set_position(e, pos0 + a + 1) != FL_OK) return -1;
+    draft_cache->cache_len = pos0 + a + 1;
+    *num_output = a + 1;
+    return a + 1;
+}
+
+FL_API int speculative_generate(draft_model_t* draft, void* target_model,
+                                void (*target_forward)(void*, const float*, float*, int), const float* prompt_hidden,
+                                int prompt_len, int* output_tokens, int num_tokens, const speculative_config_t* config) {
+    if (!draft || !target_model || !prompt_hidden || !output_tokens || !config || prompt_len <= 0 || num_tokens <= 0)
+        return -1;
+    if (target_forward != fl_cuda_target_forward) {
+        set_error(FL_E_UNSUPPORTED, "speculative_generate: target_forward must be fl_cuda_target_forward");
+        return -1;
+    }
+    if (config->temperature > 0.0f) {
+        set_error(FL_E_UNSUPPORTED, "speculative_generate: sampled acceptance runs through fl_engine_spec_sample");
+        return -1;
+    }
+    fl_engine_t* e = (fl_engine_t*)target_model;
+    if (fl_engine_bind_draft(e, draft) != FL_OK) return -1;
+    std::vector<int> prompt(prompt_len);
+    for (int i = 0; i < prompt_len; i++) prompt[i] = (int)prompt_hidden[i];
+    const int K = config->num_draft_tokens;
+    if (fl_engine_spec_generate(e, prompt.data(), prompt_len, num_tokens, K, config->max_accepted, output_tokens,
+                                nullptr, nullptr) != FL_OK)
+        return -1;
+    return num_tokens;
+}
+
+// ------------------------------------------------------------------ medusa.h
+
+FL_API medusa_model_t* medusa_model_create(int num_heads, int hidden_size, int vocab_size) {
+    if (num_heads <= 0 || hidden_size <= 0 || vocab_size <= 0) return nullptr;
+    medusa_model_t* m = (medusa_model_t*)calloc(1, sizeof(medusa_model_t));
+    if (!m) return nullptr;
+    m->heads = (medusa_head_t*)calloc(num_heads, sizeof(medusa_head_t));
+    if (!m->heads) { free(m); return nullptr; }
+    m->num_heads = num_heads;
+    m->hidden_size = hidden_size;
+    m->vocab_size = vocab_size;
+    for (int h = 0; h < num_heads; h++) {
+        m->heads[h].head_id = h;
+        m->heads[h].hidden_size = hidden_size;
+        m->heads[h].vocab_size = vocab_size;
+        m->heads[h].weights = (dequantized_tensor_t*)calloc(1, sizeof(dequantized_tensor_t));
+    }
+    return m;
+}
+
+FL_API int medusa_model_load(medusa_model_t* m, const char* path) {
+    uint64_t seed = 0;
+    if (!m || !parse_synthetic(path, &seed)) {
+        set_error(FL_E_UNSUPPORTED, "medusa_model_load: only \"synthetic:<seed>\" sources are supported");
+        return -1;
+    }
+    for (int h = 0; h < m->num_heads; h++)
+        if (!m->heads[h].weights ||
+            synth_tensor(m->heads[h].weights, seed, FL_TENSOR_ID(2, h, 0), m->hidden_size, m->hidden_size) != FL_OK)
+            return -1;
+    return 0;
+}
+
+FL_API void medusa_model_free(medusa_model_t* m) {
+    if (!m) return;
+    unbind(m);
+    for (int h = 0; h < m->num_heads; h++) {
+        free_tensor_array(m->heads[h].weights, 1);
+        free(m->heads[h].bias);
+    }
+    free(m->heads);
+    free(m);
+}
+
+FL_API medusa_tree_t* medusa_tree_create(int max_candidates) {
+    if (max_candidates <= 0) return nullptr;
+    medusa_tree_t* t = (medusa_tree_t*)calloc(1, sizeof(medusa_tree_t));
+    if (!t) return nullptr;
+    t->tokens = (int*)calloc(max_candidates, sizeof(int));
+    t->probs = (float*)calloc(max_candidates, sizeof(float));
+    t->parent_indices = (int*)calloc(max_candidates, sizeof(int));
+    t->positions = (int*)calloc(max_candidates, sizeof(int));
+    t->max_candidates = max_candidates;
+    if (!t->tokens || !t->probs || !t->parent_indices || !t->positions) {
+        medusa_tree_free(t);
+        return nullptr;
+    }
+    return t;
+}
+
+FL_API void medusa_tree_free(medusa_tree_t* t) {
+    if (!t) return;
+    free(t->tokens);
+    free(t->probs);
+    free(t->parent_indices);
+    free(t->positions);
+    free(t);
+}
+
+// The draft + Medusa combination (reference medusa.h:210-229) has no caller in
+// the reference and is not part of this library's decode paths.
+FL_API int speculative_medusa_generate(void*, void (*)(void*, const float*, float*, int), medusa_model_t*, void*,
+                                       void (*)(void*, const int*, int, float*, int), const float*, int, int*, int,
+                                       const medusa_config_t*) {
+    set_error(FL_E_UNSUPPORTED, "speculative_medusa_generate is not provided (use speculative_generate or "
+                                "medusa_generate)");
+    return -1;
+}

@@ -1,0 +1,793 @@
+// fl_engine: the base model, draft and Medusa heads resident in HBM, paged
+// fp16 KV caches, and the speculative decode loop (include/fl_cuda.h).
+//
+// Layer chain (per stack, per layer; inference.c:250-399 restated):
+//   act_quant(RMSNorm(x))           -> xq      [rows, d]   u8
+//   GEMV qkv  (EPI_QKV)             -> q f32 + K/V fp16 pages (RoPE fused)
+//   attention (tree/causal mask)    -> aq      [rows, qd]  u8
+//   GEMV o    (EPI_RESID)           -> x += o
+//   act_quant(RMSNorm(x))           -> xq
+//   GEMV gate/up interleaved (EPI_SWIGLU) -> hq [rows, F] u8
+//   GEMV down (EPI_RESID)           -> x += down
+// One speculative step is captured once as a CUDA graph whose kernels read
+// positions from the device-resident SpecState, and replayed.
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <algorithm>
+#include <string>
+#include <vector>
+
+#include "fl_common.cuh"
+#include "fl_kernels.h"
+#include "fl_runtime.h"
+#include "fl_state.h"
+
+using namespace fl;
+
+namespace {
+
+struct Linear {
+    int8_t* w = nullptr;
+    __half* s = nullptr;
+    int N = 0, K = 0;
+    unsigned need = 0, have = 0;  // bit masks of the source tensors loaded
+};
+
+struct LayerW {
+    Linear qkv, o, gu, down;
+};
+
+struct Stack {
+    int nl = 0;
+    std::vector<LayerW> L;
+    std::vector<KvLayer> kv;
+    int* block_table = nullptr;
+    int pages = 0;
+};
+
+}  // namespace
+
+struct fl_engine {
+    fl_model_config_t c;
+    int device = 0;
+    cudaStream_t s = nullptr;
+    int d = 0, qd = 0, kd = 0, F = 0, V = 0, hd = 0, H = 0, Hkv = 0;
+    float* embed = nullptr;
+    bool embed_loaded = false;
+    Linear lm;
+    Stack base, draft;
+    std::vector<Linear> medusa;
+    // work buffers for up to R rows
+    int R = 0;
+    float* x = nullptr;      // [R, d]
+    float* x2 = nullptr;     // [R, d]
+    uint8_t* xq = nullptr;   // [R, max(d, qd)]
+    float* q = nullptr;      // [R, qd]
+    uint8_t* aq = nullptr;   // [R, qd]
+    uint8_t* hq = nullptr;   // [R, F]
+    float* logits = nullptr; // [kMaxRows, V]
+    unsigned long long* amax = nullptr;  // [kMaxRows, nparts]
+    int nparts = 0;
+    float* x_v = nullptr;    // [kMaxRows, d]
+    float* x_d = nullptr;    // [kMaxRows, d]
+    int* iota = nullptr;     // [R + 16]: iota[i] = i (positions and slot scalars)
+    int* tok = nullptr;      // [R]
+    uint8_t* mask = nullptr; // [R * R] bounded by kMaxRows^2 for tests
+    int mask_cap = 0;
+    // speculative state
+    SpecState* st = nullptr;
+    SpecState* st_snap = nullptr;
+    float* xd0_snap = nullptr;
+    int* seq = nullptr;
+    int* out = nullptr;
+    int* acc = nullptr;
+    int spec_K = 0, spec_P = 0, spec_ready = 0;
+    cudaGraphExec_t step_exec = nullptr;
+    int graph_K = -1;
+    cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+    double t_draft_us = 0, t_verify_us = 0, t_total_us = 0;
+    int cb_pos = 0;               // callback API: base cache length
+    float* last_feat = nullptr;   // [d] base feature of the last appended token
+};
+
+namespace {
+
+int alloc_linear(Linear& l, int N, int K, unsigned need) {
+    l.N = N;
+    l.K = K;
+    l.need = need;
+    l.have = 0;
+    FL_CHECK_CUDA(cudaMalloc(&l.w, (size_t)N * K));
+    FL_CHECK_CUDA(cudaMalloc(&l.s, (size_t)N * (K / 32) * sizeof(__half)));
+    return FL_OK;
+}
+
+void free_linear(Linear& l) {
+    cudaFree(l.w);
+    cudaFree(l.s);
+    l.w = nullptr;
+    l.s = nullptr;
+}
+
+int alloc_stack(fl_engine* e, Stack& S, int nl) {
+    S.nl = nl;
+    S.L.resize(nl);
+    S.kv.resize(nl);
+    const int d = e->d, qd = e->qd, kd = e->kd, F = e->F;
+    S.pages = (e->c.max_seq_len + kPageSize - 1) / kPageSize;
+    for (int l = 0; l < nl; l++) {
+        LayerW& W = S.L[l];
+        FL_CHECK(alloc_linear(W.qkv, qd + 2 * kd, d, 0x7u));
+        FL_CHECK(alloc_linear(W.o, d, qd, 0x1u));
+        FL_CHECK(alloc_linear(W.gu, 2 * F, d, 0x3u));
+        FL_CHECK(alloc_linear(W.down, d, F, 0x1u));
+        const size_t kvb = (size_t)S.pages * e->Hkv * kPageSize * e->hd * sizeof(__half);
+        FL_CHECK_CUDA(cudaMalloc(&S.kv[l].k, kvb));
+        FL_CHECK_CUDA(cudaMalloc(&S.kv[l].v, kvb));
+        FL_CHECK_CUDA(cudaMemset(S.kv[l].k, 0, kvb));
+        FL_CHECK_CUDA(cudaMemset(S.kv[l].v, 0, kvb));
+    }
+    // One sequence: identity block table (pages are still addressed through it).
+    std::vector<int> bt(S.pages);
+    for (int i = 0; i < S.pages; i++) bt[i] = i;
+    FL_CHECK_CUDA(cudaMalloc(&S.block_table, sizeof(int) * S.pages));
+    FL_CHECK_CUDA(cudaMemcpy(S.block_table, bt.data(), sizeof(int) * S.pages, cudaMemcpyHostToDevice));
+    return FL_OK;
+}
+
+void free_stack(Stack& S) {
+    for (auto& W : S.L) {
+        free_linear(W.qkv);
+        free_linear(W.o);
+        free_linear(W.gu);
+        free_linear(W.down);
+    }
+    for (auto& kv : S.kv) {
+        cudaFree(kv.k);
+        cudaFree(kv.v);
+    }
+    cudaFree(S.block_table);
+    S.L.clear();
+    S.kv.clear();
+}
+
+// Copies `rows` rows of int8 weights / fp16 scales into a fused matrix at
+// destination row dst_row0 with a destination row stride of dst_stride rows
+// (stride 2 interleaves gate and up).
+int put_rows(Linear& l, int dst_row0, int dst_stride, const int8_t* w, const uint16_t* sc, int rows,
+             int cols, cudaStream_t s) {
+    if (cols != l.K) return set_error(FL_E_INVAL, "load_linear: column count does not match the model");
+    const size_t kb = (size_t)cols / 32;
+    FL_CHECK_CUDA(cudaMemcpy2DAsync(l.w + (size_t)dst_row0 * cols, (size_t)dst_stride * cols, w, cols, cols,
+                                    rows, cudaMemcpyHostToDevice, s));
+    FL_CHECK_CUDA(cudaMemcpy2DAsync(l.s + (size_t)dst_row0 * kb, (size_t)dst_stride * kb * sizeof(__half), sc,
+                                    kb * sizeof(__half), kb * sizeof(__half), rows, cudaMemcpyHostToDevice, s));
+    FL_CHECK_CUDA(cudaStreamSynchronize(s));
+    return FL_OK;
+}
+
+bool linear_ready(const Linear& l) { return l.w && (l.have & l.need) == l.need; }
+
+bool stack_ready(const Stack& S) {
+    for (const auto& W : S.L)
+        if (!linear_ready(W.qkv) || !linear_ready(W.o) || !linear_ready(W.gu) || !linear_ready(W.down))
+            return false;
+    return true;
+}
+
+GemvParams gemv_base(const Linear& l, const uint8_t* aq, const int* done) {
+    GemvParams g = {};
+    g.aq = aq;
+    g.w = l.w;
+    g.sblk = l.s;
+    g.N = l.N;
+    g.K = l.K;
+    g.done = done;
+    return g;
+}
+
+int launch_chunks(GemvParams g, int epi, int M, const int* dyn_M, cudaStream_t s, bool pdl) {
+    if (dyn_M) {
+        g.dyn_M = dyn_M;
+        g.row0 = 0;
+        g.M = kMaxRows;
+        FL_CHECK_CUDA(launch_gemv(g, epi, false, false, s, pdl));
+        return FL_OK;
+    }
+    for (int r0 = 0; r0 < M; r0 += kMaxRows) {
+        g.row0 = r0;
+        g.M = std::min(kMaxRows, M - r0);
+        FL_CHECK_CUDA(launch_gemv(g, epi, false, false, s, pdl));
+    }
+    return FL_OK;
+}
+
+int act_quant(fl_engine* e, const float* x, uint8_t* q, int K, int M, const int* dyn_M, int norm,
+              const int* done, bool pdl) {
+    ActQuantParams a = {};
+    a.x = x;
+    a.q = q;
+    a.K = K;
+    a.M = M;
+    a.dyn_M = dyn_M;
+    a.norm = norm;
+    a.eps = e->c.norm_eps;
+    a.done = done;
+    FL_CHECK_CUDA(launch_act_quant(a, e->s, pdl));
+    return FL_OK;
+}
+
+// Runs M rows (M <= R; dyn_M bounds the live rows when set, M <= kMaxRows)
+// through a stack. slot_base / pos are device pointers.
+int run_stack(fl_engine* e, Stack& S, float* x, int M, const int* dyn_M, const int* slot_base, const int* pos,
+              const uint8_t* mask, const int* done, bool pdl) {
+    const int d = e->d, qd = e->qd, F = e->F;
+    for (int l = 0; l < S.nl; l++) {
+        LayerW& W = S.L[l];
+        FL_CHECK(act_quant(e, x, e->xq, d, M, dyn_M, 1, done, pdl));
+        GemvParams g = gemv_base(W.qkv, e->xq, done);
+        g.q_out = e->q;
+        g.kv = S.kv[l];
+        g.block_table = S.block_table;
+        g.slot_base = slot_base;
+        g.pos = pos;
+        g.q_dim = qd;
+        g.kv_dim = e->kd;
+        g.head_dim = e->hd;
+        g.kv_heads = e->Hkv;
+        g.theta = e->c.rope_theta;
+        FL_CHECK(launch_chunks(g, EPI_QKV, M, dyn_M, e->s, pdl));
+        AttnParams at = {};
+        at.q = e->q;
+        at.kv = S.kv[l];
+        at.block_table = S.block_table;
+        at.slot_base = slot_base;
+        at.M = M;
+        at.dyn_M = dyn_M;
+        at.mask = mask;
+        at.heads = e->H;
+        at.kv_heads = e->Hkv;
+        at.head_dim = e->hd;
+        at.max_ctx = e->c.max_seq_len;
+        at.out_q = e->aq;
+        at.done = done;
+        FL_CHECK_CUDA(launch_attention(at, e->s, pdl));
+        g = gemv_base(W.o, e->aq, done);
+        g.out = x;
+        g.ldo = d;
+        FL_CHECK(launch_chunks(g, EPI_RESID, M, dyn_M, e->s, pdl));
+        FL_CHECK(act_quant(e, x, e->xq, d, M, dyn_M, 1, done, pdl));
+        g = gemv_base(W.gu, e->xq, done);
+        g.hq = e->hq;
+        g.F = F;
+        FL_CHECK(launch_chunks(g, EPI_SWIGLU, M, dyn_M, e->s, pdl));
+        g = gemv_base(W.down, e->hq, done);
+        g.out = x;
+        g.ldo = d;
+        FL_CHECK(launch_chunks(g, EPI_RESID, M, dyn_M, e->s, pdl));
+    }
+    return FL_OK;
+}
+
+// LM head over rows of x (M <= kMaxRows): logits [M, V] and argmax partials.
+int run_lm(fl_engine* e, const float* x, int M, const int* dyn_src_row, const int* done, bool pdl) {
+    ActQuantParams a = {};
+    a.x = x;
+    a.q = e->xq;
+    a.K = e->d;
+    a.M = M;
+    a.norm = 1;
+    a.eps = e->c.norm_eps;
+    a.done = done;
+    a.dyn_src_row = dyn_src_row;
+    FL_CHECK_CUDA(launch_act_quant(a, e->s, pdl));
+    GemvParams g = gemv_base(e->lm, e->xq, done);
+    g.out = e->logits;
+    g.ldo = e->V;
+    g.amax_part = e->amax;
+    g.M = M;
+    g.row0 = 0;
+    FL_CHECK_CUDA(launch_gemv(g, EPI_LOGITS, false, false, e->s, pdl));
+    return FL_OK;
+}
+
+int ensure_mask(fl_engine* e, int M) {
+    if (e->mask_cap >= M * M) return FL_OK;
+    cudaFree(e->mask);
+    e->mask = nullptr;
+    FL_CHECK_CUDA(cudaMalloc(&e->mask, (size_t)M * M));
+    e->mask_cap = M * M;
+    return FL_OK;
+}
+
+StepBuffers step_buffers(fl_engine* e) {
+    StepBuffers b;
+    b.st = e->st;
+    b.seq = e->seq;
+    b.out = e->out;
+    b.acc_hist = e->acc;
+    b.embed = e->embed;
+    b.x_d = e->x_d;
+    b.x_v = e->x_v;
+    b.amax_part = e->amax;
+    b.nparts = e->nparts;
+    b.d = e->d;
+    return b;
+}
+
+int check_ready(fl_engine* e, bool need_draft) {
+    if (!e) return set_error(FL_E_INVAL, "engine is NULL");
+    if (!fl_engine_ready(e)) return set_error(FL_E_STATE, "engine weights not fully loaded");
+    if (need_draft && e->c.draft_layers <= 0) return set_error(FL_E_STATE, "engine has no draft model");
+    FL_CHECK_CUDA(cudaSetDevice(e->device));
+    return FL_OK;
+}
+
+// Records one speculative step (include/speculative.h rule) on e->s.
+int record_step(fl_engine* e, bool pdl) {
+    const int K = e->spec_K;
+    SpecState* st = e->st;
+    const int* done = &st->done;
+    StepBuffers b = step_buffers(e);
+    for (int j = 1; j < K; j++) {
+        FL_CHECK(run_stack(e, e->draft, e->x_d, 1, &st->one, &st->draft_base, st->draft_pos, nullptr, done, pdl));
+        FL_CHECK(run_lm(e, e->x_d, 1, nullptr, done, pdl));
+        FL_CHECK_CUDA(launch_draft_pick(b, j, e->s, pdl));
+    }
+    FL_CHECK_CUDA(launch_verify_prep(b, K, e->s, pdl));
+    FL_CHECK(run_stack(e, e->base, e->x_v, K + 1, nullptr, &st->verify_base, st->verify_pos, nullptr, done, pdl));
+    FL_CHECK(run_lm(e, e->x_v, K + 1, nullptr, done, pdl));
+    FL_CHECK_CUDA(launch_accept(b, K, e->s, pdl));
+    FL_CHECK_CUDA(launch_catchup_prep(b, K, e->s, pdl));
+    FL_CHECK(run_stack(e, e->draft, e->x_d, K + 1, &st->rows, &st->draft_base, st->draft_pos, nullptr, done, pdl));
+    FL_CHECK(run_lm(e, e->x_d, 1, &st->last_row, done, pdl));
+    FL_CHECK_CUDA(launch_draft_pick(b, 0, e->s, pdl));
+    return FL_OK;
+}
+
+int build_step_graph(fl_engine* e) {
+    if (e->step_exec && e->graph_K == e->spec_K) return FL_OK;
+    if (e->step_exec) {
+        cudaGraphExecDestroy(e->step_exec);
+        e->step_exec = nullptr;
+    }
+    cudaGraph_t g = nullptr;
+    FL_CHECK_CUDA(cudaStreamBeginCapture(e->s, cudaStreamCaptureModeThreadLocal));
+    int rc = record_step(e, true);
+    cudaError_t ce = cudaStreamEndCapture(e->s, &g);
+    if (rc != FL_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    FL_CHECK_CUDA(ce);
+    ce = cudaGraphInstantiate(&e->step_exec, g, 0);
+    cudaGraphDestroy(g);
+    FL_CHECK_CUDA(ce);
+    e->graph_K = e->spec_K;
+    return FL_OK;
+}
+
+int prefill_base(fl_engine* e, const int* prompt, int P) {
+    FL_CHECK_CUDA(cudaMemcpyAsync(e->seq, prompt, sizeof(int) * P, cudaMemcpyHostToDevice, e->s));
+    FL_CHECK_CUDA(launch_embed_rows(e->embed, e->V, e->seq, nullptr, 0, e->x, e->d, P, nullptr, nullptr, e->s, false));
+    FL_CHECK(run_stack(e, e->base, e->x, P, nullptr, e->iota, e->iota, nullptr, nullptr, false));
+    // next token from the last row
+    FL_CHECK_CUDA(cudaMemcpyAsync(e->x_v, e->x + (size_t)(P - 1) * e->d, sizeof(float) * e->d,
+                                  cudaMemcpyDeviceToDevice, e->s));
+    FL_CHECK(run_lm(e, e->x_v, 1, nullptr, nullptr, false));
+    FL_CHECK_CUDA(launch_argmax_rows(e->amax, e->nparts, 1, e->seq + P, nullptr, e->s));
+    return FL_OK;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+
+FL_API fl_engine_t* fl_engine_create(const fl_model_config_t* cfg, int device) {
+    if (!cfg) { set_error(FL_E_INVAL, "config is NULL"); return nullptr; }
+    const fl_model_config_t& c = *cfg;
+    if (c.hidden_size <= 0 || c.num_heads <= 0 || c.num_kv_heads <= 0 || c.head_dim <= 0 ||
+        c.num_heads % c.num_kv_heads != 0 || c.hidden_size % 32 != 0 || c.intermediate_size % 32 != 0 ||
+        (c.num_heads * c.head_dim) % 32 != 0 || c.head_dim % 2 != 0 || c.head_dim > 128 ||
+        c.vocab_size <= 0 || c.num_layers <= 0 || c.max_seq_len < 16 || c.draft_layers < 0 || c.medusa_heads < 0) {
+        set_error(FL_E_INVAL, "fl_engine_create: unsupported model configuration");
+        return nullptr;
+    }
+    if (ensure_device() != FL_OK) return nullptr;
+    if (cudaSetDevice(device) != cudaSuccess) { set_error(FL_E_NODEV, "cudaSetDevice failed"); return nullptr; }
+    fl_engine* e = new fl_engine();
+    e->c = c;
+    e->device = device;
+    e->d = c.hidden_size;
+    e->H = c.num_heads;
+    e->Hkv = c.num_kv_heads;
+    e->hd = c.head_dim;
+    e->qd = c.num_heads * c.head_dim;
+    e->kd = c.num_kv_heads * c.head_dim;
+    e->F = c.intermediate_size;
+    e->V = c.vocab_size;
+    e->R = c.max_seq_len;
+    auto fail = [&](int) -> fl_engine_t* { fl_engine_destroy(e); return nullptr; };
+    if (cudaStreamCreateWithFlags(&e->s, cudaStreamNonBlocking) != cudaSuccess) return fail(set_error(FL_E_CUDA, "stream"));
+    for (auto& ev : e->ev)
+        if (cudaEventCreate(&ev) != cudaSuccess) return fail(set_error(FL_E_CUDA, "event"));
+    if (alloc_stack(e, e->base, c.num_layers) != FL_OK) return fail(0);
+    if (c.draft_layers > 0 && alloc_stack(e, e->draft, c.draft_layers) != FL_OK) return fail(0);
+    if (alloc_linear(e->lm, e->V, e->d, 0x1u) != FL_OK) return fail(0);
+    e->medusa.resize(c.medusa_heads);
+    for (auto& m : e->medusa)
+        if (alloc_linear(m, e->d, e->d, 0x1u) != FL_OK) return fail(0);
+    const size_t R = e->R, d = e->d;
+    const size_t wq = std::max(e->d, e->qd);
+    e->nparts = gemv_grid(e->V);
+    bool ok = cudaMalloc(&e->embed, sizeof(float) * (size_t)e->V * d) == cudaSuccess &&
+              cudaMalloc(&e->x, sizeof(float) * R * d) == cudaSuccess &&
+              cudaMalloc(&e->x2, sizeof(float) * R * d) == cudaSuccess &&
+              cudaMalloc(&e->xq, R * wq) == cudaSuccess &&
+              cudaMalloc(&e->q, sizeof(float) * R * e->qd) == cudaSuccess &&
+              cudaMalloc(&e->aq, R * e->qd) == cudaSuccess &&
+              cudaMalloc(&e->hq, R * e->F) == cudaSuccess &&
+              cudaMalloc(&e->logits, sizeof(float) * kMaxRows * e->V) == cudaSuccess &&
+              cudaMalloc(&e->amax, sizeof(unsigned long long) * kMaxRows * e->nparts) == cudaSuccess &&
+              cudaMalloc(&e->x_v, sizeof(float) * kMaxRows * d) == cudaSuccess &&
+              cudaMalloc(&e->x_d, sizeof(float) * kMaxRows * d) == cudaSuccess &&
+              cudaMalloc(&e->iota, sizeof(int) * (R + 16)) == cudaSuccess &&
+              cudaMalloc(&e->tok, sizeof(int) * R) == cudaSuccess &&
+              cudaMalloc(&e->st, sizeof(SpecState)) == cudaSuccess &&
+              cudaMalloc(&e->st_snap, sizeof(SpecState)) == cudaSuccess &&
+              cudaMalloc(&e->xd0_snap, sizeof(float) * d) == cudaSuccess &&
+              cudaMalloc(&e->seq, sizeof(int) * (R + 16)) == cudaSuccess &&
+              cudaMalloc(&e->out, sizeof(int) * (R + 16)) == cudaSuccess &&
+              cudaMalloc(&e->acc, sizeof(int) * (R + 16)) == cudaSuccess &&
+              cudaMalloc(&e->last_feat, sizeof(float) * d) == cudaSuccess;
+    if (!ok) return fail(set_error(FL_E_NOMEM, "fl_engine_create: device allocation failed"));
+    std::vector<int> io(R + 16);
+    for (size_t i = 0; i < io.size(); i++) io[i] = (int)i;
+    if (cudaMemcpy(e->iota, io.data(), sizeof(int) * io.size(), cudaMemcpyHostToDevice) != cudaSuccess)
+        return fail(set_error(FL_E_CUDA, "iota upload"));
+    return e;
+}
+
+FL_API void fl_engine_destroy(fl_engine_t* e) {
+    if (!e) return;
+    cudaSetDevice(e->device);
+    if (e->s) cudaStreamSynchronize(e->s);
+    if (e->step_exec) cudaGraphExecDestroy(e->step_exec);
+    free_stack(e->base);
+    free_stack(e->draft);
+    free_linear(e->lm);
+    for (auto& m : e->medusa) free_linear(m);
+    void* bufs[] = {e->embed, e->x, e->x2, e->xq, e->q, e->aq, e->hq, e->logits, e->amax, e->x_v, e->x_d,
+                    e->iota, e->tok, e->mask, e->st, e->st_snap, e->xd0_snap, e->seq, e->out, e->acc,
+                    e->last_feat};
+    for (void* p : bufs) cudaFree(p);
+    for (auto& ev : e->ev)
+        if (ev) cudaEventDestroy(ev);
+    if (e->s) cudaStreamDestroy(e->s);
+    delete e;
+}
+
+FL_API int fl_engine_load_linear(fl_engine_t* e, int stack, int layer, int proj, const int8_t* w,
+                                 const uint16_t* d, int rows, int cols) {
+    if (!e || !w || !d) return set_error(FL_E_INVAL, "load_linear: NULL argument");
+    FL_CHECK_CUDA(cudaSetDevice(e->device));
+    if (stack == 3) {
+        if (proj != 1 || rows != e->V) return set_error(FL_E_INVAL, "load_linear: shared stack takes the LM head (proj 1)");
+        FL_CHECK(put_rows(e->lm, 0, 1, w, d, rows, cols, e->s));
+        e->lm.have |= 1u;
+        return FL_OK;
+    }
+    if (stack == 2) {
+        if (layer < 0 || layer >= (int)e->medusa.size() || proj != 0 || rows != e->d)
+            return set_error(FL_E_INVAL, "load_linear: bad Medusa head");
+        FL_CHECK(put_rows(e->medusa[layer], 0, 1, w, d, rows, cols, e->s));
+        e->medusa[layer].have |= 1u;
+        return FL_OK;
+    }
+    if (stack != 0 && stack != 1) return set_error(FL_E_INVAL, "load_linear: bad stack");
+    Stack& S = stack == 0 ? e->base : e->draft;
+    if (layer < 0 || layer >= S.nl) return set_error(FL_E_INVAL, "load_linear: bad layer");
+    LayerW& W = S.L[layer];
+    switch (proj) {
+        case 0:
+            if (rows != e->qd) return set_error(FL_E_INVAL, "load_linear: q rows");
+            FL_CHECK(put_rows(W.qkv, 0, 1, w, d, rows, cols, e->s));
+            W.qkv.have |= 1u;
+            return FL_OK;
+        case 1:
+        case 2:
+            if (rows != e->kd) return set_error(FL_E_INVAL, "load_linear: k/v rows");
+            FL_CHECK(put_rows(W.qkv, e->qd + (proj == 2 ? e->kd : 0), 1, w, d, rows, cols, e->s));
+            W.qkv.have |= (proj == 1 ? 2u : 4u);
+            return FL_OK;
+        case 3:
+            if (rows != e->d) return set_error(FL_E_INVAL, "load_linear: o rows");
+            FL_CHECK(put_rows(W.o, 0, 1, w, d, rows, cols, e->s));
+            W.o.have |= 1u;
+            return FL_OK;
+        case 4:
+        case 5:
+            if (rows != e->F) return set_error(FL_E_INVAL, "load_linear: gate/up rows");
+            FL_CHECK(put_rows(W.gu, proj == 4 ? 0 : 1, 2, w, d, rows, cols, e->s));
+            W.gu.have |= (proj == 4 ? 1u : 2u);
+            return FL_OK;
+        case 6:
+            if (rows != e->d) return set_error(FL_E_INVAL, "load_linear: down rows");
+            FL_CHECK(put_rows(W.down, 0, 1, w, d, rows, cols, e->s));
+            W.down.have |= 1u;
+            return FL_OK;
+        default:
+            return set_error(FL_E_INVAL, "load_linear: bad projection");
+    }
+}
+
+FL_API int fl_engine_load_embedding(fl_engine_t* e, const float* table) {
+    if (!e || !table) return set_error(FL_E_INVAL, "load_embedding: NULL argument");
+    FL_CHECK_CUDA(cudaSetDevice(e->device));
+    FL_CHECK_CUDA(cudaMemcpy(e->embed, table, sizeof(float) * (size_t)e->V * e->d, cudaMemcpyHostToDevice));
+    e->embed_loaded = true;
+    return FL_OK;
+}
+
+FL_API int fl_engine_ready(const fl_engine_t* e) {
+    if (!e || !e->embed_loaded || !linear_ready(e->lm)) return 0;
+    if (!stack_ready(e->base) || !stack_ready(e->draft)) return 0;
+    for (const auto& m : e->medusa)
+        if (!linear_ready(m)) return 0;
+    return 1;
+}
+
+FL_API int fl_engine_synthesize(fl_engine_t* e, uint64_t seed) {
+    if (!e) return set_error(FL_E_INVAL, "engine is NULL");
+    const int d = e->d, qd = e->qd, kd = e->kd, F = e->F, V = e->V;
+    const size_t maxel = std::max({(size_t)V * d, (size_t)2 * F * d, (size_t)qd * d});
+    std::vector<int8_t> w(maxel);
+    std::vector<uint16_t> sc(maxel / 32);
+    const float stdv = 0.02f;
+    auto gen = [&](int stack, int layer, int proj, int rows, int cols) -> int {
+        int rc = fl_synth_q4_0_i8(seed, FL_TENSOR_ID(stack, layer, proj), rows, cols, stdv, w.data(), sc.data());
+        if (rc != FL_OK) return set_error(rc, "synth failed");
+        return fl_engine_load_linear(e, stack, layer, proj, w.data(), sc.data(), rows, cols);
+    };
+    for (int s = 0; s < 2; s++) {
+        const Stack& S = s == 0 ? e->base : e->draft;
+        for (int l = 0; l < S.nl; l++) {
+            FL_CHECK(gen(s, l, 0, qd, d));
+            FL_CHECK(gen(s, l, 1, kd, d));
+            FL_CHECK(gen(s, l, 2, kd, d));
+            FL_CHECK(gen(s, l, 3, d, qd));
+            FL_CHECK(gen(s, l, 4, F, d));
+            FL_CHECK(gen(s, l, 5, F, d));
+            FL_CHECK(gen(s, l, 6, d, F));
+        }
+    }
+    for (int h = 0; h < (int)e->medusa.size(); h++) FL_CHECK(gen(2, h, 0, d, d));
+    FL_CHECK(gen(3, 0, 1, V, d));
+    std::vector<float> emb((size_t)V * d);
+    FL_CHECK(fl_synth_q4_0_f32(seed, FL_TENSOR_ID(3, 0, 0), V, d, stdv, emb.data()));
+    return fl_engine_load_embedding(e, emb.data());
+}
+
+FL_API int fl_engine_forward_rows(fl_engine_t* e, int stack, const float* x_in, int M, int base, const int* pos,
+                                  const uint8_t* mask, float* x_out, float* logits) {
+    FL_CHECK(check_ready(e, stack == 1));
+    if (!x_in || !pos || M <= 0 || base < 0 || base + M > e->R) return set_error(FL_E_INVAL, "forward_rows: bad arguments");
+    if (stack != 0 && stack != 1) return set_error(FL_E_INVAL, "forward_rows: stack must be 0 or 1");
+    Stack& S = stack == 0 ? e->base : e->draft;
+    const size_t xb = sizeof(float) * (size_t)M * e->d;
+    FL_CHECK_CUDA(cudaMemcpyAsync(e->x, x_in, xb, cudaMemcpyHostToDevice, e->s));
+    FL_CHECK_CUDA(cudaMemcpyAsync(e->tok, pos, sizeof(int) * M, cudaMemcpyHostToDevice, e->s));
+    const uint8_t* dmask = nullptr;
+    if (mask) {
+        FL_CHECK(ensure_mask(e, M));
+        FL_CHECK_CUDA(cudaMemcpyAsync(e->mask, mask, (size_t)M * M, cudaMemcpyHostToDevice, e->s));
+        dmask = e->mask;
+    }
+    FL_CHECK(run_stack(e, S, e->x, M, nullptr, e->iota + base, e->tok, dmask, nullptr, false));
+    if (x_out) FL_CHECK_CUDA(cudaMemcpyAsync(x_out, e->x, xb, cudaMemcpyDeviceToHost, e->s));
+    if (logits) {
+        for (int r0 = 0; r0 < M; r0 += kMaxRows) {
+            const int m = std::min(kMaxRows, M - r0);
+            FL_CHECK(run_lm(e, e->x + (size_t)r0 * e->d, m, nullptr, nullptr, false));
+            FL_CHECK_CUDA(cudaMemcpyAsync(logits + (size_t)r0 * e->V, e->logits, sizeof(float) * (size_t)m * e->V,
+                                          cudaMemcpyDeviceToHost, e->s));
+        }
+    }
+    FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
+    return FL_OK;
+}
+
+FL_API int fl_engine_greedy_generate(fl_engine_t* e, const int* prompt, int P, int n_new, int* out) {
+    FL_CHECK(check_ready(e, false));
+    if (!prompt || !out || P <= 0 || n_new <= 0 || P + n_new + 1 > e->R)
+        return set_error(FL_E_INVAL, "greedy_generate: bad arguments or context too long");
+    FL_CHECK(prefill_base(e, prompt, P));
+    for (int i = 1; i < n_new; i++) {
+        const int n = P + i - 1;  // seq[n] is the newest token
+        FL_CHECK_CUDA(launch_embed_rows(e->embed, e->V, e->seq + n, nullptr, 0, e->x_v, e->d, 1, nullptr, nullptr, e->s, false));
+        FL_CHECK(run_stack(e, e->base, e->x_v, 1, nullptr, e->iota + n, e->iota + n, nullptr, nullptr, false));
+        FL_CHECK(run_lm(e, e->x_v, 1, nullptr, nullptr, false));
+        FL_CHECK_CUDA(launch_argmax_rows(e->amax, e->nparts, 1, e->seq + n + 1, nullptr, e->s));
+    }
+    FL_CHECK_CUDA(cudaMemcpyAsync(out, e->seq + P, sizeof(int) * n_new, cudaMemcpyDeviceToHost, e->s));
+    FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
+    return FL_OK;
+}
+
+FL_API int fl_engine_spec_prefill(fl_engine_t* e, const int* prompt, int P, int K, int max_acc) {
+    FL_CHECK(check_ready(e, true));
+    if (!prompt || P <= 0 || K < 1 || K > kMaxDraft || P + 2 > e->R)
+        return set_error(FL_E_INVAL, "spec_prefill: bad arguments (1 <= K <= 7)");
+    e->spec_ready = 0;
+    e->spec_K = K;
+    e->spec_P = P;
+    FL_CHECK(prefill_base(e, prompt, P));
+    // Draft catch-up over positions 0..P: x_i = F_{i-1} + E[t_i], F_{-1} = 0.
+    FL_CHECK_CUDA(launch_embed_rows(e->embed, e->V, e->seq, e->x, 1, e->x2, e->d, P + 1, nullptr, nullptr, e->s, false));
+    FL_CHECK(run_stack(e, e->draft, e->x2, P + 1, nullptr, e->iota, e->iota, nullptr, nullptr, false));
+    FL_CHECK_CUDA(cudaMemcpyAsync(e->x_d, e->x2 + (size_t)P * e->d, sizeof(float) * e->d, cudaMemcpyDeviceToDevice, e->s));
+    SpecState h = {};
+    h.n = P;
+    h.produced = 1;
+    h.n_new = 1;
+    h.done = 0;
+    h.K = K;
+    h.max_acc = max_acc < 0 ? K : std::min(max_acc, K);
+    h.one = 1;
+    h.rows = 1;
+    h.last_row = 0;
+    FL_CHECK_CUDA(cudaMemcpyAsync(e->st, &h, sizeof(h), cudaMemcpyHostToDevice, e->s));
+    FL_CHECK_CUDA(cudaMemcpyAsync(e->out, e->seq + P, sizeof(int), cudaMemcpyDeviceToDevice, e->s));
+    FL_CHECK(run_lm(e, e->x_d, 1, nullptr, nullptr, false));
+    FL_CHECK_CUDA(launch_draft_pick(step_buffers(e), 0, e->s, false));
+    FL_CHECK_CUDA(cudaMemcpyAsync(e->st_snap, e->st, sizeof(SpecState), cudaMemcpyDeviceToDevice, e->s));
+    FL_CHECK_CUDA(cudaMemcpyAsync(e->xd0_snap, e->x_d, sizeof(float) * e->d, cudaMemcpyDeviceToDevice, e->s));
+    FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
+    FL_CHECK(build_step_graph(e));
+    e->spec_ready = 1;
+    return FL_OK;
+}
+
+FL_API int fl_engine_spec_decode(fl_engine_t* e, int n_new, int* out, int* acc_hist, int* steps) {
+    FL_CHECK(check_ready(e, true));
+    if (!e->spec_ready) return set_error(FL_E_STATE, "spec_decode: call fl_engine_spec_prefill first");
+    const int K = e->spec_K;
+    if (n_new <= 0 || e->spec_P + n_new + K + 2 > e->R) return set_error(FL_E_INVAL, "spec_decode: context too long");
+    FL_CHECK_CUDA(cudaMemcpyAsync(e->st, e->st_snap, sizeof(SpecState), cudaMemcpyDeviceToDevice, e->s));
+    FL_CHECK_CUDA(cudaMemcpyAsync(e->x_d, e->xd0_snap, sizeof(float) * e->d, cudaMemcpyDeviceToDevice, e->s));
+    const int patch[2] = {n_new, n_new <= 1 ? 1 : 0};
+    FL_CHECK_CUDA(cudaMemcpyAsync(&e->st->n_new, patch, sizeof(patch), cudaMemcpyHostToDevice, e->s));
+    FL_CHECK_CUDA(cudaEventRecord(e->ev[0], e->s));
+    SpecState h = {};
+    int produced = 1;
+    while (produced < n_new) {
+        const int batch = (n_new - produced + K) / (K + 1);
+        for (int i = 0; i < batch; i++) FL_CHECK_CUDA(cudaGraphLaunch(e->step_exec, e->s));
+        FL_CHECK_CUDA(cudaMemcpyAsync(&h, e->st, sizeof(h), cudaMemcpyDeviceToHost, e->s));
+        FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
+        if (h.produced <= produced) return set_error(FL_E_STATE, "spec_decode: no progress");
+        produced = h.produced;
+    }
+    FL_CHECK_CUDA(cudaEventRecord(e->ev[1], e->s));
+    FL_CHECK_CUDA(cudaEventSynchronize(e->ev[1]));
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, e->ev[0], e->ev[1]);
+    e->t_total_us = ms * 1000.0;
+    if (out) FL_CHECK_CUDA(cudaMemcpy(out, e->out, sizeof(int) * n_new, cudaMemcpyDeviceToHost));
+    if (acc_hist) FL_CHECK_CUDA(cudaMemcpy(acc_hist, e->acc, sizeof(int) * h.steps, cudaMemcpyDeviceToHost));
+    if (steps) *steps = h.steps;
+    return FL_OK;
+}
+
+FL_API int fl_engine_spec_generate(fl_engine_t* e, const int* prompt, int P, int n_new, int K, int max_acc,
+                                   int* out, int* acc_hist, int* steps) {
+    FL_CHECK(fl_engine_spec_prefill(e, prompt, P, K, max_acc));
+    return fl_engine_spec_decode(e, n_new, out, acc_hist, steps);
+}
+
+FL_API int fl_engine_last_timing(const fl_engine_t* e, double* draft_us, double* verify_us, double* total_us) {
+    if (!e) return set_error(FL_E_INVAL, "engine is NULL");
+    if (draft_us) *draft_us = e->t_draft_us;
+    if (verify_us) *verify_us = e->t_verify_us;
+    if (total_us) *total_us = e->t_total_us;
+    return FL_OK;
+}
+
+FL_API void* fl_engine_stream(const fl_engine_t* e) { return e ? (void*)e->s : nullptr; }
+
+// ---------------------------------------------------------------------------
+// Callback-level API: the engine as the reference's target_forward /
+// base_forward model, with an explicit base-cache position.
+// ---------------------------------------------------------------------------
+
+FL_API int fl_engine_position(const fl_engine_t* e) { return e ? e->cb_pos : -1; }
+
+FL_API int fl_engine_set_position(fl_engine_t* e, int pos) {
+    if (!e || pos < 0 || pos > e->R) return set_error(FL_E_INVAL, "set_position: out of range");
+    e->cb_pos = pos;
+    return FL_OK;
+}
+
+FL_API int fl_engine_last_feature(const fl_engine_t* e, float* out) {
+    if (!e || !out) return set_error(FL_E_INVAL, "last_feature: NULL");
+    FL_CHECK_CUDA(cudaSetDevice(e->device));
+    FL_CHECK_CUDA(cudaMemcpy(out, e->last_feat, sizeof(float) * e->d, cudaMemcpyDeviceToHost));
+    return FL_OK;
+}
+
+// Appends len tokens at the callback position through the base model.
+static int base_append(fl_engine* e, const int* tokens, int len, float* logits_out) {
+    FL_CHECK(check_ready(e, false));
+    if (len <= 0 || e->cb_pos + len > e->R) return set_error(FL_E_INVAL, "base forward: context full");
+    FL_CHECK_CUDA(cudaMemcpyAsync(e->tok, tokens, sizeof(int) * len, cudaMemcpyHostToDevice, e->s));
+    FL_CHECK_CUDA(launch_embed_rows(e->embed, e->V, e->tok, nullptr, 0, e->x, e->d, len, nullptr, nullptr, e->s, false));
+    FL_CHECK(run_stack(e, e->base, e->x, len, nullptr, e->iota + e->cb_pos, e->iota + e->cb_pos, nullptr, nullptr,
+                       false));
+    FL_CHECK_CUDA(cudaMemcpyAsync(e->last_feat, e->x + (size_t)(len - 1) * e->d, sizeof(float) * e->d,
+                                  cudaMemcpyDeviceToDevice, e->s));
+    if (logits_out) {
+        for (int r0 = 0; r0 < len; r0 += kMaxRows) {
+            const int m = std::min(kMaxRows, len - r0);
+            FL_CHECK(run_lm(e, e->x + (size_t)r0 * e->d, m, nullptr, nullptr, false));
+            FL_CHECK_CUDA(cudaMemcpyAsync(logits_out + (size_t)r0 * e->V, e->logits, sizeof(float) * (size_t)m * e->V,
+                                          cudaMemcpyDeviceToHost, e->s));
+        }
+    }
+    FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
+    e->cb_pos += len;
+    return FL_OK;
+}
+
+FL_API void fl_cuda_target_forward(void* model, const float* input, float* output, int len) {
+    fl_engine* e = (fl_engine*)model;
+    if (!e || !input || !output || len <= 0) {
+        set_error(FL_E_INVAL, "target_forward: bad arguments");
+        return;
+    }
+    std::vector<int> t(len);
+    for (int i = 0; i < len; i++) t[i] = (int)input[i];
+    base_append(e, t.data(), len, output);
+}
+
+FL_API void fl_cuda_base_forward(void* model, const int* tokens, int len, float* hidden, int hidden_size) {
+    fl_engine* e = (fl_engine*)model;
+    if (!e || !tokens || len <= 0) {
+        set_error(FL_E_INVAL, "base_forward: bad arguments");
+        return;
+    }
+    if (base_append(e, tokens, len, nullptr) != FL_OK) return;
+    if (hidden && hidden_size == e->d) fl_engine_last_feature(e, hidden);
+}
+
+// Single-row draft chain: x = hidden + E[tok] at position pos, then K greedy
+// draft tokens (each next input = draft output + E[previous draft]).
+FL_API int fl_engine_draft_chain(fl_engine_t* e, const float* hidden, int tok, int pos, int K, int* out_tokens,
+                                 float* out_probs) {
+    FL_CHECK(check_ready(e, true));
+    if (!hidden || !out_tokens || K <= 0 || pos < 0 || pos + K > e->R) return set_error(FL_E_INVAL, "draft_chain: bad arguments");
+    std::vector<float> lg(e->V);
+    FL_CHECK_CUDA(cudaMemcpyAsync(e->x2, hidden, sizeof(float) * e->d, cudaMemcpyHostToDevice, e->s));
+    FL_CHECK_CUDA(cudaMemcpyAsync(e->tok, &tok, sizeof(int), cudaMemcpyHostToDevice, e->s));
+    FL_CHECK_CUDA(launch_embed_rows(e->embed, e->V, e->tok, e->x2, 0, e->x_d, e->d, 1, nullptr, nullptr, e->s, false));
+    for (int j = 0; j < K; j++) {
+        FL_CHECK(run_stack(e, e->draft, e->x_d, 1, nullptr, e->iota + pos + j, e->iota + pos + j, nullptr, nullptr, false));
+        FL_CHECK(run_lm(e, e->x_d, 1, nullptr, nullptr, false));
+        FL_CHECK_CUDA(launch_argmax_rows(e->amax, e->nparts, 1, e->tok, nullptr, e->s));
+        FL_CHECK_CUDA(cudaMemcpyAsync(lg.data(), e->logits, sizeof(float) * e->V, cudaMemcpyDeviceToHost, e->s));
+        FL_CHECK_CUDA(cudaMemcpyAsync(&out_tokens[j], e->tok, sizeof(int), cudaMemcpyDeviceToHost, e->s));
+        FL_CHECK_CUDA(launch_embed_rows(e->embed, e->V, e->tok, e->x_d, 0, e->x_d, e->d, 1, nullptr, nullptr, e->s, false));
+        FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
+        if (out_probs) {
+            float mx = lg[0];
+            for (float v : lg) mx = v > mx ? v : mx;
+            double sum = 0.0;
+            for (float v : lg) sum += exp((double)(v - mx));
+            out_probs[j] = (float)(exp((double)(lg[out_tokens[j]] - mx)) / sum);
+        }
+    }
+    return FL_OK;
+}

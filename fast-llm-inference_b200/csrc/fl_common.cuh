@@ -1,0 +1,122 @@
+// Shared device helpers of the sm_100a speculative-decoding kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#define FL_API extern "C" __attribute__((visibility("default")))
+
+namespace fl {
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch (PDL). Every kernel calls pdl_trigger() early
+// so the next kernel in the stream can be scheduled and start streaming its
+// weights, and pdl_wait() before it reads anything an earlier kernel wrote or
+// writes anything an earlier kernel reads.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Activation quantization, dequantized_tensor.c:112-135: one fused
+// multiply-add x*127+128, conversion rounding to nearest even with the x86
+// cvtps2dq out-of-range rule (NaN or |v| >= 2^31 gives INT32_MIN), then
+// saturation to int16 and to [0, 255] -- net effect: clamp to [0, 255] with
+// out-of-range values mapping to 0.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t quant_u8(float x) {
+    float v = __fmaf_rn(x, 127.0f, 128.0f);
+    if (!(v > -2147483648.0f && v < 2147483648.0f)) return 0u;
+    int i = __float2int_rn(v);
+    i = i < 0 ? 0 : i;
+    i = i > 255 ? 255 : i;
+    return (uint32_t)i;
+}
+
+__device__ __forceinline__ uint32_t quant_pack4(float a, float b, float c, float d) {
+    return quant_u8(a) | (quant_u8(b) << 8) | (quant_u8(c) << 16) | (quant_u8(d) << 24);
+}
+
+// u8 x s8 4-way dot into int32 (plain, no saturation): dp4a with an
+// unsigned first and a signed second operand.
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t w, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(w), "r"(c));
+    return d;
+}
+
+// dot_product_u8_i8's pair rule (dequantized_tensor.c:168-176) on one 32-bit
+// word: (a0*w0 + a1*w1) and (a2*w2 + a3*w3) each saturated to int16.
+__device__ __forceinline__ int dp4_pairsat(uint32_t a, uint32_t w, int c) {
+    uint32_t a01 = __byte_perm(a, 0u, 0x4140);  // a0, 0, a1, 0 -> two u16
+    uint32_t a23 = __byte_perm(a, 0u, 0x4342);  // a2, 0, a3, 0
+    int p0 = __dp2a_lo((int)a01, (int)w, 0);    // a0*w0 + a1*w1
+    int p1 = __dp2a_hi((int)a23, (int)w, 0);    // a2*w2 + a3*w3
+    p0 = max(-32768, min(32767, p0));
+    p1 = max(-32768, min(32767, p1));
+    return c + p0 + p1;
+}
+
+// Reference polynomial sigmoid (activations_avx2.c:33-63), written in the
+// order of its source: clamp to [-10, 10], exp(-x) ~ 1 - x + x^2/2 - x^3/6
+// + x^4/24, sigma = 1 / (1 + that). No FMA contraction.
+__device__ __forceinline__ float poly_sigmoid(float x) {
+    x = fmaxf(-10.0f, fminf(10.0f, x));
+    float nx = __fsub_rn(0.0f, x);
+    float x2 = __fmul_rn(x, x);
+    float x3 = __fmul_rn(x2, x);
+    float x4 = __fmul_rn(x2, x2);
+    float t = __fadd_rn(__fmul_rn(x3, -0.166667f), __fmul_rn(x4, 0.041667f));
+    t = __fadd_rn(__fmul_rn(x2, 0.5f), t);
+    t = __fadd_rn(nx, t);
+    float p = __fadd_rn(1.0f, t);
+    return __fdiv_rn(1.0f, __fadd_rn(1.0f, p));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ int warp_sum_i(int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Streaming 16-byte load that bypasses L1 allocation (weights are read once).
+__device__ __forceinline__ uint4 ld_stream16(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+// Orderable 64-bit key for a deterministic argmax: larger value wins, ties go
+// to the lower index (inference.c:104-111 keeps the first maximum).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+    uint32_t b = __float_as_uint(v);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return ((unsigned long long)b << 32) | (uint32_t)(0x7fffffff - idx);
+}
+__device__ __forceinline__ int argmax_key_index(unsigned long long k) {
+    return 0x7fffffff - (int)(uint32_t)(k & 0xffffffffu);
+}
+__device__ __forceinline__ float argmax_key_value(unsigned long long k) {
+    uint32_t b = (uint32_t)(k >> 32);
+    b = (b & 0x80000000u) ? (b & 0x7fffffffu) : ~b;
+    return __uint_as_float(b);
+}
+
+}  // namespace fl

@@ -1,0 +1,96 @@
+// Launch-side declarations of the sm_100a kernels (host code includes this).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace fl {
+
+constexpr int kMaxRows = 8;      // rows of activations per GEMV launch
+constexpr int kPageSize = 64;    // KV positions per page
+
+enum Epilogue : int {
+    EPI_STORE = 0,   // out[m, n] = y
+    EPI_RESID = 1,   // out[m, n] += y  (residual add)
+    EPI_QKV = 2,     // RoPE on q/k pairs, q -> f32 buffer, k/v -> fp16 KV pages
+    EPI_SWIGLU = 3,  // interleaved gate/up rows -> quantized SwiGLU output
+    EPI_LOGITS = 4,  // out[m, n] = y and per-CTA argmax partials
+    EPI_DOTS = 5,    // per-(m, n, block) int32 dots (test path)
+};
+
+// One paged KV pool of one layer: [pages][kv_heads][kPageSize][head_dim].
+struct KvLayer {
+    __half* k;
+    __half* v;
+};
+
+struct GemvParams {
+    const uint8_t* aq;        // [rows, K] quantized activations
+    const int8_t* w;          // [N, K]
+    const __half* sblk;       // [N, K/32] block scales (block mode)
+    const float* srow;        // [N] per-row scales (per-row mode)
+    int M;                    // rows in this launch (<= kMaxRows)
+    const int* dyn_M;         // if set, rows = min(*dyn_M - row0, kMaxRows)
+    int row0;                 // first activation row of this launch
+    int N, K;
+    const int* done;          // if set and *done, the kernel exits
+    // EPI_STORE / EPI_RESID / EPI_LOGITS
+    float* out;
+    int ldo;
+    // EPI_QKV
+    float* q_out;             // [rows, q_dim]
+    KvLayer kv;
+    const int* block_table;   // slot / kPageSize -> page
+    const int* slot_base;     // device scalar: cache slot of activation row 0
+    const int* pos;           // [rows] rotary positions
+    int q_dim, kv_dim, head_dim, kv_heads;
+    float theta;
+    // EPI_SWIGLU
+    uint8_t* hq;              // [rows, F]
+    int F;
+    // EPI_LOGITS: partial argmax keys [rows][gridDim.x]
+    unsigned long long* amax_part;
+    // EPI_DOTS
+    int32_t* dots;            // [rows, N, K/32]
+};
+
+// Chooses the kernel variant; `rowmode` selects per-row scales and
+// `pairsat` the int16 pair-saturating dot. `pdl` enables programmatic
+// dependent launch.
+cudaError_t launch_gemv(const GemvParams& p, int epi, bool rowmode, bool pairsat,
+                        cudaStream_t s, bool pdl);
+int gemv_grid(int N);
+
+struct ActQuantParams {
+    const float* x;           // [rows, K]
+    uint8_t* q;               // [rows, K]
+    int K;
+    int M;                    // rows (grid size)
+    const int* dyn_M;         // optional device row count (<= M)
+    int row0;                 // first row handled
+    int norm;                 // 1 = RMSNorm (unit weights) before quantization
+    float eps;
+    const int* done;
+    const int* dyn_src_row;   // if set: source row *dyn_src_row + blockIdx.x,
+                              // written to output row row0 + blockIdx.x
+};
+cudaError_t launch_act_quant(const ActQuantParams& p, cudaStream_t s, bool pdl);
+
+struct AttnParams {
+    const float* q;           // [rows, heads*head_dim], rotated
+    KvLayer kv;
+    const int* block_table;
+    const int* slot_base;     // device scalar: slot of new row 0 (= prefix length)
+    int M;                    // new rows
+    const int* dyn_M;
+    const uint8_t* mask;      // [M*M] visibility among new rows, NULL = causal
+    int heads, kv_heads, head_dim;
+    int max_ctx;              // upper bound of slot_base + M (smem sizing)
+    uint8_t* out_q;           // [rows, heads*head_dim] quantized output
+    float* out_f;             // optional f32 output
+    const int* done;
+};
+cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl);
+
+}  // namespace fl

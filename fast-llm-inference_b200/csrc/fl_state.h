@@ -1,0 +1,78 @@
+// Device-resident state of one speculative decode and the kernels that
+// advance it between the draft and verify passes.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "fl_kernels.h"
+
+namespace fl {
+
+constexpr int kMaxDraft = kMaxRows - 1;  // K <= 7 so that K + 1 rows fit a launch
+
+// Lives in HBM; every step kernel reads positions from here so one captured
+// step graph replays unchanged. Index convention: seq[n] is the newest
+// committed token, not yet in the base KV cache (base holds slots [0, n)).
+struct SpecState {
+    int n;                  // newest committed token index
+    int produced;           // tokens emitted so far
+    int n_new;              // tokens requested
+    int done;               // 1 once produced >= n_new: later kernels exit
+    int steps;
+    int K;                  // drafted tokens per step
+    int max_acc;            // cap on accepted drafts
+    int one;                // constant 1 (row count of single-row passes)
+    int rows;               // rows of the current draft catch-up pass
+    int last_row;           // rows - 1
+    int draft_base;         // cache slot of row 0 of the current draft pass
+    int verify_base;        // cache slot of verify row 0 (= n)
+    int a_last;             // drafts accepted by the last verify
+    int draft_pos[kMaxRows];
+    int verify_pos[kMaxRows];
+    int drafted[kMaxRows];  // draft tokens d_1..d_K of the current step
+    int target[kMaxRows];   // base-model argmax of the verify rows
+};
+
+struct StepBuffers {
+    SpecState* st;
+    int* seq;               // committed tokens
+    int* out;               // emitted tokens [n_new]
+    int* acc_hist;          // accepted drafts per step
+    const float* embed;     // [vocab, d]
+    float* x_d;             // draft rows [kMaxRows, d]
+    float* x_v;             // verify rows [kMaxRows, d]
+    const unsigned long long* amax_part;  // [rows][nparts]
+    int nparts;             // partials per row (LM-head GEMV grid)
+    int d;
+};
+
+// x[r] = E[tok[r]] + (r >= shift ? feat[r - shift] : 0) for r < rows,
+// rows = dyn_rows ? *dyn_rows : rows_static; ids outside [0, vocab) read row 0.
+cudaError_t launch_embed_rows(const float* embed, int vocab, const int* tok, const float* feat, int shift,
+                              float* x, int d, int rows_static, const int* dyn_rows,
+                              const int* done, cudaStream_t s, bool pdl);
+
+// Greedy pick of draft token j from the LM-head partials of row 0; writes
+// drafted[j] and, when j + 1 < K, the next single-row draft input
+// x_d[0] = g + E[drafted[j]] with g = x_d[g_row] (g_row = last_row when
+// j == 0, else 0) at slot/position n + j + 1.
+cudaError_t launch_draft_pick(const StepBuffers& b, int j, cudaStream_t s, bool pdl);
+
+// Verify rows: x_v[r] = E[tok_r], tok_0 = seq[n], tok_r = drafted[r - 1],
+// positions n + r.
+cudaError_t launch_verify_prep(const StepBuffers& b, int K, cudaStream_t s, bool pdl);
+
+// Base argmax per verify row, longest accepted prefix, commit tokens,
+// advance the state (include/speculative.h rule).
+cudaError_t launch_accept(const StepBuffers& b, int K, cudaStream_t s, bool pdl);
+
+// Next draft catch-up rows: x_d[r] = x_v[r] + E[seq[n_old + 1 + r]] for
+// r <= a_last, positions n_old + 1 + r.
+cudaError_t launch_catchup_prep(const StepBuffers& b, int K, cudaStream_t s, bool pdl);
+
+// out_tok[r] = argmax over the LM partials of row r, r < rows.
+cudaError_t launch_argmax_rows(const unsigned long long* part, int nparts, int rows, int* out_tok,
+                               float* out_val, cudaStream_t s);
+
+}  // namespace fl

@@ -1,0 +1,283 @@
+// fl_cuda runtime: errors, device streams, memory helpers, INT8 tensor upload
+// and the INT8 matmul entry points (include/fl_cuda.h).
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "fl_common.cuh"
+#include "fl_kernels.h"
+#include "fl_runtime.h"
+
+namespace fl {
+
+namespace {
+thread_local std::string g_err;
+std::mutex g_mu;
+std::vector<cudaStream_t> g_streams;  // per device
+}  // namespace
+
+int set_error(int code, const std::string& msg) {
+    g_err = msg;
+    return code;
+}
+
+int cuda_error(cudaError_t e, const char* what) {
+    std::string m = std::string(what) + ": " + cudaGetErrorString(e);
+    cudaGetLastError();  // clear a sticky launch error where possible
+    return set_error(e == cudaErrorMemoryAllocation ? FL_E_NOMEM
+                     : e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver ? FL_E_NODEV
+                                                                                  : FL_E_CUDA,
+                     m);
+}
+
+int ensure_device() {
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return set_error(FL_E_NODEV, "no CUDA device available (the INT8 path has no CPU fallback)");
+    }
+    return FL_OK;
+}
+
+cudaStream_t device_stream() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if ((int)g_streams.size() <= dev) g_streams.resize(dev + 1, nullptr);
+    if (!g_streams[dev]) {
+        cudaStream_t s = nullptr;
+        if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
+        g_streams[dev] = s;
+    }
+    return g_streams[dev];
+}
+
+int upload_tensor(dequantized_tensor_t* t) {
+    if (!t || !t->weights || t->rows <= 0 || t->cols <= 0)
+        return set_error(FL_E_INVAL, "upload_tensor: tensor without int8 weights");
+    if (t->dev) return FL_OK;
+    FL_CHECK(ensure_device());
+    const int blk = t->scale_block;
+    if (blk != 0 && blk != 32) return set_error(FL_E_INVAL, "upload_tensor: scale_block must be 0 or 32");
+    if (blk == 32 && (!t->scales_f16 || t->cols % 32 != 0))
+        return set_error(FL_E_INVAL, "upload_tensor: block mode needs scales_f16 and cols % 32 == 0");
+    if (blk == 0 && !t->scales) return set_error(FL_E_INVAL, "upload_tensor: per-row mode needs scales");
+    DevTensor* d = (DevTensor*)calloc(1, sizeof(DevTensor));
+    if (!d) return set_error(FL_E_NOMEM, "upload_tensor: host allocation");
+    d->rows = t->rows;
+    d->cols = t->cols;
+    d->scale_block = blk;
+    cudaGetDevice(&d->device);
+    const size_t nw = (size_t)t->rows * t->cols;
+    cudaError_t e = cudaMalloc(&d->w, nw);
+    if (e == cudaSuccess) e = cudaMemcpy(d->w, t->weights, nw, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && blk == 32) {
+        const size_t ns = (size_t)t->rows * (t->cols / 32) * sizeof(__half);
+        e = cudaMalloc(&d->sblk, ns);
+        if (e == cudaSuccess) e = cudaMemcpy(d->sblk, t->scales_f16, ns, cudaMemcpyHostToDevice);
+    }
+    if (e == cudaSuccess && blk == 0) {
+        e = cudaMalloc(&d->srow, (size_t)t->rows * sizeof(float));
+        if (e == cudaSuccess)
+            e = cudaMemcpy(d->srow, t->scales, (size_t)t->rows * sizeof(float), cudaMemcpyHostToDevice);
+        // The int16 pair saturation of dot_product_u8_i8 can only trigger when
+        // some |w| > 64 (255 * 64 * 2 < 32768): pick the exact kernel variant.
+        for (size_t i = 0; i < nw; i++) {
+            const int v = t->weights[i];
+            if (v > 64 || v < -64) { d->pairsat = 1; break; }
+        }
+    }
+    if (e != cudaSuccess) {
+        cudaFree(d->w);
+        cudaFree(d->sblk);
+        cudaFree(d->srow);
+        free(d);
+        return cuda_error(e, "upload_tensor");
+    }
+    t->dev = d;
+    return FL_OK;
+}
+
+void release_tensor(dequantized_tensor_t* t) {
+    if (!t || !t->dev) return;
+    DevTensor* d = (DevTensor*)t->dev;
+    int cur = 0;
+    cudaGetDevice(&cur);
+    cudaSetDevice(d->device);
+    cudaFree(d->w);
+    cudaFree(d->sblk);
+    cudaFree(d->srow);
+    cudaSetDevice(cur);
+    free(d);
+    t->dev = nullptr;
+}
+
+// Fills the operand part of GemvParams from an uploaded tensor.
+static int tensor_params(const dequantized_tensor_t* B, int N, int K, GemvParams& p) {
+    if (!B || !B->dev) return set_error(FL_E_STATE, "tensor not uploaded (fl_cuda_upload_tensor)");
+    const DevTensor* d = (const DevTensor*)B->dev;
+    if (d->rows != N || d->cols != K) return set_error(FL_E_INVAL, "matmul: N/K do not match the tensor");
+    if (K % 32 != 0) return set_error(FL_E_INVAL, "matmul: K must be a multiple of 32");
+    int cur = 0;
+    cudaGetDevice(&cur);
+    if (cur != d->device) return set_error(FL_E_STATE, "matmul: tensor lives on another device");
+    p.w = d->w;
+    p.sblk = d->sblk;
+    p.srow = d->srow;
+    p.N = N;
+    p.K = K;
+    return FL_OK;
+}
+
+static int run_gemv_chunks(const uint8_t* Aq, const dequantized_tensor_t* B, float* C, int32_t* D,
+                           int M, int N, int K, cudaStream_t s, int epi) {
+    GemvParams p = {};
+    FL_CHECK(tensor_params(B, N, K, p));
+    const DevTensor* d = (const DevTensor*)B->dev;
+    p.aq = Aq;
+    p.out = C;
+    p.ldo = N;
+    p.dots = D;
+    for (int r0 = 0; r0 < M; r0 += kMaxRows) {
+        p.row0 = r0;
+        p.M = M - r0 < kMaxRows ? M - r0 : kMaxRows;
+        FL_CHECK_CUDA(launch_gemv(p, epi, d->scale_block == 0, d->pairsat != 0, s, false));
+    }
+    return FL_OK;
+}
+
+// Scratch for quantized activations of the host-facing matmul entry points.
+struct Scratch {
+    uint8_t* q = nullptr;
+    size_t cap = 0;
+};
+static thread_local std::vector<Scratch> t_scratch;
+
+static int scratch_q(size_t bytes, uint8_t** out) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if ((int)t_scratch.size() <= dev) t_scratch.resize(dev + 1);
+    Scratch& sc = t_scratch[dev];
+    if (sc.cap < bytes) {
+        if (sc.q) cudaFree(sc.q);
+        sc.q = nullptr;
+        sc.cap = 0;
+        FL_CHECK_CUDA(cudaMalloc(&sc.q, bytes));
+        sc.cap = bytes;
+    }
+    *out = sc.q;
+    return FL_OK;
+}
+
+}  // namespace fl
+
+using namespace fl;
+
+FL_API const char* fl_cuda_last_error(void) { return g_err.c_str(); }
+
+FL_API int fl_cuda_device_count(int* count) {
+    if (!count) return set_error(FL_E_INVAL, "count is NULL");
+    *count = 0;
+    cudaError_t e = cudaGetDeviceCount(count);
+    if (e != cudaSuccess) {
+        *count = 0;
+        cudaGetLastError();
+    }
+    return FL_OK;
+}
+
+FL_API int fl_cuda_init(int device) {
+    FL_CHECK(ensure_device());
+    FL_CHECK_CUDA(cudaSetDevice(device));
+    if (!device_stream()) return set_error(FL_E_CUDA, "stream creation failed");
+    return FL_OK;
+}
+
+FL_API int fl_cuda_sync(void) {
+    cudaStream_t s = device_stream();
+    if (!s) return set_error(FL_E_NODEV, "no device");
+    FL_CHECK_CUDA(cudaStreamSynchronize(s));
+    return FL_OK;
+}
+
+FL_API void* fl_cuda_stream(void) { return (void*)device_stream(); }
+
+FL_API int fl_cuda_malloc(void** dptr, size_t bytes) {
+    if (!dptr) return set_error(FL_E_INVAL, "dptr is NULL");
+    FL_CHECK(ensure_device());
+    FL_CHECK_CUDA(cudaMalloc(dptr, bytes));
+    return FL_OK;
+}
+
+FL_API int fl_cuda_free(void* dptr) {
+    FL_CHECK_CUDA(cudaFree(dptr));
+    return FL_OK;
+}
+
+FL_API int fl_cuda_h2d(void* dst, const void* src, size_t bytes) {
+    FL_CHECK_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, device_stream()));
+    FL_CHECK_CUDA(cudaStreamSynchronize(device_stream()));
+    return FL_OK;
+}
+
+FL_API int fl_cuda_d2h(void* dst, const void* src, size_t bytes) {
+    FL_CHECK_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, device_stream()));
+    FL_CHECK_CUDA(cudaStreamSynchronize(device_stream()));
+    return FL_OK;
+}
+
+FL_API int fl_cuda_memset(void* dptr, int value, size_t bytes) {
+    FL_CHECK_CUDA(cudaMemsetAsync(dptr, value, bytes, device_stream()));
+    return FL_OK;
+}
+
+FL_API int fl_cuda_upload_tensor(dequantized_tensor_t* t) { return upload_tensor(t); }
+
+FL_API int fl_cuda_act_quant(const float* x, uint8_t* q, int M, int K, int rmsnorm, float eps,
+                             void* stream) {
+    if (!x || !q || M <= 0 || K <= 0 || K % 4 != 0) return set_error(FL_E_INVAL, "act_quant: bad arguments");
+    ActQuantParams p = {};
+    p.x = x;
+    p.q = q;
+    p.K = K;
+    p.M = M;
+    p.norm = rmsnorm;
+    p.eps = eps;
+    cudaStream_t s = stream ? (cudaStream_t)stream : device_stream();
+    FL_CHECK_CUDA(launch_act_quant(p, s, false));
+    return FL_OK;
+}
+
+FL_API int fl_cuda_gemv_i8(const uint8_t* Aq, const dequantized_tensor_t* B, float* C, int M, int N,
+                           int K, void* stream) {
+    if (!Aq || !C || M <= 0) return set_error(FL_E_INVAL, "gemv: bad arguments");
+    cudaStream_t s = stream ? (cudaStream_t)stream : device_stream();
+    return run_gemv_chunks(Aq, B, C, nullptr, M, N, K, s, EPI_STORE);
+}
+
+FL_API int fl_cuda_matmul_i8(const float* A, const dequantized_tensor_t* B, float* C, int M, int N,
+                             int K, void* stream) {
+    if (!A || !C || M <= 0 || N <= 0 || K <= 0) return set_error(FL_E_INVAL, "matmul: bad arguments");
+    if (K % 32 != 0) return set_error(FL_E_INVAL, "matmul: K must be a multiple of 32");
+    cudaStream_t s = stream ? (cudaStream_t)stream : device_stream();
+    uint8_t* q = nullptr;
+    FL_CHECK(scratch_q((size_t)M * K, &q));
+    FL_CHECK(fl_cuda_act_quant(A, q, M, K, 0, 0.0f, s));
+    return run_gemv_chunks(q, B, C, nullptr, M, N, K, s, EPI_STORE);
+}
+
+FL_API int fl_cuda_block_dots_i8(const float* A, const dequantized_tensor_t* B, int32_t* D, int M, int N,
+                                 int K, void* stream) {
+    if (!A || !D || M <= 0 || N <= 0 || K <= 0) return set_error(FL_E_INVAL, "block_dots: bad arguments");
+    if (K % 32 != 0) return set_error(FL_E_INVAL, "block_dots: K must be a multiple of 32");
+    cudaStream_t s = stream ? (cudaStream_t)stream : device_stream();
+    uint8_t* q = nullptr;
+    FL_CHECK(scratch_q((size_t)M * K, &q));
+    FL_CHECK(fl_cuda_act_quant(A, q, M, K, 0, 0.0f, s));
+    return run_gemv_chunks(q, B, nullptr, D, M, N, K, s, EPI_DOTS);
+}

@@ -1,0 +1,317 @@
+"""ctypes binding of libfl_b200.so (include/*.h) for Python callers.
+
+The library is the product: C ABI, sm_100a kernels, no Python compute. This
+module only declares the signatures and offers numpy conveniences. Loading
+fails loudly when the shared library is missing; there is no fallback.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libfl_b200.so")
+
+FL_OK = 0
+
+
+class FLError(RuntimeError):
+    pass
+
+
+class DequantizedTensor(C.Structure):
+    """dequantized_tensor_t (include/dequantized_tensor.h)."""
+    _fields_ = [
+        ("weights", C.POINTER(C.c_int8)),
+        ("scales", C.POINTER(C.c_float)),
+        ("f32_weights", C.POINTER(C.c_float)),
+        ("rows", C.c_int),
+        ("cols", C.c_int),
+        ("original_bits", C.c_int),
+        ("scale_block", C.c_int),
+        ("scales_f16", C.POINTER(C.c_uint16)),
+        ("dev", C.c_void_p),
+    ]
+
+
+class ModelConfig(C.Structure):
+    """fl_model_config_t (include/fl_cuda.h)."""
+    _fields_ = [
+        ("vocab_size", C.c_int),
+        ("hidden_size", C.c_int),
+        ("intermediate_size", C.c_int),
+        ("num_layers", C.c_int),
+        ("num_heads", C.c_int),
+        ("num_kv_heads", C.c_int),
+        ("head_dim", C.c_int),
+        ("draft_layers", C.c_int),
+        ("medusa_heads", C.c_int),
+        ("max_seq_len", C.c_int),
+        ("rope_theta", C.c_float),
+        ("norm_eps", C.c_float),
+    ]
+
+
+class SpecConfig(C.Structure):
+    """speculative_config_t (include/speculative.h)."""
+    _fields_ = [("num_draft_tokens", C.c_int), ("temperature", C.c_float), ("max_accepted", C.c_int)]
+
+
+class DraftTree(C.Structure):
+    _fields_ = [("tokens", C.POINTER(C.c_int)), ("probs", C.POINTER(C.c_float)),
+                ("num_tokens", C.c_int), ("max_tokens", C.c_int)]
+
+
+class DraftKV(C.Structure):
+    _fields_ = [("k_cache", C.POINTER(C.c_float)), ("v_cache", C.POINTER(C.c_float)),
+                ("cache_len", C.c_int), ("max_len", C.c_int)]
+
+
+class DraftModel(C.Structure):
+    _fields_ = [(n, C.POINTER(DequantizedTensor)) for n in
+                ("w_q_proj", "w_k_proj", "w_v_proj", "w_o_proj", "w_gate", "w_up", "w_down", "w_lm_head")] + \
+               [("num_layers", C.c_int), ("hidden_size", C.c_int), ("intermediate_size", C.c_int),
+                ("vocab_size", C.c_int)]
+
+
+VP = C.c_void_p
+I = C.c_int
+F = C.c_float
+U64 = C.c_uint64
+U32 = C.c_uint32
+SZ = C.c_size_t
+
+_SIGS = {
+    "fl_cuda_last_error": (C.c_char_p, []),
+    "fl_cuda_init": (I, [I]),
+    "fl_cuda_device_count": (I, [C.POINTER(I)]),
+    "fl_cuda_sync": (I, []),
+    "fl_cuda_stream": (VP, []),
+    "fl_cuda_malloc": (I, [C.POINTER(VP), SZ]),
+    "fl_cuda_free": (I, [VP]),
+    "fl_cuda_h2d": (I, [VP, VP, SZ]),
+    "fl_cuda_d2h": (I, [VP, VP, SZ]),
+    "fl_cuda_memset": (I, [VP, I, SZ]),
+    "fl_cuda_upload_tensor": (I, [C.POINTER(DequantizedTensor)]),
+    "fl_cuda_act_quant": (I, [VP, VP, I, I, I, F, VP]),
+    "fl_cuda_matmul_i8": (I, [VP, C.POINTER(DequantizedTensor), VP, I, I, I, VP]),
+    "fl_cuda_gemv_i8": (I, [VP, C.POINTER(DequantizedTensor), VP, I, I, I, VP]),
+    "fl_cuda_block_dots_i8": (I, [VP, C.POINTER(DequantizedTensor), VP, I, I, I, VP]),
+    "fl_synth_q4_0_i8": (I, [U64, U32, I, I, F, VP, VP]),
+    "fl_synth_q4_0_f32": (I, [U64, U32, I, I, F, VP]),
+    "fl_synth_normal": (I, [U64, U32, SZ, F, VP]),
+    "fl_q4_0_to_i8": (I, [VP, I, I, VP, VP]),
+    "fl_philox4x32_10": (None, [VP, VP, VP]),
+    "fl_engine_create": (VP, [C.POINTER(ModelConfig), I]),
+    "fl_engine_destroy": (None, [VP]),
+    "fl_engine_load_linear": (I, [VP, I, I, I, VP, VP, I, I]),
+    "fl_engine_load_embedding": (I, [VP, VP]),
+    "fl_engine_synthesize": (I, [VP, U64]),
+    "fl_engine_ready": (I, [VP]),
+    "fl_engine_forward_rows": (I, [VP, I, VP, I, I, VP, VP, VP, VP]),
+    "fl_engine_greedy_generate": (I, [VP, VP, I, I, VP]),
+    "fl_engine_spec_generate": (I, [VP, VP, I, I, I, I, VP, VP, VP]),
+    "fl_engine_spec_prefill": (I, [VP, VP, I, I, I]),
+    "fl_engine_spec_decode": (I, [VP, I, VP, VP, VP]),
+    "fl_engine_last_timing": (I, [VP, VP, VP, VP]),
+    "fl_engine_stream": (VP, [VP]),
+    "fl_engine_position": (I, [VP]),
+    "fl_engine_set_position": (I, [VP, I]),
+    "fl_engine_last_feature": (I, [VP, VP]),
+    "fl_engine_draft_chain": (I, [VP, VP, I, I, I, VP, VP]),
+    "fl_engine_bind_draft": (I, [VP, VP]),
+    "fl_draft_tree_set_vocab": (I, [VP, I]),
+    "matmul_dequantized": (None, [VP, C.POINTER(DequantizedTensor), VP, I, I, I]),
+    "dequantized_tensor_free": (None, [C.POINTER(DequantizedTensor)]),
+    "dequantized_from_q4": (C.POINTER(DequantizedTensor), [VP]),
+    "dequantized_from_q8": (C.POINTER(DequantizedTensor), [VP]),
+    "draft_model_create": (C.POINTER(DraftModel), [I, I, I, I]),
+    "draft_model_load": (I, [C.POINTER(DraftModel), C.c_char_p]),
+    "draft_model_free": (None, [C.POINTER(DraftModel)]),
+    "draft_tree_create": (C.POINTER(DraftTree), [I]),
+    "draft_tree_free": (None, [C.POINTER(DraftTree)]),
+    "draft_kv_cache_create": (C.POINTER(DraftKV), [I, I, I]),
+    "draft_kv_cache_free": (None, [C.POINTER(DraftKV)]),
+    "verify_tokens": (I, [VP, C.POINTER(DraftTree), VP, C.POINTER(I), C.POINTER(SpecConfig)]),
+    "speculative_generate": (I, [C.POINTER(DraftModel), VP, VP, VP, I, VP, I, C.POINTER(SpecConfig)]),
+}
+
+
+def ptr(a: np.ndarray | None) -> int | None:
+    if a is None:
+        return None
+    assert a.flags["C_CONTIGUOUS"], "arrays passed to the C ABI must be contiguous"
+    return a.ctypes.data
+
+
+class Lib:
+    """Loaded libfl_b200.so with typed functions."""
+
+    def __init__(self, path: str = LIB_PATH):
+        if not os.path.exists(path):
+            raise FLError(f"{path} is missing: build it with fast-llm-inference_b200/build.py")
+        self.path = path
+        self.so = C.CDLL(path)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(self.so, name)
+            fn.restype = res
+            fn.argtypes = args
+            setattr(self, name, fn)
+
+    def err(self) -> str:
+        m = self.fl_cuda_last_error()
+        return m.decode() if m else ""
+
+    def check(self, rc: int, what: str = "") -> None:
+        if rc != FL_OK:
+            raise FLError(f"{what} failed ({rc}): {self.err()}")
+
+    def device_count(self) -> int:
+        n = C.c_int(0)
+        self.fl_cuda_device_count(C.byref(n))
+        return n.value
+
+    # --------------------------------------------------------------- synth
+    def synth_q4_0_i8(self, seed: int, tid: int, rows: int, cols: int, std: float = 0.02):
+        w = np.empty((rows, cols), np.int8)
+        d = np.empty((rows, cols // 32), np.uint16)
+        self.check(self.fl_synth_q4_0_i8(seed, tid, rows, cols, std, ptr(w), ptr(d)), "synth")
+        return w, d
+
+    def synth_q4_0_f32(self, seed: int, tid: int, rows: int, cols: int, std: float = 0.02):
+        o = np.empty((rows, cols), np.float32)
+        self.check(self.fl_synth_q4_0_f32(seed, tid, rows, cols, std, ptr(o)), "synth")
+        return o
+
+    def synth_normal(self, seed: int, tid: int, count: int, std: float = 1.0):
+        o = np.empty(count, np.float32)
+        self.check(self.fl_synth_normal(seed, tid, count, std, ptr(o)), "synth")
+        return o
+
+    def philox(self, ctr, key):
+        c = np.asarray(ctr, np.uint32)
+        k = np.asarray(key, np.uint32)
+        o = np.empty(4, np.uint32)
+        self.fl_philox4x32_10(ptr(c), ptr(k), ptr(o))
+        return o
+
+
+def tensor_id(stack: int, layer: int, proj: int) -> int:
+    return (stack << 24) | (layer << 8) | proj
+
+
+def block_tensor(w: np.ndarray, d: np.ndarray) -> DequantizedTensor:
+    """Block-mode dequantized_tensor_t over numpy arrays (kept alive by caller)."""
+    t = DequantizedTensor()
+    t.weights = w.ctypes.data_as(C.POINTER(C.c_int8))
+    t.scales = None
+    t.f32_weights = None
+    t.rows, t.cols = w.shape
+    t.original_bits = 4
+    t.scale_block = 32
+    t.scales_f16 = d.ctypes.data_as(C.POINTER(C.c_uint16))
+    t.dev = None
+    return t
+
+
+def row_tensor(w: np.ndarray, s: np.ndarray) -> DequantizedTensor:
+    """Per-row-scale dequantized_tensor_t (the reference's own mode)."""
+    t = DequantizedTensor()
+    t.weights = w.ctypes.data_as(C.POINTER(C.c_int8))
+    t.scales = s.ctypes.data_as(C.POINTER(C.c_float))
+    t.f32_weights = None
+    t.rows, t.cols = w.shape
+    t.original_bits = 8
+    t.scale_block = 0
+    t.scales_f16 = None
+    t.dev = None
+    return t
+
+
+PHI3_MINI = dict(vocab_size=32064, hidden_size=3072, intermediate_size=8192, num_layers=32, num_heads=32,
+                 num_kv_heads=32, head_dim=96, draft_layers=4, medusa_heads=0, max_seq_len=1024,
+                 rope_theta=10000.0, norm_eps=1e-5)
+
+
+def model_config(**kw) -> ModelConfig:
+    c = ModelConfig()
+    for k, v in kw.items():
+        setattr(c, k, v)
+    return c
+
+
+class Engine:
+    """Owns an fl_engine_t."""
+
+    def __init__(self, lib: Lib, cfg: dict, device: int = 0):
+        self.lib = lib
+        self.cfg = dict(cfg)
+        self._c = model_config(**cfg)
+        h = lib.fl_engine_create(C.byref(self._c), device)
+        if not h:
+            raise FLError(f"fl_engine_create failed: {lib.err()}")
+        self.h = h
+
+    def close(self):
+        if self.h:
+            self.lib.fl_engine_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def load_linear(self, stack, layer, proj, w, d):
+        self.lib.check(self.lib.fl_engine_load_linear(self.h, stack, layer, proj, ptr(w), ptr(d), w.shape[0],
+                                                      w.shape[1]), "load_linear")
+
+    def load_embedding(self, e):
+        self.lib.check(self.lib.fl_engine_load_embedding(self.h, ptr(e)), "load_embedding")
+
+    def synthesize(self, seed):
+        self.lib.check(self.lib.fl_engine_synthesize(self.h, seed), "synthesize")
+
+    def forward_rows(self, stack, x, base, pos, mask=None, logits=True):
+        x = np.ascontiguousarray(x, np.float32)
+        M = x.shape[0]
+        pos = np.ascontiguousarray(pos, np.int32)
+        xo = np.empty_like(x)
+        lg = np.empty((M, self.cfg["vocab_size"]), np.float32) if logits else None
+        mk = None if mask is None else np.ascontiguousarray(mask, np.uint8)
+        self.lib.check(self.lib.fl_engine_forward_rows(self.h, stack, ptr(x), M, base, ptr(pos), ptr(mk), ptr(xo),
+                                                       ptr(lg)), "forward_rows")
+        return xo, lg
+
+    def greedy(self, prompt, n_new):
+        p = np.ascontiguousarray(prompt, np.int32)
+        o = np.empty(n_new, np.int32)
+        self.lib.check(self.lib.fl_engine_greedy_generate(self.h, ptr(p), len(p), n_new, ptr(o)), "greedy")
+        return o
+
+    def spec_prefill(self, prompt, k, max_acc=-1):
+        p = np.ascontiguousarray(prompt, np.int32)
+        self.lib.check(self.lib.fl_engine_spec_prefill(self.h, ptr(p), len(p), k, max_acc), "spec_prefill")
+
+    def spec_decode(self, n_new):
+        o = np.empty(n_new, np.int32)
+        acc = np.zeros(n_new + 1, np.int32)
+        steps = C.c_int(0)
+        self.lib.check(self.lib.fl_engine_spec_decode(self.h, n_new, ptr(o), ptr(acc), C.byref(steps)),
+                       "spec_decode")
+        return o, acc[: steps.value]
+
+    def spec_generate(self, prompt, n_new, k, max_acc=-1):
+        self.spec_prefill(prompt, k, max_acc)
+        return self.spec_decode(n_new)
+
+    def last_timing(self):
+        a, b, c = C.c_double(), C.c_double(), C.c_double()
+        self.lib.check(self.lib.fl_engine_last_timing(self.h, C.byref(a), C.byref(b), C.byref(c)), "timing")
+        return a.value, b.value, c.value
+
+    def stream(self) -> int:
+        return self.lib.fl_engine_stream(self.h)

@@ -1,0 +1,226 @@
+/*
+ * fl_cuda -- the thin C ABI between the C host code of the speculative-
+ * decoding path and its sm_100a kernels.
+ *
+ * The reference calls its AVX2 kernels directly from C (inference.c:131-156
+ * matvec, dequantized_tensor.c:204 matmul_dequantized). This header is the
+ * replacement seam: plain pointers, sizes and int status codes, no C++ or
+ * framework types. Every call is ordered on the library's CUDA stream of the
+ * current device unless a stream (a cudaStream_t passed as void*) is given.
+ *
+ * Status: 0 on success, a negative FL_E_* code otherwise; the message of the
+ * last failure on the calling thread is returned by fl_cuda_last_error().
+ * No function aborts or exits the process.
+ */
+#ifndef FL_CUDA_H
+#define FL_CUDA_H
+
+#include <stdint.h>
+#include <stddef.h>
+#include "dequantized_tensor.h"
+#include "medusa.h"
+#include "quant_types.h"
+#include "speculative.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FL_OK             0
+#define FL_E_INVAL       -1   /* bad argument / unsupported shape          */
+#define FL_E_CUDA        -2   /* CUDA runtime or launch failure            */
+#define FL_E_NOMEM       -3   /* host or device allocation failed          */
+#define FL_E_UNSUPPORTED -4   /* valid request this build does not serve   */
+#define FL_E_TIMEOUT     -5   /* a bounded device-side wait gave up        */
+#define FL_E_NODEV       -6   /* no CUDA device                            */
+#define FL_E_STATE       -7   /* call out of order (e.g. not uploaded)     */
+
+/* ------------------------------------------------------------------ */
+/* runtime                                                             */
+/* ------------------------------------------------------------------ */
+
+const char* fl_cuda_last_error(void);
+int fl_cuda_init(int device);                 /* select device, create stream */
+int fl_cuda_device_count(int* count);
+int fl_cuda_sync(void);                       /* drain the library stream     */
+void* fl_cuda_stream(void);                   /* cudaStream_t of the device   */
+
+int fl_cuda_malloc(void** dptr, size_t bytes);
+int fl_cuda_free(void* dptr);
+int fl_cuda_h2d(void* dst, const void* src, size_t bytes);
+int fl_cuda_d2h(void* dst, const void* src, size_t bytes);
+int fl_cuda_memset(void* dptr, int value, size_t bytes);
+
+/* ------------------------------------------------------------------ */
+/* INT8 tensors and the GEMV / skinny GEMM                             */
+/* ------------------------------------------------------------------ */
+
+/* Uploads t->weights (and t->scales or t->scales_f16) to HBM once and sets
+ * t->dev. Block mode needs cols % 32 == 0. Replaces the host-side use of
+ * the tensor in matmul_dequantized (dequantized_tensor.c:229-243). */
+int fl_cuda_upload_tensor(dequantized_tensor_t* t);
+
+/* Activation quantization of the reference (dequantized_tensor.c:112-135),
+ * optionally preceded by RMSNorm with unit weights (activations_avx2.c:
+ * 108-143): q[M, K] u8 from x[M, K] f32, device pointers. */
+int fl_cuda_act_quant(const float* x, uint8_t* q, int M, int K, int rmsnorm,
+                      float eps, void* stream);
+
+/* C[M, N] = A[M, K] @ B^T on device pointers: activation quantization, INT8
+ * dot products and the scale epilogue of matmul_dequantized
+ * (dequantized_tensor.c:204-247; block mode per dequantized_tensor.h).
+ * B must be uploaded. K % 32 == 0. Any M >= 1. */
+int fl_cuda_matmul_i8(const float* A, const dequantized_tensor_t* B, float* C,
+                      int M, int N, int K, void* stream);
+
+/* Same product from already-quantized activations Aq[M, K] (u8). */
+int fl_cuda_gemv_i8(const uint8_t* Aq, const dequantized_tensor_t* B, float* C,
+                    int M, int N, int K, void* stream);
+
+/* Per-(m, n, block) INT32 dot products of the quantized A row and the
+ * weight row over each 32-element block, D[M, N, K/32], computed by the same
+ * kernel as fl_cuda_matmul_i8 with its epilogue replaced by a store of the
+ * integers. Per-row-mode tensors use the pair-saturated reduction of
+ * dot_product_u8_i8 (dequantized_tensor.c:149-196) inside each block. */
+int fl_cuda_block_dots_i8(const float* A, const dequantized_tensor_t* B, int32_t* D,
+                          int M, int N, int K, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* seeded synthetic weights (the loader side; host code)               */
+/* ------------------------------------------------------------------ */
+
+/* Tensor ids name a weight of the model: stack 0 base, 1 draft, 2 Medusa
+ * heads, 3 shared; proj 0..6 = q, k, v, o, gate, up, down; shared proj 0 =
+ * embedding, 1 = LM head. */
+#define FL_TENSOR_ID(stack, layer, proj) \
+    ((uint32_t)(((stack) << 24) | ((layer) << 8) | (proj)))
+
+/* rows x cols values N(0, std) from Philox4x32-10 (key = seed, counter =
+ * (element/4, tensor_id)) and Box-Muller, quantized to GGUF Q4_0 blocks
+ * (ggml quantize_row_q4_0_ref rule), pre-dequantized to int8 q-8 in [-8, 7]
+ * plus one fp16 scale per 32 values. cols % 32 == 0. Multithreaded and
+ * deterministic. */
+int fl_synth_q4_0_i8(uint64_t seed, uint32_t tensor_id, int rows, int cols,
+                     float std, int8_t* w, uint16_t* d);
+
+/* Same values as fl_synth_q4_0_i8 dequantized to f32 ((q-8)*d), the
+ * form the reference loader keeps embeddings in (gguf_loader.c:147-161). */
+int fl_synth_q4_0_f32(uint64_t seed, uint32_t tensor_id, int rows, int cols,
+                      float std, float* out);
+
+/* Raw N(0, std) values of a tensor (before quantization). */
+int fl_synth_normal(uint64_t seed, uint32_t tensor_id, size_t count, float std,
+                    float* out);
+
+/* GGUF Q4_0 (18-byte blocks) -> int8 q-8 plus fp16 scales: the load-time
+ * pre-dequantization. Nibble order of gguf_loader.c:147-161. */
+int fl_q4_0_to_i8(const block_q4_0_gguf* blocks, int rows, int cols, int8_t* w,
+                  uint16_t* d);
+
+/* Philox4x32-10 block (Salmon et al. 2011), host copy of the device one. */
+void fl_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t out[4]);
+
+/* ------------------------------------------------------------------ */
+/* engine: base model + draft + Medusa heads resident in HBM           */
+/* ------------------------------------------------------------------ */
+
+typedef struct fl_engine fl_engine_t;
+
+typedef struct {
+    int vocab_size;          /* 32064 for Phi-3-mini                     */
+    int hidden_size;         /* d                                        */
+    int intermediate_size;   /* SwiGLU width                             */
+    int num_layers;          /* base decoder layers                      */
+    int num_heads;           /* query heads                              */
+    int num_kv_heads;        /* key/value heads (GQA when < num_heads)   */
+    int head_dim;
+    int draft_layers;        /* 0 = no draft                             */
+    int medusa_heads;        /* 0 = no Medusa heads                      */
+    int max_seq_len;         /* KV capacity per sequence (positions)     */
+    float rope_theta;
+    float norm_eps;
+} fl_model_config_t;
+
+fl_engine_t* fl_engine_create(const fl_model_config_t* cfg, int device);
+void fl_engine_destroy(fl_engine_t* e);
+
+/* Loads one INT8 linear from host arrays: stack/layer/proj as in
+ * FL_TENSOR_ID (stack 3 proj 1 = LM head; stack 2 layer h proj 0 = Medusa
+ * head h). w [rows, cols] int8 in [-8, 7], d [rows, cols/32] fp16 bits. */
+int fl_engine_load_linear(fl_engine_t* e, int stack, int layer, int proj,
+                          const int8_t* w, const uint16_t* d, int rows, int cols);
+/* Token embedding table [vocab, d] f32. */
+int fl_engine_load_embedding(fl_engine_t* e, const float* table);
+/* Generates and loads every tensor with fl_synth_* (std 0.02). */
+int fl_engine_synthesize(fl_engine_t* e, uint64_t seed);
+/* 1 when every tensor the configuration needs has been loaded. */
+int fl_engine_ready(const fl_engine_t* e);
+
+/* Runs M rows through a stack (0 base, 1 draft) at cache slots
+ * [base, base+M) with rotary positions pos[M] and visibility mask[M*M]
+ * (NULL = causal) over the new rows; slots [0, base) are visible to all.
+ * Host buffers: x_in/x_out [M, d]; logits [M, vocab] (NULL to skip). */
+int fl_engine_forward_rows(fl_engine_t* e, int stack, const float* x_in, int M,
+                           int base, const int* pos, const uint8_t* mask,
+                           float* x_out, float* logits);
+
+/* Greedy base-model decoding: prefill the prompt, emit n_new tokens. */
+int fl_engine_greedy_generate(fl_engine_t* e, const int* prompt, int prompt_len,
+                              int n_new, int* out);
+
+/* Greedy chain speculative decoding (include/speculative.h rule), k drafted
+ * tokens per step. out[n_new] tokens; acc_hist[steps] accepted counts (may
+ * be NULL; size >= n_new); *steps the number of steps (may be NULL). */
+int fl_engine_spec_generate(fl_engine_t* e, const int* prompt, int prompt_len,
+                            int n_new, int k, int max_accepted, int* out,
+                            int* acc_hist, int* steps);
+
+/* Split form for timing: prefill once, then decode from the saved
+ * post-prefill state as often as wanted (each decode restarts there). */
+int fl_engine_spec_prefill(fl_engine_t* e, const int* prompt, int prompt_len, int k,
+                           int max_accepted);
+int fl_engine_spec_decode(fl_engine_t* e, int n_new, int* out, int* acc_hist,
+                          int* steps);
+/* Per-stage device times of the last fl_engine_spec_decode (microseconds,
+ * summed over its steps): draft passes, verify passes, total. */
+int fl_engine_last_timing(const fl_engine_t* e, double* draft_us, double* verify_us,
+                          double* total_us);
+/* cudaStream_t (as void*) the engine launches on. */
+void* fl_engine_stream(const fl_engine_t* e);
+
+/* Callback-level position of the base cache: tokens appended through
+ * fl_cuda_target_forward / fl_cuda_base_forward land at this position.
+ * Setting it lower discards (rolls back) the later cache entries. */
+int fl_engine_position(const fl_engine_t* e);
+int fl_engine_set_position(fl_engine_t* e, int pos);
+/* Base feature F (last-layer output before the final norm) of the last
+ * token appended through the callbacks, [hidden_size] host floats. */
+int fl_engine_last_feature(const fl_engine_t* e, float* out);
+
+/* Single-row greedy draft chain: input hidden + E[tok] at draft position
+ * pos, K tokens out, each with its draft softmax probability. */
+int fl_engine_draft_chain(fl_engine_t* e, const float* hidden, int tok, int pos, int K,
+                          int* out_tokens, float* out_probs);
+
+/* Loads a draft_model_t's host tensors (block mode) into the engine's draft
+ * stack and binds it, so draft_tokens can run it. */
+int fl_engine_bind_draft(fl_engine_t* e, draft_model_t* draft);
+
+/* Vocabulary of the logits rows verify_tokens reads for this tree. */
+int fl_draft_tree_set_vocab(draft_tree_t* tree, int vocab);
+
+/* Callback of the reference's target_forward type (speculative.h:153)
+ * served by an fl_engine_t: input = len token ids as floats appended at the
+ * engine's next positions, output = logits [len, vocab]. */
+void fl_cuda_target_forward(void* model, const float* input, float* output, int len);
+
+/* Callback of the reference's base_forward type (medusa.h:143): tokens[len]
+ * appended, hidden = base feature F of the last token [hidden_size]. */
+void fl_cuda_base_forward(void* model, const int* tokens, int len, float* hidden,
+                          int hidden_size);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FL_CUDA_H */

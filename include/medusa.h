@@ -1,0 +1,140 @@
+/*
+ * Medusa multi-token prediction on B200.
+ *
+ * Same types, defaults and function signatures as the reference's medusa.h
+ * (fast_llm/include/medusa.h:32-229). The reference declares this API but
+ * ships no implementation; the behaviour below is this library's and the CPU
+ * oracle restates the same rules.
+ *
+ * Head i (0-based) predicts the token at offset i+2 from the last verified
+ * position (the base LM head itself predicts offset 1). A head is a residual
+ * block on the normalised base hidden state h = RMSNorm(F):
+ *     z_i = h + SiLU(W_i h),   logits_i = LM_head(z_i)
+ * with W_i an INT8 [hidden, hidden] tensor in medusa_head_t.weights and the
+ * base model's INT8 LM head shared by every head. SiLU uses the reference's
+ * polynomial sigmoid (activations_avx2.c:33-63). medusa_head_t.bias, when
+ * non-NULL, is added to W_i h before SiLU.
+ *
+ * Candidate tree: the root is the base model's next token; level L+1 holds
+ * the children proposed by head L for every level-L node. Each head keeps its
+ * top-k tokens (k per level from fl_medusa_set_topk, default config->top_k),
+ * a node's score is the product of its ancestors' softmax probabilities, and
+ * the tree is pruned to the max_candidates highest-scoring nodes (ties:
+ * shallower first, then lower head rank); a child never outscores its
+ * parent, so the kept set is ancestor-closed. Verification runs every node
+ * through the base model in one pass with a tree attention mask; the longest
+ * root-to-leaf path whose every token equals the base model's greedy choice
+ * at its parent is accepted, plus the base model's token after it.
+ */
+#ifndef FL_MEDUSA_H
+#define FL_MEDUSA_H
+
+#include <stdint.h>
+#include <stdbool.h>
+#include "dequantized_tensor.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct {
+    int num_heads;             /* number of Medusa heads                 */
+    int top_k;                 /* candidates kept per head (default k)   */
+    float temperature;         /* <= 0 greedy acceptance                 */
+} medusa_config_t;
+
+typedef struct {
+    dequantized_tensor_t* weights;   /* residual-block linear [hidden, hidden] */
+    float* bias;                     /* optional [hidden]                      */
+    int head_id;                     /* predicts offset head_id + 2            */
+    int hidden_size;
+    int vocab_size;
+} medusa_head_t;
+
+typedef struct {
+    medusa_head_t* heads;
+    int num_heads;
+    int hidden_size;
+    int vocab_size;
+} medusa_model_t;
+
+/* Candidate tree. Node 0 is the root; parent_indices[0] = -1. positions[i]
+ * is the node's depth (root 0); its sequence position is prefix + depth. */
+typedef struct {
+    int* tokens;
+    float* probs;
+    int* parent_indices;
+    int* positions;
+    int num_candidates;
+    int max_candidates;
+} medusa_tree_t;
+
+static inline medusa_config_t medusa_default_config(void) {
+    medusa_config_t cfg;
+    cfg.num_heads = 3;
+    cfg.top_k = 8;
+    cfg.temperature = 0.8f;
+    return cfg;
+}
+
+medusa_model_t* medusa_model_create(int num_heads, int hidden_size, int vocab_size);
+
+/* "synthetic:<seed>" fills every head with the seeded Q4_0 -> INT8 generator.
+ * Returns 0 on success, -1 otherwise. */
+int medusa_model_load(medusa_model_t* model, const char* path);
+void medusa_model_free(medusa_model_t* model);
+
+medusa_tree_t* medusa_tree_create(int max_candidates);
+void medusa_tree_free(medusa_tree_t* tree);
+
+/* Runs every head on hidden_state (host [hidden_size], the base feature F
+ * before the final norm) and builds the candidate tree rooted at
+ * current_token. The Medusa model must be bound to a base model
+ * (fl_engine_bind_medusa). Returns tree->num_candidates or -1. */
+int medusa_predict(medusa_model_t* model, const float* hidden_state,
+                   int current_token, medusa_tree_t* tree,
+                   const medusa_config_t* config);
+
+/* Same as medusa_predict with the root token taken from tree->tokens[0]. */
+int medusa_build_tree(medusa_model_t* model, const float* hidden_state,
+                      medusa_tree_t* tree, const medusa_config_t* config);
+
+/* Verifies the tree with one tree-masked base-model pass. base_model must be
+ * an fl_engine_t* and base_forward fl_cuda_base_forward. Writes the accepted
+ * tokens plus the base model's next token to accepted_tokens, the accepted
+ * count (excluding that last token) to *num_accepted, and returns it. */
+int medusa_verify_tree(void* base_model,
+                       void (*base_forward)(void*, const int*, int, float*, int),
+                       const medusa_tree_t* tree, int* accepted_tokens,
+                       int* num_accepted, const medusa_config_t* config);
+
+/* One predict + verify + accept step. Returns tokens produced (>= 1). */
+int medusa_decode_step(void* base_model,
+                       void (*base_forward)(void*, const int*, int, float*, int),
+                       medusa_model_t* medusa, const float* current_hidden,
+                       int current_token, int* output_tokens, int* num_output,
+                       const medusa_config_t* config);
+
+/* Prefill prompt_len float-encoded token ids, then Medusa steps until
+ * num_tokens new tokens exist. Returns the count written or -1. */
+int medusa_generate(void* base_model,
+                    void (*base_forward)(void*, const int*, int, float*, int),
+                    medusa_model_t* medusa, const float* prompt_hidden,
+                    int prompt_len, int* output_tokens, int num_tokens,
+                    const medusa_config_t* config);
+
+/* Draft + Medusa combination (reference medusa.h:210). Not provided by this
+ * library: returns -1 and records the reason. */
+int speculative_medusa_generate(void* draft_model,
+                                void (*draft_forward)(void*, const float*, float*, int),
+                                medusa_model_t* medusa, void* target_model,
+                                void (*target_forward)(void*, const int*, int, float*, int),
+                                const float* prompt_hidden, int prompt_len,
+                                int* output_tokens, int num_tokens,
+                                const medusa_config_t* config);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FL_MEDUSA_H */

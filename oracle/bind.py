@@ -1,0 +1,307 @@
+"""ctypes binding of the CPU oracle -- TEST INFRASTRUCTURE.
+
+Loads oracle/liboracle.so (the restatement) and, when present,
+oracle/_ref/libref.so (the reference's own sources compiled in place). Only
+tests/, the smoke() check and bench.py's CPU-baseline leg import this; the
+product library never does.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libref.so")
+
+VP, I, F = C.c_void_p, C.c_int, C.c_float
+
+
+def _p(a):
+    if a is None:
+        return None
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data
+
+
+class Dims(C.Structure):
+    _fields_ = [("vocab", I), ("d", I), ("ffn", I), ("layers", I), ("heads", I), ("kv_heads", I),
+                ("head_dim", I), ("theta", F), ("eps", F)]
+
+
+class Lin(C.Structure):
+    _fields_ = [("w", VP), ("s", VP), ("N", I), ("K", I), ("f32", VP)]
+
+
+class Layer(C.Structure):
+    _fields_ = [(n, Lin) for n in ("q", "k", "v", "o", "gate", "up", "down")]
+
+
+class Model(C.Structure):
+    _fields_ = [("dims", Dims), ("embed", VP), ("base", C.POINTER(Layer)), ("draft_layers", I),
+                ("draft", C.POINTER(Layer)), ("lm", Lin), ("n_medusa", I), ("medusa", C.POINTER(Lin))]
+
+
+class KV(C.Structure):
+    _fields_ = [("k", VP), ("v", VP), ("layers", I), ("cap", I), ("kv_heads", I), ("head_dim", I)]
+
+
+class Oracle:
+    def __init__(self, path: str = ORACLE_SO):
+        if not os.path.exists(path):
+            raise RuntimeError(f"{path} missing: make -C oracle")
+        self.so = C.CDLL(path)
+        s = self.so
+        s.orc_dot_pairsat.restype = C.c_int32
+        s.orc_dot_plain.restype = C.c_int32
+        s.orc_fast_sigmoid.restype = F
+        s.orc_fast_sigmoid.argtypes = [F]
+        s.orc_rmsnorm.argtypes = [VP, VP, I, F]
+        s.orc_rope_vec.argtypes = [VP, I, I, I, F]
+        s.orc_f16_to_f32.restype = F
+        s.orc_f16_to_f32.argtypes = [C.c_uint16]
+        s.orc_f32_to_f16.restype = C.c_uint16
+        s.orc_f32_to_f16.argtypes = [F]
+        s.orc_argmax.restype = I
+        s.orc_spec_generate.restype = I
+        s.orc_kv_init.restype = I
+        s.orc_stack_forward.argtypes = [C.POINTER(Model), C.POINTER(Layer), I, C.POINTER(KV), VP, I, I, VP, VP]
+        s.orc_lm_logits.argtypes = [C.POINTER(Model), VP, VP, I]
+        s.orc_kv_init.argtypes = [C.POINTER(KV), I, I, I, I]
+        s.orc_kv_free.argtypes = [C.POINTER(KV)]
+        s.orc_spec_generate.argtypes = [C.POINTER(Model), VP, I, I, I, I, VP, VP, VP]
+        s.orc_greedy_generate.argtypes = [C.POINTER(Model), VP, I, I, VP, VP]
+
+    # ----------------------------------------------------------- primitives
+    def quant_u8(self, x):
+        x = np.ascontiguousarray(x, np.float32)
+        q = np.empty(x.shape, np.uint8)
+        self.so.orc_quant_u8(_p(x), _p(q), x.size)
+        return q
+
+    def dot_pairsat(self, a, w):
+        return self.so.orc_dot_pairsat(_p(a), _p(w), a.size)
+
+    def matmul_rowscale(self, A, W, s):
+        M, K = A.shape
+        N = W.shape[0]
+        Cm = np.empty((M, N), np.float32)
+        self.so.orc_matmul_rowscale(_p(A), _p(W), _p(s), _p(Cm), M, N, K)
+        return Cm
+
+    def matmul_block(self, A, W, d):
+        A = np.ascontiguousarray(A, np.float32)
+        M, K = A.shape
+        N = W.shape[0]
+        Cm = np.empty((M, N), np.float32)
+        self.so.orc_matmul_block(_p(A), _p(W), _p(d), _p(Cm), M, N, K)
+        return Cm
+
+    def block_dots(self, A, W):
+        A = np.ascontiguousarray(A, np.float32)
+        M, K = A.shape
+        N = W.shape[0]
+        D = np.empty((M, N, K // 32), np.int32)
+        self.so.orc_block_dots(_p(A), _p(W), _p(D), M, N, K)
+        return D
+
+    def rmsnorm(self, x, eps=1e-5):
+        x = np.ascontiguousarray(x, np.float32)
+        o = np.empty_like(x)
+        self.so.orc_rmsnorm(_p(x), _p(o), x.size, eps)
+        return o
+
+    def swiglu(self, g, u):
+        g = np.ascontiguousarray(g, np.float32)
+        u = np.ascontiguousarray(u, np.float32)
+        o = np.empty_like(g)
+        self.so.orc_swiglu(_p(g), _p(u), _p(o), g.size)
+        return o
+
+    def silu(self, x):
+        x = np.ascontiguousarray(x, np.float32)
+        o = np.empty_like(x)
+        self.so.orc_silu(_p(x), _p(o), x.size)
+        return o
+
+    def rope_vec(self, v, heads, head_dim, pos, theta):
+        v = np.array(v, np.float32, copy=True)
+        self.so.orc_rope_vec(_p(v), heads, head_dim, pos, theta)
+        return v
+
+    def q4_0_i8(self, x):
+        x = np.ascontiguousarray(x, np.float32)
+        w = np.empty(x.size, np.int8)
+        d = np.empty(x.size // 32, np.uint16)
+        self.so.orc_q4_0_quantize_i8(_p(x), x.size, _p(w), _p(d))
+        return w, d
+
+    def philox(self, ctr, key):
+        c = np.asarray(ctr, np.uint32)
+        k = np.asarray(key, np.uint32)
+        o = np.empty(4, np.uint32)
+        self.so.orc_philox4x32_10(_p(c), _p(k), _p(o))
+        return o
+
+
+class OracleModel:
+    """Oracle model over numpy weights. `w` maps (stack, layer, proj) to
+    (int8 [N,K], fp16 bits [N,K/32]); stack 3 proj 1 = LM head."""
+
+    def __init__(self, orc: Oracle, dims: dict, embed, w, draft_layers=0, n_medusa=0, f32=None):
+        self.orc = orc
+        self.keep = [embed]
+        self.m = Model()
+        D = self.m.dims
+        for k in ("vocab", "d", "ffn", "layers", "heads", "kv_heads", "head_dim", "theta", "eps"):
+            setattr(D, k, dims[k])
+        self.m.embed = _p(embed)
+
+        def lin(key):
+            L = Lin()
+            if f32 is not None and key in f32:
+                a = np.ascontiguousarray(f32[key], np.float32)
+                self.keep.append(a)
+                L.f32 = _p(a)
+                L.N, L.K = a.shape
+                return L
+            wq, dq = w[key]
+            self.keep += [wq, dq]
+            L.w, L.s = _p(wq), _p(dq)
+            L.N, L.K = wq.shape
+            return L
+
+        def stack(s, n):
+            arr = (Layer * max(n, 1))()
+            for l in range(n):
+                for pi, name in enumerate(("q", "k", "v", "o", "gate", "up", "down")):
+                    setattr(arr[l], name, lin((s, l, pi)))
+            self.keep.append(arr)
+            return arr
+
+        self.m.base = stack(0, dims["layers"])
+        self.m.draft_layers = draft_layers
+        self.m.draft = stack(1, draft_layers)
+        self.m.lm = lin((3, 0, 1))
+        self.m.n_medusa = n_medusa
+        med = (Lin * max(n_medusa, 1))()
+        for h in range(n_medusa):
+            med[h] = lin((2, h, 0))
+        self.keep.append(med)
+        self.m.medusa = med
+
+    def kv(self, layers, cap):
+        kv = KV()
+        self.orc.so.orc_kv_init(C.byref(kv), layers, cap, self.m.dims.kv_heads, self.m.dims.head_dim)
+        return kv
+
+    def stack_forward(self, stack, kv, x, base, pos, mask=None):
+        x = np.array(x, np.float32, copy=True)
+        pos = np.ascontiguousarray(pos, np.int32)
+        mk = None if mask is None else np.ascontiguousarray(mask, np.uint8)
+        layers = self.m.base if stack == 0 else self.m.draft
+        n = self.m.dims.layers if stack == 0 else self.m.draft_layers
+        self.orc.so.orc_stack_forward(C.byref(self.m), layers, n, C.byref(kv), _p(x), x.shape[0], base, _p(pos),
+                                      _p(mk))
+        return x
+
+    def lm_logits(self, x):
+        x = np.ascontiguousarray(x, np.float32)
+        lg = np.empty((x.shape[0], self.m.dims.vocab), np.float32)
+        self.orc.so.orc_lm_logits(C.byref(self.m), _p(x), _p(lg), x.shape[0])
+        return lg
+
+    def greedy(self, prompt, n_new):
+        p = np.ascontiguousarray(prompt, np.int32)
+        o = np.empty(n_new, np.int32)
+        mg = np.empty(n_new, np.float32)
+        self.orc.so.orc_greedy_generate(C.byref(self.m), _p(p), len(p), n_new, _p(o), _p(mg))
+        return o, mg
+
+    def spec(self, prompt, n_new, k, max_acc=None):
+        p = np.ascontiguousarray(prompt, np.int32)
+        o = np.empty(n_new, np.int32)
+        acc = np.zeros(n_new + 1, np.int32)
+        mg = np.empty(n_new, np.float32)
+        steps = self.orc.so.orc_spec_generate(C.byref(self.m), _p(p), len(p), k, k if max_acc is None else max_acc,
+                                              n_new, _p(o), _p(acc), _p(mg))
+        return o, acc[:steps], mg
+
+
+class Ref:
+    """The reference's own functions (oracle/_ref/libref.so)."""
+
+    def __init__(self, path: str = REF_SO):
+        if not os.path.exists(path):
+            raise RuntimeError(f"{path} missing: make -C oracle (needs the reference sources)")
+        self.so = C.CDLL(path)
+        s = self.so
+        s.ref_dot_product_u8_i8.restype = C.c_int32
+        s.ref_rms_norm.argtypes = [VP, VP, I, F]
+        s.ref_apply_rope.argtypes = [VP, VP, I, I, I, I, F]
+        s.ref_model_forward_f32.restype = I
+
+    def quant_u8(self, x):
+        x = np.ascontiguousarray(x, np.float32)
+        q = np.empty(x.shape, np.uint8)
+        self.so.ref_quantize_to_uint8(_p(x), _p(q), x.size)
+        return q
+
+    def dot(self, a, w):
+        return self.so.ref_dot_product_u8_i8(_p(a), _p(w), a.size)
+
+    def matmul_dequantized(self, A, W, s):
+        A = np.ascontiguousarray(A, np.float32)
+        M, K = A.shape
+        N = W.shape[0]
+        Cm = np.empty((M, N), np.float32)
+        self.so.ref_matmul_dequantized(_p(A), _p(W), _p(s), _p(Cm), M, N, K)
+        return Cm
+
+    def rms_norm(self, x, eps=1e-5):
+        x = np.ascontiguousarray(x, np.float32)
+        o = np.empty_like(x)
+        self.so.ref_rms_norm(_p(x), _p(o), x.size, eps)
+        return o
+
+    def swiglu(self, g, u):
+        o = np.empty_like(g)
+        self.so.ref_swiglu(_p(g), _p(u), _p(o), g.size)
+        return o
+
+    def silu(self, x):
+        o = np.empty_like(x)
+        self.so.ref_silu(_p(x), _p(o), x.size)
+        return o
+
+    def apply_rope(self, q, k, seq, heads, kv_heads, hd, theta):
+        q = np.array(q, np.float32, copy=True)
+        k = np.array(k, np.float32, copy=True)
+        self.so.ref_apply_rope(_p(q), _p(k), seq, heads, kv_heads, hd, theta)
+        return q, k
+
+    def compute_attention(self, Q, K, V, seq, heads, kv_heads, hd):
+        Q = np.array(Q, np.float32, copy=True)
+        K = np.array(K, np.float32, copy=True)
+        V = np.ascontiguousarray(V, np.float32)
+        out = np.empty((seq, heads * hd), np.float32)
+        self.so.ref_compute_attention(_p(Q), _p(K), _p(V), _p(out), seq, heads, kv_heads, hd)
+        return out
+
+    def model_forward_f32(self, dims, embed, layers_w, lm, tokens):
+        """layers_w: list of 7-tuples of f32 [out, in] arrays per layer."""
+        ptrs = (VP * (7 * len(layers_w)))()
+        keep = []
+        for l, lw in enumerate(layers_w):
+            for j, a in enumerate(lw):
+                a = np.ascontiguousarray(a, np.float32)
+                keep.append(a)
+                ptrs[7 * l + j] = _p(a)
+        toks = np.ascontiguousarray(tokens, np.int32)
+        logits = np.empty(dims["vocab"], np.float32)
+        tok = self.so.ref_model_forward_f32(dims["vocab"], dims["d"], dims["ffn"], len(layers_w), dims["heads"],
+                                            dims["kv_heads"], dims["head_dim"], VP(_p(embed)), ptrs, VP(_p(lm)),
+                                            VP(_p(toks)), len(toks), VP(_p(logits)))
+        return tok, logits

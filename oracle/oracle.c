@@ -1,0 +1,556 @@
+/*
+ * CPU oracle for the speculative-decoding hot path -- TEST INFRASTRUCTURE.
+ * Used only by tests/, the smoke() check and the CPU-baseline leg of
+ * bench.py, never by the product library. See oracle.h for the contract.
+ *
+ * Build: oracle/Makefile (-O2 -mavx2 -mfma -fopenmp -ffp-contract=off: every
+ * float operation happens in the order written here; FMAs only where the
+ * reference issues one explicitly).
+ */
+#include "oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+#include <float.h>
+#include <immintrin.h>
+
+/* ------------------------------------------------------------------ */
+/* fp16 conversion (IEEE binary16)                                     */
+/* ------------------------------------------------------------------ */
+
+float orc_f16_to_f32(uint16_t h) {
+    uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    uint32_t exp = (h >> 10) & 0x1Fu;
+    uint32_t man = h & 0x3FFu;
+    uint32_t bits;
+    if (exp == 0) {
+        if (man == 0) {
+            bits = sign;
+        } else { /* subnormal: renormalise */
+            int e = -1;
+            do { man <<= 1; e++; } while ((man & 0x400u) == 0);
+            man &= 0x3FFu;
+            bits = sign | ((uint32_t)(127 - 15 - e) << 23) | (man << 13);
+        }
+    } else if (exp == 31) {
+        bits = sign | 0x7F800000u | (man << 13);
+    } else {
+        bits = sign | ((exp + 127 - 15) << 23) | (man << 13);
+    }
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+uint16_t orc_f32_to_f16(float f) {
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    uint32_t sign = (x >> 16) & 0x8000u;
+    uint32_t absx = x & 0x7FFFFFFFu;
+    if (absx >= 0x7F800000u) /* inf / nan */
+        return (uint16_t)(sign | 0x7C00u | (absx > 0x7F800000u ? 0x200u : 0u));
+    if (absx >= 0x477FF000u) /* rounds to >= 65520: inf */
+        return (uint16_t)(sign | 0x7C00u);
+    uint32_t e = absx >> 23;
+    uint32_t m = (absx & 0x7FFFFFu) | 0x800000u;
+    uint32_t shift, q;
+    if (absx < 0x38800000u) {          /* half subnormal: q = |f| / 2^-24 */
+        if (absx < 0x33000000u) return (uint16_t)sign;
+        shift = 126u - e;              /* 14 .. 24 */
+        q = m >> shift;
+    } else {                           /* half normal */
+        shift = 13u;
+        q = ((e - 112u) << 10) | ((m & 0x7FFFFFu) >> 13);
+    }
+    uint32_t rem = m & ((1u << shift) - 1u);
+    uint32_t half = 1u << (shift - 1u);
+    if (rem > half || (rem == half && (q & 1u))) q++;
+    return (uint16_t)(sign | q);
+}
+
+/* ------------------------------------------------------------------ */
+/* activation quantization and dots                                    */
+/* ------------------------------------------------------------------ */
+
+/* cvtps2dq: round to nearest even; NaN or |v| >= 2^31 -> INT32_MIN. */
+static inline int32_t cvt_rne_x86(float v) {
+    if (!(v > -2147483648.0f && v < 2147483648.0f)) return INT32_MIN;
+    return (int32_t)nearbyintf(v);
+}
+
+static inline uint8_t quant_one(float x) {
+    int32_t i = cvt_rne_x86(fmaf(x, 127.0f, 128.0f));
+    /* packs_epi32 saturates to int16, packus_epi16 to [0, 255]. */
+    if (i < -32768) i = -32768;
+    if (i > 32767) i = 32767;
+    if (i < 0) i = 0;
+    if (i > 255) i = 255;
+    return (uint8_t)i;
+}
+
+void orc_quant_u8(const float* x, uint8_t* q, int n) {
+    for (int i = 0; i < n; i++) q[i] = quant_one(x[i]);
+}
+
+int32_t orc_dot_pairsat(const uint8_t* a, const int8_t* w, int n) {
+    int32_t s = 0;
+    for (int j = 0; j < n; j += 2) {
+        int32_t p = (int32_t)a[j] * w[j] + (int32_t)a[j + 1] * w[j + 1];
+        if (p > 32767) p = 32767;
+        if (p < -32768) p = -32768;
+        s += p;
+    }
+    return s;
+}
+
+int32_t orc_dot_plain(const uint8_t* a, const int8_t* w, int n) {
+    int32_t s = 0;
+    for (int j = 0; j < n; j++) s += (int32_t)a[j] * w[j];
+    return s;
+}
+
+/* AVX2 block dot (32 bytes): maddubs (pair-saturating) + madd + hsum. The
+ * pair sums of [-8,7] weights never saturate, so this equals the plain dot. */
+static inline int32_t block_dot32(const uint8_t* a, const int8_t* w) {
+    __m256i va = _mm256_loadu_si256((const __m256i*)a);
+    __m256i vw = _mm256_loadu_si256((const __m256i*)w);
+    __m256i p16 = _mm256_maddubs_epi16(va, vw);
+    __m256i p32 = _mm256_madd_epi16(p16, _mm256_set1_epi16(1));
+    __m128i s = _mm_add_epi32(_mm256_castsi256_si128(p32), _mm256_extracti128_si256(p32, 1));
+    s = _mm_hadd_epi32(s, s);
+    s = _mm_hadd_epi32(s, s);
+    return _mm_cvtsi128_si32(s);
+}
+
+void orc_matmul_rowscale(const float* A, const int8_t* W, const float* scales,
+                         float* C, int M, int N, int K) {
+    uint8_t* q = (uint8_t*)malloc((size_t)M * K);
+    for (int m = 0; m < M; m++) orc_quant_u8(A + (size_t)m * K, q + (size_t)m * K, K);
+#pragma omp parallel for schedule(static)
+    for (int n = 0; n < N; n++) {
+        const int8_t* wr = W + (size_t)n * K;
+        for (int m = 0; m < M; m++) {
+            int32_t dot = orc_dot_pairsat(q + (size_t)m * K, wr, K);
+            /* the reference's `/ (127 * 16.0f)` compiled with -ffast-math is a
+             * multiply by the rounded reciprocal (bit-exact with libref). */
+            C[(size_t)m * N + n] = ((float)dot * scales[n]) * (1.0f / 2032.0f);
+        }
+    }
+    free(q);
+}
+
+static void matmul_block_q(const uint8_t* q, const int8_t* W, const uint16_t* S,
+                           float* C, int M, int N, int K) {
+    const int nb = K / 32;
+#pragma omp parallel for schedule(static)
+    for (int n = 0; n < N; n++) {
+        const int8_t* wr = W + (size_t)n * K;
+        const uint16_t* sr = S + (size_t)n * nb;
+        for (int m = 0; m < M; m++) {
+            const uint8_t* qa = q + (size_t)m * K;
+            float acc = 0.0f;
+            for (int b = 0; b < nb; b++) {
+                int32_t dot = block_dot32(qa + 32 * b, wr + 32 * b);
+                float t = (float)dot * orc_f16_to_f32(sr[b]);
+                acc = acc + t;
+            }
+            C[(size_t)m * N + n] = acc / 127.0f;
+        }
+    }
+}
+
+void orc_matmul_block(const float* A, const int8_t* W, const uint16_t* scales,
+                      float* C, int M, int N, int K) {
+    uint8_t* q = (uint8_t*)malloc((size_t)M * K);
+    for (int m = 0; m < M; m++) orc_quant_u8(A + (size_t)m * K, q + (size_t)m * K, K);
+    matmul_block_q(q, W, scales, C, M, N, K);
+    free(q);
+}
+
+void orc_block_dots(const float* A, const int8_t* W, int32_t* D, int M, int N, int K) {
+    const int nb = K / 32;
+    uint8_t* q = (uint8_t*)malloc((size_t)M * K);
+    for (int m = 0; m < M; m++) orc_quant_u8(A + (size_t)m * K, q + (size_t)m * K, K);
+    for (int m = 0; m < M; m++)
+        for (int n = 0; n < N; n++)
+            for (int b = 0; b < nb; b++)
+                D[((size_t)m * N + n) * nb + b] =
+                    orc_dot_pairsat(q + (size_t)m * K + 32 * b, W + (size_t)n * K + 32 * b, 32);
+    free(q);
+}
+
+/* ------------------------------------------------------------------ */
+/* norm / activations / rope                                           */
+/* ------------------------------------------------------------------ */
+
+void orc_rmsnorm(const float* x, float* out, int n, float eps) {
+    float lane[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int i = 0;
+    for (; i <= n - 8; i += 8)
+        for (int j = 0; j < 8; j++) lane[j] = fmaf(x[i + j], x[i + j], lane[j]);
+    /* Horizontal sum in the order the reference build reduces the vector
+     * (high/low 128-bit halves, then pairs). The reference binary computes
+     * 1/sqrtf with rsqrtss plus one Newton step under -ffast-math, which is
+     * CPU-model dependent; the exact expression of the source is used here
+     * and the two agree within a few ulp. */
+    float s = ((lane[0] + lane[4]) + (lane[2] + lane[6])) + ((lane[1] + lane[5]) + (lane[3] + lane[7]));
+    for (; i < n; i++) s += x[i] * x[i];
+    float scale = 1.0f / sqrtf(s / (float)n + eps);
+    for (i = 0; i < n; i++) out[i] = x[i] * scale;
+}
+
+float orc_fast_sigmoid(float x) {
+    x = fmaxf(-10.0f, fminf(10.0f, x));
+    float nx = 0.0f - x;
+    float x2 = x * x;
+    float x3 = x2 * x;
+    float x4 = x2 * x2;
+    float p = 1.0f + (nx + (x2 * 0.5f + (x3 * -0.166667f + x4 * 0.041667f)));
+    return 1.0f / (1.0f + p);
+}
+
+void orc_swiglu(const float* g, const float* u, float* out, int n) {
+    for (int i = 0; i < n; i++) {
+        float s = orc_fast_sigmoid(g[i]);
+        out[i] = (g[i] * s) * u[i];
+    }
+}
+
+void orc_silu(const float* x, float* out, int n) {
+    for (int i = 0; i < n; i++) out[i] = x[i] * orc_fast_sigmoid(x[i]);
+}
+
+void orc_rope_vec(float* v, int heads, int head_dim, int pos, float theta) {
+    for (int h = 0; h < heads; h++) {
+        float* p = v + (size_t)h * head_dim;
+        for (int i = 0; i < head_dim; i += 2) {
+            float freq = 1.0f / powf(theta, (float)i / (float)head_dim);
+            float ang = (float)pos * freq;
+            float c = cosf(ang), s = sinf(ang);
+            float a = p[i], b = p[i + 1];
+            p[i] = a * c - b * s;
+            p[i + 1] = a * s + b * c;
+        }
+    }
+}
+
+/* ------------------------------------------------------------------ */
+/* Q4_0 and Philox                                                     */
+/* ------------------------------------------------------------------ */
+
+void orc_q4_0_quantize_i8(const float* x, int n, int8_t* w, uint16_t* d) {
+    for (int b = 0; b < n / 32; b++) {
+        const float* xb = x + 32 * b;
+        float amax = 0.0f, vmax = 0.0f;
+        for (int j = 0; j < 32; j++) {
+            float a = fabsf(xb[j]);
+            if (amax < a) { amax = a; vmax = xb[j]; }
+        }
+        float dd = vmax / -8.0f;
+        float id = dd != 0.0f ? 1.0f / dd : 0.0f;
+        d[b] = orc_f32_to_f16(dd);
+        for (int j = 0; j < 32; j++) {
+            int q = (int)(int8_t)(xb[j] * id + 8.5f);
+            if (q > 15) q = 15;
+            w[32 * b + j] = (int8_t)(q - 8);
+        }
+    }
+}
+
+static inline void mulhilo32(uint32_t a, uint32_t b, uint32_t* hi, uint32_t* lo) {
+    uint64_t p = (uint64_t)a * b;
+    *hi = (uint32_t)(p >> 32);
+    *lo = (uint32_t)p;
+}
+
+void orc_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t out[4]) {
+    uint32_t c0 = ctr[0], c1 = ctr[1], c2 = ctr[2], c3 = ctr[3];
+    uint32_t k0 = key[0], k1 = key[1];
+    for (int r = 0; r < 10; r++) {
+        uint32_t hi0, lo0, hi1, lo1;
+        mulhilo32(0xD2511F53u, c0, &hi0, &lo0);
+        mulhilo32(0xCD9E8D57u, c2, &hi1, &lo1);
+        uint32_t n0 = hi1 ^ c1 ^ k0, n1 = lo1, n2 = hi0 ^ c3 ^ k1, n3 = lo0;
+        c0 = n0; c1 = n1; c2 = n2; c3 = n3;
+        k0 += 0x9E3779B9u;
+        k1 += 0xBB67AE85u;
+    }
+    out[0] = c0; out[1] = c1; out[2] = c2; out[3] = c3;
+}
+
+/* ------------------------------------------------------------------ */
+/* model                                                               */
+/* ------------------------------------------------------------------ */
+
+int orc_kv_init(orc_kv_t* kv, int layers, int cap, int kv_heads, int head_dim) {
+    size_t n = (size_t)layers * cap * kv_heads * head_dim;
+    kv->k = (float*)calloc(n, sizeof(float));
+    kv->v = (float*)calloc(n, sizeof(float));
+    kv->layers = layers; kv->cap = cap; kv->kv_heads = kv_heads; kv->head_dim = head_dim;
+    return (kv->k && kv->v) ? 0 : -1;
+}
+
+void orc_kv_free(orc_kv_t* kv) {
+    free(kv->k); free(kv->v);
+    kv->k = kv->v = NULL;
+}
+
+static void lin(const orc_lin_t* L, const float* x, float* y, int M) {
+    if (L->f32) { /* inference.c:131-141 */
+        for (int m = 0; m < M; m++)
+            for (int o = 0; o < L->N; o++) {
+                const float* row = L->f32 + (size_t)o * L->K;
+                const float* in = x + (size_t)m * L->K;
+                float s = 0.0f;
+                for (int i = 0; i < L->K; i++) s += in[i] * row[i];
+                y[(size_t)m * L->N + o] = s;
+            }
+        return;
+    }
+    orc_matmul_block(x, L->w, L->s, y, M, L->N, L->K);
+}
+
+/* inference.c:193-247 for one query row against the visible cache slots. */
+static void attend_row(const float* q, const float* Kc, const float* Vc, int kvh, int hd,
+                       int stride, const int* slots, int ns, float* out, float* sc) {
+    float scale = 1.0f / sqrtf((float)hd);
+    for (int t = 0; t < ns; t++) {
+        const float* kk = Kc + (size_t)slots[t] * stride + (size_t)kvh * hd;
+        float dot = 0.0f;
+        for (int e = 0; e < hd; e++) dot += q[e] * kk[e];
+        sc[t] = dot * scale;
+    }
+    float mx = sc[0];
+    for (int t = 1; t < ns; t++) if (sc[t] > mx) mx = sc[t];
+    float sum = 0.0f;
+    for (int t = 0; t < ns; t++) { sc[t] = expf(sc[t] - mx); sum += sc[t]; }
+    for (int t = 0; t < ns; t++) sc[t] /= sum;
+    for (int e = 0; e < hd; e++) {
+        float acc = 0.0f;
+        for (int t = 0; t < ns; t++)
+            acc += sc[t] * Vc[(size_t)slots[t] * stride + (size_t)kvh * hd + e];
+        out[e] = acc;
+    }
+}
+
+void orc_stack_forward(const orc_model_t* mdl, const orc_layer_t* layers, int n_layers,
+                       orc_kv_t* kv, float* x, int M, int base, const int* pos,
+                       const uint8_t* mask) {
+    const orc_dims_t* D = &mdl->dims;
+    const int d = D->d, H = D->heads, Hk = D->kv_heads, hd = D->head_dim, F = D->ffn;
+    const int qd = H * hd, kd = Hk * hd, grp = H / Hk;
+    float* nrm = (float*)malloc(sizeof(float) * (size_t)M * d);
+    float* q = (float*)malloc(sizeof(float) * (size_t)M * qd);
+    float* k = (float*)malloc(sizeof(float) * (size_t)M * kd);
+    float* v = (float*)malloc(sizeof(float) * (size_t)M * kd);
+    float* att = (float*)malloc(sizeof(float) * (size_t)M * qd);
+    float* o = (float*)malloc(sizeof(float) * (size_t)M * d);
+    float* g = (float*)malloc(sizeof(float) * (size_t)M * F);
+    float* u = (float*)malloc(sizeof(float) * (size_t)M * F);
+    int* slots_all = (int*)malloc(sizeof(int) * (size_t)M * (base + M));
+    int* nslots = (int*)malloc(sizeof(int) * M);
+    for (int m = 0; m < M; m++) {
+        int* s = slots_all + (size_t)m * (base + M);
+        int c = 0;
+        for (int t = 0; t < base; t++) s[c++] = t;
+        for (int j = 0; j < M; j++) {
+            int vis = mask ? mask[(size_t)m * M + j] != 0 : (j <= m);
+            if (vis) s[c++] = base + j;
+        }
+        nslots[m] = c;
+    }
+    const int stride = kd;
+    for (int l = 0; l < n_layers; l++) {
+        const orc_layer_t* L = &layers[l];
+        float* Kc = kv->k + (size_t)l * kv->cap * kd;
+        float* Vc = kv->v + (size_t)l * kv->cap * kd;
+        for (int m = 0; m < M; m++) orc_rmsnorm(x + (size_t)m * d, nrm + (size_t)m * d, d, D->eps);
+        lin(&L->q, nrm, q, M);
+        lin(&L->k, nrm, k, M);
+        lin(&L->v, nrm, v, M);
+        for (int m = 0; m < M; m++) {
+            orc_rope_vec(q + (size_t)m * qd, H, hd, pos[m], D->theta);
+            orc_rope_vec(k + (size_t)m * kd, Hk, hd, pos[m], D->theta);
+            memcpy(Kc + (size_t)(base + m) * kd, k + (size_t)m * kd, sizeof(float) * kd);
+            memcpy(Vc + (size_t)(base + m) * kd, v + (size_t)m * kd, sizeof(float) * kd);
+        }
+#pragma omp parallel
+        {
+            float* sc = (float*)malloc(sizeof(float) * (size_t)(base + M));
+#pragma omp for collapse(2) schedule(static)
+            for (int m = 0; m < M; m++)
+                for (int h = 0; h < H; h++)
+                    attend_row(q + (size_t)m * qd + (size_t)h * hd, Kc, Vc, h / grp, hd, stride,
+                               slots_all + (size_t)m * (base + M), nslots[m],
+                               att + (size_t)m * qd + (size_t)h * hd, sc);
+            free(sc);
+        }
+        lin(&L->o, att, o, M);
+        for (size_t i = 0; i < (size_t)M * d; i++) x[i] = x[i] + o[i];
+        for (int m = 0; m < M; m++) orc_rmsnorm(x + (size_t)m * d, nrm + (size_t)m * d, d, D->eps);
+        lin(&L->gate, nrm, g, M);
+        lin(&L->up, nrm, u, M);
+        for (int m = 0; m < M; m++) orc_swiglu(g + (size_t)m * F, u + (size_t)m * F, g + (size_t)m * F, F);
+        lin(&L->down, g, o, M);
+        for (size_t i = 0; i < (size_t)M * d; i++) x[i] = x[i] + o[i];
+    }
+    free(nrm); free(q); free(k); free(v); free(att); free(o); free(g); free(u);
+    free(slots_all); free(nslots);
+}
+
+void orc_lm_logits(const orc_model_t* mdl, const float* x, float* logits, int M) {
+    const int d = mdl->dims.d;
+    float* nrm = (float*)malloc(sizeof(float) * (size_t)M * d);
+    for (int m = 0; m < M; m++) orc_rmsnorm(x + (size_t)m * d, nrm + (size_t)m * d, d, mdl->dims.eps);
+    lin(&mdl->lm, nrm, logits, M);
+    free(nrm);
+}
+
+/* inference.c:421-422: ids at or above the vocabulary read row 0. */
+static inline int tok_or_zero(int t, int vocab) { return (t < 0 || t >= vocab) ? 0 : t; }
+
+int orc_argmax(const float* v, int n) {
+    int bi = 0;
+    float bv = v[0];
+    for (int i = 1; i < n; i++)
+        if (v[i] > bv) { bv = v[i]; bi = i; }
+    return bi;
+}
+
+/* (top1 - top2) / |top1|: the relative margin of the greedy choice. */
+static float top2_margin(const float* v, int n) {
+    float a = -FLT_MAX, b = -FLT_MAX;
+    for (int i = 0; i < n; i++) {
+        if (v[i] > a) { b = a; a = v[i]; }
+        else if (v[i] > b) b = v[i];
+    }
+    float s = fabsf(a) > 1e-30f ? fabsf(a) : 1e-30f;
+    return (a - b) / s;
+}
+
+void orc_greedy_generate(const orc_model_t* mdl, const int* prompt, int P, int n_new,
+                         int* out, float* margins) {
+    const orc_dims_t* D = &mdl->dims;
+    const int d = D->d, V = D->vocab;
+    orc_kv_t kv;
+    orc_kv_init(&kv, D->layers, P + n_new + 1, D->kv_heads, D->head_dim);
+    float* x = (float*)malloc(sizeof(float) * (size_t)P * d);
+    float* lg = (float*)malloc(sizeof(float) * V);
+    int* pos = (int*)malloc(sizeof(int) * P);
+    for (int i = 0; i < P; i++) {
+        memcpy(x + (size_t)i * d, mdl->embed + (size_t)tok_or_zero(prompt[i], V) * d, sizeof(float) * d);
+        pos[i] = i;
+    }
+    orc_stack_forward(mdl, mdl->base, D->layers, &kv, x, P, 0, pos, NULL);
+    orc_lm_logits(mdl, x + (size_t)(P - 1) * d, lg, 1);
+    int cur = orc_argmax(lg, V);
+    out[0] = cur;
+    if (margins) margins[0] = top2_margin(lg, V);
+    for (int i = 1; i < n_new; i++) {
+        int p = P + i - 1;
+        memcpy(x, mdl->embed + (size_t)cur * d, sizeof(float) * d);
+        orc_stack_forward(mdl, mdl->base, D->layers, &kv, x, 1, p, &p, NULL);
+        orc_lm_logits(mdl, x, lg, 1);
+        cur = orc_argmax(lg, V);
+        out[i] = cur;
+        if (margins) margins[i] = top2_margin(lg, V);
+    }
+    free(x); free(lg); free(pos);
+    orc_kv_free(&kv);
+}
+
+int orc_spec_generate(const orc_model_t* mdl, const int* prompt, int P, int K,
+                      int max_acc, int n_new, int* out, int* acc_hist, float* margins) {
+    const orc_dims_t* D = &mdl->dims;
+    const int d = D->d, V = D->vocab;
+    const int cap = P + n_new + K + 2;
+    orc_kv_t kvb, kvd;
+    orc_kv_init(&kvb, D->layers, cap, D->kv_heads, D->head_dim);
+    orc_kv_init(&kvd, mdl->draft_layers, cap, D->kv_heads, D->head_dim);
+    int* seq = (int*)malloc(sizeof(int) * (size_t)(cap + 1));
+    const int rows_max = (P + 1 > K + 1) ? P + 1 : K + 1;
+    float* x = (float*)malloc(sizeof(float) * (size_t)rows_max * d);
+    float* feat = (float*)malloc(sizeof(float) * (size_t)rows_max * d); /* F_{m-1}.. */
+    float* lg = (float*)malloc(sizeof(float) * (size_t)(K + 1) * V);
+    int* pos = (int*)malloc(sizeof(int) * rows_max);
+    int* drafted = (int*)malloc(sizeof(int) * (K + 1));
+
+    for (int i = 0; i < P; i++) seq[i] = tok_or_zero(prompt[i], V);
+    /* prefill */
+    for (int i = 0; i < P; i++) {
+        memcpy(x + (size_t)i * d, mdl->embed + (size_t)seq[i] * d, sizeof(float) * d);
+        pos[i] = i;
+    }
+    orc_stack_forward(mdl, mdl->base, D->layers, &kvb, x, P, 0, pos, NULL);
+    /* features F_{-1}=0, F_0..F_{P-1} for draft rows 0..P */
+    memset(feat, 0, sizeof(float) * d);
+    memcpy(feat + d, x, sizeof(float) * (size_t)(P - 1) * d);  /* F_0..F_{P-2} */
+    float* last_f = (float*)malloc(sizeof(float) * d);
+    memcpy(last_f, x + (size_t)(P - 1) * d, sizeof(float) * d);
+    orc_lm_logits(mdl, last_f, lg, 1);
+    int n = P;                 /* seq[n] is the last token, not in base KV */
+    seq[n] = orc_argmax(lg, V);
+    int produced = 0;
+    out[produced] = seq[n];
+    if (margins) margins[produced] = top2_margin(lg, V);
+    produced++;
+    /* feat rows for draft catch-up: positions m..n use F_{m-1}..F_{n-1} */
+    memcpy(feat + (size_t)P * d, last_f, sizeof(float) * d); /* F_{P-1} */
+    int m = 0;                 /* draft KV clean length */
+    int steps = 0;
+    while (produced < n_new) {
+        /* --- draft catch-up pass: rows m..n --- */
+        int R = n - m + 1;
+        for (int r = 0; r < R; r++) {
+            const float* e = mdl->embed + (size_t)seq[m + r] * d;
+            for (int i = 0; i < d; i++) x[(size_t)r * d + i] = feat[(size_t)r * d + i] + e[i];
+            pos[r] = m + r;
+        }
+        orc_stack_forward(mdl, mdl->draft, mdl->draft_layers, &kvd, x, R, m, pos, NULL);
+        float* g = (float*)malloc(sizeof(float) * d);
+        memcpy(g, x + (size_t)(R - 1) * d, sizeof(float) * d);
+        orc_lm_logits(mdl, g, lg, 1);
+        drafted[0] = orc_argmax(lg, V);
+        for (int j = 1; j < K; j++) {
+            int p = n + j;
+            const float* e = mdl->embed + (size_t)drafted[j - 1] * d;
+            for (int i = 0; i < d; i++) x[i] = g[i] + e[i];
+            orc_stack_forward(mdl, mdl->draft, mdl->draft_layers, &kvd, x, 1, p, &p, NULL);
+            memcpy(g, x, sizeof(float) * d);
+            orc_lm_logits(mdl, g, lg, 1);
+            drafted[j] = orc_argmax(lg, V);
+        }
+        free(g);
+        m = n + 1;
+        /* --- verify rows n..n+K --- */
+        for (int r = 0; r <= K; r++) {
+            int t = r == 0 ? seq[n] : drafted[r - 1];
+            memcpy(x + (size_t)r * d, mdl->embed + (size_t)t * d, sizeof(float) * d);
+            pos[r] = n + r;
+        }
+        orc_stack_forward(mdl, mdl->base, D->layers, &kvb, x, K + 1, n, pos, NULL);
+        orc_lm_logits(mdl, x, lg, K + 1);
+        int a = 0;
+        while (a < K && a < max_acc && drafted[a] == orc_argmax(lg + (size_t)a * V, V)) a++;
+        int bonus = orc_argmax(lg + (size_t)a * V, V);
+        if (acc_hist) acc_hist[steps] = a;
+        steps++;
+        for (int j = 0; j <= a; j++) {
+            int t = j < a ? drafted[j] : bonus;
+            seq[n + 1 + j] = t;
+            if (produced < n_new) {
+                out[produced] = t;
+                if (margins) margins[produced] = top2_margin(lg + (size_t)j * V, V);
+                produced++;
+            }
+        }
+        /* features for the next catch-up: F_n..F_{n+a} = verify rows 0..a */
+        memcpy(feat, x, sizeof(float) * (size_t)(a + 1) * d);
+        n = n + a + 1;
+    }
+    free(seq); free(x); free(feat); free(lg); free(pos); free(drafted); free(last_f);
+    orc_kv_free(&kvb);
+    orc_kv_free(&kvd);
+    return steps;
+}
