@@ -193,13 +193,13 @@ int launch_chunks(GemvParams g, int epi, int M, const int* dyn_M, cudaStream_t s
         g.dyn_M = dyn_M;
         g.row0 = 0;
         g.M = kMaxRows;
-        FL_CHECK_CUDA(launch_gemv(g, epi, false, false, s, pdl));
+        FL_CHECK_CUDA(launch_gemv_auto(g, epi, s, pdl));
         return FL_OK;
     }
     for (int r0 = 0; r0 < M; r0 += kMaxRows) {
         g.row0 = r0;
         g.M = std::min(kMaxRows, M - r0);
-        FL_CHECK_CUDA(launch_gemv(g, epi, false, false, s, pdl));
+        FL_CHECK_CUDA(launch_gemv_auto(g, epi, s, pdl));
     }
     return FL_OK;
 }
@@ -289,7 +289,7 @@ int run_lm(fl_engine* e, const float* x, int M, const int* dyn_src_row, const in
     g.amax_part = e->amax;
     g.M = M;
     g.row0 = 0;
-    FL_CHECK_CUDA(launch_gemv(g, EPI_LOGITS, false, false, e->s, pdl));
+    FL_CHECK_CUDA(launch_gemv_auto(g, EPI_LOGITS, e->s, pdl));
     return FL_OK;
 }
 
@@ -423,7 +423,7 @@ FL_API fl_engine_t* fl_engine_create(const fl_model_config_t* cfg, int device) {
         if (alloc_linear(m, e->d, e->d, 0x1u) != FL_OK) return fail(0);
     const size_t R = e->R, d = e->d;
     const size_t wq = std::max(e->d, e->qd);
-    e->nparts = gemv_grid(e->V);
+    e->nparts = gemv_auto_grid(e->V, e->d);
     bool ok = cudaMalloc(&e->embed, sizeof(float) * (size_t)e->V * d) == cudaSuccess &&
               cudaMalloc(&e->x, sizeof(float) * R * d) == cudaSuccess &&
               cudaMalloc(&e->x2, sizeof(float) * R * d) == cudaSuccess &&
@@ -674,6 +674,7 @@ FL_API int fl_engine_spec_decode(fl_engine_t* e, int n_new, int* out, int* acc_h
     }
     FL_CHECK_CUDA(cudaEventRecord(e->ev[1], e->s));
     FL_CHECK_CUDA(cudaEventSynchronize(e->ev[1]));
+    if (take_device_error() != 0) return set_error(FL_E_TIMEOUT, "spec_decode: a bounded device wait gave up");
     float ms = 0.0f;
     cudaEventElapsedTime(&ms, e->ev[0], e->ev[1]);
     e->t_total_us = ms * 1000.0;

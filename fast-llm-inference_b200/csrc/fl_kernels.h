@@ -62,6 +62,19 @@ cudaError_t launch_gemv(const GemvParams& p, int epi, bool rowmode, bool pairsat
                         cudaStream_t s, bool pdl);
 int gemv_grid(int N);
 
+// Persistent TMA-ring variant for block-mode weights (gemv_tma.cu): one CTA
+// per SM. Supported when K % 256 == 0 and the ring fits (tma_gemv_supported).
+cudaError_t launch_gemv_tma(const GemvParams& p, int epi, cudaStream_t s, bool pdl);
+bool tma_gemv_supported(int K, int M);
+int tma_gemv_grid();
+// Block-mode GEMV through the TMA kernel when the shape allows it, else the
+// register-streamed kernel; gemv_auto_grid is the grid it uses for up to
+// kMaxRows rows (the number of argmax partials per row for EPI_LOGITS).
+cudaError_t launch_gemv_auto(const GemvParams& p, int epi, cudaStream_t s, bool pdl);
+int gemv_auto_grid(int N, int K);
+// Returns and clears the device error word (bounded waits that gave up).
+int take_device_error();
+
 struct ActQuantParams {
     const float* x;           // [rows, K]
     uint8_t* q;               // [rows, K]

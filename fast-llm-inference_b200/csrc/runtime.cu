@@ -146,7 +146,10 @@ static int run_gemv_chunks(const uint8_t* Aq, const dequantized_tensor_t* B, flo
     for (int r0 = 0; r0 < M; r0 += kMaxRows) {
         p.row0 = r0;
         p.M = M - r0 < kMaxRows ? M - r0 : kMaxRows;
-        FL_CHECK_CUDA(launch_gemv(p, epi, d->scale_block == 0, d->pairsat != 0, s, false));
+        if (d->scale_block == 32)
+            FL_CHECK_CUDA(launch_gemv_auto(p, epi, s, false));
+        else
+            FL_CHECK_CUDA(launch_gemv(p, epi, true, d->pairsat != 0, s, false));
     }
     return FL_OK;
 }
@@ -202,6 +205,7 @@ FL_API int fl_cuda_sync(void) {
     cudaStream_t s = device_stream();
     if (!s) return set_error(FL_E_NODEV, "no device");
     FL_CHECK_CUDA(cudaStreamSynchronize(s));
+    if (take_device_error() != 0) return set_error(FL_E_TIMEOUT, "a bounded device-side wait gave up");
     return FL_OK;
 }
 

@@ -73,6 +73,19 @@ class Oracle:
         s.orc_kv_free.argtypes = [C.POINTER(KV)]
         s.orc_spec_generate.argtypes = [C.POINTER(Model), VP, I, I, I, I, VP, VP, VP]
         s.orc_greedy_generate.argtypes = [C.POINTER(Model), VP, I, I, VP, VP]
+        # Every pointer argument must be declared: an undeclared Python int is
+        # passed as a 32-bit C int and truncates heap addresses.
+        s.orc_quant_u8.argtypes = [VP, VP, I]
+        s.orc_dot_pairsat.argtypes = [VP, VP, I]
+        s.orc_dot_plain.argtypes = [VP, VP, I]
+        s.orc_matmul_rowscale.argtypes = [VP, VP, VP, VP, I, I, I]
+        s.orc_matmul_block.argtypes = [VP, VP, VP, VP, I, I, I]
+        s.orc_block_dots.argtypes = [VP, VP, VP, I, I, I]
+        s.orc_swiglu.argtypes = [VP, VP, VP, I]
+        s.orc_silu.argtypes = [VP, VP, I]
+        s.orc_q4_0_quantize_i8.argtypes = [VP, I, VP, VP]
+        s.orc_philox4x32_10.argtypes = [VP, VP, VP]
+        s.orc_argmax.argtypes = [VP, I]
 
     # ----------------------------------------------------------- primitives
     def quant_u8(self, x):
@@ -239,9 +252,16 @@ class Ref:
         self.so = C.CDLL(path)
         s = self.so
         s.ref_dot_product_u8_i8.restype = C.c_int32
+        s.ref_dot_product_u8_i8.argtypes = [VP, VP, I]
+        s.ref_quantize_to_uint8.argtypes = [VP, VP, I]
+        s.ref_matmul_dequantized.argtypes = [VP, VP, VP, VP, I, I, I]
         s.ref_rms_norm.argtypes = [VP, VP, I, F]
+        s.ref_swiglu.argtypes = [VP, VP, VP, I]
+        s.ref_silu.argtypes = [VP, VP, I]
         s.ref_apply_rope.argtypes = [VP, VP, I, I, I, I, F]
+        s.ref_compute_attention.argtypes = [VP, VP, VP, VP, I, I, I, I]
         s.ref_model_forward_f32.restype = I
+        s.ref_model_forward_f32.argtypes = [I, I, I, I, I, I, I, VP, VP, VP, VP, I, VP]
 
     def quant_u8(self, x):
         x = np.ascontiguousarray(x, np.float32)

@@ -1,8 +1,11 @@
 """Seeded small models shared by the CPU and GPU tests."""
 import numpy as np
 
-SMALL = dict(vocab=512, d=256, ffn=512, layers=2, heads=4, kv_heads=4, head_dim=64, theta=10000.0, eps=1e-5)
-SMALL_GQA = dict(SMALL, heads=4, kv_heads=2)
+# d, ffn and q_dim multiples of 512 take the TMA-ring GEMV; SMALL_V1 (d 256)
+# takes the register-streamed fallback kernel.
+SMALL = dict(vocab=1000, d=512, ffn=1024, layers=2, heads=8, kv_heads=8, head_dim=64, theta=10000.0, eps=1e-5)
+SMALL_GQA = dict(SMALL, kv_heads=4)
+SMALL_V1 = dict(vocab=512, d=256, ffn=512, layers=2, heads=4, kv_heads=4, head_dim=64, theta=10000.0, eps=1e-5)
 
 
 def engine_cfg(dims, draft_layers=1, medusa_heads=0, max_seq_len=256):

@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 
 import flb200
-from _model import SMALL, SMALL_GQA, engine_cfg, load_engine, make_weights, prompt
+from _model import SMALL, SMALL_GQA, SMALL_V1, engine_cfg, load_engine, make_weights, prompt
 
 pytestmark = pytest.mark.gpu
 
@@ -21,9 +21,9 @@ def oracle_model(orc, dims, w, embed, draft_layers=1, n_medusa=0):
     return bind.OracleModel(orc, dims, embed, w, draft_layers=draft_layers, n_medusa=n_medusa)
 
 
-@pytest.fixture(scope="module", params=["mha", "gqa"])
+@pytest.fixture(scope="module", params=["mha", "gqa", "v1"])
 def small(request, gpu, orc):
-    dims = SMALL if request.param == "mha" else SMALL_GQA
+    dims = {"mha": SMALL, "gqa": SMALL_GQA, "v1": SMALL_V1}[request.param]
     w, embed = make_weights(gpu, dims, seed=21)
     eng = flb200.Engine(gpu, engine_cfg(dims, draft_layers=1))
     load_engine(eng, w, embed)
