@@ -257,8 +257,11 @@ FL_API int draft_tokens(draft_model_t* model, draft_kv_cache_t* cache, const flo
 
 FL_API int fl_engine_bind_draft(fl_engine_t* e, draft_model_t* dm) {
     if (!e || !dm) return set_error(FL_E_INVAL, "bind_draft: NULL");
+    // Weights go to HBM once per (engine, draft) pair; later calls reuse them.
+    if (bound(dm) == e && fl_engine_draft_bound(e, dm)) return FL_OK;
     FL_CHECK(load_draft_into(e, dm));
     bind(dm, e);
+    fl_engine_note_draft(e, dm);
     return FL_OK;
 }
 

@@ -50,17 +50,21 @@ __global__ void __launch_bounds__(kQThreads) act_quant_kernel(const ActQuantPara
     }
 }
 
-constexpr int kAThreads = 128;
+constexpr int kAThreads = 256;
 constexpr int kARows = 8;     // query rows per CTA
 constexpr int kMaxHd = 128;
+constexpr int kTile = 128;    // keys per shared-memory tile
 
 // Attention of up to kARows query rows of one head over slots
 // [0, base + M): prefix slots [0, base) are visible to every row, new slot
 // base + j to new row i iff mask[i*M + j] (causal j <= i when mask is NULL).
-// inference.c:193-247 restated for a KV cache: scores = q.k * 1/sqrt(hd),
-// softmax with max subtraction and expf, then the p-weighted sum of V.
+// inference.c:193-247 restated for a paged KV cache: scores q.k / sqrt(hd),
+// softmax, p-weighted sum of V. Keys stream through shared memory in tiles
+// of kTile with coalesced loads; the softmax is accumulated online (running
+// max and sum per row, rescaled per tile), which equals the reference's
+// two-pass softmax up to float rounding.
 __global__ void __launch_bounds__(kAThreads) attention_kernel(const AttnParams p) {
-    extern __shared__ float sm[];
+    extern __shared__ __align__(16) float sm[];
     pdl_trigger();
     pdl_wait();
     if (p.done && *p.done) return;
@@ -72,118 +76,152 @@ __global__ void __launch_bounds__(kAThreads) attention_kernel(const AttnParams p
     const int base = *p.slot_base;
     const int ctx = base + M;
     const int hd = p.head_dim;
+    const int hd2 = hd >> 1;
     const int kvh = h / (p.heads / p.kv_heads);
     const int qd = p.heads * hd;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kstride = hd2 + 1;  // words per K row in smem (odd: conflict-free)
 
-    float* q_s = sm;                         // [kARows][hd]
-    float* sc = sm + kARows * kMaxHd;        // [kARows][ctx]
-    __shared__ float red[kAThreads / 32];
-    __shared__ float rowstat[kARows];
+    float* q_s = sm;                                   // [kARows][hd]
+    float* sc = q_s + kARows * kMaxHd;                 // [kARows][kTile]
+    uint32_t* Ks = reinterpret_cast<uint32_t*>(sc + kARows * kTile);  // [kTile][kstride] half2
+    uint32_t* Vs = Ks + kTile * (kMaxHd / 2 + 1);      // [kTile][hd2] half2
+    float* red = reinterpret_cast<float*>(Vs + kTile * (kMaxHd / 2));  // [groups][kARows][hd]
+    __shared__ float m_run[kARows], l_run[kARows], alpha_s[kARows];
 
     for (int i = threadIdx.x; i < nr * hd; i += kAThreads) {
         const int rr = i / hd, dd = i - rr * hd;
         q_s[rr * hd + dd] = p.q[(size_t)(r0 + rr) * qd + (size_t)h * hd + dd];
     }
-    __syncthreads();
-
+    if (threadIdx.x < kARows) {
+        m_run[threadIdx.x] = -INFINITY;
+        l_run[threadIdx.x] = 0.0f;
+    }
     const float scale = __fdiv_rn(1.0f, sqrtf((float)hd));
-    // scores: one key per thread, all rows of the CTA
-    for (int j = threadIdx.x; j < ctx; j += kAThreads) {
-        const int page = p.block_table[j / kPageSize];
-        const __half2* kr = reinterpret_cast<const __half2*>(
-            p.kv.k + (((size_t)page * p.kv_heads + kvh) * kPageSize + (j % kPageSize)) * hd);
-        float acc[kARows];
+    // P.V mapping: thread -> (dimension pair d2, key group g)
+    const int G = kAThreads / hd2;
+    const int d2 = threadIdx.x % hd2;
+    const int g = threadIdx.x / hd2;
+    const bool pv = g < G;
+    float a0[kARows], a1[kARows];
 #pragma unroll
-        for (int rr = 0; rr < kARows; rr++) acc[rr] = 0.0f;
-        for (int d2 = 0; d2 < hd / 2; d2++) {
-            const float2 kv = __half22float2(kr[d2]);
+    for (int rr = 0; rr < kARows; rr++) { a0[rr] = 0.0f; a1[rr] = 0.0f; }
+
+    for (int j0 = 0; j0 < ctx; j0 += kTile) {
+        const int nt = min(kTile, ctx - j0);
+        __syncthreads();  // previous tile fully consumed
+        // K and V tile: half2 words, consecutive threads -> consecutive words
+        for (int i = threadIdx.x; i < nt * hd2; i += kAThreads) {
+            const int key = i / hd2, c = i - key * hd2;
+            const int slot = j0 + key;
+            const int page = p.block_table[slot / kPageSize];
+            const size_t off = (((size_t)page * p.kv_heads + kvh) * kPageSize + (slot % kPageSize)) * hd2 + c;
+            Ks[key * kstride + c] = reinterpret_cast<const uint32_t*>(p.kv.k)[off];
+            Vs[key * hd2 + c] = reinterpret_cast<const uint32_t*>(p.kv.v)[off];
+        }
+        __syncthreads();
+        // scores: one key per thread (kTile <= kAThreads)
+        if (threadIdx.x < nt) {
+            const int j = j0 + threadIdx.x;
+            float acc[kARows];
+#pragma unroll
+            for (int rr = 0; rr < kARows; rr++) acc[rr] = 0.0f;
+            const uint32_t* kr = Ks + threadIdx.x * kstride;
+            for (int e = 0; e < hd2; e++) {
+                const float2 kf = __half22float2(*reinterpret_cast<const __half2*>(&kr[e]));
+#pragma unroll
+                for (int rr = 0; rr < kARows; rr++) {
+                    if (rr < nr) {
+                        acc[rr] = __fmaf_rn(q_s[rr * hd + 2 * e], kf.x, acc[rr]);
+                        acc[rr] = __fmaf_rn(q_s[rr * hd + 2 * e + 1], kf.y, acc[rr]);
+                    }
+                }
+            }
 #pragma unroll
             for (int rr = 0; rr < kARows; rr++) {
                 if (rr < nr) {
-                    acc[rr] = __fmaf_rn(q_s[rr * hd + 2 * d2], kv.x, acc[rr]);
-                    acc[rr] = __fmaf_rn(q_s[rr * hd + 2 * d2 + 1], kv.y, acc[rr]);
+                    bool vis = true;
+                    if (j >= base) {
+                        const int jj = j - base, ii = r0 + rr;
+                        vis = p.mask ? (p.mask[(size_t)ii * M + jj] != 0) : (jj <= ii);
+                    }
+                    sc[rr * kTile + threadIdx.x] = vis ? __fmul_rn(acc[rr], scale) : -INFINITY;
                 }
             }
         }
+        __syncthreads();
+        // online softmax update: warp rr owns row rr
+        if (warp < nr) {
+            float* s = sc + warp * kTile;
+            float mx = -INFINITY;
+            for (int t = lane; t < nt; t += 32) mx = fmaxf(mx, s[t]);
+            mx = warp_max(mx);
+            const float m_old = m_run[warp];
+            const float m_new = fmaxf(m_old, mx);
+            float sum = 0.0f;
+            for (int t = lane; t < nt; t += 32) {
+                const float e = (s[t] == -INFINITY) ? 0.0f : expf(__fsub_rn(s[t], m_new));
+                s[t] = e;
+                sum += e;
+            }
+            sum = warp_sum(sum);
+            if (lane == 0) {
+                const float al = (m_old == -INFINITY) ? 0.0f : expf(__fsub_rn(m_old, m_new));
+                alpha_s[warp] = al;
+                l_run[warp] = __fmaf_rn(l_run[warp], al, sum);
+                m_run[warp] = m_new;
+            }
+        }
+        __syncthreads();
+        if (pv) {
+#pragma unroll
+            for (int rr = 0; rr < kARows; rr++) {
+                if (rr < nr) {
+                    a0[rr] *= alpha_s[rr];
+                    a1[rr] *= alpha_s[rr];
+                }
+            }
+            for (int t = g; t < nt; t += G) {
+                const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&Vs[t * hd2 + d2]));
+#pragma unroll
+                for (int rr = 0; rr < kARows; rr++) {
+                    if (rr < nr) {
+                        const float w = sc[rr * kTile + t];
+                        a0[rr] = __fmaf_rn(w, v.x, a0[rr]);
+                        a1[rr] = __fmaf_rn(w, v.y, a1[rr]);
+                    }
+                }
+            }
+        }
+    }
+    // reduce the key groups, normalise, quantize
+    __syncthreads();
+    if (pv) {
 #pragma unroll
         for (int rr = 0; rr < kARows; rr++) {
             if (rr < nr) {
-                bool vis = true;
-                if (j >= base) {
-                    const int jj = j - base, ii = r0 + rr;
-                    vis = p.mask ? (p.mask[(size_t)ii * M + jj] != 0) : (jj <= ii);
-                }
-                sc[rr * ctx + j] = vis ? __fmul_rn(acc[rr], scale) : -FLT_MAX;
+                red[(g * kARows + rr) * hd + 2 * d2] = a0[rr];
+                red[(g * kARows + rr) * hd + 2 * d2 + 1] = a1[rr];
             }
         }
     }
     __syncthreads();
-
-    // softmax per row (max, exp, sum, normalise)
-    for (int rr = 0; rr < nr; rr++) {
-        float* s = sc + rr * ctx;
-        float mx = -FLT_MAX;
-        for (int j = threadIdx.x; j < ctx; j += kAThreads) mx = fmaxf(mx, s[j]);
-        mx = warp_max(mx);
-        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            float t = red[0];
-            for (int w = 1; w < kAThreads / 32; w++) t = fmaxf(t, red[w]);
-            rowstat[rr] = t;
-        }
-        __syncthreads();
-        mx = rowstat[rr];
-        float sum = 0.0f;
-        for (int j = threadIdx.x; j < ctx; j += kAThreads) {
-            const float e = s[j] == -FLT_MAX ? 0.0f : expf(__fsub_rn(s[j], mx));
-            s[j] = e;
-            sum += e;
-        }
-        sum = warp_sum(sum);
-        __syncthreads();
-        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            float t = 0.0f;
-            for (int w = 0; w < kAThreads / 32; w++) t += red[w];
-            rowstat[rr] = t;
-        }
-        __syncthreads();
-        const float tot = rowstat[rr];
-        for (int j = threadIdx.x; j < ctx; j += kAThreads) s[j] = __fdiv_rn(s[j], tot);
-        __syncthreads();
+    for (int i = threadIdx.x; i < nr * hd; i += kAThreads) {
+        const int rr = i / hd, dd = i - rr * hd;
+        float o = 0.0f;
+        for (int gg = 0; gg < G; gg++) o += red[(gg * kARows + rr) * hd + dd];
+        o = __fdiv_rn(o, l_run[rr]);
+        const size_t idx = (size_t)(r0 + rr) * qd + (size_t)h * hd + dd;
+        p.out_q[idx] = (uint8_t)quant_u8(o);
+        if (p.out_f) p.out_f[idx] = o;
     }
+}
 
-    // out[rr][d] = sum_j p[rr][j] * v[j][d]; thread -> dimension pair
-    for (int d2 = threadIdx.x; d2 < hd / 2; d2 += kAThreads) {
-        float a0[kARows], a1[kARows];
-#pragma unroll
-        for (int rr = 0; rr < kARows; rr++) { a0[rr] = 0.0f; a1[rr] = 0.0f; }
-        for (int j = 0; j < ctx; j++) {
-            const int page = p.block_table[j / kPageSize];
-            const __half2* vr = reinterpret_cast<const __half2*>(
-                p.kv.v + (((size_t)page * p.kv_heads + kvh) * kPageSize + (j % kPageSize)) * hd);
-            const float2 v = __half22float2(vr[d2]);
-#pragma unroll
-            for (int rr = 0; rr < kARows; rr++) {
-                if (rr < nr) {
-                    const float w = sc[rr * ctx + j];
-                    a0[rr] = __fmaf_rn(w, v.x, a0[rr]);
-                    a1[rr] = __fmaf_rn(w, v.y, a1[rr]);
-                }
-            }
-        }
-#pragma unroll
-        for (int rr = 0; rr < kARows; rr++) {
-            if (rr < nr) {
-                const size_t o = (size_t)(r0 + rr) * qd + (size_t)h * hd + 2 * d2;
-                p.out_q[o] = (uint8_t)quant_u8(a0[rr]);
-                p.out_q[o + 1] = (uint8_t)quant_u8(a1[rr]);
-                if (p.out_f) { p.out_f[o] = a0[rr]; p.out_f[o + 1] = a1[rr]; }
-            }
-        }
-    }
+size_t attention_smem() {
+    const size_t f = (size_t)kARows * kMaxHd + (size_t)kARows * kTile;
+    const size_t kv = (size_t)kTile * (kMaxHd / 2 + 1) + (size_t)kTile * (kMaxHd / 2);
+    const size_t red = (size_t)(kAThreads / 32) * kARows * kMaxHd;  // G <= kAThreads / (hd/2), hd >= 64
+    return sizeof(float) * (f + red) + sizeof(uint32_t) * kv;
 }
 
 }  // namespace
@@ -203,9 +241,9 @@ cudaError_t launch_act_quant(const ActQuantParams& p, cudaStream_t s, bool pdl) 
 }
 
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl) {
-    if (p.head_dim > kMaxHd || p.head_dim % 2 != 0 || p.heads % p.kv_heads != 0) return cudaErrorInvalidValue;
-    const size_t smem = sizeof(float) * ((size_t)kARows * kMaxHd + (size_t)kARows * p.max_ctx);
-    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    if (p.head_dim > kMaxHd || p.head_dim < 64 || p.head_dim % 2 != 0 || p.heads % p.kv_heads != 0)
+        return cudaErrorInvalidValue;
+    const size_t smem = attention_smem();
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)smem);

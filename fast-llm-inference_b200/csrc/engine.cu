@@ -90,6 +90,9 @@ struct fl_engine {
     double t_draft_us = 0, t_verify_us = 0, t_total_us = 0;
     int cb_pos = 0;               // callback API: base cache length
     float* last_feat = nullptr;   // [d] base feature of the last appended token
+    int graph_kernels = 0;        // kernel nodes in the step graph
+    long long last_launches = 0;  // kernels launched by the last decode
+    const void* bound_draft = nullptr;
 };
 
 namespace {
@@ -224,10 +227,18 @@ int act_quant(fl_engine* e, const float* x, uint8_t* q, int K, int M, const int*
 int run_stack(fl_engine* e, Stack& S, float* x, int M, const int* dyn_M, const int* slot_base, const int* pos,
               const uint8_t* mask, const int* done, bool pdl) {
     const int d = e->d, qd = e->qd, F = e->F;
+    // Fused RMSNorm + quantization prologues need K % 128 == 0; otherwise a
+    // separate act_quant launch produces xq.
+    const bool fuse = (d % 128) == 0;
     for (int l = 0; l < S.nl; l++) {
         LayerW& W = S.L[l];
-        FL_CHECK(act_quant(e, x, e->xq, d, M, dyn_M, 1, done, pdl));
+        if (!fuse) FL_CHECK(act_quant(e, x, e->xq, d, M, dyn_M, 1, done, pdl));
         GemvParams g = gemv_base(W.qkv, e->xq, done);
+        if (fuse) {
+            g.x = x;
+            g.norm = 1;
+            g.eps = e->c.norm_eps;
+        }
         g.q_out = e->q;
         g.kv = S.kv[l];
         g.block_table = S.block_table;
@@ -258,8 +269,13 @@ int run_stack(fl_engine* e, Stack& S, float* x, int M, const int* dyn_M, const i
         g.out = x;
         g.ldo = d;
         FL_CHECK(launch_chunks(g, EPI_RESID, M, dyn_M, e->s, pdl));
-        FL_CHECK(act_quant(e, x, e->xq, d, M, dyn_M, 1, done, pdl));
+        if (!fuse) FL_CHECK(act_quant(e, x, e->xq, d, M, dyn_M, 1, done, pdl));
         g = gemv_base(W.gu, e->xq, done);
+        if (fuse) {
+            g.x = x;
+            g.norm = 1;
+            g.eps = e->c.norm_eps;
+        }
         g.hq = e->hq;
         g.F = F;
         FL_CHECK(launch_chunks(g, EPI_SWIGLU, M, dyn_M, e->s, pdl));
@@ -272,18 +288,26 @@ int run_stack(fl_engine* e, Stack& S, float* x, int M, const int* dyn_M, const i
 }
 
 // LM head over rows of x (M <= kMaxRows): logits [M, V] and argmax partials.
+// dyn_src_row (device) selects the first source row of x.
 int run_lm(fl_engine* e, const float* x, int M, const int* dyn_src_row, const int* done, bool pdl) {
-    ActQuantParams a = {};
-    a.x = x;
-    a.q = e->xq;
-    a.K = e->d;
-    a.M = M;
-    a.norm = 1;
-    a.eps = e->c.norm_eps;
-    a.done = done;
-    a.dyn_src_row = dyn_src_row;
-    FL_CHECK_CUDA(launch_act_quant(a, e->s, pdl));
     GemvParams g = gemv_base(e->lm, e->xq, done);
+    if ((e->d % 128) == 0) {
+        g.x = x;
+        g.norm = 1;
+        g.eps = e->c.norm_eps;
+        g.x_row_dyn = dyn_src_row;
+    } else {
+        ActQuantParams a = {};
+        a.x = x;
+        a.q = e->xq;
+        a.K = e->d;
+        a.M = M;
+        a.norm = 1;
+        a.eps = e->c.norm_eps;
+        a.done = done;
+        a.dyn_src_row = dyn_src_row;
+        FL_CHECK_CUDA(launch_act_quant(a, e->s, pdl));
+    }
     g.out = e->logits;
     g.ldo = e->V;
     g.amax_part = e->amax;
@@ -332,7 +356,7 @@ int record_step(fl_engine* e, bool pdl) {
     const int* done = &st->done;
     StepBuffers b = step_buffers(e);
     for (int j = 1; j < K; j++) {
-        FL_CHECK(run_stack(e, e->draft, e->x_d, 1, &st->one, &st->draft_base, st->draft_pos, nullptr, done, pdl));
+        FL_CHECK(run_stack(e, e->draft, e->x_d, 1, nullptr, &st->draft_base, st->draft_pos, nullptr, done, pdl));
         FL_CHECK(run_lm(e, e->x_d, 1, nullptr, done, pdl));
         FL_CHECK_CUDA(launch_draft_pick(b, j, e->s, pdl));
     }
@@ -362,6 +386,16 @@ int build_step_graph(fl_engine* e) {
         return rc;
     }
     FL_CHECK_CUDA(ce);
+    size_t nn = 0;
+    cudaGraphGetNodes(g, nullptr, &nn);
+    std::vector<cudaGraphNode_t> nodes(nn);
+    cudaGraphGetNodes(g, nodes.data(), &nn);
+    int nk = 0;
+    for (auto nd : nodes) {
+        cudaGraphNodeType t;
+        if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) nk++;
+    }
+    e->graph_kernels = nk;
     ce = cudaGraphInstantiate(&e->step_exec, g, 0);
     cudaGraphDestroy(g);
     FL_CHECK_CUDA(ce);
@@ -664,9 +698,11 @@ FL_API int fl_engine_spec_decode(fl_engine_t* e, int n_new, int* out, int* acc_h
     FL_CHECK_CUDA(cudaEventRecord(e->ev[0], e->s));
     SpecState h = {};
     int produced = 1;
+    long long launched = 0;
     while (produced < n_new) {
         const int batch = (n_new - produced + K) / (K + 1);
         for (int i = 0; i < batch; i++) FL_CHECK_CUDA(cudaGraphLaunch(e->step_exec, e->s));
+        launched += batch;
         FL_CHECK_CUDA(cudaMemcpyAsync(&h, e->st, sizeof(h), cudaMemcpyDeviceToHost, e->s));
         FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
         if (h.produced <= produced) return set_error(FL_E_STATE, "spec_decode: no progress");
@@ -678,6 +714,7 @@ FL_API int fl_engine_spec_decode(fl_engine_t* e, int n_new, int* out, int* acc_h
     float ms = 0.0f;
     cudaEventElapsedTime(&ms, e->ev[0], e->ev[1]);
     e->t_total_us = ms * 1000.0;
+    e->last_launches = (long long)launched * e->graph_kernels;
     if (out) FL_CHECK_CUDA(cudaMemcpy(out, e->out, sizeof(int) * n_new, cudaMemcpyDeviceToHost));
     if (acc_hist) FL_CHECK_CUDA(cudaMemcpy(acc_hist, e->acc, sizeof(int) * h.steps, cudaMemcpyDeviceToHost));
     if (steps) *steps = h.steps;
@@ -699,6 +736,57 @@ FL_API int fl_engine_last_timing(const fl_engine_t* e, double* draft_us, double*
 }
 
 FL_API void* fl_engine_stream(const fl_engine_t* e) { return e ? (void*)e->s : nullptr; }
+
+FL_API long long fl_engine_last_launches(const fl_engine_t* e) { return e ? e->last_launches : -1; }
+
+FL_API int fl_engine_draft_bound(const fl_engine_t* e, const void* draft) { return e && e->bound_draft == draft; }
+FL_API void fl_engine_note_draft(fl_engine_t* e, const void* draft) {
+    if (e) e->bound_draft = draft;
+}
+
+// Times one projection of every layer of a stack (kind 0 qkv, 1 o, 2
+// gate/up, 3 down) as captured back-to-back GEMV launches at M rows: the
+// per-launch device time and the algorithmic bytes of one launch (int8
+// weights + fp16 scales + activations in + outputs). The layers' weights
+// together exceed L2 for the full-size model.
+FL_API int fl_engine_bench_linear(fl_engine_t* e, int stack, int kind, int M, int reps, double* us_per_launch,
+                                  double* bytes_per_launch) {
+    FL_CHECK(check_ready(e, stack == 1));
+    if (kind < 0 || kind > 3 || M < 1 || M > kMaxRows || reps < 1) return set_error(FL_E_INVAL, "bench_linear: bad arguments");
+    Stack& S = stack == 0 ? e->base : e->draft;
+    cudaGraph_t g = nullptr;
+    FL_CHECK_CUDA(cudaStreamBeginCapture(e->s, cudaStreamCaptureModeThreadLocal));
+    int rc = FL_OK;
+    const Linear* l0 = nullptr;
+    for (int l = 0; l < S.nl && rc == FL_OK; l++) {
+        const Linear& L = kind == 0 ? S.L[l].qkv : kind == 1 ? S.L[l].o : kind == 2 ? S.L[l].gu : S.L[l].down;
+        l0 = &L;
+        GemvParams gp = gemv_base(L, kind == 3 ? e->hq : e->xq, nullptr);
+        gp.M = M;
+        gp.out = e->q;  // scratch rows of at least N floats
+        gp.ldo = L.N;
+        if (launch_gemv_auto(gp, EPI_STORE, e->s, true) != cudaSuccess) rc = set_error(FL_E_CUDA, "bench_linear launch");
+    }
+    cudaError_t ce = cudaStreamEndCapture(e->s, &g);
+    if (rc != FL_OK) { if (g) cudaGraphDestroy(g); return rc; }
+    FL_CHECK_CUDA(ce);
+    cudaGraphExec_t ex = nullptr;
+    ce = cudaGraphInstantiate(&ex, g, 0);
+    cudaGraphDestroy(g);
+    FL_CHECK_CUDA(ce);
+    FL_CHECK_CUDA(cudaGraphLaunch(ex, e->s));  // warm-up
+    FL_CHECK_CUDA(cudaEventRecord(e->ev[2], e->s));
+    for (int r = 0; r < reps; r++) FL_CHECK_CUDA(cudaGraphLaunch(ex, e->s));
+    FL_CHECK_CUDA(cudaEventRecord(e->ev[3], e->s));
+    FL_CHECK_CUDA(cudaEventSynchronize(e->ev[3]));
+    cudaGraphExecDestroy(ex);
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, e->ev[2], e->ev[3]);
+    if (us_per_launch) *us_per_launch = ms * 1000.0 / ((double)reps * S.nl);
+    if (bytes_per_launch)
+        *bytes_per_launch = (double)l0->N * l0->K * (1.0 + 1.0 / 16.0) + (double)M * l0->K + 4.0 * M * l0->N;
+    return FL_OK;
+}
 
 // ---------------------------------------------------------------------------
 // Callback-level API: the engine as the reference's target_forward /

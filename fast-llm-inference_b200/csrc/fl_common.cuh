@@ -94,6 +94,46 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+// Exact float of an int with |v| < 2^22 using full-rate integer and float
+// adds (the int->float conversion instruction runs at a fraction of the FMA
+// rate): 0x4B400000 is 1.5 * 2^23, whose ulp is 1.
+__device__ __forceinline__ float i2f_exact(int v) {
+    return __fsub_rn(__int_as_float(v + 0x4B400000), 12582912.0f);
+}
+
+// GEMV activation prologue: rows of f32 x (row stride K) -> u8 codes in
+// shared memory, optionally after RMSNorm with unit weights
+// (activations_avx2.c:108-143 then dequantized_tensor.c:112-135). Warp w
+// handles rows w, w + nwarps, ...; K % 128 == 0.
+__device__ __forceinline__ void act_prologue(uint8_t* act, const float* x, int K, int rows, int norm, float eps,
+                                             int warp, int lane, int nwarps) {
+    for (int m = warp; m < rows; m += nwarps) {
+        const float* xr = x + (size_t)m * K;
+        float scale = 1.0f;
+        if (norm) {
+            float s = 0.0f;
+#pragma unroll 4
+            for (int i = lane * 4; i < K; i += 128) {
+                const float4 v = *reinterpret_cast<const float4*>(xr + i);
+                s = __fmaf_rn(v.x, v.x, s);
+                s = __fmaf_rn(v.y, v.y, s);
+                s = __fmaf_rn(v.z, v.z, s);
+                s = __fmaf_rn(v.w, v.w, s);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)K), eps)));
+        }
+#pragma unroll 4
+        for (int i = lane * 4; i < K; i += 128) {
+            const float4 v = *reinterpret_cast<const float4*>(xr + i);
+            *reinterpret_cast<uint32_t*>(act + (size_t)m * K + i) =
+                quant_pack4(__fmul_rn(v.x, scale), __fmul_rn(v.y, scale), __fmul_rn(v.z, scale),
+                            __fmul_rn(v.w, scale));
+        }
+    }
+}
+
 // Streaming 16-byte load that bypasses L1 allocation (weights are read once).
 __device__ __forceinline__ uint4 ld_stream16(const void* p) {
     uint4 r;

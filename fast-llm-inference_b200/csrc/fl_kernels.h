@@ -35,6 +35,13 @@ struct GemvParams {
     int row0;                 // first activation row of this launch
     int N, K;
     const int* done;          // if set and *done, the kernel exits
+    // Fused activation prologue: when x is set the kernel quantizes rows of
+    // x (f32, row stride K; RMSNorm first when norm) itself instead of
+    // reading aq. Source row of activation row 0: *x_row_dyn if set, else row0.
+    const float* x;
+    int norm;
+    float eps;
+    const int* x_row_dyn;
     // EPI_STORE / EPI_RESID / EPI_LOGITS
     float* out;
     int ldo;

@@ -112,8 +112,8 @@ __device__ __forceinline__ void compute_batch(const Batch& b, const uint4* act, 
                     i0[m] += d0;
                     i1[m] += d1;
                 } else {
-                    f0[m] = __fmaf_rn((float)d0, b.s0[u], f0[m]);
-                    f1[m] = __fmaf_rn((float)d1, b.s1[u], f1[m]);
+                    f0[m] = __fmaf_rn(i2f_exact(d0), b.s0[u], f0[m]);
+                    f1[m] = __fmaf_rn(i2f_exact(d1), b.s1[u], f1[m]);
                 }
             }
         }
@@ -163,7 +163,11 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const GemvParams p) {
 
     // Quantized activations of this launch's rows into shared memory.
     const int K16 = K >> 4;
-    {
+    if (p.x) {
+        const int src0 = p.x_row_dyn ? *p.x_row_dyn : p.row0;
+        act_prologue(reinterpret_cast<uint8_t*>(act_s), p.x + (size_t)src0 * K, K, rows, p.norm, p.eps, warp, lane,
+                     kWarps);
+    } else {
         const uint4* src = reinterpret_cast<const uint4*>(p.aq + (size_t)p.row0 * K);
         const int total = rows * K16;
         for (int i = threadIdx.x; i < total; i += kThreads) act_s[i] = src[i];
@@ -328,6 +332,7 @@ int gemv_grid(int N) { return ((N + 1) / 2 + kWarps - 1) / kWarps; }
 cudaError_t launch_gemv(const GemvParams& p, int epi, bool rowmode, bool pairsat, cudaStream_t s,
                         bool pdl) {
     if (p.K % 32 != 0 || p.N <= 0 || p.K <= 0) return cudaErrorInvalidValue;
+    if (p.x && p.K % 128 != 0) return cudaErrorInvalidValue;
     if (!p.dyn_M && (p.M <= 0 || p.M > kMaxRows)) return cudaErrorInvalidValue;
     switch (epi) {
         case EPI_STORE: return launch_e<EPI_STORE>(p, rowmode, pairsat, s, pdl);

@@ -142,7 +142,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_tma_kernel(const GemvParams 
     int rows_m = p.M;
     if (p.dyn_M) rows_m = min(*p.dyn_M - p.row0, kMaxRows);
     rows_m = min(rows_m, MMAX);
-    {
+    if (p.x) {
+        const int src0 = p.x_row_dyn ? *p.x_row_dyn : p.row0;
+        act_prologue(act, p.x + (size_t)src0 * K, K, max(rows_m, 0), p.norm, p.eps, warp, lane, kCWarps);
+    } else {
         const int K16 = K >> 4;
         const uint4* src = reinterpret_cast<const uint4*>(p.aq + (size_t)p.row0 * K);
         uint4* dst = reinterpret_cast<uint4*>(act);
@@ -186,8 +189,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_tma_kernel(const GemvParams 
                 for (int m = 0; m < MMAX; m++) {
                     if (m < rows_m) {
                         const uint4 a = act4[m * K16 + ka];
-                        f0[m] = __fmaf_rn((float)dot16<true>(a, w0), s0, f0[m]);
-                        f1[m] = __fmaf_rn((float)dot16<true>(a, w1), s1, f1[m]);
+                        f0[m] = __fmaf_rn(i2f_exact(dot16<true>(a, w0)), s0, f0[m]);
+                        f1[m] = __fmaf_rn(i2f_exact(dot16<true>(a, w1)), s1, f1[m]);
                     }
                 }
             }
@@ -352,6 +355,7 @@ cudaError_t launch_gemv_tma(const GemvParams& p, int epi, cudaStream_t s, bool p
     const int mm = mmax <= 1 ? 1 : mmax <= 2 ? 2 : mmax <= 4 ? 4 : 8;
     TmaShape sh;
     if (!tma_shape(p.K, mm, sh)) return cudaErrorInvalidValue;
+    if (p.x && p.K % 128 != 0) return cudaErrorInvalidValue;
     if (!p.dyn_M && (p.M <= 0 || p.M > kMaxRows)) return cudaErrorInvalidValue;
     switch (epi) {
         case EPI_STORE: return launch_e<EPI_STORE>(p, mm, sh, s, pdl);

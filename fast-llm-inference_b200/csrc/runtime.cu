@@ -135,11 +135,12 @@ static int tensor_params(const dequantized_tensor_t* B, int N, int K, GemvParams
 }
 
 static int run_gemv_chunks(const uint8_t* Aq, const dequantized_tensor_t* B, float* C, int32_t* D,
-                           int M, int N, int K, cudaStream_t s, int epi) {
+                           int M, int N, int K, cudaStream_t s, int epi, const float* X = nullptr) {
     GemvParams p = {};
     FL_CHECK(tensor_params(B, N, K, p));
     const DevTensor* d = (const DevTensor*)B->dev;
     p.aq = Aq;
+    p.x = X;
     p.out = C;
     p.ldo = N;
     p.dots = D;
@@ -269,6 +270,8 @@ FL_API int fl_cuda_matmul_i8(const float* A, const dequantized_tensor_t* B, floa
     if (!A || !C || M <= 0 || N <= 0 || K <= 0) return set_error(FL_E_INVAL, "matmul: bad arguments");
     if (K % 32 != 0) return set_error(FL_E_INVAL, "matmul: K must be a multiple of 32");
     cudaStream_t s = stream ? (cudaStream_t)stream : device_stream();
+    if (B && B->dev && ((const DevTensor*)B->dev)->scale_block == 32 && K % 128 == 0)
+        return run_gemv_chunks(nullptr, B, C, nullptr, M, N, K, s, EPI_STORE, A);  // fused quantization
     uint8_t* q = nullptr;
     FL_CHECK(scratch_q((size_t)M * K, &q));
     FL_CHECK(fl_cuda_act_quant(A, q, M, K, 0, 0.0f, s));

@@ -117,6 +117,10 @@ _SIGS = {
     "fl_engine_spec_decode": (I, [VP, I, VP, VP, VP]),
     "fl_engine_last_timing": (I, [VP, VP, VP, VP]),
     "fl_engine_stream": (VP, [VP]),
+    "fl_engine_last_launches": (C.c_longlong, [VP]),
+    "fl_engine_draft_bound": (I, [VP, VP]),
+    "fl_engine_note_draft": (None, [VP, VP]),
+    "fl_engine_bench_linear": (I, [VP, I, I, I, I, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "fl_engine_position": (I, [VP]),
     "fl_engine_set_position": (I, [VP, I]),
     "fl_engine_last_feature": (I, [VP, VP]),
@@ -315,3 +319,12 @@ class Engine:
 
     def stream(self) -> int:
         return self.lib.fl_engine_stream(self.h)
+
+    def last_launches(self) -> int:
+        return self.lib.fl_engine_last_launches(self.h)
+
+    def bench_linear(self, stack, kind, M, reps=10):
+        us, by = C.c_double(), C.c_double()
+        self.lib.check(self.lib.fl_engine_bench_linear(self.h, stack, kind, M, reps, C.byref(us), C.byref(by)),
+                       "bench_linear")
+        return us.value, by.value

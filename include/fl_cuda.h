@@ -187,6 +187,17 @@ int fl_engine_last_timing(const fl_engine_t* e, double* draft_us, double* verify
                           double* total_us);
 /* cudaStream_t (as void*) the engine launches on. */
 void* fl_engine_stream(const fl_engine_t* e);
+/* Number of kernels the last fl_engine_spec_decode launched. */
+long long fl_engine_last_launches(const fl_engine_t* e);
+/* 1 when `draft` (a draft_model_t*) is the draft whose weights the engine
+ * holds; fl_engine_note_draft records it after a load. */
+int fl_engine_draft_bound(const fl_engine_t* e, const void* draft);
+void fl_engine_note_draft(fl_engine_t* e, const void* draft);
+/* Device time per launch of one projection kind (0 qkv, 1 o, 2 gate/up,
+ * 3 down) over all layers of a stack at M rows, captured back to back and
+ * replayed reps times, and the algorithmic bytes of one launch. */
+int fl_engine_bench_linear(fl_engine_t* e, int stack, int kind, int M, int reps,
+                           double* us_per_launch, double* bytes_per_launch);
 
 /* Callback-level position of the base cache: tokens appended through
  * fl_cuda_target_forward / fl_cuda_base_forward land at this position.

@@ -86,6 +86,7 @@ class Oracle:
         s.orc_q4_0_quantize_i8.argtypes = [VP, I, VP, VP]
         s.orc_philox4x32_10.argtypes = [VP, VP, VP]
         s.orc_argmax.argtypes = [VP, I]
+        s.orc_last_decode_seconds.restype = C.c_double
 
     # ----------------------------------------------------------- primitives
     def quant_u8(self, x):

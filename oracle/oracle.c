@@ -13,7 +13,18 @@
 #include <stdlib.h>
 #include <string.h>
 #include <float.h>
+#include <time.h>
 #include <immintrin.h>
+
+static double g_last_decode_s = 0.0;
+
+static double now_s(void) {
+    struct timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return ts.tv_sec + ts.tv_nsec * 1e-9;
+}
+
+double orc_last_decode_seconds(void) { return g_last_decode_s; }
 
 /* ------------------------------------------------------------------ */
 /* fp16 conversion (IEEE binary16)                                     */
@@ -499,6 +510,7 @@ int orc_spec_generate(const orc_model_t* mdl, const int* prompt, int P, int K,
     memcpy(feat + (size_t)P * d, last_f, sizeof(float) * d); /* F_{P-1} */
     int m = 0;                 /* draft KV clean length */
     int steps = 0;
+    const double t0 = now_s();
     while (produced < n_new) {
         /* --- draft catch-up pass: rows m..n --- */
         int R = n - m + 1;
@@ -549,6 +561,7 @@ int orc_spec_generate(const orc_model_t* mdl, const int* prompt, int P, int K,
         memcpy(feat, x, sizeof(float) * (size_t)(a + 1) * d);
         n = n + a + 1;
     }
+    g_last_decode_s = now_s() - t0;
     free(seq); free(x); free(feat); free(lg); free(pos); free(drafted); free(last_f);
     orc_kv_free(&kvb);
     orc_kv_free(&kvd);

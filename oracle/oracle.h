@@ -149,6 +149,10 @@ int orc_spec_generate(const orc_model_t* mdl, const int* prompt, int prompt_len,
                       int k_draft, int max_accepted, int n_new, int* out,
                       int* acc_hist, float* margins);
 
+/* Wall time of the decode loop (after prefill and the first token) of the
+ * last orc_spec_generate call, seconds. */
+double orc_last_decode_seconds(void);
+
 /* Plain greedy decoding with the base model only. */
 void orc_greedy_generate(const orc_model_t* mdl, const int* prompt, int prompt_len,
                          int n_new, int* out, float* margins);
