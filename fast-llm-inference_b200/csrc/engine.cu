@@ -192,10 +192,10 @@ GemvParams gemv_base(const Linear& l, const uint8_t* aq, const int* done) {
 }
 
 int launch_chunks(GemvParams g, int epi, int M, const int* dyn_M, cudaStream_t s, bool pdl) {
-    if (dyn_M) {
+    if (dyn_M) {  // M is the static upper bound of *dyn_M (<= kMaxRows)
         g.dyn_M = dyn_M;
         g.row0 = 0;
-        g.M = kMaxRows;
+        g.M = std::min(M, kMaxRows);
         FL_CHECK_CUDA(launch_gemv_auto(g, epi, s, pdl));
         return FL_OK;
     }

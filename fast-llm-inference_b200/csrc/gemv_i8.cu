@@ -157,7 +157,7 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const GemvParams p) {
     pdl_wait();
     if (p.done && *p.done) return;
     int rows = p.M;
-    if (p.dyn_M) rows = min(*p.dyn_M - p.row0, kMaxRows);
+    if (p.dyn_M) rows = min(*p.dyn_M - p.row0, p.M);
     rows = min(rows, MMAX);
     if (rows <= 0) return;
 
@@ -309,7 +309,7 @@ cudaError_t launch_t(const GemvParams& p, cudaStream_t s, bool pdl) {
 
 template <bool ROWMODE, bool PAIRSAT, int EPI>
 cudaError_t launch_m(const GemvParams& p, cudaStream_t s, bool pdl) {
-    const int m = p.dyn_M ? kMaxRows : p.M;
+    const int m = p.M;
     if (m <= 1) return launch_t<1, ROWMODE, PAIRSAT, EPI>(p, s, pdl);
     if (m <= 2) return launch_t<2, ROWMODE, PAIRSAT, EPI>(p, s, pdl);
     if (m <= 4) return launch_t<4, ROWMODE, PAIRSAT, EPI>(p, s, pdl);
@@ -333,7 +333,7 @@ cudaError_t launch_gemv(const GemvParams& p, int epi, bool rowmode, bool pairsat
                         bool pdl) {
     if (p.K % 32 != 0 || p.N <= 0 || p.K <= 0) return cudaErrorInvalidValue;
     if (p.x && p.K % 128 != 0) return cudaErrorInvalidValue;
-    if (!p.dyn_M && (p.M <= 0 || p.M > kMaxRows)) return cudaErrorInvalidValue;
+    if (p.M <= 0 || p.M > kMaxRows) return cudaErrorInvalidValue;
     switch (epi) {
         case EPI_STORE: return launch_e<EPI_STORE>(p, rowmode, pairsat, s, pdl);
         case EPI_RESID: return launch_e<EPI_RESID>(p, rowmode, pairsat, s, pdl);

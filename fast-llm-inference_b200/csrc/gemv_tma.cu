@@ -21,11 +21,15 @@ namespace fl {
 
 namespace {
 
-constexpr int kCWarps = 8;                   // consumer warps
+constexpr int kCWarps = 16;                  // consumer warps
 constexpr int kThreads = (kCWarps + 1) * 32; // + producer warp
 constexpr int kRowsPerStage = 2 * kCWarps;   // one row pair per consumer warp
 constexpr int kMaxStages = 8;
-constexpr int kSmemLimit = 227 * 1024;
+// Ring budget: ~half the SM's shared memory, so that the CTA of the next
+// kernel in the stream (launched early by PDL) fits beside this one and
+// starts its own weight stream while this kernel drains.
+constexpr int kSmemLimit = 112 * 1024;
+constexpr int kMaxSeg = 2048;
 
 struct TmaShape {
     int seg;      // bytes of one row segment (K / nseg)
@@ -35,25 +39,31 @@ struct TmaShape {
     size_t act_bytes;
 };
 
-__host__ __device__ inline int seg_bytes(int K) {
-    for (int n = 1; n <= 64; n++)
-        if (K % n == 0 && (K / n) <= 4096 && (K / n) % 512 == 0) return K / n;
-    return 0;
-}
+inline size_t stage_bytes(int seg) { return (size_t)kRowsPerStage * seg + (size_t)kRowsPerStage * (seg / 16); }
 
-inline bool tma_shape(int K, int mmax, TmaShape& s) {
-    if (K % 256 != 0) return false;
-    s.seg = seg_bytes(K);
-    if (!s.seg) return false;
-    s.nseg = K / s.seg;
-    s.act_bytes = ((size_t)mmax * K + 127) & ~(size_t)127;
-    const size_t stage = (size_t)kRowsPerStage * s.seg + (size_t)kRowsPerStage * (s.seg / 16);
+// Ring geometry for K and `mrows` activation rows held in shared memory:
+// the largest row segment (a multiple of 512 bytes dividing K, at most
+// kMaxSeg) that still leaves >= 3 stages, else >= 2.
+inline bool tma_shape(int K, int mrows, TmaShape& s) {
+    if (K % 256 != 0 || mrows < 1 || mrows > kMaxRows) return false;
+    s.act_bytes = ((size_t)mrows * K + 127) & ~(size_t)127;
+    if (s.act_bytes + 256 >= (size_t)kSmemLimit) return false;
     const size_t avail = kSmemLimit - s.act_bytes - 256;
-    s.stages = (int)(avail / stage);
-    if (s.stages > kMaxStages) s.stages = kMaxStages;
-    if (s.stages < 2) return false;
-    s.smem = s.act_bytes + (size_t)s.stages * stage;
-    return true;
+    for (int want = 3; want >= 2; want--) {
+        for (int n = 1; n <= 64; n++) {
+            if (K % n || (K / n) > kMaxSeg || (K / n) % 512) continue;
+            const int seg = K / n;
+            const int st = (int)(avail / stage_bytes(seg));
+            if (st >= want) {
+                s.seg = seg;
+                s.nseg = n;
+                s.stages = st > kMaxStages ? kMaxStages : st;
+                s.smem = s.act_bytes + (size_t)s.stages * stage_bytes(seg);
+                return true;
+            }
+        }
+    }
+    return false;
 }
 
 template <bool PAIR_ROWS>
@@ -139,8 +149,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_tma_kernel(const GemvParams 
         for (int i = 0; i < first; i++) mbar_wait(&full_bar[i], 0);
         return;
     }
+    // p.M bounds the rows (shared memory holds p.M rows); dyn_M narrows it.
     int rows_m = p.M;
-    if (p.dyn_M) rows_m = min(*p.dyn_M - p.row0, kMaxRows);
+    if (p.dyn_M) rows_m = min(*p.dyn_M - p.row0, p.M);
     rows_m = min(rows_m, MMAX);
     if (p.x) {
         const int src0 = p.x_row_dyn ? *p.x_row_dyn : p.row0;
@@ -338,8 +349,7 @@ int take_device_error() {
 }
 
 cudaError_t launch_gemv_auto(const GemvParams& p, int epi, cudaStream_t s, bool pdl) {
-    const int m = p.dyn_M ? kMaxRows : p.M;
-    if (epi != EPI_DOTS && tma_gemv_supported(p.K, m)) return launch_gemv_tma(p, epi, s, pdl);
+    if (epi != EPI_DOTS && tma_gemv_supported(p.K, p.M)) return launch_gemv_tma(p, epi, s, pdl);
     return launch_gemv(p, epi, false, false, s, pdl);
 }
 
@@ -347,16 +357,17 @@ int gemv_auto_grid(int N, int K) { return tma_gemv_supported(K, kMaxRows) ? tma_
 
 bool tma_gemv_supported(int K, int M) {
     TmaShape sh;
-    return tma_shape(K, M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8, sh);
+    return tma_shape(K, M, sh);
 }
 
+// p.M: rows held in shared memory (static count, or the upper bound of
+// *p.dyn_M), 1..kMaxRows.
 cudaError_t launch_gemv_tma(const GemvParams& p, int epi, cudaStream_t s, bool pdl) {
-    const int mmax = p.dyn_M ? kMaxRows : p.M;
-    const int mm = mmax <= 1 ? 1 : mmax <= 2 ? 2 : mmax <= 4 ? 4 : 8;
+    if (p.M <= 0 || p.M > kMaxRows) return cudaErrorInvalidValue;
+    const int mm = p.M <= 1 ? 1 : p.M <= 2 ? 2 : p.M <= 4 ? 4 : 8;
     TmaShape sh;
-    if (!tma_shape(p.K, mm, sh)) return cudaErrorInvalidValue;
+    if (!tma_shape(p.K, p.M, sh)) return cudaErrorInvalidValue;
     if (p.x && p.K % 128 != 0) return cudaErrorInvalidValue;
-    if (!p.dyn_M && (p.M <= 0 || p.M > kMaxRows)) return cudaErrorInvalidValue;
     switch (epi) {
         case EPI_STORE: return launch_e<EPI_STORE>(p, mm, sh, s, pdl);
         case EPI_RESID: return launch_e<EPI_RESID>(p, mm, sh, s, pdl);
