@@ -21,6 +21,7 @@
 
 #include "fl_common.cuh"
 #include "fl_kernels.h"
+#include "fl_layout.cuh"
 #include "fl_runtime.h"
 #include "fl_state.h"
 
@@ -32,6 +33,7 @@ struct Linear {
     int8_t* w = nullptr;
     __half* s = nullptr;
     int N = 0, K = 0;
+    int P = 0;  // tiled-layout panel width (fl_layout.cuh), 0 = row-major
     unsigned need = 0, have = 0;  // bit masks of the source tensors loaded
 };
 
@@ -102,6 +104,8 @@ int alloc_linear(Linear& l, int N, int K, unsigned need) {
     l.K = K;
     l.need = need;
     l.have = 0;
+    // The TMA-ring GEMV reads the tiled layout; shapes it cannot serve stay row-major.
+    l.P = tma_gemv_supported(N, K, 1) ? panel_width(K) : 0;
     FL_CHECK_CUDA(cudaMalloc(&l.w, (size_t)N * K));
     FL_CHECK_CUDA(cudaMalloc(&l.s, (size_t)N * (K / 32) * sizeof(__half)));
     return FL_OK;
@@ -162,12 +166,7 @@ void free_stack(Stack& S) {
 int put_rows(Linear& l, int dst_row0, int dst_stride, const int8_t* w, const uint16_t* sc, int rows,
              int cols, cudaStream_t s) {
     if (cols != l.K) return set_error(FL_E_INVAL, "load_linear: column count does not match the model");
-    const size_t kb = (size_t)cols / 32;
-    FL_CHECK_CUDA(cudaMemcpy2DAsync(l.w + (size_t)dst_row0 * cols, (size_t)dst_stride * cols, w, cols, cols,
-                                    rows, cudaMemcpyHostToDevice, s));
-    FL_CHECK_CUDA(cudaMemcpy2DAsync(l.s + (size_t)dst_row0 * kb, (size_t)dst_stride * kb * sizeof(__half), sc,
-                                    kb * sizeof(__half), kb * sizeof(__half), rows, cudaMemcpyHostToDevice, s));
-    FL_CHECK_CUDA(cudaStreamSynchronize(s));
+    FL_CHECK_CUDA(upload_rows(l.w, l.s, l.N, l.K, l.P, dst_row0, dst_stride, w, sc, rows, s));
     return FL_OK;
 }
 
@@ -184,6 +183,7 @@ GemvParams gemv_base(const Linear& l, const uint8_t* aq, const int* done) {
     GemvParams g = {};
     g.aq = aq;
     g.w = l.w;
+    g.P = l.P;
     g.sblk = l.s;
     g.N = l.N;
     g.K = l.K;

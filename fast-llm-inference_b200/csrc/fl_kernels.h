@@ -27,7 +27,8 @@ struct KvLayer {
 
 struct GemvParams {
     const uint8_t* aq;        // [rows, K] quantized activations
-    const int8_t* w;          // [N, K]
+    const int8_t* w;          // [N, K]: row-major (P == 0) or tiled (fl_layout.cuh)
+    int P;                    // tiled-layout panel width; 0 = plain row-major
     const __half* sblk;       // [N, K/32] block scales (block mode)
     const float* srow;        // [N] per-row scales (per-row mode)
     int M;                    // rows in this launch (<= kMaxRows)
@@ -72,7 +73,13 @@ int gemv_grid(int N);
 // Persistent TMA-ring variant for block-mode weights (gemv_tma.cu): one CTA
 // per SM. Supported when K % 256 == 0 and the ring fits (tma_gemv_supported).
 cudaError_t launch_gemv_tma(const GemvParams& p, int epi, cudaStream_t s, bool pdl);
-bool tma_gemv_supported(int K, int M);
+bool tma_gemv_supported(int N, int K, int M);
+
+// Copies `rows` host rows (int8 [rows, K], fp16 scales [rows, K/32]) into a
+// device matrix of N rows at rows dst_row0 + i * dst_stride, in the tiled
+// layout when P != 0 (a device relayout kernel) or row-major when P == 0.
+cudaError_t upload_rows(int8_t* dst_w, __half* dst_s, int N, int K, int P, int dst_row0, int dst_stride,
+                        const int8_t* host_w, const uint16_t* host_s, int rows, cudaStream_t s);
 int tma_gemv_grid();
 // Block-mode GEMV through the TMA kernel when the shape allows it, else the
 // register-streamed kernel; gemv_auto_grid is the grid it uses for up to

@@ -29,6 +29,7 @@ struct DevTensor {
     int scale_block;
     int pairsat;       // per-row mode with max|w| > 64
     int device;
+    int P;             // tiled-layout panel width (block mode), 0 = row-major
 };
 
 int upload_tensor(dequantized_tensor_t* t);

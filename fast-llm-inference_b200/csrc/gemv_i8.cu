@@ -15,6 +15,7 @@
 // issued before griddepcontrol.wait so it overlaps the previous kernel.
 #include "fl_common.cuh"
 #include "fl_kernels.h"
+#include "fl_layout.cuh"
 
 namespace fl {
 
@@ -39,6 +40,13 @@ __device__ __forceinline__ void load_batch(Batch& b, const GemvParams& p, const 
         const int k = c * 512 + lane * 16;
         const bool ok = (c < nchunk) && (k < p.K);
         if (ok) {
+            if (p.P) {  // tiled layout (fl_layout.cuh)
+                b.w0[u] = ld_stream16(p.w + tiled_w_off(p.N, p.P, n0, k >> 4));
+                b.w1[u] = ld_stream16(p.w + tiled_w_off(p.N, p.P, n1, k >> 4));
+                b.s0[u] = __half2float(p.sblk[tiled_s_off(p.N, p.P, n0, k >> 5)]);
+                b.s1[u] = __half2float(p.sblk[tiled_s_off(p.N, p.P, n1, k >> 5)]);
+                continue;
+            }
             b.w0[u] = ld_stream16(w0 + k);
             b.w1[u] = ld_stream16(w1 + k);
             if (!ROWMODE) {
@@ -328,6 +336,63 @@ cudaError_t launch_e(const GemvParams& p, bool rowmode, bool pairsat, cudaStream
 }  // namespace
 
 int gemv_grid(int N) { return ((N + 1) / 2 + kWarps - 1) / kWarps; }
+
+namespace {
+
+__global__ void relayout_w_kernel(const int8_t* src, int rows, int K, int8_t* dst, int N, int P, int row0,
+                                  int stride) {
+    const int cpr = K >> 4;
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)rows * cpr) return;
+    const int r = (int)(i / cpr), c = (int)(i - (long long)r * cpr);
+    const int n = row0 + r * stride;
+    *reinterpret_cast<uint4*>(dst + tiled_w_off(N, P, n, c)) =
+        *reinterpret_cast<const uint4*>(src + (size_t)r * K + (size_t)c * 16);
+}
+
+__global__ void relayout_s_kernel(const __half* src, int rows, int K, __half* dst, int N, int P, int row0,
+                                  int stride) {
+    const int bpr = K >> 5;
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)rows * bpr) return;
+    const int r = (int)(i / bpr), b = (int)(i - (long long)r * bpr);
+    dst[tiled_s_off(N, P, row0 + r * stride, b)] = src[(size_t)r * bpr + b];
+}
+
+}  // namespace
+
+cudaError_t upload_rows(int8_t* dst_w, __half* dst_s, int N, int K, int P, int dst_row0, int dst_stride,
+                        const int8_t* host_w, const uint16_t* host_s, int rows, cudaStream_t s) {
+    const size_t kb = (size_t)K / 32;
+    if (P == 0) {
+        cudaError_t e = cudaMemcpy2DAsync(dst_w + (size_t)dst_row0 * K, (size_t)dst_stride * K, host_w, K, K, rows,
+                                          cudaMemcpyHostToDevice, s);
+        if (e != cudaSuccess) return e;
+        e = cudaMemcpy2DAsync(dst_s + (size_t)dst_row0 * kb, (size_t)dst_stride * kb * sizeof(__half), host_s,
+                              kb * sizeof(__half), kb * sizeof(__half), rows, cudaMemcpyHostToDevice, s);
+        if (e != cudaSuccess) return e;
+        return cudaStreamSynchronize(s);
+    }
+    if (K % P != 0 || P % 128 != 0 || dst_row0 + (rows - 1) * dst_stride >= N) return cudaErrorInvalidValue;
+    int8_t* tw = nullptr;
+    __half* ts = nullptr;
+    cudaError_t e = cudaMalloc(&tw, (size_t)rows * K);
+    if (e == cudaSuccess) e = cudaMalloc(&ts, (size_t)rows * kb * sizeof(__half));
+    if (e == cudaSuccess) e = cudaMemcpyAsync(tw, host_w, (size_t)rows * K, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(ts, host_s, (size_t)rows * kb * sizeof(__half), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) {
+        const long long nw = (long long)rows * (K / 16), ns = (long long)rows * (long long)kb;
+        relayout_w_kernel<<<(unsigned)((nw + 255) / 256), 256, 0, s>>>(tw, rows, K, dst_w, N, P, dst_row0, dst_stride);
+        relayout_s_kernel<<<(unsigned)((ns + 255) / 256), 256, 0, s>>>(ts, rows, K, dst_s, N, P, dst_row0,
+                                                                        dst_stride);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    cudaFree(tw);
+    cudaFree(ts);
+    return e;
+}
 
 cudaError_t launch_gemv(const GemvParams& p, int epi, bool rowmode, bool pairsat, cudaStream_t s,
                         bool pdl) {

@@ -1,72 +1,64 @@
-// Persistent INT8 GEMV streaming weights through a TMA bulk-copy ring
-// (sm_100a). Same contract and epilogues as gemv_i8.cu's block-mode kernel
-// (matmul_dequantized, dequantized_tensor.c:204-247, with the fused layer
-// epilogues of inference.c:286-386), built for bs1 decode where a launch is
-// only 9-100 MB and must not be latency bound:
+// Persistent INT8 GEMV / skinny GEMM (M <= 8 activation rows) streaming
+// weights through a TMA bulk-copy ring (sm_100a).
 //
-//   * one CTA per SM, each owning a contiguous range of weight-row pairs;
-//   * a producer warp issues 1-D cp.async.bulk copies of whole row segments
-//     (weights + their fp16 block scales) into an S-stage shared-memory ring
-//     -- up to ~200 KB in flight per SM -- starting BEFORE
-//     griddepcontrol.wait, so the stream overlaps the previous kernel's tail;
-//   * 8 consumer warps each take one row pair of a 16-row stage, multiply
-//     with dp4a against the u8 activations held in shared memory, and release
-//     the slot through an mbarrier;
+// Contract and epilogues as matmul_dequantized (fast_llm/src/kernels/
+// dequantized_tensor.c:204-247) with the fused layer epilogues of
+// transformer_layer (fast_llm/src/inference.c:286-386). Built for bs1 decode,
+// where one launch is only 9-100 MB of weights:
+//
+//   * one CTA per SM; CTA c owns a contiguous range of 8-row units;
+//   * weights are in the tiled layout (fl_layout.cuh): a ring stage is 16
+//     rows x one K-panel, moved by ONE 1-D cp.async.bulk (+ one for its fp16
+//     block scales) issued by a producer warp -- the first stages before
+//     griddepcontrol.wait, so the stream overlaps the previous kernel;
+//   * M == 1: 8 consumer warps, a row pair each, u8 x s8 dp4a (the
+//     instruction count per weight byte is low enough);
+//   * M >= 2: dp4a would be instruction bound, so each consumer warp runs
+//     mma.sync m16n8k32 u8 x s8 -> s32 on its share of the stage's
+//     32-element blocks (B operand = 8 weight rows via ldmatrix, A operand =
+//     the activation rows), scales each block's int32 by its fp16 scale
+//     and reduces across warps once per 16-row tile;
 //   * every mbarrier wait is bounded (fl_tma.cuh).
 #include "fl_common.cuh"
 #include "fl_kernels.h"
+#include "fl_layout.cuh"
 #include "fl_tma.cuh"
 
 namespace fl {
 
 namespace {
 
-constexpr int kCWarps = 16;                  // consumer warps
+constexpr int kCWarps = 8;                   // consumer warps
 constexpr int kThreads = (kCWarps + 1) * 32; // + producer warp
-constexpr int kRowsPerStage = 2 * kCWarps;   // one row pair per consumer warp
+constexpr int kStageRows = 16;
 constexpr int kMaxStages = 8;
-// Ring budget: ~half the SM's shared memory, so that the CTA of the next
-// kernel in the stream (launched early by PDL) fits beside this one and
-// starts its own weight stream while this kernel drains.
-constexpr int kSmemLimit = 112 * 1024;
-constexpr int kMaxSeg = 2048;
+// Dynamic shared memory budget: 227 KB per block minus the static reduction
+// buffers and barriers (~8.5 KB).
+constexpr int kSmemLimit = 216 * 1024;
 
-struct TmaShape {
-    int seg;      // bytes of one row segment (K / nseg)
-    int nseg;
-    int stages;
-    size_t smem;  // dynamic shared memory
-    size_t act_bytes;
+struct Geo {
+    int P;         // panel width (bytes of a stage row)
+    int npan;      // K / P
+    int S;         // ring stages
+    int act_ld;    // activation row stride in shared memory (K + 16)
+    int act_bytes; // shared bytes of the activation rows
 };
 
-inline size_t stage_bytes(int seg) { return (size_t)kRowsPerStage * seg + (size_t)kRowsPerStage * (seg / 16); }
+__host__ __device__ inline size_t slot_bytes(int P) { return (size_t)kStageRows * P + (size_t)kStageRows * (P / 16); }
 
-// Ring geometry for K and `mrows` activation rows held in shared memory:
-// the largest row segment (a multiple of 512 bytes dividing K, at most
-// kMaxSeg) that still leaves >= 3 stages, else >= 2.
-inline bool tma_shape(int K, int mrows, TmaShape& s) {
-    if (K % 256 != 0 || mrows < 1 || mrows > kMaxRows) return false;
-    s.act_bytes = ((size_t)mrows * K + 127) & ~(size_t)127;
-    if (s.act_bytes + 256 >= (size_t)kSmemLimit) return false;
-    const size_t avail = kSmemLimit - s.act_bytes - 256;
-    for (int want = 3; want >= 2; want--) {
-        for (int n = 1; n <= 64; n++) {
-            if (K % n || (K / n) > kMaxSeg || (K / n) % 512) continue;
-            const int seg = K / n;
-            const int st = (int)(avail / stage_bytes(seg));
-            if (st >= want) {
-                s.seg = seg;
-                s.nseg = n;
-                s.stages = st > kMaxStages ? kMaxStages : st;
-                s.smem = s.act_bytes + (size_t)s.stages * stage_bytes(seg);
-                return true;
-            }
-        }
-    }
-    return false;
+inline bool make_geo(int K, int mrows, Geo& g) {
+    g.P = panel_width(K);
+    if (!g.P || mrows < 1 || mrows > kMaxRows) return false;
+    g.npan = K / g.P;
+    g.act_ld = K + 16;
+    g.act_bytes = ((mrows * g.act_ld) + 127) & ~127;
+    const long avail = (long)kSmemLimit - g.act_bytes - 256;
+    const int S = (int)(avail / (long)slot_bytes(g.P));
+    if (S < 2) return false;
+    g.S = S > kMaxStages ? kMaxStages : S;
+    return true;
 }
 
-template <bool PAIR_ROWS>
 __device__ __forceinline__ int dot16(const uint4& a, const uint4& w) {
     int d = dp4a_us(a.x, w.x, 0);
     d = dp4a_us(a.y, w.y, d);
@@ -74,29 +66,94 @@ __device__ __forceinline__ int dot16(const uint4& a, const uint4& w) {
     return dp4a_us(a.w, w.w, d);
 }
 
-template <int MMAX, int EPI>
-__global__ void __launch_bounds__(kThreads, 1) gemv_tma_kernel(const GemvParams p, const int seg, const int nseg,
-                                                               const int S, const int act_bytes) {
+__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+// D(16x8, s32) = A(16x32, u8, row) x B(32x8, s8, col); A rows 8-15 are zero,
+// so only the first two accumulator registers carry results.
+__device__ __forceinline__ void mma_u8s8(uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1, int& d0, int& d1) {
+    int c2, c3;
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+        : "=r"(d0), "=r"(d1), "=r"(c2), "=r"(c3)
+        : "r"(a0), "r"(0), "r"(a2), "r"(0), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+// Epilogue of one weight-row pair (n0, n0 + 1) for activation row r.
+template <int EPI>
+__device__ __forceinline__ void pair_epilogue(const GemvParams& p, int r, int n0, bool has1, float y0, float y1,
+                                              unsigned long long* best_s) {
+    if (EPI == EPI_STORE || EPI == EPI_LOGITS) {
+        p.out[(size_t)r * p.ldo + n0] = y0;
+        if (has1) p.out[(size_t)r * p.ldo + n0 + 1] = y1;
+        if (EPI == EPI_LOGITS) {
+            unsigned long long k = argmax_key(y0, n0);
+            if (has1) {
+                const unsigned long long k1 = argmax_key(y1, n0 + 1);
+                k = k1 > k ? k1 : k;
+            }
+            atomicMax(&best_s[r - p.row0], k);
+        }
+    } else if (EPI == EPI_RESID) {
+        float* o = p.out + (size_t)r * p.ldo + n0;
+        o[0] = __fadd_rn(o[0], y0);
+        if (has1) o[1] = __fadd_rn(o[1], y1);
+    } else if (EPI == EPI_QKV) {
+        float v0 = y0, v1 = y1;
+        const int qkd = p.q_dim + p.kv_dim;
+        if (n0 < qkd) {
+            // inference.c:165-173 adjacent-pair rotation at position pos[r]
+            const int ii = (n0 < p.q_dim ? n0 : n0 - p.q_dim) % p.head_dim;
+            const float freq = __fdiv_rn(1.0f, powf(p.theta, __fdiv_rn((float)ii, (float)p.head_dim)));
+            const float ang = __fmul_rn((float)p.pos[r], freq);
+            float sn, cs;
+            sincosf(ang, &sn, &cs);
+            v0 = __fsub_rn(__fmul_rn(y0, cs), __fmul_rn(y1, sn));
+            v1 = __fadd_rn(__fmul_rn(y0, sn), __fmul_rn(y1, cs));
+        }
+        if (n0 < p.q_dim) {
+            p.q_out[(size_t)r * p.q_dim + n0] = v0;
+            p.q_out[(size_t)r * p.q_dim + n0 + 1] = v1;
+        } else {
+            const bool is_k = n0 < qkd;
+            const int c = n0 - (is_k ? p.q_dim : qkd);
+            const int h = c / p.head_dim;
+            const int dd = c - h * p.head_dim;
+            const int slot = *p.slot_base + r;
+            const int page = p.block_table[slot / kPageSize];
+            const size_t off = (((size_t)page * p.kv_heads + h) * kPageSize + (slot % kPageSize)) * p.head_dim + dd;
+            *reinterpret_cast<__half2*>((is_k ? p.kv.k : p.kv.v) + off) = __floats2half2_rn(v0, v1);
+        }
+    } else if (EPI == EPI_SWIGLU) {
+        // rows (n0, n0 + 1) = (gate_i, up_i): activations_avx2.c:86-105
+        const float h = __fmul_rn(__fmul_rn(y0, poly_sigmoid(y0)), y1);
+        p.hq[(size_t)r * p.F + (n0 >> 1)] = (uint8_t)quant_u8(h);
+    }
+}
+
+template <int MMAX, int EPI, bool MMA>
+__global__ void __launch_bounds__(kThreads, 1) gemv_tma_kernel(const GemvParams p, const Geo geo) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full_bar[kMaxStages];
     __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
-    __shared__ unsigned long long red_s[kCWarps][kMaxRows];
+    __shared__ unsigned long long best_s[kMaxRows];
+    __shared__ float red[2][kCWarps][32][4];
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int K = p.K;
-    const int npairs = (p.N + 1) >> 1;
-    const int pr0 = (int)(((long long)npairs * blockIdx.x) / gridDim.x);
-    const int pr1 = (int)(((long long)npairs * (blockIdx.x + 1)) / gridDim.x);
-    const int row0 = 2 * pr0;
-    const int row1 = min(2 * pr1, p.N);
-    const int nrows = row1 - row0;
-    const int nrounds = (nrows + kRowsPerStage - 1) / kRowsPerStage;
-    const int total = nrounds * nseg;
-    const int sw = kRowsPerStage * seg;           // weight bytes of a full stage
-    const int ss = kRowsPerStage * (seg / 16);    // scale bytes of a full stage
+    const int N = p.N, K = p.K, P = geo.P, npan = geo.npan, S = geo.S;
+    const int nunits = N >> 3;
+    const int u0 = (int)(((long long)nunits * blockIdx.x) / gridDim.x);
+    const int u1 = (int)(((long long)nunits * (blockIdx.x + 1)) / gridDim.x);
+    const int row0 = u0 * 8, row1 = u1 * 8;
+    const int ntiles = (row1 - row0 + kStageRows - 1) / kStageRows;
+    const int total = ntiles * npan;
+    const size_t slot = slot_bytes(P);
     uint8_t* act = smem;
-    uint8_t* ring = smem + act_bytes;
+    uint8_t* ring = smem + geo.act_bytes;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; i++) {
@@ -105,37 +162,31 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_tma_kernel(const GemvParams 
         }
         mbar_fence_init();
     }
+    if (threadIdx.x < kMaxRows) best_s[threadIdx.x] = 0ull;
     __syncthreads();
     pdl_trigger();
-
-    const int8_t* wbase = p.w;
-    const uint8_t* sbase = reinterpret_cast<const uint8_t*>(p.sblk);
-    const size_t srow = (size_t)(K / 16);  // scale bytes per weight row
 
     if (warp == kCWarps) {
         // ---------------- producer ----------------
         if (lane != 0) return;
-        const int first = total < S ? total : S;
+        const uint8_t* sbase = reinterpret_cast<const uint8_t*>(p.sblk);
         auto issue = [&](int i) {
-            const int slot = i % S;
-            const int round = i / nseg, sg = i - round * nseg;
-            const int r = row0 + round * kRowsPerStage;
-            const int rows = min(kRowsPerStage, row1 - r);
-            uint8_t* dw = ring + (size_t)slot * (sw + ss);
-            uint8_t* ds = dw + sw;
-            mbar_arrive_expect_tx(&full_bar[slot], (uint32_t)(rows * (seg + seg / 16)));
-            for (int j = 0; j < rows; j++) {
-                bulk_g2s(dw + (size_t)j * seg, wbase + (size_t)(r + j) * K + (size_t)sg * seg, seg, &full_bar[slot]);
-                bulk_g2s(ds + (size_t)j * (seg / 16), sbase + (size_t)(r + j) * srow + (size_t)sg * (seg / 16),
-                         seg / 16, &full_bar[slot]);
-            }
+            const int sl = i % S;
+            const int tile = i / npan, pan = i - tile * npan;
+            const int r = row0 + tile * kStageRows;
+            const int rows = min(kStageRows, row1 - r);
+            uint8_t* dw = ring + (size_t)sl * slot;
+            uint8_t* ds = dw + (size_t)kStageRows * P;
+            mbar_arrive_expect_tx(&full_bar[sl], (uint32_t)(rows * P + rows * (P / 16)));
+            bulk_g2s(dw, p.w + ((size_t)pan * N + r) * P, (uint32_t)(rows * P), &full_bar[sl]);
+            bulk_g2s(ds, sbase + ((size_t)pan * N + r) * (P / 16), (uint32_t)(rows * (P / 16)), &full_bar[sl]);
         };
+        const int first = total < S ? total : S;
         for (int i = 0; i < first; i++) issue(i);  // weights need no dependency
         pdl_wait();
         if (p.done && *p.done) return;
         for (int i = first; i < total; i++) {
-            const int slot = i % S;
-            if (!mbar_wait(&empty_bar[slot], ((i / S) - 1) & 1)) return;
+            if (!mbar_wait(&empty_bar[i % S], ((i / S) - 1) & 1)) return;
             issue(i);
         }
         return;
@@ -144,155 +195,145 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_tma_kernel(const GemvParams 
     // ---------------- consumers ----------------
     pdl_wait();
     if (p.done && *p.done) {
-        // drain the prefetched stages before leaving
         const int first = total < S ? total : S;
-        for (int i = 0; i < first; i++) mbar_wait(&full_bar[i], 0);
+        for (int i = 0; i < first; i++) mbar_wait(&full_bar[i], 0);  // drain the prefetch
         return;
     }
-    // p.M bounds the rows (shared memory holds p.M rows); dyn_M narrows it.
     int rows_m = p.M;
     if (p.dyn_M) rows_m = min(*p.dyn_M - p.row0, p.M);
-    rows_m = min(rows_m, MMAX);
+    rows_m = max(0, min(rows_m, MMAX));
+    const int ald = geo.act_ld;
     if (p.x) {
         const int src0 = p.x_row_dyn ? *p.x_row_dyn : p.row0;
-        act_prologue(act, p.x + (size_t)src0 * K, K, max(rows_m, 0), p.norm, p.eps, warp, lane, kCWarps);
+        for (int m = warp; m < rows_m; m += kCWarps)
+            act_prologue(act + (size_t)m * ald, p.x + (size_t)(src0 + m) * K, K, 1, p.norm, p.eps, 0, lane, 1);
     } else {
         const int K16 = K >> 4;
         const uint4* src = reinterpret_cast<const uint4*>(p.aq + (size_t)p.row0 * K);
-        uint4* dst = reinterpret_cast<uint4*>(act);
-        const int tot = max(rows_m, 0) * K16;
-        for (int i = threadIdx.x; i < tot; i += kCWarps * 32) dst[i] = src[i];
+        for (int i = threadIdx.x; i < rows_m * K16; i += kCWarps * 32) {
+            const int m = i / K16, c = i - m * K16;
+            *reinterpret_cast<uint4*>(act + (size_t)m * ald + (size_t)c * 16) = src[(size_t)m * K16 + c];
+        }
     }
     asm volatile("bar.sync 1, %0;" ::"n"(kCWarps * 32) : "memory");
 
-    float f0[MMAX], f1[MMAX];
-#pragma unroll
-    for (int m = 0; m < MMAX; m++) f0[m] = f1[m] = 0.0f;
-    unsigned long long best = 0ull;  // EPI_LOGITS: lane m keeps row m's best key
-    const uint4* act4 = reinterpret_cast<const uint4*>(act);
-    const int K16 = K >> 4;
-    const int nj = seg >> 9;  // 512-byte sweeps per segment
-
-    for (int i = 0; i < total; i++) {
-        const int slot = i % S;
-        const int round = i / nseg, sg = i - round * nseg;
-        const int r = row0 + round * kRowsPerStage;
-        const int rows = min(kRowsPerStage, row1 - r);
-        // On a timeout stop consuming but still reach the final barrier below.
-        if (!mbar_wait(&full_bar[slot], (i / S) & 1)) break;
-        const int lr = 2 * warp;  // local row of this warp's pair
-        if (lr < rows && rows_m > 0) {
-            const bool two = lr + 1 < rows;
-            const uint8_t* dw = ring + (size_t)slot * (sw + ss);
-            const __half* ds = reinterpret_cast<const __half*>(dw + sw);
-            const uint4* w0p = reinterpret_cast<const uint4*>(dw + (size_t)lr * seg);
-            const uint4* w1p = reinterpret_cast<const uint4*>(dw + (size_t)(two ? lr + 1 : lr) * seg);
-            const __half* s0p = ds + (size_t)lr * (seg / 32);
-            const __half* s1p = ds + (size_t)(two ? lr + 1 : lr) * (seg / 32);
-            for (int j = 0; j < nj; j++) {
-                const int kl = j * 512 + lane * 16;  // byte within the segment
-                const uint4 w0 = w0p[kl >> 4];
-                const uint4 w1 = w1p[kl >> 4];
-                const float s0 = __half2float(s0p[kl >> 5]);
-                const float s1 = __half2float(s1p[kl >> 5]);
-                const int ka = (sg * seg + kl) >> 4;
-#pragma unroll
-                for (int m = 0; m < MMAX; m++) {
-                    if (m < rows_m) {
-                        const uint4 a = act4[m * K16 + ka];
-                        f0[m] = __fmaf_rn(i2f_exact(dot16<true>(a, w0)), s0, f0[m]);
-                        f1[m] = __fmaf_rn(i2f_exact(dot16<true>(a, w1)), s1, f1[m]);
-                    }
+    const int bpp = P >> 5;   // 32-element blocks per panel row
+    bool bad = false;
+    if (!MMA) {
+        // ---- dp4a path: warp = row pair (2w, 2w + 1) of each 16-row stage ----
+        float f0 = 0.0f, f1 = 0.0f;
+        const int lr = 2 * warp;
+        const int nj = P >> 9;
+        for (int i = 0; i < total; i++) {
+            const int sl = i % S;
+            const int tile = i / npan, pan = i - tile * npan;
+            const int r = row0 + tile * kStageRows;
+            const int rows = min(kStageRows, row1 - r);
+            // After a timed-out wait keep looping without waiting or computing,
+            // so every warp still reaches the same barriers and the kernel ends.
+            if (!bad && !mbar_wait(&full_bar[sl], (i / S) & 1)) bad = true;
+            if (!bad && lr < rows && rows_m > 0) {
+                const bool two = lr + 1 < rows;
+                const uint8_t* dw = ring + (size_t)sl * slot;
+                const __half* ds = reinterpret_cast<const __half*>(dw + (size_t)kStageRows * P);
+                const int ra = lr, rb = two ? lr + 1 : lr;
+                const uint8_t* wa = dw + (size_t)ra * P;
+                const uint8_t* wb = dw + (size_t)rb * P;
+                for (int j = 0; j < nj; j++) {
+                    const int c = j * 32 + lane;  // logical chunk within the panel row
+                    const uint4 w0 = *reinterpret_cast<const uint4*>(wa + swz_chunk(c, r + ra) * 16);
+                    const uint4 w1 = *reinterpret_cast<const uint4*>(wb + swz_chunk(c, r + rb) * 16);
+                    const float s0 = __half2float(ds[ra * bpp + (c >> 1)]);
+                    const float s1 = __half2float(ds[rb * bpp + (c >> 1)]);
+                    const uint4 a = *reinterpret_cast<const uint4*>(act + (size_t)pan * P + (size_t)c * 16);
+                    f0 = __fmaf_rn(i2f_exact(dot16(a, w0)), s0, f0);
+                    f1 = __fmaf_rn(i2f_exact(dot16(a, w1)), s1, f1);
                 }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty_bar[sl]);
+            if (pan == npan - 1) {
+                const float t0 = __fdiv_rn(warp_sum(f0), 127.0f);
+                const float t1 = __fdiv_rn(warp_sum(f1), 127.0f);
+                f0 = f1 = 0.0f;
+                if (lane == 0 && lr < rows && rows_m > 0)
+                    pair_epilogue<EPI>(p, p.row0, r + lr, lr + 1 < rows, t0, t1, best_s);
             }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty_bar[slot]);
-
-        if (sg == nseg - 1) {
-            // the pair (r + lr, r + lr + 1) is complete: reduce and apply the epilogue
-            const int n0 = r + lr;
-            const bool active = lr < rows;
-            const bool has1 = active && lr + 1 < rows;
-            float y_own = 0.0f, yp0 = 0.0f, yp1 = 0.0f;
-            const int m_own = lane >> 1, sel = lane & 1;
-#pragma unroll
-            for (int m = 0; m < MMAX; m++) {
-                if (m < rows_m) {
-                    const float t0 = __fdiv_rn(warp_sum(f0[m]), 127.0f);
-                    const float t1 = __fdiv_rn(warp_sum(f1[m]), 127.0f);
-                    if (m == m_own) y_own = sel ? t1 : t0;
-                    if (m == lane) { yp0 = t0; yp1 = t1; }
-                    f0[m] = f1[m] = 0.0f;
+    } else {
+        // ---- MMA path: warp = a slice of the stage's blocks, all 16 rows ----
+        const int g = lane >> 2, t = lane & 3;
+        const int kb0 = (warp * bpp) / kCWarps, kb1 = ((warp + 1) * bpp) / kCWarps;
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        int buf = 0;
+        // ldmatrix row address of this lane: matrix j = lane / 8, row q = lane % 8
+        const int lj = lane >> 3, lq = lane & 7;
+        const int lrow = lq + 8 * (lj >> 1);
+        const bool arow = g < rows_m;
+        for (int i = 0; i < total; i++) {
+            const int sl = i % S;
+            const int tile = i / npan, pan = i - tile * npan;
+            const int r = row0 + tile * kStageRows;
+            const int rows = min(kStageRows, row1 - r);
+            if (!bad && !mbar_wait(&full_bar[sl], (i / S) & 1)) bad = true;
+            const uint8_t* dw = ring + (size_t)sl * slot;
+            const __half* ds = reinterpret_cast<const __half*>(dw + (size_t)kStageRows * P);
+            const uint32_t wrow = smem_u32(dw + (size_t)lrow * P);
+            const uint8_t* arow_p = act + (size_t)g * ald + (size_t)pan * P;
+            for (int kb = kb0; kb < (bad ? kb0 : kb1); kb++) {
+                const int chunk = 2 * kb + (lj & 1);
+                uint32_t b00, b01, b10, b11;
+                ldmatrix_x4(wrow + swz_chunk(chunk, r + lrow) * 16, b00, b01, b10, b11);
+                uint32_t a0 = 0, a2 = 0;
+                if (arow) {
+                    a0 = *reinterpret_cast<const uint32_t*>(arow_p + kb * 32 + 4 * t);
+                    a2 = *reinterpret_cast<const uint32_t*>(arow_p + kb * 32 + 16 + 4 * t);
                 }
+                int d0, d1, d2, d3;
+                mma_u8s8(a0, a2, b00, b01, d0, d1);
+                mma_u8s8(a0, a2, b10, b11, d2, d3);
+                const float s0 = __half2float(ds[(2 * t) * bpp + kb]);
+                const float s1 = __half2float(ds[(2 * t + 1) * bpp + kb]);
+                const float s2 = __half2float(ds[(8 + 2 * t) * bpp + kb]);
+                const float s3 = __half2float(ds[(9 + 2 * t) * bpp + kb]);
+                acc[0] = __fmaf_rn(i2f_exact(d0), s0, acc[0]);
+                acc[1] = __fmaf_rn(i2f_exact(d1), s1, acc[1]);
+                acc[2] = __fmaf_rn(i2f_exact(d2), s2, acc[2]);
+                acc[3] = __fmaf_rn(i2f_exact(d3), s3, acc[3]);
             }
-            if (active) {
-                if (EPI == EPI_STORE || EPI == EPI_LOGITS) {
-                    if (m_own < rows_m && (sel == 0 || has1))
-                        p.out[(size_t)(p.row0 + m_own) * p.ldo + n0 + sel] = y_own;
-                    if (EPI == EPI_LOGITS && lane < rows_m) {
-                        unsigned long long k = argmax_key(yp0, n0);
-                        if (has1) {
-                            const unsigned long long k1 = argmax_key(yp1, n0 + 1);
-                            k = k1 > k ? k1 : k;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty_bar[sl]);
+            if (pan == npan - 1) {
+                // reduce the warps' block slices of this 16-row tile, then epilogue
+#pragma unroll
+                for (int q = 0; q < 4; q++) red[buf][warp][lane][q] = acc[q];
+                acc[0] = acc[1] = acc[2] = acc[3] = 0.0f;
+                asm volatile("bar.sync 1, %0;" ::"n"(kCWarps * 32) : "memory");
+                const int tid = threadIdx.x;
+                if (tid < 64) {
+                    const int pr = tid & 7, m = tid >> 3;  // row pair pr of the tile, activation row m
+                    if (m < rows_m && 2 * pr < rows) {
+                        const int src_lane = 4 * m + (pr & 3);
+                        const int q0 = (pr >> 2) * 2;
+                        float y0 = 0.0f, y1 = 0.0f;
+#pragma unroll
+                        for (int w = 0; w < kCWarps; w++) {
+                            y0 += red[buf][w][src_lane][q0];
+                            y1 += red[buf][w][src_lane][q0 + 1];
                         }
-                        best = k > best ? k : best;
-                    }
-                } else if (EPI == EPI_RESID) {
-                    if (m_own < rows_m && (sel == 0 || has1)) {
-                        float* o = p.out + (size_t)(p.row0 + m_own) * p.ldo + n0 + sel;
-                        *o = __fadd_rn(*o, y_own);
-                    }
-                } else if (EPI == EPI_QKV) {
-                    if (lane < rows_m) {
-                        const int rr = p.row0 + lane;
-                        float v0 = yp0, v1 = yp1;
-                        const int qkd = p.q_dim + p.kv_dim;
-                        if (n0 < qkd) {
-                            const int ii = (n0 < p.q_dim ? n0 : n0 - p.q_dim) % p.head_dim;
-                            const float freq =
-                                __fdiv_rn(1.0f, powf(p.theta, __fdiv_rn((float)ii, (float)p.head_dim)));
-                            const float ang = __fmul_rn((float)p.pos[rr], freq);
-                            float sn, cs;
-                            sincosf(ang, &sn, &cs);
-                            const float a = v0, b = v1;
-                            v0 = __fsub_rn(__fmul_rn(a, cs), __fmul_rn(b, sn));
-                            v1 = __fadd_rn(__fmul_rn(a, sn), __fmul_rn(b, cs));
-                        }
-                        if (n0 < p.q_dim) {
-                            p.q_out[(size_t)rr * p.q_dim + n0] = v0;
-                            p.q_out[(size_t)rr * p.q_dim + n0 + 1] = v1;
-                        } else {
-                            const bool is_k = n0 < qkd;
-                            const int c = n0 - (is_k ? p.q_dim : qkd);
-                            const int h = c / p.head_dim;
-                            const int dd = c - h * p.head_dim;
-                            const int slotk = *p.slot_base + rr;
-                            const int page = p.block_table[slotk / kPageSize];
-                            const size_t off =
-                                (((size_t)page * p.kv_heads + h) * kPageSize + (slotk % kPageSize)) * p.head_dim + dd;
-                            *reinterpret_cast<__half2*>((is_k ? p.kv.k : p.kv.v) + off) = __floats2half2_rn(v0, v1);
-                        }
-                    }
-                } else if (EPI == EPI_SWIGLU) {
-                    if (lane < rows_m) {
-                        const int rr = p.row0 + lane;
-                        const float h = __fmul_rn(__fmul_rn(yp0, poly_sigmoid(yp0)), yp1);
-                        p.hq[(size_t)rr * p.F + (n0 >> 1)] = (uint8_t)quant_u8(h);
+                        pair_epilogue<EPI>(p, p.row0 + m, r + 2 * pr, 2 * pr + 1 < rows, __fdiv_rn(y0, 127.0f),
+                                           __fdiv_rn(y1, 127.0f), best_s);
                     }
                 }
+                buf ^= 1;
             }
         }
     }
 
     if (EPI == EPI_LOGITS) {
-        if (lane < kMaxRows) red_s[warp][lane] = lane < rows_m ? best : 0ull;
         asm volatile("bar.sync 1, %0;" ::"n"(kCWarps * 32) : "memory");
-        if (threadIdx.x < (unsigned)rows_m) {
-            unsigned long long b = 0ull;
-            for (int w = 0; w < kCWarps; w++) b = red_s[w][threadIdx.x] > b ? red_s[w][threadIdx.x] : b;
-            p.amax_part[(size_t)(p.row0 + threadIdx.x) * gridDim.x + blockIdx.x] = b;
-        }
+        if (threadIdx.x < (unsigned)rows_m)
+            p.amax_part[(size_t)(p.row0 + threadIdx.x) * gridDim.x + blockIdx.x] = best_s[threadIdx.x];
     }
 }
 
@@ -308,30 +349,31 @@ int sm_count() {
     return n;
 }
 
-template <int MMAX, int EPI>
-cudaError_t launch_t(const GemvParams& p, const TmaShape& sh, cudaStream_t s, bool pdl) {
-    auto kern = gemv_tma_kernel<MMAX, EPI>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sh.smem);
+template <int MMAX, int EPI, bool MMA>
+cudaError_t launch_t(const GemvParams& p, const Geo& geo, cudaStream_t s, bool pdl) {
+    auto kern = gemv_tma_kernel<MMAX, EPI, MMA>;
+    const size_t smem = (size_t)geo.act_bytes + (size_t)geo.S * slot_bytes(geo.P);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(tma_gemv_grid());
+    cfg.gridDim = dim3(sm_count());
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = sh.smem;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, kern, p, sh.seg, sh.nseg, sh.stages, (int)sh.act_bytes);
+    return cudaLaunchKernelEx(&cfg, kern, p, geo);
 }
 
 template <int EPI>
-cudaError_t launch_e(const GemvParams& p, int mmax, const TmaShape& sh, cudaStream_t s, bool pdl) {
-    if (mmax <= 1) return launch_t<1, EPI>(p, sh, s, pdl);
-    if (mmax <= 2) return launch_t<2, EPI>(p, sh, s, pdl);
-    if (mmax <= 4) return launch_t<4, EPI>(p, sh, s, pdl);
-    return launch_t<8, EPI>(p, sh, s, pdl);
+cudaError_t launch_e(const GemvParams& p, const Geo& geo, cudaStream_t s, bool pdl) {
+    if (p.M <= 1) return launch_t<1, EPI, false>(p, geo, s, pdl);
+    if (p.M <= 2) return launch_t<2, EPI, true>(p, geo, s, pdl);
+    if (p.M <= 4) return launch_t<4, EPI, true>(p, geo, s, pdl);
+    return launch_t<8, EPI, true>(p, geo, s, pdl);
 }
 
 }  // namespace
@@ -348,34 +390,33 @@ int take_device_error() {
     return v;
 }
 
-cudaError_t launch_gemv_auto(const GemvParams& p, int epi, cudaStream_t s, bool pdl) {
-    if (epi != EPI_DOTS && tma_gemv_supported(p.K, p.M)) return launch_gemv_tma(p, epi, s, pdl);
-    return launch_gemv(p, epi, false, false, s, pdl);
+bool tma_gemv_supported(int N, int K, int M) {
+    Geo g;
+    return N > 0 && N % 8 == 0 && make_geo(K, M, g);
 }
 
-int gemv_auto_grid(int N, int K) { return tma_gemv_supported(K, kMaxRows) ? tma_gemv_grid() : gemv_grid(N); }
-
-bool tma_gemv_supported(int K, int M) {
-    TmaShape sh;
-    return tma_shape(K, M, sh);
-}
-
-// p.M: rows held in shared memory (static count, or the upper bound of
-// *p.dyn_M), 1..kMaxRows.
+// p.M: rows held in shared memory (a static count, or the upper bound of
+// *p.dyn_M), 1..kMaxRows. Weights must be in the tiled layout (p.P != 0).
 cudaError_t launch_gemv_tma(const GemvParams& p, int epi, cudaStream_t s, bool pdl) {
-    if (p.M <= 0 || p.M > kMaxRows) return cudaErrorInvalidValue;
-    const int mm = p.M <= 1 ? 1 : p.M <= 2 ? 2 : p.M <= 4 ? 4 : 8;
-    TmaShape sh;
-    if (!tma_shape(p.K, p.M, sh)) return cudaErrorInvalidValue;
+    if (p.M <= 0 || p.M > kMaxRows || p.N % 8 != 0 || p.P == 0) return cudaErrorInvalidValue;
+    Geo geo;
+    if (!make_geo(p.K, p.M, geo) || geo.P != p.P) return cudaErrorInvalidValue;
     if (p.x && p.K % 128 != 0) return cudaErrorInvalidValue;
     switch (epi) {
-        case EPI_STORE: return launch_e<EPI_STORE>(p, mm, sh, s, pdl);
-        case EPI_RESID: return launch_e<EPI_RESID>(p, mm, sh, s, pdl);
-        case EPI_QKV: return launch_e<EPI_QKV>(p, mm, sh, s, pdl);
-        case EPI_SWIGLU: return launch_e<EPI_SWIGLU>(p, mm, sh, s, pdl);
-        case EPI_LOGITS: return launch_e<EPI_LOGITS>(p, mm, sh, s, pdl);
+        case EPI_STORE: return launch_e<EPI_STORE>(p, geo, s, pdl);
+        case EPI_RESID: return launch_e<EPI_RESID>(p, geo, s, pdl);
+        case EPI_QKV: return launch_e<EPI_QKV>(p, geo, s, pdl);
+        case EPI_SWIGLU: return launch_e<EPI_SWIGLU>(p, geo, s, pdl);
+        case EPI_LOGITS: return launch_e<EPI_LOGITS>(p, geo, s, pdl);
         default: return cudaErrorInvalidValue;
     }
 }
+
+cudaError_t launch_gemv_auto(const GemvParams& p, int epi, cudaStream_t s, bool pdl) {
+    if (epi != EPI_DOTS && p.P != 0 && tma_gemv_supported(p.N, p.K, p.M)) return launch_gemv_tma(p, epi, s, pdl);
+    return launch_gemv(p, epi, false, false, s, pdl);
+}
+
+int gemv_auto_grid(int N, int K) { return tma_gemv_supported(N, K, kMaxRows) ? tma_gemv_grid() : gemv_grid(N); }
 
 }  // namespace fl

@@ -10,6 +10,7 @@
 
 #include "fl_common.cuh"
 #include "fl_kernels.h"
+#include "fl_layout.cuh"
 #include "fl_runtime.h"
 
 namespace fl {
@@ -75,11 +76,16 @@ int upload_tensor(dequantized_tensor_t* t) {
     cudaGetDevice(&d->device);
     const size_t nw = (size_t)t->rows * t->cols;
     cudaError_t e = cudaMalloc(&d->w, nw);
-    if (e == cudaSuccess) e = cudaMemcpy(d->w, t->weights, nw, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess && blk == 32) {
+    if (blk == 32) {
+        // block mode: the TMA-ring GEMV's tiled layout whenever it can serve the shape
+        d->P = tma_gemv_supported(t->rows, t->cols, 1) ? panel_width(t->cols) : 0;
         const size_t ns = (size_t)t->rows * (t->cols / 32) * sizeof(__half);
-        e = cudaMalloc(&d->sblk, ns);
-        if (e == cudaSuccess) e = cudaMemcpy(d->sblk, t->scales_f16, ns, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMalloc(&d->sblk, ns);
+        if (e == cudaSuccess)
+            e = upload_rows(d->w, d->sblk, t->rows, t->cols, d->P, 0, 1, t->weights, t->scales_f16, t->rows,
+                            device_stream());
+    } else if (e == cudaSuccess) {
+        e = cudaMemcpy(d->w, t->weights, nw, cudaMemcpyHostToDevice);
     }
     if (e == cudaSuccess && blk == 0) {
         e = cudaMalloc(&d->srow, (size_t)t->rows * sizeof(float));
@@ -127,6 +133,7 @@ static int tensor_params(const dequantized_tensor_t* B, int N, int K, GemvParams
     cudaGetDevice(&cur);
     if (cur != d->device) return set_error(FL_E_STATE, "matmul: tensor lives on another device");
     p.w = d->w;
+    p.P = d->P;
     p.sblk = d->sblk;
     p.srow = d->srow;
     p.N = N;
