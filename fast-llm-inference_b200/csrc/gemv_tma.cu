@@ -223,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_tma_kernel(const GemvParams 
         // ---- dp4a path: warp = row pair (2w, 2w + 1) of each 16-row stage ----
         float f0 = 0.0f, f1 = 0.0f;
         const int lr = 2 * warp;
-        const int nj = P >> 9;
+        const int cpp = P >> 4;  // 16-byte chunks per panel row
         for (int i = 0; i < total; i++) {
             const int sl = i % S;
             const int tile = i / npan, pan = i - tile * npan;
@@ -239,8 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_tma_kernel(const GemvParams 
                 const int ra = lr, rb = two ? lr + 1 : lr;
                 const uint8_t* wa = dw + (size_t)ra * P;
                 const uint8_t* wb = dw + (size_t)rb * P;
-                for (int j = 0; j < nj; j++) {
-                    const int c = j * 32 + lane;  // logical chunk within the panel row
+                for (int c = lane; c < cpp; c += 32) {  // logical chunk within the panel row
                     const uint4 w0 = *reinterpret_cast<const uint4*>(wa + swz_chunk(c, r + ra) * 16);
                     const uint4 w1 = *reinterpret_cast<const uint4*>(wb + swz_chunk(c, r + rb) * 16);
                     const float s0 = __half2float(ds[ra * bpp + (c >> 1)]);
