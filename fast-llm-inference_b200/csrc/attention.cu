@@ -217,6 +217,179 @@ __global__ void __launch_bounds__(kAThreads) attention_kernel(const AttnParams p
     }
 }
 
+
+constexpr int kSplit = 64;     // keys per split = one KV page
+constexpr int kDThreads = 128;
+
+// Decode attention (M <= 8 new rows), split-K over pages: CTA (h, sp) takes
+// the 64 slots of page sp, computes each row's local max, sum of exp and
+// unnormalised P.V, writes them to scratch; the last CTA of the head to
+// arrive (device-scope counter) combines the splits in split order --
+// deterministic -- normalises, quantizes, and re-arms the counter. Same
+// arithmetic as inference.c:193-247 up to float rounding.
+template <int MR>
+__global__ void __launch_bounds__(kDThreads) attention_split_kernel(const AttnParams p) {
+    __shared__ __align__(16) float q_s[MR][kMaxHd];
+    __shared__ uint32_t Ks[kSplit][kMaxHd / 2 + 1];
+    __shared__ uint32_t Vs[kSplit][kMaxHd / 2];
+    __shared__ float sc[MR][kSplit];
+    __shared__ float ml_s[MR][2];
+    __shared__ int ticket_s;
+    pdl_trigger();
+    pdl_wait();
+    if (p.done && *p.done) return;
+    const int M = p.dyn_M ? *p.dyn_M : p.M;
+    const int nr = min(M, MR);
+    const int h = blockIdx.x, sp = blockIdx.y;
+    const int base = *p.slot_base;
+    const int ctx = base + M;
+    const int nsplit = (ctx + kSplit - 1) / kSplit;
+    if (sp >= nsplit || nr <= 0) return;
+    const int hd = p.head_dim, hd2 = hd >> 1;
+    const int kvh = h / (p.heads / p.kv_heads);
+    const int qd = p.heads * hd;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int j0 = sp * kSplit;
+    const int nt = min(kSplit, ctx - j0);
+
+    for (int i = threadIdx.x; i < nr * hd; i += kDThreads) {
+        const int rr = i / hd, dd = i - rr * hd;
+        q_s[rr][dd] = p.q[(size_t)rr * qd + (size_t)h * hd + dd];
+    }
+    {   // the split is one page: contiguous [64][hd] halves for this kv head
+        const int page = p.block_table[sp];
+        const size_t base_off = (((size_t)page * p.kv_heads + kvh) * kPageSize) * hd2;
+        const uint32_t* kg = reinterpret_cast<const uint32_t*>(p.kv.k) + base_off;
+        const uint32_t* vg = reinterpret_cast<const uint32_t*>(p.kv.v) + base_off;
+        for (int i = threadIdx.x; i < nt * hd2; i += kDThreads) {
+            const int key = i / hd2, c = i - key * hd2;
+            Ks[key][c] = kg[i];
+            Vs[key][c] = vg[i];
+        }
+    }
+    __syncthreads();
+    const float scale = __fdiv_rn(1.0f, sqrtf((float)hd));
+    {   // scores: warp w -> keys lane + 32 (w & 1), rows (w >> 1) + 2i
+        const int key = lane + 32 * (warp & 1);
+        const int rb = warp >> 1;
+        if (key < nt) {
+            float acc[(MR + 1) / 2];
+#pragma unroll
+            for (int i = 0; i < (MR + 1) / 2; i++) acc[i] = 0.0f;
+            for (int e = 0; e < hd2; e++) {
+                const float2 kf = __half22float2(*reinterpret_cast<const __half2*>(&Ks[key][e]));
+#pragma unroll
+                for (int i = 0; i < (MR + 1) / 2; i++) {
+                    const int rr = rb + 2 * i;
+                    if (rr < nr) {
+                        const float2 qf = *reinterpret_cast<const float2*>(&q_s[rr][2 * e]);
+                        acc[i] = __fmaf_rn(qf.x, kf.x, acc[i]);
+                        acc[i] = __fmaf_rn(qf.y, kf.y, acc[i]);
+                    }
+                }
+            }
+            const int j = j0 + key;
+#pragma unroll
+            for (int i = 0; i < (MR + 1) / 2; i++) {
+                const int rr = rb + 2 * i;
+                if (rr < nr) {
+                    bool vis = true;
+                    if (j >= base) {
+                        const int jj = j - base;
+                        vis = p.mask ? (p.mask[(size_t)rr * M + jj] != 0) : (jj <= rr);
+                    }
+                    sc[rr][key] = vis ? __fmul_rn(acc[i], scale) : -INFINITY;
+                }
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < (MR + 1) / 2; i++) {
+                const int rr = rb + 2 * i;
+                if (rr < nr && key < kSplit) sc[rr][key] = -INFINITY;
+            }
+        }
+    }
+    __syncthreads();
+    // local softmax statistics: warp w -> rows w, w + 4
+    for (int rr = warp; rr < nr; rr += 4) {
+        const float s0 = sc[rr][lane], s1 = sc[rr][lane + 32];
+        const float mx = warp_max(fmaxf(s0, s1));
+        float e0 = 0.0f, e1 = 0.0f;
+        if (mx != -INFINITY) {
+            e0 = s0 == -INFINITY ? 0.0f : expf(__fsub_rn(s0, mx));
+            e1 = s1 == -INFINITY ? 0.0f : expf(__fsub_rn(s1, mx));
+        }
+        sc[rr][lane] = e0;
+        sc[rr][lane + 32] = e1;
+        const float sum = warp_sum(e0 + e1);
+        if (lane == 0) {
+            ml_s[rr][0] = mx;
+            ml_s[rr][1] = sum;
+        }
+    }
+    __syncthreads();
+    // unnormalised P.V: thread -> (dimension pair d2, row parity)
+    const int pstride = hd + 2;  // per (h, split, row): [max, sum, o[hd]]
+    float* part = p.part + (((size_t)h * gridDim.y + sp) * MR) * pstride;
+    if (threadIdx.x < 2 * hd2) {
+        const int d2 = threadIdx.x % hd2, rb = threadIdx.x / hd2;
+        float a0[(MR + 1) / 2], a1[(MR + 1) / 2];
+#pragma unroll
+        for (int i = 0; i < (MR + 1) / 2; i++) a0[i] = a1[i] = 0.0f;
+        for (int t = 0; t < nt; t++) {
+            const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&Vs[t][d2]));
+#pragma unroll
+            for (int i = 0; i < (MR + 1) / 2; i++) {
+                const int rr = rb + 2 * i;
+                if (rr < nr) {
+                    const float w = sc[rr][t];
+                    a0[i] = __fmaf_rn(w, v.x, a0[i]);
+                    a1[i] = __fmaf_rn(w, v.y, a1[i]);
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < (MR + 1) / 2; i++) {
+            const int rr = rb + 2 * i;
+            if (rr < nr) {
+                part[(size_t)rr * pstride + 2 + 2 * d2] = a0[i];
+                part[(size_t)rr * pstride + 2 + 2 * d2 + 1] = a1[i];
+            }
+        }
+    }
+    if (threadIdx.x < nr) {
+        part[(size_t)threadIdx.x * pstride] = ml_s[threadIdx.x][0];
+        part[(size_t)threadIdx.x * pstride + 1] = ml_s[threadIdx.x][1];
+    }
+    // last CTA of this head combines
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) ticket_s = atomicAdd(&p.counters[h], 1);
+    __syncthreads();
+    if (ticket_s != nsplit - 1) return;
+    __threadfence();
+    const float* ph = p.part + ((size_t)h * gridDim.y * MR) * pstride;
+    for (int i = threadIdx.x; i < nr * hd; i += kDThreads) {
+        const int rr = i / hd, dd = i - rr * hd;
+        float gm = -INFINITY;
+        for (int s = 0; s < nsplit; s++) gm = fmaxf(gm, __ldcg(ph + ((size_t)s * MR + rr) * pstride));
+        float L = 0.0f, O = 0.0f;
+        for (int s = 0; s < nsplit; s++) {
+            const float* q = ph + ((size_t)s * MR + rr) * pstride;
+            const float m = __ldcg(q);
+            if (m == -INFINITY) continue;
+            const float wgt = expf(__fsub_rn(m, gm));
+            L = __fmaf_rn(__ldcg(q + 1), wgt, L);
+            O = __fmaf_rn(__ldcg(q + 2 + dd), wgt, O);
+        }
+        const float o = __fdiv_rn(O, L);
+        const size_t idx = (size_t)rr * qd + (size_t)h * hd + dd;
+        p.out_q[idx] = (uint8_t)quant_u8(o);
+        if (p.out_f) p.out_f[idx] = o;
+    }
+    if (threadIdx.x == 0) p.counters[h] = 0;  // re-arm for the next launch
+}
+
 size_t attention_smem() {
     const size_t f = (size_t)kARows * kMaxHd + (size_t)kARows * kTile;
     const size_t kv = (size_t)kTile * (kMaxHd / 2 + 1) + (size_t)kTile * (kMaxHd / 2);
@@ -240,9 +413,37 @@ cudaError_t launch_act_quant(const ActQuantParams& p, cudaStream_t s, bool pdl) 
     return cudaLaunchKernelEx(&cfg, act_quant_kernel, p);
 }
 
+size_t attention_scratch_floats(int heads, int head_dim, int max_ctx) {
+    return (size_t)heads * ((max_ctx + kSplit - 1) / kSplit) * kMaxRows * (head_dim + 2);
+}
+size_t attention_scratch_counters(int heads) { return (size_t)heads; }
+
+template <int MR>
+cudaError_t launch_split(const AttnParams& p, cudaStream_t s, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.heads, (p.max_ctx + kSplit - 1) / kSplit);
+    cfg.blockDim = dim3(kDThreads);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, attention_split_kernel<MR>, p);
+}
+
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl) {
     if (p.head_dim > kMaxHd || p.head_dim < 64 || p.head_dim % 2 != 0 || p.heads % p.kv_heads != 0)
         return cudaErrorInvalidValue;
+    if (p.M <= kMaxRows && p.part && p.counters) {
+        // grid.y covers every page the context can reach; the partial layout
+        // indexes (head, split) with gridDim.y, so max_ctx must be the one the
+        // scratch was sized for.
+        if (p.M <= 1) return launch_split<1>(p, s, pdl);
+        if (p.M <= 2) return launch_split<2>(p, s, pdl);
+        if (p.M <= 4) return launch_split<4>(p, s, pdl);
+        return launch_split<8>(p, s, pdl);
+    }
     const size_t smem = attention_smem();
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -92,6 +92,8 @@ struct fl_engine {
     double t_draft_us = 0, t_verify_us = 0, t_total_us = 0;
     int cb_pos = 0;               // callback API: base cache length
     float* last_feat = nullptr;   // [d] base feature of the last appended token
+    float* attn_part = nullptr;   // decode attention split-K scratch
+    int* attn_cnt = nullptr;      // per-head arrival counters (zero at rest)
     int graph_kernels = 0;        // kernel nodes in the step graph
     long long last_launches = 0;  // kernels launched by the last decode
     const void* bound_draft = nullptr;
@@ -264,6 +266,8 @@ int run_stack(fl_engine* e, Stack& S, float* x, int M, const int* dyn_M, const i
         at.max_ctx = e->c.max_seq_len;
         at.out_q = e->aq;
         at.done = done;
+        at.part = e->attn_part;
+        at.counters = e->attn_cnt;
         FL_CHECK_CUDA(launch_attention(at, e->s, pdl));
         g = gemv_base(W.o, e->aq, done);
         g.out = x;
@@ -477,7 +481,11 @@ FL_API fl_engine_t* fl_engine_create(const fl_model_config_t* cfg, int device) {
               cudaMalloc(&e->seq, sizeof(int) * (R + 16)) == cudaSuccess &&
               cudaMalloc(&e->out, sizeof(int) * (R + 16)) == cudaSuccess &&
               cudaMalloc(&e->acc, sizeof(int) * (R + 16)) == cudaSuccess &&
-              cudaMalloc(&e->last_feat, sizeof(float) * d) == cudaSuccess;
+              cudaMalloc(&e->last_feat, sizeof(float) * d) == cudaSuccess &&
+              cudaMalloc(&e->attn_part, sizeof(float) * attention_scratch_floats(e->H, e->hd, c.max_seq_len)) ==
+                  cudaSuccess &&
+              cudaMalloc(&e->attn_cnt, sizeof(int) * attention_scratch_counters(e->H)) == cudaSuccess &&
+              cudaMemset(e->attn_cnt, 0, sizeof(int) * attention_scratch_counters(e->H)) == cudaSuccess;
     if (!ok) return fail(set_error(FL_E_NOMEM, "fl_engine_create: device allocation failed"));
     std::vector<int> io(R + 16);
     for (size_t i = 0; i < io.size(); i++) io[i] = (int)i;
@@ -497,7 +505,7 @@ FL_API void fl_engine_destroy(fl_engine_t* e) {
     for (auto& m : e->medusa) free_linear(m);
     void* bufs[] = {e->embed, e->x, e->x2, e->xq, e->q, e->aq, e->hq, e->logits, e->amax, e->x_v, e->x_d,
                     e->iota, e->tok, e->mask, e->st, e->st_snap, e->xd0_snap, e->seq, e->out, e->acc,
-                    e->last_feat};
+                    e->last_feat, e->attn_part, e->attn_cnt};
     for (void* p : bufs) cudaFree(p);
     for (auto& ev : e->ev)
         if (ev) cudaEventDestroy(ev);

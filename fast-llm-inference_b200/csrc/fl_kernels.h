@@ -117,7 +117,14 @@ struct AttnParams {
     uint8_t* out_q;           // [rows, heads*head_dim] quantized output
     float* out_f;             // optional f32 output
     const int* done;
+    // Decode split-K scratch (M <= kMaxRows): per (head, split, row) partial
+    // max / sum / unnormalised output, and one arrival counter per head
+    // (zero between launches). Sizes from attention_scratch_*.
+    float* part;
+    int* counters;
 };
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl);
+size_t attention_scratch_floats(int heads, int head_dim, int max_ctx);
+size_t attention_scratch_counters(int heads);
 
 }  // namespace fl
