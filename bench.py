@@ -186,6 +186,53 @@ def run_reference(a, rank, world):
     return 0
 
 
+MICRO_SHAPES = {"gateup": (16384, 3072), "qkv": (9216, 3072), "o": (3072, 3072), "down": (3072, 8192),
+                "lm": (32064, 3072)}
+
+
+def run_microbench(a):
+    """One GEMV shape of the model in isolation (for ncu captures and kernel
+    timing): NT device copies of the weights (> 300 MB together, so launches
+    stream from HBM), M activation rows, fl_cuda_matmul_i8 launches back to
+    back on the library stream, timed with CUDA events."""
+    import ctypes as C
+    import torch
+    import flb200
+    lib = flb200.Lib()
+    lib.check(lib.fl_cuda_init(0), "init")
+    N, K = MICRO_SHAPES[a.microbench]
+    w, d = lib.synth_q4_0_i8(SEED, 7000 + N + K, N, K)
+    nt = max(4, int(np.ceil(300e6 / (N * K * 17 / 16))))
+    ts = []
+    for _ in range(nt):
+        t = flb200.block_tensor(w, d)
+        lib.check(lib.fl_cuda_upload_tensor(C.byref(t)), "upload")
+        ts.append(t)
+    x = torch.randn(a.m, K, device="cuda")
+    out = torch.empty(a.m, N, device="cuda")
+    s = lib.fl_cuda_stream()
+    stream = torch.cuda.ExternalStream(s)
+
+    def sweep():
+        for t in ts:
+            lib.check(lib.fl_cuda_matmul_i8(x.data_ptr(), C.byref(t), out.data_ptr(), a.m, N, K, s), "matmul")
+
+    sweep()
+    lib.check(lib.fl_cuda_sync(), "sync")
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(a.iters):
+        sweep()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / (a.iters * nt)
+    byts = N * K * 17 / 16 + a.m * K * 4 + a.m * N * 4
+    print(json.dumps({"microbench": a.microbench, "N": N, "K": K, "M": a.m, "launches": a.iters * nt,
+                      "us_per_launch": us, "GBps": byts / us / 1e3}), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -197,7 +244,12 @@ def main():
     ap.add_argument("--k", type=int, default=4)
     ap.add_argument("--cpu-tokens", type=int, default=16, help="tokens of the bounded CPU decode sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--microbench", choices=sorted(MICRO_SHAPES), help="time one GEMV shape in isolation")
+    ap.add_argument("--m", type=int, default=5, help="activation rows for --microbench")
+    ap.add_argument("--iters", type=int, default=10, help="sweeps for --microbench")
     a = ap.parse_args()
+    if a.microbench:
+        return run_microbench(a)
     a.warmup = max(a.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

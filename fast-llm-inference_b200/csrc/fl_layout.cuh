@@ -1,8 +1,7 @@
 // Device layout of INT8 weights for the TMA-ring GEMV ("tiled" layout).
 //
-// A [N, K] int8 matrix is cut along K into panels of width P (P = K when
-// K <= 4096, else the largest divisor of K <= 4096 that is a multiple of
-// 128). Panel p is stored as a row-major [N, P] block, so R consecutive rows
+// A [N, K] int8 matrix is cut along K into panels of width P (the largest
+// divisor of K that is a multiple of 128 and at most FL_PANEL_MAX bytes). Panel p is stored as a row-major [N, P] block, so R consecutive rows
 // of one panel are contiguous: one 1-D bulk copy moves a whole ring stage.
 // Inside a row the 16-byte chunks of every 128-byte group are XOR-swizzled
 // by (row & 7): chunk c of row n sits at chunk (c & ~7) | ((c & 7) ^ (n & 7)).
@@ -18,11 +17,14 @@
 
 namespace fl {
 
+#ifndef FL_PANEL_MAX
+#define FL_PANEL_MAX 4096
+#endif
+// Widest divisor of K that is a multiple of 128 and at most FL_PANEL_MAX.
 __host__ __device__ inline int panel_width(int K) {
     if (K <= 0 || K % 128) return 0;
-    if (K <= 4096) return K;
-    for (int n = 2; n <= 64; n++)
-        if (K % n == 0 && (K / n) <= 4096 && (K / n) % 128 == 0) return K / n;
+    for (int n = 1; n <= 128; n++)
+        if (K % n == 0 && (K / n) <= FL_PANEL_MAX && (K / n) % 128 == 0) return K / n;
     return 0;
 }
 

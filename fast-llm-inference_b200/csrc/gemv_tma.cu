@@ -32,9 +32,16 @@ constexpr int kCWarps = 8;                   // consumer warps
 constexpr int kThreads = (kCWarps + 1) * 32; // + producer warp
 constexpr int kStageRows = 16;
 constexpr int kMaxStages = 8;
-// Dynamic shared memory budget: 227 KB per block minus the static reduction
-// buffers and barriers (~8.5 KB).
-constexpr int kSmemLimit = 216 * 1024;
+#ifndef FL_TMA_SMEM_KB
+#define FL_TMA_SMEM_KB 216
+#endif
+#ifndef FL_TMA_CTAS_PER_SM
+#define FL_TMA_CTAS_PER_SM 1
+#endif
+// Dynamic shared memory budget per CTA: 227 KB per block minus the static
+// reduction buffers and barriers (~8.5 KB) when one CTA owns the SM.
+constexpr int kSmemLimit = FL_TMA_SMEM_KB * 1024;
+constexpr int kCtasPerSm = FL_TMA_CTAS_PER_SM;
 
 struct Geo {
     int P;         // panel width (bytes of a stage row)
@@ -135,7 +142,7 @@ __device__ __forceinline__ void pair_epilogue(const GemvParams& p, int r, int n0
 }
 
 template <int MMAX, int EPI, bool MMA>
-__global__ void __launch_bounds__(kThreads, 1) gemv_tma_kernel(const GemvParams p, const Geo geo) {
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const GemvParams p, const Geo geo) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full_bar[kMaxStages];
     __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
@@ -355,7 +362,7 @@ cudaError_t launch_t(const GemvParams& p, const Geo& geo, cudaStream_t s, bool p
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(sm_count());
+    cfg.gridDim = dim3(sm_count() * kCtasPerSm);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
@@ -377,7 +384,7 @@ cudaError_t launch_e(const GemvParams& p, const Geo& geo, cudaStream_t s, bool p
 
 }  // namespace
 
-int tma_gemv_grid() { return sm_count(); }
+int tma_gemv_grid() { return sm_count() * kCtasPerSm; }
 
 int take_device_error() {
     int v = 0;
