@@ -24,6 +24,7 @@
 #include "fl_layout.cuh"
 #include "fl_runtime.h"
 #include "fl_state.h"
+#include "fl_step.h"
 
 using namespace fl;
 
@@ -92,6 +93,10 @@ struct fl_engine {
     double t_draft_us = 0, t_verify_us = 0, t_total_us = 0;
     int cb_pos = 0;               // callback API: base cache length
     float* last_feat = nullptr;   // [d] base feature of the last appended token
+    unsigned* step_bar = nullptr;  // step kernel: grid barrier + error word
+    Phase* d_phases = nullptr;     // step kernel phase list (device)
+    int n_phases = 0;
+    bool step_kernel = false;      // last step graph uses the one-kernel step
     float* attn_part = nullptr;   // decode attention split-K scratch
     int* attn_cnt = nullptr;      // per-head arrival counters (zero at rest)
     int graph_kernels = 0;        // kernel nodes in the step graph
@@ -375,6 +380,151 @@ int record_step(fl_engine* e, bool pdl) {
     return FL_OK;
 }
 
+// ---- one-kernel step: the same sequence as record_step as a phase list ----
+Phase gemv_phase_of(const GemvParams& g, int epi) {
+    Phase ph;
+    memset(&ph, 0, sizeof(ph));
+    ph.kind = PH_GEMV;
+    ph.epi = epi;
+    ph.g = g;
+    return ph;
+}
+
+bool stack_phases(fl_engine* e, Stack& S, float* x, int M, const int* dyn_M, const int* slot_base,
+                  const int* pos, const int* done, std::vector<Phase>& out) {
+    const int d = e->d;
+    for (int l = 0; l < S.nl; l++) {
+        LayerW& W = S.L[l];
+        if (!W.qkv.P || !W.o.P || !W.gu.P || !W.down.P) return false;
+        GemvParams g = gemv_base(W.qkv, e->xq, done);
+        g.x = x;
+        g.norm = 1;
+        g.eps = e->c.norm_eps;
+        g.M = M;
+        g.dyn_M = dyn_M;
+        g.q_out = e->q;
+        g.kv = S.kv[l];
+        g.block_table = S.block_table;
+        g.slot_base = slot_base;
+        g.pos = pos;
+        g.q_dim = e->qd;
+        g.kv_dim = e->kd;
+        g.head_dim = e->hd;
+        g.kv_heads = e->Hkv;
+        g.theta = e->c.rope_theta;
+        out.push_back(gemv_phase_of(g, EPI_QKV));
+        Phase a;
+        memset(&a, 0, sizeof(a));
+        a.kind = PH_ATTN;
+        a.a.q = e->q;
+        a.a.kv = S.kv[l];
+        a.a.block_table = S.block_table;
+        a.a.slot_base = slot_base;
+        a.a.M = M;
+        a.a.dyn_M = dyn_M;
+        a.a.heads = e->H;
+        a.a.kv_heads = e->Hkv;
+        a.a.head_dim = e->hd;
+        a.a.max_ctx = e->c.max_seq_len;
+        a.a.out_q = e->aq;
+        a.a.done = done;
+        a.a.part = e->attn_part;
+        a.a.counters = e->attn_cnt;
+        out.push_back(a);
+        g = gemv_base(W.o, e->aq, done);
+        g.M = M;
+        g.dyn_M = dyn_M;
+        g.out = x;
+        g.ldo = d;
+        out.push_back(gemv_phase_of(g, EPI_RESID));
+        g = gemv_base(W.gu, e->xq, done);
+        g.x = x;
+        g.norm = 1;
+        g.eps = e->c.norm_eps;
+        g.M = M;
+        g.dyn_M = dyn_M;
+        g.hq = e->hq;
+        g.F = e->F;
+        out.push_back(gemv_phase_of(g, EPI_SWIGLU));
+        g = gemv_base(W.down, e->hq, done);
+        g.M = M;
+        g.dyn_M = dyn_M;
+        g.out = x;
+        g.ldo = d;
+        out.push_back(gemv_phase_of(g, EPI_RESID));
+    }
+    return true;
+}
+
+bool lm_phase(fl_engine* e, const float* x, int M, const int* dyn_src_row, const int* done, std::vector<Phase>& out) {
+    if (!e->lm.P) return false;
+    GemvParams g = gemv_base(e->lm, e->xq, done);
+    g.x = x;
+    g.norm = 1;
+    g.eps = e->c.norm_eps;
+    g.x_row_dyn = dyn_src_row;
+    g.out = e->logits;
+    g.ldo = e->V;
+    g.amax_part = e->amax;
+    g.M = M;
+    out.push_back(gemv_phase_of(g, EPI_LOGITS));
+    return true;
+}
+
+Phase control_phase(int kind, int arg) {
+    Phase ph;
+    memset(&ph, 0, sizeof(ph));
+    ph.kind = kind;
+    ph.arg = arg;
+    return ph;
+}
+
+// The whole speculative step of record_step as one phase list.
+bool step_phases(fl_engine* e, std::vector<Phase>& ph) {
+    const int K = e->spec_K;
+    SpecState* st = e->st;
+    const int* done = &st->done;
+    for (int j = 1; j < K; j++) {
+        if (!stack_phases(e, e->draft, e->x_d, 1, nullptr, &st->draft_base, st->draft_pos, done, ph)) return false;
+        if (!lm_phase(e, e->x_d, 1, nullptr, done, ph)) return false;
+        ph.push_back(control_phase(PH_DRAFT_PICK, j));
+    }
+    ph.push_back(control_phase(PH_VERIFY_PREP, 0));
+    if (!stack_phases(e, e->base, e->x_v, K + 1, nullptr, &st->verify_base, st->verify_pos, done, ph)) return false;
+    if (!lm_phase(e, e->x_v, K + 1, nullptr, done, ph)) return false;
+    ph.push_back(control_phase(PH_ACCEPT, 0));
+    ph.push_back(control_phase(PH_CATCHUP_PREP, 0));
+    if (!stack_phases(e, e->draft, e->x_d, K + 1, &st->rows, &st->draft_base, st->draft_pos, done, ph)) return false;
+    if (!lm_phase(e, e->x_d, 1, &st->last_row, done, ph)) return false;
+    ph.push_back(control_phase(PH_DRAFT_PICK, 0));
+    return true;
+}
+
+// Captures the one-kernel step; returns FL_E_UNSUPPORTED when some weight is
+// not in the tiled layout (the caller then records the multi-kernel step).
+int record_step_kernel(fl_engine* e) {
+    std::vector<Phase> ph;
+    if (!step_phases(e, ph)) return FL_E_UNSUPPORTED;
+    StepParams sp = {};
+    size_t smem = 0;
+    if (!step_plan(ph.data(), (int)ph.size(), sp, &smem)) return FL_E_UNSUPPORTED;
+    if (e->d_phases && e->n_phases < (int)ph.size()) {
+        cudaFree(e->d_phases);
+        e->d_phases = nullptr;
+    }
+    if (!e->d_phases) FL_CHECK_CUDA(cudaMalloc(&e->d_phases, sizeof(Phase) * ph.size()));
+    e->n_phases = (int)ph.size();
+    FL_CHECK_CUDA(cudaMemcpy(e->d_phases, ph.data(), sizeof(Phase) * ph.size(), cudaMemcpyHostToDevice));
+    sp.phases = e->d_phases;
+    sp.nphases = (int)ph.size();
+    sp.sb = step_buffers(e);
+    sp.K = e->spec_K;
+    sp.bar = e->step_bar;
+    sp.done = &e->st->done;
+    FL_CHECK_CUDA(launch_step(sp, smem, e->s));
+    return FL_OK;
+}
+
 int build_step_graph(fl_engine* e) {
     if (e->step_exec && e->graph_K == e->spec_K) return FL_OK;
     if (e->step_exec) {
@@ -383,7 +533,10 @@ int build_step_graph(fl_engine* e) {
     }
     cudaGraph_t g = nullptr;
     FL_CHECK_CUDA(cudaStreamBeginCapture(e->s, cudaStreamCaptureModeThreadLocal));
-    int rc = record_step(e, true);
+    const char* dis = getenv("FL_DISABLE_STEP_KERNEL");
+    int rc = (dis && dis[0] == '1') ? FL_E_UNSUPPORTED : record_step_kernel(e);
+    e->step_kernel = rc == FL_OK;
+    if (rc == FL_E_UNSUPPORTED) rc = record_step(e, true);
     cudaError_t ce = cudaStreamEndCapture(e->s, &g);
     if (rc != FL_OK) {
         if (g) cudaGraphDestroy(g);
@@ -485,6 +638,8 @@ FL_API fl_engine_t* fl_engine_create(const fl_model_config_t* cfg, int device) {
               cudaMalloc(&e->attn_part, sizeof(float) * attention_scratch_floats(e->H, e->hd, c.max_seq_len)) ==
                   cudaSuccess &&
               cudaMalloc(&e->attn_cnt, sizeof(int) * attention_scratch_counters(e->H)) == cudaSuccess &&
+              cudaMalloc(&e->step_bar, sizeof(unsigned) * 4) == cudaSuccess &&
+              cudaMemset(e->step_bar, 0, sizeof(unsigned) * 4) == cudaSuccess &&
               cudaMemset(e->attn_cnt, 0, sizeof(int) * attention_scratch_counters(e->H)) == cudaSuccess;
     if (!ok) return fail(set_error(FL_E_NOMEM, "fl_engine_create: device allocation failed"));
     std::vector<int> io(R + 16);
@@ -505,7 +660,7 @@ FL_API void fl_engine_destroy(fl_engine_t* e) {
     for (auto& m : e->medusa) free_linear(m);
     void* bufs[] = {e->embed, e->x, e->x2, e->xq, e->q, e->aq, e->hq, e->logits, e->amax, e->x_v, e->x_d,
                     e->iota, e->tok, e->mask, e->st, e->st_snap, e->xd0_snap, e->seq, e->out, e->acc,
-                    e->last_feat, e->attn_part, e->attn_cnt};
+                    e->last_feat, e->attn_part, e->attn_cnt, e->step_bar, e->d_phases};
     for (void* p : bufs) cudaFree(p);
     for (auto& ev : e->ev)
         if (ev) cudaEventDestroy(ev);
@@ -719,6 +874,14 @@ FL_API int fl_engine_spec_decode(fl_engine_t* e, int n_new, int* out, int* acc_h
     FL_CHECK_CUDA(cudaEventRecord(e->ev[1], e->s));
     FL_CHECK_CUDA(cudaEventSynchronize(e->ev[1]));
     if (take_device_error() != 0) return set_error(FL_E_TIMEOUT, "spec_decode: a bounded device wait gave up");
+    if (e->step_kernel) {
+        unsigned err = 0;
+        FL_CHECK_CUDA(cudaMemcpy(&err, e->step_bar + 2, sizeof(unsigned), cudaMemcpyDeviceToHost));
+        if (err) {
+            cudaMemset(e->step_bar, 0, sizeof(unsigned) * 4);
+            return set_error(FL_E_TIMEOUT, "spec_decode: a bounded wait of the step kernel gave up");
+        }
+    }
     float ms = 0.0f;
     cudaEventElapsedTime(&ms, e->ev[0], e->ev[1]);
     e->t_total_us = ms * 1000.0;
@@ -746,6 +909,8 @@ FL_API int fl_engine_last_timing(const fl_engine_t* e, double* draft_us, double*
 FL_API void* fl_engine_stream(const fl_engine_t* e) { return e ? (void*)e->s : nullptr; }
 
 FL_API long long fl_engine_last_launches(const fl_engine_t* e) { return e ? e->last_launches : -1; }
+
+FL_API int fl_engine_step_kernel(const fl_engine_t* e) { return e && e->step_kernel ? 1 : 0; }
 
 FL_API int fl_engine_draft_bound(const fl_engine_t* e, const void* draft) { return e && e->bound_draft == draft; }
 FL_API void fl_engine_note_draft(fl_engine_t* e, const void* draft) {

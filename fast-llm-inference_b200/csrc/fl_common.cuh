@@ -114,7 +114,7 @@ __device__ __forceinline__ void act_prologue(uint8_t* act, const float* x, int K
             float s = 0.0f;
 #pragma unroll 4
             for (int i = lane * 4; i < K; i += 128) {
-                const float4 v = *reinterpret_cast<const float4*>(xr + i);
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(xr + i));
                 s = __fmaf_rn(v.x, v.x, s);
                 s = __fmaf_rn(v.y, v.y, s);
                 s = __fmaf_rn(v.z, v.z, s);
@@ -126,7 +126,7 @@ __device__ __forceinline__ void act_prologue(uint8_t* act, const float* x, int K
         }
 #pragma unroll 4
         for (int i = lane * 4; i < K; i += 128) {
-            const float4 v = *reinterpret_cast<const float4*>(xr + i);
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(xr + i));
             *reinterpret_cast<uint32_t*>(act + (size_t)m * K + i) =
                 quant_pack4(__fmul_rn(v.x, scale), __fmul_rn(v.y, scale), __fmul_rn(v.z, scale),
                             __fmul_rn(v.w, scale));

@@ -118,6 +118,7 @@ _SIGS = {
     "fl_engine_last_timing": (I, [VP, VP, VP, VP]),
     "fl_engine_stream": (VP, [VP]),
     "fl_engine_last_launches": (C.c_longlong, [VP]),
+    "fl_engine_step_kernel": (I, [VP]),
     "fl_engine_draft_bound": (I, [VP, VP]),
     "fl_engine_note_draft": (None, [VP, VP]),
     "fl_engine_bench_linear": (I, [VP, I, I, I, I, C.POINTER(C.c_double), C.POINTER(C.c_double)]),

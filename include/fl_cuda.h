@@ -189,6 +189,9 @@ int fl_engine_last_timing(const fl_engine_t* e, double* draft_us, double* verify
 void* fl_engine_stream(const fl_engine_t* e);
 /* Number of kernels the last fl_engine_spec_decode launched. */
 long long fl_engine_last_launches(const fl_engine_t* e);
+/* 1 when speculative steps run as one persistent kernel per step (all
+ * weights in the tiled layout), 0 when they run as one kernel per op. */
+int fl_engine_step_kernel(const fl_engine_t* e);
 /* 1 when `draft` (a draft_model_t*) is the draft whose weights the engine
  * holds; fl_engine_note_draft records it after a load. */
 int fl_engine_draft_bound(const fl_engine_t* e, const void* draft);
