@@ -96,6 +96,8 @@ struct fl_engine {
     unsigned* step_bar = nullptr;  // step kernel: grid barrier + error word
     Phase* d_phases = nullptr;     // step kernel phase list (device)
     int n_phases = 0;
+    std::vector<int> phase_desc;   // per phase: kind, epilogue, N, K (host)
+    unsigned long long* d_trace = nullptr;  // FL_STEP_TRACE=1: 3 words per phase
     bool step_kernel = false;      // last step graph uses the one-kernel step
     float* attn_part = nullptr;   // decode attention split-K scratch
     int* attn_cnt = nullptr;      // per-head arrival counters (zero at rest)
@@ -500,14 +502,18 @@ bool step_phases(fl_engine* e, std::vector<Phase>& ph) {
     return true;
 }
 
-// Captures the one-kernel step; returns FL_E_UNSUPPORTED when some weight is
-// not in the tiled layout (the caller then records the multi-kernel step).
-int record_step_kernel(fl_engine* e) {
+// Builds and uploads the phase list of the one-kernel step (outside any
+// capture); returns FL_E_UNSUPPORTED when some weight is not in the tiled
+// layout or the LM partials are not laid out per SM (the caller then
+// records the multi-kernel step).
+int prepare_step_kernel(fl_engine* e, StepParams& sp, size_t& smem) {
     std::vector<Phase> ph;
     if (!step_phases(e, ph)) return FL_E_UNSUPPORTED;
-    StepParams sp = {};
-    size_t smem = 0;
+    if (e->nparts != step_grid()) return FL_E_UNSUPPORTED;
+    sp = StepParams{};
+    smem = 0;
     if (!step_plan(ph.data(), (int)ph.size(), sp, &smem)) return FL_E_UNSUPPORTED;
+    FL_CHECK_CUDA(step_set_smem(smem));
     if (e->d_phases && e->n_phases < (int)ph.size()) {
         cudaFree(e->d_phases);
         e->d_phases = nullptr;
@@ -515,13 +521,27 @@ int record_step_kernel(fl_engine* e) {
     if (!e->d_phases) FL_CHECK_CUDA(cudaMalloc(&e->d_phases, sizeof(Phase) * ph.size()));
     e->n_phases = (int)ph.size();
     FL_CHECK_CUDA(cudaMemcpy(e->d_phases, ph.data(), sizeof(Phase) * ph.size(), cudaMemcpyHostToDevice));
+    e->phase_desc.clear();
+    for (const Phase& q : ph) {
+        const bool g = q.kind == PH_GEMV;
+        e->phase_desc.insert(e->phase_desc.end(), {q.kind, g ? q.epi : q.arg, g ? q.g.N : 0, g ? q.g.K : 0});
+    }
+    const char* tr = getenv("FL_STEP_TRACE");
+    if (tr && tr[0] == '1') {
+        if (e->d_trace) cudaFree(e->d_trace);
+        e->d_trace = nullptr;
+        FL_CHECK_CUDA(cudaMalloc(&e->d_trace, sizeof(unsigned long long) * (6 * ph.size() + 512)));
+        FL_CHECK_CUDA(cudaMemset(e->d_trace, 0, sizeof(unsigned long long) * (6 * ph.size() + 512)));
+    }
+    sp.trace = e->d_trace;
+    const char* tp = getenv("FL_STEP_TRACE_PHASE");
+    sp.trace_phase = tp ? atoi(tp) : -1;
     sp.phases = e->d_phases;
     sp.nphases = (int)ph.size();
     sp.sb = step_buffers(e);
     sp.K = e->spec_K;
     sp.bar = e->step_bar;
     sp.done = &e->st->done;
-    FL_CHECK_CUDA(launch_step(sp, smem, e->s));
     return FL_OK;
 }
 
@@ -531,18 +551,42 @@ int build_step_graph(fl_engine* e) {
         cudaGraphExecDestroy(e->step_exec);
         e->step_exec = nullptr;
     }
-    cudaGraph_t g = nullptr;
-    FL_CHECK_CUDA(cudaStreamBeginCapture(e->s, cudaStreamCaptureModeThreadLocal));
     const char* dis = getenv("FL_DISABLE_STEP_KERNEL");
-    int rc = (dis && dis[0] == '1') ? FL_E_UNSUPPORTED : record_step_kernel(e);
-    e->step_kernel = rc == FL_OK;
-    if (rc == FL_E_UNSUPPORTED) rc = record_step(e, true);
-    cudaError_t ce = cudaStreamEndCapture(e->s, &g);
-    if (rc != FL_OK) {
-        if (g) cudaGraphDestroy(g);
-        return rc;
+    StepParams sp;
+    size_t smem = 0;
+    int prc = (dis && dis[0] == '1') ? FL_E_UNSUPPORTED : prepare_step_kernel(e, sp, smem);
+    if (prc != FL_OK && prc != FL_E_UNSUPPORTED) return prc;
+    cudaGraph_t g = nullptr;
+    int rc = FL_E_UNSUPPORTED;
+    cudaError_t ce = cudaSuccess;
+    if (prc == FL_OK) {
+        // one-kernel step; if the cooperative launch cannot be captured the
+        // multi-kernel step is recorded instead
+        FL_CHECK_CUDA(cudaStreamBeginCapture(e->s, cudaStreamCaptureModeThreadLocal));
+        // the grid-barrier counter starts every launch at zero
+        rc = cudaMemsetAsync(e->step_bar, 0, sizeof(unsigned long long), e->s) == cudaSuccess &&
+                     launch_step(sp, smem, e->s) == cudaSuccess
+                 ? FL_OK
+                 : FL_E_UNSUPPORTED;
+        ce = cudaStreamEndCapture(e->s, &g);
+        if (rc != FL_OK || ce != cudaSuccess) {
+            if (g) cudaGraphDestroy(g);
+            g = nullptr;
+            (void)cudaGetLastError();
+            rc = FL_E_UNSUPPORTED;
+        }
     }
-    FL_CHECK_CUDA(ce);
+    e->step_kernel = rc == FL_OK;
+    if (rc == FL_E_UNSUPPORTED) {
+        FL_CHECK_CUDA(cudaStreamBeginCapture(e->s, cudaStreamCaptureModeThreadLocal));
+        rc = record_step(e, true);
+        ce = cudaStreamEndCapture(e->s, &g);
+        if (rc != FL_OK) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        FL_CHECK_CUDA(ce);
+    }
     size_t nn = 0;
     cudaGraphGetNodes(g, nullptr, &nn);
     std::vector<cudaGraphNode_t> nodes(nn);
@@ -660,7 +704,7 @@ FL_API void fl_engine_destroy(fl_engine_t* e) {
     for (auto& m : e->medusa) free_linear(m);
     void* bufs[] = {e->embed, e->x, e->x2, e->xq, e->q, e->aq, e->hq, e->logits, e->amax, e->x_v, e->x_d,
                     e->iota, e->tok, e->mask, e->st, e->st_snap, e->xd0_snap, e->seq, e->out, e->acc,
-                    e->last_feat, e->attn_part, e->attn_cnt, e->step_bar, e->d_phases};
+                    e->last_feat, e->attn_part, e->attn_cnt, e->step_bar, e->d_phases, e->d_trace};
     for (void* p : bufs) cudaFree(p);
     for (auto& ev : e->ev)
         if (ev) cudaEventDestroy(ev);
@@ -868,7 +912,15 @@ FL_API int fl_engine_spec_decode(fl_engine_t* e, int n_new, int* out, int* acc_h
         launched += batch;
         FL_CHECK_CUDA(cudaMemcpyAsync(&h, e->st, sizeof(h), cudaMemcpyDeviceToHost, e->s));
         FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
-        if (h.produced <= produced) return set_error(FL_E_STATE, "spec_decode: no progress");
+        if (h.produced <= produced) {
+            unsigned err = 0;
+            if (e->step_kernel && cudaMemcpy(&err, e->step_bar + 2, sizeof(unsigned), cudaMemcpyDeviceToHost) == cudaSuccess &&
+                err) {
+                cudaMemset(e->step_bar, 0, sizeof(unsigned) * 4);
+                return set_error(FL_E_TIMEOUT, "spec_decode: a bounded wait of the step kernel gave up");
+            }
+            return set_error(FL_E_STATE, "spec_decode: no progress");
+        }
         produced = h.produced;
     }
     FL_CHECK_CUDA(cudaEventRecord(e->ev[1], e->s));
@@ -911,6 +963,28 @@ FL_API void* fl_engine_stream(const fl_engine_t* e) { return e ? (void*)e->s : n
 FL_API long long fl_engine_last_launches(const fl_engine_t* e) { return e ? e->last_launches : -1; }
 
 FL_API int fl_engine_step_kernel(const fl_engine_t* e) { return e && e->step_kernel ? 1 : 0; }
+
+FL_API int fl_engine_step_trace_stages(const fl_engine_t* e, unsigned long long* t) {
+    if (!e) return set_error(FL_E_INVAL, "engine is NULL");
+    if (!e->step_kernel || !e->d_trace || !t) return 0;
+    FL_CHECK_CUDA(cudaSetDevice(e->device));
+    FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
+    FL_CHECK_CUDA(cudaMemcpy(t, e->d_trace + 6 * (size_t)e->n_phases, sizeof(unsigned long long) * 512,
+                             cudaMemcpyDeviceToHost));
+    return 64;
+}
+
+FL_API int fl_engine_step_trace(const fl_engine_t* e, unsigned long long* t, int* desc, int cap) {
+    if (!e) return set_error(FL_E_INVAL, "engine is NULL");
+    if (!e->step_kernel || !e->d_trace) return 0;
+    const int n = e->n_phases < cap ? e->n_phases : cap;
+    if (n <= 0) return 0;
+    FL_CHECK_CUDA(cudaSetDevice(e->device));
+    FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
+    if (t) FL_CHECK_CUDA(cudaMemcpy(t, e->d_trace, sizeof(unsigned long long) * 6 * n, cudaMemcpyDeviceToHost));
+    if (desc) memcpy(desc, e->phase_desc.data(), sizeof(int) * 4 * n);
+    return n;
+}
 
 FL_API int fl_engine_draft_bound(const fl_engine_t* e, const void* draft) { return e && e->bound_draft == draft; }
 FL_API void fl_engine_note_draft(fl_engine_t* e, const void* draft) {

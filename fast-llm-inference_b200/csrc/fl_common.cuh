@@ -134,6 +134,142 @@ __device__ __forceinline__ void act_prologue(uint8_t* act, const float* x, int K
     }
 }
 
+// RMS-norm (optional) + u8 quantisation of `rows` <= MR rows (row m of x at
+// x + m * K, of act at act + m * ald) by all NT threads of the calling group:
+// thread t handles float4 columns t, t + NT, t + 2 NT, ... of every row. The
+// sum of squares of a row is the per-thread sums (column order), a butterfly
+// per warp, then the NT / 32 warp sums added in warp order, so the result
+// depends on NT only. With CACHE and K / 4 <= NT * CPT all loads of all rows
+// are issued at once and the values stay in registers for the quantisation
+// (one round trip); otherwise columns go in batches of CPT and are loaded
+// again to quantise. `red` holds MR * NT / 32 floats; the barrier is named
+// barrier `bar_id` over the NT threads. The caller synchronises before
+// reading `act`. Per element the arithmetic is that of act_prologue
+// (activations_avx2.c:108-143, dequantized_tensor.c:112-135).
+template <int NT, int MR, int CPT, bool CACHE>
+__device__ __forceinline__ void act_prologue_cta(uint8_t* act, int ald, const float* x, int K, int rows, int norm,
+                                                 float eps, float* red, int tid, int bar_id) {
+    constexpr int NW = NT / 32;
+    const int K4 = K >> 2;
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    float scale[MR];
+#pragma unroll
+    for (int m = 0; m < MR; m++) scale[m] = 1.0f;
+    if (CACHE && K4 <= NT * CPT) {
+        float4 v[MR][CPT];
+#pragma unroll
+        for (int m = 0; m < MR; m++)
+#pragma unroll
+            for (int j = 0; j < CPT; j++) {
+                const int c = tid + j * NT;
+                v[m][j] = (m < rows && c < K4) ? __ldcg(x4 + (size_t)m * K4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        if (norm) {
+#pragma unroll
+            for (int m = 0; m < MR; m++) {
+                float s = 0.0f;
+#pragma unroll
+                for (int j = 0; j < CPT; j++) {
+                    if (tid + j * NT < K4) {
+                        s = __fmaf_rn(v[m][j].x, v[m][j].x, s);
+                        s = __fmaf_rn(v[m][j].y, v[m][j].y, s);
+                        s = __fmaf_rn(v[m][j].z, v[m][j].z, s);
+                        s = __fmaf_rn(v[m][j].w, v[m][j].w, s);
+                    }
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+                if (m < rows && (tid & 31) == 0) red[m * NW + (tid >> 5)] = s;
+            }
+            asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "n"(NT) : "memory");
+#pragma unroll
+            for (int m = 0; m < MR; m++) {
+                if (m < rows) {
+                    float tot = red[m * NW];
+                    for (int w = 1; w < NW; w++) tot += red[m * NW + w];
+                    scale[m] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), eps)));
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < MR; m++)
+#pragma unroll
+            for (int j = 0; j < CPT; j++) {
+                const int c = tid + j * NT;
+                if (m < rows && c < K4)
+                    *reinterpret_cast<uint32_t*>(act + (size_t)m * ald + 4 * c) =
+                        quant_pack4(__fmul_rn(v[m][j].x, scale[m]), __fmul_rn(v[m][j].y, scale[m]),
+                                    __fmul_rn(v[m][j].z, scale[m]), __fmul_rn(v[m][j].w, scale[m]));
+            }
+        return;
+    }
+    if (norm) {
+        float s[MR];
+#pragma unroll
+        for (int m = 0; m < MR; m++) s[m] = 0.0f;
+        for (int c0 = tid; c0 < K4; c0 += NT * CPT) {
+            // unrolled: the loads carry no dependence and are issued first
+#pragma unroll
+            for (int j = 0; j < CPT; j++)
+#pragma unroll
+                for (int m = 0; m < MR; m++)
+                    if (m < rows && c0 + j * NT < K4) {
+                        const float4 v = __ldcg(x4 + (size_t)m * K4 + c0 + j * NT);
+                        s[m] = __fmaf_rn(v.x, v.x, s[m]);
+                        s[m] = __fmaf_rn(v.y, v.y, s[m]);
+                        s[m] = __fmaf_rn(v.z, v.z, s[m]);
+                        s[m] = __fmaf_rn(v.w, v.w, s[m]);
+                    }
+        }
+#pragma unroll
+        for (int m = 0; m < MR; m++) {
+            if (m < rows) {
+                float t = s[m];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+                if ((tid & 31) == 0) red[m * NW + (tid >> 5)] = t;
+            }
+        }
+        asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "n"(NT) : "memory");
+#pragma unroll
+        for (int m = 0; m < MR; m++) {
+            if (m < rows) {
+                float tot = red[m * NW];
+                for (int w = 1; w < NW; w++) tot += red[m * NW + w];
+                scale[m] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), eps)));
+            }
+        }
+    }
+    for (int c0 = tid; c0 < K4; c0 += NT * CPT) {
+#pragma unroll
+        for (int j = 0; j < CPT; j++)
+#pragma unroll
+            for (int m = 0; m < MR; m++)
+                if (m < rows && c0 + j * NT < K4) {
+                    const float4 v = __ldcg(x4 + (size_t)m * K4 + c0 + j * NT);
+                    *reinterpret_cast<uint32_t*>(act + (size_t)m * ald + 4 * (c0 + j * NT)) =
+                        quant_pack4(__fmul_rn(v.x, scale[m]), __fmul_rn(v.y, scale[m]), __fmul_rn(v.z, scale[m]),
+                                    __fmul_rn(v.w, scale[m]));
+                }
+    }
+}
+
+// act_prologue_cta with the row count rounded up to 1, 2, 4 or 8 (at most
+// MMAX); CACHE keeps up to 24 float4 per thread in registers.
+template <int NT, int MMAX, bool CACHE>
+__device__ __forceinline__ void act_prologue_rows(uint8_t* act, int ald, const float* x, int K, int rows, int norm,
+                                                  float eps, float* red, int tid, int bar_id) {
+    if (rows <= 1 || MMAX == 1)
+        act_prologue_cta<NT, 1, (CACHE ? 12 : 8), CACHE>(act, ald, x, K, rows, norm, eps, red, tid, bar_id);
+    else if (rows <= 2 || MMAX == 2)
+        act_prologue_cta<NT, 2, (CACHE ? 6 : 4), CACHE>(act, ald, x, K, rows, norm, eps, red, tid, bar_id);
+    else if (rows <= 4 || MMAX == 4)
+        act_prologue_cta<NT, 4, (CACHE ? 3 : 2), CACHE>(act, ald, x, K, rows, norm, eps, red, tid, bar_id);
+    else
+        act_prologue_cta<NT, (MMAX < 8 ? MMAX : 8), (CACHE ? 3 : 1), CACHE>(act, ald, x, K, rows, norm, eps, red, tid,
+                                                                           bar_id);
+}
+
 // Streaming 16-byte load that bypasses L1 allocation (weights are read once).
 __device__ __forceinline__ uint4 ld_stream16(const void* p) {
     uint4 r;

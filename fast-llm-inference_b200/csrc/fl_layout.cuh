@@ -18,7 +18,7 @@
 namespace fl {
 
 #ifndef FL_PANEL_MAX
-#define FL_PANEL_MAX 4096
+#define FL_PANEL_MAX 256
 #endif
 // Widest divisor of K that is a multiple of 128 and at most FL_PANEL_MAX.
 __host__ __device__ inline int panel_width(int K) {

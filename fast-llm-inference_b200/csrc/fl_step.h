@@ -34,17 +34,33 @@ struct StepParams {
     int nphases;
     StepBuffers sb;        // control phases
     int K;                 // drafted tokens per step
-    unsigned* bar;         // grid barrier: [0] arrivals, [1] generation
+    unsigned* bar;         // [0..1] 64-bit barrier counter (zero at launch), [2] error word
     const int* done;       // skip everything when set at kernel start
     int region_bytes;      // activation / attention scratch region
     int slot_bytes;        // ring slot size
     int S;                 // ring slots
+    // Optional phase trace (nullptr = off), 6 words per phase, %globaltimer ns:
+    // [6i] CTA 0 start of phase i, [6i+1] CTA 0 end of its work in phase i,
+    // [6i+2] latest end over all CTAs (atomicMax; timestamps only grow, so
+    // after a decode every word holds the last launch's value); GEMV phases,
+    // CTA 0: [6i+3] activation prologue done, [6i+4] ns warp 0 waited for
+    // full ring stages, [6i+5] first stage ready.
+    unsigned long long* trace;
+    // Stage trace of phase `trace_phase` (-1 = off), CTA 0, after the phase
+    // words: 64 stages x 8 words = warp 0 stage ready, warp 0 stage done,
+    // warp 7 stage ready, warp 7 stage done, producer starts waiting for the
+    // slot, producer issues the stage, 2 unused.
+    int trace_phase;
 };
 
 // Shared-memory plan for a phase list (host): fills region / slot / S and
 // returns false if some GEMV phase cannot be served.
 bool step_plan(const Phase* host_phases, int n, StepParams& sp, size_t* smem_bytes);
 
+// Raises the kernel's dynamic shared-memory limit (call outside capture).
+cudaError_t step_set_smem(size_t smem_bytes);
+
+// Cooperative launch, grid = step_grid() CTAs of one per SM.
 cudaError_t launch_step(const StepParams& p, size_t smem_bytes, cudaStream_t s);
 
 int step_grid();

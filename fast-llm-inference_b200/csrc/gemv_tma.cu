@@ -148,6 +148,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const Ge
     __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
     __shared__ unsigned long long best_s[kMaxRows];
     __shared__ float red[2][kCWarps][32][4];
+    __shared__ float nred[kMaxRows * kCWarps];
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -212,8 +213,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const Ge
     const int ald = geo.act_ld;
     if (p.x) {
         const int src0 = p.x_row_dyn ? *p.x_row_dyn : p.row0;
-        for (int m = warp; m < rows_m; m += kCWarps)
-            act_prologue(act + (size_t)m * ald, p.x + (size_t)(src0 + m) * K, K, 1, p.norm, p.eps, 0, lane, 1);
+        act_prologue_rows<kCWarps * 32, MMAX, false>(act, ald, p.x + (size_t)src0 * K, K, rows_m, p.norm, p.eps, nred,
+                                              threadIdx.x, 1);
     } else {
         const int K16 = K >> 4;
         const uint4* src = reinterpret_cast<const uint4*>(p.aq + (size_t)p.row0 * K);

@@ -25,10 +25,11 @@ namespace {
 constexpr int kCW = 8;                    // consumer warps
 constexpr int kCThreads = kCW * 32;
 constexpr int kThr = kCThreads + 32;      // + producer warp
-constexpr int kMaxSlots = 8;
-constexpr int kSmemLimit = 216 * 1024;
+constexpr int kMaxSlots = 12;
+constexpr int kSmemLimit = 222 * 1024;    // + static shared memory <= 227 KB
 constexpr unsigned long long kWaitNs = 2000000000ull;  // every wait gives up after ~2 s
 constexpr int kErrRing = 1, kErrGrid = 2;
+constexpr int kTr = 6;  // trace words per phase (fl_step.h)
 
 __device__ __forceinline__ unsigned long long gtime() {
     unsigned long long t;
@@ -40,6 +41,16 @@ __device__ __forceinline__ unsigned long long gtime() {
 __device__ __forceinline__ uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
 __device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, %0;" ::"n"(kCThreads) : "memory"); }
+// Consumer barrier that also ORs a flag over the consumer threads.
+__device__ __forceinline__ bool cbar_or(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, 1, %2, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "n"(kCThreads)
+        : "memory");
+    return r != 0;
+}
 __device__ __forceinline__ void abar() { asm volatile("bar.sync 2, 128;" ::: "memory"); }  // warps 0-3
 
 __device__ __forceinline__ void mb_init(uint64_t* b, uint32_t n) {
@@ -78,34 +89,41 @@ __device__ __forceinline__ void bulk(void* dst, const void* src, uint32_t bytes,
                  : "memory");
 }
 
-// Grid-wide barrier of the consumer threads of all CTAs (generation
-// counter). A CTA that already failed a wait (bad) passes without arriving
-// or waiting, so a failure ends the kernel within one wait limit per CTA.
-__device__ bool grid_sync(unsigned* bar, int* err, int* ok_s, bool bad) {
-    if (bad) return false;
-    cbar();
+// Grid-wide barrier of the consumer threads of all CTAs: a 64-bit arrival
+// counter, zeroed before every launch, that only grows. Barrier b of a
+// launch is open once the counter reaches (b + 1) * grid: each CTA adds 1
+// with release semantics (no return value to wait for) and polls with
+// acquire loads. `bad` is first made uniform over the CTA's consumer warps;
+// a CTA that failed a wait passes without arriving or waiting, so a failure
+// ends the kernel within one wait limit per CTA (the host zeroes the
+// counter again after an error).
+__device__ __forceinline__ unsigned long long ld_acquire(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ bool grid_sync(unsigned long long* ctr, unsigned long long target, int* err, int* ok_s, bool bad,
+                          unsigned long long* tr) {
+    if (cbar_or(bad)) return false;
     if (threadIdx.x == 0) {
-        volatile unsigned* gen = bar + 1;
-        const unsigned g = *gen;
-        __threadfence();
-        const unsigned a = atomicAdd(bar, 1u);
+        if (tr) {
+            const unsigned long long t = gtime();
+            if (blockIdx.x == 0) tr[1] = t;
+            atomicMax(tr + 2, t);
+        }
+        asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(ctr) : "memory");
         int ok = 1;
-        if (a == gridDim.x - 1) {
-            atomicExch(bar, 0u);
-            __threadfence();
-            atomicAdd(bar + 1, 1u);
-        } else {
+        if (ld_acquire(ctr) < target) {
             const unsigned long long t0 = gtime();
-            while (*gen == g) {
+            while (ld_acquire(ctr) < target) {
                 if (gtime() - t0 > kWaitNs) {
                     ok = 0;
                     atomicOr(err, kErrGrid);
                     break;
                 }
-                __nanosleep(32);
             }
         }
-        __threadfence();
         *ok_s = ok;
     }
     cbar();
@@ -113,34 +131,32 @@ __device__ bool grid_sync(unsigned* bar, int* err, int* ok_s, bool bad) {
 }
 
 // ---------------------------------------------------------------- GEMV geometry
+// A ring stage is one tile of kTileRows weight rows x one panel (P bytes
+// per row, plus the rows' fp16 block scales). Consumer warp w owns rows
+// [16w, 16w + 16) of every tile over the whole K: it accumulates its rows'
+// block products across the tile's panels and writes their outputs itself,
+// so a GEMV phase has no cross-warp reduction and no CTA barrier. The
+// weight rows are the 16-row A operand of m16n8k32 and the (up to 8)
+// activation rows the 8-column B operand.
+constexpr int kWarpRows = 16;
+constexpr int kTileRows = kCW * kWarpRows;
+
 struct GGeo {
-    int P, npan, R, row0, row1, ntiles, nstages;
+    int P, npan, row0, row1, ntiles, nstages;
 };
 
-__host__ __device__ inline int stage_rows(int P, int slot_bytes) {
-    int R = slot_bytes / (P + P / 16);
-    if (R > 16) R = 16;
-    return R & ~1;
-}
+__host__ __device__ inline int slot_need(int P) { return (kTileRows * (P + P / 16) + 127) & ~127; }
 
-__host__ __device__ inline void gemv_geo(const GemvParams& g, int slot_bytes, int cta, int ncta, GGeo& o) {
+__host__ __device__ inline void gemv_geo(const GemvParams& g, int cta, int ncta, GGeo& o) {
     o.P = g.P;
     o.npan = g.K / g.P;
-    o.R = stage_rows(g.P, slot_bytes);
     const int nunits = g.N >> 3;
     const int u0 = (int)(((long long)nunits * cta) / ncta);
     const int u1 = (int)(((long long)nunits * (cta + 1)) / ncta);
     o.row0 = u0 * 8;
     o.row1 = u1 * 8;
-    o.ntiles = (o.row1 - o.row0 + o.R - 1) / o.R;
+    o.ntiles = (o.row1 - o.row0 + kTileRows - 1) / kTileRows;
     o.nstages = o.ntiles * o.npan;
-}
-
-__device__ __forceinline__ int dot16(const uint4& a, const uint4& w) {
-    int d = dp4a_us(a.x, w.x, 0);
-    d = dp4a_us(a.y, w.y, d);
-    d = dp4a_us(a.z, w.z, d);
-    return dp4a_us(a.w, w.w, d);
 }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -149,20 +165,34 @@ __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r
                  : "r"(addr));
 }
 
-__device__ __forceinline__ void mma_u8s8(uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1, int& d0, int& d1) {
-    int c2, c3;
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
-        : "=r"(d0), "=r"(d1), "=r"(c2), "=r"(c3)
-        : "r"(a0), "r"(0), "r"(a2), "r"(0), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
-    (void)c2;
-    (void)c3;
+// m16n8k32 s8 (weights, 16 rows) x u8 (activations, 8 columns) -> s32:
+// lane (g = lane / 4, t = lane % 4) gets weight rows g and g + 8 against
+// activation rows 2t and 2t + 1.
+__device__ __forceinline__ void mma_s8u8(const uint32_t (&a)[4], uint32_t b0, uint32_t b1, int (&d)[4]) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 
-// Epilogue of weight-row pair (n0, n0 + 1) for activation row r (same
-// arithmetic as gemv_tma.cu's pair_epilogue, epilogue chosen at run time).
-__device__ void pair_epi(const GemvParams& p, int epi, int r, int n0, bool has1, float y0, float y1,
-                         unsigned long long* best_s) {
+// Per-phase epilogue inputs staged in shared memory at the start of a GEMV
+// phase (so no epilogue waits on a global load): RoPE positions, KV page
+// and in-page slot per activation row, the RoPE inverse frequencies, and
+// the residual slice [rows_m, nr] of the CTA's output rows.
+constexpr int kResFloats = 512;
+struct EpiSmem {
+    int pos[kMaxRows];
+    int page[kMaxRows];
+    int off[kMaxRows];
+    float freq[64];
+    float res[kResFloats];
+};
+
+// Epilogue of weight-row pair (n0, n0 + 1) for activation row r = p.row0 + m
+// (same arithmetic as gemv_tma.cu's pair_epilogue, chosen at run time).
+// rbase / nr: first output row and row count of this CTA (residual slice).
+__device__ void pair_epi(const GemvParams& p, int epi, int m, int n0, bool has1, float y0, float y1,
+                         unsigned long long* best_s, const EpiSmem& es, int rbase, int nr) {
+    const int r = p.row0 + m;
     if (epi == EPI_STORE || epi == EPI_LOGITS) {
         p.out[(size_t)r * p.ldo + n0] = y0;
         if (has1) p.out[(size_t)r * p.ldo + n0 + 1] = y1;
@@ -172,19 +202,19 @@ __device__ void pair_epi(const GemvParams& p, int epi, int r, int n0, bool has1,
                 const unsigned long long k1 = argmax_key(y1, n0 + 1);
                 k = k1 > k ? k1 : k;
             }
-            atomicMax(&best_s[r - p.row0], k);
+            atomicMax(&best_s[m], k);
         }
     } else if (epi == EPI_RESID) {
         float* o = p.out + (size_t)r * p.ldo + n0;
-        o[0] = __fadd_rn(__ldcg(o), y0);
-        if (has1) o[1] = __fadd_rn(__ldcg(o + 1), y1);
+        const float* res = es.res + m * nr + (n0 - rbase);
+        o[0] = __fadd_rn(res[0], y0);
+        if (has1) o[1] = __fadd_rn(res[1], y1);
     } else if (epi == EPI_QKV) {
         float v0 = y0, v1 = y1;
         const int qkd = p.q_dim + p.kv_dim;
         if (n0 < qkd) {
             const int ii = (n0 < p.q_dim ? n0 : n0 - p.q_dim) % p.head_dim;
-            const float freq = __fdiv_rn(1.0f, powf(p.theta, __fdiv_rn((float)ii, (float)p.head_dim)));
-            const float ang = __fmul_rn((float)__ldcg(p.pos + r), freq);
+            const float ang = __fmul_rn((float)es.pos[m], es.freq[ii >> 1]);
             float sn, cs;
             sincosf(ang, &sn, &cs);
             v0 = __fsub_rn(__fmul_rn(y0, cs), __fmul_rn(y1, sn));
@@ -198,9 +228,7 @@ __device__ void pair_epi(const GemvParams& p, int epi, int r, int n0, bool has1,
             const int c = n0 - (is_k ? p.q_dim : qkd);
             const int h = c / p.head_dim;
             const int dd = c - h * p.head_dim;
-            const int slot = __ldcg(p.slot_base) + r;
-            const int page = p.block_table[slot / kPageSize];
-            const size_t off = (((size_t)page * p.kv_heads + h) * kPageSize + (slot % kPageSize)) * p.head_dim + dd;
+            const size_t off = (((size_t)es.page[m] * p.kv_heads + h) * kPageSize + es.off[m]) * p.head_dim + dd;
             *reinterpret_cast<__half2*>((is_k ? p.kv.k : p.kv.v) + off) = __floats2half2_rn(v0, v1);
         }
     } else if (epi == EPI_SWIGLU) {
@@ -216,11 +244,23 @@ struct Ring {
     int S, slot;
 };
 
-// Consumer side of one GEMV phase. `s` is the global stage counter.
+// The activation prologue out of line: its batched loads want registers
+// that the GEMV loops around it do not need at the same time.
+__device__ __noinline__ void step_prologue(uint8_t* act, int ald, const float* x, int K, int rows, int norm, float eps,
+                                           float* red, int tid) {
+    act_prologue_rows<kCThreads, kMaxRows, true>(act, ald, x, K, rows, norm, eps, red, tid, 1);
+}
+
+// Consumer side of one GEMV phase. `s` is the global stage counter; every
+// consumer warp waits for and releases every stage of the phase.
 __device__ void gemv_phase(const GemvParams& p, int epi, bool skip, const Ring& rg, int& s, bool& bad, int* err,
-                           uint8_t* act, unsigned long long* best_s, float (*red)[kCW][32][4]) {
+                           uint8_t* act, unsigned long long* best_s, float* nred, EpiSmem& es,
+                           unsigned long long* tr, unsigned long long* str) {
+    // tr (CTA 0 only, may be null): [3] prologue done, [4] thread 0's time
+    // waiting for full stages, [5] first stage ready
+    unsigned long long wait_ns = 0;
     GGeo geo;
-    gemv_geo(p, rg.slot, blockIdx.x, gridDim.x, geo);
+    gemv_geo(p, blockIdx.x, gridDim.x, geo);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int rows_m = p.M;
     if (p.dyn_M) rows_m = min(__ldcg(p.dyn_M) - p.row0, p.M);
@@ -234,123 +274,138 @@ __device__ void gemv_phase(const GemvParams& p, int epi, bool skip, const Ring& 
         }
         return;
     }
-    const int K = p.K, P = geo.P, R = geo.R, npan = geo.npan;
+    const int K = p.K, P = geo.P, npan = geo.npan;
     const int ald = K + 16;
-    if (threadIdx.x < kMaxRows) best_s[threadIdx.x] = 0ull;
+    const int tid = threadIdx.x;
+    const int nr = geo.row1 - geo.row0;
+    if (tid < kMaxRows) best_s[tid] = 0ull;
+    // epilogue inputs, loaded in parallel before the activation prologue
+    if (epi == EPI_QKV) {
+        if (tid < rows_m) {
+            const int r = p.row0 + tid;
+            const int slot = __ldcg(p.slot_base) + r;
+            es.pos[tid] = __ldcg(p.pos + r);
+            es.page[tid] = p.block_table[slot / kPageSize];
+            es.off[tid] = slot % kPageSize;
+        }
+        const int half = p.head_dim >> 1;
+        if (tid >= 32 && tid < 32 + half) {
+            const int i = tid - 32;
+            es.freq[i] = __fdiv_rn(1.0f, powf(p.theta, __fdiv_rn((float)(2 * i), (float)p.head_dim)));
+        }
+    } else if (epi == EPI_RESID) {
+        for (int i = tid; i < rows_m * nr; i += kCThreads) {
+            const int m = i / nr, j = i - m * nr;
+            es.res[i] = __ldcg(p.out + (size_t)(p.row0 + m) * p.ldo + geo.row0 + j);
+        }
+    }
     if (p.x) {
         const int src0 = p.x_row_dyn ? __ldcg(p.x_row_dyn) : p.row0;
-        for (int m = warp; m < rows_m; m += kCW)
-            act_prologue(act + (size_t)m * ald, p.x + (size_t)(src0 + m) * K, K, 1, p.norm, p.eps, 0, lane, 1);
+        step_prologue(act, ald, p.x + (size_t)src0 * K, K, rows_m, p.norm, p.eps, nred, tid);
     } else {
         const int K16 = K >> 4;
         const uint4* src = reinterpret_cast<const uint4*>(p.aq + (size_t)p.row0 * K);
-        for (int i = threadIdx.x; i < rows_m * K16; i += kCThreads) {
+        for (int i = tid; i < rows_m * K16; i += kCThreads) {
             const int m = i / K16, c = i - m * K16;
             *reinterpret_cast<uint4*>(act + (size_t)m * ald + (size_t)c * 16) = __ldcg(src + (size_t)m * K16 + c);
         }
     }
     cbar();
-    const int bpp = P >> 5;
-    if (rows_m == 1) {
-        // dp4a: warp = row pair (2w, 2w + 1) of the stage
-        float f0 = 0.0f, f1 = 0.0f;
-        const int lr = 2 * warp;
-        const int cpp = P >> 4;
-        for (int i = 0; i < geo.nstages; i++, s++) {
-            const int sl = s % rg.S;
-            const int tile = i / npan, pan = i - tile * npan;
-            const int r = geo.row0 + tile * R;
-            const int rows = min(R, geo.row1 - r);
+    if (tr && tid == 0) tr[3] = gtime();
+    const int bpp = P >> 5;                 // 32-element blocks per panel row (a multiple of 4)
+    const int g = lane >> 2, t = lane & 3;  // mma fragment coordinates
+    const int lj = lane >> 3, lq = lane & 7;
+    const int wr0 = kWarpRows * warp;       // this warp's first row within a tile
+    // ldmatrix x4 of a 16-row x 32-byte block: matrices (rows 0-7, bytes
+    // 0-15), (rows 8-15, bytes 0-15), (rows 0-7, 16-31), (rows 8-15, 16-31)
+    const int lrow = wr0 + (lj & 1) * 8 + lq;
+    const int lch = lj >> 1;
+    // B fragment: activation row 'col' = g, bytes 4t.. and 16 + 4t.. of a block
+    const bool bcol = g < rows_m;
+    const uint8_t* bcol_p = act + (size_t)g * ald + 4 * t;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // (row g, act 2t), (g, 2t+1), (g+8, 2t), (g+8, 2t+1)
+    for (int i = 0; i < geo.nstages; i++, s++) {
+        const int sl = s % rg.S;
+        const int tile = i / npan, pan = i - tile * npan;
+        const int r = geo.row0 + tile * kTileRows;
+        const int rows = min(kTileRows, geo.row1 - r);  // a multiple of 8
+        const bool mine = wr0 < rows;                   // warp-uniform
+        {
+            // timer reads cost ~0.1 us each: thread 0 (and warp 7's lane 0
+            // for the stage trace) only
+            const bool t0r = tr && tid == 0;
+            const unsigned long long w0 = t0r ? gtime() : 0;
             if (!bad && !mb_wait(&rg.full[sl], (s / rg.S) & 1, err)) bad = true;
-            if (!bad && lr < rows) {
-                const uint8_t* dw = rg.base + (size_t)sl * rg.slot;
-                const __half* ds = reinterpret_cast<const __half*>(dw + (size_t)R * P);
-                const int ra = lr, rb = (lr + 1 < rows) ? lr + 1 : lr;
-                const uint8_t* wa = dw + (size_t)ra * P;
-                const uint8_t* wb = dw + (size_t)rb * P;
-                for (int c = lane; c < cpp; c += 32) {
-                    const uint4 w0 = *reinterpret_cast<const uint4*>(wa + swz_chunk(c, r + ra) * 16);
-                    const uint4 w1 = *reinterpret_cast<const uint4*>(wb + swz_chunk(c, r + rb) * 16);
-                    const float s0 = __half2float(ds[ra * bpp + (c >> 1)]);
-                    const float s1 = __half2float(ds[rb * bpp + (c >> 1)]);
-                    const uint4 a = *reinterpret_cast<const uint4*>(act + (size_t)pan * P + (size_t)c * 16);
-                    f0 = __fmaf_rn(i2f_exact(dot16(a, w0)), s0, f0);
-                    f1 = __fmaf_rn(i2f_exact(dot16(a, w1)), s1, f1);
-                }
+            if (t0r) {
+                const unsigned long long w1 = gtime();
+                wait_ns += w1 - w0;
+                if (i == 0) tr[5] = w1;
+                if (str && i < 64) str[8 * i] = w1;
             }
-            __syncwarp();
-            if (lane == 0) mb_arrive(&rg.empty[sl]);
-            if (pan == npan - 1) {
-                const float t0 = __fdiv_rn(warp_sum(f0), 127.0f);
-                const float t1 = __fdiv_rn(warp_sum(f1), 127.0f);
-                f0 = f1 = 0.0f;
-                if (!bad && lane == 0 && lr < rows) pair_epi(p, epi, p.row0, r + lr, lr + 1 < rows, t0, t1, best_s);
+            if (str && i < 64 && tid == 32 * (kCW - 1)) str[8 * i + 2] = gtime();
+        }
+        if (!bad && mine) {
+            const uint8_t* dw = rg.base + (size_t)sl * rg.slot;
+            const __half* ds = reinterpret_cast<const __half*>(dw + (size_t)kTileRows * P);
+            // rows past the tile (last tile of a CTA: rows % 16 == 8) read
+            // the tile's last row: in bounds, results dropped
+            const int ar = min(lrow, rows - 1);
+            const uint32_t wrow = saddr(dw + (size_t)ar * P);
+            const int gn = r + ar;  // global row: the swizzle key
+            const __half* sg0 = ds + (size_t)min(wr0 + g, rows - 1) * bpp;
+            const __half* sg8 = ds + (size_t)min(wr0 + g + 8, rows - 1) * bpp;
+            const uint8_t* bp = bcol_p + (size_t)pan * P;
+#pragma unroll 4
+            for (int kb = 0; kb < bpp; kb++) {
+                uint32_t a[4];
+                ldsm_x4(wrow + swz_chunk(2 * kb + lch, gn) * 16, a[0], a[1], a[2], a[3]);
+                uint32_t b0 = 0, b1 = 0;
+                if (bcol) {
+                    b0 = *reinterpret_cast<const uint32_t*>(bp + kb * 32);
+                    b1 = *reinterpret_cast<const uint32_t*>(bp + kb * 32 + 16);
+                }
+                int d[4];
+                mma_s8u8(a, b0, b1, d);
+                const float s0 = __half2float(sg0[kb]);
+                const float s8 = __half2float(sg8[kb]);
+                // sequential over blocks, product then sum (matmul_dequantized's order)
+                acc[0] = __fadd_rn(acc[0], __fmul_rn(i2f_exact(d[0]), s0));
+                acc[1] = __fadd_rn(acc[1], __fmul_rn(i2f_exact(d[1]), s0));
+                acc[2] = __fadd_rn(acc[2], __fmul_rn(i2f_exact(d[2]), s8));
+                acc[3] = __fadd_rn(acc[3], __fmul_rn(i2f_exact(d[3]), s8));
             }
         }
-    } else {
-        // MMA: warp = a slice of the stage's blocks, all rows of the stage
-        const int g = lane >> 2, t = lane & 3;
-        const int kb0 = (warp * bpp) / kCW, kb1 = ((warp + 1) * bpp) / kCW;
-        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        int buf = 0;
-        const int lj = lane >> 3, lq = lane & 7;
-        const bool arow = g < rows_m;
-        for (int i = 0; i < geo.nstages; i++, s++) {
-            const int sl = s % rg.S;
-            const int tile = i / npan, pan = i - tile * npan;
-            const int r = geo.row0 + tile * R;
-            const int rows = min(R, geo.row1 - r);
-            if (!bad && !mb_wait(&rg.full[sl], (s / rg.S) & 1, err)) bad = true;
-            const uint8_t* dw = rg.base + (size_t)sl * rg.slot;
-            const __half* ds = reinterpret_cast<const __half*>(dw + (size_t)R * P);
-            // rows past the stage read its last row (in-bounds, results ignored)
-            const int lrow = min(lq + 8 * (lj >> 1), rows - 1);
-            const uint32_t wrow = saddr(dw + (size_t)lrow * P);
-            const uint8_t* arow_p = act + (size_t)g * ald + (size_t)pan * P;
-            const int sr0 = min(2 * t, rows - 1), sr1 = min(2 * t + 1, rows - 1);
-            const int sr2 = min(8 + 2 * t, rows - 1), sr3 = min(9 + 2 * t, rows - 1);
-            for (int kb = kb0; kb < (bad ? kb0 : kb1); kb++) {
-                uint32_t b00, b01, b10, b11;
-                ldsm_x4(wrow + swz_chunk(2 * kb + (lj & 1), r + lrow) * 16, b00, b01, b10, b11);
-                uint32_t a0 = 0, a2 = 0;
-                if (arow) {
-                    a0 = *reinterpret_cast<const uint32_t*>(arow_p + kb * 32 + 4 * t);
-                    a2 = *reinterpret_cast<const uint32_t*>(arow_p + kb * 32 + 16 + 4 * t);
-                }
-                int d0, d1, d2, d3;
-                mma_u8s8(a0, a2, b00, b01, d0, d1);
-                mma_u8s8(a0, a2, b10, b11, d2, d3);
-                acc[0] = __fmaf_rn(i2f_exact(d0), __half2float(ds[sr0 * bpp + kb]), acc[0]);
-                acc[1] = __fmaf_rn(i2f_exact(d1), __half2float(ds[sr1 * bpp + kb]), acc[1]);
-                acc[2] = __fmaf_rn(i2f_exact(d2), __half2float(ds[sr2 * bpp + kb]), acc[2]);
-                acc[3] = __fmaf_rn(i2f_exact(d3), __half2float(ds[sr3 * bpp + kb]), acc[3]);
-            }
-            __syncwarp();
-            if (lane == 0) mb_arrive(&rg.empty[sl]);
-            if (pan == npan - 1) {
+        __syncwarp();
+        if (str && i < 64 && (tid == 0 || tid == 32 * (kCW - 1))) str[8 * i + (warp ? 3 : 1)] = gtime();
+        if (lane == 0) mb_arrive(&rg.empty[sl]);
+        if (pan == npan - 1) {
+            if (!bad && mine) {
+                // weight-row pairs (g, g + 1) for even g: the odd row comes
+                // from lane + 4 (g + 1, same t)
+                float o[4];
 #pragma unroll
-                for (int q = 0; q < 4; q++) red[buf][warp][lane][q] = acc[q];
-                acc[0] = acc[1] = acc[2] = acc[3] = 0.0f;
-                cbar();
-                if (threadIdx.x < 64 && !bad) {
-                    const int pr = threadIdx.x & 7, m = threadIdx.x >> 3;
-                    if (m < rows_m && 2 * pr < rows) {
-                        const int src_lane = 4 * m + (pr & 3);
-                        const int q0 = (pr >> 2) * 2;
-                        float y0 = 0.0f, y1 = 0.0f;
+                for (int q = 0; q < 4; q++) o[q] = __shfl_xor_sync(0xffffffffu, acc[q], 4);
+                if (!(g & 1)) {
 #pragma unroll
-                        for (int w = 0; w < kCW; w++) {
-                            y0 += red[buf][w][src_lane][q0];
-                            y1 += red[buf][w][src_lane][q0 + 1];
+                    for (int h = 0; h < 2; h++) {          // rows g / g + 8
+                        const int lr = wr0 + g + 8 * h;
+                        if (lr < rows) {
+#pragma unroll
+                            for (int c2 = 0; c2 < 2; c2++) {  // activation rows 2t / 2t + 1
+                                const int m = 2 * t + c2;
+                                if (m < rows_m)
+                                    pair_epi(p, epi, m, r + lr, true, __fdiv_rn(acc[2 * h + c2], 127.0f),
+                                             __fdiv_rn(o[2 * h + c2], 127.0f), best_s, es, geo.row0, nr);
+                            }
                         }
-                        pair_epi(p, epi, p.row0 + m, r + 2 * pr, 2 * pr + 1 < rows, __fdiv_rn(y0, 127.0f),
-                                 __fdiv_rn(y1, 127.0f), best_s);
                     }
                 }
-                buf ^= 1;
             }
+#pragma unroll
+            for (int q = 0; q < 4; q++) acc[q] = 0.0f;
         }
     }
+    if (tr && tid == 0) tr[4] = wait_ns;
     if (epi == EPI_LOGITS) {
         cbar();
         if (threadIdx.x < (unsigned)rows_m)
@@ -392,14 +447,22 @@ __device__ void attn_unit(const AttnParams& p, int h, int sp, int nsplit_max, At
         sm.q[rr][dd] = __ldcg(p.q + (size_t)rr * qd + (size_t)h * hd + dd);
     }
     {
+        // the page of this head is nt * hd contiguous halves: 16-byte loads
         const int page = p.block_table[sp];
         const size_t off = (((size_t)page * p.kv_heads + kvh) * kPageSize) * hd2;
-        const uint32_t* kg = reinterpret_cast<const uint32_t*>(p.kv.k) + off;
-        const uint32_t* vg = reinterpret_cast<const uint32_t*>(p.kv.v) + off;
-        for (int i = tid; i < nt * hd2; i += 128) {
-            const int key = i / hd2, c = i - key * hd2;
-            sm.K[key][c] = __ldcg(kg + i);
-            sm.V[key][c] = __ldcg(vg + i);
+        const uint4* kg = reinterpret_cast<const uint4*>(reinterpret_cast<const uint32_t*>(p.kv.k) + off);
+        const uint4* vg = reinterpret_cast<const uint4*>(reinterpret_cast<const uint32_t*>(p.kv.v) + off);
+        const int hd8 = hd2 >> 2;  // 16-byte chunks per key
+#pragma unroll 4
+        for (int i = tid; i < nt * hd8; i += 128) {
+            const uint4 kv4 = __ldcg(kg + i);
+            const uint4 vv4 = __ldcg(vg + i);
+            const int key = i / hd8, c = (i - key * hd8) * 4;
+            sm.K[key][c] = kv4.x;
+            sm.K[key][c + 1] = kv4.y;
+            sm.K[key][c + 2] = kv4.z;
+            sm.K[key][c + 3] = kv4.w;
+            *reinterpret_cast<uint4*>(&sm.V[key][c]) = vv4;
         }
     }
     abar();
@@ -616,9 +679,15 @@ __global__ void __launch_bounds__(kThr, 1) step_kernel(const StepParams p, int* 
     __shared__ __align__(8) uint64_t empty[kMaxSlots];
     __shared__ unsigned long long best_s[kMaxRows];
     __shared__ unsigned long long red8[kCW];
-    __shared__ float red[2][kCW][32][4];
     __shared__ int tgt[kMaxRows];
     __shared__ int ok_s, skip_s;
+    __shared__ float nred[kMaxRows * kCW];
+    __shared__ EpiSmem es;
+    // phase descriptors, double-buffered: phase ph + 1 is loaded into
+    // registers at the start of phase ph and stored here at its end
+    constexpr int kPW = (int)(sizeof(Phase) / sizeof(uint2));
+    static_assert(sizeof(Phase) % sizeof(uint2) == 0, "Phase is copied in 8-byte words");
+    __shared__ uint2 sph[2][kPW];
 
     if (__ldcg(p.done)) return;  // whole step already finished: uniform early exit
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -641,37 +710,58 @@ __global__ void __launch_bounds__(kThr, 1) step_kernel(const StepParams p, int* 
         // ---------------- producer: every GEMV phase's stages, in order ----------------
         if (lane != 0) return;
         int s = 0;
-        for (int ph = 0; ph < p.nphases; ph++) {
+        bool ok = true;
+        for (int ph = 0; ph < p.nphases && ok; ph++) {
             const Phase* P = p.phases + ph;
             if (P->kind != PH_GEMV) continue;
+            unsigned long long* str =
+                p.trace && blockIdx.x == 0 && ph == p.trace_phase ? p.trace + kTr * p.nphases : nullptr;
             GGeo geo;
-            gemv_geo(P->g, p.slot_bytes, blockIdx.x, gridDim.x, geo);
+            gemv_geo(P->g, blockIdx.x, gridDim.x, geo);
             const int N = P->g.N;
             const uint8_t* sb = reinterpret_cast<const uint8_t*>(P->g.sblk);
             for (int i = 0; i < geo.nstages; i++, s++) {
                 const int sl = s % p.S;
-                if (s >= p.S && !mb_wait(&empty[sl], ((s / p.S) - 1) & 1, err)) return;
+                if (str && i < 64) str[8 * i + 4] = gtime();
+                if (s >= p.S && !mb_wait(&empty[sl], ((s / p.S) - 1) & 1, err)) {
+                    ok = false;
+                    break;
+                }
+                if (str && i < 64) str[8 * i + 5] = gtime();
                 const int tile = i / geo.npan, pan = i - tile * geo.npan;
-                const int r = geo.row0 + tile * geo.R;
-                const int rows = min(geo.R, geo.row1 - r);
+                const int r = geo.row0 + tile * kTileRows;
+                const int rows = min(kTileRows, geo.row1 - r);
                 uint8_t* dw = rg.base + (size_t)sl * p.slot_bytes;
-                uint8_t* ds = dw + (size_t)geo.R * geo.P;
+                uint8_t* ds = dw + (size_t)kTileRows * geo.P;
                 mb_expect(&full[sl], (uint32_t)(rows * geo.P + rows * (geo.P / 16)));
                 bulk(dw, P->g.w + ((size_t)pan * N + r) * geo.P, (uint32_t)(rows * geo.P), &full[sl]);
                 bulk(ds, sb + ((size_t)pan * N + r) * (geo.P / 16), (uint32_t)(rows * (geo.P / 16)), &full[sl]);
             }
         }
+        // The CTA stays alive until the copies of the last S issued stages
+        // have landed (bounded), whatever the consumers did.
+        for (int t = s - p.S < 0 ? 0 : s - p.S; t < s; t++)
+            if (!mb_wait(&full[t % p.S], (t / p.S) & 1, err)) break;
         return;
     }
 
     // ---------------- consumers ----------------
     int s = 0;
     bool bad = false, skip = false;
+    const uint2* gph = reinterpret_cast<const uint2*>(p.phases);
+    if (threadIdx.x < kPW) sph[0][threadIdx.x] = __ldg(gph + threadIdx.x);
+    cbar();
     for (int ph = 0; ph < p.nphases; ph++) {
-        const Phase& P = p.phases[ph];
+        const bool more = ph + 1 < p.nphases;
+        uint2 nxt = make_uint2(0u, 0u);
+        if (more && threadIdx.x < kPW) nxt = __ldg(gph + (size_t)(ph + 1) * kPW + threadIdx.x);
+        const Phase& P = *reinterpret_cast<const Phase*>(sph[ph & 1]);
         const int kind = P.kind;
+        if (p.trace && blockIdx.x == 0 && threadIdx.x == 0) p.trace[kTr * ph] = gtime();
         if (kind == PH_GEMV) {
-            gemv_phase(P.g, P.epi, skip || bad, rg, s, bad, err, smem, best_s, red);
+            gemv_phase(P.g, P.epi, skip || bad, rg, s, bad, err, smem, best_s, nred, es,
+                       p.trace && blockIdx.x == 0 ? p.trace + kTr * ph : nullptr,
+                       p.trace && blockIdx.x == 0 && ph == p.trace_phase ? p.trace + kTr * p.nphases : nullptr);
         } else if (kind == PH_ATTN) {
             if (!skip && !bad && warp < 4) {
                 const AttnParams& a = P.a;
@@ -683,11 +773,17 @@ __global__ void __launch_bounds__(kThr, 1) step_kernel(const StepParams p, int* 
         } else if (!skip && !bad && blockIdx.x == 0) {
             control(kind, P.arg, p.sb, p.K, red8, tgt);
         }
-        if (ph + 1 < p.nphases) {
-            if (!grid_sync(p.bar, err, &ok_s, bad)) bad = true;
-            if (threadIdx.x == 0) skip_s = __ldcg(p.done);
-            cbar();
-            skip = skip_s != 0;
+        if (more) {
+            if (threadIdx.x < kPW) sph[(ph + 1) & 1][threadIdx.x] = nxt;
+            if (!grid_sync(reinterpret_cast<unsigned long long*>(p.bar), (unsigned long long)(ph + 1) * gridDim.x,
+                           err, &ok_s, bad, p.trace ? p.trace + kTr * ph : nullptr))
+                bad = true;
+            if (kind == PH_ACCEPT) {
+                // `done` changes only in the acceptance phase
+                if (threadIdx.x == 0) skip_s = __ldcg(p.done);
+                cbar();
+                skip = skip_s != 0;
+            }
         }
     }
 }
@@ -713,32 +809,23 @@ bool step_plan(const Phase* ph, int n, StepParams& sp, size_t* smem_bytes) {
         if (ph[i].kind != PH_GEMV) continue;
         const GemvParams& g = ph[i].g;
         if (g.P == 0 || g.N % 8 || g.K % g.P || g.M < 1 || g.M > kMaxRows) return false;
+        if (ph[i].epi == EPI_QKV && (g.head_dim > kHdMax || g.head_dim % 8)) return false;
+        if (ph[i].epi == EPI_RESID) {
+            const int grid = step_grid();
+            const int rows_cta = ((g.N / 8 + grid - 1) / grid) * 8;
+            if (rows_cta * g.M > kResFloats) return false;
+        }
         region = region > g.M * (g.K + 16) ? region : g.M * (g.K + 16);
         pmax = pmax > g.P ? pmax : g.P;
     }
     region = (region + 127) & ~127;
     const int avail = kSmemLimit - region;
-    // choose the slot count that keeps the most bytes in flight (>= 2 slots,
-    // and a stage of at least 2 rows of the widest panel)
-    int best_s = 0, best_slot = 0;
-    long best_inflight = -1;
-    for (int S = 2; S <= kMaxSlots; S++) {
-        int slot = (avail / S) & ~127;
-        if (stage_rows(pmax ? pmax : 128, slot) < 2) break;
-        long used = 0;
-        for (int i = 0; i < n; i++) {
-            if (ph[i].kind != PH_GEMV) continue;
-            const int R = stage_rows(ph[i].g.P, slot);
-            const long u = (long)S * R * (ph[i].g.P + ph[i].g.P / 16);
-            used = used == 0 ? u : (u < used ? u : used);  // worst phase decides
-        }
-        if (used > best_inflight) {
-            best_inflight = used;
-            best_s = S;
-            best_slot = slot;
-        }
-    }
-    if (!best_s) return false;
+    // one slot holds a tile of the widest panel; as many slots as fit
+    const int slot = slot_need(pmax ? pmax : 128);
+    int best_s = avail / slot;
+    if (best_s > kMaxSlots) best_s = kMaxSlots;
+    if (best_s < 2) return false;
+    const int best_slot = slot;
     sp.region_bytes = region;
     sp.S = best_s;
     sp.slot_bytes = best_slot;
@@ -746,9 +833,11 @@ bool step_plan(const Phase* ph, int n, StepParams& sp, size_t* smem_bytes) {
     return true;
 }
 
+cudaError_t step_set_smem(size_t smem) {
+    return cudaFuncSetAttribute(step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+}
+
 cudaError_t launch_step(const StepParams& p, size_t smem, cudaStream_t s) {
-    cudaError_t e = cudaFuncSetAttribute(step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
     int* err = reinterpret_cast<int*>(p.bar + 2);  // bar: [arrivals, generation, error word]
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(step_grid());

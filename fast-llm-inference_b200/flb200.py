@@ -119,6 +119,8 @@ _SIGS = {
     "fl_engine_stream": (VP, [VP]),
     "fl_engine_last_launches": (C.c_longlong, [VP]),
     "fl_engine_step_kernel": (I, [VP]),
+    "fl_engine_step_trace": (I, [VP, VP, VP, I]),
+    "fl_engine_step_trace_stages": (I, [VP, VP]),
     "fl_engine_draft_bound": (I, [VP, VP]),
     "fl_engine_note_draft": (None, [VP, VP]),
     "fl_engine_bench_linear": (I, [VP, I, I, I, I, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
@@ -323,6 +325,26 @@ class Engine:
 
     def last_launches(self) -> int:
         return self.lib.fl_engine_last_launches(self.h)
+
+    def step_kernel(self) -> bool:
+        """True when the current step graph is the one-kernel step."""
+        return bool(self.lib.fl_engine_step_kernel(self.h))
+
+    def step_trace(self, cap=4096):
+        """(t [n,6] uint64 ns, desc [n,4] int32) of the last step-kernel
+        launch; empty when FL_STEP_TRACE=1 was not set at graph build."""
+        t = np.zeros((cap, 6), np.uint64)
+        d = np.zeros((cap, 4), np.int32)
+        n = self.lib.fl_engine_step_trace(self.h, ptr(t), ptr(d), cap)
+        if n < 0:
+            self.lib.check(n, "step_trace")
+        return t[:n], d[:n]
+
+    def step_trace_stages(self):
+        """[64, 4] uint64 stage stamps of the phase FL_STEP_TRACE_PHASE names."""
+        t = np.zeros((64, 8), np.uint64)
+        self.lib.fl_engine_step_trace_stages(self.h, ptr(t))
+        return t
 
     def bench_linear(self, stack, kind, M, reps=10):
         us, by = C.c_double(), C.c_double()

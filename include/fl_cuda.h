@@ -192,6 +192,22 @@ long long fl_engine_last_launches(const fl_engine_t* e);
 /* 1 when speculative steps run as one persistent kernel per step (all
  * weights in the tiled layout), 0 when they run as one kernel per op. */
 int fl_engine_step_kernel(const fl_engine_t* e);
+/* Phase trace of the last step-kernel launch, recorded only when the
+ * environment has FL_STEP_TRACE=1 when the step graph is built. For each of
+ * the first min(cap, phases) phases: t[6i] start on CTA 0, t[6i+1] end of
+ * CTA 0's work, t[6i+2] latest end over all CTAs (%globaltimer ns; the last
+ * phase has no end stamps), for GEMV phases on CTA 0 t[6i+3] activation
+ * prologue done, t[6i+4] ns spent waiting for weight stages, t[6i+5] first
+ * stage ready; and desc[4i..4i+3] = kind (0 GEMV, 1 attention,
+ * 2 draft pick, 3 verify prep, 4 accept, 5 catch-up prep), epilogue (GEMV)
+ * or argument, N, K. Returns the phase count written, 0 when not tracing. */
+int fl_engine_step_trace(const fl_engine_t* e, unsigned long long* t, int* desc, int cap);
+/* Stage trace of the phase named by FL_STEP_TRACE_PHASE (with FL_STEP_TRACE=1)
+ * in the last launch, CTA 0: t[8s..8s+5] = warp 0 stage s ready, warp 0
+ * done, last consumer warp ready, done, producer starts waiting for the
+ * slot, producer issues the copy (%globaltimer ns), 64 stages; 512 words.
+ * Returns 64, or 0 when not tracing. */
+int fl_engine_step_trace_stages(const fl_engine_t* e, unsigned long long* t);
 /* 1 when `draft` (a draft_model_t*) is the draft whose weights the engine
  * holds; fl_engine_note_draft records it after a load. */
 int fl_engine_draft_bound(const fl_engine_t* e, const void* draft);

@@ -127,6 +127,31 @@ def test_spec_decode_repeatable(small):
     assert np.array_equal(c, a[:7])
 
 
+@pytest.mark.parametrize("k", [1, 4])
+def test_step_kernel_and_multi_kernel_match_oracle(small, gpu, monkeypatch, k):
+    """The one-kernel step (persistent cooperative kernel) and the
+    multi-kernel step graph each reproduce the oracle's stream over several
+    steps (their GEMV reductions are ordered differently, so they are
+    compared with the oracle, not bit for bit with each other)."""
+    dims, eng, om, embed = small
+    p = prompt(12, 16, dims["vocab"])
+    want, acc_want, margins = om.spec(p, 33, k)
+    got, acc = eng.spec_generate(p, 33, k)
+    if dims is not SMALL_V1:
+        assert eng.step_kernel(), "tiled block-scaled weights should take the one-kernel step"
+    assert_stream_matches(got, want, margins)
+    if np.array_equal(got, want):
+        assert np.array_equal(acc, acc_want)
+    w, embed2 = make_weights(gpu, dims, seed=21)
+    monkeypatch.setenv("FL_DISABLE_STEP_KERNEL", "1")
+    ref = flb200.Engine(gpu, engine_cfg(dims, draft_layers=1))
+    load_engine(ref, w, embed2)
+    got_mk, acc_mk = ref.spec_generate(p, 33, k)
+    assert not ref.step_kernel()
+    ref.close()
+    assert_stream_matches(got_mk, want, margins)
+
+
 def test_max_accepted_cap(small):
     dims, eng, om, embed = small
     p = prompt(8, 16, dims["vocab"])
