@@ -58,6 +58,14 @@ cudaStream_t device_stream() {
     return g_streams[dev];
 }
 
+// The library stream of the current device if it exists (never creates one).
+cudaStream_t existing_device_stream() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    return dev < (int)g_streams.size() ? g_streams[dev] : nullptr;
+}
+
 int upload_tensor(dequantized_tensor_t* t) {
     if (!t || !t->weights || t->rows <= 0 || t->cols <= 0)
         return set_error(FL_E_INVAL, "upload_tensor: tensor without int8 weights");
@@ -185,6 +193,35 @@ static int scratch_q(size_t bytes, uint8_t** out) {
     return FL_OK;
 }
 
+// Fixed scratch of fl_cuda_block_dots_i8_noalloc: the quantized activations
+// of one call (M * K bytes), in the module's static device memory so that
+// the call allocates nothing. Each byte a call reads is first written by
+// the same call's quantization, so nothing needs to start at zero. One
+// buffer per device: overlapping calls (other streams or threads) race.
+static __device__ __align__(256) uint8_t g_noalloc_q[FL_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+static uint8_t* g_noalloc_ptr[kMaxDevices] = {};
+static std::mutex g_noalloc_mu;
+
+// Device address of g_noalloc_q on the current device, resolved once per
+// device (the first resolution may load the module).
+static int noalloc_scratch(uint8_t** out) {
+    int dev = 0;
+    FL_CHECK_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return set_error(FL_E_INVAL, "block_dots_noalloc: device index out of range");
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* a = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&a, g_noalloc_q);
+        if (e != cudaSuccess || !a) return cuda_error(e != cudaSuccess ? e : cudaErrorInvalidSymbol,
+                                                      "block_dots_noalloc: cudaGetSymbolAddress of the static scratch");
+        g_noalloc_ptr[dev] = static_cast<uint8_t*>(a);
+    }
+    *out = g_noalloc_ptr[dev];
+    return FL_OK;
+}
+
 }  // namespace fl
 
 using namespace fl;
@@ -283,6 +320,22 @@ FL_API int fl_cuda_matmul_i8(const float* A, const dequantized_tensor_t* B, floa
     FL_CHECK(scratch_q((size_t)M * K, &q));
     FL_CHECK(fl_cuda_act_quant(A, q, M, K, 0, 0.0f, s));
     return run_gemv_chunks(q, B, C, nullptr, M, N, K, s, EPI_STORE);
+}
+
+FL_API int fl_cuda_block_dots_i8_noalloc(const float* A, const dequantized_tensor_t* B, int32_t* D, int M, int N,
+                                         int K, void* stream) {
+    if (!A || !D || M <= 0 || N <= 0 || K <= 0) return set_error(FL_E_INVAL, "block_dots_noalloc: bad arguments");
+    if (K % 32 != 0) return set_error(FL_E_INVAL, "block_dots_noalloc: K must be a multiple of 32");
+    if ((size_t)M * (size_t)K > (size_t)FL_NOALLOC_SCRATCH_BYTES)
+        return set_error(FL_E_INVAL, "block_dots_noalloc: M * K = " + std::to_string((size_t)M * (size_t)K) +
+                                         " exceeds the static scratch of " +
+                                         std::to_string((size_t)FL_NOALLOC_SCRATCH_BYTES) + " bytes");
+    cudaStream_t s = stream ? (cudaStream_t)stream : existing_device_stream();
+    if (!s) return set_error(FL_E_STATE, "block_dots_noalloc: pass a stream or call fl_cuda_init first");
+    uint8_t* q = nullptr;
+    FL_CHECK(noalloc_scratch(&q));
+    FL_CHECK(fl_cuda_act_quant(A, q, M, K, 0, 0.0f, s));
+    return run_gemv_chunks(q, B, nullptr, D, M, N, K, s, EPI_DOTS);
 }
 
 FL_API int fl_cuda_block_dots_i8(const float* A, const dequantized_tensor_t* B, int32_t* D, int M, int N,

@@ -85,6 +85,23 @@ int fl_cuda_gemv_i8(const uint8_t* Aq, const dequantized_tensor_t* B, float* C,
 int fl_cuda_block_dots_i8(const float* A, const dequantized_tensor_t* B, int32_t* D,
                           int M, int N, int K, void* stream);
 
+/* fl_cuda_block_dots_i8 without any allocation: no counterpart in the
+ * reference. The quantized activations go to a fixed device scratch of
+ * FL_NOALLOC_SCRATCH_BYTES in the library's static device memory (one per
+ * device) instead of a buffer cudaMalloc'd and grown on demand; calls with
+ * M * K above that size fail with FL_E_INVAL. For callers that must not
+ * allocate or free device memory: cudaFree synchronises the whole device
+ * and cudaMalloc can fail once a serving process has reserved the rest of
+ * HBM (KV page pools sized to the free memory). `stream` may be NULL only
+ * after fl_cuda_init() created the library stream of the device. The first
+ * call on a device resolves the scratch address (cudaGetSymbolAddress,
+ * which may load the module); make it before any stream capture. Calls that
+ * overlap in time (other streams or threads on the same device) race on
+ * the one scratch; calls on one stream are ordered. */
+#define FL_NOALLOC_SCRATCH_BYTES (1 << 20)
+int fl_cuda_block_dots_i8_noalloc(const float* A, const dequantized_tensor_t* B, int32_t* D,
+                                  int M, int N, int K, void* stream);
+
 /* ------------------------------------------------------------------ */
 /* seeded synthetic weights (the loader side; host code)               */
 /* ------------------------------------------------------------------ */
