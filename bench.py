@@ -245,6 +245,8 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=16, help="tokens of the bounded CPU decode sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--microbench", choices=sorted(MICRO_SHAPES), help="time one GEMV shape in isolation")
+    ap.add_argument("--step-kernel", action="store_true",
+                    help="one persistent tcgen05 kernel per speculative step (128-byte panels)")
     ap.add_argument("--m", type=int, default=5, help="activation rows for --microbench")
     ap.add_argument("--iters", type=int, default=10, help="sweeps for --microbench")
     a = ap.parse_args()
@@ -257,6 +259,8 @@ def main():
 
     if a.impl == "reference":
         return run_reference(a, rank, world)
+    if a.step_kernel:
+        os.environ["FL_STEP_KERNEL"] = "1"
 
     import torch
     import flb200
@@ -378,7 +382,9 @@ def main():
             "config": {"workload": f"phi3-mini int8 (32L d3072 ffn8192 vocab32064) + {DRAFT_LAYERS}-layer draft, "
                                    f"greedy chain k={a.k}, bs1, prompt {a.prompt_len}, {a.new_tokens} new tokens "
                                    f"per step", "parallelism": "replicas only" if world > 1 else "single GPU",
-                       "l2": "inputs larger than L2 (6.4 GB of weights per speculative step)"},
+                       "l2": "inputs larger than L2 (6.4 GB of weights per speculative step)",
+                       "step_path": "one persistent tcgen05 kernel per step" if eng.step_kernel()
+                       else "multi-kernel CUDA graph per step"},
             "spec": {"spec_steps_per_decode": spec_steps, "mean_accepted": float(acc_cat.mean()),
                      "accepted_hist": np.bincount(acc_cat, minlength=a.k + 1).tolist(),
                      "step_us": step_us, "step_bytes": step_bytes(a.k, ctx_mid), "step_gbs": step_gbs,

@@ -99,6 +99,7 @@ struct fl_engine {
     std::vector<int> phase_desc;   // per phase: kind, epilogue, N, K (host)
     unsigned long long* d_trace = nullptr;  // FL_STEP_TRACE=1: 3 words per phase
     bool step_kernel = false;      // last step graph uses the one-kernel step
+    bool step_layout = false;      // weights in 128-byte panels for the tcgen05 step kernel
     float* attn_part = nullptr;   // decode attention split-K scratch
     int* attn_cnt = nullptr;      // per-head arrival counters (zero at rest)
     int graph_kernels = 0;        // kernel nodes in the step graph
@@ -108,13 +109,18 @@ struct fl_engine {
 
 namespace {
 
-int alloc_linear(Linear& l, int N, int K, unsigned need) {
+int alloc_linear(Linear& l, int N, int K, unsigned need, bool step_layout) {
     l.N = N;
     l.K = K;
     l.need = need;
     l.have = 0;
-    // The TMA-ring GEMV reads the tiled layout; shapes it cannot serve stay row-major.
-    l.P = tma_gemv_supported(N, K, 1) ? panel_width(K) : 0;
+    // The TMA-ring GEMV reads the tiled layout; shapes it cannot serve stay
+    // row-major. The tcgen05 step kernel wants 128-byte panels (pairs of them
+    // per ring stage); the TMA-ring GEMV reads those too.
+    if (step_layout && N % 8 == 0 && K % (2 * kStepPanel) == 0)
+        l.P = kStepPanel;
+    else
+        l.P = tma_gemv_supported(N, K, 1) ? panel_width(K) : 0;
     FL_CHECK_CUDA(cudaMalloc(&l.w, (size_t)N * K));
     FL_CHECK_CUDA(cudaMalloc(&l.s, (size_t)N * (K / 32) * sizeof(__half)));
     return FL_OK;
@@ -135,10 +141,10 @@ int alloc_stack(fl_engine* e, Stack& S, int nl) {
     S.pages = (e->c.max_seq_len + kPageSize - 1) / kPageSize;
     for (int l = 0; l < nl; l++) {
         LayerW& W = S.L[l];
-        FL_CHECK(alloc_linear(W.qkv, qd + 2 * kd, d, 0x7u));
-        FL_CHECK(alloc_linear(W.o, d, qd, 0x1u));
-        FL_CHECK(alloc_linear(W.gu, 2 * F, d, 0x3u));
-        FL_CHECK(alloc_linear(W.down, d, F, 0x1u));
+        FL_CHECK(alloc_linear(W.qkv, qd + 2 * kd, d, 0x7u, e->step_layout));
+        FL_CHECK(alloc_linear(W.o, d, qd, 0x1u, e->step_layout));
+        FL_CHECK(alloc_linear(W.gu, 2 * F, d, 0x3u, e->step_layout));
+        FL_CHECK(alloc_linear(W.down, d, F, 0x1u, e->step_layout));
         const size_t kvb = (size_t)S.pages * e->Hkv * kPageSize * e->hd * sizeof(__half);
         FL_CHECK_CUDA(cudaMalloc(&S.kv[l].k, kvb));
         FL_CHECK_CUDA(cudaMalloc(&S.kv[l].v, kvb));
@@ -636,6 +642,12 @@ FL_API fl_engine_t* fl_engine_create(const fl_model_config_t* cfg, int device) {
     if (cudaSetDevice(device) != cudaSuccess) { set_error(FL_E_NODEV, "cudaSetDevice failed"); return nullptr; }
     fl_engine* e = new fl_engine();
     e->c = c;
+    {
+        // FL_STEP_KERNEL=1: 128-byte panels and one persistent tcgen05 kernel
+        // per speculative step; otherwise the multi-kernel step graph
+        const char* sk = getenv("FL_STEP_KERNEL");
+        e->step_layout = sk && sk[0] == '1';
+    }
     e->device = device;
     e->d = c.hidden_size;
     e->H = c.num_heads;
@@ -652,10 +664,10 @@ FL_API fl_engine_t* fl_engine_create(const fl_model_config_t* cfg, int device) {
         if (cudaEventCreate(&ev) != cudaSuccess) return fail(set_error(FL_E_CUDA, "event"));
     if (alloc_stack(e, e->base, c.num_layers) != FL_OK) return fail(0);
     if (c.draft_layers > 0 && alloc_stack(e, e->draft, c.draft_layers) != FL_OK) return fail(0);
-    if (alloc_linear(e->lm, e->V, e->d, 0x1u) != FL_OK) return fail(0);
+    if (alloc_linear(e->lm, e->V, e->d, 0x1u, e->step_layout) != FL_OK) return fail(0);
     e->medusa.resize(c.medusa_heads);
     for (auto& m : e->medusa)
-        if (alloc_linear(m, e->d, e->d, 0x1u) != FL_OK) return fail(0);
+        if (alloc_linear(m, e->d, e->d, 0x1u, e->step_layout) != FL_OK) return fail(0);
     const size_t R = e->R, d = e->d;
     const size_t wq = std::max(e->d, e->qd);
     e->nparts = gemv_auto_grid(e->V, e->d);

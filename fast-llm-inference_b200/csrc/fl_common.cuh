@@ -145,8 +145,15 @@ __device__ __forceinline__ void act_prologue(uint8_t* act, const float* x, int K
 // again to quantise. `red` holds MR * NT / 32 floats; the barrier is named
 // barrier `bar_id` over the NT threads. The caller synchronises before
 // reading `act`. Per element the arithmetic is that of act_prologue
-// (activations_avx2.c:108-143, dequantized_tensor.c:112-135).
-template <int NT, int MR, int CPT, bool CACHE>
+// (activations_avx2.c:108-143, dequantized_tensor.c:112-135). Layout of
+// `act`: row-major with row stride `ald`, or with CM the tensor-core
+// core-matrix layout of 8 rows (16-byte column chunk c of rows 0..7 is 128
+// contiguous bytes at c * 128; `ald` unused).
+__device__ __forceinline__ size_t act_off(bool cm, int m, int c4, int ald) {
+    return cm ? ((size_t)(c4 >> 2) * 128 + (size_t)m * 16 + 4 * (c4 & 3)) : ((size_t)m * ald + 4 * (size_t)c4);
+}
+
+template <int NT, int MR, int CPT, bool CACHE, bool CM = false>
 __device__ __forceinline__ void act_prologue_cta(uint8_t* act, int ald, const float* x, int K, int rows, int norm,
                                                  float eps, float* red, int tid, int bar_id) {
     constexpr int NW = NT / 32;
@@ -197,7 +204,7 @@ __device__ __forceinline__ void act_prologue_cta(uint8_t* act, int ald, const fl
             for (int j = 0; j < CPT; j++) {
                 const int c = tid + j * NT;
                 if (m < rows && c < K4)
-                    *reinterpret_cast<uint32_t*>(act + (size_t)m * ald + 4 * c) =
+                    *reinterpret_cast<uint32_t*>(act + act_off(CM, m, c, ald)) =
                         quant_pack4(__fmul_rn(v[m][j].x, scale[m]), __fmul_rn(v[m][j].y, scale[m]),
                                     __fmul_rn(v[m][j].z, scale[m]), __fmul_rn(v[m][j].w, scale[m]));
             }
@@ -247,7 +254,7 @@ __device__ __forceinline__ void act_prologue_cta(uint8_t* act, int ald, const fl
             for (int m = 0; m < MR; m++)
                 if (m < rows && c0 + j * NT < K4) {
                     const float4 v = __ldcg(x4 + (size_t)m * K4 + c0 + j * NT);
-                    *reinterpret_cast<uint32_t*>(act + (size_t)m * ald + 4 * (c0 + j * NT)) =
+                    *reinterpret_cast<uint32_t*>(act + act_off(CM, m, c0 + j * NT, ald)) =
                         quant_pack4(__fmul_rn(v.x, scale[m]), __fmul_rn(v.y, scale[m]), __fmul_rn(v.z, scale[m]),
                                     __fmul_rn(v.w, scale[m]));
                 }
@@ -256,18 +263,18 @@ __device__ __forceinline__ void act_prologue_cta(uint8_t* act, int ald, const fl
 
 // act_prologue_cta with the row count rounded up to 1, 2, 4 or 8 (at most
 // MMAX); CACHE keeps up to 24 float4 per thread in registers.
-template <int NT, int MMAX, bool CACHE>
+template <int NT, int MMAX, bool CACHE, bool CM = false>
 __device__ __forceinline__ void act_prologue_rows(uint8_t* act, int ald, const float* x, int K, int rows, int norm,
                                                   float eps, float* red, int tid, int bar_id) {
     if (rows <= 1 || MMAX == 1)
-        act_prologue_cta<NT, 1, (CACHE ? 12 : 8), CACHE>(act, ald, x, K, rows, norm, eps, red, tid, bar_id);
+        act_prologue_cta<NT, 1, (CACHE ? 12 : 8), CACHE, CM>(act, ald, x, K, rows, norm, eps, red, tid, bar_id);
     else if (rows <= 2 || MMAX == 2)
-        act_prologue_cta<NT, 2, (CACHE ? 6 : 4), CACHE>(act, ald, x, K, rows, norm, eps, red, tid, bar_id);
+        act_prologue_cta<NT, 2, (CACHE ? 6 : 4), CACHE, CM>(act, ald, x, K, rows, norm, eps, red, tid, bar_id);
     else if (rows <= 4 || MMAX == 4)
-        act_prologue_cta<NT, 4, (CACHE ? 3 : 2), CACHE>(act, ald, x, K, rows, norm, eps, red, tid, bar_id);
+        act_prologue_cta<NT, 4, (CACHE ? 3 : 2), CACHE, CM>(act, ald, x, K, rows, norm, eps, red, tid, bar_id);
     else
-        act_prologue_cta<NT, (MMAX < 8 ? MMAX : 8), (CACHE ? 3 : 1), CACHE>(act, ald, x, K, rows, norm, eps, red, tid,
-                                                                           bar_id);
+        act_prologue_cta<NT, (MMAX < 8 ? MMAX : 8), (CACHE ? 3 : 1), CACHE, CM>(act, ald, x, K, rows, norm, eps, red,
+                                                                               tid, bar_id);
 }
 
 // Streaming 16-byte load that bypasses L1 allocation (weights are read once).

@@ -1,7 +1,8 @@
 // Device layout of INT8 weights for the TMA-ring GEMV ("tiled" layout).
 //
-// A [N, K] int8 matrix is cut along K into panels of width P (the largest
-// divisor of K that is a multiple of 128 and at most FL_PANEL_MAX bytes). Panel p is stored as a row-major [N, P] block, so R consecutive rows
+// A [N, K] int8 matrix is cut along K into panels of width P (a divisor of
+// K that is a multiple of 128: the widest up to FL_PANEL_MAX bytes for the
+// TMA-ring GEMV, 128 for the tcgen05 step kernel). Panel p is stored as a row-major [N, P] block, so R consecutive rows
 // of one panel are contiguous: one 1-D bulk copy moves a whole ring stage.
 // Inside a row the 16-byte chunks of every 128-byte group are XOR-swizzled
 // by (row & 7): chunk c of row n sits at chunk (c & ~7) | ((c & 7) ^ (n & 7)).
@@ -18,13 +19,17 @@
 namespace fl {
 
 #ifndef FL_PANEL_MAX
-#define FL_PANEL_MAX 256
+#define FL_PANEL_MAX 4096
 #endif
-// Widest divisor of K that is a multiple of 128 and at most FL_PANEL_MAX.
-__host__ __device__ inline int panel_width(int K) {
+// Panel width of the tcgen05 step kernel: 128-byte rows are the SWIZZLE_128B
+// K-major operand layout.
+constexpr int kStepPanel = 128;
+
+// Widest divisor of K that is a multiple of 128 and at most pmax.
+__host__ __device__ inline int panel_width(int K, int pmax = FL_PANEL_MAX) {
     if (K <= 0 || K % 128) return 0;
-    for (int n = 1; n <= 128; n++)
-        if (K % n == 0 && (K / n) <= FL_PANEL_MAX && (K / n) % 128 == 0) return K / n;
+    for (int n = 1; n <= K / 128; n++)
+        if (K % n == 0 && (K / n) <= pmax && (K / n) % 128 == 0) return K / n;
     return 0;
 }
 

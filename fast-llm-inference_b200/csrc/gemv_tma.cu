@@ -53,9 +53,10 @@ struct Geo {
 
 __host__ __device__ inline size_t slot_bytes(int P) { return (size_t)kStageRows * P + (size_t)kStageRows * (P / 16); }
 
-inline bool make_geo(int K, int mrows, Geo& g) {
-    g.P = panel_width(K);
-    if (!g.P || mrows < 1 || mrows > kMaxRows) return false;
+// P: the weights' panel width (0 = the default width for K).
+inline bool make_geo(int K, int mrows, Geo& g, int P = 0) {
+    g.P = P ? P : panel_width(K);
+    if (!g.P || g.P % 128 || K % g.P || mrows < 1 || mrows > kMaxRows) return false;
     g.npan = K / g.P;
     g.act_ld = K + 16;
     g.act_bytes = ((mrows * g.act_ld) + 127) & ~127;
@@ -407,7 +408,7 @@ bool tma_gemv_supported(int N, int K, int M) {
 cudaError_t launch_gemv_tma(const GemvParams& p, int epi, cudaStream_t s, bool pdl) {
     if (p.M <= 0 || p.M > kMaxRows || p.N % 8 != 0 || p.P == 0) return cudaErrorInvalidValue;
     Geo geo;
-    if (!make_geo(p.K, p.M, geo) || geo.P != p.P) return cudaErrorInvalidValue;
+    if (!make_geo(p.K, p.M, geo, p.P)) return cudaErrorInvalidValue;
     if (p.x && p.K % 128 != 0) return cudaErrorInvalidValue;
     switch (epi) {
         case EPI_STORE: return launch_e<EPI_STORE>(p, geo, s, pdl);
@@ -420,7 +421,9 @@ cudaError_t launch_gemv_tma(const GemvParams& p, int epi, cudaStream_t s, bool p
 }
 
 cudaError_t launch_gemv_auto(const GemvParams& p, int epi, cudaStream_t s, bool pdl) {
-    if (epi != EPI_DOTS && p.P != 0 && tma_gemv_supported(p.N, p.K, p.M)) return launch_gemv_tma(p, epi, s, pdl);
+    Geo geo;
+    if (epi != EPI_DOTS && p.P != 0 && p.N % 8 == 0 && make_geo(p.K, p.M, geo, p.P))
+        return launch_gemv_tma(p, epi, s, pdl);
     return launch_gemv(p, epi, false, false, s, pdl);
 }
 

@@ -22,9 +22,12 @@ namespace fl {
 
 namespace {
 
-constexpr int kCW = 8;                    // consumer warps
+constexpr int kCW = 8;                    // consumer warps (phase work, barriers)
+constexpr int kRW = 4;                    // of them, TMEM readout warps in GEMV phases
 constexpr int kCThreads = kCW * 32;
-constexpr int kThr = kCThreads + 32;      // + producer warp
+constexpr int kProdWarp = kCW;            // TMA producer
+constexpr int kMmaWarp = kCW + 1;         // tcgen05.mma issuer, TMEM owner
+constexpr int kThr = (kCW + 2) * 32;
 constexpr int kMaxSlots = 12;
 constexpr int kSmemLimit = 222 * 1024;    // + static shared memory <= 227 KB
 constexpr unsigned long long kWaitNs = 2000000000ull;  // every wait gives up after ~2 s
@@ -131,47 +134,76 @@ __device__ bool grid_sync(unsigned long long* ctr, unsigned long long target, in
 }
 
 // ---------------------------------------------------------------- GEMV geometry
-// A ring stage is one tile of kTileRows weight rows x one panel (P bytes
-// per row, plus the rows' fp16 block scales). Consumer warp w owns rows
-// [16w, 16w + 16) of every tile over the whole K: it accumulates its rows'
-// block products across the tile's panels and writes their outputs itself,
-// so a GEMV phase has no cross-warp reduction and no CTA barrier. The
-// weight rows are the 16-row A operand of m16n8k32 and the (up to 8)
-// activation rows the 8-column B operand.
-constexpr int kWarpRows = 16;
-constexpr int kTileRows = kCW * kWarpRows;
+// Weights are in the tiled layout with 128-byte panels (fl_layout.cuh): a
+// panel's rows are 128 contiguous bytes whose 16-byte chunks are XORed with
+// (row & 7), i.e. the tcgen05 SWIZZLE_128B K-major layout when a group of
+// 8 rows starts on a 1024-byte boundary. A ring stage is a tile of
+// kTileRows weight rows x kPPS panels, plus their fp16 block scales; the
+// MMA warp issues one tcgen05.mma kind::i8 (A = 128 weight rows s8,
+// B = the 8 activation rows u8, K = 32) per 32-element block into its own
+// group of 8 TMEM columns, and readout warp w takes TMEM lanes (rows)
+// 32w .. 32w + 31: it scales each block's s32 products by the row's block
+// scale and adds them in block order (matmul_dequantized's order).
+constexpr int kP = 128;                         // panel bytes per row
+constexpr int kPPS = 2;                         // panels per stage
+constexpr int kTileRows = 128;                  // UMMA M
+constexpr int kKBS = kPPS * kP / 32;            // 32-element blocks per stage
+constexpr int kSlot = kPPS * (kTileRows * kP + kTileRows * (kP / 16));  // 34 KB
+constexpr int kCB = kKBS * 8;                   // TMEM columns per stage
+constexpr int kNB = 4;                          // TMEM stage buffers
+constexpr int kTmemCols = kNB * kCB;            // 256
+static_assert(kSlot % 1024 == 0, "stage slots keep the 1024-byte swizzle alignment");
 
 struct GGeo {
-    int P, npan, row0, row1, ntiles, nstages;
+    int nps, row0, row1, ntiles, nstages;  // nps: stages per tile
 };
 
-__host__ __device__ inline int slot_need(int P) { return (kTileRows * (P + P / 16) + 127) & ~127; }
-
 __host__ __device__ inline void gemv_geo(const GemvParams& g, int cta, int ncta, GGeo& o) {
-    o.P = g.P;
-    o.npan = g.K / g.P;
+    o.nps = g.K / (kP * kPPS);
     const int nunits = g.N >> 3;
     const int u0 = (int)(((long long)nunits * cta) / ncta);
     const int u1 = (int)(((long long)nunits * (cta + 1)) / ncta);
     o.row0 = u0 * 8;
     o.row1 = u1 * 8;
     o.ntiles = (o.row1 - o.row0 + kTileRows - 1) / kTileRows;
-    o.nstages = o.ntiles * o.npan;
+    o.nstages = o.ntiles * o.nps;
 }
 
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                 : "r"(addr));
+// Shared-memory matrix descriptor (tcgen05): start, leading / stride byte
+// offsets, version 1, layout type (0 none, 2 128-byte swizzle).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+    uint64_t d = (uint64_t)((addr >> 4) & 0x3FFF);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)(layout & 7) << 61;
+    return d;
 }
 
-// m16n8k32 s8 (weights, 16 rows) x u8 (activations, 8 columns) -> s32:
-// lane (g = lane / 4, t = lane % 4) gets weight rows g and g + 8 against
-// activation rows 2t and 2t + 1.
-__device__ __forceinline__ void mma_s8u8(const uint32_t (&a)[4], uint32_t b0, uint32_t b1, int (&d)[4]) {
-    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
-        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+// D (s32, TMEM) = A (s8, 128 x 32) x B (u8, 32 x 8), not accumulated.
+__device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t da, uint64_t db) {
+    // instruction descriptor: D s32, A s8, B u8, both K-major, N = 8, M = 128
+    constexpr uint32_t idesc = (2u << 4) | (1u << 7) | (0u << 10) | (1u << 17) | (8u << 24);
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(idesc), "r"(0)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* b) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(saddr(b))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// warp-uniform bounded wait: lane 0 waits, the result is broadcast
+__device__ __forceinline__ bool warp_wait(uint64_t* b, uint32_t par, int* err) {
+    bool ok = true;
+    if ((threadIdx.x & 31) == 0) ok = mb_wait(b, par, err);
+    return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
 }
 
 // Per-phase epilogue inputs staged in shared memory at the start of a GEMV
@@ -239,48 +271,117 @@ __device__ void pair_epi(const GemvParams& p, int epi, int m, int n0, bool has1,
 
 struct Ring {
     uint8_t* base;
-    uint64_t* full;
-    uint64_t* empty;
+    uint64_t* full;    // TMA bytes landed
+    uint64_t* empty;   // slot free (readout warps)
+    uint64_t* mdone;   // [kNB] stage MMAs complete (tcgen05.commit)
+    uint64_t* tfree;   // [kNB] stage TMEM read (readout warps)
+    uint64_t* actrdy;  // activations of the phase written
+    uint32_t tmem;
     int S, slot;
 };
 
 // The activation prologue out of line: its batched loads want registers
 // that the GEMV loops around it do not need at the same time.
-__device__ __noinline__ void step_prologue(uint8_t* act, int ald, const float* x, int K, int rows, int norm, float eps,
+__device__ __noinline__ void step_prologue(uint8_t* act, const float* x, int K, int rows, int norm, float eps,
                                            float* red, int tid) {
-    act_prologue_rows<kCThreads, kMaxRows, true>(act, ald, x, K, rows, norm, eps, red, tid, 1);
+    act_prologue_rows<kCThreads, kMaxRows, true, true>(act, 0, x, K, rows, norm, eps, red, tid, 1);
 }
 
-// Consumer side of one GEMV phase. `s` is the global stage counter; every
-// consumer warp waits for and releases every stage of the phase.
-__device__ void gemv_phase(const GemvParams& p, int epi, bool skip, const Ring& rg, int& s, bool& bad, int* err,
-                           uint8_t* act, unsigned long long* best_s, float* nred, EpiSmem& es,
+// Consumer side of one GEMV phase (all 8 consumer warps: prologue; warps
+// 0..3: TMEM readout and epilogue). `s` is the global stage counter, `g`
+// the GEMV phase counter. With `skip` the protocol runs but no output is
+// written.
+template <int MR>
+__device__ void gemv_readout(const GemvParams& p, int epi, bool skip, const Ring& rg, int s, bool& bad, int* err,
+                             const GGeo& geo, int rows_m, unsigned long long* best_s, const EpiSmem& es,
+                             unsigned long long* tr, unsigned long long* str) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row = 32 * warp + lane;  // tile row = TMEM lane
+    const int nr = geo.row1 - geo.row0;
+    float acc[MR];
+#pragma unroll
+    for (int m = 0; m < MR; m++) acc[m] = 0.0f;
+    for (int i = 0; i < geo.nstages; i++, s++) {
+        const int sl = s % rg.S, buf = s % kNB;
+        const int tile = i / geo.nps, pp = i - tile * geo.nps;
+        const int r = geo.row0 + tile * kTileRows;
+        const int rows = min(kTileRows, geo.row1 - r);
+        if (bad) break;
+        if (!warp_wait(&rg.mdone[buf], (s / kNB) & 1, err)) {
+            bad = true;
+            break;
+        }
+        if (tr && threadIdx.x == 0 && i == 0) tr[5] = gtime();
+        if (str && i < 64 && threadIdx.x == 0) str[8 * i] = gtime();
+        tc_fence_after();
+        uint32_t v[kKBS * MR];
+        const uint32_t ta = rg.tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(buf * kCB);
+#pragma unroll
+        for (int kb = 0; kb < kKBS; kb++) {
+            if (MR == 8) {
+                asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                             : "=r"(v[kb * MR + 0]), "=r"(v[kb * MR + 1]), "=r"(v[kb * MR + 2]), "=r"(v[kb * MR + 3]),
+                               "=r"(v[kb * MR + 4]), "=r"(v[kb * MR + 5]), "=r"(v[kb * MR + 6]), "=r"(v[kb * MR + 7])
+                             : "r"(ta + kb * 8));
+            } else {
+                asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(v[kb * MR]) : "r"(ta + kb * 8));
+            }
+        }
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mb_arrive(&rg.tfree[buf]);
+        // the row's block scales; the slot is released right after
+        if (!warp_wait(&rg.full[sl], (s / rg.S) & 1, err)) {
+            bad = true;
+            break;
+        }
+        const uint8_t* dsc = rg.base + (size_t)sl * rg.slot + kPPS * kTileRows * kP;
+        uint2 sc[kPPS];
+#pragma unroll
+        for (int j = 0; j < kPPS; j++) sc[j] = *reinterpret_cast<const uint2*>(dsc + j * kTileRows * (kP / 16) + row * 8);
+        __syncwarp();
+        if (lane == 0) mb_arrive(&rg.empty[sl]);
+        if (str && i < 64 && threadIdx.x == 0) str[8 * i + 1] = gtime();
+#pragma unroll
+        for (int kb = 0; kb < kKBS; kb++) {
+            const uint32_t hw = (kb & 2) ? sc[kb / 4].y : sc[kb / 4].x;
+            const __half2 h2 = *reinterpret_cast<const __half2*>(&hw);
+            const float sk = (kb & 1) ? __high2float(h2) : __low2float(h2);
+#pragma unroll
+            for (int m = 0; m < MR; m++) acc[m] = __fadd_rn(acc[m], __fmul_rn(i2f_exact((int)v[kb * MR + m]), sk));
+        }
+        if (pp == geo.nps - 1) {
+            // weight-row pairs (row, row + 1) for even rows: the odd row's
+            // values come from lane + 1
+#pragma unroll
+            for (int m = 0; m < MR; m++) {
+                const float o = __shfl_down_sync(0xffffffffu, acc[m], 1);
+                if (!skip && !(lane & 1) && row < rows && m < rows_m)
+                    pair_epi(p, epi, m, r + row, true, __fdiv_rn(acc[m], 127.0f), __fdiv_rn(o, 127.0f), best_s, es,
+                             geo.row0, nr);
+                acc[m] = 0.0f;
+            }
+        }
+    }
+}
+
+__device__ void gemv_phase(const GemvParams& p, int epi, bool skip, const Ring& rg, int& s, int& g, bool& bad,
+                           int* err, uint8_t* act, unsigned long long* best_s, float* nred, EpiSmem& es,
                            unsigned long long* tr, unsigned long long* str) {
-    // tr (CTA 0 only, may be null): [3] prologue done, [4] thread 0's time
-    // waiting for full stages, [5] first stage ready
-    unsigned long long wait_ns = 0;
+    // tr (CTA 0 only, may be null): [3] prologue done, [5] first stage read
     GGeo geo;
     gemv_geo(p, blockIdx.x, gridDim.x, geo);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
     int rows_m = p.M;
     if (p.dyn_M) rows_m = min(__ldcg(p.dyn_M) - p.row0, p.M);
     rows_m = max(0, min(rows_m, kMaxRows));
-    if (skip || rows_m == 0) {
-        // keep the ring in step with the producer without computing
-        for (int i = 0; i < geo.nstages; i++, s++) {
-            if (!bad && !mb_wait(&rg.full[s % rg.S], (s / rg.S) & 1, err)) bad = true;
-            __syncwarp();
-            if (lane == 0) mb_arrive(&rg.empty[s % rg.S]);
-        }
-        return;
-    }
-    const int K = p.K, P = geo.P, npan = geo.npan;
-    const int ald = K + 16;
+    const int K = p.K;
     const int tid = threadIdx.x;
     const int nr = geo.row1 - geo.row0;
     if (tid < kMaxRows) best_s[tid] = 0ull;
     // epilogue inputs, loaded in parallel before the activation prologue
-    if (epi == EPI_QKV) {
+    if (!skip && epi == EPI_QKV) {
         if (tid < rows_m) {
             const int r = p.row0 + tid;
             const int slot = __ldcg(p.slot_base) + r;
@@ -293,122 +394,50 @@ __device__ void gemv_phase(const GemvParams& p, int epi, bool skip, const Ring& 
             const int i = tid - 32;
             es.freq[i] = __fdiv_rn(1.0f, powf(p.theta, __fdiv_rn((float)(2 * i), (float)p.head_dim)));
         }
-    } else if (epi == EPI_RESID) {
+    } else if (!skip && epi == EPI_RESID) {
         for (int i = tid; i < rows_m * nr; i += kCThreads) {
             const int m = i / nr, j = i - m * nr;
             es.res[i] = __ldcg(p.out + (size_t)(p.row0 + m) * p.ldo + geo.row0 + j);
         }
     }
-    if (p.x) {
+    // activations in the core-matrix layout of 8 rows; rows >= rows_m zero
+    if (!skip && p.x && rows_m > 0) {
         const int src0 = p.x_row_dyn ? __ldcg(p.x_row_dyn) : p.row0;
-        step_prologue(act, ald, p.x + (size_t)src0 * K, K, rows_m, p.norm, p.eps, nred, tid);
-    } else {
+        step_prologue(act, p.x + (size_t)src0 * K, K, rows_m, p.norm, p.eps, nred, tid);
+    } else if (!skip && rows_m > 0) {
         const int K16 = K >> 4;
         const uint4* src = reinterpret_cast<const uint4*>(p.aq + (size_t)p.row0 * K);
         for (int i = tid; i < rows_m * K16; i += kCThreads) {
             const int m = i / K16, c = i - m * K16;
-            *reinterpret_cast<uint4*>(act + (size_t)m * ald + (size_t)c * 16) = __ldcg(src + (size_t)m * K16 + c);
+            *reinterpret_cast<uint4*>(act + (size_t)c * 128 + m * 16) = __ldcg(src + (size_t)m * K16 + c);
         }
     }
+    {
+        const int K16 = K >> 4;
+        const int zr = kMaxRows - rows_m;
+        for (int i = tid; i < zr * K16; i += kCThreads) {
+            const int m = rows_m + i / K16, c = i % K16;
+            *reinterpret_cast<uint4*>(act + (size_t)c * 128 + m * 16) = make_uint4(0u, 0u, 0u, 0u);
+        }
+    }
+    // generic-proxy writes -> visible to the tensor core's async proxy
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     cbar();
-    if (tr && tid == 0) tr[3] = gtime();
-    const int bpp = P >> 5;                 // 32-element blocks per panel row (a multiple of 4)
-    const int g = lane >> 2, t = lane & 3;  // mma fragment coordinates
-    const int lj = lane >> 3, lq = lane & 7;
-    const int wr0 = kWarpRows * warp;       // this warp's first row within a tile
-    // ldmatrix x4 of a 16-row x 32-byte block: matrices (rows 0-7, bytes
-    // 0-15), (rows 8-15, bytes 0-15), (rows 0-7, 16-31), (rows 8-15, 16-31)
-    const int lrow = wr0 + (lj & 1) * 8 + lq;
-    const int lch = lj >> 1;
-    // B fragment: activation row 'col' = g, bytes 4t.. and 16 + 4t.. of a block
-    const bool bcol = g < rows_m;
-    const uint8_t* bcol_p = act + (size_t)g * ald + 4 * t;
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // (row g, act 2t), (g, 2t+1), (g+8, 2t), (g+8, 2t+1)
-    for (int i = 0; i < geo.nstages; i++, s++) {
-        const int sl = s % rg.S;
-        const int tile = i / npan, pan = i - tile * npan;
-        const int r = geo.row0 + tile * kTileRows;
-        const int rows = min(kTileRows, geo.row1 - r);  // a multiple of 8
-        const bool mine = wr0 < rows;                   // warp-uniform
-        {
-            // timer reads cost ~0.1 us each: thread 0 (and warp 7's lane 0
-            // for the stage trace) only
-            const bool t0r = tr && tid == 0;
-            const unsigned long long w0 = t0r ? gtime() : 0;
-            if (!bad && !mb_wait(&rg.full[sl], (s / rg.S) & 1, err)) bad = true;
-            if (t0r) {
-                const unsigned long long w1 = gtime();
-                wait_ns += w1 - w0;
-                if (i == 0) tr[5] = w1;
-                if (str && i < 64) str[8 * i] = w1;
-            }
-            if (str && i < 64 && tid == 32 * (kCW - 1)) str[8 * i + 2] = gtime();
-        }
-        if (!bad && mine) {
-            const uint8_t* dw = rg.base + (size_t)sl * rg.slot;
-            const __half* ds = reinterpret_cast<const __half*>(dw + (size_t)kTileRows * P);
-            // rows past the tile (last tile of a CTA: rows % 16 == 8) read
-            // the tile's last row: in bounds, results dropped
-            const int ar = min(lrow, rows - 1);
-            const uint32_t wrow = saddr(dw + (size_t)ar * P);
-            const int gn = r + ar;  // global row: the swizzle key
-            const __half* sg0 = ds + (size_t)min(wr0 + g, rows - 1) * bpp;
-            const __half* sg8 = ds + (size_t)min(wr0 + g + 8, rows - 1) * bpp;
-            const uint8_t* bp = bcol_p + (size_t)pan * P;
-#pragma unroll 4
-            for (int kb = 0; kb < bpp; kb++) {
-                uint32_t a[4];
-                ldsm_x4(wrow + swz_chunk(2 * kb + lch, gn) * 16, a[0], a[1], a[2], a[3]);
-                uint32_t b0 = 0, b1 = 0;
-                if (bcol) {
-                    b0 = *reinterpret_cast<const uint32_t*>(bp + kb * 32);
-                    b1 = *reinterpret_cast<const uint32_t*>(bp + kb * 32 + 16);
-                }
-                int d[4];
-                mma_s8u8(a, b0, b1, d);
-                const float s0 = __half2float(sg0[kb]);
-                const float s8 = __half2float(sg8[kb]);
-                // sequential over blocks, product then sum (matmul_dequantized's order)
-                acc[0] = __fadd_rn(acc[0], __fmul_rn(i2f_exact(d[0]), s0));
-                acc[1] = __fadd_rn(acc[1], __fmul_rn(i2f_exact(d[1]), s0));
-                acc[2] = __fadd_rn(acc[2], __fmul_rn(i2f_exact(d[2]), s8));
-                acc[3] = __fadd_rn(acc[3], __fmul_rn(i2f_exact(d[3]), s8));
-            }
-        }
-        __syncwarp();
-        if (str && i < 64 && (tid == 0 || tid == 32 * (kCW - 1))) str[8 * i + (warp ? 3 : 1)] = gtime();
-        if (lane == 0) mb_arrive(&rg.empty[sl]);
-        if (pan == npan - 1) {
-            if (!bad && mine) {
-                // weight-row pairs (g, g + 1) for even g: the odd row comes
-                // from lane + 4 (g + 1, same t)
-                float o[4];
-#pragma unroll
-                for (int q = 0; q < 4; q++) o[q] = __shfl_xor_sync(0xffffffffu, acc[q], 4);
-                if (!(g & 1)) {
-#pragma unroll
-                    for (int h = 0; h < 2; h++) {          // rows g / g + 8
-                        const int lr = wr0 + g + 8 * h;
-                        if (lr < rows) {
-#pragma unroll
-                            for (int c2 = 0; c2 < 2; c2++) {  // activation rows 2t / 2t + 1
-                                const int m = 2 * t + c2;
-                                if (m < rows_m)
-                                    pair_epi(p, epi, m, r + lr, true, __fdiv_rn(acc[2 * h + c2], 127.0f),
-                                             __fdiv_rn(o[2 * h + c2], 127.0f), best_s, es, geo.row0, nr);
-                            }
-                        }
-                    }
-                }
-            }
-#pragma unroll
-            for (int q = 0; q < 4; q++) acc[q] = 0.0f;
-        }
+    if (tid == 0) {
+        mb_arrive(rg.actrdy);
+        if (tr) tr[3] = gtime();
     }
-    if (tr && tid == 0) tr[4] = wait_ns;
+    g++;
+    if (warp < kRW) {
+        if (rows_m <= 1)
+            gemv_readout<1>(p, epi, skip || rows_m == 0, rg, s, bad, err, geo, rows_m, best_s, es, tr, str);
+        else
+            gemv_readout<8>(p, epi, skip, rg, s, bad, err, geo, rows_m, best_s, es, tr, str);
+    }
+    s += geo.nstages;
     if (epi == EPI_LOGITS) {
         cbar();
-        if (threadIdx.x < (unsigned)rows_m)
+        if (!skip && threadIdx.x < (unsigned)rows_m)
             p.amax_part[(size_t)(p.row0 + threadIdx.x) * gridDim.x + blockIdx.x] = best_s[threadIdx.x];
     }
 }
@@ -674,9 +703,13 @@ __device__ void control(int kind, int arg, const StepBuffers& b, int K, unsigned
 
 // ---------------------------------------------------------------- the kernel
 __global__ void __launch_bounds__(kThr, 1) step_kernel(const StepParams p, int* err) {
-    extern __shared__ __align__(128) uint8_t smem[];
+    extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[kMaxSlots];
     __shared__ __align__(8) uint64_t empty[kMaxSlots];
+    __shared__ __align__(8) uint64_t mdone[kNB];
+    __shared__ __align__(8) uint64_t tfree[kNB];
+    __shared__ __align__(8) uint64_t actrdy;
+    __shared__ uint32_t tmem_base;
     __shared__ unsigned long long best_s[kMaxRows];
     __shared__ unsigned long long red8[kCW];
     __shared__ int tgt[kMaxRows];
@@ -689,102 +722,178 @@ __global__ void __launch_bounds__(kThr, 1) step_kernel(const StepParams p, int* 
     static_assert(sizeof(Phase) % sizeof(uint2) == 0, "Phase is copied in 8-byte words");
     __shared__ uint2 sph[2][kPW];
 
-    if (__ldcg(p.done)) return;  // whole step already finished: uniform early exit
+    // uniform early exits, before any barrier or TMEM allocation
+    if (__ldcg(p.done)) return;  // the whole decode already finished
+    if ((saddr(smem) + p.region_bytes) & 1023) {
+        if (threadIdx.x == 0) atomicOr(err, kErrRing);  // the swizzled ring needs 1024-byte alignment
+        return;
+    }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     Ring rg;
     rg.base = smem + p.region_bytes;
     rg.full = full;
     rg.empty = empty;
+    rg.mdone = mdone;
+    rg.tfree = tfree;
+    rg.actrdy = &actrdy;
     rg.S = p.S;
     rg.slot = p.slot_bytes;
     if (threadIdx.x == 0) {
         for (int i = 0; i < p.S; i++) {
             mb_init(&full[i], 1);
-            mb_init(&empty[i], kCW);
+            mb_init(&empty[i], kRW);
         }
+        for (int i = 0; i < kNB; i++) {
+            mb_init(&mdone[i], 1);
+            mb_init(&tfree[i], kRW);
+        }
+        mb_init(&actrdy, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    if (warp == kMmaWarp) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&tmem_base)),
+                     "n"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
     __syncthreads();
+    tc_fence_after();
+    rg.tmem = tmem_base;
 
-    if (warp == kCW) {
+    if (warp == kProdWarp) {
         // ---------------- producer: every GEMV phase's stages, in order ----------------
-        if (lane != 0) return;
-        int s = 0;
+        if (lane == 0) {
+            int s = 0;
+            bool ok = true;
+            for (int ph = 0; ph < p.nphases && ok; ph++) {
+                const Phase* P = p.phases + ph;
+                if (P->kind != PH_GEMV) continue;
+                GGeo geo;
+                gemv_geo(P->g, blockIdx.x, gridDim.x, geo);
+                const int N = P->g.N;
+                const uint8_t* sb = reinterpret_cast<const uint8_t*>(P->g.sblk);
+                for (int i = 0; i < geo.nstages; i++, s++) {
+                    const int sl = s % p.S;
+                    if (s >= p.S && !mb_wait(&empty[sl], ((s / p.S) - 1) & 1, err)) {
+                        ok = false;
+                        break;
+                    }
+                    const int tile = i / geo.nps, pp = i - tile * geo.nps;
+                    const int r = geo.row0 + tile * kTileRows;
+                    const int rows = min(kTileRows, geo.row1 - r);
+                    uint8_t* dw = rg.base + (size_t)sl * p.slot_bytes;
+                    mb_expect(&full[sl], (uint32_t)(kPPS * rows * (kP + kP / 16)));
+#pragma unroll
+                    for (int j = 0; j < kPPS; j++) {
+                        const size_t pan = (size_t)(pp * kPPS + j);
+                        bulk(dw + j * kTileRows * kP, P->g.w + (pan * N + r) * kP, (uint32_t)(rows * kP), &full[sl]);
+                        bulk(dw + kPPS * kTileRows * kP + j * kTileRows * (kP / 16), sb + (pan * N + r) * (kP / 16),
+                             (uint32_t)(rows * (kP / 16)), &full[sl]);
+                    }
+                }
+            }
+            // the copies of the last S issued stages land before the CTA ends
+            for (int t = s - p.S < 0 ? 0 : s - p.S; t < s; t++)
+                if (!mb_wait(&full[t % p.S], (t / p.S) & 1, err)) break;
+        }
+    } else if (warp == kMmaWarp) {
+        // ---------------- MMA issuer: every GEMV phase's stages, in order ----------------
+        int s = 0, g = 0, issued = 0;
         bool ok = true;
+        const uint32_t act_addr = saddr(smem);
         for (int ph = 0; ph < p.nphases && ok; ph++) {
             const Phase* P = p.phases + ph;
             if (P->kind != PH_GEMV) continue;
-            unsigned long long* str =
-                p.trace && blockIdx.x == 0 && ph == p.trace_phase ? p.trace + kTr * p.nphases : nullptr;
             GGeo geo;
             gemv_geo(P->g, blockIdx.x, gridDim.x, geo);
-            const int N = P->g.N;
-            const uint8_t* sb = reinterpret_cast<const uint8_t*>(P->g.sblk);
+            unsigned long long* str =
+                p.trace && blockIdx.x == 0 && ph == p.trace_phase ? p.trace + kTr * p.nphases : nullptr;
+            if (!warp_wait(&actrdy, g & 1, err)) {
+                ok = false;
+                break;
+            }
+            g++;
             for (int i = 0; i < geo.nstages; i++, s++) {
-                const int sl = s % p.S;
-                if (str && i < 64) str[8 * i + 4] = gtime();
-                if (s >= p.S && !mb_wait(&empty[sl], ((s / p.S) - 1) & 1, err)) {
+                const int sl = s % p.S, buf = s % kNB;
+                const int pp = i % geo.nps;
+                if (!warp_wait(&full[sl], (s / p.S) & 1, err)) {
                     ok = false;
                     break;
                 }
-                if (str && i < 64) str[8 * i + 5] = gtime();
-                const int tile = i / geo.npan, pan = i - tile * geo.npan;
-                const int r = geo.row0 + tile * kTileRows;
-                const int rows = min(kTileRows, geo.row1 - r);
-                uint8_t* dw = rg.base + (size_t)sl * p.slot_bytes;
-                uint8_t* ds = dw + (size_t)kTileRows * geo.P;
-                mb_expect(&full[sl], (uint32_t)(rows * geo.P + rows * (geo.P / 16)));
-                bulk(dw, P->g.w + ((size_t)pan * N + r) * geo.P, (uint32_t)(rows * geo.P), &full[sl]);
-                bulk(ds, sb + ((size_t)pan * N + r) * (geo.P / 16), (uint32_t)(rows * (geo.P / 16)), &full[sl]);
+                if (s >= kNB && !warp_wait(&tfree[buf], ((s / kNB) - 1) & 1, err)) {
+                    ok = false;
+                    break;
+                }
+                if (str && i < 64 && lane == 0) str[8 * i + 4] = gtime();
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t wbase = saddr(rg.base + (size_t)sl * p.slot_bytes);
+#pragma unroll
+                    for (int kb = 0; kb < kKBS; kb++) {
+                        const int j = kb / (kP / 32), kk = kb % (kP / 32);
+                        const uint64_t da = smem_desc(wbase + j * kTileRows * kP + kk * 32, 16, 1024, 2);
+                        const uint64_t db = smem_desc(act_addr + (uint32_t)((pp * kKBS + kb) * 256), 128, 256, 0);
+                        umma_i8(rg.tmem + (uint32_t)(buf * kCB + kb * 8), da, db);
+                    }
+                    umma_commit(&mdone[buf]);
+                    if (str && i < 64) str[8 * i + 5] = gtime();
+                }
+                __syncwarp();
+                issued = s + 1;
             }
         }
-        // The CTA stays alive until the copies of the last S issued stages
-        // have landed (bounded), whatever the consumers did.
-        for (int t = s - p.S < 0 ? 0 : s - p.S; t < s; t++)
-            if (!mb_wait(&full[t % p.S], (t / p.S) & 1, err)) break;
-        return;
+        // the MMAs in flight complete before TMEM is released
+        for (int t = issued - kNB < 0 ? 0 : issued - kNB; t < issued; t++)
+            if (!warp_wait(&mdone[t % kNB], (t / kNB) & 1, err)) break;
+    } else {
+        // ---------------- consumers ----------------
+        int s = 0, g = 0;
+        bool bad = false, skip = false;
+        const uint2* gph = reinterpret_cast<const uint2*>(p.phases);
+        if (threadIdx.x < kPW) sph[0][threadIdx.x] = __ldg(gph + threadIdx.x);
+        cbar();
+        for (int ph = 0; ph < p.nphases; ph++) {
+            const bool more = ph + 1 < p.nphases;
+            uint2 nxt = make_uint2(0u, 0u);
+            if (more && threadIdx.x < kPW) nxt = __ldg(gph + (size_t)(ph + 1) * kPW + threadIdx.x);
+            const Phase& P = *reinterpret_cast<const Phase*>(sph[ph & 1]);
+            const int kind = P.kind;
+            if (p.trace && blockIdx.x == 0 && threadIdx.x == 0) p.trace[kTr * ph] = gtime();
+            if (kind == PH_GEMV) {
+                gemv_phase(P.g, P.epi, skip || bad, rg, s, g, bad, err, smem, best_s, nred, es,
+                           p.trace && blockIdx.x == 0 ? p.trace + kTr * ph : nullptr,
+                           p.trace && blockIdx.x == 0 && ph == p.trace_phase ? p.trace + kTr * p.nphases : nullptr);
+            } else if (kind == PH_ATTN) {
+                if (!skip && !bad && warp < 4) {
+                    const AttnParams& a = P.a;
+                    const int nsm = (a.max_ctx + kSplit - 1) / kSplit;
+                    const int units = a.heads * nsm;
+                    for (int u = blockIdx.x; u < units; u += gridDim.x)
+                        attn_unit(a, u / nsm, u % nsm, nsm, *reinterpret_cast<AttnSmem*>(smem));
+                }
+            } else if (!skip && !bad && blockIdx.x == 0) {
+                control(kind, P.arg, p.sb, p.K, red8, tgt);
+            }
+            if (more) {
+                if (threadIdx.x < kPW) sph[(ph + 1) & 1][threadIdx.x] = nxt;
+                if (!grid_sync(reinterpret_cast<unsigned long long*>(p.bar), (unsigned long long)(ph + 1) * gridDim.x,
+                               err, &ok_s, bad, p.trace ? p.trace + kTr * ph : nullptr))
+                    bad = true;
+                if (kind == PH_ACCEPT) {
+                    // `done` changes only in the acceptance phase
+                    if (threadIdx.x == 0) skip_s = __ldcg(p.done);
+                    cbar();
+                    skip = skip_s != 0;
+                }
+            }
+        }
     }
-
-    // ---------------- consumers ----------------
-    int s = 0;
-    bool bad = false, skip = false;
-    const uint2* gph = reinterpret_cast<const uint2*>(p.phases);
-    if (threadIdx.x < kPW) sph[0][threadIdx.x] = __ldg(gph + threadIdx.x);
-    cbar();
-    for (int ph = 0; ph < p.nphases; ph++) {
-        const bool more = ph + 1 < p.nphases;
-        uint2 nxt = make_uint2(0u, 0u);
-        if (more && threadIdx.x < kPW) nxt = __ldg(gph + (size_t)(ph + 1) * kPW + threadIdx.x);
-        const Phase& P = *reinterpret_cast<const Phase*>(sph[ph & 1]);
-        const int kind = P.kind;
-        if (p.trace && blockIdx.x == 0 && threadIdx.x == 0) p.trace[kTr * ph] = gtime();
-        if (kind == PH_GEMV) {
-            gemv_phase(P.g, P.epi, skip || bad, rg, s, bad, err, smem, best_s, nred, es,
-                       p.trace && blockIdx.x == 0 ? p.trace + kTr * ph : nullptr,
-                       p.trace && blockIdx.x == 0 && ph == p.trace_phase ? p.trace + kTr * p.nphases : nullptr);
-        } else if (kind == PH_ATTN) {
-            if (!skip && !bad && warp < 4) {
-                const AttnParams& a = P.a;
-                const int nsm = (a.max_ctx + kSplit - 1) / kSplit;
-                const int units = a.heads * nsm;
-                for (int u = blockIdx.x; u < units; u += gridDim.x)
-                    attn_unit(a, u / nsm, u % nsm, nsm, *reinterpret_cast<AttnSmem*>(smem));
-            }
-        } else if (!skip && !bad && blockIdx.x == 0) {
-            control(kind, P.arg, p.sb, p.K, red8, tgt);
-        }
-        if (more) {
-            if (threadIdx.x < kPW) sph[(ph + 1) & 1][threadIdx.x] = nxt;
-            if (!grid_sync(reinterpret_cast<unsigned long long*>(p.bar), (unsigned long long)(ph + 1) * gridDim.x,
-                           err, &ok_s, bad, p.trace ? p.trace + kTr * ph : nullptr))
-                bad = true;
-            if (kind == PH_ACCEPT) {
-                // `done` changes only in the acceptance phase
-                if (threadIdx.x == 0) skip_s = __ldcg(p.done);
-                cbar();
-                skip = skip_s != 0;
-            }
-        }
+    // TMEM is released by its owner once every warp is done with it
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(rg.tmem), "n"(kTmemCols));
     }
 }
 
@@ -804,32 +913,27 @@ int step_grid() {
 
 bool step_plan(const Phase* ph, int n, StepParams& sp, size_t* smem_bytes) {
     int region = (int)sizeof(AttnSmem);
-    int pmax = 0;
     for (int i = 0; i < n; i++) {
         if (ph[i].kind != PH_GEMV) continue;
         const GemvParams& g = ph[i].g;
-        if (g.P == 0 || g.N % 8 || g.K % g.P || g.M < 1 || g.M > kMaxRows) return false;
+        if (g.P != kP || g.N % 8 || g.K % (kP * kPPS) || g.M < 1 || g.M > kMaxRows) return false;
         if (ph[i].epi == EPI_QKV && (g.head_dim > kHdMax || g.head_dim % 8)) return false;
         if (ph[i].epi == EPI_RESID) {
             const int grid = step_grid();
             const int rows_cta = ((g.N / 8 + grid - 1) / grid) * 8;
             if (rows_cta * g.M > kResFloats) return false;
         }
-        region = region > g.M * (g.K + 16) ? region : g.M * (g.K + 16);
-        pmax = pmax > g.P ? pmax : g.P;
+        region = region > kMaxRows * g.K ? region : kMaxRows * g.K;  // core-matrix activations
     }
-    region = (region + 127) & ~127;
+    region = (region + 1023) & ~1023;
     const int avail = kSmemLimit - region;
-    // one slot holds a tile of the widest panel; as many slots as fit
-    const int slot = slot_need(pmax ? pmax : 128);
-    int best_s = avail / slot;
-    if (best_s > kMaxSlots) best_s = kMaxSlots;
-    if (best_s < 2) return false;
-    const int best_slot = slot;
+    int S = avail / kSlot;
+    if (S > kMaxSlots) S = kMaxSlots;
+    if (S < 2) return false;
     sp.region_bytes = region;
-    sp.S = best_s;
-    sp.slot_bytes = best_slot;
-    *smem_bytes = (size_t)region + (size_t)best_s * best_slot;
+    sp.S = S;
+    sp.slot_bytes = kSlot;
+    *smem_bytes = (size_t)region + (size_t)S * kSlot;
     return true;
 }
 

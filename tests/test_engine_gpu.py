@@ -129,27 +129,29 @@ def test_spec_decode_repeatable(small):
 
 @pytest.mark.parametrize("k", [1, 4])
 def test_step_kernel_and_multi_kernel_match_oracle(small, gpu, monkeypatch, k):
-    """The one-kernel step (persistent cooperative kernel) and the
-    multi-kernel step graph each reproduce the oracle's stream over several
-    steps (their GEMV reductions are ordered differently, so they are
-    compared with the oracle, not bit for bit with each other)."""
+    """The multi-kernel step graph (default engine) and the one-kernel
+    tcgen05 step (engine created with FL_STEP_KERNEL=1: 128-byte panels, one
+    persistent cooperative kernel per step) each reproduce the oracle's
+    stream over several steps."""
     dims, eng, om, embed = small
     p = prompt(12, 16, dims["vocab"])
     want, acc_want, margins = om.spec(p, 33, k)
     got, acc = eng.spec_generate(p, 33, k)
-    if dims is not SMALL_V1:
-        assert eng.step_kernel(), "tiled block-scaled weights should take the one-kernel step"
+    assert not eng.step_kernel()
     assert_stream_matches(got, want, margins)
     if np.array_equal(got, want):
         assert np.array_equal(acc, acc_want)
     w, embed2 = make_weights(gpu, dims, seed=21)
-    monkeypatch.setenv("FL_DISABLE_STEP_KERNEL", "1")
-    ref = flb200.Engine(gpu, engine_cfg(dims, draft_layers=1))
-    load_engine(ref, w, embed2)
-    got_mk, acc_mk = ref.spec_generate(p, 33, k)
-    assert not ref.step_kernel()
-    ref.close()
-    assert_stream_matches(got_mk, want, margins)
+    monkeypatch.setenv("FL_STEP_KERNEL", "1")
+    sk = flb200.Engine(gpu, engine_cfg(dims, draft_layers=1))
+    load_engine(sk, w, embed2)
+    got_sk, acc_sk = sk.spec_generate(p, 33, k)
+    on_step_kernel = sk.step_kernel()
+    sk.close()
+    assert on_step_kernel, "the FL_STEP_KERNEL=1 engine should take the one-kernel step"
+    assert_stream_matches(got_sk, want, margins)
+    if np.array_equal(got_sk, want):
+        assert np.array_equal(acc_sk, acc_want)
 
 
 def test_max_accepted_cap(small):
