@@ -231,7 +231,7 @@ template <int MR>
 __global__ void __launch_bounds__(kDThreads) attention_split_kernel(const AttnParams p) {
     __shared__ __align__(16) float q_s[MR][kMaxHd];
     __shared__ uint32_t Ks[kSplit][kMaxHd / 2 + 1];
-    __shared__ uint32_t Vs[kSplit][kMaxHd / 2];
+    __shared__ __align__(16) uint32_t Vs[kSplit][kMaxHd / 2];
     __shared__ float sc[MR][kSplit];
     __shared__ float ml_s[MR][2];
     __shared__ int ticket_s;
@@ -261,10 +261,28 @@ __global__ void __launch_bounds__(kDThreads) attention_split_kernel(const AttnPa
         const size_t base_off = (((size_t)page * p.kv_heads + kvh) * kPageSize) * hd2;
         const uint32_t* kg = reinterpret_cast<const uint32_t*>(p.kv.k) + base_off;
         const uint32_t* vg = reinterpret_cast<const uint32_t*>(p.kv.v) + base_off;
-        for (int i = threadIdx.x; i < nt * hd2; i += kDThreads) {
-            const int key = i / hd2, c = i - key * hd2;
-            Ks[key][c] = kg[i];
-            Vs[key][c] = vg[i];
+        if ((hd2 & 3) == 0) {
+            // 16-byte loads, all issued before the shared-memory stores
+            const uint4* kg4 = reinterpret_cast<const uint4*>(kg);
+            const uint4* vg4 = reinterpret_cast<const uint4*>(vg);
+            const int hd8 = hd2 >> 2;
+#pragma unroll 4
+            for (int i = threadIdx.x; i < nt * hd8; i += kDThreads) {
+                const uint4 k4 = kg4[i];
+                const uint4 v4 = vg4[i];
+                const int key = i / hd8, c = (i - key * hd8) * 4;
+                Ks[key][c] = k4.x;
+                Ks[key][c + 1] = k4.y;
+                Ks[key][c + 2] = k4.z;
+                Ks[key][c + 3] = k4.w;
+                *reinterpret_cast<uint4*>(&Vs[key][c]) = v4;
+            }
+        } else {
+            for (int i = threadIdx.x; i < nt * hd2; i += kDThreads) {
+                const int key = i / hd2, c = i - key * hd2;
+                Ks[key][c] = kg[i];
+                Vs[key][c] = vg[i];
+            }
         }
     }
     __syncthreads();
