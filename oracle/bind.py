@@ -73,6 +73,10 @@ class Oracle:
         s.orc_kv_free.argtypes = [C.POINTER(KV)]
         s.orc_spec_generate.argtypes = [C.POINTER(Model), VP, I, I, I, I, VP, VP, VP]
         s.orc_greedy_generate.argtypes = [C.POINTER(Model), VP, I, I, VP, VP]
+        s.orc_medusa_generate.restype = I
+        s.orc_medusa_generate.argtypes = [C.POINTER(Model), VP, I, VP, I, I, VP, VP, VP]
+        s.orc_medusa_tree.restype = I
+        s.orc_medusa_tree.argtypes = [I, I, VP, VP, VP, I, I, VP, VP, VP, VP]
         # Every pointer argument must be declared: an undeclared Python int is
         # passed as a 32-bit C int and truncates heap addresses.
         s.orc_quant_u8.argtypes = [VP, VP, I]
@@ -242,6 +246,30 @@ class OracleModel:
         steps = self.orc.so.orc_spec_generate(C.byref(self.m), _p(p), len(p), k, k if max_acc is None else max_acc,
                                               n_new, _p(o), _p(acc), _p(mg))
         return o, acc[:steps], mg
+
+
+    def medusa(self, prompt, n_new, topk, max_nodes):
+        """Medusa greedy decoding: (tokens, accepted per step, margins)."""
+        p = np.ascontiguousarray(prompt, np.int32)
+        tk = np.ascontiguousarray(topk, np.int32)
+        o = np.empty(n_new, np.int32)
+        acc = np.zeros(n_new + 1, np.int32)
+        mg = np.empty(n_new, np.float32)
+        steps = self.orc.so.orc_medusa_generate(C.byref(self.m), _p(p), len(p), _p(tk), max_nodes, n_new, _p(o),
+                                                _p(acc), _p(mg))
+        return o, acc[:steps], mg
+
+
+def medusa_tree(orc, root, topk, tok, prob, max_nodes):
+    """orc_medusa_tree: (tokens, parents, depths, scores) of the kept nodes."""
+    tk = np.ascontiguousarray(topk, np.int32)
+    kmax = tok.shape[1]
+    t = np.ascontiguousarray(tok, np.int32)
+    pr = np.ascontiguousarray(prob, np.float32)
+    ot, op, od = (np.empty(max_nodes, np.int32) for _ in range(3))
+    osc = np.empty(max_nodes, np.float32)
+    n = orc.so.orc_medusa_tree(root, len(tk), _p(tk), _p(t), _p(pr), kmax, max_nodes, _p(ot), _p(op), _p(od), _p(osc))
+    return ot[:n], op[:n], od[:n], osc[:n]
 
 
 class Ref:

@@ -567,3 +567,204 @@ int orc_spec_generate(const orc_model_t* mdl, const int* prompt, int P, int K,
     orc_kv_free(&kvd);
     return steps;
 }
+
+/* ------------------------------------------------------------------ */
+/* Medusa (include/medusa.h rule; the reference declares the API at   */
+/* medusa.h:84-229 without an implementation)                          */
+/* ------------------------------------------------------------------ */
+
+/* Top-k of one logits row (value desc, lower index first on ties) with
+ * softmax probabilities p = exp(l - max) / sum_j exp(l_j - max), the sum in
+ * index order. */
+static void topk_probs(const float* lg, int V, int k, int* tok, float* prob) {
+    float mx = lg[0];
+    for (int i = 1; i < V; i++) if (lg[i] > mx) mx = lg[i];
+    float sum = 0.0f;
+    for (int i = 0; i < V; i++) sum += expf(lg[i] - mx);
+    for (int j = 0; j < k; j++) {
+        int bi = -1;
+        for (int i = 0; i < V; i++) {
+            int taken = 0;
+            for (int q = 0; q < j; q++) if (tok[q] == i) { taken = 1; break; }
+            if (taken) continue;
+            if (bi < 0 || lg[i] > lg[bi]) bi = i;
+        }
+        tok[j] = bi;
+        prob[j] = expf(lg[bi] - mx) / sum;
+    }
+}
+
+typedef struct {
+    float score;
+    int depth, gen, parent_gen, token;
+} med_cand_t;
+
+/* score desc, depth asc, generation order asc */
+static int cand_cmp(const void* a, const void* b) {
+    const med_cand_t* x = (const med_cand_t*)a;
+    const med_cand_t* y = (const med_cand_t*)b;
+    if (x->score != y->score) return x->score > y->score ? -1 : 1;
+    if (x->depth != y->depth) return x->depth < y->depth ? -1 : 1;
+    return x->gen < y->gen ? -1 : (x->gen > y->gen);
+}
+
+int orc_medusa_tree(int root_tok, int n_heads, const int* topk, const int* tok, const float* prob, int kmax,
+                    int max_nodes, int* out_tok, int* out_parent, int* out_depth, float* out_score) {
+    /* candidates in generation (breadth-first) order: level L+1 = head L's
+     * top-k under every level-L candidate; the root is generation -1 */
+    int total = 0, width = 1;
+    for (int h = 0; h < n_heads; h++) { width *= topk[h]; total += width; }
+    med_cand_t* c = (med_cand_t*)malloc(sizeof(med_cand_t) * (size_t)(total > 0 ? total : 1));
+    int lvl_begin = 0, lvl_end = 0, n = 0;
+    for (int h = 0; h < n_heads; h++) {
+        const int pb = lvl_begin, pe = lvl_end;  /* parents: previous level ([0,0) = the root) */
+        lvl_begin = n;
+        if (h == 0) {
+            for (int k = 0; k < topk[0]; k++, n++) {
+                c[n].score = prob[k];
+                c[n].depth = 1;
+                c[n].gen = n;
+                c[n].parent_gen = -1;
+                c[n].token = tok[k];
+            }
+        } else {
+            for (int pi = pb; pi < pe; pi++)
+                for (int k = 0; k < topk[h]; k++, n++) {
+                    c[n].score = c[pi].score * prob[h * kmax + k];
+                    c[n].depth = h + 1;
+                    c[n].gen = n;
+                    c[n].parent_gen = pi;
+                    c[n].token = tok[h * kmax + k];
+                }
+        }
+        lvl_end = n;
+    }
+    med_cand_t* s = (med_cand_t*)malloc(sizeof(med_cand_t) * (size_t)(n > 0 ? n : 1));
+    memcpy(s, c, sizeof(med_cand_t) * (size_t)n);
+    qsort(s, (size_t)n, sizeof(med_cand_t), cand_cmp);
+    int keep = max_nodes - 1 < n ? max_nodes - 1 : n;
+    /* generation index -> output node index */
+    int* where = (int*)malloc(sizeof(int) * (size_t)(n > 0 ? n : 1));
+    for (int i = 0; i < n; i++) where[i] = -1;
+    for (int i = 0; i < keep; i++) where[s[i].gen] = i + 1;
+    out_tok[0] = root_tok;
+    out_parent[0] = -1;
+    out_depth[0] = 0;
+    if (out_score) out_score[0] = 1.0f;
+    for (int i = 0; i < keep; i++) {
+        out_tok[i + 1] = s[i].token;
+        out_parent[i + 1] = s[i].parent_gen < 0 ? 0 : where[s[i].parent_gen];
+        out_depth[i + 1] = s[i].depth;
+        if (out_score) out_score[i + 1] = s[i].score;
+    }
+    free(c); free(s); free(where);
+    return keep + 1;
+}
+
+int orc_medusa_generate(const orc_model_t* mdl, const int* prompt, int P, const int* topk, int max_nodes,
+                        int n_new, int* out, int* acc_hist, float* margins) {
+    const orc_dims_t* D = &mdl->dims;
+    const int d = D->d, V = D->vocab, H = mdl->n_medusa;
+    int kmax = 1;
+    for (int h = 0; h < H; h++) if (topk[h] > kmax) kmax = topk[h];
+    const int cap = P + n_new + max_nodes + 2;
+    orc_kv_t kv;
+    orc_kv_init(&kv, D->layers, cap, D->kv_heads, D->head_dim);
+    const int rows_max = P > max_nodes ? P : max_nodes;
+    float* x = (float*)malloc(sizeof(float) * (size_t)rows_max * d);
+    float* lg = (float*)malloc(sizeof(float) * (size_t)max_nodes * V);
+    float* feat = (float*)malloc(sizeof(float) * d);
+    float* h = (float*)malloc(sizeof(float) * d);
+    float* y = (float*)malloc(sizeof(float) * d);
+    float* z = (float*)malloc(sizeof(float) * d);
+    float* hl = (float*)malloc(sizeof(float) * V);
+    int* pos = (int*)malloc(sizeof(int) * rows_max);
+    int* ttok = (int*)malloc(sizeof(int) * (size_t)(H > 0 ? H : 1) * kmax);
+    float* tprob = (float*)malloc(sizeof(float) * (size_t)(H > 0 ? H : 1) * kmax);
+    int* ntok = (int*)malloc(sizeof(int) * max_nodes);
+    int* npar = (int*)malloc(sizeof(int) * max_nodes);
+    int* ndep = (int*)malloc(sizeof(int) * max_nodes);
+    int* target = (int*)malloc(sizeof(int) * max_nodes);
+    int* path = (int*)malloc(sizeof(int) * max_nodes);
+    uint8_t* mask = (uint8_t*)malloc((size_t)max_nodes * max_nodes);
+
+    /* prefill: base KV 0..P-1, first token from the last prompt row */
+    for (int i = 0; i < P; i++) {
+        memcpy(x + (size_t)i * d, mdl->embed + (size_t)tok_or_zero(prompt[i], V) * d, sizeof(float) * d);
+        pos[i] = i;
+    }
+    orc_stack_forward(mdl, mdl->base, D->layers, &kv, x, P, 0, pos, NULL);
+    memcpy(feat, x + (size_t)(P - 1) * d, sizeof(float) * d);
+    orc_lm_logits(mdl, feat, lg, 1);
+    int n = P;                  /* the newest token (seq[n]) is not in the KV yet */
+    int cur_tok = orc_argmax(lg, V);
+    int produced = 0;
+    out[produced] = cur_tok;
+    if (margins) margins[produced] = top2_margin(lg, V);
+    produced++;
+    int steps = 0;
+    const double t0 = now_s();
+    while (produced < n_new) {
+        /* heads on h = RMSNorm(F): z_i = h + SiLU(W_i h), logits_i = LM(z_i) */
+        orc_rmsnorm(feat, h, d, D->eps);
+        for (int i = 0; i < H; i++) {
+            lin(&mdl->medusa[i], h, y, 1);
+            orc_silu(y, z, d);
+            for (int j = 0; j < d; j++) z[j] = h[j] + z[j];
+            lin(&mdl->lm, z, hl, 1);
+            topk_probs(hl, V, topk[i], ttok + (size_t)i * kmax, tprob + (size_t)i * kmax);
+        }
+        const int M = orc_medusa_tree(cur_tok, H, topk, ttok, tprob, kmax, max_nodes, ntok, npar, ndep, NULL);
+        /* tree-masked verify: node i at slot n + i, position n + depth */
+        for (int i = 0; i < M; i++) {
+            memcpy(x + (size_t)i * d, mdl->embed + (size_t)tok_or_zero(ntok[i], V) * d, sizeof(float) * d);
+            pos[i] = n + ndep[i];
+            for (int j = 0; j < M; j++) mask[(size_t)i * M + j] = 0;
+            for (int j = i; j >= 0; j = npar[j]) mask[(size_t)i * M + j] = 1;
+        }
+        orc_stack_forward(mdl, mdl->base, D->layers, &kv, x, M, n, pos, mask);
+        orc_lm_logits(mdl, x, lg, M);
+        for (int i = 0; i < M; i++) target[i] = orc_argmax(lg + (size_t)i * V, V);
+        /* longest path whose tokens are the base model's greedy choices */
+        int a = 0, cur = 0;
+        path[0] = 0;
+        for (;;) {
+            int nxt = -1;
+            for (int c2 = 1; c2 < M; c2++)
+                if (npar[c2] == cur && ntok[c2] == target[cur]) { nxt = c2; break; }
+            if (nxt < 0) break;
+            path[++a] = nxt;
+            cur = nxt;
+        }
+        if (acc_hist) acc_hist[steps] = a;
+        steps++;
+        /* emitted: the accepted children, then the base token after the last one */
+        for (int j = 1; j <= a + 1 && produced < n_new; j++) {
+            const int t = j <= a ? ntok[path[j]] : target[cur];
+            out[produced] = t;
+            if (margins) margins[produced] = top2_margin(lg + (size_t)path[j - 1] * V, V);
+            produced++;
+        }
+        /* KV compaction: the accepted nodes move to slots n .. n + a (their
+         * rotary positions were already n + depth) */
+        for (int j = 1; j <= a; j++) {
+            const int src = n + path[j], dst = n + j;
+            if (src == dst) continue;
+            for (int l = 0; l < kv.layers; l++) {
+                const size_t row = (size_t)kv.kv_heads * kv.head_dim;
+                float* kb = kv.k + (size_t)l * kv.cap * row;
+                float* vb = kv.v + (size_t)l * kv.cap * row;
+                memcpy(kb + (size_t)dst * row, kb + (size_t)src * row, sizeof(float) * row);
+                memcpy(vb + (size_t)dst * row, vb + (size_t)src * row, sizeof(float) * row);
+            }
+        }
+        memcpy(feat, x + (size_t)cur * d, sizeof(float) * d);
+        cur_tok = target[cur];
+        n += a + 1;
+    }
+    g_last_decode_s = now_s() - t0;
+    free(x); free(lg); free(feat); free(h); free(y); free(z); free(hl); free(pos); free(ttok); free(tprob);
+    free(ntok); free(npar); free(ndep); free(target); free(path); free(mask);
+    orc_kv_free(&kv);
+    return steps;
+}
