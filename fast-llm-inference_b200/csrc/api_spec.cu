@@ -9,6 +9,7 @@
 #include <map>
 #include <mutex>
 #include <string>
+#include <unordered_map>
 #include <vector>
 
 #include "fl_common.cuh"
@@ -106,7 +107,52 @@ int load_draft_into(fl_engine_t* e, const draft_model_t* dm) {
     return FL_OK;
 }
 
+// Medusa tree settings per model (medusa_model_t has no room for them):
+// per-head top-k and the node budget.
+struct MedusaTree {
+    std::vector<int> topk;
+    int max_nodes = 64;
+};
+std::unordered_map<const void*, MedusaTree> g_med_tree;
+
 }  // namespace
+
+int medusa_tree_settings(const medusa_model_t* m, const medusa_config_t* cfg, std::vector<int>& topk,
+                         int* max_nodes) {
+    std::lock_guard<std::mutex> lk(g_bind_mu);
+    const int H = m->num_heads < cfg->num_heads ? m->num_heads : cfg->num_heads;
+    auto it = g_med_tree.find(m);
+    topk.assign(H, cfg->top_k);
+    *max_nodes = 64;
+    if (it != g_med_tree.end()) {
+        for (int h = 0; h < H && h < (int)it->second.topk.size(); h++) topk[h] = it->second.topk[h];
+        *max_nodes = it->second.max_nodes;
+    }
+    return H;
+}
+
+int medusa_bind(fl_engine_t* e, medusa_model_t* m) {
+    if (bound(m) == e) return FL_OK;
+    for (int h = 0; h < m->num_heads; h++) {
+        const dequantized_tensor_t* t = m->heads[h].weights;
+        if (!t || !t->weights) return set_error(FL_E_STATE, "medusa head without weights");
+        if (t->scale_block != 32 || !t->scales_f16)
+            return set_error(FL_E_UNSUPPORTED, "medusa heads must be in block mode (scale_block 32)");
+        if (m->heads[h].bias) return set_error(FL_E_UNSUPPORTED, "medusa head bias is not supported");
+        FL_CHECK(fl_engine_load_linear(e, 2, h, 0, t->weights, t->scales_f16, t->rows, t->cols));
+    }
+    bind(m, e);
+    return FL_OK;
+}
+
+FL_API int fl_medusa_set_tree(medusa_model_t* m, const int* topk, int n, int max_nodes) {
+    if (!m || !topk || n <= 0 || max_nodes < 2) return set_error(FL_E_INVAL, "fl_medusa_set_tree: bad arguments");
+    std::lock_guard<std::mutex> lk(g_bind_mu);
+    MedusaTree& t = g_med_tree[m];
+    t.topk.assign(topk, topk + n);
+    t.max_nodes = max_nodes;
+    return FL_OK;
+}
 
 // ------------------------------------------------------------------ speculative.h
 
@@ -362,6 +408,10 @@ FL_API int medusa_model_load(medusa_model_t* m, const char* path) {
 FL_API void medusa_model_free(medusa_model_t* m) {
     if (!m) return;
     unbind(m);
+    {
+        std::lock_guard<std::mutex> lk(g_bind_mu);
+        g_med_tree.erase(m);
+    }
     for (int h = 0; h < m->num_heads; h++) {
         free_tensor_array(m->heads[h].weights, 1);
         free(m->heads[h].bias);

@@ -1139,3 +1139,214 @@ FL_API int fl_engine_draft_chain(fl_engine_t* e, const float* hidden, int tok, i
     }
     return FL_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Medusa greedy decoding (include/medusa.h rule)
+// ---------------------------------------------------------------------------
+namespace {
+
+// out[M, N] = L(quantise(x)) (optionally RMSNorm first), M <= kMaxRows.
+int gemv_rows(fl_engine* e, const Linear& L, const float* x, int M, bool norm, float* out, int ldo) {
+    GemvParams g = gemv_base(L, e->xq, nullptr);
+    if ((L.K % 128) == 0) {
+        g.x = x;
+        g.norm = norm ? 1 : 0;
+        g.eps = e->c.norm_eps;
+    } else {
+        ActQuantParams a = {};
+        a.x = x;
+        a.q = e->xq;
+        a.K = L.K;
+        a.M = M;
+        a.norm = norm ? 1 : 0;
+        a.eps = e->c.norm_eps;
+        FL_CHECK_CUDA(launch_act_quant(a, e->s, false));
+    }
+    g.out = out;
+    g.ldo = ldo;
+    g.M = M;
+    g.row0 = 0;
+    FL_CHECK_CUDA(launch_gemv_auto(g, EPI_STORE, e->s, false));
+    return FL_OK;
+}
+
+struct MedCand {
+    float score;
+    int depth, gen, parent_gen, token;
+};
+
+// Candidate tree from the heads' top-k lists: level L + 1 = head L's top-k
+// under every level-L node (breadth-first generation order), score = product
+// of the probabilities along the path; the best max_nodes - 1 candidates by
+// (score desc, depth asc, generation asc) are kept, root first. A child never
+// outscores its parent and loses ties to it, so the kept set is
+// ancestor-closed and every parent precedes its children.
+int build_tree(int root_tok, int H, const int* topk, const int* tok, const float* prob, int kmax, int max_nodes,
+               std::vector<int>& ntok, std::vector<int>& npar, std::vector<int>& ndep) {
+    std::vector<MedCand> c;
+    int pb = 0, pe = 0;
+    for (int h = 0; h < H; h++) {
+        const int lb = (int)c.size();
+        if (h == 0) {
+            for (int k = 0; k < topk[0]; k++)
+                c.push_back({prob[k], 1, (int)c.size(), -1, tok[k]});
+        } else {
+            for (int pi = pb; pi < pe; pi++)
+                for (int k = 0; k < topk[h]; k++)
+                    c.push_back({c[pi].score * prob[h * kmax + k], h + 1, (int)c.size(), pi, tok[h * kmax + k]});
+        }
+        pb = lb;
+        pe = (int)c.size();
+    }
+    std::vector<MedCand> s = c;
+    std::sort(s.begin(), s.end(), [](const MedCand& x, const MedCand& y) {
+        if (x.score != y.score) return x.score > y.score;
+        if (x.depth != y.depth) return x.depth < y.depth;
+        return x.gen < y.gen;
+    });
+    const int keep = std::min<int>(max_nodes - 1, (int)s.size());
+    std::vector<int> where(c.size(), -1);
+    for (int i = 0; i < keep; i++) where[s[i].gen] = i + 1;
+    ntok.assign(1, root_tok);
+    npar.assign(1, -1);
+    ndep.assign(1, 0);
+    for (int i = 0; i < keep; i++) {
+        ntok.push_back(s[i].token);
+        npar.push_back(s[i].parent_gen < 0 ? 0 : where[s[i].parent_gen]);
+        ndep.push_back(s[i].depth);
+    }
+    return keep + 1;
+}
+
+}  // namespace
+
+FL_API int fl_engine_medusa_generate(fl_engine_t* e, const int* prompt, int P, int n_new, const int* topk, int H,
+                                     int max_nodes, int* out, int* acc_hist, int* steps_out) {
+    FL_CHECK(check_ready(e, false));
+    if (!prompt || !out || !topk || P <= 0 || n_new <= 0 || H <= 0 || H > (int)e->medusa.size() || H > kMaxRows ||
+        max_nodes < 2 || max_nodes > 256 || P + n_new + max_nodes + 2 > e->R)
+        return set_error(FL_E_INVAL, "medusa_generate: bad arguments, missing heads or context too long");
+    int kmax = 1;
+    for (int h = 0; h < H; h++) {
+        if (topk[h] < 1 || topk[h] > 32) return set_error(FL_E_INVAL, "medusa_generate: top-k must be 1..32");
+        kmax = std::max(kmax, topk[h]);
+    }
+    const int d = e->d, V = e->V;
+    cudaStream_t s = e->s;
+    // device work buffers for this call
+    float *mf = nullptr, *my = nullptr, *mz = nullptr, *mprob = nullptr;
+    int *mk = nullptr, *mtt = nullptr, *mtok = nullptr, *mpos = nullptr, *mtarget = nullptr, *mpath = nullptr;
+    KvLayer* dkv = nullptr;
+    auto cleanup = [&]() {
+        void* bufs[] = {mf, my, mz, mprob, mk, mtt, mtok, mpos, mtarget, mpath, dkv};
+        for (void* p : bufs) cudaFree(p);
+    };
+    auto fail = [&](int rc) {
+        cleanup();
+        return rc;
+    };
+#define FL_MED_CUDA(expr)                                                    \
+    do {                                                                     \
+        cudaError_t fl_e_ = (expr);                                          \
+        if (fl_e_ != cudaSuccess) return fail(cuda_error(fl_e_, #expr));     \
+    } while (0)
+#define FL_MED(expr)                      \
+    do {                                  \
+        int fl_r_ = (expr);               \
+        if (fl_r_ != FL_OK) return fail(fl_r_); \
+    } while (0)
+    FL_MED_CUDA(cudaMalloc(&mf, sizeof(float) * d));
+    FL_MED_CUDA(cudaMalloc(&my, sizeof(float) * (size_t)H * d));
+    FL_MED_CUDA(cudaMalloc(&mz, sizeof(float) * (size_t)H * d));
+    FL_MED_CUDA(cudaMalloc(&mprob, sizeof(float) * (size_t)H * kmax));
+    FL_MED_CUDA(cudaMalloc(&mk, sizeof(int) * H));
+    FL_MED_CUDA(cudaMalloc(&mtt, sizeof(int) * (size_t)H * kmax));
+    FL_MED_CUDA(cudaMalloc(&mtok, sizeof(int) * max_nodes));
+    FL_MED_CUDA(cudaMalloc(&mpos, sizeof(int) * max_nodes));
+    FL_MED_CUDA(cudaMalloc(&mtarget, sizeof(int) * max_nodes));
+    FL_MED_CUDA(cudaMalloc(&mpath, sizeof(int) * max_nodes));
+    FL_MED_CUDA(cudaMalloc(&dkv, sizeof(KvLayer) * e->base.nl));
+    FL_MED_CUDA(cudaMemcpyAsync(dkv, e->base.kv.data(), sizeof(KvLayer) * e->base.nl, cudaMemcpyHostToDevice, s));
+    FL_MED_CUDA(cudaMemcpyAsync(mk, topk, sizeof(int) * H, cudaMemcpyHostToDevice, s));
+    FL_MED(ensure_mask(e, max_nodes));
+
+    // prefill: base KV 0 .. P-1, first token from the last prompt row
+    FL_MED(prefill_base(e, prompt, P));
+    FL_MED_CUDA(cudaMemcpyAsync(mf, e->x + (size_t)(P - 1) * d, sizeof(float) * d, cudaMemcpyDeviceToDevice, s));
+    int cur_tok = 0;
+    FL_MED_CUDA(cudaMemcpyAsync(&cur_tok, e->seq + P, sizeof(int), cudaMemcpyDeviceToHost, s));
+    FL_MED_CUDA(cudaStreamSynchronize(s));
+    int produced = 0, steps = 0, n = P;
+    out[produced++] = cur_tok;
+    std::vector<int> htok((size_t)H * kmax), target(max_nodes), ntok, npar, ndep, path;
+    std::vector<float> hprob((size_t)H * kmax);
+    std::vector<int> hpos(max_nodes);
+    std::vector<uint8_t> mask((size_t)max_nodes * max_nodes);
+    FL_MED_CUDA(cudaEventRecord(e->ev[0], s));
+    while (produced < n_new) {
+        // heads: h = RMSNorm(F), y_i = W_i h, z_i = h + SiLU(y_i), logits_i = LM(z_i)
+        FL_MED_CUDA(launch_medusa_z(mf, my, e->x2, mz, d, 0, e->c.norm_eps, s));  // h -> x2
+        for (int h = 0; h < H; h++) FL_MED(gemv_rows(e, e->medusa[h], e->x2, 1, false, my + (size_t)h * d, d));
+        FL_MED_CUDA(launch_medusa_z(mf, my, nullptr, mz, d, H, e->c.norm_eps, s));
+        FL_MED(gemv_rows(e, e->lm, mz, H, false, e->logits, V));
+        FL_MED_CUDA(launch_topk_rows(e->logits, H, V, V, mk, kmax, mtt, mprob, s));
+        FL_MED_CUDA(cudaMemcpyAsync(htok.data(), mtt, sizeof(int) * htok.size(), cudaMemcpyDeviceToHost, s));
+        FL_MED_CUDA(cudaMemcpyAsync(hprob.data(), mprob, sizeof(float) * hprob.size(), cudaMemcpyDeviceToHost, s));
+        FL_MED_CUDA(cudaStreamSynchronize(s));
+        const int M = build_tree(cur_tok, H, topk, htok.data(), hprob.data(), kmax, max_nodes, ntok, npar, ndep);
+        for (int i = 0; i < M; i++) {
+            hpos[i] = n + ndep[i];
+            for (int j = 0; j < M; j++) mask[(size_t)i * M + j] = 0;
+            for (int j = i; j >= 0; j = npar[j]) mask[(size_t)i * M + j] = 1;
+        }
+        FL_MED_CUDA(cudaMemcpyAsync(mtok, ntok.data(), sizeof(int) * M, cudaMemcpyHostToDevice, s));
+        FL_MED_CUDA(cudaMemcpyAsync(mpos, hpos.data(), sizeof(int) * M, cudaMemcpyHostToDevice, s));
+        FL_MED_CUDA(cudaMemcpyAsync(e->mask, mask.data(), (size_t)M * M, cudaMemcpyHostToDevice, s));
+        // tree-masked verify: node i at slot n + i, rotary position n + depth
+        FL_MED_CUDA(launch_embed_rows(e->embed, V, mtok, nullptr, 0, e->x, d, M, nullptr, nullptr, s, false));
+        FL_MED(run_stack(e, e->base, e->x, M, nullptr, e->iota + n, mpos, e->mask, nullptr, false));
+        for (int r0 = 0; r0 < M; r0 += kMaxRows) {
+            const int m = std::min(kMaxRows, M - r0);
+            FL_MED(run_lm(e, e->x + (size_t)r0 * d, m, nullptr, nullptr, false));
+            FL_MED_CUDA(launch_argmax_rows(e->amax, e->nparts, m, mtarget + r0, nullptr, s));
+        }
+        FL_MED_CUDA(cudaMemcpyAsync(target.data(), mtarget, sizeof(int) * M, cudaMemcpyDeviceToHost, s));
+        FL_MED_CUDA(cudaStreamSynchronize(s));
+        // longest path of the base model's greedy choices
+        path.assign(1, 0);
+        int cur = 0;
+        for (;;) {
+            int nxt = -1;
+            for (int c2 = 1; c2 < M; c2++)
+                if (npar[c2] == cur && ntok[c2] == target[cur]) {
+                    nxt = c2;
+                    break;
+                }
+            if (nxt < 0) break;
+            path.push_back(nxt);
+            cur = nxt;
+        }
+        const int a = (int)path.size() - 1;
+        if (acc_hist) acc_hist[steps] = a;
+        steps++;
+        for (int j = 1; j <= a + 1 && produced < n_new; j++) out[produced++] = j <= a ? ntok[path[j]] : target[cur];
+        if (a > 0) {
+            FL_MED_CUDA(cudaMemcpyAsync(mpath, path.data(), sizeof(int) * (a + 1), cudaMemcpyHostToDevice, s));
+            FL_MED_CUDA(launch_kv_compact(dkv, e->base.nl, e->base.block_table, e->Hkv, e->hd, e->iota + n, mpath, a, s));
+        }
+        FL_MED_CUDA(cudaMemcpyAsync(mf, e->x + (size_t)cur * d, sizeof(float) * d, cudaMemcpyDeviceToDevice, s));
+        cur_tok = target[cur];
+        n += a + 1;
+    }
+    FL_MED_CUDA(cudaEventRecord(e->ev[1], s));
+    FL_MED_CUDA(cudaEventSynchronize(e->ev[1]));
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, e->ev[0], e->ev[1]);
+    e->t_total_us = ms * 1000.0;
+    if (steps_out) *steps_out = steps;
+#undef FL_MED_CUDA
+#undef FL_MED
+    cleanup();
+    if (take_device_error() != 0) return set_error(FL_E_TIMEOUT, "medusa_generate: a bounded device wait gave up");
+    return FL_OK;
+}

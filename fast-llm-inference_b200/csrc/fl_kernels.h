@@ -127,4 +127,15 @@ cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl);
 size_t attention_scratch_floats(int heads, int head_dim, int max_ctx);
 size_t attention_scratch_counters(int heads);
 
+// Medusa (medusa_ops.cu): h = RMSNorm(x), z_i = h + SiLU(y_i) for H rows of
+// y (h written when h != nullptr); per-row top-k (k[row] <= kmax <= 32)
+// with softmax probabilities; in-place compaction of an accepted tree path
+// (slot base + j <- slot base + src[j], j = 1 .. a) over every layer.
+cudaError_t launch_medusa_z(const float* x, const float* y, float* h, float* z, int d, int H, float eps,
+                            cudaStream_t s);
+cudaError_t launch_topk_rows(const float* logits, int rows, int V, int ld, const int* k, int kmax, int* tok,
+                             float* prob, cudaStream_t s);
+cudaError_t launch_kv_compact(const KvLayer* layers, int n_layers, const int* block_table, int kv_heads, int head_dim,
+                              const int* base, const int* src, int a, cudaStream_t s);
+
 }  // namespace fl

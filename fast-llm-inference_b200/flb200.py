@@ -54,6 +54,11 @@ class ModelConfig(C.Structure):
     ]
 
 
+class MedusaConfig(C.Structure):
+    """medusa_config_t"""
+    _fields_ = [("num_heads", C.c_int), ("top_k", C.c_int), ("temperature", C.c_float)]
+
+
 class SpecConfig(C.Structure):
     """speculative_config_t (include/speculative.h)."""
     _fields_ = [("num_draft_tokens", C.c_int), ("temperature", C.c_float), ("max_accepted", C.c_int)]
@@ -122,6 +127,7 @@ _SIGS = {
     "fl_engine_step_kernel": (I, [VP]),
     "fl_engine_step_trace": (I, [VP, VP, VP, I]),
     "fl_engine_step_trace_stages": (I, [VP, VP]),
+    "fl_engine_medusa_generate": (I, [VP, VP, I, I, VP, I, I, VP, VP, VP]),
     "fl_engine_draft_bound": (I, [VP, VP]),
     "fl_engine_note_draft": (None, [VP, VP]),
     "fl_engine_bench_linear": (I, [VP, I, I, I, I, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
@@ -144,6 +150,11 @@ _SIGS = {
     "draft_kv_cache_free": (None, [C.POINTER(DraftKV)]),
     "verify_tokens": (I, [VP, C.POINTER(DraftTree), VP, C.POINTER(I), C.POINTER(SpecConfig)]),
     "speculative_generate": (I, [C.POINTER(DraftModel), VP, VP, VP, I, VP, I, C.POINTER(SpecConfig)]),
+    "medusa_model_create": (VP, [I, I, I]),
+    "medusa_model_load": (I, [VP, C.c_char_p]),
+    "medusa_model_free": (None, [VP]),
+    "medusa_generate": (I, [VP, VP, VP, VP, I, VP, I, C.POINTER(MedusaConfig)]),
+    "fl_medusa_set_tree": (I, [VP, VP, I, I]),
 }
 
 
@@ -340,6 +351,17 @@ class Engine:
         if n < 0:
             self.lib.check(n, "step_trace")
         return t[:n], d[:n]
+
+    def medusa_generate(self, prompt, n_new, topk, max_nodes):
+        """Medusa greedy decoding: (tokens, accepted count per step)."""
+        p = np.ascontiguousarray(prompt, np.int32)
+        tk = np.ascontiguousarray(topk, np.int32)
+        o = np.empty(n_new, np.int32)
+        acc = np.zeros(n_new + 1, np.int32)
+        steps = C.c_int(0)
+        self.lib.check(self.lib.fl_engine_medusa_generate(self.h, ptr(p), len(p), n_new, ptr(tk), len(tk), max_nodes,
+                                                          ptr(o), ptr(acc), C.byref(steps)), "medusa_generate")
+        return o, acc[: steps.value]
 
     def step_trace_stages(self):
         """[64, 4] uint64 stage stamps of the phase FL_STEP_TRACE_PHASE names."""

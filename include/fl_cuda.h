@@ -225,6 +225,16 @@ int fl_engine_step_trace(const fl_engine_t* e, unsigned long long* t, int* desc,
  * slot, producer issues the copy (%globaltimer ns), 64 stages; 512 words.
  * Returns 64, or 0 when not tracing. */
 int fl_engine_step_trace_stages(const fl_engine_t* e, unsigned long long* t);
+
+/* Medusa greedy decoding on the device (include/medusa.h rule): prefill P
+ * prompt ids, then steps of: heads (residual block + shared LM head) on the
+ * last hidden state, per-head top-k (topk[h] <= 32 for h < H <= 8 heads),
+ * candidate tree of at most max_nodes nodes (<= 256), one tree-masked base
+ * pass, longest accepted path, KV compaction. Writes n_new tokens (the first
+ * from the prefill) and the accepted count of each step. The engine needs
+ * H <= medusa_heads loaded heads and P + n_new + max_nodes + 2 <= max_seq_len. */
+int fl_engine_medusa_generate(fl_engine_t* e, const int* prompt, int P, int n_new, const int* topk, int H,
+                              int max_nodes, int* out, int* acc_hist, int* steps);
 /* 1 when `draft` (a draft_model_t*) is the draft whose weights the engine
  * holds; fl_engine_note_draft records it after a load. */
 int fl_engine_draft_bound(const fl_engine_t* e, const void* draft);

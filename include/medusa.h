@@ -17,7 +17,7 @@
  *
  * Candidate tree: the root is the base model's next token; level L+1 holds
  * the children proposed by head L for every level-L node. Each head keeps its
- * top-k tokens (k per level from fl_medusa_set_topk, default config->top_k),
+ * top-k tokens (k per level from fl_medusa_set_tree, default config->top_k),
  * a node's score is the product of its ancestors' softmax probabilities, and
  * the tree is pruned to the max_candidates highest-scoring nodes (ties:
  * shallower first, then lower head rank); a child never outscores its
@@ -87,41 +87,40 @@ void medusa_model_free(medusa_model_t* model);
 medusa_tree_t* medusa_tree_create(int max_candidates);
 void medusa_tree_free(medusa_tree_t* tree);
 
-/* Runs every head on hidden_state (host [hidden_size], the base feature F
- * before the final norm) and builds the candidate tree rooted at
- * current_token. The Medusa model must be bound to a base model
- * (fl_engine_bind_medusa). Returns tree->num_candidates or -1. */
+/* The step-level entry points below are not provided by this library yet:
+ * they return -1 and record the reason (fl_cuda_last_error). medusa_generate
+ * runs the whole loop -- heads, tree, verification, acceptance, KV
+ * compaction -- on the device. */
 int medusa_predict(medusa_model_t* model, const float* hidden_state,
                    int current_token, medusa_tree_t* tree,
                    const medusa_config_t* config);
-
-/* Same as medusa_predict with the root token taken from tree->tokens[0]. */
 int medusa_build_tree(medusa_model_t* model, const float* hidden_state,
                       medusa_tree_t* tree, const medusa_config_t* config);
-
-/* Verifies the tree with one tree-masked base-model pass. base_model must be
- * an fl_engine_t* and base_forward fl_cuda_base_forward. Writes the accepted
- * tokens plus the base model's next token to accepted_tokens, the accepted
- * count (excluding that last token) to *num_accepted, and returns it. */
 int medusa_verify_tree(void* base_model,
                        void (*base_forward)(void*, const int*, int, float*, int),
                        const medusa_tree_t* tree, int* accepted_tokens,
                        int* num_accepted, const medusa_config_t* config);
-
-/* One predict + verify + accept step. Returns tokens produced (>= 1). */
 int medusa_decode_step(void* base_model,
                        void (*base_forward)(void*, const int*, int, float*, int),
                        medusa_model_t* medusa, const float* current_hidden,
                        int current_token, int* output_tokens, int* num_output,
                        const medusa_config_t* config);
 
-/* Prefill prompt_len float-encoded token ids, then Medusa steps until
+/* base_model: an fl_engine_t* created with medusa_heads >= the heads used;
+ * base_forward: fl_cuda_base_forward. Greedy acceptance only (temperature
+ * <= 0). The heads' weights are loaded into the engine on the first call.
+ * Prefill prompt_len float-encoded token ids, then Medusa steps until
  * num_tokens new tokens exist. Returns the count written or -1. */
 int medusa_generate(void* base_model,
                     void (*base_forward)(void*, const int*, int, float*, int),
                     medusa_model_t* medusa, const float* prompt_hidden,
                     int prompt_len, int* output_tokens, int num_tokens,
                     const medusa_config_t* config);
+
+/* This library: per-model tree settings used by medusa_generate (no
+ * counterpart in the reference): top-k of head h = topk[h] (h < n; default
+ * config->top_k), at most max_nodes tree nodes (default 64). */
+int fl_medusa_set_tree(medusa_model_t* model, const int* topk, int n, int max_nodes);
 
 /* Draft + Medusa combination (reference medusa.h:210). Not provided by this
  * library: returns -1 and records the reason. */

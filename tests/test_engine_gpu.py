@@ -202,3 +202,67 @@ def test_phi3_mini_full_size_spec(gpu, orc):
     want, acc_want, margins = om.spec(p, 16, 4)
     assert_stream_matches(got, want, margins)
     eng.close()
+
+
+MEDUSA_TOPK = [10, 5, 3, 2]
+
+
+def test_medusa_stream_matches_oracle(gpu, orc):
+    """Medusa on the device (heads, top-k, tree, tree-masked verify, path
+    acceptance, KV compaction) against the oracle; 16-token vocabulary so
+    that multi-node paths are accepted and compacted."""
+    dims = dict(SMALL, vocab=16)
+    w, embed = make_weights(gpu, dims, seed=3, draft_layers=0, medusa_heads=4)
+    eng = flb200.Engine(gpu, engine_cfg(dims, draft_layers=0, medusa_heads=4, max_seq_len=256))
+    load_engine(eng, w, embed)
+    p = prompt(4, 12, dims["vocab"])
+    got, acc = eng.medusa_generate(p, 48, MEDUSA_TOPK, 64)
+    eng.close()
+    om = oracle_model(orc, dims, w, embed, draft_layers=0, n_medusa=4)
+    want, acc_want, margins = om.medusa(p, 48, MEDUSA_TOPK, 64)
+    assert_stream_matches(got, want, margins)
+    assert acc.max() >= 2, f"no multi-node path accepted: {acc.tolist()}"
+    g_want, _ = om.greedy(p, 48)
+    assert np.array_equal(want, g_want)
+
+
+def test_medusa_phi3_mini_shapes(gpu, orc):
+    """Config-2 shapes: Phi-3-mini base, 4 heads of 3072 x 3072, top-k
+    10/5/3/2, 64-node tree; the first 8 tokens after a 64-token prompt."""
+    dims = dict(vocab=32064, d=3072, ffn=8192, layers=32, heads=32, kv_heads=32, head_dim=96, theta=10000.0,
+                eps=1e-5)
+    w, embed = make_weights(gpu, dims, seed=1, draft_layers=0, medusa_heads=4)
+    eng = flb200.Engine(gpu, engine_cfg(dims, draft_layers=0, medusa_heads=4, max_seq_len=256))
+    load_engine(eng, w, embed)
+    p = prompt(2025, 64, dims["vocab"])
+    got, acc = eng.medusa_generate(p, 8, MEDUSA_TOPK, 64)
+    eng.close()
+    om = oracle_model(orc, dims, w, embed, draft_layers=0, n_medusa=4)
+    want, _, margins = om.medusa(p, 8, MEDUSA_TOPK, 64)
+    assert_stream_matches(got, want, margins)
+
+
+def test_medusa_generate_reference_api(gpu, orc):
+    """medusa_generate() through the reference signature: heads from
+    medusa_model_load("synthetic:SEED"), base = the engine with
+    fl_cuda_base_forward, per-head top-k from fl_medusa_set_tree."""
+    import ctypes as C
+    dims = dict(SMALL, vocab=16)
+    w, embed = make_weights(gpu, dims, seed=3, draft_layers=0, medusa_heads=4)
+    eng = flb200.Engine(gpu, engine_cfg(dims, draft_layers=0, medusa_heads=4, max_seq_len=256))
+    load_engine(eng, {k: v for k, v in w.items() if k[0] != 2}, embed)
+    mm = gpu.medusa_model_create(4, dims["d"], dims["vocab"])
+    assert gpu.medusa_model_load(mm, b"synthetic:3") == 0
+    tk = np.array(MEDUSA_TOPK, np.int32)
+    assert gpu.fl_medusa_set_tree(mm, flb200.ptr(tk), 4, 64) == 0
+    cfg = flb200.MedusaConfig(4, 10, 0.0)
+    p = prompt(4, 12, dims["vocab"])
+    ph = p.astype(np.float32)
+    out = np.empty(48, np.int32)
+    n = gpu.medusa_generate(eng.h, C.cast(gpu.so.fl_cuda_base_forward, C.c_void_p), mm, flb200.ptr(ph), len(p),
+                            flb200.ptr(out), 48, C.byref(cfg))
+    assert n == 48, gpu.err()
+    gpu.medusa_model_free(mm)
+    eng.close()
+    want, _, margins = oracle_model(orc, dims, w, embed, draft_layers=0, n_medusa=4).medusa(p, 48, MEDUSA_TOPK, 64)
+    assert_stream_matches(out, want, margins)
