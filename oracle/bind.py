@@ -73,6 +73,14 @@ class Oracle:
         s.orc_kv_free.argtypes = [C.POINTER(KV)]
         s.orc_spec_generate.argtypes = [C.POINTER(Model), VP, I, I, I, I, VP, VP, VP]
         s.orc_greedy_generate.argtypes = [C.POINTER(Model), VP, I, I, VP, VP]
+        s.orc_philox_uniform.restype = C.c_float
+        s.orc_philox_uniform.argtypes = [C.c_uint32] * 5
+        s.orc_sample_dist.argtypes = [VP, I, C.c_float, C.c_float, VP]
+        s.orc_sample_index.restype = I
+        s.orc_sample_index.argtypes = [VP, I, C.c_float]
+        s.orc_spec_generate_sampled.restype = I
+        s.orc_spec_generate_sampled.argtypes = [C.POINTER(Model), VP, I, I, I, C.c_float, C.c_float, C.c_uint32,
+                                                C.c_uint32, VP, VP]
         s.orc_medusa_generate.restype = I
         s.orc_medusa_generate.argtypes = [C.POINTER(Model), VP, I, VP, I, I, VP, VP, VP]
         s.orc_medusa_tree.restype = I
@@ -155,6 +163,16 @@ class Oracle:
         d = np.empty(x.size // 32, np.uint16)
         self.so.orc_q4_0_quantize_i8(_p(x), x.size, _p(w), _p(d))
         return w, d
+
+    def sample_dist(self, logits, T, top_p):
+        lg = np.ascontiguousarray(logits, np.float32)
+        q = np.empty_like(lg)
+        self.so.orc_sample_dist(_p(lg), lg.size, T, top_p, _p(q))
+        return q
+
+    def sample_index(self, w, u):
+        w = np.ascontiguousarray(w, np.float32)
+        return self.so.orc_sample_index(_p(w), w.size, u)
 
     def philox(self, ctr, key):
         c = np.asarray(ctr, np.uint32)
@@ -247,6 +265,15 @@ class OracleModel:
                                               n_new, _p(o), _p(acc), _p(mg))
         return o, acc[:steps], mg
 
+
+    def spec_sampled(self, prompt, n_new, k, T, top_p, seed, seq_id=0):
+        """Stochastic speculative decoding: (tokens, accepted per step)."""
+        p = np.ascontiguousarray(prompt, np.int32)
+        o = np.empty(n_new, np.int32)
+        acc = np.zeros(n_new + 1, np.int32)
+        steps = self.orc.so.orc_spec_generate_sampled(C.byref(self.m), _p(p), len(p), k, n_new, T, top_p, seed,
+                                                      seq_id, _p(o), _p(acc))
+        return o, acc[:steps]
 
     def medusa(self, prompt, n_new, topk, max_nodes):
         """Medusa greedy decoding: (tokens, accepted per step, margins)."""

@@ -768,3 +768,171 @@ int orc_medusa_generate(const orc_model_t* mdl, const int* prompt, int P, const 
     orc_kv_free(&kv);
     return steps;
 }
+
+/* ------------------------------------------------------------------ */
+/* Stochastic speculative decoding (include/speculative.h rule for     */
+/* temperature > 0; the reference declares the contract without code)  */
+/* ------------------------------------------------------------------ */
+
+/* Uniform in [0, 1) from 24 bits of Philox4x32-10 with key (seed, 0) and
+ * counter (sequence, step, position, purpose). */
+float orc_philox_uniform(uint32_t seed, uint32_t seq, uint32_t step, uint32_t pos, uint32_t purpose) {
+    const uint32_t ctr[4] = {seq, step, pos, purpose};
+    const uint32_t key[2] = {seed, 0u};
+    uint32_t o[4];
+    orc_philox4x32_10(ctr, key, o);
+    return (float)(o[0] >> 8) * (1.0f / 16777216.0f);
+}
+
+/* p[i] = softmax(l / T)[i]; the nucleus is {i : p[i] >= tau} with tau the
+ * largest float whose mass S(tau) = sum_{p_i >= tau} p_i (index order)
+ * reaches top_p (bisection over the float bit patterns); q[i] = p[i] / S(tau)
+ * inside the nucleus, 0 outside. */
+void orc_sample_dist(const float* l, int V, float T, float top_p, float* q) {
+    float mx = l[0];
+    for (int i = 1; i < V; i++) if (l[i] > mx) mx = l[i];
+    float z = 0.0f;
+    for (int i = 0; i < V; i++) { q[i] = expf((l[i] - mx) / T); z += q[i]; }
+    for (int i = 0; i < V; i++) q[i] = q[i] / z;
+    /* largest bit pattern b with S(as_float(b)) >= top_p; S(0) = sum(p) ~ 1 */
+    uint32_t lo = 0u, hi = 0x3F800001u;  /* S(lo) >= top_p, S(hi) < top_p */
+    while (hi - lo > 1u) {
+        const uint32_t mid = lo + (hi - lo) / 2u;
+        float t;
+        memcpy(&t, &mid, 4);
+        float s = 0.0f;
+        for (int i = 0; i < V; i++) if (q[i] >= t) s += q[i];
+        if (s >= top_p) lo = mid; else hi = mid;
+    }
+    float tau;
+    memcpy(&tau, &lo, 4);
+    float s = 0.0f;
+    for (int i = 0; i < V; i++) if (q[i] >= tau) s += q[i];
+    for (int i = 0; i < V; i++) q[i] = q[i] >= tau ? q[i] / s : 0.0f;
+}
+
+/* Inverse CDF in index order: the first i whose running sum of w exceeds
+ * u * sum(w); the last i with w[i] > 0 if rounding leaves none. */
+int orc_sample_index(const float* w, int V, float u) {
+    float z = 0.0f;
+    for (int i = 0; i < V; i++) z += w[i];
+    const float tgt = u * z;
+    float c = 0.0f;
+    int last = 0;
+    for (int i = 0; i < V; i++) {
+        if (w[i] <= 0.0f) continue;
+        c += w[i];
+        last = i;
+        if (tgt < c) return i;
+    }
+    return last;
+}
+
+int orc_spec_generate_sampled(const orc_model_t* mdl, const int* prompt, int P, int K, int n_new, float T,
+                              float top_p, uint32_t seed, uint32_t seq_id, int* out, int* acc_hist) {
+    const orc_dims_t* D = &mdl->dims;
+    const int d = D->d, V = D->vocab;
+    const int cap = P + n_new + K + 2;
+    orc_kv_t kvb, kvd;
+    orc_kv_init(&kvb, D->layers, cap, D->kv_heads, D->head_dim);
+    orc_kv_init(&kvd, mdl->draft_layers, cap, D->kv_heads, D->head_dim);
+    int* seq = (int*)malloc(sizeof(int) * (size_t)(cap + 1));
+    const int rows_max = (P + 1 > K + 1) ? P + 1 : K + 1;
+    float* x = (float*)malloc(sizeof(float) * (size_t)rows_max * d);
+    float* feat = (float*)malloc(sizeof(float) * (size_t)rows_max * d);
+    float* lg = (float*)malloc(sizeof(float) * (size_t)(K + 1) * V);
+    float* qd = (float*)malloc(sizeof(float) * (size_t)K * V);       /* draft distributions */
+    float* pt = (float*)malloc(sizeof(float) * (size_t)(K + 1) * V); /* target distributions */
+    float* r = (float*)malloc(sizeof(float) * V);
+    int* pos = (int*)malloc(sizeof(int) * rows_max);
+    int* drafted = (int*)malloc(sizeof(int) * (K + 1));
+    float* g = (float*)malloc(sizeof(float) * d);
+
+    for (int i = 0; i < P; i++) seq[i] = tok_or_zero(prompt[i], V);
+    for (int i = 0; i < P; i++) {
+        memcpy(x + (size_t)i * d, mdl->embed + (size_t)seq[i] * d, sizeof(float) * d);
+        pos[i] = i;
+    }
+    orc_stack_forward(mdl, mdl->base, D->layers, &kvb, x, P, 0, pos, NULL);
+    memset(feat, 0, sizeof(float) * d);
+    memcpy(feat + d, x, sizeof(float) * (size_t)(P - 1) * d);
+    memcpy(g, x + (size_t)(P - 1) * d, sizeof(float) * d);
+    orc_lm_logits(mdl, g, lg, 1);
+    orc_sample_dist(lg, V, T, top_p, r);
+    int n = P;
+    seq[n] = orc_sample_index(r, V, orc_philox_uniform(seed, seq_id, 0xFFFFFFFFu, (uint32_t)n, 2u));
+    int produced = 0;
+    out[produced++] = seq[n];
+    memcpy(feat + (size_t)P * d, g, sizeof(float) * d);
+    int m = 0, steps = 0;
+    const double t0 = now_s();
+    while (produced < n_new) {
+        /* draft catch-up rows m..n, then K sampled draft tokens */
+        int R = n - m + 1;
+        for (int rr = 0; rr < R; rr++) {
+            const float* e = mdl->embed + (size_t)seq[m + rr] * d;
+            for (int i = 0; i < d; i++) x[(size_t)rr * d + i] = feat[(size_t)rr * d + i] + e[i];
+            pos[rr] = m + rr;
+        }
+        orc_stack_forward(mdl, mdl->draft, mdl->draft_layers, &kvd, x, R, m, pos, NULL);
+        memcpy(g, x + (size_t)(R - 1) * d, sizeof(float) * d);
+        for (int j = 0; j < K; j++) {
+            if (j > 0) {
+                int p = n + j;
+                const float* e = mdl->embed + (size_t)drafted[j - 1] * d;
+                for (int i = 0; i < d; i++) x[i] = g[i] + e[i];
+                orc_stack_forward(mdl, mdl->draft, mdl->draft_layers, &kvd, x, 1, p, &p, NULL);
+                memcpy(g, x, sizeof(float) * d);
+            }
+            orc_lm_logits(mdl, g, lg, 1);
+            orc_sample_dist(lg, V, T, top_p, qd + (size_t)j * V);
+            drafted[j] = orc_sample_index(qd + (size_t)j * V, V,
+                                          orc_philox_uniform(seed, seq_id, (uint32_t)steps, (uint32_t)(n + 1 + j), 0u));
+        }
+        m = n + 1;
+        /* verify rows n..n+K */
+        for (int rr = 0; rr <= K; rr++) {
+            int t = rr == 0 ? seq[n] : drafted[rr - 1];
+            memcpy(x + (size_t)rr * d, mdl->embed + (size_t)t * d, sizeof(float) * d);
+            pos[rr] = n + rr;
+        }
+        orc_stack_forward(mdl, mdl->base, D->layers, &kvb, x, K + 1, n, pos, NULL);
+        orc_lm_logits(mdl, x, lg, K + 1);
+        for (int rr = 0; rr <= K; rr++) orc_sample_dist(lg + (size_t)rr * V, V, T, top_p, pt + (size_t)rr * V);
+        /* rejection sampling (accept with probability min(1, p / q)) */
+        int a = 0, last;
+        for (;;) {
+            if (a == K) {
+                last = orc_sample_index(pt + (size_t)K * V, V,
+                                        orc_philox_uniform(seed, seq_id, (uint32_t)steps, (uint32_t)(n + 1 + K), 2u));
+                break;
+            }
+            const int xt = drafted[a];
+            const float pq = pt[(size_t)a * V + xt] / qd[(size_t)a * V + xt];
+            const float u = orc_philox_uniform(seed, seq_id, (uint32_t)steps, (uint32_t)(n + 1 + a), 1u);
+            if (u < pq) { a++; continue; }
+            float zr = 0.0f;
+            for (int i = 0; i < V; i++) {
+                r[i] = fmaxf(0.0f, pt[(size_t)a * V + i] - qd[(size_t)a * V + i]);
+                zr += r[i];
+            }
+            const float ur = orc_philox_uniform(seed, seq_id, (uint32_t)steps, (uint32_t)(n + 1 + a), 2u);
+            last = zr > 0.0f ? orc_sample_index(r, V, ur) : orc_sample_index(pt + (size_t)a * V, V, ur);
+            break;
+        }
+        if (acc_hist) acc_hist[steps] = a;
+        steps++;
+        for (int j = 0; j <= a; j++) {
+            int t = j < a ? drafted[j] : last;
+            seq[n + 1 + j] = t;
+            if (produced < n_new) out[produced++] = t;
+        }
+        memcpy(feat, x, sizeof(float) * (size_t)(a + 1) * d);
+        n = n + a + 1;
+    }
+    g_last_decode_s = now_s() - t0;
+    free(seq); free(x); free(feat); free(lg); free(qd); free(pt); free(r); free(pos); free(drafted); free(g);
+    orc_kv_free(&kvb);
+    orc_kv_free(&kvd);
+    return steps;
+}

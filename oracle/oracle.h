@@ -171,6 +171,21 @@ int orc_medusa_tree(int root_tok, int n_heads, const int* topk, const int* tok,
                     const float* prob, int kmax, int max_nodes, int* out_tok,
                     int* out_parent, int* out_depth, float* out_score);
 
+/* Stochastic speculative decoding (temperature T > 0, top-p nucleus):
+ * Philox4x32-10 uniforms keyed by (seed, 0), counter (sequence, step,
+ * position, purpose: 0 draft sample, 1 acceptance test, 2 resample / bonus;
+ * the first token after the prefill uses step 0xFFFFFFFF). */
+float orc_philox_uniform(uint32_t seed, uint32_t seq, uint32_t step, uint32_t pos, uint32_t purpose);
+/* q = the nucleus-filtered, renormalised softmax(l / T) (see oracle.c). */
+void orc_sample_dist(const float* l, int V, float T, float top_p, float* q);
+/* Inverse CDF of weights w (index order) at u in [0, 1). */
+int orc_sample_index(const float* w, int V, float u);
+/* Draft tokens sampled from the draft distribution, accepted with
+ * probability min(1, p / q), rejection resampled from norm(max(0, p - q)),
+ * bonus from p when all K are accepted. Returns steps. */
+int orc_spec_generate_sampled(const orc_model_t* mdl, const int* prompt, int prompt_len, int K, int n_new,
+                              float T, float top_p, uint32_t seed, uint32_t seq_id, int* out, int* acc_hist);
+
 #ifdef __cplusplus
 }
 #endif
