@@ -261,7 +261,7 @@ FL_API int verify_tokens(const float* target_hidden, const draft_tree_t* tree, i
     }
     if (config->temperature > 0.0f) {
         set_error(FL_E_UNSUPPORTED, "verify_tokens: host rejection sampling needs the draft distributions; "
-                                    "use the engine's sampled decode");
+                                    "use speculative_generate (or fl_engine_set_sampling)");
         return -1;
     }
     const int K = tree->num_tokens;
@@ -357,12 +357,16 @@ FL_API int speculative_generate(draft_model_t* draft, void* target_model,
         set_error(FL_E_UNSUPPORTED, "speculative_generate: target_forward must be fl_cuda_target_forward");
         return -1;
     }
-    if (config->temperature > 0.0f) {
-        set_error(FL_E_UNSUPPORTED, "speculative_generate: sampled acceptance runs through fl_engine_spec_sample");
-        return -1;
-    }
     fl_engine_t* e = (fl_engine_t*)target_model;
     if (fl_engine_bind_draft(e, draft) != FL_OK) return -1;
+    // temperature > 0: rejection sampling with the engine's top_p and Philox
+    // key (fl_engine_set_sampling); otherwise greedy
+    float t0 = 0.0f, top_p = 1.0f;
+    unsigned seed = 0, seq_id = 0;
+    if (fl_engine_get_sampling(e, &t0, &top_p, &seed, &seq_id) != FL_OK ||
+        fl_engine_set_sampling(e, config->temperature > 0.0f ? config->temperature : 0.0f, top_p, seed, seq_id) !=
+            FL_OK)
+        return -1;
     std::vector<int> prompt(prompt_len);
     for (int i = 0; i < prompt_len; i++) prompt[i] = (int)prompt_hidden[i];
     const int K = config->num_draft_tokens;

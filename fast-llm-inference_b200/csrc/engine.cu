@@ -105,6 +105,20 @@ struct fl_engine {
     int graph_kernels = 0;        // kernel nodes in the step graph
     long long last_launches = 0;  // kernels launched by the last decode
     const void* bound_draft = nullptr;
+    // stochastic speculative decoding (temperature > 0); set by
+    // fl_engine_set_sampling, used by the next fl_engine_spec_prefill
+    bool samp = false;
+    float samp_T = 0.0f, samp_top_p = 1.0f;
+    uint32_t samp_seed = 0, samp_seq = 0;
+    uint32_t* samp_q = nullptr;            // [kMaxDraft, V] draft nucleus weights
+    uint32_t* samp_p = nullptr;            // [kMaxRows, V] target nucleus weights
+    unsigned long long* samp_m = nullptr;  // [kMaxDraft + kMaxRows] kept masses (draft, then target)
+    unsigned long long* samp_r = nullptr;  // [V] rejection residual weights
+    // post-prefill draft state of step 0: its mass, weights and traced logits
+    // (8 + 4V + 4V bytes)
+    unsigned char* samp_snap = nullptr;
+    float* samp_trace = nullptr;  // [2 * kMaxRows, V] logits behind each draw (trace on)
+    bool trace_on = false;
 };
 
 namespace {
@@ -355,6 +369,18 @@ StepBuffers step_buffers(fl_engine* e) {
     b.amax_part = e->amax;
     b.nparts = e->nparts;
     b.d = e->d;
+    b.logits = e->logits;
+    b.V = e->V;
+    b.temp = e->samp_T;
+    b.top_p = e->samp_top_p;
+    b.seed = e->samp_seed;
+    b.seq_id = e->samp_seq;
+    b.qd = e->samp_q;
+    b.qm = e->samp_m;
+    b.pt = e->samp_p;
+    b.pm = e->samp_m ? e->samp_m + kMaxDraft : nullptr;
+    b.resid = e->samp_r;
+    b.trace = e->trace_on ? e->samp_trace : nullptr;
     return b;
 }
 
@@ -372,19 +398,29 @@ int record_step(fl_engine* e, bool pdl) {
     SpecState* st = e->st;
     const int* done = &st->done;
     StepBuffers b = step_buffers(e);
+    // greedy: argmax picks and exact-match acceptance; sampling: nucleus
+    // draws and rejection-sampling acceptance
+    auto pick = [&](int j) {
+        return e->samp ? launch_sample_pick(b, j, e->s, pdl) : launch_draft_pick(b, j, e->s, pdl);
+    };
     for (int j = 1; j < K; j++) {
         FL_CHECK(run_stack(e, e->draft, e->x_d, 1, nullptr, &st->draft_base, st->draft_pos, nullptr, done, pdl));
         FL_CHECK(run_lm(e, e->x_d, 1, nullptr, done, pdl));
-        FL_CHECK_CUDA(launch_draft_pick(b, j, e->s, pdl));
+        FL_CHECK_CUDA(pick(j));
     }
     FL_CHECK_CUDA(launch_verify_prep(b, K, e->s, pdl));
     FL_CHECK(run_stack(e, e->base, e->x_v, K + 1, nullptr, &st->verify_base, st->verify_pos, nullptr, done, pdl));
     FL_CHECK(run_lm(e, e->x_v, K + 1, nullptr, done, pdl));
-    FL_CHECK_CUDA(launch_accept(b, K, e->s, pdl));
+    if (e->samp) {
+        FL_CHECK_CUDA(launch_target_dist(b, K, e->s, pdl));
+        FL_CHECK_CUDA(launch_accept_sampled(b, K, e->s, pdl));
+    } else {
+        FL_CHECK_CUDA(launch_accept(b, K, e->s, pdl));
+    }
     FL_CHECK_CUDA(launch_catchup_prep(b, K, e->s, pdl));
     FL_CHECK(run_stack(e, e->draft, e->x_d, K + 1, &st->rows, &st->draft_base, st->draft_pos, nullptr, done, pdl));
     FL_CHECK(run_lm(e, e->x_d, 1, &st->last_row, done, pdl));
-    FL_CHECK_CUDA(launch_draft_pick(b, 0, e->s, pdl));
+    FL_CHECK_CUDA(pick(0));
     return FL_OK;
 }
 
@@ -560,7 +596,8 @@ int build_step_graph(fl_engine* e) {
     const char* dis = getenv("FL_DISABLE_STEP_KERNEL");
     StepParams sp;
     size_t smem = 0;
-    int prc = (dis && dis[0] == '1') ? FL_E_UNSUPPORTED : prepare_step_kernel(e, sp, smem);
+    // the one-kernel step implements the greedy rule only
+    int prc = ((dis && dis[0] == '1') || e->samp) ? FL_E_UNSUPPORTED : prepare_step_kernel(e, sp, smem);
     if (prc != FL_OK && prc != FL_E_UNSUPPORTED) return prc;
     cudaGraph_t g = nullptr;
     int rc = FL_E_UNSUPPORTED;
@@ -716,7 +753,8 @@ FL_API void fl_engine_destroy(fl_engine_t* e) {
     for (auto& m : e->medusa) free_linear(m);
     void* bufs[] = {e->embed, e->x, e->x2, e->xq, e->q, e->aq, e->hq, e->logits, e->amax, e->x_v, e->x_d,
                     e->iota, e->tok, e->mask, e->st, e->st_snap, e->xd0_snap, e->seq, e->out, e->acc,
-                    e->last_feat, e->attn_part, e->attn_cnt, e->step_bar, e->d_phases, e->d_trace};
+                    e->last_feat, e->attn_part, e->attn_cnt, e->step_bar, e->d_phases, e->d_trace,
+                    e->samp_q, e->samp_p, e->samp_r, e->samp_trace, e->samp_snap, e->samp_m};
     for (void* p : bufs) cudaFree(p);
     for (auto& ev : e->ev)
         if (ev) cudaEventDestroy(ev);
@@ -871,6 +909,36 @@ FL_API int fl_engine_greedy_generate(fl_engine_t* e, const int* prompt, int P, i
     return FL_OK;
 }
 
+namespace {
+// Saves (save) or restores the draft state of step 0 that the prefill leaves
+// behind: kept mass, weights and, with the trace on, the logits row.
+int sample_snapshot(fl_engine* e, bool save) {
+    const size_t V = e->V;
+    unsigned char* s = e->samp_snap;
+    struct Part { void* live; unsigned char* snap; size_t bytes; } parts[3] = {
+        {e->samp_m, s, 8}, {e->samp_q, s + 8, 4 * V}, {e->samp_trace, s + 8 + 4 * V, 4 * V}};
+    for (int i = 0; i < (e->trace_on ? 3 : 2); i++) {
+        void* dst = save ? (void*)parts[i].snap : parts[i].live;
+        const void* src = save ? (const void*)parts[i].live : (const void*)parts[i].snap;
+        FL_CHECK_CUDA(cudaMemcpyAsync(dst, src, parts[i].bytes, cudaMemcpyDeviceToDevice, e->s));
+    }
+    return FL_OK;
+}
+
+// The step graph holds the rule, its key and the trace pointer by value:
+// drop it so that the next prefill records it again.
+int drop_step_graph(fl_engine* e) {
+    e->spec_ready = 0;
+    if (e->step_exec) {
+        FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
+        cudaGraphExecDestroy(e->step_exec);
+        e->step_exec = nullptr;
+    }
+    e->graph_K = -1;
+    return FL_OK;
+}
+}  // namespace
+
 FL_API int fl_engine_spec_prefill(fl_engine_t* e, const int* prompt, int P, int K, int max_acc) {
     FL_CHECK(check_ready(e, true));
     if (!prompt || P <= 0 || K < 1 || K > kMaxDraft || P + 2 > e->R)
@@ -879,6 +947,8 @@ FL_API int fl_engine_spec_prefill(fl_engine_t* e, const int* prompt, int P, int 
     e->spec_K = K;
     e->spec_P = P;
     FL_CHECK(prefill_base(e, prompt, P));
+    // sampling: the first token is drawn from the last prompt row's logits
+    if (e->samp) FL_CHECK_CUDA(launch_sample_first(step_buffers(e), P, e->s));
     // Draft catch-up over positions 0..P: x_i = F_{i-1} + E[t_i], F_{-1} = 0.
     FL_CHECK_CUDA(launch_embed_rows(e->embed, e->V, e->seq, e->x, 1, e->x2, e->d, P + 1, nullptr, nullptr, e->s, false));
     FL_CHECK(run_stack(e, e->draft, e->x2, P + 1, nullptr, e->iota, e->iota, nullptr, nullptr, false));
@@ -896,24 +966,123 @@ FL_API int fl_engine_spec_prefill(fl_engine_t* e, const int* prompt, int P, int 
     FL_CHECK_CUDA(cudaMemcpyAsync(e->st, &h, sizeof(h), cudaMemcpyHostToDevice, e->s));
     FL_CHECK_CUDA(cudaMemcpyAsync(e->out, e->seq + P, sizeof(int), cudaMemcpyDeviceToDevice, e->s));
     FL_CHECK(run_lm(e, e->x_d, 1, nullptr, nullptr, false));
-    FL_CHECK_CUDA(launch_draft_pick(step_buffers(e), 0, e->s, false));
+    if (e->samp)
+        FL_CHECK_CUDA(launch_sample_pick(step_buffers(e), 0, e->s, false));
+    else
+        FL_CHECK_CUDA(launch_draft_pick(step_buffers(e), 0, e->s, false));
     FL_CHECK_CUDA(cudaMemcpyAsync(e->st_snap, e->st, sizeof(SpecState), cudaMemcpyDeviceToDevice, e->s));
     FL_CHECK_CUDA(cudaMemcpyAsync(e->xd0_snap, e->x_d, sizeof(float) * e->d, cudaMemcpyDeviceToDevice, e->s));
+    if (e->samp) FL_CHECK(sample_snapshot(e, true));
     FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
     FL_CHECK(build_step_graph(e));
     e->spec_ready = 1;
     return FL_OK;
 }
 
-FL_API int fl_engine_spec_decode(fl_engine_t* e, int n_new, int* out, int* acc_hist, int* steps) {
+
+FL_API int fl_engine_set_sampling(fl_engine_t* e, float temperature, float top_p, unsigned seed,
+                                  unsigned seq_id) {
+    if (!e) return set_error(FL_E_INVAL, "engine is NULL");
+    if (!(temperature <= 0.0f) && !(top_p > 0.0f && top_p <= 1.0f))
+        return set_error(FL_E_INVAL, "set_sampling: top_p must be in (0, 1]");
+    if (!(temperature <= 0.0f) && !(temperature < INFINITY))
+        return set_error(FL_E_INVAL, "set_sampling: temperature must be finite");
+    FL_CHECK_CUDA(cudaSetDevice(e->device));
+    const bool samp = temperature > 0.0f;
+    if (samp == e->samp && (!samp || (temperature == e->samp_T && top_p == e->samp_top_p &&
+                                      seed == e->samp_seed && seq_id == e->samp_seq)))
+        return FL_OK;  // unchanged: keep the recorded step graph
+    if (samp && !e->samp_q) {
+        FL_CHECK_CUDA(cudaMalloc(&e->samp_q, sizeof(uint32_t) * (size_t)kMaxDraft * e->V));
+        FL_CHECK_CUDA(cudaMalloc(&e->samp_p, sizeof(uint32_t) * (size_t)kMaxRows * e->V));
+        FL_CHECK_CUDA(cudaMalloc(&e->samp_m, sizeof(unsigned long long) * (kMaxDraft + kMaxRows)));
+        FL_CHECK_CUDA(cudaMalloc(&e->samp_r, sizeof(unsigned long long) * (size_t)e->V));
+        FL_CHECK_CUDA(cudaMalloc(&e->samp_snap, 8 + (size_t)8 * e->V));
+    }
+    e->samp = samp;
+    e->samp_T = samp ? temperature : 0.0f;
+    e->samp_top_p = samp ? top_p : 1.0f;
+    e->samp_seed = seed;
+    e->samp_seq = seq_id;
+    return drop_step_graph(e);
+}
+
+FL_API int fl_engine_sample_trace_enable(fl_engine_t* e, int on) {
+    if (!e) return set_error(FL_E_INVAL, "engine is NULL");
+    if ((on != 0) == e->trace_on) return FL_OK;
+    FL_CHECK_CUDA(cudaSetDevice(e->device));
+    if (on && !e->samp_trace)
+        FL_CHECK_CUDA(cudaMalloc(&e->samp_trace, sizeof(float) * (size_t)2 * kMaxRows * e->V));
+    e->trace_on = on != 0;
+    return drop_step_graph(e);
+}
+
+FL_API int fl_engine_sample_trace(const fl_engine_t* e, float* logits, unsigned* qd, unsigned long long* qm,
+                                  unsigned* pt, unsigned long long* pm, int* drafted) {
+    if (!e) return set_error(FL_E_INVAL, "engine is NULL");
+    if (!e->trace_on || !e->samp_q) return set_error(FL_E_STATE, "sample_trace: enable the trace and sampling first");
+    FL_CHECK_CUDA(cudaSetDevice(e->device));
+    FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
+    const size_t V = e->V;
+    if (logits) FL_CHECK_CUDA(cudaMemcpy(logits, e->samp_trace, sizeof(float) * 2 * kMaxRows * V, cudaMemcpyDeviceToHost));
+    if (qd) FL_CHECK_CUDA(cudaMemcpy(qd, e->samp_q, sizeof(uint32_t) * kMaxDraft * V, cudaMemcpyDeviceToHost));
+    if (pt) FL_CHECK_CUDA(cudaMemcpy(pt, e->samp_p, sizeof(uint32_t) * kMaxRows * V, cudaMemcpyDeviceToHost));
+    if (qm) FL_CHECK_CUDA(cudaMemcpy(qm, e->samp_m, sizeof(unsigned long long) * kMaxDraft, cudaMemcpyDeviceToHost));
+    if (pm)
+        FL_CHECK_CUDA(cudaMemcpy(pm, e->samp_m + kMaxDraft, sizeof(unsigned long long) * kMaxRows, cudaMemcpyDeviceToHost));
+    if (drafted) {
+        SpecState h;
+        FL_CHECK_CUDA(cudaMemcpy(&h, e->st, sizeof(h), cudaMemcpyDeviceToHost));
+        memcpy(drafted, h.drafted, sizeof(int) * kMaxDraft);
+    }
+    return FL_OK;
+}
+
+FL_API int fl_engine_get_sampling(const fl_engine_t* e, float* temperature, float* top_p, unsigned* seed,
+                                  unsigned* seq_id) {
+    if (!e) return set_error(FL_E_INVAL, "engine is NULL");
+    if (temperature) *temperature = e->samp_T;
+    if (top_p) *top_p = e->samp_top_p;
+    if (seed) *seed = e->samp_seed;
+    if (seq_id) *seq_id = e->samp_seq;
+    return FL_OK;
+}
+
+FL_API int fl_engine_spec_begin(fl_engine_t* e, int n_new) {
     FL_CHECK(check_ready(e, true));
     if (!e->spec_ready) return set_error(FL_E_STATE, "spec_decode: call fl_engine_spec_prefill first");
-    const int K = e->spec_K;
-    if (n_new <= 0 || e->spec_P + n_new + K + 2 > e->R) return set_error(FL_E_INVAL, "spec_decode: context too long");
+    if (n_new <= 0 || e->spec_P + n_new + e->spec_K + 2 > e->R)
+        return set_error(FL_E_INVAL, "spec_decode: context too long");
     FL_CHECK_CUDA(cudaMemcpyAsync(e->st, e->st_snap, sizeof(SpecState), cudaMemcpyDeviceToDevice, e->s));
     FL_CHECK_CUDA(cudaMemcpyAsync(e->x_d, e->xd0_snap, sizeof(float) * e->d, cudaMemcpyDeviceToDevice, e->s));
+    // the step-0 draft weights are part of the saved state
+    if (e->samp) FL_CHECK(sample_snapshot(e, false));
     const int patch[2] = {n_new, n_new <= 1 ? 1 : 0};
     FL_CHECK_CUDA(cudaMemcpyAsync(&e->st->n_new, patch, sizeof(patch), cudaMemcpyHostToDevice, e->s));
+    return FL_OK;
+}
+
+FL_API int fl_engine_spec_step(fl_engine_t* e, int* state) {
+    FL_CHECK(check_ready(e, true));
+    if (!e->spec_ready || !e->step_exec) return set_error(FL_E_STATE, "spec_step: call fl_engine_spec_begin first");
+    FL_CHECK_CUDA(cudaGraphLaunch(e->step_exec, e->s));
+    SpecState h;
+    FL_CHECK_CUDA(cudaMemcpyAsync(&h, e->st, sizeof(h), cudaMemcpyDeviceToHost, e->s));
+    FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
+    if (take_device_error() != 0) return set_error(FL_E_TIMEOUT, "spec_step: a bounded device wait gave up");
+    if (state) {
+        state[0] = h.n;
+        state[1] = h.produced;
+        state[2] = h.steps;
+        state[3] = h.a_last;
+        state[4] = h.done;
+    }
+    return FL_OK;
+}
+
+FL_API int fl_engine_spec_decode(fl_engine_t* e, int n_new, int* out, int* acc_hist, int* steps) {
+    FL_CHECK(fl_engine_spec_begin(e, n_new));
+    const int K = e->spec_K;
     FL_CHECK_CUDA(cudaEventRecord(e->ev[0], e->s));
     SpecState h = {};
     int produced = 1;

@@ -45,6 +45,21 @@ struct StepBuffers {
     const unsigned long long* amax_part;  // [rows][nparts]
     int nparts;             // partials per row (LM-head GEMV grid)
     int d;
+    // stochastic mode (temp > 0): LM-head logits rows, integer nucleus
+    // weights of the draft / target rows and their kept masses, Philox key
+    const float* logits;    // [kMaxRows, V]
+    int V;
+    float temp, top_p;
+    uint32_t seed, seq_id;
+    uint32_t* qd;           // [kMaxDraft, V] draft weights
+    unsigned long long* qm; // [kMaxDraft]
+    uint32_t* pt;           // [kMaxRows, V] target weights
+    unsigned long long* pm; // [kMaxRows]
+    unsigned long long* resid;  // [V] residual weights of a rejection
+    // optional trace (null unless enabled): logits rows behind each draw,
+    // [2 * kMaxRows, V]: draft j at row j, verify row r at kMaxDraft + r,
+    // the first token after the prefill at 2 * kMaxRows - 1
+    float* trace;
 };
 
 // x[r] = E[tok[r]] + (r >= shift ? feat[r - shift] : 0) for r < rows,
@@ -72,6 +87,14 @@ cudaError_t launch_accept(const StepBuffers& b, int K, cudaStream_t s, bool pdl)
 cudaError_t launch_catchup_prep(const StepBuffers& b, int K, cudaStream_t s, bool pdl);
 
 // out_tok[r] = argmax over the LM partials of row r, r < rows.
+// Stochastic mode (sample_ops.cu): first token after the prefill from logits
+// row 0; sampled draft pick j; nucleus distributions of the K + 1 verify rows;
+// rejection-sampling acceptance with the same state update as launch_accept.
+cudaError_t launch_sample_first(const StepBuffers& b, int P, cudaStream_t s);
+cudaError_t launch_sample_pick(const StepBuffers& b, int j, cudaStream_t s, bool pdl);
+cudaError_t launch_target_dist(const StepBuffers& b, int K, cudaStream_t s, bool pdl);
+cudaError_t launch_accept_sampled(const StepBuffers& b, int K, cudaStream_t s, bool pdl);
+
 cudaError_t launch_argmax_rows(const unsigned long long* part, int nparts, int rows, int* out_tok,
                                float* out_val, cudaStream_t s);
 

@@ -121,6 +121,12 @@ _SIGS = {
     "fl_engine_spec_generate": (I, [VP, VP, I, I, I, I, VP, VP, VP]),
     "fl_engine_spec_prefill": (I, [VP, VP, I, I, I]),
     "fl_engine_spec_decode": (I, [VP, I, VP, VP, VP]),
+    "fl_engine_set_sampling": (I, [VP, F, F, U32, U32]),
+    "fl_engine_get_sampling": (I, [VP, VP, VP, VP, VP]),
+    "fl_engine_sample_trace_enable": (I, [VP, I]),
+    "fl_engine_sample_trace": (I, [VP, VP, VP, VP, VP, VP, VP]),
+    "fl_engine_spec_begin": (I, [VP, I]),
+    "fl_engine_spec_step": (I, [VP, VP]),
     "fl_engine_last_timing": (I, [VP, VP, VP, VP]),
     "fl_engine_stream": (VP, [VP]),
     "fl_engine_last_launches": (C.c_longlong, [VP]),
@@ -326,6 +332,41 @@ class Engine:
     def spec_generate(self, prompt, n_new, k, max_acc=-1):
         self.spec_prefill(prompt, k, max_acc)
         return self.spec_decode(n_new)
+
+    def set_sampling(self, temperature, top_p=1.0, seed=0, seq_id=0):
+        """temperature <= 0: greedy; > 0: Philox-keyed rejection sampling
+        over top-p nucleus distributions (next spec_prefill onwards)."""
+        self.lib.check(self.lib.fl_engine_set_sampling(self.h, float(temperature), float(top_p), int(seed) & 0xFFFFFFFF,
+                                                       int(seq_id) & 0xFFFFFFFF), "set_sampling")
+
+    def sample_trace_enable(self, on=True):
+        self.lib.check(self.lib.fl_engine_sample_trace_enable(self.h, 1 if on else 0), "sample_trace_enable")
+
+    def sample_trace(self):
+        """dict(logits [16, V], qd [7, V] uint32, qm [7], pt [8, V] uint32,
+        pm [8], drafted [7]) of the last step."""
+        V = self.cfg["vocab_size"]
+        t = dict(logits=np.empty((16, V), np.float32), qd=np.empty((7, V), np.uint32), qm=np.empty(7, np.uint64),
+                 pt=np.empty((8, V), np.uint32), pm=np.empty(8, np.uint64), drafted=np.empty(7, np.int32))
+        self.lib.check(self.lib.fl_engine_sample_trace(self.h, ptr(t["logits"]), ptr(t["qd"]), ptr(t["qm"]),
+                                                       ptr(t["pt"]), ptr(t["pm"]), ptr(t["drafted"])),
+                       "sample_trace")
+        return t
+
+    def spec_begin(self, n_new):
+        self.lib.check(self.lib.fl_engine_spec_begin(self.h, n_new), "spec_begin")
+
+    def spec_step(self):
+        """One speculative step: dict(n, produced, steps, accepted, done)."""
+        s = np.zeros(5, np.int32)
+        self.lib.check(self.lib.fl_engine_spec_step(self.h, ptr(s)), "spec_step")
+        return dict(zip(("n", "produced", "steps", "accepted", "done"), (int(v) for v in s)))
+
+    def get_sampling(self):
+        t, p, s, q = C.c_float(), C.c_float(), C.c_uint32(), C.c_uint32()
+        self.lib.check(self.lib.fl_engine_get_sampling(self.h, C.byref(t), C.byref(p), C.byref(s), C.byref(q)),
+                       "get_sampling")
+        return t.value, p.value, s.value, q.value
 
     def last_timing(self):
         a, b, c = C.c_double(), C.c_double(), C.c_double()

@@ -192,6 +192,46 @@ int fl_engine_spec_generate(fl_engine_t* e, const int* prompt, int prompt_len,
                             int n_new, int k, int max_accepted, int* out,
                             int* acc_hist, int* steps);
 
+/* Decoding rule of the next fl_engine_spec_prefill / spec_generate.
+ * temperature <= 0: greedy (argmax drafts, exact-match acceptance; the
+ * default). temperature > 0: stochastic speculative decoding
+ * (speculative.h:121-185 speculative_config_t.temperature): drafts are drawn
+ * from the top-p nucleus q of softmax(l / temperature), each accepted with
+ * probability min(1, p(x) / q(x)) against the target's nucleus p, the first
+ * rejection resampled from max(0, p - q) (p when that is empty) and, when all
+ * are accepted, a bonus token drawn from the last target row. Uniforms come
+ * from Philox4x32-10 keyed by (seed, 0) at counter (seq_id, step, position,
+ * purpose); the stream is a pure function of (weights, prompt, k,
+ * temperature, top_p, seed, seq_id). top_p in (0, 1]. Distributions are
+ * integer weights trunc(e^((l - max) / T) * 2^24) with exact sums, so the
+ * draws do not depend on any reduction order (speculative.h states the rule). */
+int fl_engine_set_sampling(fl_engine_t* e, float temperature, float top_p, unsigned seed,
+                           unsigned seq_id);
+/* The rule set last: temperature 0 for greedy; top_p 1, seed 0 and seq_id 0
+ * until set. speculative_generate with config->temperature > 0 keeps this
+ * top_p, seed and seq_id. */
+int fl_engine_get_sampling(const fl_engine_t* e, float* temperature, float* top_p, unsigned* seed,
+                           unsigned* seq_id);
+
+/* Sampling trace, for checking the sampling rule against the oracle: when on
+ * (before the next fl_engine_spec_prefill), the step records the logits
+ * behind every draw. fl_engine_sample_trace copies (any may be NULL):
+ * logits [2 * 8, V] (draft j at row j, verify row r at row 7 + r, the first
+ * token after the prefill at row 15), the integer nucleus weights of the
+ * drafts qd [7, V] with their kept masses qm [7], those of the verify rows
+ * pt [8, V] with pm [8], and the drafted tokens [7]. Row 0 of qd / logits,
+ * qm[0] and drafted[0] already belong to the next step once a step ends. */
+int fl_engine_sample_trace_enable(fl_engine_t* e, int on);
+int fl_engine_sample_trace(const fl_engine_t* e, float* logits, unsigned* qd, unsigned long long* qm,
+                           unsigned* pt, unsigned long long* pm, int* drafted);
+
+/* Step-wise decoding: fl_engine_spec_begin restores the post-prefill state
+ * for n_new tokens (as fl_engine_spec_decode does); each fl_engine_spec_step
+ * runs one speculative step and returns state[5] = {n (sequence length),
+ * produced, steps, accepted drafts of this step, done}. */
+int fl_engine_spec_begin(fl_engine_t* e, int n_new);
+int fl_engine_spec_step(fl_engine_t* e, int* state);
+
 /* Split form for timing: prefill once, then decode from the saved
  * post-prefill state as often as wanted (each decode restarts there). */
 int fl_engine_spec_prefill(fl_engine_t* e, const int* prompt, int prompt_len, int k,

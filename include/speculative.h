@@ -19,6 +19,23 @@
  *     rows [t_n, d_1..d_K] with the base model in one pass, accept the longest
  *     prefix with d_j == argmax(base logits at row j-1), then append the base
  *     model's token at the first mismatch (or after d_K): 1..K+1 new tokens.
+ *   - temperature > 0 (speculative_generate through the device engine):
+ *     distributions are integer nucleus weights. E_i = trunc(e^x * 2^24) of
+ *     x = (l_i - max l) / temperature (0 below x = -17; e^x by Cody-Waite
+ *     reduction by ln 2 and the degree-7 Taylor polynomial in Horner form,
+ *     each step a correctly rounded fma or multiply). The nucleus keeps
+ *     E_i >= t*, t* the largest integer whose kept mass S(t) reaches
+ *     trunc(top_p * 2^24) / 2^24 of the total; M is the kept mass. A draw at
+ *     U (24 bits of Philox4x32-10 keyed by (seed, 0) at counter (seq_id,
+ *     step, position, purpose), purpose 0 draft, 1 acceptance, 2 resample or
+ *     bonus; the first token after the prefill at step 0xFFFFFFFF) picks the
+ *     first token whose running weight sum exceeds trunc(U * M / 2^24).
+ *     d_j is drawn from the draft's weights q_j and accepted iff
+ *     U * Mp * q_j(d_j) < 2^24 * p_j(d_j) * Mq (u < p / q); the first
+ *     rejection draws from the residual max(0, p_j * Mq - q_j * Mp) / 2^24
+ *     (from p_j when it is empty); when all K are accepted a bonus token is
+ *     drawn from p_{K+1}. All sums are exact integers. top_p, seed and
+ *     seq_id come from fl_engine_set_sampling (default 1.0, 0, 0).
  *
  * Host/device split: every weight, KV page and activation lives in HBM; the
  * structs below are host handles. The seven projection pointers of

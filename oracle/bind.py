@@ -75,9 +75,19 @@ class Oracle:
         s.orc_greedy_generate.argtypes = [C.POINTER(Model), VP, I, I, VP, VP]
         s.orc_philox_uniform.restype = C.c_float
         s.orc_philox_uniform.argtypes = [C.c_uint32] * 5
+        s.orc_philox_u24.restype = C.c_uint32
+        s.orc_philox_u24.argtypes = [C.c_uint32] * 5
         s.orc_sample_dist.argtypes = [VP, I, C.c_float, C.c_float, VP]
-        s.orc_sample_index.restype = I
-        s.orc_sample_index.argtypes = [VP, I, C.c_float]
+        s.orc_sample_weight.restype = C.c_uint32
+        s.orc_sample_weight.argtypes = [C.c_float]
+        s.orc_sample_weights.restype = C.c_uint64
+        s.orc_sample_weights.argtypes = [VP, I, C.c_float, C.c_float, VP]
+        s.orc_sample_pick.restype = I
+        s.orc_sample_pick.argtypes = [VP, VP, I, C.c_uint64, C.c_uint32]
+        s.orc_sample_accept.restype = I
+        s.orc_sample_accept.argtypes = [C.c_uint32, C.c_uint32, C.c_uint64, C.c_uint32, C.c_uint64]
+        s.orc_sample_residual.restype = C.c_uint64
+        s.orc_sample_residual.argtypes = [VP, C.c_uint64, VP, C.c_uint64, I, VP]
         s.orc_spec_generate_sampled.restype = I
         s.orc_spec_generate_sampled.argtypes = [C.POINTER(Model), VP, I, I, I, C.c_float, C.c_float, C.c_uint32,
                                                 C.c_uint32, VP, VP]
@@ -170,9 +180,36 @@ class Oracle:
         self.so.orc_sample_dist(_p(lg), lg.size, T, top_p, _p(q))
         return q
 
-    def sample_index(self, w, u):
-        w = np.ascontiguousarray(w, np.float32)
-        return self.so.orc_sample_index(_p(w), w.size, u)
+    def sample_weights(self, logits, T, top_p):
+        """(E uint32 nucleus weights, kept mass M)."""
+        lg = np.ascontiguousarray(logits, np.float32)
+        E = np.empty(lg.size, np.uint32)
+        M = self.so.orc_sample_weights(_p(lg), lg.size, T, top_p, _p(E))
+        return E, int(M)
+
+    def sample_weight(self, x):
+        return int(self.so.orc_sample_weight(float(x)))
+
+    def sample_pick(self, w, total, U):
+        """Inverse-CDF pick over integer weights (uint32 or uint64) at U / 2^24."""
+        if w.dtype == np.uint32:
+            w = np.ascontiguousarray(w)
+            return self.so.orc_sample_pick(_p(w), None, w.size, int(total), int(U))
+        w = np.ascontiguousarray(w, np.uint64)
+        return self.so.orc_sample_pick(None, _p(w), w.size, int(total), int(U))
+
+    def sample_accept(self, U, Ep, Mp, Eq, Mq):
+        return bool(self.so.orc_sample_accept(int(U), int(Ep), int(Mp), int(Eq), int(Mq)))
+
+    def sample_residual(self, Ep, Mp, Eq, Mq):
+        Ep = np.ascontiguousarray(Ep, np.uint32)
+        Eq = np.ascontiguousarray(Eq, np.uint32)
+        R = np.empty(Ep.size, np.uint64)
+        s = self.so.orc_sample_residual(_p(Ep), int(Mp), _p(Eq), int(Mq), Ep.size, _p(R))
+        return R, int(s)
+
+    def philox_u24(self, seed, seq, step, pos, purpose):
+        return int(self.so.orc_philox_u24(seed & 0xFFFFFFFF, seq, step & 0xFFFFFFFF, pos, purpose))
 
     def philox(self, ctr, key):
         c = np.asarray(ctr, np.uint32)

@@ -774,58 +774,113 @@ int orc_medusa_generate(const orc_model_t* mdl, const int* prompt, int P, const 
 /* temperature > 0; the reference declares the contract without code)  */
 /* ------------------------------------------------------------------ */
 
-/* Uniform in [0, 1) from 24 bits of Philox4x32-10 with key (seed, 0) and
- * counter (sequence, step, position, purpose). */
-float orc_philox_uniform(uint32_t seed, uint32_t seq, uint32_t step, uint32_t pos, uint32_t purpose) {
+/* 24 bits of Philox4x32-10 (Salmon et al., SC'11) with key (seed, 0) at
+ * counter (sequence, step, position, purpose): U in [0, 2^24), u = U / 2^24. */
+uint32_t orc_philox_u24(uint32_t seed, uint32_t seq, uint32_t step, uint32_t pos, uint32_t purpose) {
     const uint32_t ctr[4] = {seq, step, pos, purpose};
     const uint32_t key[2] = {seed, 0u};
     uint32_t o[4];
     orc_philox4x32_10(ctr, key, o);
-    return (float)(o[0] >> 8) * (1.0f / 16777216.0f);
+    return o[0] >> 8;
 }
 
-/* p[i] = softmax(l / T)[i]; the nucleus is {i : p[i] >= tau} with tau the
- * largest float whose mass S(tau) = sum_{p_i >= tau} p_i (index order)
- * reaches top_p (bisection over the float bit patterns); q[i] = p[i] / S(tau)
- * inside the nucleus, 0 outside. */
-void orc_sample_dist(const float* l, int V, float T, float top_p, float* q) {
+float orc_philox_uniform(uint32_t seed, uint32_t seq, uint32_t step, uint32_t pos, uint32_t purpose) {
+    return (float)orc_philox_u24(seed, seq, step, pos, purpose) * (1.0f / 16777216.0f);
+}
+
+/* Integer sampling weight of x = (l - max) / T <= 0: E = trunc(e^x * 2^24),
+ * 0 below x = -17. e^x by Cody-Waite range reduction x = k ln2 + r (ln2 split
+ * into a 16-bit head and a float tail, |k| <= 25 so k * head is exact) and
+ * the degree-7 Taylor polynomial of e^r on |r| <= ln2 / 2 in Horner form
+ * (truncation error below 6e-9), every step one correctly rounded fma or
+ * multiply, then the exact scale 2^(k + 24). The device evaluates the same
+ * operations, so E is the same integer on both. */
+uint32_t orc_sample_weight(float x) {
+    if (!(x >= -17.0f)) return 0u;
+    const float kf = rintf(x * 1.442695f);
+    float r = fmaf(-kf, 0.693145751953125f, x);
+    r = fmaf(-kf, 1.4286068e-06f, r);
+    float p = 0.0001984127f;
+    p = fmaf(p, r, 0.0013888889f);
+    p = fmaf(p, r, 0.008333334f);
+    p = fmaf(p, r, 0.041666668f);
+    p = fmaf(p, r, 0.16666667f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    const float s = ldexpf(p, (int)kf + 24);
+    const uint32_t E = (uint32_t)s;
+    return E > (1u << 24) ? (1u << 24) : E;
+}
+
+/* Nucleus weights of logits l: E_i = weight((l_i - max) / T); the nucleus is
+ * {i : E_i >= t*} with t* the largest integer whose kept mass
+ * S(t) = sum_{E_i >= t} E_i satisfies S(t) * 2^24 >= P * z, z = S(1) and
+ * P = max(1, trunc(top_p * 2^24)). Kept weights stay, the rest become 0;
+ * returns the kept mass M. All sums are exact integers. */
+uint64_t orc_sample_weights(const float* l, int V, float T, float top_p, uint32_t* E) {
     float mx = l[0];
     for (int i = 1; i < V; i++) if (l[i] > mx) mx = l[i];
-    float z = 0.0f;
-    for (int i = 0; i < V; i++) { q[i] = expf((l[i] - mx) / T); z += q[i]; }
-    for (int i = 0; i < V; i++) q[i] = q[i] / z;
-    /* largest bit pattern b with S(as_float(b)) >= top_p; S(0) = sum(p) ~ 1 */
-    uint32_t lo = 0u, hi = 0x3F800001u;  /* S(lo) >= top_p, S(hi) < top_p */
+    uint64_t z = 0;
+    for (int i = 0; i < V; i++) {
+        E[i] = orc_sample_weight((l[i] - mx) / T);
+        z += E[i];
+    }
+    uint32_t P = (uint32_t)(top_p * 16777216.0f);
+    if (P < 1u) P = 1u;
+    const unsigned __int128 need = (unsigned __int128)P * z;
+    uint32_t lo = 1u, hi = (1u << 24) + 1u; /* S(lo) meets the mass, S(hi) = 0 does not */
     while (hi - lo > 1u) {
         const uint32_t mid = lo + (hi - lo) / 2u;
-        float t;
-        memcpy(&t, &mid, 4);
-        float s = 0.0f;
-        for (int i = 0; i < V; i++) if (q[i] >= t) s += q[i];
-        if (s >= top_p) lo = mid; else hi = mid;
+        uint64_t s = 0;
+        for (int i = 0; i < V; i++) if (E[i] >= mid) s += E[i];
+        if (((unsigned __int128)s << 24) >= need) lo = mid; else hi = mid;
     }
-    float tau;
-    memcpy(&tau, &lo, 4);
-    float s = 0.0f;
-    for (int i = 0; i < V; i++) if (q[i] >= tau) s += q[i];
-    for (int i = 0; i < V; i++) q[i] = q[i] >= tau ? q[i] / s : 0.0f;
+    uint64_t M = 0;
+    for (int i = 0; i < V; i++) {
+        if (E[i] < lo) E[i] = 0u;
+        M += E[i];
+    }
+    return M;
+}
+
+/* q_i = E_i / M as floats (for inspection). */
+void orc_sample_dist(const float* l, int V, float T, float top_p, float* q) {
+    uint32_t* E = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)V);
+    const uint64_t M = orc_sample_weights(l, V, T, top_p, E);
+    for (int i = 0; i < V; i++) q[i] = (float)((double)E[i] / (double)M);
+    free(E);
 }
 
 /* Inverse CDF in index order: the first i whose running sum of w exceeds
- * u * sum(w); the last i with w[i] > 0 if rounding leaves none. */
-int orc_sample_index(const float* w, int V, float u) {
-    float z = 0.0f;
-    for (int i = 0; i < V; i++) z += w[i];
-    const float tgt = u * z;
-    float c = 0.0f;
-    int last = 0;
+ * trunc(U * total / 2^24) (total = sum w > 0). w32 or w64 gives the weights. */
+int orc_sample_pick(const uint32_t* w32, const uint64_t* w64, int V, uint64_t total, uint32_t U) {
+    const uint64_t tgt = (uint64_t)(((unsigned __int128)U * total) >> 24);
+    uint64_t c = 0;
     for (int i = 0; i < V; i++) {
-        if (w[i] <= 0.0f) continue;
-        c += w[i];
-        last = i;
-        if (tgt < c) return i;
+        c += w32 ? w32[i] : w64[i];
+        if (c > tgt) return i;
     }
-    return last;
+    return V - 1;
+}
+
+/* Acceptance of drafted x: u < p(x) / q(x) with p = Ep / Mp, q = Eq / Mq,
+ * i.e. U * Mp * Eq < 2^24 * Ep * Mq. */
+int orc_sample_accept(uint32_t U, uint32_t Ep, uint64_t Mp, uint32_t Eq, uint64_t Mq) {
+    return (unsigned __int128)U * Mp * Eq < (((unsigned __int128)Ep * Mq) << 24);
+}
+
+/* Residual weights R_i = max(0, Ep_i * Mq - Eq_i * Mp) / 2^24 (truncated),
+ * proportional to max(0, p - q); returns their sum. */
+uint64_t orc_sample_residual(const uint32_t* Ep, uint64_t Mp, const uint32_t* Eq, uint64_t Mq, int V,
+                             uint64_t* R) {
+    uint64_t s = 0;
+    for (int i = 0; i < V; i++) {
+        const unsigned __int128 a = (unsigned __int128)Ep[i] * Mq, b = (unsigned __int128)Eq[i] * Mp;
+        R[i] = a > b ? (uint64_t)((a - b) >> 24) : 0u;
+        s += R[i];
+    }
+    return s;
 }
 
 int orc_spec_generate_sampled(const orc_model_t* mdl, const int* prompt, int P, int K, int n_new, float T,
@@ -841,9 +896,11 @@ int orc_spec_generate_sampled(const orc_model_t* mdl, const int* prompt, int P, 
     float* x = (float*)malloc(sizeof(float) * (size_t)rows_max * d);
     float* feat = (float*)malloc(sizeof(float) * (size_t)rows_max * d);
     float* lg = (float*)malloc(sizeof(float) * (size_t)(K + 1) * V);
-    float* qd = (float*)malloc(sizeof(float) * (size_t)K * V);       /* draft distributions */
-    float* pt = (float*)malloc(sizeof(float) * (size_t)(K + 1) * V); /* target distributions */
-    float* r = (float*)malloc(sizeof(float) * V);
+    uint32_t* qd = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)K * V);       /* draft weights */
+    uint32_t* pt = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)(K + 1) * V); /* target weights */
+    uint64_t* qm = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)(K + 1));
+    uint64_t* pm = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)(K + 1));
+    uint64_t* r = (uint64_t*)malloc(sizeof(uint64_t) * V);
     int* pos = (int*)malloc(sizeof(int) * rows_max);
     int* drafted = (int*)malloc(sizeof(int) * (K + 1));
     float* g = (float*)malloc(sizeof(float) * d);
@@ -858,9 +915,11 @@ int orc_spec_generate_sampled(const orc_model_t* mdl, const int* prompt, int P, 
     memcpy(feat + d, x, sizeof(float) * (size_t)(P - 1) * d);
     memcpy(g, x + (size_t)(P - 1) * d, sizeof(float) * d);
     orc_lm_logits(mdl, g, lg, 1);
-    orc_sample_dist(lg, V, T, top_p, r);
     int n = P;
-    seq[n] = orc_sample_index(r, V, orc_philox_uniform(seed, seq_id, 0xFFFFFFFFu, (uint32_t)n, 2u));
+    {
+        const uint64_t M = orc_sample_weights(lg, V, T, top_p, pt);
+        seq[n] = orc_sample_pick(pt, NULL, V, M, orc_philox_u24(seed, seq_id, 0xFFFFFFFFu, (uint32_t)n, 2u));
+    }
     int produced = 0;
     out[produced++] = seq[n];
     memcpy(feat + (size_t)P * d, g, sizeof(float) * d);
@@ -885,9 +944,10 @@ int orc_spec_generate_sampled(const orc_model_t* mdl, const int* prompt, int P, 
                 memcpy(g, x, sizeof(float) * d);
             }
             orc_lm_logits(mdl, g, lg, 1);
-            orc_sample_dist(lg, V, T, top_p, qd + (size_t)j * V);
-            drafted[j] = orc_sample_index(qd + (size_t)j * V, V,
-                                          orc_philox_uniform(seed, seq_id, (uint32_t)steps, (uint32_t)(n + 1 + j), 0u));
+            uint32_t* qj = qd + (size_t)j * V;
+            qm[j] = orc_sample_weights(lg, V, T, top_p, qj);
+            drafted[j] = orc_sample_pick(qj, NULL, V, qm[j],
+                                         orc_philox_u24(seed, seq_id, (uint32_t)steps, (uint32_t)(n + 1 + j), 0u));
         }
         m = n + 1;
         /* verify rows n..n+K */
@@ -898,26 +958,26 @@ int orc_spec_generate_sampled(const orc_model_t* mdl, const int* prompt, int P, 
         }
         orc_stack_forward(mdl, mdl->base, D->layers, &kvb, x, K + 1, n, pos, NULL);
         orc_lm_logits(mdl, x, lg, K + 1);
-        for (int rr = 0; rr <= K; rr++) orc_sample_dist(lg + (size_t)rr * V, V, T, top_p, pt + (size_t)rr * V);
+        for (int rr = 0; rr <= K; rr++)
+            pm[rr] = orc_sample_weights(lg + (size_t)rr * V, V, T, top_p, pt + (size_t)rr * V);
         /* rejection sampling (accept with probability min(1, p / q)) */
         int a = 0, last;
         for (;;) {
+            const uint32_t pos_a = (uint32_t)(n + 1 + a);
             if (a == K) {
-                last = orc_sample_index(pt + (size_t)K * V, V,
-                                        orc_philox_uniform(seed, seq_id, (uint32_t)steps, (uint32_t)(n + 1 + K), 2u));
+                last = orc_sample_pick(pt + (size_t)K * V, NULL, V, pm[K],
+                                       orc_philox_u24(seed, seq_id, (uint32_t)steps, pos_a, 2u));
                 break;
             }
             const int xt = drafted[a];
-            const float pq = pt[(size_t)a * V + xt] / qd[(size_t)a * V + xt];
-            const float u = orc_philox_uniform(seed, seq_id, (uint32_t)steps, (uint32_t)(n + 1 + a), 1u);
-            if (u < pq) { a++; continue; }
-            float zr = 0.0f;
-            for (int i = 0; i < V; i++) {
-                r[i] = fmaxf(0.0f, pt[(size_t)a * V + i] - qd[(size_t)a * V + i]);
-                zr += r[i];
+            const uint32_t U = orc_philox_u24(seed, seq_id, (uint32_t)steps, pos_a, 1u);
+            if (orc_sample_accept(U, pt[(size_t)a * V + xt], pm[a], qd[(size_t)a * V + xt], qm[a])) {
+                a++;
+                continue;
             }
-            const float ur = orc_philox_uniform(seed, seq_id, (uint32_t)steps, (uint32_t)(n + 1 + a), 2u);
-            last = zr > 0.0f ? orc_sample_index(r, V, ur) : orc_sample_index(pt + (size_t)a * V, V, ur);
+            const uint64_t zr = orc_sample_residual(pt + (size_t)a * V, pm[a], qd + (size_t)a * V, qm[a], V, r);
+            const uint32_t Ur = orc_philox_u24(seed, seq_id, (uint32_t)steps, pos_a, 2u);
+            last = zr > 0 ? orc_sample_pick(NULL, r, V, zr, Ur) : orc_sample_pick(pt + (size_t)a * V, NULL, V, pm[a], Ur);
             break;
         }
         if (acc_hist) acc_hist[steps] = a;
@@ -931,7 +991,8 @@ int orc_spec_generate_sampled(const orc_model_t* mdl, const int* prompt, int P, 
         n = n + a + 1;
     }
     g_last_decode_s = now_s() - t0;
-    free(seq); free(x); free(feat); free(lg); free(qd); free(pt); free(r); free(pos); free(drafted); free(g);
+    free(seq); free(x); free(feat); free(lg); free(qd); free(pt); free(qm); free(pm); free(r); free(pos);
+    free(drafted); free(g);
     orc_kv_free(&kvb);
     orc_kv_free(&kvd);
     return steps;

@@ -176,10 +176,18 @@ int orc_medusa_tree(int root_tok, int n_heads, const int* topk, const int* tok,
  * position, purpose: 0 draft sample, 1 acceptance test, 2 resample / bonus;
  * the first token after the prefill uses step 0xFFFFFFFF). */
 float orc_philox_uniform(uint32_t seed, uint32_t seq, uint32_t step, uint32_t pos, uint32_t purpose);
-/* q = the nucleus-filtered, renormalised softmax(l / T) (see oracle.c). */
+uint32_t orc_philox_u24(uint32_t seed, uint32_t seq, uint32_t step, uint32_t pos, uint32_t purpose);
+/* Integer sampling rule (exact sums, so any summation order gives the same
+ * result; see oracle.c): weight E = trunc(e^x * 2^24) of x = (l - max) / T;
+ * nucleus weights (0 outside) and their mass; inverse-CDF pick at U / 2^24;
+ * acceptance test u < p(x) / q(x); residual weights of max(0, p - q). */
+uint32_t orc_sample_weight(float x);
+uint64_t orc_sample_weights(const float* l, int V, float T, float top_p, uint32_t* E);
 void orc_sample_dist(const float* l, int V, float T, float top_p, float* q);
-/* Inverse CDF of weights w (index order) at u in [0, 1). */
-int orc_sample_index(const float* w, int V, float u);
+int orc_sample_pick(const uint32_t* w32, const uint64_t* w64, int V, uint64_t total, uint32_t U);
+int orc_sample_accept(uint32_t U, uint32_t Ep, uint64_t Mp, uint32_t Eq, uint64_t Mq);
+uint64_t orc_sample_residual(const uint32_t* Ep, uint64_t Mp, const uint32_t* Eq, uint64_t Mq, int V,
+                             uint64_t* R);
 /* Draft tokens sampled from the draft distribution, accepted with
  * probability min(1, p / q), rejection resampled from norm(max(0, p - q)),
  * bonus from p when all K are accepted. Returns steps. */

@@ -266,3 +266,172 @@ def test_medusa_generate_reference_api(gpu, orc):
     eng.close()
     want, _, margins = oracle_model(orc, dims, w, embed, draft_layers=0, n_medusa=4).medusa(p, 48, MEDUSA_TOPK, 64)
     assert_stream_matches(out, want, margins)
+
+
+# ---- stochastic speculative decoding (temperature > 0) ----
+#
+# The sampling rule works on integer weights with exact sums, so given the
+# same logits the device and the oracle make bit-identical decisions. Device
+# and oracle logits agree within the logit tolerance but not bit for bit
+# (activation-quantization rounding can flip on reordered float sums), and a
+# draw moves with logit changes far below that tolerance; so the rule is
+# checked by replay: every draw, acceptance test and emitted token of a device
+# decode is recomputed by the oracle from the logits the device drew from,
+# with the same Philox counters, and must be identical.
+
+SAMPLE_T, SAMPLE_TOP_P, SAMPLE_SEED = 0.8, 0.95, 1234
+FIRST_ROW, TARGET_ROW0 = 15, 7
+
+
+def check_weights(orc, E_dev, M_dev, logits, T, top_p, what):
+    E, M = orc.sample_weights(logits, T, top_p)
+    assert np.array_equal(E_dev, E), f"{what}: nucleus weights differ at {np.nonzero(E_dev != E)[0][:5]}"
+    assert int(M_dev) == M, f"{what}: kept mass"
+    return E, M
+
+
+def replay_sampled(eng, orc, p, k, n_new, T, top_p, seed, seq_id=0):
+    """Steps the device decode and replays every sampling decision; returns
+    (tokens, accepted per step)."""
+    P = len(p)
+    u24 = lambda step, pos, purpose: orc.philox_u24(seed, seq_id, step, pos, purpose)
+    eng.set_sampling(T, top_p, seed, seq_id)
+    eng.sample_trace_enable(True)
+    eng.spec_prefill(p, k)
+    out, acc_hist = eng.spec_decode(n_new)  # the stream; the steps below repeat it
+    t = eng.sample_trace()
+    E, M = orc.sample_weights(t["logits"][FIRST_ROW], T, top_p)
+    assert out[0] == orc.sample_pick(E, M, u24(0xFFFFFFFF, P, 2)), "first token"
+    eng.spec_begin(n_new)
+    t = eng.sample_trace()
+    state = dict(n=P, produced=1, steps=0, done=0)
+    while not state["done"]:
+        n, s, produced = state["n"], state["steps"], state["produced"]
+        pre = (t["logits"][0].copy(), t["qd"][0].copy(), int(t["qm"][0]), int(t["drafted"][0]))
+        state = eng.spec_step()
+        t = eng.sample_trace()
+        d_lg = [pre[0]] + [t["logits"][j] for j in range(1, k)]
+        d_q = [pre[1]] + [t["qd"][j] for j in range(1, k)]
+        d_m = [pre[2]] + [int(t["qm"][j]) for j in range(1, k)]
+        drafted = [pre[3]] + [int(t["drafted"][j]) for j in range(1, k)]
+        for j in range(k):
+            check_weights(orc, d_q[j], d_m[j], d_lg[j], T, top_p, f"step {s} draft {j}")
+            assert drafted[j] == orc.sample_pick(d_q[j], d_m[j], u24(s, n + 1 + j, 0)), f"step {s}: draft draw {j}"
+        pt, pm = t["pt"], [int(v) for v in t["pm"]]
+        for r in range(k + 1):
+            check_weights(orc, pt[r], pm[r], t["logits"][TARGET_ROW0 + r], T, top_p, f"step {s} target {r}")
+        a = 0
+        while True:
+            pos = n + 1 + a
+            if a == k:
+                last = orc.sample_pick(pt[k], pm[k], u24(s, pos, 2))
+                break
+            x = drafted[a]
+            if orc.sample_accept(u24(s, pos, 1), pt[a][x], pm[a], d_q[a][x], d_m[a]):
+                a += 1
+                continue
+            R, zr = orc.sample_residual(pt[a], pm[a], d_q[a], d_m[a])
+            last = orc.sample_pick(R, zr, u24(s, pos, 2)) if zr > 0 else orc.sample_pick(pt[a], pm[a], u24(s, pos, 2))
+            break
+        assert state["accepted"] == a and acc_hist[s] == a, f"step {s}: accepted {state['accepted']} vs {a}"
+        assert state["n"] == n + a + 1
+        want = (drafted[:a] + [last])[: n_new - produced]
+        assert out[produced: produced + len(want)].tolist() == want, f"step {s}: emitted tokens"
+    assert state["produced"] == n_new and state["steps"] == len(acc_hist)
+    eng.sample_trace_enable(False)
+    eng.set_sampling(0.0)
+    return out, acc_hist
+
+
+@pytest.mark.parametrize("T,top_p", [(SAMPLE_T, SAMPLE_TOP_P), (1.5, 1.0), (0.3, 0.5)])
+def test_sampled_decisions_replay_on_oracle(small, orc, T, top_p):
+    """Every draft draw, target distribution, acceptance test, residual or
+    bonus draw and the emitted tokens of a 40-token sampled decode (k = 4)
+    follow the oracle's rule and counter layout."""
+    dims, eng, om, embed = small
+    p = prompt(12, 16, dims["vocab"])
+    try:
+        out, acc = replay_sampled(eng, orc, p, 4, 40, T, top_p, SAMPLE_SEED)
+    finally:
+        eng.sample_trace_enable(False)
+        eng.set_sampling(0.0)
+    assert acc.min() < 4, "no rejection exercised"
+
+
+def test_sampled_stream_repeatable(small):
+    """Same seed and counter layout, same stream (also after restarting from
+    the saved state); another seed or sequence id, another stream."""
+    dims, eng, om, embed = small
+    p = prompt(12, 16, dims["vocab"])
+    try:
+        eng.set_sampling(SAMPLE_T, SAMPLE_TOP_P, SAMPLE_SEED)
+        a, ha = eng.spec_generate(p, 40, 4)
+        b, hb = eng.spec_decode(40)
+        c, _ = eng.spec_generate(p, 40, 4)
+        eng.set_sampling(SAMPLE_T, SAMPLE_TOP_P, SAMPLE_SEED + 1)
+        d, _ = eng.spec_generate(p, 40, 4)
+        eng.set_sampling(SAMPLE_T, SAMPLE_TOP_P, SAMPLE_SEED, 1)
+        f, _ = eng.spec_generate(p, 40, 4)
+    finally:
+        eng.set_sampling(0.0)
+    assert np.array_equal(a, b) and np.array_equal(ha, hb) and np.array_equal(a, c)
+    assert not np.array_equal(a, d) and not np.array_equal(a, f)
+
+
+def test_sampled_greedy_limit(small):
+    """A vanishing temperature with a one-token nucleus is greedy decoding."""
+    dims, eng, om, embed = small
+    p = prompt(13, 16, dims["vocab"])
+    want, margins = om.greedy(p, 32)
+    try:
+        eng.set_sampling(1e-4, 1e-6, 7)
+        got, _ = eng.spec_generate(p, 32, 4)
+    finally:
+        eng.set_sampling(0.0)
+    assert_stream_matches(got, want, margins)
+
+
+def test_sampled_large_vocab(gpu, orc):
+    """Vocabulary above the register-resident size (32768): the nucleus
+    passes read the distribution from memory."""
+    dims = dict(SMALL_V1, vocab=40000)
+    w, embed = make_weights(gpu, dims, seed=5)
+    eng = flb200.Engine(gpu, engine_cfg(dims, draft_layers=1))
+    load_engine(eng, w, embed)
+    p = prompt(14, 12, dims["vocab"])
+    try:
+        replay_sampled(eng, orc, p, 4, 24, 1.0, 0.9, 77, 3)
+    finally:
+        eng.close()
+
+
+def test_speculative_generate_sampled_reference_api(gpu, orc):
+    """speculative_generate() with config->temperature > 0 runs the sampled
+    rule with the engine's top_p and Philox key: the same stream as the
+    engine's own sampled decode."""
+    import ctypes as C
+    dims = SMALL
+    w, embed = make_weights(gpu, dims, seed=31)
+    eng = flb200.Engine(gpu, engine_cfg(dims, draft_layers=1))
+    load_engine(eng, {k: v for k, v in w.items() if k[0] != 1}, embed)
+    dm = gpu.draft_model_create(1, dims["d"], dims["ffn"], dims["vocab"])
+    assert gpu.draft_model_load(dm, b"synthetic:31") == 0
+    eng.set_sampling(0.5, SAMPLE_TOP_P, 99, 2)
+    cfg = flb200.SpecConfig(4, 0.7, 4)  # the call's temperature wins
+    p = prompt(9, 12, dims["vocab"])
+    ph = p.astype(np.float32)
+    out = np.empty(20, np.int32)
+    n = gpu.speculative_generate(dm, eng.h, C.cast(gpu.so.fl_cuda_target_forward, C.c_void_p), flb200.ptr(ph),
+                                 len(p), flb200.ptr(out), 20, C.byref(cfg))
+    assert n == 20, gpu.err()
+    assert eng.get_sampling() == pytest.approx((0.7, SAMPLE_TOP_P, 99, 2))
+    want, _ = eng.spec_generate(p, 20, 4)
+    assert np.array_equal(out, want)
+    cfg = flb200.SpecConfig(4, 0.0, 4)
+    n = gpu.speculative_generate(dm, eng.h, C.cast(gpu.so.fl_cuda_target_forward, C.c_void_p), flb200.ptr(ph),
+                                 len(p), flb200.ptr(out), 20, C.byref(cfg))
+    assert n == 20 and eng.get_sampling()[0] == 0.0
+    g_want, _, margins = oracle_model(orc, dims, w, embed).spec(p, 20, 4)
+    assert_stream_matches(out, g_want, margins)
+    gpu.draft_model_free(dm)
+    eng.close()
