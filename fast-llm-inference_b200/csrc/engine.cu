@@ -220,7 +220,39 @@ GemvParams gemv_base(const Linear& l, const uint8_t* aq, const int* done) {
     return g;
 }
 
+// Many static rows (more than two GEMV launches' worth) go through the
+// tcgen05 GEMM (weights read once); the fused RMSNorm prologue then runs as
+// its own quantization pass.
+constexpr int kGemmMinRows = 2 * kMaxRows;
+bool gemm_enabled() {
+    static const bool on = [] {
+        const char* v = getenv("FL_GEMM_TC");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
 int launch_chunks(GemvParams g, int epi, int M, const int* dyn_M, cudaStream_t s, bool pdl) {
+    if (!dyn_M && M > kGemmMinRows && gemm_enabled() && g.P != 0 && g.row0 == 0) {
+        GemvParams h = g;
+        h.x = nullptr;
+        h.x_row_dyn = nullptr;
+        if (gemm_tc_supported(h, epi)) {
+            if (g.x) {
+                ActQuantParams a = {};
+                a.x = g.x;
+                a.q = const_cast<uint8_t*>(g.aq);
+                a.K = g.K;
+                a.M = M;
+                a.norm = g.norm;
+                a.eps = g.eps;
+                a.done = g.done;
+                FL_CHECK_CUDA(launch_act_quant(a, s, pdl));
+            }
+            FL_CHECK_CUDA(launch_gemm_tc(h, epi, M, s));
+            return FL_OK;
+        }
+    }
     if (dyn_M) {  // M is the static upper bound of *dyn_M (<= kMaxRows)
         g.dyn_M = dyn_M;
         g.row0 = 0;
@@ -1180,8 +1212,19 @@ FL_API void fl_engine_note_draft(fl_engine_t* e, const void* draft) {
 FL_API int fl_engine_bench_linear(fl_engine_t* e, int stack, int kind, int M, int reps, double* us_per_launch,
                                   double* bytes_per_launch) {
     FL_CHECK(check_ready(e, stack == 1));
-    if (kind < 0 || kind > 3 || M < 1 || M > kMaxRows || reps < 1) return set_error(FL_E_INVAL, "bench_linear: bad arguments");
+    if (kind < 0 || kind > 3 || M < 1 || M > e->R || reps < 1) return set_error(FL_E_INVAL, "bench_linear: bad arguments");
     Stack& S = stack == 0 ? e->base : e->draft;
+    size_t nmax = 0;
+    for (int l = 0; l < S.nl; l++) {
+        const Linear& L = kind == 0 ? S.L[l].qkv : kind == 1 ? S.L[l].o : kind == 2 ? S.L[l].gu : S.L[l].down;
+        nmax = std::max(nmax, (size_t)L.N);
+    }
+    float* out = nullptr;
+    FL_CHECK_CUDA(cudaMalloc(&out, sizeof(float) * nmax * M));
+    struct FreeOnExit {
+        float* p;
+        ~FreeOnExit() { cudaFree(p); }
+    } out_guard{out};
     cudaGraph_t g = nullptr;
     FL_CHECK_CUDA(cudaStreamBeginCapture(e->s, cudaStreamCaptureModeThreadLocal));
     int rc = FL_OK;
@@ -1191,12 +1234,18 @@ FL_API int fl_engine_bench_linear(fl_engine_t* e, int stack, int kind, int M, in
         l0 = &L;
         GemvParams gp = gemv_base(L, kind == 3 ? e->hq : e->xq, nullptr);
         gp.M = M;
-        gp.out = e->q;  // scratch rows of at least N floats
+        gp.out = out;
         gp.ldo = L.N;
-        if (launch_gemv_auto(gp, EPI_STORE, e->s, true) != cudaSuccess) rc = set_error(FL_E_CUDA, "bench_linear launch");
+        // up to 8 rows: one GEMV launch; more: the many-row path of the layers
+        if (M <= kMaxRows ? launch_gemv_auto(gp, EPI_STORE, e->s, true) != cudaSuccess
+                          : launch_chunks(gp, EPI_STORE, M, nullptr, e->s, false) != FL_OK)
+            rc = set_error(FL_E_CUDA, "bench_linear launch");
     }
     cudaError_t ce = cudaStreamEndCapture(e->s, &g);
-    if (rc != FL_OK) { if (g) cudaGraphDestroy(g); return rc; }
+    if (rc != FL_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
     FL_CHECK_CUDA(ce);
     cudaGraphExec_t ex = nullptr;
     ce = cudaGraphInstantiate(&ex, g, 0);

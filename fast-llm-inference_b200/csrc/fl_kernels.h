@@ -89,6 +89,14 @@ int gemv_auto_grid(int N, int K);
 // Returns and clears the device error word (bounded waits that gave up).
 int take_device_error();
 
+// tcgen05 INT8 GEMM for many activation rows (gemm_tc.cu): block-mode tiled
+// weights (P != 0), K a multiple of 128, N of 16, activations already
+// quantized in g.aq (rows 0 .. M-1, row stride K), epilogues STORE, RESID,
+// QKV and SWIGLU. Same result bits as the block-mode GEMV.
+bool gemm_tc_supported(const GemvParams& g, int epi);
+cudaError_t launch_gemm_tc(const GemvParams& g, int epi, int M, cudaStream_t s);
+int take_gemm_error();
+
 struct ActQuantParams {
     const float* x;           // [rows, K]
     uint8_t* q;               // [rows, K]

@@ -1,0 +1,530 @@
+// INT8 GEMM on the 5th-generation tensor cores (sm_100a) for the many-row
+// passes of the path: prompt prefill, tree verification (Medusa: 65 rows) and
+// the M >= 16 shapes of the matmul sweep. Same contract and result bits as
+// matmul_dequantized in block mode (fast_llm/src/kernels/
+// dequantized_tensor.c:204-247 with per-32-block fp16 scales):
+//   C[m, n] = (sum over blocks b, in order, of (float)dot_b(m, n) * d[n, b]) / 127
+// with dot_b the exact int32 dot of 32 u8 activations and 32 s8 weights.
+//
+// One CTA computes a tile of 128 weight rows x BN (16, 32 or 64) activation rows.
+//  - warps 0-3: producers. Per 128-byte K-group they copy the weight tile
+//    (128 rows x 128 B) with coalesced 16-byte cp.async (eight lanes per row;
+//    the tiled weight layout already stores each 128-byte group XOR-swizzled
+//    by row & 7, which is the 128-byte swizzle pattern the MMA descriptor
+//    expects, so the bytes move verbatim), and thread 0 loads the activation
+//    tile (BN rows x 128 B) by TMA with SWIZZLE_128B. Rows of the weight tile
+//    are separate 128-byte pieces of memory, which a TMA box would fetch one
+//    request at a time; the load/store unit keeps them in flight together.
+//    A stage is published (async-proxy fence, then mbarrier arrival) once
+//    its copies complete, six stages behind the newest.
+//  - warp 4: allocates all 512 TMEM columns, then issues one
+//    tcgen05.mma.cta_group::1.kind::i8 (M = 128, N = BN, K = 32) per 32-element
+//    block into its own BN TMEM columns; G consecutive blocks (G BN = 64)
+//    form a group with one commit, and the groups cycle through 8 TMEM
+//    buffers.
+//  - warps 5-12: readout, two per TMEM lane quadrant, each with BN / 2
+//    columns of its quadrant's 32 lanes. Per group
+//    it loads the G blocks' s32 dots, releases the buffer and, while the next
+//    group's load is in flight, turns each dot into the float
+//    12582912 + dot by an integer add of 0x4B400000 (exact: |dot| < 2^22).
+//    One fma with d and -12582912 d (exact) then yields exactly the rounded
+//    product (float)dot * d, which is added to the row's running sum in block
+//    order: the sum is bit-identical to the sequential reference order.
+//  - After the last block the readout warps divide by 127 and apply the layer
+//    epilogue to (n, n + 1) pairs (lane shuffles).
+// Every wait is bounded (2 s of %globaltimer): on expiry the CTA raises an
+// error word, stops issuing, waits (bounded) for its own copies and MMAs,
+// frees TMEM and exits.
+#include <cuda.h>
+
+#include "fl_common.cuh"
+#include "fl_epilogue.cuh"
+#include "fl_kernels.h"
+#include "fl_layout.cuh"
+
+namespace fl {
+
+namespace {
+
+__device__ int g_gemm_error = 0;
+
+constexpr int kProdW = 4, kMma = 4, kRd0 = 5, kWQ = 2;
+constexpr int kGThreads = (kRd0 + 4 * kWQ) * 32;
+constexpr int kProdT = kProdW * 32;
+constexpr int kInFlight = 6;  // weight stages in flight per producer thread
+constexpr int kTmaRows = 64;  // weight-tile rows fetched by TMA (the rest by cp.async)
+// blocks per TMEM group (one commit, one readout round trip): G BN = 64
+__host__ __device__ constexpr int group_blocks(int bn) { return 64 / bn; }
+constexpr int kTileN = 128;                 // weight rows per tile (UMMA M)
+constexpr int kGroup = 128;                 // K bytes per stage (four 32-element blocks)
+constexpr int kABytes = kTileN * kGroup;    // 16 KB
+constexpr int kMaxStagesG = 8;
+constexpr int kMaxBuf = 32;
+constexpr int kSmemBudget = 220 * 1024;
+constexpr unsigned long long kWaitNsG = 2000000000ull;
+constexpr uint32_t kMagicBits = 0x4B400000u;  // 12582912.0f
+constexpr float kMagic = 12582912.0f;
+
+__device__ __forceinline__ uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ unsigned long long gtime() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mb_init(uint64_t* b, uint32_t n) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(b)), "r"(n) : "memory");
+}
+__device__ __forceinline__ void mb_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(b)) : "memory");
+}
+__device__ __forceinline__ void mb_expect(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mb_try(uint64_t* b, uint32_t par) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(saddr(b)), "r"(par)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait of one thread: polls in rounds of 64 tries and reads the
+// clock only between rounds.
+__device__ __forceinline__ bool mb_wait(uint64_t* b, uint32_t par) {
+    unsigned long long t0 = 0;
+    for (;;) {
+        for (int i = 0; i < 64; i++)
+            if (mb_try(b, par)) return true;
+        const unsigned long long t = gtime();
+        if (t0 == 0) t0 = t;
+        else if (t - t0 > kWaitNsG) {
+            atomicOr(&g_gemm_error, 1);
+            return false;
+        }
+    }
+}
+// Warp-uniform bounded wait: lane 0 waits, the outcome is broadcast.
+__device__ __forceinline__ bool warp_wait(uint64_t* b, uint32_t par) {
+    int ok = 1;
+    if ((threadIdx.x & 31) == 0) ok = mb_wait(b, par) ? 1 : 0;
+    return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+// 16-byte global -> shared copy through L2; src_bytes 0 fills zeros.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(saddr(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* b) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(saddr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(saddr(b))
+        : "memory");
+}
+
+// Shared-memory operand descriptor: 128-byte swizzled K-major rows, 8-row
+// groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t addr) {
+    uint64_t d = (uint64_t)((addr >> 4) & 0x3FFF);
+    d |= (uint64_t)(16 >> 4) << 16;
+    d |= (uint64_t)(1024 >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+
+// D (s32, TMEM) = A (s8, 128 x 32, K-major) x B (u8, 32 x BN, K-major).
+template <int BN>
+__device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t da, uint64_t db) {
+    constexpr uint32_t idesc = (2u << 4) | (1u << 7) | (0u << 10) | ((uint32_t)(BN >> 3) << 17) | (8u << 24);
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(idesc), "r"(0)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* b) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(saddr(b))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld8(uint32_t ta, uint32_t* v) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(ta));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+struct GemmGeo {
+    int N, K, M, P;
+    int stages, nbuf;
+};
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kGThreads, 1)
+    gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a,
+                      const GemvParams g, const GemmGeo geo) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t full[kMaxStagesG], empty[kMaxStagesG], tfull[kMaxBuf], tempty[kMaxBuf];
+    __shared__ uint32_t tmem_base_s;
+    __shared__ int bad_s, issued_s, consumed_s, last_commit_s;
+
+    constexpr int kBBytes = BN * kGroup;
+    constexpr int kStage = kABytes + kBBytes;
+    constexpr int kNRd = 4 * kWQ;
+    constexpr int kG = group_blocks(BN);
+    constexpr int kGPS = 4 / kG;  // groups per stage
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int N = geo.N, K = geo.K, S = geo.stages, NB = geo.nbuf;
+    const int n0 = blockIdx.y * kTileN, m0 = blockIdx.x * BN;
+    const int nkg = K / kGroup;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; i++) {
+            mb_init(&full[i], kProdT + 1);  // producer threads + the activation TMA
+            mb_init(&empty[i], 1);
+        }
+        for (int i = 0; i < NB; i++) {
+            mb_init(&tfull[i], 1);
+            mb_init(&tempty[i], kNRd);
+        }
+        bad_s = 0;
+        issued_s = 0;
+        consumed_s = 0;
+        last_commit_s = -1;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == kMma) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(saddr(&tmem_base_s)));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_s;
+
+    if (warp < kProdW) {
+        const int pt = threadIdx.x, prow = pt >> 3, pch = pt & 7;
+        if (pt == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_a)) : "memory");
+        int kg = 0, pub = 0;  // stages issued / published
+        for (; kg < nkg; kg++) {
+            const int s = kg % S;
+            if (kg >= S && !warp_wait(&empty[s], ((kg / S) - 1) & 1)) {
+                if (lane == 0) atomicOr(&bad_s, 1);
+                break;
+            }
+            if (*(volatile int*)&bad_s) break;
+            uint8_t* st = smem + (size_t)s * kStage;
+            const int kb = kg * kGroup;
+            const int pan = kb / geo.P;
+            if (pt == 0) {
+                // rows 0-63 of the weight tile by TMA, the activation tile by TMA
+                mb_expect(&full[s], kBBytes + kTmaRows * kGroup);
+                tma_2d(st, &tm_w, kb - pan * geo.P, pan * N + n0, &full[s]);
+                tma_2d(st + kABytes, &tm_a, kb, m0, &full[s]);
+            }
+            const int8_t* src = g.w + (size_t)pan * N * geo.P + (kb - pan * geo.P) + pch * 16;
+#pragma unroll
+            for (int i = kTmaRows / 16; i < kTileN / 16; i++) {
+                const int row = prow + 16 * i, n = n0 + row;
+                const bool in = n < N;
+                cp_async16(st + row * kGroup + pch * 16, src + (size_t)(in ? n : 0) * geo.P, in ? 16u : 0u);
+            }
+            cp_async_commit();
+            if (kg - pub >= kInFlight - 1) {
+                cp_async_wait<kInFlight - 1>();
+                fence_async_smem();
+                mb_arrive(&full[pub % S]);
+                pub++;
+            }
+        }
+        cp_async_wait<0>();
+        fence_async_smem();
+        for (; pub < kg; pub++) mb_arrive(&full[pub % S]);
+        if (pt == 0) issued_s = kg;
+    } else if (warp == kMma) {
+        if (lane == 0) {
+            int kg = 0;
+            for (; kg < nkg; kg++) {
+                const int s = kg % S;
+                if (!mb_wait(&full[s], (kg / S) & 1)) {
+                    atomicOr(&bad_s, 1);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a_addr = saddr(smem + (size_t)s * kStage);
+                bool ok = true;
+                for (int gs = 0; gs < kGPS && ok; gs++) {
+                    const int gi = kg * kGPS + gs, t = gi % NB;
+                    if (gi >= NB && !mb_wait(&tempty[t], ((gi / NB) - 1) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    for (int jj = 0; jj < kG; jj++) {
+                        const int j = gs * kG + jj;
+                        umma_i8<BN>(tmem + (uint32_t)((t * kG + jj) * BN), desc_sw128(a_addr + 32 * j),
+                                    desc_sw128(a_addr + kABytes + 32 * j));
+                    }
+                    umma_commit(&tfull[t]);
+                }
+                umma_commit(&empty[s]);
+                last_commit_s = kg;
+                if (!ok) {
+                    atomicOr(&bad_s, 1);
+                    kg++;
+                    break;
+                }
+            }
+            consumed_s = kg;
+        }
+    } else {
+        // readout warps: TMEM lanes of quadrant (warp % 4), 1 / kWQ of the columns
+        const int q = warp & 3, part = (warp - kRd0) >> 2;  // warps 5-12: quadrants 1, 2, 3, 0, 1, 2, 3, 0
+        constexpr int kCols = BN / kWQ;
+        static_assert(kCols % 8 == 0, "TMEM loads move 8 columns");
+        const int c0 = part * kCols;
+        const int n = n0 + 32 * q + lane;
+        const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0;
+        float acc[kCols];
+#pragma unroll
+        for (int j = 0; j < kCols; j++) acc[j] = 0.0f;
+        // fp16 block scales of row n: four per K-group, prefetched one group ahead
+        const bool live = n < N;
+        auto load_sc = [&](int kg) -> uint2 {
+            if (!live || kg >= nkg) return make_uint2(0u, 0u);
+            return __ldg(reinterpret_cast<const uint2*>(g.sblk + tiled_s_off(N, geo.P, n, kg * 4)));
+        };
+        constexpr int kV = kG * kCols;  // registers per group
+        uint32_t va[kV], vb[kV];
+        auto ld_grp = [&](int gi, uint32_t* v) {
+            const uint32_t base = tq + (uint32_t)((gi % NB) * kG * BN);
+#pragma unroll
+            for (int jj = 0; jj < kG; jj++)
+#pragma unroll
+                for (int c = 0; c < kCols; c += 8) tmem_ld8(base + (uint32_t)(jj * BN + c), v + jj * kCols + c);
+        };
+        auto scale_add = [&](const uint32_t* v, float d) {
+            const float nmd = __fmul_rn(-kMagic, d);  // exact: 3 * 2^22 * d
+#pragma unroll
+            for (int c = 0; c < kCols; c++)
+                acc[c] = __fadd_rn(acc[c], __fmaf_rn(__uint_as_float(v[c] + kMagicBits), d, nmd));
+        };
+        const int ngrp = nkg * kGPS;
+        // the scales of the groups gi and gi + 1 (kG / 2 stages of four)
+        // a pair of groups covers 2 G blocks from block gi G: kSPP stages of four
+        // scales, starting at offset (gi G) % 4 of the first
+        constexpr int kSPP = (2 * kG + 3) / 4;
+        auto load_pair_sc = [&](int gi, uint2* sc) {
+#pragma unroll
+            for (int i = 0; i < kSPP; i++) sc[i] = load_sc((gi * kG) / 4 + i);
+        };
+        auto sc_of = [&](const uint2* sc, int k) -> float {  // block k, counted from the first stage's start
+            const uint32_t w = (k & 2) ? sc[k >> 2].y : sc[k >> 2].x;
+            const __half2 h = *reinterpret_cast<const __half2*>(&w);
+            return (k & 1) ? __high2float(h) : __low2float(h);
+        };
+        // one group: start the next group's load, free this group's buffer,
+        // scale and add its blocks, then wait for the load
+        auto step = [&](int gi, const uint32_t* cur, uint32_t* nxt, const uint2* sc, int k0) -> bool {
+            const bool more = gi + 1 < ngrp;
+            if (more) {
+                if (!warp_wait(&tfull[(gi + 1) % NB], ((gi + 1) / NB) & 1)) return false;
+                tc_fence_after();
+                ld_grp(gi + 1, nxt);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mb_arrive(&tempty[gi % NB]);
+#pragma unroll
+            for (int jj = 0; jj < kG; jj++) scale_add(cur + jj * kCols, sc_of(sc, k0 + jj));
+            if (more) tmem_wait_ld();
+            return true;
+        };
+        bool bad = !warp_wait(&tfull[0], 0);
+        if (!bad) {
+            tc_fence_after();
+            ld_grp(0, va);
+            tmem_wait_ld();
+        }
+        uint2 sc_next[kSPP];
+        load_pair_sc(0, sc_next);
+        for (int gi = 0; gi < ngrp && !bad; gi += 2) {
+            uint2 sc[kSPP];
+#pragma unroll
+            for (int i = 0; i < kSPP; i++) sc[i] = sc_next[i];
+            if (gi + 2 < ngrp) load_pair_sc(gi + 2, sc_next);
+            const int o = (gi * kG) & 3;
+            if (!step(gi, va, vb, sc, o)) bad = true;
+            else if (gi + 1 < ngrp && !step(gi + 1, vb, va, sc, o + kG)) bad = true;
+        }
+        if (bad) {
+            if (lane == 0) atomicOr(&bad_s, 1);
+        } else {
+#pragma unroll
+            for (int c = 0; c < kCols; c++) {
+                const float y = __fdiv_rn(acc[c], 127.0f);
+                const float y1 = __shfl_xor_sync(0xffffffffu, y, 1);
+                const int m = m0 + c0 + c;
+                if ((lane & 1) == 0 && live && m < geo.M) pair_epilogue<EPI>(g, m, n, n + 1 < N, y, y1, nullptr);
+            }
+        }
+    }
+    __syncthreads();
+    if (bad_s) {
+        // drain: copies issued but not consumed, and the MMAs of the last commit
+        // (producer threads drained their own copies with cp.async.wait_group 0)
+        if (warp == kMma && lane == 0 && last_commit_s >= 0)
+            (void)mb_wait(&empty[last_commit_s % S], (last_commit_s / S) & 1);
+        __syncthreads();
+    }
+    if (warp == kMma) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+    }
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)p;
+    }
+    return fn;
+}
+
+// 2-D u8 map: inner extent `inner` bytes, `rows` rows `stride` bytes apart,
+// box {128 bytes, box_rows}.
+bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t stride, uint32_t box_rows,
+              bool swizzle) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {inner, rows};
+    const cuuint64_t strides[1] = {stride};
+    const cuuint32_t box[2] = {(cuuint32_t)kGroup, box_rows};
+    const cuuint32_t es[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, int EPI>
+cudaError_t launch_bn(const CUtensorMap& tw, const CUtensorMap& ta, const GemvParams& g, int M, cudaStream_t s) {
+    constexpr int stage = kABytes + BN * kGroup;
+    GemmGeo geo;
+    geo.N = g.N;
+    geo.K = g.K;
+    geo.M = M;
+    geo.P = g.P;
+    geo.stages = std::min(kMaxStagesG, (kSmemBudget - 1024) / stage);
+    if (geo.stages < kInFlight + 1) return cudaErrorInvalidConfiguration;
+    geo.nbuf = 512 / (group_blocks(BN) * BN);
+    const size_t smem = (size_t)geo.stages * stage + 1024;
+    auto kern = gemm_i8_tc_kernel<BN, EPI>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    const dim3 grid((M + BN - 1) / BN, (g.N + kTileN - 1) / kTileN);
+    kern<<<grid, kGThreads, smem, s>>>(tw, ta, g, geo);
+    return cudaGetLastError();
+}
+
+template <int EPI>
+cudaError_t launch_epi(const CUtensorMap& tw, const CUtensorMap& ta, const GemvParams& g, int M, int BN,
+                       cudaStream_t s) {
+    switch (BN) {
+        case 16: return launch_bn<16, EPI>(tw, ta, g, M, s);
+        case 32: return launch_bn<32, EPI>(tw, ta, g, M, s);
+        default: return launch_bn<64, EPI>(tw, ta, g, M, s);
+    }
+}
+
+}  // namespace
+
+bool gemm_tc_supported(const GemvParams& g, int epi) {
+    if (epi != EPI_STORE && epi != EPI_RESID && epi != EPI_QKV && epi != EPI_SWIGLU) return false;
+    if (g.P == 0 || g.K % kGroup || g.P % kGroup || g.N % 16 || g.row0 != 0 || g.dyn_M || g.x) return false;
+    if (((uintptr_t)g.aq & 15) || ((uintptr_t)g.w & 15) || ((uintptr_t)g.sblk & 7)) return false;
+    return encode_fn() != nullptr;
+}
+
+// Tile width: the candidate (16, 32 or 64 rows: one TMEM group of 64
+// columns per readout round trip fits the readout threads' registers) with
+// the least modelled time = waves x per-tile time. Per-tile time grows with
+// BN (the per-element scaling of each block runs on the CUDA cores): measured
+// 1 : 1.45 : 2.75 for BN = 16 : 32 : 64 on B200. Narrow tiles also spread
+// small-N layers over more SMs (their weight tiles are then re-read from L2).
+int pick_bn(int M, int N) {
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (sms <= 0) sms = 148;
+    }
+    const int ntiles = (N + kTileN - 1) / kTileN;
+    const int cand[3] = {16, 32, 64};
+    const double cost[3] = {1.0, 1.45, 2.75};
+    int best = 64;
+    double best_t = 1e30;
+    for (int i = 0; i < 3; i++) {
+        const int bn = cand[i];
+        const int mt = (M + bn - 1) / bn;
+        const int waves = (ntiles * mt + sms - 1) / sms;
+        const double t = waves * cost[i];
+        if (t < best_t - 1e-9) {
+            best_t = t;
+            best = bn;
+        }
+        if (bn >= M) break;
+    }
+    return best;
+}
+
+cudaError_t launch_gemm_tc(const GemvParams& g, int epi, int M, cudaStream_t s) {
+    if (M <= 0) return cudaSuccess;
+    const int BN = pick_bn(M, g.N);
+    CUtensorMap tw, ta;
+    const int npan = g.K / g.P;
+    if (!make_map(&tw, g.w, (uint64_t)g.P, (uint64_t)g.N * npan, (uint64_t)g.P, kTmaRows, false) ||
+        !make_map(&ta, g.aq, (uint64_t)g.K, (uint64_t)M, (uint64_t)g.K, (uint32_t)BN, true))
+        return cudaErrorInvalidValue;
+    switch (epi) {
+        case EPI_STORE: return launch_epi<EPI_STORE>(tw, ta, g, M, BN, s);
+        case EPI_RESID: return launch_epi<EPI_RESID>(tw, ta, g, M, BN, s);
+        case EPI_QKV: return launch_epi<EPI_QKV>(tw, ta, g, M, BN, s);
+        case EPI_SWIGLU: return launch_epi<EPI_SWIGLU>(tw, ta, g, M, BN, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+int take_gemm_error() {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_gemm_error, sizeof(int)) != cudaSuccess) return -1;
+    if (v) {
+        const int z = 0;
+        cudaMemcpyToSymbol(g_gemm_error, &z, sizeof(int));
+    }
+    return v;
+}
+
+}  // namespace fl

@@ -20,6 +20,7 @@
 //     and reduces across warps once per 16-row tile;
 //   * every mbarrier wait is bounded (fl_tma.cuh).
 #include "fl_common.cuh"
+#include "fl_epilogue.cuh"
 #include "fl_kernels.h"
 #include "fl_layout.cuh"
 #include "fl_tma.cuh"
@@ -88,58 +89,6 @@ __device__ __forceinline__ void mma_u8s8(uint32_t a0, uint32_t a2, uint32_t b0, 
         "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
         : "=r"(d0), "=r"(d1), "=r"(c2), "=r"(c3)
         : "r"(a0), "r"(0), "r"(a2), "r"(0), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
-}
-
-// Epilogue of one weight-row pair (n0, n0 + 1) for activation row r.
-template <int EPI>
-__device__ __forceinline__ void pair_epilogue(const GemvParams& p, int r, int n0, bool has1, float y0, float y1,
-                                              unsigned long long* best_s) {
-    if (EPI == EPI_STORE || EPI == EPI_LOGITS) {
-        p.out[(size_t)r * p.ldo + n0] = y0;
-        if (has1) p.out[(size_t)r * p.ldo + n0 + 1] = y1;
-        if (EPI == EPI_LOGITS) {
-            unsigned long long k = argmax_key(y0, n0);
-            if (has1) {
-                const unsigned long long k1 = argmax_key(y1, n0 + 1);
-                k = k1 > k ? k1 : k;
-            }
-            atomicMax(&best_s[r - p.row0], k);
-        }
-    } else if (EPI == EPI_RESID) {
-        float* o = p.out + (size_t)r * p.ldo + n0;
-        o[0] = __fadd_rn(o[0], y0);
-        if (has1) o[1] = __fadd_rn(o[1], y1);
-    } else if (EPI == EPI_QKV) {
-        float v0 = y0, v1 = y1;
-        const int qkd = p.q_dim + p.kv_dim;
-        if (n0 < qkd) {
-            // inference.c:165-173 adjacent-pair rotation at position pos[r]
-            const int ii = (n0 < p.q_dim ? n0 : n0 - p.q_dim) % p.head_dim;
-            const float freq = __fdiv_rn(1.0f, powf(p.theta, __fdiv_rn((float)ii, (float)p.head_dim)));
-            const float ang = __fmul_rn((float)p.pos[r], freq);
-            float sn, cs;
-            sincosf(ang, &sn, &cs);
-            v0 = __fsub_rn(__fmul_rn(y0, cs), __fmul_rn(y1, sn));
-            v1 = __fadd_rn(__fmul_rn(y0, sn), __fmul_rn(y1, cs));
-        }
-        if (n0 < p.q_dim) {
-            p.q_out[(size_t)r * p.q_dim + n0] = v0;
-            p.q_out[(size_t)r * p.q_dim + n0 + 1] = v1;
-        } else {
-            const bool is_k = n0 < qkd;
-            const int c = n0 - (is_k ? p.q_dim : qkd);
-            const int h = c / p.head_dim;
-            const int dd = c - h * p.head_dim;
-            const int slot = *p.slot_base + r;
-            const int page = p.block_table[slot / kPageSize];
-            const size_t off = (((size_t)page * p.kv_heads + h) * kPageSize + (slot % kPageSize)) * p.head_dim + dd;
-            *reinterpret_cast<__half2*>((is_k ? p.kv.k : p.kv.v) + off) = __floats2half2_rn(v0, v1);
-        }
-    } else if (EPI == EPI_SWIGLU) {
-        // rows (n0, n0 + 1) = (gate_i, up_i): activations_avx2.c:86-105
-        const float h = __fmul_rn(__fmul_rn(y0, poly_sigmoid(y0)), y1);
-        p.hq[(size_t)r * p.F + (n0 >> 1)] = (uint8_t)quant_u8(h);
-    }
 }
 
 template <int MMAX, int EPI, bool MMA>
@@ -395,7 +344,8 @@ int take_device_error() {
         const int z = 0;
         cudaMemcpyToSymbol(g_fl_error, &z, sizeof(int));
     }
-    return v;
+    const int w = take_gemm_error();
+    return w < 0 ? w : (v | w);
 }
 
 bool tma_gemv_supported(int N, int K, int M) {

@@ -149,6 +149,8 @@ static int tensor_params(const dequantized_tensor_t* B, int N, int K, GemvParams
     return FL_OK;
 }
 
+static int scratch_q(size_t bytes, uint8_t** out);
+
 static int run_gemv_chunks(const uint8_t* Aq, const dequantized_tensor_t* B, float* C, int32_t* D,
                            int M, int N, int K, cudaStream_t s, int epi, const float* X = nullptr) {
     GemvParams p = {};
@@ -159,6 +161,25 @@ static int run_gemv_chunks(const uint8_t* Aq, const dequantized_tensor_t* B, flo
     p.out = C;
     p.ldo = N;
     p.dots = D;
+    if (M > 2 * kMaxRows && epi == EPI_STORE && d->scale_block == 32 && d->P != 0) {
+        // many rows: quantize once, then the tcgen05 GEMM reads every weight once
+        GemvParams h = p;
+        h.x = nullptr;
+        uint8_t* q = const_cast<uint8_t*>(Aq);
+        if (!q) {
+            FL_CHECK(scratch_q((size_t)M * K, &q));
+            FL_CHECK(fl_cuda_act_quant(X, q, M, K, 0, 0.0f, s));
+        }
+        h.aq = q;
+        h.row0 = 0;
+        h.M = M;
+        if (gemm_tc_supported(h, epi)) {
+            FL_CHECK_CUDA(launch_gemm_tc(h, epi, M, s));
+            return FL_OK;
+        }
+        p.aq = q;
+        p.x = nullptr;
+    }
     for (int r0 = 0; r0 < M; r0 += kMaxRows) {
         p.row0 = r0;
         p.M = M - r0 < kMaxRows ? M - r0 : kMaxRows;

@@ -74,16 +74,19 @@ __device__ __forceinline__ bool mb_try(uint64_t* b, uint32_t par) {
         : "memory");
     return ok != 0;
 }
+// Polls in rounds of 64 tries; the clock (a slow read) only between rounds.
 __device__ __forceinline__ bool mb_wait(uint64_t* b, uint32_t par, int* err) {
-    if (mb_try(b, par)) return true;
-    const unsigned long long t0 = gtime();
-    while (!mb_try(b, par)) {
-        if (gtime() - t0 > kWaitNs) {
+    unsigned long long t0 = 0;
+    for (;;) {
+        for (int i = 0; i < 64; i++)
+            if (mb_try(b, par)) return true;
+        const unsigned long long t = gtime();
+        if (t0 == 0) t0 = t;
+        else if (t - t0 > kWaitNs) {
             atomicOr(err, kErrRing);
             return false;
         }
     }
-    return true;
 }
 __device__ __forceinline__ void bulk(void* dst, const void* src, uint32_t bytes, uint64_t* b) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -119,8 +122,9 @@ __device__ bool grid_sync(unsigned long long* ctr, unsigned long long target, in
         int ok = 1;
         if (ld_acquire(ctr) < target) {
             const unsigned long long t0 = gtime();
-            while (ld_acquire(ctr) < target) {
-                if (gtime() - t0 > kWaitNs) {
+            for (bool open = false; !open;) {
+                for (int i = 0; i < 16 && !open; i++) open = ld_acquire(ctr) >= target;
+                if (!open && gtime() - t0 > kWaitNs) {
                     ok = 0;
                     atomicOr(err, kErrGrid);
                     break;

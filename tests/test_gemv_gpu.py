@@ -90,6 +90,22 @@ def test_block_mode_larger_m(gpu, orc, N, K, M):
     assert_block_close(got, orc.matmul_block(A, w, d))
 
 
+@pytest.mark.parametrize("N,K", SHAPES)
+@pytest.mark.parametrize("M", [17, 24, 33, 65, 129, 256])
+def test_tcgen05_gemm_bit_exact(gpu, orc, N, K, M):
+    """More than 16 rows run through the tcgen05 INT8 GEMM: its block-scaled
+    result is bit-identical to the oracle's sequential block order, on every
+    config shape (two weight panels at K = 8192, a partial 128-row tile at
+    N = 32064) and ragged row counts."""
+    lib = gpu
+    w, d = lib.synth_q4_0_i8(13, 3000 + N + K, N, K)
+    A = np.random.default_rng(M * 3 + K).standard_normal((M, K)).astype(np.float32)
+    got = gpu_matmul(lib, A, block_tensor(w, d), N)
+    want = orc.matmul_block(A, w, d)
+    bad = np.argwhere(got != want)
+    assert bad.size == 0, f"{len(bad)} outputs differ, first {bad[:3].tolist()}: {got[tuple(bad[0])]} vs {want[tuple(bad[0])]}"
+
+
 @pytest.mark.parametrize("M,N,K", [(1, 9216, 3072), (5, 3072, 8192), (3, 37, 96), (8, 1, 32), (9, 64, 64)])
 def test_block_dots_bit_exact(gpu, orc, M, N, K):
     lib = gpu
