@@ -16,6 +16,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <climits>
 #include <string>
 #include <vector>
 
@@ -114,6 +115,7 @@ struct fl_engine {
     uint32_t* samp_p = nullptr;            // [kMaxRows, V] target nucleus weights
     unsigned long long* samp_m = nullptr;  // [kMaxDraft + kMaxRows] kept masses (draft, then target)
     unsigned long long* samp_r = nullptr;  // [V] rejection residual weights
+    uint32_t* samp_key = nullptr;          // [2] Philox seed, sequence id
     // post-prefill draft state of step 0: its mass, weights and traced logits
     // (8 + 4V + 4V bytes)
     unsigned char* samp_snap = nullptr;
@@ -405,8 +407,7 @@ StepBuffers step_buffers(fl_engine* e) {
     b.V = e->V;
     b.temp = e->samp_T;
     b.top_p = e->samp_top_p;
-    b.seed = e->samp_seed;
-    b.seq_id = e->samp_seq;
+    b.key = e->samp_key;
     b.qd = e->samp_q;
     b.qm = e->samp_m;
     b.pt = e->samp_p;
@@ -786,7 +787,7 @@ FL_API void fl_engine_destroy(fl_engine_t* e) {
     void* bufs[] = {e->embed, e->x, e->x2, e->xq, e->q, e->aq, e->hq, e->logits, e->amax, e->x_v, e->x_d,
                     e->iota, e->tok, e->mask, e->st, e->st_snap, e->xd0_snap, e->seq, e->out, e->acc,
                     e->last_feat, e->attn_part, e->attn_cnt, e->step_bar, e->d_phases, e->d_trace,
-                    e->samp_q, e->samp_p, e->samp_r, e->samp_trace, e->samp_snap, e->samp_m};
+                    e->samp_q, e->samp_p, e->samp_r, e->samp_trace, e->samp_snap, e->samp_m, e->samp_key};
     for (void* p : bufs) cudaFree(p);
     for (auto& ev : e->ev)
         if (ev) cudaEventDestroy(ev);
@@ -1023,19 +1024,35 @@ FL_API int fl_engine_set_sampling(fl_engine_t* e, float temperature, float top_p
     const bool samp = temperature > 0.0f;
     if (samp == e->samp && (!samp || (temperature == e->samp_T && top_p == e->samp_top_p &&
                                       seed == e->samp_seed && seq_id == e->samp_seq)))
-        return FL_OK;  // unchanged: keep the recorded step graph
+        return FL_OK;  // unchanged
+    if (samp && e->samp && temperature == e->samp_T && top_p == e->samp_top_p) {
+        // a new key only: the step graph reads it from device memory; the
+        // post-prefill state was drawn with the old key, so prefill again
+        const uint32_t key[2] = {seed, seq_id};
+        FL_CHECK_CUDA(cudaMemcpyAsync(e->samp_key, key, sizeof(key), cudaMemcpyHostToDevice, e->s));
+        FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
+        e->samp_seed = seed;
+        e->samp_seq = seq_id;
+        e->spec_ready = 0;
+        return FL_OK;
+    }
     if (samp && !e->samp_q) {
         FL_CHECK_CUDA(cudaMalloc(&e->samp_q, sizeof(uint32_t) * (size_t)kMaxDraft * e->V));
         FL_CHECK_CUDA(cudaMalloc(&e->samp_p, sizeof(uint32_t) * (size_t)kMaxRows * e->V));
         FL_CHECK_CUDA(cudaMalloc(&e->samp_m, sizeof(unsigned long long) * (kMaxDraft + kMaxRows)));
         FL_CHECK_CUDA(cudaMalloc(&e->samp_r, sizeof(unsigned long long) * (size_t)e->V));
         FL_CHECK_CUDA(cudaMalloc(&e->samp_snap, 8 + (size_t)8 * e->V));
+        FL_CHECK_CUDA(cudaMalloc(&e->samp_key, sizeof(uint32_t) * 2));
     }
     e->samp = samp;
     e->samp_T = samp ? temperature : 0.0f;
     e->samp_top_p = samp ? top_p : 1.0f;
     e->samp_seed = seed;
     e->samp_seq = seq_id;
+    if (samp) {
+        const uint32_t key[2] = {seed, seq_id};
+        FL_CHECK_CUDA(cudaMemcpy(e->samp_key, key, sizeof(key), cudaMemcpyHostToDevice));
+    }
     return drop_step_graph(e);
 }
 
@@ -1161,6 +1178,38 @@ FL_API int fl_engine_spec_generate(fl_engine_t* e, const int* prompt, int P, int
                                    int* out, int* acc_hist, int* steps) {
     FL_CHECK(fl_engine_spec_prefill(e, prompt, P, K, max_acc));
     return fl_engine_spec_decode(e, n_new, out, acc_hist, steps);
+}
+
+FL_API int fl_engine_spec_generate_batch(fl_engine_t* e, const int* prompts, int P, int nseq, const unsigned* seq_ids,
+                                         int n_new, int K, int* out, int* steps) {
+    FL_CHECK(check_ready(e, true));
+    if (!prompts || !out || nseq <= 0 || P <= 0 || n_new <= 0) return set_error(FL_E_INVAL, "spec_generate_batch: bad arguments");
+    const float T = e->samp_T, top_p = e->samp_top_p;
+    const unsigned seed = e->samp_seed;
+    cudaEvent_t t0 = nullptr, t1 = nullptr;
+    FL_CHECK_CUDA(cudaEventCreate(&t0));
+    FL_CHECK_CUDA(cudaEventCreate(&t1));
+    struct Ev {
+        cudaEvent_t a, b;
+        ~Ev() { cudaEventDestroy(a); cudaEventDestroy(b); }
+    } ev_guard{t0, t1};
+    FL_CHECK_CUDA(cudaEventRecord(t0, e->s));
+    long long total = 0;
+    for (int i = 0; i < nseq; i++) {
+        // one sequence after another; each draws from its own Philox stream
+        if (T > 0.0f) FL_CHECK(fl_engine_set_sampling(e, T, top_p, seed, seq_ids ? seq_ids[i] : (unsigned)i));
+        int st = 0;
+        FL_CHECK(fl_engine_spec_generate(e, prompts + (size_t)i * P, P, n_new, K, -1, out + (size_t)i * n_new, nullptr,
+                                         &st));
+        if (steps) steps[i] = st;
+        total += st;
+    }
+    FL_CHECK_CUDA(cudaEventRecord(t1, e->s));
+    FL_CHECK_CUDA(cudaEventSynchronize(t1));
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, t0, t1);
+    e->t_total_us = ms * 1000.0;
+    return (int)std::min<long long>(total, INT_MAX);
 }
 
 FL_API int fl_engine_last_timing(const fl_engine_t* e, double* draft_us, double* verify_us, double* total_us) {

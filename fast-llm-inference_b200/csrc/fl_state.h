@@ -50,7 +50,7 @@ struct StepBuffers {
     const float* logits;    // [kMaxRows, V]
     int V;
     float temp, top_p;
-    uint32_t seed, seq_id;
+    const uint32_t* key;    // device [2]: Philox seed, sequence id (set without re-recording)
     uint32_t* qd;           // [kMaxDraft, V] draft weights
     unsigned long long* qm; // [kMaxDraft]
     uint32_t* pt;           // [kMaxRows, V] target weights

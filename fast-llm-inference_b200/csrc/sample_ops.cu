@@ -230,7 +230,7 @@ __global__ void __launch_bounds__(kST) sample_first_kernel(StepBuffers b, int P)
     __shared__ unsigned long long red[kSW];
     trace_row(b, 2 * kMaxRows - 1, b.logits);
     const unsigned long long M = nucleus(b.logits, b.V, b.temp, b.top_p, b.pt, red);
-    const int t = draw(b.pt, b.V, M, philox_u24(b.seed, b.seq_id, 0xFFFFFFFFu, (uint32_t)P, 2u));
+    const int t = draw(b.pt, b.V, M, philox_u24(b.key[0], b.key[1], 0xFFFFFFFFu, (uint32_t)P, 2u));
     if (threadIdx.x == 0) b.seq[P] = t;
 }
 
@@ -246,7 +246,7 @@ __global__ void __launch_bounds__(kST) sample_pick_kernel(StepBuffers b, int j) 
     uint32_t* q = b.qd + (size_t)j * b.V;
     trace_row(b, j, b.logits);
     const unsigned long long M = nucleus(b.logits, b.V, b.temp, b.top_p, q, red);
-    const int tok = draw(q, b.V, M, philox_u24(b.seed, b.seq_id, (uint32_t)st->steps, (uint32_t)(n + 1 + j), 0u));
+    const int tok = draw(q, b.V, M, philox_u24(b.key[0], b.key[1], (uint32_t)st->steps, (uint32_t)(n + 1 + j), 0u));
     if (j + 1 < st->K) {
         const int g_row = (j == 0) ? st->last_row : 0;
         const float* g = b.x_d + (size_t)g_row * b.d;
@@ -296,13 +296,13 @@ __global__ void __launch_bounds__(kST) accept_sampled_kernel(StepBuffers b, int 
         const uint32_t* p = b.pt + (size_t)a * b.V;
         const unsigned long long Mp = b.pm[a];
         if (a == cap) {
-            last = draw(p, b.V, Mp, philox_u24(b.seed, b.seq_id, step, pos, 2u));
+            last = draw(p, b.V, Mp, philox_u24(b.key[0], b.key[1], step, pos, 2u));
             break;
         }
         const int x = st->drafted[a];
         const uint32_t* q = b.qd + (size_t)a * b.V;
         const unsigned long long Mq = b.qm[a];
-        const uint32_t U = philox_u24(b.seed, b.seq_id, step, pos, 1u);
+        const uint32_t U = philox_u24(b.key[0], b.key[1], step, pos, 1u);
         if ((u128)U * Mp * q[x] < (((u128)p[x] * Mq) << 24)) {
             a++;
             continue;
@@ -315,7 +315,7 @@ __global__ void __launch_bounds__(kST) accept_sampled_kernel(StepBuffers b, int 
             s += y;
         }
         const unsigned long long zr = bsum64(s, red);
-        const uint32_t Ur = philox_u24(b.seed, b.seq_id, step, pos, 2u);
+        const uint32_t Ur = philox_u24(b.key[0], b.key[1], step, pos, 2u);
         last = zr > 0 ? draw(b.resid, b.V, zr, Ur) : draw(p, b.V, Mp, Ur);
         break;
     }

@@ -122,6 +122,7 @@ _SIGS = {
     "fl_engine_spec_prefill": (I, [VP, VP, I, I, I]),
     "fl_engine_spec_decode": (I, [VP, I, VP, VP, VP]),
     "fl_engine_set_sampling": (I, [VP, F, F, U32, U32]),
+    "fl_engine_spec_generate_batch": (I, [VP, VP, I, I, VP, I, I, VP, VP]),
     "fl_engine_get_sampling": (I, [VP, VP, VP, VP, VP]),
     "fl_engine_sample_trace_enable": (I, [VP, I]),
     "fl_engine_sample_trace": (I, [VP, VP, VP, VP, VP, VP, VP]),
@@ -332,6 +333,20 @@ class Engine:
     def spec_generate(self, prompt, n_new, k, max_acc=-1):
         self.spec_prefill(prompt, k, max_acc)
         return self.spec_decode(n_new)
+
+    def spec_generate_batch(self, prompts, n_new, k, seq_ids=None):
+        """Decodes independent sequences (rows of `prompts`) one after another
+        under the current rule; returns (tokens [nseq, n_new], steps [nseq],
+        device seconds of the whole call)."""
+        pr = np.ascontiguousarray(prompts, np.int32)
+        nseq, P = pr.shape
+        ids = None if seq_ids is None else np.ascontiguousarray(seq_ids, np.uint32)
+        out = np.empty((nseq, n_new), np.int32)
+        steps = np.empty(nseq, np.int32)
+        rc = self.lib.fl_engine_spec_generate_batch(self.h, ptr(pr), P, nseq, ptr(ids), n_new, k, ptr(out), ptr(steps))
+        if rc < 0:
+            self.lib.check(rc, "spec_generate_batch")
+        return out, steps, self.last_timing()[2] * 1e-6
 
     def set_sampling(self, temperature, top_p=1.0, seed=0, seq_id=0):
         """temperature <= 0: greedy; > 0: Philox-keyed rejection sampling

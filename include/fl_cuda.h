@@ -192,6 +192,17 @@ int fl_engine_spec_generate(fl_engine_t* e, const int* prompt, int prompt_len,
                             int n_new, int k, int max_accepted, int* out,
                             int* acc_hist, int* steps);
 
+/* Independent sequences on one engine (one rank's share of a batch): for each
+ * i < nseq, prompts[i * prompt_len ..] is decoded for n_new tokens with draft
+ * length k into out[i * n_new ..], under the rule of fl_engine_set_sampling
+ * with sequence id seq_ids[i] (i when seq_ids is NULL), so every sequence's
+ * stream is the same wherever and alongside whatever it runs. steps[i]
+ * (may be NULL) receives the speculative steps of sequence i. Returns the
+ * total number of steps or a negative FL_E_* code; fl_engine_last_timing's
+ * total_us is the device time of the whole call, prefills included. */
+int fl_engine_spec_generate_batch(fl_engine_t* e, const int* prompts, int prompt_len, int nseq,
+                                  const unsigned* seq_ids, int n_new, int k, int* out, int* steps);
+
 /* Decoding rule of the next fl_engine_spec_prefill / spec_generate.
  * temperature <= 0: greedy (argmax drafts, exact-match acceptance; the
  * default). temperature > 0: stochastic speculative decoding

@@ -435,3 +435,25 @@ def test_speculative_generate_sampled_reference_api(gpu, orc):
     assert_stream_matches(out, g_want, margins)
     gpu.draft_model_free(dm)
     eng.close()
+
+
+def test_sampled_batch_independent_of_sharding(small):
+    """A sequence's sampled stream depends only on its prompt and id: the batch
+    entry point, single decodes and any split of the ids give the same tokens."""
+    import shard
+    dims, eng, om, embed = small
+    ids = np.arange(4, dtype=np.uint32)
+    prompts = shard.prompts_for(ids, 12, dims["vocab"], 77)
+    try:
+        eng.set_sampling(SAMPLE_T, SAMPLE_TOP_P, SAMPLE_SEED)
+        all_toks, steps, secs = eng.spec_generate_batch(prompts, 20, 4, seq_ids=ids)
+        part, _, _ = eng.spec_generate_batch(prompts[2:], 20, 4, seq_ids=ids[2:])
+        singles = []
+        for i in ids:
+            eng.set_sampling(SAMPLE_T, SAMPLE_TOP_P, SAMPLE_SEED, int(i))
+            singles.append(eng.spec_generate(prompts[i], 20, 4)[0])
+    finally:
+        eng.set_sampling(0.0)
+    assert np.array_equal(all_toks, np.stack(singles))
+    assert np.array_equal(part, all_toks[2:])
+    assert len({tuple(r) for r in all_toks.tolist()}) == 4 and secs > 0 and steps.min() >= 1
