@@ -62,6 +62,7 @@ constexpr int kMaxStagesG = 8;
 constexpr int kMaxBuf = 32;
 constexpr int kSmemBudget = 220 * 1024;
 constexpr unsigned long long kWaitNsG = 2000000000ull;
+constexpr uint32_t kSuspendNs = 1000000;  // try_wait suspend-time hint (a bound; completion wakes earlier)
 constexpr uint32_t kMagicBits = 0x4B400000u;  // 12582912.0f
 constexpr float kMagic = 12582912.0f;
 
@@ -80,29 +81,29 @@ __device__ __forceinline__ void mb_arrive(uint64_t* b) {
 __device__ __forceinline__ void mb_expect(uint64_t* b, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(b)), "r"(bytes) : "memory");
 }
+// try_wait with a suspend-time hint: a thread whose phase has not completed
+// sleeps (up to the hint, woken when the phase completes) instead of spinning,
+// leaving the issue slots to the warps that do the work.
 __device__ __forceinline__ bool mb_try(uint64_t* b, uint32_t par) {
     uint32_t ok;
     asm volatile(
-        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(saddr(b)), "r"(par)
+        : "r"(saddr(b)), "r"(par), "r"(kSuspendNs)
         : "memory");
     return ok != 0;
 }
-// Bounded wait of one thread: polls in rounds of 64 tries and reads the
-// clock only between rounds.
+// Bounded wait of one thread: the clock is read between suspended tries.
 __device__ __forceinline__ bool mb_wait(uint64_t* b, uint32_t par) {
-    unsigned long long t0 = 0;
-    for (;;) {
-        for (int i = 0; i < 64; i++)
-            if (mb_try(b, par)) return true;
-        const unsigned long long t = gtime();
-        if (t0 == 0) t0 = t;
-        else if (t - t0 > kWaitNsG) {
+    if (mb_try(b, par)) return true;
+    const unsigned long long t0 = gtime();
+    while (!mb_try(b, par))
+        if (gtime() - t0 > kWaitNsG) {
             atomicOr(&g_gemm_error, 1);
             return false;
         }
-    }
+    return true;
 }
 // Warp-uniform bounded wait: lane 0 waits, the outcome is broadcast.
 __device__ __forceinline__ bool warp_wait(uint64_t* b, uint32_t par) {
