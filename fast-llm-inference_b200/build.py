@@ -78,7 +78,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
                     print(log)
     objs = [os.path.join(BUILD, os.path.basename(s)[:-3] + ".o") for s in srcs]
     if force or todo or _stale(LIB, objs):
-        cmd = [_nvcc()] + ARCH + ["-shared", "-o", LIB] + objs + ["-Xcompiler", "-fopenmp", "-lgomp"]
+        cmd = [_nvcc()] + ARCH + ["-shared", "-o", LIB] + objs + ["-Xcompiler", "-fopenmp", "-lgomp", "-ldl"]
         if verbose:
             print(" ".join(cmd), flush=True)
         r = subprocess.run(cmd, capture_output=True, text=True)

@@ -9,6 +9,10 @@ namespace fl {
 
 namespace {
 
+__device__ __forceinline__ int kv_head_of(const AttnParams& p, int h) {
+    return p.group > 0 ? (p.q_head0 + h) / p.group - p.kv_head0 : h / (p.heads / p.kv_heads);
+}
+
 constexpr int kQThreads = 256;
 
 // One CTA per activation row: optional RMSNorm with unit weights
@@ -77,7 +81,7 @@ __global__ void __launch_bounds__(kAThreads) attention_kernel(const AttnParams p
     const int ctx = base + M;
     const int hd = p.head_dim;
     const int hd2 = hd >> 1;
-    const int kvh = h / (p.heads / p.kv_heads);
+    const int kvh = kv_head_of(p, h);
     const int qd = p.heads * hd;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kstride = hd2 + 1;  // words per K row in smem (odd: conflict-free)
@@ -246,7 +250,7 @@ __global__ void __launch_bounds__(kDThreads) attention_split_kernel(const AttnPa
     const int nsplit = (ctx + kSplit - 1) / kSplit;
     if (sp >= nsplit || nr <= 0) return;
     const int hd = p.head_dim, hd2 = hd >> 1;
-    const int kvh = h / (p.heads / p.kv_heads);
+    const int kvh = kv_head_of(p, h);
     const int qd = p.heads * hd;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int j0 = sp * kSplit;
@@ -451,7 +455,7 @@ cudaError_t launch_split(const AttnParams& p, cudaStream_t s, bool pdl) {
 }
 
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl) {
-    if (p.head_dim > kMaxHd || p.head_dim < 64 || p.head_dim % 2 != 0 || p.heads % p.kv_heads != 0)
+    if (p.head_dim > kMaxHd || p.head_dim < 64 || p.head_dim % 2 != 0 || (p.group <= 0 && p.heads % p.kv_heads != 0))
         return cudaErrorInvalidValue;
     if (p.M <= kMaxRows && p.part && p.counters) {
         // grid.y covers every page the context can reach; the partial layout

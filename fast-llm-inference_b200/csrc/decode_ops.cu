@@ -165,7 +165,38 @@ __global__ void argmax_rows_kernel(const unsigned long long* part, int nparts, i
     }
 }
 
+// Tensor parallelism: this rank's best LM-head key per row, re-keyed from the
+// local row index to the global one (index + v0; the key stores
+// 0x7fffffff - index in its low word), then the maximum over all ranks'
+// gathered keys.
+__global__ void tp_local_best_kernel(const unsigned long long* part, int nparts, int v0, unsigned long long* out) {
+    const int r = blockIdx.x;
+    const unsigned long long best = block_best(part + (size_t)r * nparts, nparts);
+    if (threadIdx.x == 0) out[r] = best ? best - (unsigned long long)v0 : 0ull;
+}
+
+__global__ void tp_reduce_best_kernel(const unsigned long long* all, int size, int stride, int rows,
+                                      unsigned long long* out) {
+    const int r = threadIdx.x;
+    if (r >= rows) return;
+    unsigned long long m = 0ull;
+    for (int s = 0; s < size; s++) m = all[(size_t)s * stride + r] > m ? all[(size_t)s * stride + r] : m;
+    out[r] = m;
+}
+
 }  // namespace
+
+cudaError_t launch_tp_local_best(const unsigned long long* part, int nparts, int rows, int v0, unsigned long long* out,
+                                 cudaStream_t s) {
+    tp_local_best_kernel<<<rows, kT, 0, s>>>(part, nparts, v0, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_tp_reduce_best(const unsigned long long* all, int size, int stride, int rows,
+                                  unsigned long long* out, cudaStream_t s) {
+    tp_reduce_best_kernel<<<1, 32, 0, s>>>(all, size, stride, rows, out);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_embed_rows(const float* embed, int vocab, const int* tok, const float* feat, int shift,
                               float* x, int d, int rows_static, const int* dyn_rows,

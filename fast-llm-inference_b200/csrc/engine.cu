@@ -26,6 +26,7 @@
 #include "fl_runtime.h"
 #include "fl_state.h"
 #include "fl_step.h"
+#include "fl_tp.h"
 
 using namespace fl;
 
@@ -116,6 +117,15 @@ struct fl_engine {
     unsigned long long* samp_m = nullptr;  // [kMaxDraft + kMaxRows] kept masses (draft, then target)
     unsigned long long* samp_r = nullptr;  // [V] rejection residual weights
     uint32_t* samp_key = nullptr;          // [2] Philox seed, sequence id
+    // tensor parallelism (fl_engine_create_tp): this rank's slice of the model;
+    // H, Hkv, qd, kd, F and V above are the rank's local counts
+    int tp_rank = 0, tp_size = 1;
+    void* tp_comm = nullptr;
+    TpLayout tp = {};
+    int Vg = 0;                                // embedding rows (the full vocabulary)
+    unsigned long long* tp_keys = nullptr;     // [kMaxRows] this rank's best LM-head key per row
+    unsigned long long* tp_all = nullptr;      // [tp_size][kMaxRows] gathered
+    unsigned long long* tp_best = nullptr;     // [kMaxRows] the argmax keys the control kernels read
     // post-prefill draft state of step 0: its mass, weights and traced logits
     // (8 + 4V + 4V bytes)
     unsigned char* samp_snap = nullptr;
@@ -293,6 +303,9 @@ int run_stack(fl_engine* e, Stack& S, float* x, int M, const int* dyn_M, const i
     // Fused RMSNorm + quantization prologues need K % 128 == 0; otherwise a
     // separate act_quant launch produces xq.
     const bool fuse = (d % 128) == 0;
+    // row-parallel o / down under tensor parallelism: rank 0 adds the residual,
+    // the others store their partial sums, one all-reduce adds them up
+    const int resid_epi = (e->tp_size > 1 && e->tp_rank != 0) ? EPI_STORE : EPI_RESID;
     for (int l = 0; l < S.nl; l++) {
         LayerW& W = S.L[l];
         if (!fuse) FL_CHECK(act_quant(e, x, e->xq, d, M, dyn_M, 1, done, pdl));
@@ -324,6 +337,11 @@ int run_stack(fl_engine* e, Stack& S, float* x, int M, const int* dyn_M, const i
         at.heads = e->H;
         at.kv_heads = e->Hkv;
         at.head_dim = e->hd;
+        if (e->tp_size > 1) {
+            at.q_head0 = e->tp.q0;
+            at.kv_head0 = e->tp.kv0;
+            at.group = e->tp.group;
+        }
         at.max_ctx = e->c.max_seq_len;
         at.out_q = e->aq;
         at.done = done;
@@ -333,7 +351,8 @@ int run_stack(fl_engine* e, Stack& S, float* x, int M, const int* dyn_M, const i
         g = gemv_base(W.o, e->aq, done);
         g.out = x;
         g.ldo = d;
-        FL_CHECK(launch_chunks(g, EPI_RESID, M, dyn_M, e->s, pdl));
+        FL_CHECK(launch_chunks(g, resid_epi, M, dyn_M, e->s, pdl));
+        if (e->tp_size > 1) FL_CHECK(tp_allreduce_sum_f32(e->tp_comm, x, (size_t)M * d, e->s));
         if (!fuse) FL_CHECK(act_quant(e, x, e->xq, d, M, dyn_M, 1, done, pdl));
         g = gemv_base(W.gu, e->xq, done);
         if (fuse) {
@@ -347,7 +366,8 @@ int run_stack(fl_engine* e, Stack& S, float* x, int M, const int* dyn_M, const i
         g = gemv_base(W.down, e->hq, done);
         g.out = x;
         g.ldo = d;
-        FL_CHECK(launch_chunks(g, EPI_RESID, M, dyn_M, e->s, pdl));
+        FL_CHECK(launch_chunks(g, resid_epi, M, dyn_M, e->s, pdl));
+        if (e->tp_size > 1) FL_CHECK(tp_allreduce_sum_f32(e->tp_comm, x, (size_t)M * d, e->s));
     }
     return FL_OK;
 }
@@ -379,6 +399,12 @@ int run_lm(fl_engine* e, const float* x, int M, const int* dyn_src_row, const in
     g.M = M;
     g.row0 = 0;
     FL_CHECK_CUDA(launch_gemv_auto(g, EPI_LOGITS, e->s, pdl));
+    if (e->tp_size > 1) {
+        // vocabulary-parallel head: each rank's winner (global index), all-gathered, reduced
+        FL_CHECK_CUDA(launch_tp_local_best(e->amax, e->nparts, M, e->tp.v0, e->tp_keys, e->s));
+        FL_CHECK(tp_allgather_u64(e->tp_comm, e->tp_keys, e->tp_all, kMaxRows, e->s));
+        FL_CHECK_CUDA(launch_tp_reduce_best(e->tp_all, e->tp_size, kMaxRows, M, e->tp_best, e->s));
+    }
     return FL_OK;
 }
 
@@ -391,6 +417,11 @@ int ensure_mask(fl_engine* e, int M) {
     return FL_OK;
 }
 
+// Argmax keys of the last LM-head pass: the GEMV's per-CTA partials, or under
+// tensor parallelism the all-rank maximum (one key per row).
+const unsigned long long* amax_keys(const fl_engine* e) { return e->tp_size > 1 ? e->tp_best : e->amax; }
+int amax_nparts(const fl_engine* e) { return e->tp_size > 1 ? 1 : e->nparts; }
+
 StepBuffers step_buffers(fl_engine* e) {
     StepBuffers b;
     b.st = e->st;
@@ -400,8 +431,8 @@ StepBuffers step_buffers(fl_engine* e) {
     b.embed = e->embed;
     b.x_d = e->x_d;
     b.x_v = e->x_v;
-    b.amax_part = e->amax;
-    b.nparts = e->nparts;
+    b.amax_part = amax_keys(e);
+    b.nparts = amax_nparts(e);
     b.d = e->d;
     b.logits = e->logits;
     b.V = e->V;
@@ -682,13 +713,13 @@ int build_step_graph(fl_engine* e) {
 
 int prefill_base(fl_engine* e, const int* prompt, int P) {
     FL_CHECK_CUDA(cudaMemcpyAsync(e->seq, prompt, sizeof(int) * P, cudaMemcpyHostToDevice, e->s));
-    FL_CHECK_CUDA(launch_embed_rows(e->embed, e->V, e->seq, nullptr, 0, e->x, e->d, P, nullptr, nullptr, e->s, false));
+    FL_CHECK_CUDA(launch_embed_rows(e->embed, e->Vg, e->seq, nullptr, 0, e->x, e->d, P, nullptr, nullptr, e->s, false));
     FL_CHECK(run_stack(e, e->base, e->x, P, nullptr, e->iota, e->iota, nullptr, nullptr, false));
     // next token from the last row
     FL_CHECK_CUDA(cudaMemcpyAsync(e->x_v, e->x + (size_t)(P - 1) * e->d, sizeof(float) * e->d,
                                   cudaMemcpyDeviceToDevice, e->s));
     FL_CHECK(run_lm(e, e->x_v, 1, nullptr, nullptr, false));
-    FL_CHECK_CUDA(launch_argmax_rows(e->amax, e->nparts, 1, e->seq + P, nullptr, e->s));
+    FL_CHECK_CUDA(launch_argmax_rows(amax_keys(e), amax_nparts(e), 1, e->seq + P, nullptr, e->s));
     return FL_OK;
 }
 
@@ -698,7 +729,8 @@ int prefill_base(fl_engine* e, const int* prompt, int P) {
 // C ABI
 // ---------------------------------------------------------------------------
 
-FL_API fl_engine_t* fl_engine_create(const fl_model_config_t* cfg, int device) {
+static fl_engine_t* engine_create(const fl_model_config_t* cfg, int device, int tp_rank, int tp_size,
+                                  const unsigned char* tp_id) {
     if (!cfg) { set_error(FL_E_INVAL, "config is NULL"); return nullptr; }
     const fl_model_config_t& c = *cfg;
     if (c.hidden_size <= 0 || c.num_heads <= 0 || c.num_kv_heads <= 0 || c.head_dim <= 0 ||
@@ -727,9 +759,34 @@ FL_API fl_engine_t* fl_engine_create(const fl_model_config_t* cfg, int device) {
     e->kd = c.num_kv_heads * c.head_dim;
     e->F = c.intermediate_size;
     e->V = c.vocab_size;
+    e->Vg = c.vocab_size;
     e->R = c.max_seq_len;
     auto fail = [&](int) -> fl_engine_t* { fl_engine_destroy(e); return nullptr; };
+    if (tp_size > 1) {
+        // this rank's slice: local head, KV-head, feature and vocabulary counts
+        if (c.medusa_heads > 0) return fail(set_error(FL_E_UNSUPPORTED, "tensor parallel: Medusa heads are not sharded"));
+        if (tp_layout(c.num_heads, c.num_kv_heads, c.intermediate_size, c.vocab_size, tp_rank, tp_size, e->tp) != FL_OK)
+            return fail(0);
+        if ((e->tp.q0 * c.head_dim) % 32 || e->tp.f0 % 32 || e->tp.nf % 32)
+            return fail(set_error(FL_E_INVAL, "tensor parallel: shard boundaries must fall on 32-element blocks"));
+        e->tp_rank = tp_rank;
+        e->tp_size = tp_size;
+        e->step_layout = false;
+        e->H = e->tp.nq;
+        e->Hkv = e->tp.nkv;
+        e->qd = e->tp.nq * c.head_dim;
+        e->kd = e->tp.nkv * c.head_dim;
+        e->F = e->tp.nf;
+        e->V = e->tp.nv;
+    }
     if (cudaStreamCreateWithFlags(&e->s, cudaStreamNonBlocking) != cudaSuccess) return fail(set_error(FL_E_CUDA, "stream"));
+    if (tp_size > 1) {
+        if (tp_comm_init(tp_rank, tp_size, tp_id, &e->tp_comm) != FL_OK) return fail(0);
+        if (cudaMalloc(&e->tp_keys, sizeof(unsigned long long) * kMaxRows) != cudaSuccess ||
+            cudaMalloc(&e->tp_all, sizeof(unsigned long long) * kMaxRows * tp_size) != cudaSuccess ||
+            cudaMalloc(&e->tp_best, sizeof(unsigned long long) * kMaxRows) != cudaSuccess)
+            return fail(set_error(FL_E_NOMEM, "tensor parallel: key buffers"));
+    }
     for (auto& ev : e->ev)
         if (cudaEventCreate(&ev) != cudaSuccess) return fail(set_error(FL_E_CUDA, "event"));
     if (alloc_stack(e, e->base, c.num_layers) != FL_OK) return fail(0);
@@ -741,7 +798,7 @@ FL_API fl_engine_t* fl_engine_create(const fl_model_config_t* cfg, int device) {
     const size_t R = e->R, d = e->d;
     const size_t wq = std::max(e->d, e->qd);
     e->nparts = gemv_auto_grid(e->V, e->d);
-    bool ok = cudaMalloc(&e->embed, sizeof(float) * (size_t)e->V * d) == cudaSuccess &&
+    bool ok = cudaMalloc(&e->embed, sizeof(float) * (size_t)e->Vg * d) == cudaSuccess &&
               cudaMalloc(&e->x, sizeof(float) * R * d) == cudaSuccess &&
               cudaMalloc(&e->x2, sizeof(float) * R * d) == cudaSuccess &&
               cudaMalloc(&e->xq, R * wq) == cudaSuccess &&
@@ -775,6 +832,26 @@ FL_API fl_engine_t* fl_engine_create(const fl_model_config_t* cfg, int device) {
     return e;
 }
 
+FL_API fl_engine_t* fl_engine_create(const fl_model_config_t* cfg, int device) {
+    return engine_create(cfg, device, 0, 1, nullptr);
+}
+
+FL_API fl_engine_t* fl_engine_create_tp(const fl_model_config_t* cfg, int device, int tp_rank, int tp_size,
+                                        const unsigned char* nccl_id) {
+    if (tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size || (tp_size > 1 && !nccl_id)) {
+        set_error(FL_E_INVAL, "fl_engine_create_tp: bad rank, size or NCCL id");
+        return nullptr;
+    }
+    return engine_create(cfg, device, tp_rank, tp_size, nccl_id);
+}
+
+FL_API int fl_engine_tp(const fl_engine_t* e, int* rank, int* size) {
+    if (!e) return set_error(FL_E_INVAL, "engine is NULL");
+    if (rank) *rank = e->tp_rank;
+    if (size) *size = e->tp_size;
+    return FL_OK;
+}
+
 FL_API void fl_engine_destroy(fl_engine_t* e) {
     if (!e) return;
     cudaSetDevice(e->device);
@@ -787,18 +864,18 @@ FL_API void fl_engine_destroy(fl_engine_t* e) {
     void* bufs[] = {e->embed, e->x, e->x2, e->xq, e->q, e->aq, e->hq, e->logits, e->amax, e->x_v, e->x_d,
                     e->iota, e->tok, e->mask, e->st, e->st_snap, e->xd0_snap, e->seq, e->out, e->acc,
                     e->last_feat, e->attn_part, e->attn_cnt, e->step_bar, e->d_phases, e->d_trace,
-                    e->samp_q, e->samp_p, e->samp_r, e->samp_trace, e->samp_snap, e->samp_m, e->samp_key};
+                    e->samp_q, e->samp_p, e->samp_r, e->samp_trace, e->samp_snap, e->samp_m, e->samp_key,
+                    e->tp_keys, e->tp_all, e->tp_best};
     for (void* p : bufs) cudaFree(p);
+    tp_comm_free(e->tp_comm);
     for (auto& ev : e->ev)
         if (ev) cudaEventDestroy(ev);
     if (e->s) cudaStreamDestroy(e->s);
     delete e;
 }
 
-FL_API int fl_engine_load_linear(fl_engine_t* e, int stack, int layer, int proj, const int8_t* w,
-                                 const uint16_t* d, int rows, int cols) {
-    if (!e || !w || !d) return set_error(FL_E_INVAL, "load_linear: NULL argument");
-    FL_CHECK_CUDA(cudaSetDevice(e->device));
+static int load_linear_local(fl_engine_t* e, int stack, int layer, int proj, const int8_t* w, const uint16_t* d,
+                             int rows, int cols) {
     if (stack == 3) {
         if (proj != 1 || rows != e->V) return set_error(FL_E_INVAL, "load_linear: shared stack takes the LM head (proj 1)");
         FL_CHECK(put_rows(e->lm, 0, 1, w, d, rows, cols, e->s));
@@ -849,10 +926,49 @@ FL_API int fl_engine_load_linear(fl_engine_t* e, int stack, int layer, int proj,
     }
 }
 
+// Under tensor parallelism the caller passes every tensor whole (as a loader
+// reads it) and the rank keeps its slice: rows of Q, K, V, gate, up and the LM
+// head, columns of o and down.
+FL_API int fl_engine_load_linear(fl_engine_t* e, int stack, int layer, int proj, const int8_t* w,
+                                 const uint16_t* d, int rows, int cols) {
+    if (!e || !w || !d) return set_error(FL_E_INVAL, "load_linear: NULL argument");
+    FL_CHECK_CUDA(cudaSetDevice(e->device));
+    if (e->tp_size == 1 || cols % 32) return load_linear_local(e, stack, layer, proj, w, d, rows, cols);
+    const TpLayout& L = e->tp;
+    const int hd = e->hd;
+    auto row_slice = [&](int full_rows, int r0, int nr) -> int {
+        if (rows != full_rows) return set_error(FL_E_INVAL, "load_linear: pass the whole tensor to every rank");
+        return load_linear_local(e, stack, layer, proj, w + (size_t)r0 * cols, d + (size_t)r0 * (cols / 32), nr, cols);
+    };
+    auto col_slice = [&](int full_cols, int c0, int nc) -> int {
+        if (cols != full_cols || rows != e->d) return set_error(FL_E_INVAL, "load_linear: pass the whole tensor to every rank");
+        std::vector<int8_t> ws((size_t)rows * nc);
+        std::vector<uint16_t> ds((size_t)rows * (nc / 32));
+        for (int r = 0; r < rows; r++) {
+            memcpy(ws.data() + (size_t)r * nc, w + (size_t)r * cols + c0, (size_t)nc);
+            memcpy(ds.data() + (size_t)r * (nc / 32), d + (size_t)r * (cols / 32) + c0 / 32, sizeof(uint16_t) * (nc / 32));
+        }
+        return load_linear_local(e, stack, layer, proj, ws.data(), ds.data(), rows, nc);
+    };
+    const int Hg = e->c.num_heads, Hkvg = e->c.num_kv_heads, Fg = e->c.intermediate_size;
+    if (stack == 3) return row_slice(e->Vg, L.v0, L.nv);
+    if (stack != 0 && stack != 1) return set_error(FL_E_INVAL, "load_linear: bad stack for a tensor-parallel engine");
+    switch (proj) {
+        case 0: return row_slice(Hg * hd, L.q0 * hd, L.nq * hd);
+        case 1:
+        case 2: return row_slice(Hkvg * hd, L.kv0 * hd, L.nkv * hd);
+        case 3: return col_slice(Hg * hd, L.q0 * hd, L.nq * hd);
+        case 4:
+        case 5: return row_slice(Fg, L.f0, L.nf);
+        case 6: return col_slice(Fg, L.f0, L.nf);
+        default: return set_error(FL_E_INVAL, "load_linear: bad projection");
+    }
+}
+
 FL_API int fl_engine_load_embedding(fl_engine_t* e, const float* table) {
     if (!e || !table) return set_error(FL_E_INVAL, "load_embedding: NULL argument");
     FL_CHECK_CUDA(cudaSetDevice(e->device));
-    FL_CHECK_CUDA(cudaMemcpy(e->embed, table, sizeof(float) * (size_t)e->V * e->d, cudaMemcpyHostToDevice));
+    FL_CHECK_CUDA(cudaMemcpy(e->embed, table, sizeof(float) * (size_t)e->Vg * e->d, cudaMemcpyHostToDevice));
     e->embed_loaded = true;
     return FL_OK;
 }
@@ -867,7 +983,9 @@ FL_API int fl_engine_ready(const fl_engine_t* e) {
 
 FL_API int fl_engine_synthesize(fl_engine_t* e, uint64_t seed) {
     if (!e) return set_error(FL_E_INVAL, "engine is NULL");
-    const int d = e->d, qd = e->qd, kd = e->kd, F = e->F, V = e->V;
+    // whole tensors (a tensor-parallel rank keeps its slice in load_linear)
+    const int d = e->d, qd = e->c.num_heads * e->hd, kd = e->c.num_kv_heads * e->hd, F = e->c.intermediate_size,
+              V = e->Vg;
     const size_t maxel = std::max({(size_t)V * d, (size_t)2 * F * d, (size_t)qd * d});
     std::vector<int8_t> w(maxel);
     std::vector<uint16_t> sc(maxel / 32);
@@ -901,6 +1019,8 @@ FL_API int fl_engine_forward_rows(fl_engine_t* e, int stack, const float* x_in, 
     FL_CHECK(check_ready(e, stack == 1));
     if (!x_in || !pos || M <= 0 || base < 0 || base + M > e->R) return set_error(FL_E_INVAL, "forward_rows: bad arguments");
     if (stack != 0 && stack != 1) return set_error(FL_E_INVAL, "forward_rows: stack must be 0 or 1");
+    if (logits && e->tp_size > 1)
+        return set_error(FL_E_UNSUPPORTED, "forward_rows: a tensor-parallel rank holds a slice of the logits");
     Stack& S = stack == 0 ? e->base : e->draft;
     const size_t xb = sizeof(float) * (size_t)M * e->d;
     FL_CHECK_CUDA(cudaMemcpyAsync(e->x, x_in, xb, cudaMemcpyHostToDevice, e->s));
@@ -932,10 +1052,10 @@ FL_API int fl_engine_greedy_generate(fl_engine_t* e, const int* prompt, int P, i
     FL_CHECK(prefill_base(e, prompt, P));
     for (int i = 1; i < n_new; i++) {
         const int n = P + i - 1;  // seq[n] is the newest token
-        FL_CHECK_CUDA(launch_embed_rows(e->embed, e->V, e->seq + n, nullptr, 0, e->x_v, e->d, 1, nullptr, nullptr, e->s, false));
+        FL_CHECK_CUDA(launch_embed_rows(e->embed, e->Vg, e->seq + n, nullptr, 0, e->x_v, e->d, 1, nullptr, nullptr, e->s, false));
         FL_CHECK(run_stack(e, e->base, e->x_v, 1, nullptr, e->iota + n, e->iota + n, nullptr, nullptr, false));
         FL_CHECK(run_lm(e, e->x_v, 1, nullptr, nullptr, false));
-        FL_CHECK_CUDA(launch_argmax_rows(e->amax, e->nparts, 1, e->seq + n + 1, nullptr, e->s));
+        FL_CHECK_CUDA(launch_argmax_rows(amax_keys(e), amax_nparts(e), 1, e->seq + n + 1, nullptr, e->s));
     }
     FL_CHECK_CUDA(cudaMemcpyAsync(out, e->seq + P, sizeof(int) * n_new, cudaMemcpyDeviceToHost, e->s));
     FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
@@ -983,7 +1103,7 @@ FL_API int fl_engine_spec_prefill(fl_engine_t* e, const int* prompt, int P, int 
     // sampling: the first token is drawn from the last prompt row's logits
     if (e->samp) FL_CHECK_CUDA(launch_sample_first(step_buffers(e), P, e->s));
     // Draft catch-up over positions 0..P: x_i = F_{i-1} + E[t_i], F_{-1} = 0.
-    FL_CHECK_CUDA(launch_embed_rows(e->embed, e->V, e->seq, e->x, 1, e->x2, e->d, P + 1, nullptr, nullptr, e->s, false));
+    FL_CHECK_CUDA(launch_embed_rows(e->embed, e->Vg, e->seq, e->x, 1, e->x2, e->d, P + 1, nullptr, nullptr, e->s, false));
     FL_CHECK(run_stack(e, e->draft, e->x2, P + 1, nullptr, e->iota, e->iota, nullptr, nullptr, false));
     FL_CHECK_CUDA(cudaMemcpyAsync(e->x_d, e->x2 + (size_t)P * e->d, sizeof(float) * e->d, cudaMemcpyDeviceToDevice, e->s));
     SpecState h = {};
@@ -1022,6 +1142,8 @@ FL_API int fl_engine_set_sampling(fl_engine_t* e, float temperature, float top_p
         return set_error(FL_E_INVAL, "set_sampling: temperature must be finite");
     FL_CHECK_CUDA(cudaSetDevice(e->device));
     const bool samp = temperature > 0.0f;
+    if (samp && e->tp_size > 1)
+        return set_error(FL_E_UNSUPPORTED, "set_sampling: a tensor-parallel engine decodes greedily (its logits are split)");
     if (samp == e->samp && (!samp || (temperature == e->samp_T && top_p == e->samp_top_p &&
                                       seed == e->samp_seed && seq_id == e->samp_seq)))
         return FL_OK;  // unchanged
@@ -1337,9 +1459,11 @@ FL_API int fl_engine_last_feature(const fl_engine_t* e, float* out) {
 // Appends len tokens at the callback position through the base model.
 static int base_append(fl_engine* e, const int* tokens, int len, float* logits_out) {
     FL_CHECK(check_ready(e, false));
+    if (logits_out && e->tp_size > 1)
+        return set_error(FL_E_UNSUPPORTED, "target_forward: a tensor-parallel rank holds a slice of the logits");
     if (len <= 0 || e->cb_pos + len > e->R) return set_error(FL_E_INVAL, "base forward: context full");
     FL_CHECK_CUDA(cudaMemcpyAsync(e->tok, tokens, sizeof(int) * len, cudaMemcpyHostToDevice, e->s));
-    FL_CHECK_CUDA(launch_embed_rows(e->embed, e->V, e->tok, nullptr, 0, e->x, e->d, len, nullptr, nullptr, e->s, false));
+    FL_CHECK_CUDA(launch_embed_rows(e->embed, e->Vg, e->tok, nullptr, 0, e->x, e->d, len, nullptr, nullptr, e->s, false));
     FL_CHECK(run_stack(e, e->base, e->x, len, nullptr, e->iota + e->cb_pos, e->iota + e->cb_pos, nullptr, nullptr,
                        false));
     FL_CHECK_CUDA(cudaMemcpyAsync(e->last_feat, e->x + (size_t)(len - 1) * e->d, sizeof(float) * e->d,
@@ -1384,17 +1508,18 @@ FL_API int fl_engine_draft_chain(fl_engine_t* e, const float* hidden, int tok, i
                                  float* out_probs) {
     FL_CHECK(check_ready(e, true));
     if (!hidden || !out_tokens || K <= 0 || pos < 0 || pos + K > e->R) return set_error(FL_E_INVAL, "draft_chain: bad arguments");
+    if (e->tp_size > 1) return set_error(FL_E_UNSUPPORTED, "draft_chain: not available on a tensor-parallel engine");
     std::vector<float> lg(e->V);
     FL_CHECK_CUDA(cudaMemcpyAsync(e->x2, hidden, sizeof(float) * e->d, cudaMemcpyHostToDevice, e->s));
     FL_CHECK_CUDA(cudaMemcpyAsync(e->tok, &tok, sizeof(int), cudaMemcpyHostToDevice, e->s));
-    FL_CHECK_CUDA(launch_embed_rows(e->embed, e->V, e->tok, e->x2, 0, e->x_d, e->d, 1, nullptr, nullptr, e->s, false));
+    FL_CHECK_CUDA(launch_embed_rows(e->embed, e->Vg, e->tok, e->x2, 0, e->x_d, e->d, 1, nullptr, nullptr, e->s, false));
     for (int j = 0; j < K; j++) {
         FL_CHECK(run_stack(e, e->draft, e->x_d, 1, nullptr, e->iota + pos + j, e->iota + pos + j, nullptr, nullptr, false));
         FL_CHECK(run_lm(e, e->x_d, 1, nullptr, nullptr, false));
-        FL_CHECK_CUDA(launch_argmax_rows(e->amax, e->nparts, 1, e->tok, nullptr, e->s));
+        FL_CHECK_CUDA(launch_argmax_rows(amax_keys(e), amax_nparts(e), 1, e->tok, nullptr, e->s));
         FL_CHECK_CUDA(cudaMemcpyAsync(lg.data(), e->logits, sizeof(float) * e->V, cudaMemcpyDeviceToHost, e->s));
         FL_CHECK_CUDA(cudaMemcpyAsync(&out_tokens[j], e->tok, sizeof(int), cudaMemcpyDeviceToHost, e->s));
-        FL_CHECK_CUDA(launch_embed_rows(e->embed, e->V, e->tok, e->x_d, 0, e->x_d, e->d, 1, nullptr, nullptr, e->s, false));
+        FL_CHECK_CUDA(launch_embed_rows(e->embed, e->Vg, e->tok, e->x_d, 0, e->x_d, e->d, 1, nullptr, nullptr, e->s, false));
         FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
         if (out_probs) {
             float mx = lg[0];

@@ -121,6 +121,10 @@ struct AttnParams {
     const int* dyn_M;
     const uint8_t* mask;      // [M*M] visibility among new rows, NULL = causal
     int heads, kv_heads, head_dim;
+    // KV head of local query head h: (q_head0 + h) / group - kv_head0; group 0
+    // means heads / kv_heads with zero offsets (a tensor-parallel rank holds
+    // a slice of the heads that need not align with the GQA groups)
+    int q_head0, kv_head0, group;
     int max_ctx;              // upper bound of slot_base + M (smem sizing)
     uint8_t* out_q;           // [rows, heads*head_dim] quantized output
     float* out_f;             // optional f32 output

@@ -111,6 +111,10 @@ _SIGS = {
     "fl_q4_0_to_i8": (I, [VP, I, I, VP, VP]),
     "fl_philox4x32_10": (None, [VP, VP, VP]),
     "fl_engine_create": (VP, [C.POINTER(ModelConfig), I]),
+    "fl_engine_create_tp": (VP, [C.POINTER(ModelConfig), I, I, I, VP]),
+    "fl_engine_tp": (I, [VP, VP, VP]),
+    "fl_tp_unique_id": (I, [VP]),
+    "fl_tp_layout": (I, [C.POINTER(ModelConfig), I, I, VP]),
     "fl_engine_destroy": (None, [VP]),
     "fl_engine_load_linear": (I, [VP, I, I, I, VP, VP, I, I]),
     "fl_engine_load_embedding": (I, [VP, VP]),
@@ -268,14 +272,35 @@ def model_config(**kw) -> ModelConfig:
     return c
 
 
+def tp_unique_id(lib: "Lib") -> bytes:
+    """128-byte NCCL id for fl_engine_create_tp (make on one rank, share)."""
+    b = np.zeros(128, np.uint8)
+    lib.check(lib.fl_tp_unique_id(ptr(b)), "tp_unique_id")
+    return b.tobytes()
+
+
+def tp_layout(lib: "Lib", cfg: dict, rank: int, size: int) -> dict:
+    out = np.zeros(9, np.int32)
+    c = model_config(**cfg)
+    lib.check(lib.fl_tp_layout(C.byref(c), rank, size, ptr(out)), "tp_layout")
+    return dict(zip(("q0", "nq", "kv0", "nkv", "f0", "nf", "v0", "nv", "group"), (int(v) for v in out)))
+
+
 class Engine:
     """Owns an fl_engine_t."""
 
-    def __init__(self, lib: Lib, cfg: dict, device: int = 0):
+    def __init__(self, lib: Lib, cfg: dict, device: int = 0, tp: tuple | None = None):
+        """tp = (rank, size, nccl_id bytes from tp_unique_id) for a
+        tensor-parallel rank; every rank then passes whole tensors."""
         self.lib = lib
         self.cfg = dict(cfg)
         self._c = model_config(**cfg)
-        h = lib.fl_engine_create(C.byref(self._c), device)
+        if tp is None:
+            h = lib.fl_engine_create(C.byref(self._c), device)
+        else:
+            rank, size, uid = tp
+            idb = np.frombuffer(bytes(uid), np.uint8).copy()
+            h = lib.fl_engine_create_tp(C.byref(self._c), device, rank, size, ptr(idb))
         if not h:
             raise FLError(f"fl_engine_create failed: {lib.err()}")
         self.h = h

@@ -159,6 +159,26 @@ typedef struct {
 } fl_model_config_t;
 
 fl_engine_t* fl_engine_create(const fl_model_config_t* cfg, int device);
+
+/* Tensor parallelism over tp_size GPUs of one node (one process or thread per
+ * rank, each on its own device). Rank r holds Q heads [r H/g, (r+1) H/g)
+ * with the KV heads they read (a KV head spanning two ranks is held by both),
+ * FFN features [r F/g, (r+1) F/g) and LM-head rows [r ceil(V/g), ...), plus
+ * the whole embedding; Q/K/V and gate/up are column-parallel, o and down
+ * row-parallel with an NCCL all-reduce of the hidden rows after each, and the
+ * LM head's argmax is all-gathered. Every rank passes whole tensors to
+ * fl_engine_load_linear (or calls fl_engine_synthesize) and makes the same
+ * calls in the same order. nccl_id: 128 bytes from fl_tp_unique_id on one
+ * rank, shared by the caller. H and F must divide by tp_size; greedy
+ * decoding only. libnccl.so.2 is loaded on first use. */
+fl_engine_t* fl_engine_create_tp(const fl_model_config_t* cfg, int device, int tp_rank, int tp_size,
+                                 const unsigned char* nccl_id);
+int fl_engine_tp(const fl_engine_t* e, int* rank, int* size);
+int fl_tp_unique_id(unsigned char* id);
+/* This rank's slice: out[9] = {first Q head, Q heads, first KV head, KV
+ * heads, first FFN feature, features, first vocabulary row, rows, Q heads per
+ * KV head}. */
+int fl_tp_layout(const fl_model_config_t* cfg, int rank, int size, int* out);
 void fl_engine_destroy(fl_engine_t* e);
 
 /* Loads one INT8 linear from host arrays: stack/layer/proj as in

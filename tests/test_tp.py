@@ -1,0 +1,91 @@
+"""Tensor parallelism: the shard layout (CPU) and a 2-rank decode on two GPUs
+(skipped with fewer) that must give identical streams on both ranks, equal
+to the oracle's under the near-tie rule."""
+import numpy as np
+import pytest
+
+import flb200
+
+PHI3_MEDIUM = dict(vocab_size=32064, hidden_size=5120, intermediate_size=17920, num_layers=40, num_heads=40,
+                   num_kv_heads=10, head_dim=128, draft_layers=2, medusa_heads=0, max_seq_len=4096,
+                   rope_theta=10000.0, norm_eps=1e-5)
+
+
+@pytest.mark.parametrize("size", [1, 2, 4, 8])
+def test_layout_covers_the_model(lib, size):
+    L = [flb200.tp_layout(lib, PHI3_MEDIUM, r, size) for r in range(size)]
+    H, Hkv, F, V = 40, 10, 17920, 32064
+    G = H // Hkv
+    assert sum(l["nq"] for l in L) == H and [l["q0"] for l in L] == [r * H // size for r in range(size)]
+    assert sum(l["nf"] for l in L) == F and sum(l["nv"] for l in L) == V
+    for l in L:
+        assert l["group"] == G and l["nf"] % 32 == 0 and (l["q0"] * 128) % 32 == 0
+        needed = {q // G for q in range(l["q0"], l["q0"] + l["nq"])}
+        assert needed == set(range(l["kv0"], l["kv0"] + l["nkv"]))
+    # straddling KV heads are held by both neighbours at 4 and 8 ranks
+    held = sum(l["nkv"] for l in L)
+    assert held == Hkv if size <= 2 else held > Hkv
+
+
+def test_layout_rejects_bad_splits(lib):
+    bad = dict(PHI3_MEDIUM, num_heads=12, num_kv_heads=4)
+    with pytest.raises(flb200.FLError):
+        flb200.tp_layout(lib, bad, 0, 8)
+
+
+TP_GQA = dict(vocab=1024, d=512, ffn=1024, layers=2, heads=12, kv_heads=3, head_dim=64, theta=10000.0, eps=1e-5)
+
+
+def _rank(rank, size, uid, q):
+    import sys, os
+    sys.path[:0] = [os.path.dirname(__file__), os.path.join(os.path.dirname(__file__), "..", "fast-llm-inference_b200")]
+    import flb200 as F
+    from _model import engine_cfg, load_engine, make_weights, prompt
+    try:
+        lib = F.Lib()
+        lib.check(lib.fl_cuda_init(rank), "init")
+        w, embed = make_weights(lib, TP_GQA, seed=41)
+        eng = F.Engine(lib, engine_cfg(TP_GQA, draft_layers=1), rank, tp=(rank, size, uid))
+        load_engine(eng, w, embed)
+        p = prompt(8, 16, TP_GQA["vocab"])
+        toks, acc = eng.spec_generate(p, 24, 4)
+        g = eng.greedy(p, 12)
+        eng.close()
+        q.put((rank, toks.tolist(), acc.tolist(), g.tolist(), None))
+    except Exception as ex:  # reported to the parent
+        q.put((rank, None, None, None, repr(ex)))
+
+
+@pytest.mark.gpu
+def test_two_rank_decode_matches_oracle(gpu, orc):
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from _model import make_weights, prompt
+    import bind
+    uid = flb200.tp_unique_id(gpu)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank, args=(r, 2, uid, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r, toks, acc, g, err = q.get(timeout=600)
+        assert err is None, f"rank {r}: {err}"
+        res[r] = (np.array(toks), np.array(acc), np.array(g))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert np.array_equal(res[0][0], res[1][0]) and np.array_equal(res[0][2], res[1][2]), "ranks disagree"
+    w, embed = make_weights(gpu, TP_GQA, seed=41)
+    om = bind.OracleModel(orc, TP_GQA, embed, w, draft_layers=1)
+    p = prompt(8, 16, TP_GQA["vocab"])
+    want, _, margins = om.spec(p, 24, 4)
+    got = res[0][0]
+    diff = np.nonzero(got != want)[0]
+    assert diff.size == 0 or margins[diff[0]] < 1e-2, f"diverges at {diff[:1]} (margin {margins[diff[0]]:.3g})"
+    gw, gm = om.greedy(p, 12)
+    gd = np.nonzero(res[0][2] != gw)[0]
+    assert gd.size == 0 or gm[gd[0]] < 1e-2
