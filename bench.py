@@ -13,6 +13,7 @@ needed between timed iterations.
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
     python bench.py --workload sampled-batch [--seqs 64 --prompt-len 1024 --new-tokens 512 --k 6]
+    torchrun --nproc-per-node N bench.py --gpus N --workload tp-medium [--prompt-len 512]
 
 One process per GPU (torchrun for N > 1); this path does not shard (batch 1),
 so N GPUs run N independent replicas and `value` sums their tokens/s.
@@ -25,6 +26,12 @@ sequences (temperature 0.8, top-p 0.95, k = 6, Philox seed 1234 keyed by
 sequence id) split across the ranks with no exchange; `value` = all ranks'
 tokens / the slowest rank's device time for its share (strong scaling: the
 sequence count is fixed). Not the default line.
+
+--workload tp-medium is the tensor-parallel configuration: a Phi-3-medium-
+shaped base (40 layers, d 5120, 40 query / 10 KV heads x 128, SwiGLU 17920,
+vocab 32064) with a 2-layer draft of the same dims, greedy chain k = 4, bs1,
+sharded over the ranks (NCCL all-reduce after o and down); `value` = tokens/s
+of the one sequence (strong scaling), device-timed, max over ranks.
 """
 from __future__ import annotations
 
@@ -240,6 +247,81 @@ def run_microbench(a):
     return 0
 
 
+MEDIUM = dict(vocab_size=32064, hidden_size=5120, intermediate_size=17920, num_layers=40, num_heads=40,
+              num_kv_heads=10, head_dim=128, draft_layers=2, medusa_heads=0, rope_theta=10000.0, norm_eps=1e-5)
+
+
+def run_tp_medium(a):
+    """Phi-3-medium-shaped spec decode, tensor-parallel over the ranks."""
+    import datetime
+    import torch
+    import flb200
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    lib = flb200.Lib()
+    lib.check(lib.fl_cuda_init(local), "init")
+    cfg = dict(MEDIUM, max_seq_len=((a.prompt_len + a.new_tokens + a.k + 2 + 63) // 64) * 64)
+    tp = None
+    if world > 1:
+        box = [flb200.tp_unique_id(lib) if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        tp = (rank, world, box[0])
+    t0 = time.time()
+    eng = flb200.Engine(lib, cfg, local, tp=tp)
+    eng.synthesize(SEED)
+    prompt = np.random.default_rng(PROMPT_SEED).integers(0, MEDIUM["vocab_size"], a.prompt_len).astype(np.int32)
+    eng.spec_prefill(prompt, a.k)
+    setup_s = time.time() - t0
+    for _ in range(a.warmup):
+        eng.spec_decode(a.new_tokens)
+    stream = torch.cuda.ExternalStream(eng.stream(), device=local)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    clocks.start()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    steps_total, launches = 0, 0
+    for _ in range(a.steps):
+        toks, acc = eng.spec_decode(a.new_tokens)
+        steps_total += len(acc)
+        launches += eng.last_launches()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    if rank == 0:
+        line = {
+            "metric": "Phi-3-medium spec-decode tok/s @bs1, tensor parallel", "value": a.steps * a.new_tokens / (ms / 1e3),
+            "unit": "tok/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms / a.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8xs8->s32, f32",
+            "data": "synthetic (seeded N(0,0.02) -> Q4_0 -> INT8 weights, uniform prompt ids)",
+            "config": {"workload": f"phi3-medium int8 (40L d5120 40/10 heads x128 ffn17920 vocab32064) + 2-layer draft, "
+                                   f"greedy chain k={a.k}, bs1, prompt {a.prompt_len}, {a.new_tokens} new tokens per step",
+                       "parallelism": f"tensor parallel x{world} (NCCL all-reduce after o and down)"},
+            "spec": {"spec_steps_per_decode": steps_total / a.steps, "step_us": ms * 1e3 / max(1, steps_total)},
+            "gpu_launches": int(launches), "clocks": clk, "setup_s": setup_s,
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def run_sampled_batch(a):
     """Independent sampled sequences sharded across ranks (see the module
     docstring); one timed pass over each rank's share."""
@@ -319,7 +401,16 @@ def run_sampled_batch(a):
     return 0
 
 
+def split_host_threads():
+    """Ranks of one node share the host cores for the OpenMP weight
+    generator (set before the library, and its OpenMP runtime, load)."""
+    world = int(os.environ.get("LOCAL_WORLD_SIZE", os.environ.get("WORLD_SIZE", "1")))
+    if world > 1 and "OMP_NUM_THREADS" not in os.environ:
+        os.environ["OMP_NUM_THREADS"] = str(max(1, (os.cpu_count() or 1) // world))
+
+
 def main():
+    split_host_threads()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
@@ -335,13 +426,15 @@ def main():
                     help="one persistent tcgen05 kernel per speculative step (128-byte panels)")
     ap.add_argument("--m", type=int, default=5, help="activation rows for --microbench")
     ap.add_argument("--iters", type=int, default=10, help="sweeps for --microbench")
-    ap.add_argument("--workload", default="spec-bs1", choices=["spec-bs1", "sampled-batch"])
+    ap.add_argument("--workload", default="spec-bs1", choices=["spec-bs1", "sampled-batch", "tp-medium"])
     ap.add_argument("--seqs", type=int, default=64, help="sequences of --workload sampled-batch")
     a = ap.parse_args()
     if a.microbench:
         return run_microbench(a)
     if a.workload == "sampled-batch":
         return run_sampled_batch(a)
+    if a.workload == "tp-medium":
+        return run_tp_medium(a)
     a.warmup = max(a.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -981,11 +981,44 @@ FL_API int fl_engine_ready(const fl_engine_t* e) {
     return 1;
 }
 
+// Tensor-parallel rank: generates only its slice of every tensor (each
+// element is a pure function of the seed, the tensor id and its index).
+static int synthesize_tp(fl_engine_t* e, uint64_t seed) {
+    const TpLayout& L = e->tp;
+    const int d = e->d, hd = e->hd, Hg = e->c.num_heads, Hkvg = e->c.num_kv_heads, Fg = e->c.intermediate_size;
+    const float stdv = 0.02f;
+    std::vector<int8_t> w;
+    std::vector<uint16_t> sc;
+    auto gen = [&](int stack, int layer, int proj, int rows, int cols, int r0, int nr, int c0, int nc) -> int {
+        w.resize((size_t)nr * nc);
+        sc.resize((size_t)nr * nc / 32);
+        const int rc = fl_synth_q4_0_i8_block(seed, FL_TENSOR_ID(stack, layer, proj), rows, cols, r0, nr, c0, nc, stdv,
+                                              w.data(), sc.data());
+        if (rc != FL_OK) return set_error(rc, "synth failed");
+        return load_linear_local(e, stack, layer, proj, w.data(), sc.data(), nr, nc);
+    };
+    for (int s = 0; s < 2; s++) {
+        const Stack& S = s == 0 ? e->base : e->draft;
+        for (int l = 0; l < S.nl; l++) {
+            FL_CHECK(gen(s, l, 0, Hg * hd, d, L.q0 * hd, L.nq * hd, 0, d));
+            FL_CHECK(gen(s, l, 1, Hkvg * hd, d, L.kv0 * hd, L.nkv * hd, 0, d));
+            FL_CHECK(gen(s, l, 2, Hkvg * hd, d, L.kv0 * hd, L.nkv * hd, 0, d));
+            FL_CHECK(gen(s, l, 3, d, Hg * hd, 0, d, L.q0 * hd, L.nq * hd));
+            FL_CHECK(gen(s, l, 4, Fg, d, L.f0, L.nf, 0, d));
+            FL_CHECK(gen(s, l, 5, Fg, d, L.f0, L.nf, 0, d));
+            FL_CHECK(gen(s, l, 6, d, Fg, 0, d, L.f0, L.nf));
+        }
+    }
+    FL_CHECK(gen(3, 0, 1, e->Vg, d, L.v0, L.nv, 0, d));
+    std::vector<float> emb((size_t)e->Vg * d);
+    FL_CHECK(fl_synth_q4_0_f32(seed, FL_TENSOR_ID(3, 0, 0), e->Vg, d, stdv, emb.data()));
+    return fl_engine_load_embedding(e, emb.data());
+}
+
 FL_API int fl_engine_synthesize(fl_engine_t* e, uint64_t seed) {
     if (!e) return set_error(FL_E_INVAL, "engine is NULL");
-    // whole tensors (a tensor-parallel rank keeps its slice in load_linear)
-    const int d = e->d, qd = e->c.num_heads * e->hd, kd = e->c.num_kv_heads * e->hd, F = e->c.intermediate_size,
-              V = e->Vg;
+    if (e->tp_size > 1) return synthesize_tp(e, seed);
+    const int d = e->d, qd = e->qd, kd = e->kd, F = e->F, V = e->V;
     const size_t maxel = std::max({(size_t)V * d, (size_t)2 * F * d, (size_t)qd * d});
     std::vector<int8_t> w(maxel);
     std::vector<uint16_t> sc(maxel / 32);

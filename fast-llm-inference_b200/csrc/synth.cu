@@ -120,6 +120,25 @@ FL_API int fl_synth_q4_0_i8(uint64_t seed, uint32_t tensor_id, int rows, int col
     return FL_OK;
 }
 
+FL_API int fl_synth_q4_0_i8_block(uint64_t seed, uint32_t tensor_id, int rows, int cols, int r0, int nr, int c0, int nc,
+                                  float std, int8_t* w, uint16_t* d) {
+    if (!w || !d || rows <= 0 || cols <= 0 || cols % 32 != 0 || r0 < 0 || nr <= 0 || r0 + nr > rows || c0 < 0 ||
+        nc <= 0 || c0 + nc > cols || c0 % 32 != 0 || nc % 32 != 0)
+        return FL_E_INVAL;
+#pragma omp parallel
+    {
+        float* buf = new float[nc];
+#pragma omp for schedule(static)
+        for (int r = 0; r < nr; r++) {
+            normal_row(seed, tensor_id, (uint64_t)(r0 + r) * cols + c0, nc, std, buf);
+            for (int b = 0; b < nc / 32; b++)
+                q4_0_block(buf + 32 * b, w + (size_t)r * nc + 32 * b, d + (size_t)r * (nc / 32) + b);
+        }
+        delete[] buf;
+    }
+    return FL_OK;
+}
+
 FL_API int fl_synth_q4_0_f32(uint64_t seed, uint32_t tensor_id, int rows, int cols, float std, float* out) {
     if (!out || rows <= 0 || cols <= 0 || cols % 32 != 0) return FL_E_INVAL;
 #pragma omp parallel

@@ -106,6 +106,7 @@ _SIGS = {
     "fl_cuda_block_dots_i8": (I, [VP, C.POINTER(DequantizedTensor), VP, I, I, I, VP]),
     "fl_cuda_block_dots_i8_noalloc": (I, [VP, C.POINTER(DequantizedTensor), VP, I, I, I, VP]),
     "fl_synth_q4_0_i8": (I, [U64, U32, I, I, F, VP, VP]),
+    "fl_synth_q4_0_i8_block": (I, [U64, U32, I, I, I, I, I, I, F, VP, VP]),
     "fl_synth_q4_0_f32": (I, [U64, U32, I, I, F, VP]),
     "fl_synth_normal": (I, [U64, U32, SZ, F, VP]),
     "fl_q4_0_to_i8": (I, [VP, I, I, VP, VP]),

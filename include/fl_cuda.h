@@ -119,6 +119,11 @@ int fl_cuda_block_dots_i8_noalloc(const float* A, const dequantized_tensor_t* B,
  * deterministic. */
 int fl_synth_q4_0_i8(uint64_t seed, uint32_t tensor_id, int rows, int cols,
                      float std, int8_t* w, uint16_t* d);
+/* Rows [r0, r0 + nr) x columns [c0, c0 + nc) of the same [rows, cols] tensor
+ * (c0, nc multiples of 32): identical to that block of fl_synth_q4_0_i8's
+ * output. w [nr, nc], d [nr, nc / 32]. */
+int fl_synth_q4_0_i8_block(uint64_t seed, uint32_t tensor_id, int rows, int cols, int r0, int nr, int c0, int nc,
+                           float std, int8_t* w, uint16_t* d);
 
 /* Same values as fl_synth_q4_0_i8 dequantized to f32 ((q-8)*d), the
  * form the reference loader keeps embeddings in (gguf_loader.c:147-161). */

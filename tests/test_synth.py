@@ -57,3 +57,20 @@ def test_gguf_q4_0_nibble_order(lib):
     assert list(w[:16]) == [i - 8 for i in range(16)]
     assert list(w[16:]) == [(15 - i) - 8 for i in range(16)]
     assert d[0] == np.float16(0.5).view(np.uint16)
+
+
+def test_block_synthesis_is_a_slice(lib):
+    """A tensor-parallel rank generates only its block; it must equal that
+    block of the whole tensor."""
+    import numpy as np
+    from flb200 import ptr
+    rows, cols = 96, 256
+    w, d = lib.synth_q4_0_i8(9, 77, rows, cols)
+    for r0, nr, c0, nc in [(0, 96, 0, 256), (32, 40, 0, 256), (0, 96, 64, 128), (17, 5, 224, 32)]:
+        wb = np.empty((nr, nc), np.int8)
+        db = np.empty((nr, nc // 32), np.uint16)
+        assert lib.fl_synth_q4_0_i8_block(9, 77, rows, cols, r0, nr, c0, nc, 0.02, ptr(wb), ptr(db)) == 0
+        assert np.array_equal(wb, w[r0:r0 + nr, c0:c0 + nc])
+        assert np.array_equal(db, d[r0:r0 + nr, c0 // 32:(c0 + nc) // 32])
+    wb = np.empty((4, 30), np.int8)
+    assert lib.fl_synth_q4_0_i8_block(9, 77, rows, cols, 0, 4, 2, 30, 0.02, ptr(wb), ptr(wb)) != 0
