@@ -126,6 +126,17 @@ struct fl_engine {
     unsigned long long* tp_keys = nullptr;     // [kMaxRows] this rank's best LM-head key per row
     unsigned long long* tp_all = nullptr;      // [tp_size][kMaxRows] gathered
     unsigned long long* tp_best = nullptr;     // [kMaxRows] the argmax keys the control kernels read
+    // fused all-reduce over NVLink peer memory for decode-sized passes: the o
+    // and down GEMVs store partial rows into every rank's receive slots, a
+    // small kernel sums them (tp_reduce_kernel); larger passes use NCCL
+    bool tp_fused = false;
+    void* tp_region = nullptr;                 // this rank's receive slots + counters (peers write here)
+    size_t tp_recv_bytes = 0;
+    std::vector<void*> tp_peer;                // every rank's region as mapped here (IPC)
+    float** tp_recv_ptrs = nullptr;            // device [size]
+    unsigned long long** tp_cnt_ptrs = nullptr;  // device [size]
+    unsigned long long* tp_seq = nullptr;      // this rank's fused all-reduce count
+    int* tp_arrived = nullptr;
     // post-prefill draft state of step 0: its mass, weights and traced logits
     // (8 + 4V + 4V bytes)
     unsigned char* samp_snap = nullptr;
@@ -295,6 +306,40 @@ int act_quant(fl_engine* e, const float* x, uint8_t* q, int K, int M, const int*
     return FL_OK;
 }
 
+// x += the o / down projection g of the layer. Under tensor parallelism the
+// projection is row-parallel: decode-sized passes push partial rows to every
+// rank over NVLink and sum them there (fused path); otherwise rank 0 adds the
+// residual, the others store their partials and NCCL all-reduces x.
+int residual_linear(fl_engine* e, GemvParams g, float* x, int M, const int* dyn_M, const int* done, bool pdl) {
+    if (e->tp_size == 1) return launch_chunks(g, EPI_RESID, M, dyn_M, e->s, pdl);
+    if (e->tp_fused && M <= kMaxRows && g.P != 0 && tma_gemv_supported(g.N, g.K, M)) {
+        g.tp_recv = e->tp_recv_ptrs;
+        g.tp_cnt = e->tp_cnt_ptrs;
+        g.tp_seq = e->tp_seq;
+        g.tp_rank = e->tp_rank;
+        g.tp_size = e->tp_size;
+        g.tp_rows = kMaxRows;
+        FL_CHECK(launch_chunks(g, EPI_TP_PUSH, M, dyn_M, e->s, pdl));
+        TpReduceParams r = {};
+        r.x = x;
+        r.rows = M;
+        r.dyn_rows = dyn_M;
+        r.d = e->d;
+        r.recv = (const float*)e->tp_region;
+        r.cnt = (const unsigned long long*)((const char*)e->tp_region + e->tp_recv_bytes + 256);
+        r.size = e->tp_size;
+        r.cap = kMaxRows;
+        r.seq = e->tp_seq;
+        r.ctas_per_push = (unsigned long long)tma_gemv_grid();
+        r.arrived = e->tp_arrived;
+        r.done = done;
+        FL_CHECK_CUDA(launch_tp_reduce(r, e->s, pdl));
+        return FL_OK;
+    }
+    FL_CHECK(launch_chunks(g, e->tp_rank == 0 ? EPI_RESID : EPI_STORE, M, dyn_M, e->s, pdl));
+    return tp_allreduce_sum_f32(e->tp_comm, x, (size_t)M * e->d, e->s);
+}
+
 // Runs M rows (M <= R; dyn_M bounds the live rows when set, M <= kMaxRows)
 // through a stack. slot_base / pos are device pointers.
 int run_stack(fl_engine* e, Stack& S, float* x, int M, const int* dyn_M, const int* slot_base, const int* pos,
@@ -303,9 +348,6 @@ int run_stack(fl_engine* e, Stack& S, float* x, int M, const int* dyn_M, const i
     // Fused RMSNorm + quantization prologues need K % 128 == 0; otherwise a
     // separate act_quant launch produces xq.
     const bool fuse = (d % 128) == 0;
-    // row-parallel o / down under tensor parallelism: rank 0 adds the residual,
-    // the others store their partial sums, one all-reduce adds them up
-    const int resid_epi = (e->tp_size > 1 && e->tp_rank != 0) ? EPI_STORE : EPI_RESID;
     for (int l = 0; l < S.nl; l++) {
         LayerW& W = S.L[l];
         if (!fuse) FL_CHECK(act_quant(e, x, e->xq, d, M, dyn_M, 1, done, pdl));
@@ -351,8 +393,7 @@ int run_stack(fl_engine* e, Stack& S, float* x, int M, const int* dyn_M, const i
         g = gemv_base(W.o, e->aq, done);
         g.out = x;
         g.ldo = d;
-        FL_CHECK(launch_chunks(g, resid_epi, M, dyn_M, e->s, pdl));
-        if (e->tp_size > 1) FL_CHECK(tp_allreduce_sum_f32(e->tp_comm, x, (size_t)M * d, e->s));
+        FL_CHECK(residual_linear(e, g, x, M, dyn_M, done, pdl));
         if (!fuse) FL_CHECK(act_quant(e, x, e->xq, d, M, dyn_M, 1, done, pdl));
         g = gemv_base(W.gu, e->xq, done);
         if (fuse) {
@@ -366,8 +407,7 @@ int run_stack(fl_engine* e, Stack& S, float* x, int M, const int* dyn_M, const i
         g = gemv_base(W.down, e->hq, done);
         g.out = x;
         g.ldo = d;
-        FL_CHECK(launch_chunks(g, resid_epi, M, dyn_M, e->s, pdl));
-        if (e->tp_size > 1) FL_CHECK(tp_allreduce_sum_f32(e->tp_comm, x, (size_t)M * d, e->s));
+        FL_CHECK(residual_linear(e, g, x, M, dyn_M, done, pdl));
     }
     return FL_OK;
 }
@@ -729,6 +769,67 @@ int prefill_base(fl_engine* e, const int* prompt, int P) {
 // C ABI
 // ---------------------------------------------------------------------------
 
+// Maps every rank's receive region (CUDA IPC handles all-gathered over NCCL).
+// Fused mode needs every rank to succeed; the decision is collective.
+static int tp_fused_setup(fl_engine* e) {
+    const int g = e->tp_size;
+    e->tp_recv_bytes = (size_t)2 * g * kMaxRows * e->d * sizeof(float);
+    const size_t bytes = e->tp_recv_bytes + 256 + (size_t)2 * g * sizeof(unsigned long long);
+    int ok = 1;
+    cudaIpcMemHandle_t h;
+    if (cudaMalloc(&e->tp_region, bytes) != cudaSuccess || cudaMemset(e->tp_region, 0, bytes) != cudaSuccess ||
+        cudaIpcGetMemHandle(&h, e->tp_region) != cudaSuccess) {
+        ok = 0;
+        (void)cudaGetLastError();
+        memset(&h, 0, sizeof(h));
+    }
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handles are 64 bytes");
+    unsigned long long send[9];
+    memcpy(send, &h, 64);
+    send[8] = (unsigned long long)ok;
+    unsigned long long *dsend = nullptr, *drecv = nullptr;
+    FL_CHECK_CUDA(cudaMalloc(&dsend, sizeof(send)));
+    FL_CHECK_CUDA(cudaMalloc(&drecv, sizeof(send) * g));
+    std::vector<unsigned long long> all((size_t)9 * g);
+    int rc = FL_OK;
+    if (cudaMemcpy(dsend, send, sizeof(send), cudaMemcpyHostToDevice) != cudaSuccess ||
+        tp_allgather_u64(e->tp_comm, dsend, drecv, 9, e->s) != FL_OK || cudaStreamSynchronize(e->s) != cudaSuccess ||
+        cudaMemcpy(all.data(), drecv, sizeof(send) * g, cudaMemcpyDeviceToHost) != cudaSuccess)
+        rc = set_error(FL_E_CUDA, "tensor parallel: IPC handle exchange");
+    cudaFree(dsend);
+    cudaFree(drecv);
+    FL_CHECK(rc);
+    for (int q = 0; q < g; q++) ok = ok && all[(size_t)9 * q + 8] == 1;
+    if (!ok) return FL_OK;  // every rank stays on NCCL
+    e->tp_peer.assign(g, nullptr);
+    for (int q = 0; q < g; q++) {
+        if (q == e->tp_rank) {
+            e->tp_peer[q] = e->tp_region;
+            continue;
+        }
+        cudaIpcMemHandle_t hq;
+        memcpy(&hq, &all[(size_t)9 * q], 64);
+        FL_CHECK_CUDA(cudaIpcOpenMemHandle(&e->tp_peer[q], hq, cudaIpcMemLazyEnablePeerAccess));
+    }
+    std::vector<float*> rp(g);
+    std::vector<unsigned long long*> cp(g);
+    for (int q = 0; q < g; q++) {
+        rp[q] = (float*)e->tp_peer[q];
+        cp[q] = (unsigned long long*)((char*)e->tp_peer[q] + e->tp_recv_bytes + 256);
+    }
+    FL_CHECK_CUDA(cudaMalloc(&e->tp_recv_ptrs, sizeof(float*) * g));
+    FL_CHECK_CUDA(cudaMalloc(&e->tp_cnt_ptrs, sizeof(unsigned long long*) * g));
+    FL_CHECK_CUDA(cudaMalloc(&e->tp_seq, sizeof(unsigned long long)));
+    FL_CHECK_CUDA(cudaMalloc(&e->tp_arrived, sizeof(int)));
+    FL_CHECK_CUDA(cudaMemcpy(e->tp_recv_ptrs, rp.data(), sizeof(float*) * g, cudaMemcpyHostToDevice));
+    FL_CHECK_CUDA(cudaMemcpy(e->tp_cnt_ptrs, cp.data(), sizeof(unsigned long long*) * g, cudaMemcpyHostToDevice));
+    FL_CHECK_CUDA(cudaMemset(e->tp_seq, 0, sizeof(unsigned long long)));
+    FL_CHECK_CUDA(cudaMemset(e->tp_arrived, 0, sizeof(int)));
+    const char* v = getenv("FL_TP_FUSED");
+    e->tp_fused = !(v && v[0] == '0');
+    return FL_OK;
+}
+
 static fl_engine_t* engine_create(const fl_model_config_t* cfg, int device, int tp_rank, int tp_size,
                                   const unsigned char* tp_id) {
     if (!cfg) { set_error(FL_E_INVAL, "config is NULL"); return nullptr; }
@@ -786,6 +887,7 @@ static fl_engine_t* engine_create(const fl_model_config_t* cfg, int device, int 
             cudaMalloc(&e->tp_all, sizeof(unsigned long long) * kMaxRows * tp_size) != cudaSuccess ||
             cudaMalloc(&e->tp_best, sizeof(unsigned long long) * kMaxRows) != cudaSuccess)
             return fail(set_error(FL_E_NOMEM, "tensor parallel: key buffers"));
+        if (tp_fused_setup(e) != FL_OK) return fail(0);
     }
     for (auto& ev : e->ev)
         if (cudaEventCreate(&ev) != cudaSuccess) return fail(set_error(FL_E_CUDA, "event"));
@@ -865,8 +967,11 @@ FL_API void fl_engine_destroy(fl_engine_t* e) {
                     e->iota, e->tok, e->mask, e->st, e->st_snap, e->xd0_snap, e->seq, e->out, e->acc,
                     e->last_feat, e->attn_part, e->attn_cnt, e->step_bar, e->d_phases, e->d_trace,
                     e->samp_q, e->samp_p, e->samp_r, e->samp_trace, e->samp_snap, e->samp_m, e->samp_key,
-                    e->tp_keys, e->tp_all, e->tp_best};
+                    e->tp_keys, e->tp_all, e->tp_best, e->tp_recv_ptrs, e->tp_cnt_ptrs, e->tp_seq, e->tp_arrived};
     for (void* p : bufs) cudaFree(p);
+    for (int q = 0; q < (int)e->tp_peer.size(); q++)
+        if (q != e->tp_rank && e->tp_peer[q]) cudaIpcCloseMemHandle(e->tp_peer[q]);
+    cudaFree(e->tp_region);
     tp_comm_free(e->tp_comm);
     for (auto& ev : e->ev)
         if (ev) cudaEventDestroy(ev);

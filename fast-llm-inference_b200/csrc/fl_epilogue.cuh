@@ -54,6 +54,13 @@ __device__ __forceinline__ void pair_epilogue(const GemvParams& p, int r, int n0
             const size_t off = (((size_t)page * p.kv_heads + h) * kPageSize + (slot % kPageSize)) * p.head_dim + dd;
             *reinterpret_cast<__half2*>((is_k ? p.kv.k : p.kv.v) + off) = __floats2half2_rn(v0, v1);
         }
+    } else if (EPI == EPI_TP_PUSH) {
+        const size_t par = (size_t)(*p.tp_seq & 1ull);
+        for (int q = 0; q < p.tp_size; q++) {
+            float* dst = p.tp_recv[q] + ((par * p.tp_size + p.tp_rank) * p.tp_rows + r) * (size_t)p.ldo + n0;
+            if (has1) *reinterpret_cast<float2*>(dst) = make_float2(y0, y1);
+            else dst[0] = y0;
+        }
     } else if (EPI == EPI_SWIGLU) {
         // rows (n0, n0 + 1) = (gate_i, up_i): activations_avx2.c:86-105
         const float h = __fmul_rn(__fmul_rn(y0, poly_sigmoid(y0)), y1);

@@ -17,6 +17,7 @@ enum Epilogue : int {
     EPI_SWIGLU = 3,  // interleaved gate/up rows -> quantized SwiGLU output
     EPI_LOGITS = 4,  // out[m, n] = y and per-CTA argmax partials
     EPI_DOTS = 5,    // per-(m, n, block) int32 dots (test path)
+    EPI_TP_PUSH = 6, // tensor parallelism: partial rows stored into every rank's receive slot
 };
 
 // One paged KV pool of one layer: [pages][kv_heads][kPageSize][head_dim].
@@ -61,6 +62,14 @@ struct GemvParams {
     unsigned long long* amax_part;
     // EPI_DOTS
     int32_t* dots;            // [rows, N, K/32]
+    // EPI_TP_PUSH: output row r goes to every rank q's receive slot
+    // tp_recv[q][((parity * tp_size + tp_rank) * tp_rows + r) * ldo + n]
+    // (parity = *tp_seq & 1); when a CTA is done it adds 1 to every rank's
+    // counter tp_cnt[q][parity * tp_size + tp_rank] (TMA GEMV only)
+    float* const* tp_recv;
+    unsigned long long* const* tp_cnt;
+    const unsigned long long* tp_seq;
+    int tp_rank, tp_size, tp_rows;
 };
 
 // Chooses the kernel variant; `rowmode` selects per-row scales and
@@ -88,6 +97,26 @@ cudaError_t launch_gemv_auto(const GemvParams& p, int epi, cudaStream_t s, bool 
 int gemv_auto_grid(int N, int K);
 // Returns and clears the device error word (bounded waits that gave up).
 int take_device_error();
+
+// Tensor-parallel sum after EPI_TP_PUSH GEMVs (gemv_tma.cu): waits (bounded)
+// until every rank's counter for this parity reaches ctas_per_push x
+// (pushes of this parity so far + 1), then x[r] += sum over ranks q in order
+// of recv[parity][q][r] for r < rows (*dyn_rows when set); the last CTA
+// advances *seq. Every rank computes the same bits.
+struct TpReduceParams {
+    float* x;
+    int rows;
+    const int* dyn_rows;
+    int d;
+    const float* recv;                // this rank's receive slots [2][size][cap][d]
+    const unsigned long long* cnt;    // this rank's counters [2][size]
+    int size, cap;
+    unsigned long long* seq;          // this rank's all-reduce sequence number
+    unsigned long long ctas_per_push;
+    int* arrived;                     // CTA arrival counter (zero at rest)
+    const int* done;
+};
+cudaError_t launch_tp_reduce(const TpReduceParams& p, cudaStream_t s, bool pdl);
 
 // tcgen05 INT8 GEMM for many activation rows (gemm_tc.cu): block-mode tiled
 // weights (P != 0), K a multiple of 128, N of 16, activations already

@@ -19,6 +19,8 @@
 //     the activation rows), scales each block's int32 by its fp16 scale
 //     and reduces across warps once per 16-row tile;
 //   * every mbarrier wait is bounded (fl_tma.cuh).
+#include <algorithm>
+
 #include "fl_common.cuh"
 #include "fl_epilogue.cuh"
 #include "fl_kernels.h"
@@ -292,6 +294,68 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const Ge
         if (threadIdx.x < (unsigned)rows_m)
             p.amax_part[(size_t)(p.row0 + threadIdx.x) * gridDim.x + blockIdx.x] = best_s[threadIdx.x];
     }
+    if (EPI == EPI_TP_PUSH) {
+        // this CTA's rows are on every rank: publish (system-scope fence, then count)
+        __threadfence_system();
+        asm volatile("bar.sync 1, %0;" ::"n"(kCWarps * 32) : "memory");
+        if (threadIdx.x == 0) {
+            const int par = (int)(*p.tp_seq & 1ull);
+            for (int q = 0; q < p.tp_size; q++) atomicAdd(p.tp_cnt[q] + par * p.tp_size + p.tp_rank, 1ull);
+        }
+    }
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* a) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+    return v;
+}
+
+__global__ void __launch_bounds__(256) tp_reduce_kernel(const TpReduceParams p) {
+    __shared__ int ok_s;
+    pdl_trigger();
+    pdl_wait();
+    if (p.done && *p.done) return;  // every rank skips the same reductions
+    const unsigned long long s = *p.seq;
+    const int par = (int)(s & 1ull);
+    const unsigned long long need = p.ctas_per_push * (s / 2 + 1);
+    if (threadIdx.x == 0) ok_s = 1;
+    __syncthreads();
+    if (threadIdx.x < (unsigned)p.size) {
+        const unsigned long long* c = p.cnt + par * p.size + threadIdx.x;
+        if (ld_acquire_sys(c) < need) {
+            const long long t0 = clock64();
+            int spins = 0;
+            while (ld_acquire_sys(c) < need) {
+                __nanosleep(64);
+                // a bound of about two seconds of cycles: peers that never push raise the error
+                if (++spins % 1024 == 0 && clock64() - t0 > 4000000000ll) {
+                    atomicOr(&g_fl_error, kErrMbarTimeout);
+                    ok_s = 0;
+                    break;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (!ok_s) return;
+    const int rows = p.dyn_rows ? min(*p.dyn_rows, p.rows) : p.rows;
+    const size_t total = (size_t)rows * p.d;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t m = i / p.d, n = i - m * p.d;
+        float v = p.x[i];
+        for (int q = 0; q < p.size; q++) v = __fadd_rn(v, p.recv[(((size_t)par * p.size + q) * p.cap + m) * p.d + n]);
+        p.x[i] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(p.arrived, 1) == (int)gridDim.x - 1) {
+            *p.arrived = 0;
+            __threadfence();
+            *p.seq = s + 1;
+        }
+    }
 }
 
 int g_sm_count[16] = {0};
@@ -366,8 +430,24 @@ cudaError_t launch_gemv_tma(const GemvParams& p, int epi, cudaStream_t s, bool p
         case EPI_QKV: return launch_e<EPI_QKV>(p, geo, s, pdl);
         case EPI_SWIGLU: return launch_e<EPI_SWIGLU>(p, geo, s, pdl);
         case EPI_LOGITS: return launch_e<EPI_LOGITS>(p, geo, s, pdl);
+        case EPI_TP_PUSH: return launch_e<EPI_TP_PUSH>(p, geo, s, pdl);
         default: return cudaErrorInvalidValue;
     }
+}
+
+cudaError_t launch_tp_reduce(const TpReduceParams& p, cudaStream_t s, bool pdl) {
+    if (p.rows <= 0 || p.rows > p.cap || p.size < 1 || p.size > 256) return cudaErrorInvalidValue;
+    const int blocks = std::min(32, (int)(((size_t)p.rows * p.d + 1023) / 1024));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(blocks);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, tp_reduce_kernel, p);
 }
 
 cudaError_t launch_gemv_auto(const GemvParams& p, int epi, cudaStream_t s, bool pdl) {
