@@ -14,6 +14,7 @@ needed between timed iterations.
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
     python bench.py --workload sampled-batch [--seqs 64 --prompt-len 1024 --new-tokens 512 --k 6]
     torchrun --nproc-per-node N bench.py --gpus N --workload tp-medium [--prompt-len 512]
+    python bench.py --workload medusa [--prompt-len 512 --new-tokens 256]
 
 One process per GPU (torchrun for N > 1); this path does not shard (batch 1),
 so N GPUs run N independent replicas and `value` sums their tokens/s.
@@ -32,6 +33,12 @@ shaped base (40 layers, d 5120, 40 query / 10 KV heads x 128, SwiGLU 17920,
 vocab 32064) with a 2-layer draft of the same dims, greedy chain k = 4, bs1,
 sharded over the ranks (NCCL all-reduce after o and down); `value` = tokens/s
 of the one sequence (strong scaling), device-timed, max over ranks.
+
+--workload medusa is the Medusa configuration: the Phi-3-mini base with 4
+residual Medusa heads (3072 x 3072 INT8 each, shared LM head), per-head
+top-k 10/5/3/2, a 64-node candidate tree verified in one tree-masked pass
+(65 rows through the tcgen05 GEMM), greedy path acceptance and KV compaction;
+`value` = new tokens / device time of the decode (prefill included), bs1.
 """
 from __future__ import annotations
 
@@ -322,6 +329,51 @@ def run_tp_medium(a):
     return 0
 
 
+def run_medusa(a):
+    """Medusa heads on the Phi-3-mini base, bs1, one timed generate per step."""
+    import torch
+    import flb200
+    lib = flb200.Lib()
+    lib.check(lib.fl_cuda_init(0), "init")
+    topk, nodes = [10, 5, 3, 2], 64
+    cfg = dict(engine_cfg(((a.prompt_len + a.new_tokens + nodes + 2 + 63) // 64) * 64), draft_layers=0, medusa_heads=4)
+    eng = flb200.Engine(lib, cfg, 0)
+    eng.synthesize(SEED)
+    prompt = np.random.default_rng(PROMPT_SEED).integers(0, DIMS["vocab"], a.prompt_len).astype(np.int32)
+    for _ in range(a.warmup):
+        eng.medusa_generate(prompt, 16, topk, nodes)
+    stream = torch.cuda.ExternalStream(eng.stream())
+    torch.cuda.synchronize()
+    clocks = Clocks(0)
+    clocks.start()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    accs = []
+    for _ in range(a.steps):
+        toks, acc = eng.medusa_generate(prompt, a.new_tokens, topk, nodes)
+        accs.append(acc)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    acc_cat = np.concatenate(accs)
+    line = {
+        "metric": "Phi-3-mini Medusa decode tok/s @bs1", "value": a.steps * a.new_tokens / (ms / 1e3), "unit": "tok/s",
+        "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms / a.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u8xs8->s32, f32",
+        "data": "synthetic (seeded N(0,0.02) -> Q4_0 -> INT8 weights, uniform prompt ids)",
+        "config": {"workload": f"phi3-mini int8 + 4 Medusa heads, top-k {topk}, {nodes}-node tree, bs1, "
+                               f"prompt {a.prompt_len}, {a.new_tokens} new tokens per step (prefill included)"},
+        "medusa": {"tree_steps_per_generate": len(acc_cat) / a.steps, "mean_accepted": float(acc_cat.mean()),
+                   "step_us": ms * 1e3 / max(1, len(acc_cat))},
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+    eng.close()
+    return 0
+
+
 def run_sampled_batch(a):
     """Independent sampled sequences sharded across ranks (see the module
     docstring); one timed pass over each rank's share."""
@@ -426,7 +478,7 @@ def main():
                     help="one persistent tcgen05 kernel per speculative step (128-byte panels)")
     ap.add_argument("--m", type=int, default=5, help="activation rows for --microbench")
     ap.add_argument("--iters", type=int, default=10, help="sweeps for --microbench")
-    ap.add_argument("--workload", default="spec-bs1", choices=["spec-bs1", "sampled-batch", "tp-medium"])
+    ap.add_argument("--workload", default="spec-bs1", choices=["spec-bs1", "sampled-batch", "tp-medium", "medusa"])
     ap.add_argument("--seqs", type=int, default=64, help="sequences of --workload sampled-batch")
     a = ap.parse_args()
     if a.microbench:
@@ -435,6 +487,8 @@ def main():
         return run_sampled_batch(a)
     if a.workload == "tp-medium":
         return run_tp_medium(a)
+    if a.workload == "medusa":
+        return run_medusa(a)
     a.warmup = max(a.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
