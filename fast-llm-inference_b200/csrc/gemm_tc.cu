@@ -22,14 +22,16 @@
 //    block into its own BN TMEM columns; G consecutive blocks (G BN = 64)
 //    form a group with one commit, and the groups cycle through 8 TMEM
 //    buffers.
-//  - warps 5-12: readout, two per TMEM lane quadrant, each with BN / 2
-//    columns of its quadrant's 32 lanes. Per group
+//  - warps 5 ..: readout, four per TMEM lane quadrant (two when BN = 16),
+//    each with 8 or 16 columns of its quadrant's 32 lanes. Per group
 //    it loads the G blocks' s32 dots, releases the buffer and, while the next
 //    group's load is in flight, turns each dot into the float
 //    12582912 + dot by an integer add of 0x4B400000 (exact: |dot| < 2^22).
 //    One fma with d and -12582912 d (exact) then yields exactly the rounded
 //    product (float)dot * d, which is added to the row's running sum in block
-//    order: the sum is bit-identical to the sequential reference order.
+//    order: the sum is bit-identical to the sequential reference order. Pairs
+//    of columns go through the packed f32x2 fma / add (per-lane rounding
+//    identical to the scalar instructions).
 //  - After the last block the readout warps divide by 127 and apply the layer
 //    epilogue to (n, n + 1) pairs (lane shuffles).
 // Every wait is bounded (2 s of %globaltimer): on expiry the CTA raises an
@@ -48,8 +50,10 @@ namespace {
 
 __device__ int g_gemm_error = 0;
 
-constexpr int kProdW = 4, kMma = 4, kRd0 = 5, kWQ = 2;
-constexpr int kGThreads = (kRd0 + 4 * kWQ) * 32;
+constexpr int kProdW = 4, kMma = 4, kRd0 = 5;
+// readout warps per TMEM lane quadrant (8 columns each at least), threads
+__host__ __device__ constexpr int rd_per_quad(int bn) { return bn >= 32 ? 4 : 2; }
+__host__ __device__ constexpr int gemm_threads(int bn) { return (kRd0 + 4 * rd_per_quad(bn)) * 32; }
 constexpr int kProdT = kProdW * 32;
 constexpr int kInFlight = 6;  // weight stages in flight per producer thread
 constexpr int kTmaRows = 64;  // weight-tile rows fetched by TMA (the rest by cp.async)
@@ -172,8 +176,24 @@ struct GemmGeo {
     int stages, nbuf;
 };
 
+// Two floats in one 64-bit register: sm_100 packed arithmetic (f32x2), each
+// lane rounded exactly like the scalar instruction.
+__device__ __forceinline__ unsigned long long pk2(uint32_t lo, uint32_t hi) {
+    return ((unsigned long long)hi << 32) | lo;
+}
+__device__ __forceinline__ unsigned long long fma2(unsigned long long a, unsigned long long b, unsigned long long c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ unsigned long long add2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
 template <int BN, int EPI>
-__global__ void __launch_bounds__(kGThreads, 1)
+__global__ void __launch_bounds__(gemm_threads(BN), 1)
     gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a,
                       const GemvParams g, const GemmGeo geo) {
     extern __shared__ uint8_t smem_raw[];
@@ -183,6 +203,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
 
     constexpr int kBBytes = BN * kGroup;
     constexpr int kStage = kABytes + kBBytes;
+    constexpr int kWQ = rd_per_quad(BN);
     constexpr int kNRd = 4 * kWQ;
     constexpr int kG = group_blocks(BN);
     constexpr int kGPS = 4 / kG;  // groups per stage
@@ -299,9 +320,9 @@ __global__ void __launch_bounds__(kGThreads, 1)
         const int c0 = part * kCols;
         const int n = n0 + 32 * q + lane;
         const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0;
-        float acc[kCols];
+        unsigned long long acc2[kCols / 2];  // column pairs (2c, 2c + 1)
 #pragma unroll
-        for (int j = 0; j < kCols; j++) acc[j] = 0.0f;
+        for (int j = 0; j < kCols / 2; j++) acc2[j] = 0ull;
         // fp16 block scales of row n: four per K-group, prefetched one group ahead
         const bool live = n < N;
         auto load_sc = [&](int kg) -> uint2 {
@@ -319,9 +340,11 @@ __global__ void __launch_bounds__(kGThreads, 1)
         };
         auto scale_add = [&](const uint32_t* v, float d) {
             const float nmd = __fmul_rn(-kMagic, d);  // exact: 3 * 2^22 * d
+            const unsigned long long d2 = pk2(__float_as_uint(d), __float_as_uint(d));
+            const unsigned long long n2 = pk2(__float_as_uint(nmd), __float_as_uint(nmd));
 #pragma unroll
-            for (int c = 0; c < kCols; c++)
-                acc[c] = __fadd_rn(acc[c], __fmaf_rn(__uint_as_float(v[c] + kMagicBits), d, nmd));
+            for (int c = 0; c < kCols / 2; c++)
+                acc2[c] = add2(acc2[c], fma2(pk2(v[2 * c] + kMagicBits, v[2 * c + 1] + kMagicBits), d2, n2));
         };
         const int ngrp = nkg * kGPS;
         // the scales of the groups gi and gi + 1 (kG / 2 stages of four)
@@ -376,7 +399,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
         } else {
 #pragma unroll
             for (int c = 0; c < kCols; c++) {
-                const float y = __fdiv_rn(acc[c], 127.0f);
+                const uint32_t bits = (c & 1) ? (uint32_t)(acc2[c >> 1] >> 32) : (uint32_t)acc2[c >> 1];
+                const float y = __fdiv_rn(__uint_as_float(bits), 127.0f);
                 const float y1 = __shfl_xor_sync(0xffffffffu, y, 1);
                 const int m = m0 + c0 + c;
                 if ((lane & 1) == 0 && live && m < geo.M) pair_epilogue<EPI>(g, m, n, n + 1 < N, y, y1, nullptr);
@@ -445,7 +469,7 @@ cudaError_t launch_bn(const CUtensorMap& tw, const CUtensorMap& ta, const GemvPa
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     const dim3 grid((M + BN - 1) / BN, (g.N + kTileN - 1) / kTileN);
-    kern<<<grid, kGThreads, smem, s>>>(tw, ta, g, geo);
+    kern<<<grid, gemm_threads(BN), smem, s>>>(tw, ta, g, geo);
     return cudaGetLastError();
 }
 
