@@ -6,6 +6,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
 #include <map>
 #include <mutex>
 #include <string>
@@ -449,12 +450,39 @@ FL_API void medusa_tree_free(medusa_tree_t* t) {
     free(t);
 }
 
-// The draft + Medusa combination (reference medusa.h:210-229) has no caller in
-// the reference and is not part of this library's decode paths.
-FL_API int speculative_medusa_generate(void*, void (*)(void*, const float*, float*, int), medusa_model_t*, void*,
-                                       void (*)(void*, const int*, int, float*, int), const float*, int, int*, int,
-                                       const medusa_config_t*) {
-    set_error(FL_E_UNSUPPORTED, "speculative_medusa_generate is not provided (use speculative_generate or "
-                                "medusa_generate)");
-    return -1;
+// Draft + Medusa (reference medusa.h:210-229): draft_model is a draft_model_t
+// bound to the engine, draft_forward fl_cuda_target_forward (the draft runs
+// inside the engine) or NULL, target_model the engine with its base_forward
+// fl_cuda_base_forward; the draft chain length is config->num_heads (at most
+// 7), the Medusa heads and tree settings as for medusa_generate. Greedy only.
+FL_API int speculative_medusa_generate(void* draft_model, void (*draft_forward)(void*, const float*, float*, int),
+                                       medusa_model_t* medusa, void* target_model,
+                                       void (*target_forward)(void*, const int*, int, float*, int),
+                                       const float* prompt_hidden, int prompt_len, int* output_tokens, int num_tokens,
+                                       const medusa_config_t* config) {
+    if (!draft_model || !medusa || !target_model || !prompt_hidden || prompt_len <= 0 || !output_tokens ||
+        num_tokens <= 0 || !config)
+        return -1;
+    if (target_forward != fl_cuda_base_forward || (draft_forward && draft_forward != fl_cuda_target_forward)) {
+        set_error(FL_E_UNSUPPORTED, "speculative_medusa_generate: the forwards must be fl_cuda_base_forward "
+                                    "(target) and fl_cuda_target_forward or NULL (draft)");
+        return -1;
+    }
+    if (config->temperature > 0.0f) {
+        set_error(FL_E_UNSUPPORTED, "speculative_medusa_generate: only greedy acceptance (temperature <= 0)");
+        return -1;
+    }
+    fl_engine_t* e = (fl_engine_t*)target_model;
+    if (fl_engine_bind_draft(e, (draft_model_t*)draft_model) != FL_OK || medusa_bind(e, medusa) != FL_OK) return -1;
+    std::vector<int> topk;
+    int max_nodes = 64;
+    const int H = medusa_tree_settings(medusa, config, topk, &max_nodes);
+    if (H <= 0) return -1;
+    const int K = std::min(std::max(config->num_heads, 1), 7);
+    std::vector<int> prompt(prompt_len);
+    for (int i = 0; i < prompt_len; i++) prompt[i] = (int)prompt_hidden[i];
+    if (fl_engine_spec_medusa_generate(e, prompt.data(), prompt_len, num_tokens, K, topk.data(), H,
+                                       std::max(max_nodes, K + 2), output_tokens, nullptr, nullptr) != FL_OK)
+        return -1;
+    return num_tokens;
 }

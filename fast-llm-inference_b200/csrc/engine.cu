@@ -1748,6 +1748,44 @@ int build_tree(int root_tok, int H, const int* topk, const int* tok, const float
     return keep + 1;
 }
 
+// Draft + Medusa candidate tree: the draft chain d_1 .. d_K as one branch
+// under the root (always kept), then the Medusa tree's nodes in its own order
+// (parents first), each merged with an existing node of the same token under
+// the same parent or added while fewer than max_nodes nodes exist; a node
+// whose parent was dropped is dropped. Returns the node count.
+int merge_chain_tree(int root_tok, const int* chain, int K, const std::vector<int>& mtok, const std::vector<int>& mpar,
+                     const std::vector<int>& mdep, int max_nodes, std::vector<int>& ntok, std::vector<int>& npar,
+                     std::vector<int>& ndep) {
+    ntok.assign(1, root_tok);
+    npar.assign(1, -1);
+    ndep.assign(1, 0);
+    for (int j = 0; j < K && (int)ntok.size() < max_nodes; j++) {
+        ntok.push_back(chain[j]);
+        npar.push_back(j);
+        ndep.push_back(j + 1);
+    }
+    std::vector<int> map(mtok.size(), -1);
+    map[0] = 0;
+    for (size_t i = 1; i < mtok.size(); i++) {
+        const int pp = map[mpar[i]];
+        if (pp < 0) continue;
+        int found = -1;
+        for (size_t k = 1; k < ntok.size(); k++)
+            if (npar[k] == pp && ntok[k] == mtok[i]) {
+                found = (int)k;
+                break;
+            }
+        if (found < 0 && (int)ntok.size() < max_nodes) {
+            found = (int)ntok.size();
+            ntok.push_back(mtok[i]);
+            npar.push_back(pp);
+            ndep.push_back(mdep[i]);
+        }
+        map[i] = found;
+    }
+    return (int)ntok.size();
+}
+
 }  // namespace
 
 FL_API int fl_engine_medusa_generate(fl_engine_t* e, const int* prompt, int P, int n_new, const int* topk, int H,
@@ -1878,5 +1916,174 @@ FL_API int fl_engine_medusa_generate(fl_engine_t* e, const int* prompt, int P, i
 #undef FL_MED
     cleanup();
     if (take_device_error() != 0) return set_error(FL_E_TIMEOUT, "medusa_generate: a bounded device wait gave up");
+    return FL_OK;
+}
+
+// Draft + Medusa (medusa.h:210-229 speculative_medusa_generate; the reference
+// declares it without code): each step the EAGLE-style draft drafts a chain of
+// K tokens from its state at the newest position while the Medusa heads
+// propose per-depth candidates from the base feature; the merged tree
+// (merge_chain_tree) is verified in one tree-masked base pass, the longest
+// path of the base model's greedy choices is accepted (plus the base token
+// after it), the base KV of that path is compacted, and the draft catches up
+// over the accepted positions from the base features of the path's tree rows
+// (draft input at position p = F_{p-1} + E[t_p]). The output is the base
+// model's greedy stream whatever the tree.
+FL_API int fl_engine_spec_medusa_generate(fl_engine_t* e, const int* prompt, int P, int n_new, int K, const int* topk,
+                                          int H, int max_nodes, int* out, int* acc_hist, int* steps_out) {
+    FL_CHECK(check_ready(e, true));
+    if (!prompt || !out || !topk || P <= 0 || n_new <= 0 || K < 1 || K > kMaxDraft || H <= 0 ||
+        H > (int)e->medusa.size() || H > kMaxRows || max_nodes < K + 2 || max_nodes > 256 ||
+        P + n_new + max_nodes + K + 2 > e->R)
+        return set_error(FL_E_INVAL, "spec_medusa_generate: bad arguments, missing heads or context too long");
+    if (e->tp_size > 1) return set_error(FL_E_UNSUPPORTED, "spec_medusa_generate: not on a tensor-parallel engine");
+    int kmax = 1;
+    for (int h = 0; h < H; h++) {
+        if (topk[h] < 1 || topk[h] > 32) return set_error(FL_E_INVAL, "spec_medusa_generate: top-k must be 1..32");
+        kmax = std::max(kmax, topk[h]);
+    }
+    const int d = e->d, V = e->V;
+    cudaStream_t s = e->s;
+    float *mf = nullptr, *my = nullptr, *mz = nullptr, *mprob = nullptr;
+    int *mk = nullptr, *mtt = nullptr, *mtok = nullptr, *mpos = nullptr, *mtarget = nullptr, *mpath = nullptr,
+        *mchain = nullptr, *mcat = nullptr;
+    KvLayer* dkv = nullptr;
+    auto cleanup = [&]() {
+        void* bufs[] = {mf, my, mz, mprob, mk, mtt, mtok, mpos, mtarget, mpath, mchain, mcat, dkv};
+        for (void* p : bufs) cudaFree(p);
+    };
+    auto fail = [&](int rc) {
+        cleanup();
+        return rc;
+    };
+#define FL_SM_CUDA(expr)                                                     \
+    do {                                                                     \
+        cudaError_t fl_e_ = (expr);                                          \
+        if (fl_e_ != cudaSuccess) return fail(cuda_error(fl_e_, #expr));     \
+    } while (0)
+#define FL_SM(expr)                       \
+    do {                                  \
+        int fl_r_ = (expr);               \
+        if (fl_r_ != FL_OK) return fail(fl_r_); \
+    } while (0)
+    FL_SM_CUDA(cudaMalloc(&mf, sizeof(float) * d));
+    FL_SM_CUDA(cudaMalloc(&my, sizeof(float) * (size_t)H * d));
+    FL_SM_CUDA(cudaMalloc(&mz, sizeof(float) * (size_t)H * d));
+    FL_SM_CUDA(cudaMalloc(&mprob, sizeof(float) * (size_t)H * kmax));
+    FL_SM_CUDA(cudaMalloc(&mk, sizeof(int) * H));
+    FL_SM_CUDA(cudaMalloc(&mtt, sizeof(int) * (size_t)H * kmax));
+    FL_SM_CUDA(cudaMalloc(&mtok, sizeof(int) * max_nodes));
+    FL_SM_CUDA(cudaMalloc(&mpos, sizeof(int) * max_nodes));
+    FL_SM_CUDA(cudaMalloc(&mtarget, sizeof(int) * max_nodes));
+    FL_SM_CUDA(cudaMalloc(&mpath, sizeof(int) * max_nodes));
+    FL_SM_CUDA(cudaMalloc(&mchain, sizeof(int) * kMaxRows));
+    FL_SM_CUDA(cudaMalloc(&mcat, sizeof(int) * max_nodes));
+    FL_SM_CUDA(cudaMalloc(&dkv, sizeof(KvLayer) * e->base.nl));
+    FL_SM_CUDA(cudaMemcpyAsync(dkv, e->base.kv.data(), sizeof(KvLayer) * e->base.nl, cudaMemcpyHostToDevice, s));
+    FL_SM_CUDA(cudaMemcpyAsync(mk, topk, sizeof(int) * H, cudaMemcpyHostToDevice, s));
+    FL_SM(ensure_mask(e, max_nodes));
+
+    // prefill: base KV 0 .. P-1 and the first token; draft catch-up over 0 .. P
+    FL_SM(prefill_base(e, prompt, P));
+    FL_SM_CUDA(cudaMemcpyAsync(mf, e->x + (size_t)(P - 1) * d, sizeof(float) * d, cudaMemcpyDeviceToDevice, s));
+    FL_SM_CUDA(launch_embed_rows(e->embed, e->Vg, e->seq, e->x, 1, e->x2, d, P + 1, nullptr, nullptr, s, false));
+    FL_SM(run_stack(e, e->draft, e->x2, P + 1, nullptr, e->iota, e->iota, nullptr, nullptr, false));
+    FL_SM_CUDA(cudaMemcpyAsync(e->x_d, e->x2 + (size_t)P * d, sizeof(float) * d, cudaMemcpyDeviceToDevice, s));
+    int cur_tok = 0;
+    FL_SM_CUDA(cudaMemcpyAsync(&cur_tok, e->seq + P, sizeof(int), cudaMemcpyDeviceToHost, s));
+    FL_SM_CUDA(cudaStreamSynchronize(s));
+    int produced = 0, steps = 0, n = P;
+    out[produced++] = cur_tok;
+    std::vector<int> htok((size_t)H * kmax), target(max_nodes), chain(K), mtk, mpr, mdp, ntok, npar, ndep, path, cat;
+    std::vector<float> hprob((size_t)H * kmax);
+    std::vector<int> hpos(max_nodes);
+    std::vector<uint8_t> mask((size_t)max_nodes * max_nodes);
+    FL_SM_CUDA(cudaEventRecord(e->ev[0], s));
+    while (produced < n_new) {
+        // draft chain from the draft state at position n (x_d row 0)
+        for (int j = 0; j < K; j++) {
+            if (j > 0) {
+                FL_SM_CUDA(launch_embed_rows(e->embed, e->Vg, mchain + j - 1, e->x_d, 0, e->x_d, d, 1, nullptr, nullptr, s,
+                                             false));
+                FL_SM(run_stack(e, e->draft, e->x_d, 1, nullptr, e->iota + n + j, e->iota + n + j, nullptr, nullptr,
+                                false));
+            }
+            FL_SM(run_lm(e, e->x_d, 1, nullptr, nullptr, false));
+            FL_SM_CUDA(launch_argmax_rows(amax_keys(e), amax_nparts(e), 1, mchain + j, nullptr, s));
+        }
+        // Medusa heads from the base feature of position n - 1
+        FL_SM_CUDA(launch_medusa_z(mf, my, e->x2, mz, d, 0, e->c.norm_eps, s));
+        for (int h = 0; h < H; h++) FL_SM(gemv_rows(e, e->medusa[h], e->x2, 1, false, my + (size_t)h * d, d));
+        FL_SM_CUDA(launch_medusa_z(mf, my, nullptr, mz, d, H, e->c.norm_eps, s));
+        FL_SM(gemv_rows(e, e->lm, mz, H, false, e->logits, V));
+        FL_SM_CUDA(launch_topk_rows(e->logits, H, V, V, mk, kmax, mtt, mprob, s));
+        FL_SM_CUDA(cudaMemcpyAsync(chain.data(), mchain, sizeof(int) * K, cudaMemcpyDeviceToHost, s));
+        FL_SM_CUDA(cudaMemcpyAsync(htok.data(), mtt, sizeof(int) * htok.size(), cudaMemcpyDeviceToHost, s));
+        FL_SM_CUDA(cudaMemcpyAsync(hprob.data(), mprob, sizeof(float) * hprob.size(), cudaMemcpyDeviceToHost, s));
+        FL_SM_CUDA(cudaStreamSynchronize(s));
+        build_tree(cur_tok, H, topk, htok.data(), hprob.data(), kmax, max_nodes, mtk, mpr, mdp);
+        const int M = merge_chain_tree(cur_tok, chain.data(), K, mtk, mpr, mdp, max_nodes, ntok, npar, ndep);
+        for (int i = 0; i < M; i++) {
+            hpos[i] = n + ndep[i];
+            for (int j = 0; j < M; j++) mask[(size_t)i * M + j] = 0;
+            for (int j = i; j >= 0; j = npar[j]) mask[(size_t)i * M + j] = 1;
+        }
+        FL_SM_CUDA(cudaMemcpyAsync(mtok, ntok.data(), sizeof(int) * M, cudaMemcpyHostToDevice, s));
+        FL_SM_CUDA(cudaMemcpyAsync(mpos, hpos.data(), sizeof(int) * M, cudaMemcpyHostToDevice, s));
+        FL_SM_CUDA(cudaMemcpyAsync(e->mask, mask.data(), (size_t)M * M, cudaMemcpyHostToDevice, s));
+        FL_SM_CUDA(launch_embed_rows(e->embed, e->Vg, mtok, nullptr, 0, e->x, d, M, nullptr, nullptr, s, false));
+        FL_SM(run_stack(e, e->base, e->x, M, nullptr, e->iota + n, mpos, e->mask, nullptr, false));
+        for (int r0 = 0; r0 < M; r0 += kMaxRows) {
+            const int m = std::min(kMaxRows, M - r0);
+            FL_SM(run_lm(e, e->x + (size_t)r0 * d, m, nullptr, nullptr, false));
+            FL_SM_CUDA(launch_argmax_rows(amax_keys(e), amax_nparts(e), m, mtarget + r0, nullptr, s));
+        }
+        FL_SM_CUDA(cudaMemcpyAsync(target.data(), mtarget, sizeof(int) * M, cudaMemcpyDeviceToHost, s));
+        FL_SM_CUDA(cudaStreamSynchronize(s));
+        path.assign(1, 0);
+        int cur = 0;
+        for (;;) {
+            int nxt = -1;
+            for (int c2 = 1; c2 < M; c2++)
+                if (npar[c2] == cur && ntok[c2] == target[cur]) {
+                    nxt = c2;
+                    break;
+                }
+            if (nxt < 0) break;
+            path.push_back(nxt);
+            cur = nxt;
+        }
+        const int a = (int)path.size() - 1;
+        if (acc_hist) acc_hist[steps] = a;
+        steps++;
+        for (int j = 1; j <= a + 1 && produced < n_new; j++) out[produced++] = j <= a ? ntok[path[j]] : target[cur];
+        // draft catch-up over positions n+1 .. n+a+1: F of the path's tree rows + E[token]
+        cat.resize(a + 1);
+        for (int j = 0; j <= a; j++) cat[j] = j < a ? ntok[path[j + 1]] : target[cur];
+        FL_SM_CUDA(cudaMemcpyAsync(mcat, cat.data(), sizeof(int) * (a + 1), cudaMemcpyHostToDevice, s));
+        for (int j = 0; j <= a; j++)
+            FL_SM_CUDA(cudaMemcpyAsync(e->x2 + (size_t)j * d, e->x + (size_t)path[j] * d, sizeof(float) * d,
+                                       cudaMemcpyDeviceToDevice, s));
+        if (a > 0) {
+            FL_SM_CUDA(cudaMemcpyAsync(mpath, path.data(), sizeof(int) * (a + 1), cudaMemcpyHostToDevice, s));
+            FL_SM_CUDA(launch_kv_compact(dkv, e->base.nl, e->base.block_table, e->Hkv, e->hd, e->iota + n, mpath, a, s));
+        }
+        FL_SM_CUDA(cudaMemcpyAsync(mf, e->x + (size_t)cur * d, sizeof(float) * d, cudaMemcpyDeviceToDevice, s));
+        FL_SM_CUDA(launch_embed_rows(e->embed, e->Vg, mcat, e->x2, 0, e->x2, d, a + 1, nullptr, nullptr, s, false));
+        FL_SM(run_stack(e, e->draft, e->x2, a + 1, nullptr, e->iota + n + 1, e->iota + n + 1, nullptr, nullptr, false));
+        FL_SM_CUDA(cudaMemcpyAsync(e->x_d, e->x2 + (size_t)a * d, sizeof(float) * d, cudaMemcpyDeviceToDevice, s));
+        cur_tok = target[cur];
+        n += a + 1;
+    }
+    FL_SM_CUDA(cudaEventRecord(e->ev[1], s));
+    FL_SM_CUDA(cudaEventSynchronize(e->ev[1]));
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, e->ev[0], e->ev[1]);
+    e->t_total_us = ms * 1000.0;
+    if (steps_out) *steps_out = steps;
+#undef FL_SM_CUDA
+#undef FL_SM
+    cleanup();
+    if (take_device_error() != 0) return set_error(FL_E_TIMEOUT, "spec_medusa_generate: a bounded device wait gave up");
     return FL_OK;
 }

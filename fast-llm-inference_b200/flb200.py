@@ -140,6 +140,7 @@ _SIGS = {
     "fl_engine_step_trace": (I, [VP, VP, VP, I]),
     "fl_engine_step_trace_stages": (I, [VP, VP]),
     "fl_engine_medusa_generate": (I, [VP, VP, I, I, VP, I, I, VP, VP, VP]),
+    "fl_engine_spec_medusa_generate": (I, [VP, VP, I, I, I, VP, I, I, VP, VP, VP]),
     "fl_engine_draft_bound": (I, [VP, VP]),
     "fl_engine_note_draft": (None, [VP, VP]),
     "fl_engine_bench_linear": (I, [VP, I, I, I, I, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
@@ -166,6 +167,7 @@ _SIGS = {
     "medusa_model_load": (I, [VP, C.c_char_p]),
     "medusa_model_free": (None, [VP]),
     "medusa_generate": (I, [VP, VP, VP, VP, I, VP, I, C.POINTER(MedusaConfig)]),
+    "speculative_medusa_generate": (I, [C.POINTER(DraftModel), VP, VP, VP, VP, VP, I, VP, I, C.POINTER(MedusaConfig)]),
     "fl_medusa_set_tree": (I, [VP, VP, I, I]),
 }
 
@@ -443,6 +445,18 @@ class Engine:
         steps = C.c_int(0)
         self.lib.check(self.lib.fl_engine_medusa_generate(self.h, ptr(p), len(p), n_new, ptr(tk), len(tk), max_nodes,
                                                           ptr(o), ptr(acc), C.byref(steps)), "medusa_generate")
+        return o, acc[: steps.value]
+
+    def spec_medusa_generate(self, prompt, n_new, k, topk, max_nodes):
+        """Draft chain + Medusa tree, greedy: (tokens, accepted count per step)."""
+        p = np.ascontiguousarray(prompt, np.int32)
+        tk = np.ascontiguousarray(topk, np.int32)
+        o = np.empty(n_new, np.int32)
+        acc = np.zeros(n_new + 1, np.int32)
+        steps = C.c_int(0)
+        self.lib.check(self.lib.fl_engine_spec_medusa_generate(self.h, ptr(p), len(p), n_new, k, ptr(tk), len(tk),
+                                                               max_nodes, ptr(o), ptr(acc), C.byref(steps)),
+                       "spec_medusa_generate")
         return o, acc[: steps.value]
 
     def step_trace_stages(self):

@@ -311,6 +311,18 @@ int fl_engine_step_trace_stages(const fl_engine_t* e, unsigned long long* t);
  * H <= medusa_heads loaded heads and P + n_new + max_nodes + 2 <= max_seq_len. */
 int fl_engine_medusa_generate(fl_engine_t* e, const int* prompt, int P, int n_new, const int* topk, int H,
                               int max_nodes, int* out, int* acc_hist, int* steps);
+
+/* Draft + Medusa (speculative_medusa_generate): each step the draft drafts a
+ * chain of k tokens and the Medusa heads propose per-depth top-k candidates;
+ * the chain (always kept) and the heads' tree (merged, then added in score
+ * order up to max_nodes nodes) are verified in one tree-masked base pass;
+ * the longest path of the base model's greedy choices is accepted, its base
+ * KV compacted, and the draft catches up over the accepted positions from
+ * the base features of the path's tree rows. The output is the base model's
+ * greedy stream. Needs a draft stack and Medusa heads. */
+int fl_engine_spec_medusa_generate(fl_engine_t* e, const int* prompt, int prompt_len, int n_new, int k,
+                                   const int* topk, int n_heads, int max_nodes, int* out, int* acc_hist,
+                                   int* steps);
 /* 1 when `draft` (a draft_model_t*) is the draft whose weights the engine
  * holds; fl_engine_note_draft records it after a load. */
 int fl_engine_draft_bound(const fl_engine_t* e, const void* draft);

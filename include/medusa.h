@@ -122,8 +122,14 @@ int medusa_generate(void* base_model,
  * config->top_k), at most max_nodes tree nodes (default 64). */
 int fl_medusa_set_tree(medusa_model_t* model, const int* topk, int n, int max_nodes);
 
-/* Draft + Medusa combination (reference medusa.h:210). Not provided by this
- * library: returns -1 and records the reason. */
+/* Draft + Medusa combination (reference medusa.h:210; the reference ships no
+ * implementation). draft_model: a draft_model_t loaded for the engine;
+ * draft_forward: fl_cuda_target_forward or NULL (the draft runs inside the
+ * engine); target_model: the engine, target_forward fl_cuda_base_forward.
+ * Each step the draft chain (config->num_heads tokens, at most 7) and the
+ * Medusa heads' candidate tree (fl_medusa_set_tree settings) are verified
+ * together in one tree pass; greedy acceptance of the longest matching path.
+ * Returns num_tokens or -1. */
 int speculative_medusa_generate(void* draft_model,
                                 void (*draft_forward)(void*, const float*, float*, int),
                                 medusa_model_t* medusa, void* target_model,

@@ -457,3 +457,41 @@ def test_sampled_batch_independent_of_sharding(small):
     assert np.array_equal(all_toks, np.stack(singles))
     assert np.array_equal(part, all_toks[2:])
     assert len({tuple(r) for r in all_toks.tolist()}) == 4 and secs > 0 and steps.min() >= 1
+
+
+def test_spec_medusa_stream_is_greedy(gpu, orc):
+    """Draft chain + Medusa heads in one tree: the output is the base model's
+    greedy stream (oracle), with multi-token steps; the reference signature
+    speculative_medusa_generate gives the same tokens."""
+    import ctypes as C
+    dims = dict(SMALL, vocab=16)
+    w, embed = make_weights(gpu, dims, seed=3, draft_layers=1, medusa_heads=4)
+    eng = flb200.Engine(gpu, engine_cfg(dims, draft_layers=1, medusa_heads=4, max_seq_len=256))
+    load_engine(eng, w, embed)
+    p = prompt(4, 12, dims["vocab"])
+    got, acc = eng.spec_medusa_generate(p, 40, 3, MEDUSA_TOPK, 48)
+    om = oracle_model(orc, dims, w, embed, draft_layers=1, n_medusa=4)
+    want, margins = om.greedy(p, 40)
+    assert_stream_matches(got, want, margins)
+    assert acc.max() >= 2, f"no multi-node path accepted: {acc.tolist()}"
+    eng.close()
+    # the same through the reference API: draft and heads loaded from "synthetic:SEED"
+    eng = flb200.Engine(gpu, engine_cfg(dims, draft_layers=1, medusa_heads=4, max_seq_len=256))
+    load_engine(eng, {k: v for k, v in w.items() if k[0] == 0 or k[0] == 3}, embed)
+    dm = gpu.draft_model_create(1, dims["d"], dims["ffn"], dims["vocab"])
+    assert gpu.draft_model_load(dm, b"synthetic:3") == 0
+    mm = gpu.medusa_model_create(4, dims["d"], dims["vocab"])
+    assert gpu.medusa_model_load(mm, b"synthetic:3") == 0
+    tk = np.array(MEDUSA_TOPK, np.int32)
+    assert gpu.fl_medusa_set_tree(mm, flb200.ptr(tk), 4, 48) == 0
+    cfg = flb200.MedusaConfig(3, 10, 0.0)
+    ph = p.astype(np.float32)
+    out = np.empty(40, np.int32)
+    n = gpu.speculative_medusa_generate(dm, C.cast(gpu.so.fl_cuda_target_forward, C.c_void_p), mm, eng.h,
+                                        C.cast(gpu.so.fl_cuda_base_forward, C.c_void_p), flb200.ptr(ph), len(p),
+                                        flb200.ptr(out), 40, C.byref(cfg))
+    assert n == 40, gpu.err()
+    assert_stream_matches(out, want, margins)
+    gpu.medusa_model_free(mm)
+    gpu.draft_model_free(dm)
+    eng.close()
