@@ -132,6 +132,14 @@ int medusa_tree_settings(const medusa_model_t* m, const medusa_config_t* cfg, st
     return H;
 }
 
+int medusa_bind(fl_engine_t* e, medusa_model_t* m);
+fl_engine_t* medusa_engine(const medusa_model_t* m) { return bound(m); }
+
+FL_API int fl_engine_bind_medusa(fl_engine_t* e, void* m) {
+    if (!e || !m) return set_error(FL_E_INVAL, "bind_medusa: NULL");
+    return medusa_bind(e, (medusa_model_t*)m);
+}
+
 int medusa_bind(fl_engine_t* e, medusa_model_t* m) {
     if (bound(m) == e) return FL_OK;
     for (int h = 0; h < m->num_heads; h++) {

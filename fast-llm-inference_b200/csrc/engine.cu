@@ -1712,7 +1712,8 @@ struct MedCand {
 // outscores its parent and loses ties to it, so the kept set is
 // ancestor-closed and every parent precedes its children.
 int build_tree(int root_tok, int H, const int* topk, const int* tok, const float* prob, int kmax, int max_nodes,
-               std::vector<int>& ntok, std::vector<int>& npar, std::vector<int>& ndep) {
+               std::vector<int>& ntok, std::vector<int>& npar, std::vector<int>& ndep,
+               std::vector<float>* nscore = nullptr) {
     std::vector<MedCand> c;
     int pb = 0, pe = 0;
     for (int h = 0; h < H; h++) {
@@ -1740,10 +1741,12 @@ int build_tree(int root_tok, int H, const int* topk, const int* tok, const float
     ntok.assign(1, root_tok);
     npar.assign(1, -1);
     ndep.assign(1, 0);
+    if (nscore) nscore->assign(1, 1.0f);
     for (int i = 0; i < keep; i++) {
         ntok.push_back(s[i].token);
         npar.push_back(s[i].parent_gen < 0 ? 0 : where[s[i].parent_gen]);
         ndep.push_back(s[i].depth);
+        if (nscore) nscore->push_back(s[i].score);
     }
     return keep + 1;
 }
@@ -2085,5 +2088,184 @@ FL_API int fl_engine_spec_medusa_generate(fl_engine_t* e, const int* prompt, int
 #undef FL_SM
     cleanup();
     if (take_device_error() != 0) return set_error(FL_E_TIMEOUT, "spec_medusa_generate: a bounded device wait gave up");
+    return FL_OK;
+}
+
+// Medusa candidate tree from a base feature F (host [d]): the heads' per-head
+// top-k (h = RMSNorm(F), z_i = h + SiLU(W_i h), LM(z_i)) and the tree rule of
+// include/medusa.h. root >= 0 is the root token; root < 0 takes the base LM
+// head's argmax of F. Writes up to max_nodes nodes; returns the node count.
+FL_API int fl_engine_medusa_tree(fl_engine_t* e, const float* F, int root, const int* topk, int H, int max_nodes,
+                                 int* tok, int* parent, int* depth, float* score) {
+    FL_CHECK(check_ready(e, false));
+    if (!F || !topk || !tok || !parent || !depth || H <= 0 || H > (int)e->medusa.size() || H > kMaxRows ||
+        max_nodes < 1 || max_nodes > 256)
+        return set_error(FL_E_INVAL, "medusa_tree: bad arguments or missing heads");
+    if (e->tp_size > 1) return set_error(FL_E_UNSUPPORTED, "medusa_tree: not on a tensor-parallel engine");
+    int kmax = 1;
+    for (int h = 0; h < H; h++) {
+        if (topk[h] < 1 || topk[h] > 32) return set_error(FL_E_INVAL, "medusa_tree: top-k must be 1..32");
+        kmax = std::max(kmax, topk[h]);
+    }
+    const int d = e->d, V = e->V;
+    cudaStream_t s = e->s;
+    float *mf = nullptr, *my = nullptr, *mz = nullptr, *mprob = nullptr;
+    int *mk = nullptr, *mtt = nullptr, *mroot = nullptr;
+    auto cleanup = [&]() {
+        void* bufs[] = {mf, my, mz, mprob, mk, mtt, mroot};
+        for (void* p : bufs) cudaFree(p);
+    };
+    int rc = FL_OK;
+    std::vector<int> htok((size_t)H * kmax), ntok, npar, ndep;
+    std::vector<float> hprob((size_t)H * kmax), nscore;
+    do {
+        if (cudaMalloc(&mf, sizeof(float) * d) || cudaMalloc(&my, sizeof(float) * (size_t)H * d) ||
+            cudaMalloc(&mz, sizeof(float) * (size_t)H * d) || cudaMalloc(&mprob, sizeof(float) * (size_t)H * kmax) ||
+            cudaMalloc(&mk, sizeof(int) * H) || cudaMalloc(&mtt, sizeof(int) * (size_t)H * kmax) ||
+            cudaMalloc(&mroot, sizeof(int))) {
+            rc = set_error(FL_E_NOMEM, "medusa_tree: device buffers");
+            break;
+        }
+        if (cudaMemcpyAsync(mf, F, sizeof(float) * d, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+            cudaMemcpyAsync(mk, topk, sizeof(int) * H, cudaMemcpyHostToDevice, s) != cudaSuccess) {
+            rc = set_error(FL_E_CUDA, "medusa_tree: upload");
+            break;
+        }
+        if (root < 0) {
+            if ((rc = run_lm(e, mf, 1, nullptr, nullptr, false)) != FL_OK) break;
+            if (launch_argmax_rows(amax_keys(e), amax_nparts(e), 1, mroot, nullptr, s) != cudaSuccess ||
+                cudaMemcpyAsync(&root, mroot, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess) {
+                rc = set_error(FL_E_CUDA, "medusa_tree: root");
+                break;
+            }
+        }
+        if (launch_medusa_z(mf, my, e->x2, mz, d, 0, e->c.norm_eps, s) != cudaSuccess) {
+            rc = set_error(FL_E_CUDA, "medusa_tree: heads");
+            break;
+        }
+        for (int h = 0; h < H && rc == FL_OK; h++) rc = gemv_rows(e, e->medusa[h], e->x2, 1, false, my + (size_t)h * d, d);
+        if (rc != FL_OK) break;
+        if (launch_medusa_z(mf, my, nullptr, mz, d, H, e->c.norm_eps, s) != cudaSuccess) {
+            rc = set_error(FL_E_CUDA, "medusa_tree: heads");
+            break;
+        }
+        if ((rc = gemv_rows(e, e->lm, mz, H, false, e->logits, V)) != FL_OK) break;
+        if (launch_topk_rows(e->logits, H, V, V, mk, kmax, mtt, mprob, s) != cudaSuccess ||
+            cudaMemcpyAsync(htok.data(), mtt, sizeof(int) * htok.size(), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+            cudaMemcpyAsync(hprob.data(), mprob, sizeof(float) * hprob.size(), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+            cudaStreamSynchronize(s) != cudaSuccess) {
+            rc = set_error(FL_E_CUDA, "medusa_tree: top-k");
+            break;
+        }
+    } while (0);
+    cleanup();
+    FL_CHECK(rc);
+    const int M = build_tree(root, H, topk, htok.data(), hprob.data(), kmax, max_nodes, ntok, npar, ndep, &nscore);
+    for (int i = 0; i < M; i++) {
+        tok[i] = ntok[i];
+        parent[i] = npar[i];
+        depth[i] = ndep[i];
+        if (score) score[i] = nscore[i];
+    }
+    return M;
+}
+
+// Tree verification at the callback position (fl_engine_position): node i is
+// fed at cache slot pos + i with rotary position pos + depth[i], attending to
+// its ancestors; the longest path of the base model's greedy choices is
+// accepted, its KV moved to slots pos + 1 .. pos + a, and the position
+// advances by a + 1 (root and accepted nodes). out_tokens receives the a
+// accepted tokens and the base model's token after them (a + 1 entries);
+// *accepted = a. The feature of the last accepted node becomes the last
+// feature (fl_engine_last_feature).
+FL_API int fl_engine_tree_verify(fl_engine_t* e, const int* tok, const int* parent, const int* depth, int M,
+                                 int* out_tokens, int* accepted) {
+    FL_CHECK(check_ready(e, false));
+    if (!tok || !parent || !depth || !out_tokens || M < 1 || M > 256 || e->cb_pos < 1 || e->cb_pos + M > e->R)
+        return set_error(FL_E_INVAL, "tree_verify: bad arguments or context full");
+    if (parent[0] != -1 || depth[0] != 0) return set_error(FL_E_INVAL, "tree_verify: node 0 must be the root");
+    for (int i = 1; i < M; i++)
+        if (parent[i] < 0 || parent[i] >= i || depth[i] != depth[parent[i]] + 1)
+            return set_error(FL_E_INVAL, "tree_verify: parents must precede children, depth = parent depth + 1");
+    if (e->tp_size > 1) return set_error(FL_E_UNSUPPORTED, "tree_verify: not on a tensor-parallel engine");
+    const int d = e->d, n = e->cb_pos;
+    cudaStream_t s = e->s;
+    FL_CHECK(ensure_mask(e, M));
+    std::vector<int> pos(M), target(M), path;
+    std::vector<uint8_t> mask((size_t)M * M, 0);
+    for (int i = 0; i < M; i++) {
+        pos[i] = n + depth[i];
+        for (int j = i; j >= 0; j = parent[j]) mask[(size_t)i * M + j] = 1;
+    }
+    int *mtok = nullptr, *mpos = nullptr, *mtarget = nullptr, *mpath = nullptr;
+    KvLayer* dkv = nullptr;
+    auto cleanup = [&]() {
+        void* bufs[] = {mtok, mpos, mtarget, mpath, dkv};
+        for (void* p : bufs) cudaFree(p);
+    };
+    int rc = FL_OK;
+    do {
+        if (cudaMalloc(&mtok, sizeof(int) * M) || cudaMalloc(&mpos, sizeof(int) * M) ||
+            cudaMalloc(&mtarget, sizeof(int) * M) || cudaMalloc(&mpath, sizeof(int) * M) ||
+            cudaMalloc(&dkv, sizeof(KvLayer) * e->base.nl)) {
+            rc = set_error(FL_E_NOMEM, "tree_verify: device buffers");
+            break;
+        }
+        if (cudaMemcpyAsync(mtok, tok, sizeof(int) * M, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+            cudaMemcpyAsync(mpos, pos.data(), sizeof(int) * M, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+            cudaMemcpyAsync(e->mask, mask.data(), (size_t)M * M, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+            cudaMemcpyAsync(dkv, e->base.kv.data(), sizeof(KvLayer) * e->base.nl, cudaMemcpyHostToDevice, s) !=
+                cudaSuccess ||
+            launch_embed_rows(e->embed, e->Vg, mtok, nullptr, 0, e->x, d, M, nullptr, nullptr, s, false) != cudaSuccess) {
+            rc = set_error(FL_E_CUDA, "tree_verify: inputs");
+            break;
+        }
+        if ((rc = run_stack(e, e->base, e->x, M, nullptr, e->iota + n, mpos, e->mask, nullptr, false)) != FL_OK) break;
+        for (int r0 = 0; r0 < M && rc == FL_OK; r0 += kMaxRows) {
+            const int m = std::min(kMaxRows, M - r0);
+            if ((rc = run_lm(e, e->x + (size_t)r0 * d, m, nullptr, nullptr, false)) != FL_OK) break;
+            if (launch_argmax_rows(amax_keys(e), amax_nparts(e), m, mtarget + r0, nullptr, s) != cudaSuccess)
+                rc = set_error(FL_E_CUDA, "tree_verify: argmax");
+        }
+        if (rc != FL_OK) break;
+        if (cudaMemcpyAsync(target.data(), mtarget, sizeof(int) * M, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+            cudaStreamSynchronize(s) != cudaSuccess) {
+            rc = set_error(FL_E_CUDA, "tree_verify: targets");
+            break;
+        }
+        path.assign(1, 0);
+        int cur = 0;
+        for (;;) {
+            int nxt = -1;
+            for (int c2 = 1; c2 < M; c2++)
+                if (parent[c2] == cur && tok[c2] == target[cur]) {
+                    nxt = c2;
+                    break;
+                }
+            if (nxt < 0) break;
+            path.push_back(nxt);
+            cur = nxt;
+        }
+        const int a = (int)path.size() - 1;
+        for (int j = 1; j <= a; j++) out_tokens[j - 1] = tok[path[j]];
+        out_tokens[a] = target[cur];
+        if (accepted) *accepted = a;
+        if (a > 0 && (cudaMemcpyAsync(mpath, path.data(), sizeof(int) * (a + 1), cudaMemcpyHostToDevice, s) != cudaSuccess ||
+                      launch_kv_compact(dkv, e->base.nl, e->base.block_table, e->Hkv, e->hd, e->iota + n, mpath, a, s) !=
+                          cudaSuccess)) {
+            rc = set_error(FL_E_CUDA, "tree_verify: compaction");
+            break;
+        }
+        if (cudaMemcpyAsync(e->last_feat, e->x + (size_t)cur * d, sizeof(float) * d, cudaMemcpyDeviceToDevice, s) !=
+                cudaSuccess ||
+            cudaStreamSynchronize(s) != cudaSuccess) {
+            rc = set_error(FL_E_CUDA, "tree_verify: feature");
+            break;
+        }
+        e->cb_pos = n + a + 1;
+    } while (0);
+    cleanup();
+    FL_CHECK(rc);
+    if (take_device_error() != 0) return set_error(FL_E_TIMEOUT, "tree_verify: a bounded device wait gave up");
     return FL_OK;
 }

@@ -59,6 +59,13 @@ class MedusaConfig(C.Structure):
     _fields_ = [("num_heads", C.c_int), ("top_k", C.c_int), ("temperature", C.c_float)]
 
 
+class MedusaTree(C.Structure):
+    """medusa_tree_t"""
+    _fields_ = [("tokens", C.POINTER(C.c_int)), ("probs", C.POINTER(C.c_float)),
+                ("parent_indices", C.POINTER(C.c_int)), ("positions", C.POINTER(C.c_int)),
+                ("num_candidates", C.c_int), ("max_candidates", C.c_int)]
+
+
 class SpecConfig(C.Structure):
     """speculative_config_t (include/speculative.h)."""
     _fields_ = [("num_draft_tokens", C.c_int), ("temperature", C.c_float), ("max_accepted", C.c_int)]
@@ -141,11 +148,15 @@ _SIGS = {
     "fl_engine_step_trace_stages": (I, [VP, VP]),
     "fl_engine_medusa_generate": (I, [VP, VP, I, I, VP, I, I, VP, VP, VP]),
     "fl_engine_spec_medusa_generate": (I, [VP, VP, I, I, I, VP, I, I, VP, VP, VP]),
+    "fl_engine_medusa_tree": (I, [VP, VP, I, VP, I, I, VP, VP, VP, VP]),
+    "fl_engine_tree_verify": (I, [VP, VP, VP, VP, I, VP, VP]),
+    "fl_engine_bind_medusa": (I, [VP, VP]),
     "fl_engine_draft_bound": (I, [VP, VP]),
     "fl_engine_note_draft": (None, [VP, VP]),
     "fl_engine_bench_linear": (I, [VP, I, I, I, I, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "fl_engine_position": (I, [VP]),
     "fl_engine_set_position": (I, [VP, I]),
+    "fl_cuda_base_forward": (None, [VP, VP, I, VP, I]),
     "fl_engine_last_feature": (I, [VP, VP]),
     "fl_engine_draft_chain": (I, [VP, VP, I, I, I, VP, VP]),
     "fl_engine_bind_draft": (I, [VP, VP]),
@@ -169,6 +180,12 @@ _SIGS = {
     "medusa_generate": (I, [VP, VP, VP, VP, I, VP, I, C.POINTER(MedusaConfig)]),
     "speculative_medusa_generate": (I, [C.POINTER(DraftModel), VP, VP, VP, VP, VP, I, VP, I, C.POINTER(MedusaConfig)]),
     "fl_medusa_set_tree": (I, [VP, VP, I, I]),
+    "medusa_tree_create": (C.POINTER(MedusaTree), [I]),
+    "medusa_tree_free": (None, [C.POINTER(MedusaTree)]),
+    "medusa_predict": (I, [VP, VP, I, C.POINTER(MedusaTree), C.POINTER(MedusaConfig)]),
+    "medusa_build_tree": (I, [VP, VP, C.POINTER(MedusaTree), C.POINTER(MedusaConfig)]),
+    "medusa_verify_tree": (I, [VP, VP, C.POINTER(MedusaTree), VP, VP, C.POINTER(MedusaConfig)]),
+    "medusa_decode_step": (I, [VP, VP, VP, VP, I, VP, VP, C.POINTER(MedusaConfig)]),
 }
 
 

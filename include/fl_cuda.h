@@ -323,6 +323,29 @@ int fl_engine_medusa_generate(fl_engine_t* e, const int* prompt, int P, int n_ne
 int fl_engine_spec_medusa_generate(fl_engine_t* e, const int* prompt, int prompt_len, int n_new, int k,
                                    const int* topk, int n_heads, int max_nodes, int* out, int* acc_hist,
                                    int* steps);
+
+/* Step-level Medusa pieces (medusa_predict / medusa_build_tree /
+ * medusa_verify_tree / medusa_decode_step run on these).
+ * fl_engine_medusa_tree: the heads' candidate tree from a base feature F
+ * (host [d]); root >= 0 is the root token, root < 0 takes the LM head's
+ * argmax of F; writes at most max_nodes nodes (tok, parent (-1 for the root),
+ * depth, score = product of the softmax probabilities; score may be NULL) and
+ * returns the node count.
+ * fl_engine_tree_verify: feeds the tree at the callback position (node i at
+ * slot pos + i, rotary position pos + depth[i], attending to its ancestors),
+ * accepts the longest path of the base model's greedy choices, moves its KV
+ * to slots pos + 1 .. pos + a, advances the position by a + 1 and makes the
+ * last accepted node's feature the last feature; out_tokens gets the a
+ * accepted tokens then the base model's next token. Parents must precede
+ * their children. */
+int fl_engine_medusa_tree(fl_engine_t* e, const float* F, int root, const int* topk, int n_heads, int max_nodes,
+                          int* tok, int* parent, int* depth, float* score);
+int fl_engine_tree_verify(fl_engine_t* e, const int* tok, const int* parent, const int* depth, int n_nodes,
+                          int* out_tokens, int* accepted);
+/* Loads a medusa_model_t's heads (medusa_model: a medusa_model_t*) into the
+ * engine, as medusa_generate does on its first call, so that medusa_predict /
+ * medusa_build_tree find the engine. */
+int fl_engine_bind_medusa(fl_engine_t* e, void* medusa_model);
 /* 1 when `draft` (a draft_model_t*) is the draft whose weights the engine
  * holds; fl_engine_note_draft records it after a load. */
 int fl_engine_draft_bound(const fl_engine_t* e, const void* draft);

@@ -87,10 +87,19 @@ void medusa_model_free(medusa_model_t* model);
 medusa_tree_t* medusa_tree_create(int max_candidates);
 void medusa_tree_free(medusa_tree_t* tree);
 
-/* The step-level entry points below are not provided by this library yet:
- * they return -1 and record the reason (fl_cuda_last_error). medusa_generate
- * runs the whole loop -- heads, tree, verification, acceptance, KV
- * compaction -- on the device. */
+/* Step-level entry points (greedy). The heads must be bound to an engine
+ * (medusa_generate, medusa_decode_step or fl_engine_bind_medusa).
+ * medusa_predict: candidate tree with current_token as the root, from the
+ * base feature hidden_state (the feature of the position before
+ * current_token); tree->probs holds node scores. medusa_build_tree: the same
+ * with the base LM head's argmax of hidden_state as the root.
+ * medusa_verify_tree: one tree-masked base pass at the engine's callback
+ * position (fl_engine_position): accepted_tokens gets the accepted path and
+ * then the base model's next token, *num_accepted the path length; the path's
+ * KV is compacted and the position advances past root and path.
+ * medusa_decode_step: predict + verify; output_tokens gets the accepted tokens
+ * and the next token (*num_output = accepted + 1); the next current_hidden is
+ * fl_engine_last_feature and the next current_token the last output. */
 int medusa_predict(medusa_model_t* model, const float* hidden_state,
                    int current_token, medusa_tree_t* tree,
                    const medusa_config_t* config);

@@ -495,3 +495,58 @@ def test_spec_medusa_stream_is_greedy(gpu, orc):
     gpu.medusa_model_free(mm)
     gpu.draft_model_free(dm)
     eng.close()
+
+
+def test_medusa_step_api_matches_generate(gpu, orc):
+    """The reference's step-level Medusa API on the engine's callback position
+    (prefill with fl_cuda_base_forward, then medusa_decode_step /
+    medusa_build_tree + medusa_verify_tree) reproduces the greedy stream."""
+    import ctypes as C
+    dims = dict(SMALL, vocab=16)
+    w, embed = make_weights(gpu, dims, seed=3, draft_layers=0, medusa_heads=4)
+    eng = flb200.Engine(gpu, engine_cfg(dims, draft_layers=0, medusa_heads=4, max_seq_len=256))
+    load_engine(eng, {k: v for k, v in w.items() if k[0] != 2}, embed)
+    mm = gpu.medusa_model_create(4, dims["d"], dims["vocab"])
+    assert gpu.medusa_model_load(mm, b"synthetic:3") == 0
+    tk = np.array(MEDUSA_TOPK, np.int32)
+    assert gpu.fl_medusa_set_tree(mm, flb200.ptr(tk), 4, 48) == 0
+    cfg = flb200.MedusaConfig(4, 10, 0.0)
+    base_fwd = C.cast(gpu.so.fl_cuda_base_forward, C.c_void_p)
+    p = prompt(4, 12, dims["vocab"])
+    om = oracle_model(orc, dims, w, embed, draft_layers=0, n_medusa=4)
+    want, margins = om.greedy(p, 30)
+    # heads into the engine, then the prompt through base_forward (the feature
+    # of its last position comes back)
+    assert gpu.fl_engine_bind_medusa(eng.h, mm) == 0, gpu.err()
+    assert gpu.fl_engine_set_position(eng.h, 0) == 0
+    F = np.empty(dims["d"], np.float32)
+    gpu.fl_cuda_base_forward(eng.h, flb200.ptr(p), len(p), flb200.ptr(F), dims["d"])
+    assert gpu.fl_engine_position(eng.h) == len(p), gpu.err()
+    # first token: the root of a tree built from the prompt's last feature
+    tree = gpu.medusa_tree_create(48)
+    assert gpu.medusa_build_tree(mm, flb200.ptr(F), tree, C.byref(cfg)) > 0
+    got = [tree.contents.tokens[0]]
+    acc = []
+    out = np.empty(48, np.int32)
+    nout = C.c_int(0)
+    while len(got) < 30:
+        # alternate the two decompositions of a step
+        if len(acc) % 2 == 0:
+            r = gpu.medusa_decode_step(eng.h, base_fwd, mm, flb200.ptr(F), got[-1], flb200.ptr(out), C.byref(nout),
+                                       C.byref(cfg))
+            assert r == nout.value and r >= 1, gpu.err()
+        else:
+            assert gpu.medusa_predict(mm, flb200.ptr(F), got[-1], tree, C.byref(cfg)) > 0
+            na = C.c_int(0)
+            a = gpu.medusa_verify_tree(eng.h, base_fwd, tree, flb200.ptr(out), C.byref(na), C.byref(cfg))
+            assert a == na.value and a >= 0, gpu.err()
+            nout.value = a + 1
+        acc.append(nout.value - 1)
+        got.extend(out[:nout.value].tolist())
+        assert gpu.fl_engine_last_feature(eng.h, flb200.ptr(F)) == 0
+    got = np.array(got[:30])
+    assert_stream_matches(got, want, margins)
+    assert max(acc) >= 2, f"no multi-node path accepted: {acc}"
+    gpu.medusa_tree_free(tree)
+    gpu.medusa_model_free(mm)
+    eng.close()
