@@ -6,7 +6,7 @@
 //   C[m, n] = (sum over blocks b, in order, of (float)dot_b(m, n) * d[n, b]) / 127
 // with dot_b the exact int32 dot of 32 u8 activations and 32 s8 weights.
 //
-// One CTA computes a tile of 128 weight rows x BN (16, 32 or 64) activation rows.
+// One CTA computes a tile of 128 weight rows x BN (16 or 32) activation rows.
 //  - warps 0-3: producers. Per 128-byte K-group they copy the weight tile
 //    (128 rows x 128 B) with coalesced 16-byte cp.async (eight lanes per row;
 //    the tiled weight layout already stores each 128-byte group XOR-swizzled
@@ -19,13 +19,16 @@
 //    its copies complete, six stages behind the newest.
 //  - warp 4: allocates all 512 TMEM columns, then issues one
 //    tcgen05.mma.cta_group::1.kind::i8 (M = 128, N = BN, K = 32) per 32-element
-//    block into its own BN TMEM columns; G consecutive blocks (G BN = 64)
-//    form a group with one commit, and the groups cycle through 8 TMEM
-//    buffers.
+//    block into its own BN TMEM columns, and one tcgen05.commit per stage
+//    (four blocks): the commit both frees the stage's shared-memory slot and
+//    hands its TMEM buffer (4 BN columns, one of 512 / (4 BN)) to the
+//    readout. Commits are slow enough (about half a microsecond apiece here)
+//    that one per block was the kernel's bottleneck.
 //  - warps 5 ..: readout, four per TMEM lane quadrant (two when BN = 16),
-//    each with 8 or 16 columns of its quadrant's 32 lanes. Per group
-//    it loads the G blocks' s32 dots, releases the buffer and, while the next
-//    group's load is in flight, turns each dot into the float
+//    each with 8 columns of its quadrant's 32 lanes. Per half stage (two
+//    blocks) it loads the s32 dots, releases a stage's TMEM buffer once both
+//    halves are in registers and, while the next half's load is in flight,
+//    turns each dot into the float
 //    12582912 + dot by an integer add of 0x4B400000 (exact: |dot| < 2^22).
 //    One fma with d and -12582912 d (exact) then yields exactly the rounded
 //    product (float)dot * d, which is added to the row's running sum in block
@@ -57,8 +60,6 @@ __host__ __device__ constexpr int gemm_threads(int bn) { return (kRd0 + 4 * rd_p
 constexpr int kProdT = kProdW * 32;
 constexpr int kInFlight = 6;  // weight stages in flight per producer thread
 constexpr int kTmaRows = 64;  // weight-tile rows fetched by TMA (the rest by cp.async)
-// blocks per TMEM group (one commit, one readout round trip): G BN = 64
-__host__ __device__ constexpr int group_blocks(int bn) { return 64 / bn; }
 constexpr int kTileN = 128;                 // weight rows per tile (UMMA M)
 constexpr int kGroup = 128;                 // K bytes per stage (four 32-element blocks)
 constexpr int kABytes = kTileN * kGroup;    // 16 KB
@@ -197,7 +198,10 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
     gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a,
                       const GemvParams g, const GemmGeo geo) {
     extern __shared__ uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t full[kMaxStagesG], empty[kMaxStagesG], tfull[kMaxBuf], tempty[kMaxBuf];
+    // full: stage copied (producers); done: stage's MMAs complete (one
+    // tcgen05.commit per stage: frees the smem slot and hands the TMEM buffer
+    // to the readout); tempty: TMEM buffer read (readout warps)
+    __shared__ __align__(8) uint64_t full[kMaxStagesG], done[kMaxStagesG], tempty[kMaxBuf];
     __shared__ uint32_t tmem_base_s;
     __shared__ int bad_s, issued_s, consumed_s, last_commit_s;
 
@@ -205,8 +209,6 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
     constexpr int kStage = kABytes + kBBytes;
     constexpr int kWQ = rd_per_quad(BN);
     constexpr int kNRd = 4 * kWQ;
-    constexpr int kG = group_blocks(BN);
-    constexpr int kGPS = 4 / kG;  // groups per stage
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int N = geo.N, K = geo.K, S = geo.stages, NB = geo.nbuf;
@@ -216,12 +218,9 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; i++) {
             mb_init(&full[i], kProdT + 1);  // producer threads + the activation TMA
-            mb_init(&empty[i], 1);
+            mb_init(&done[i], 1);
         }
-        for (int i = 0; i < NB; i++) {
-            mb_init(&tfull[i], 1);
-            mb_init(&tempty[i], kNRd);
-        }
+        for (int i = 0; i < NB; i++) mb_init(&tempty[i], kNRd);
         bad_s = 0;
         issued_s = 0;
         consumed_s = 0;
@@ -243,7 +242,7 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
         int kg = 0, pub = 0;  // stages issued / published
         for (; kg < nkg; kg++) {
             const int s = kg % S;
-            if (kg >= S && !warp_wait(&empty[s], ((kg / S) - 1) & 1)) {
+            if (kg >= S && !warp_wait(&done[s], ((kg / S) - 1) & 1)) {
                 if (lane == 0) atomicOr(&bad_s, 1);
                 break;
             }
@@ -285,30 +284,19 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
                     atomicOr(&bad_s, 1);
                     break;
                 }
-                tc_fence_after();
-                const uint32_t a_addr = saddr(smem + (size_t)s * kStage);
-                bool ok = true;
-                for (int gs = 0; gs < kGPS && ok; gs++) {
-                    const int gi = kg * kGPS + gs, t = gi % NB;
-                    if (gi >= NB && !mb_wait(&tempty[t], ((gi / NB) - 1) & 1)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    for (int jj = 0; jj < kG; jj++) {
-                        const int j = gs * kG + jj;
-                        umma_i8<BN>(tmem + (uint32_t)((t * kG + jj) * BN), desc_sw128(a_addr + 32 * j),
-                                    desc_sw128(a_addr + kABytes + 32 * j));
-                    }
-                    umma_commit(&tfull[t]);
-                }
-                umma_commit(&empty[s]);
-                last_commit_s = kg;
-                if (!ok) {
+                const int t = kg % NB;
+                if (kg >= NB && !mb_wait(&tempty[t], ((kg / NB) - 1) & 1)) {
                     atomicOr(&bad_s, 1);
-                    kg++;
                     break;
                 }
+                tc_fence_after();
+                const uint32_t a_addr = saddr(smem + (size_t)s * kStage);
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    umma_i8<BN>(tmem + (uint32_t)((t * 4 + j) * BN), desc_sw128(a_addr + 32 * j),
+                                desc_sw128(a_addr + kABytes + 32 * j));
+                umma_commit(&done[s]);
+                last_commit_s = kg;
             }
             consumed_s = kg;
         }
@@ -329,14 +317,15 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
             if (!live || kg >= nkg) return make_uint2(0u, 0u);
             return __ldg(reinterpret_cast<const uint2*>(g.sblk + tiled_s_off(N, geo.P, n, kg * 4)));
         };
-        constexpr int kV = kG * kCols;  // registers per group
+        constexpr int kV = 2 * kCols;  // registers per half stage (two blocks)
         uint32_t va[kV], vb[kV];
-        auto ld_grp = [&](int gi, uint32_t* v) {
-            const uint32_t base = tq + (uint32_t)((gi % NB) * kG * BN);
+        // half stage h: blocks 2 (h & 1), 2 (h & 1) + 1 of stage h / 2
+        auto ld_half = [&](int h, uint32_t* v) {
+            const uint32_t base = tq + (uint32_t)(((h >> 1) % NB) * 4 * BN + (h & 1) * 2 * BN);
 #pragma unroll
-            for (int jj = 0; jj < kG; jj++)
+            for (int j = 0; j < 2; j++)
 #pragma unroll
-                for (int c = 0; c < kCols; c += 8) tmem_ld8(base + (uint32_t)(jj * BN + c), v + jj * kCols + c);
+                for (int c = 0; c < kCols; c += 8) tmem_ld8(base + (uint32_t)(j * BN + c), v + j * kCols + c);
         };
         auto scale_add = [&](const uint32_t* v, float d) {
             const float nmd = __fmul_rn(-kMagic, d);  // exact: 3 * 2^22 * d
@@ -346,53 +335,43 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
             for (int c = 0; c < kCols / 2; c++)
                 acc2[c] = add2(acc2[c], fma2(pk2(v[2 * c] + kMagicBits, v[2 * c + 1] + kMagicBits), d2, n2));
         };
-        const int ngrp = nkg * kGPS;
-        // the scales of the groups gi and gi + 1 (kG / 2 stages of four)
-        // a pair of groups covers 2 G blocks from block gi G: kSPP stages of four
-        // scales, starting at offset (gi G) % 4 of the first
-        constexpr int kSPP = (2 * kG + 3) / 4;
-        auto load_pair_sc = [&](int gi, uint2* sc) {
-#pragma unroll
-            for (int i = 0; i < kSPP; i++) sc[i] = load_sc((gi * kG) / 4 + i);
-        };
-        auto sc_of = [&](const uint2* sc, int k) -> float {  // block k, counted from the first stage's start
-            const uint32_t w = (k & 2) ? sc[k >> 2].y : sc[k >> 2].x;
-            const __half2 h = *reinterpret_cast<const __half2*>(&w);
-            return (k & 1) ? __high2float(h) : __low2float(h);
-        };
-        // one group: start the next group's load, free this group's buffer,
-        // scale and add its blocks, then wait for the load
-        auto step = [&](int gi, const uint32_t* cur, uint32_t* nxt, const uint2* sc, int k0) -> bool {
-            const bool more = gi + 1 < ngrp;
+        const int nh = 2 * nkg;
+        // one half stage: start the next half's load (waiting for its stage's
+        // MMAs when it opens a stage), free a stage's TMEM buffer once both its
+        // halves are in registers, scale and add two blocks, wait for the load
+        auto step = [&](int h, const uint32_t* cur, uint32_t* nxt, uint32_t scw) -> bool {
+            const bool more = h + 1 < nh;
             if (more) {
-                if (!warp_wait(&tfull[(gi + 1) % NB], ((gi + 1) / NB) & 1)) return false;
-                tc_fence_after();
-                ld_grp(gi + 1, nxt);
+                if (((h + 1) & 1) == 0) {
+                    const int kg = (h + 1) >> 1;
+                    if (!warp_wait(&done[kg % S], (kg / S) & 1)) return false;
+                    tc_fence_after();
+                }
+                ld_half(h + 1, nxt);
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mb_arrive(&tempty[gi % NB]);
-#pragma unroll
-            for (int jj = 0; jj < kG; jj++) scale_add(cur + jj * kCols, sc_of(sc, k0 + jj));
+            if (h & 1) {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mb_arrive(&tempty[(h >> 1) % NB]);
+            }
+            const __half2 hs = *reinterpret_cast<const __half2*>(&scw);
+            scale_add(cur, __low2float(hs));
+            scale_add(cur + kCols, __high2float(hs));
             if (more) tmem_wait_ld();
             return true;
         };
-        bool bad = !warp_wait(&tfull[0], 0);
+        bool bad = !warp_wait(&done[0], 0);
         if (!bad) {
             tc_fence_after();
-            ld_grp(0, va);
+            ld_half(0, va);
             tmem_wait_ld();
         }
-        uint2 sc_next[kSPP];
-        load_pair_sc(0, sc_next);
-        for (int gi = 0; gi < ngrp && !bad; gi += 2) {
-            uint2 sc[kSPP];
-#pragma unroll
-            for (int i = 0; i < kSPP; i++) sc[i] = sc_next[i];
-            if (gi + 2 < ngrp) load_pair_sc(gi + 2, sc_next);
-            const int o = (gi * kG) & 3;
-            if (!step(gi, va, vb, sc, o)) bad = true;
-            else if (gi + 1 < ngrp && !step(gi + 1, vb, va, sc, o + kG)) bad = true;
+        uint2 sc_next = load_sc(0);
+        for (int kg = 0; kg < nkg && !bad; kg++) {
+            const uint2 sc = sc_next;
+            sc_next = load_sc(kg + 1);
+            if (!step(2 * kg, va, vb, sc.x)) bad = true;
+            else if (!step(2 * kg + 1, vb, va, sc.y)) bad = true;
         }
         if (bad) {
             if (lane == 0) atomicOr(&bad_s, 1);
@@ -412,7 +391,7 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
         // drain: copies issued but not consumed, and the MMAs of the last commit
         // (producer threads drained their own copies with cp.async.wait_group 0)
         if (warp == kMma && lane == 0 && last_commit_s >= 0)
-            (void)mb_wait(&empty[last_commit_s % S], (last_commit_s / S) & 1);
+            (void)mb_wait(&done[last_commit_s % S], (last_commit_s / S) & 1);
         __syncthreads();
     }
     if (warp == kMma) {
@@ -463,7 +442,7 @@ cudaError_t launch_bn(const CUtensorMap& tw, const CUtensorMap& ta, const GemvPa
     geo.P = g.P;
     geo.stages = std::min(kMaxStagesG, (kSmemBudget - 1024) / stage);
     if (geo.stages < kInFlight + 1) return cudaErrorInvalidConfiguration;
-    geo.nbuf = 512 / (group_blocks(BN) * BN);
+    geo.nbuf = std::min(geo.stages, 512 / (4 * BN));  // TMEM stage buffers (no more than smem stages)
     const size_t smem = (size_t)geo.stages * stage + 1024;
     auto kern = gemm_i8_tc_kernel<BN, EPI>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -478,8 +457,7 @@ cudaError_t launch_epi(const CUtensorMap& tw, const CUtensorMap& ta, const GemvP
                        cudaStream_t s) {
     switch (BN) {
         case 16: return launch_bn<16, EPI>(tw, ta, g, M, s);
-        case 32: return launch_bn<32, EPI>(tw, ta, g, M, s);
-        default: return launch_bn<64, EPI>(tw, ta, g, M, s);
+        default: return launch_bn<32, EPI>(tw, ta, g, M, s);
     }
 }
 
@@ -492,11 +470,10 @@ bool gemm_tc_supported(const GemvParams& g, int epi) {
     return encode_fn() != nullptr;
 }
 
-// Tile width: the candidate (16, 32 or 64 rows: one TMEM group of 64
-// columns per readout round trip fits the readout threads' registers) with
-// the least modelled time = waves x per-tile time. Per-tile time grows with
-// BN (the per-element scaling of each block runs on the CUDA cores): measured
-// 1 : 1.45 : 2.75 for BN = 16 : 32 : 64 on B200. Narrow tiles also spread
+// Tile width: the candidate (16 or 32 rows: a stage's TMEM buffer of 4 BN
+// columns, double-buffered by half stages, fits the readout registers) with
+// the least modelled time = waves x per-tile time; per-tile time grows with
+// BN (measured about 1 : 1.45 for 16 : 32 on B200). Narrow tiles also spread
 // small-N layers over more SMs (their weight tiles are then re-read from L2).
 int pick_bn(int M, int N) {
     static int sms = 0;
@@ -507,11 +484,11 @@ int pick_bn(int M, int N) {
         if (sms <= 0) sms = 148;
     }
     const int ntiles = (N + kTileN - 1) / kTileN;
-    const int cand[3] = {16, 32, 64};
-    const double cost[3] = {1.0, 1.45, 2.75};
-    int best = 64;
+    const int cand[2] = {16, 32};
+    const double cost[2] = {1.0, 1.45};
+    int best = 32;
     double best_t = 1e30;
-    for (int i = 0; i < 3; i++) {
+    for (int i = 0; i < 2; i++) {
         const int bn = cand[i];
         const int mt = (M + bn - 1) / bn;
         const int waves = (ntiles * mt + sms - 1) / sms;
