@@ -24,9 +24,12 @@ speculative decoder) on the host cores, rank 0 only.
 
 --workload sampled-batch is the batched stochastic configuration: independent
 sequences (temperature 0.8, top-p 0.95, k = 6, Philox seed 1234 keyed by
-sequence id) split across the ranks with no exchange; `value` = all ranks'
-tokens / the slowest rank's device time for its share (strong scaling: the
-sequence count is fixed). Not the default line.
+sequence id) split across the ranks with no exchange, each rank decoding its
+share as one in-GPU batch (the verify pass runs sequences x (k + 1) rows
+through the tcgen05 GEMM); `value` = all ranks' tokens / the slowest rank's
+device time for its share, prefills included (strong scaling: the sequence
+count is fixed); `spec.decode_only_tok_s` leaves the prefills out. Not the
+default line.
 
 --workload tp-medium is the tensor-parallel configuration: a Phi-3-medium-
 shaped base (40 layers, d 5120, 40 query / 10 KV heads x 128, SwiGLU 17920,
@@ -397,10 +400,15 @@ def run_sampled_batch(a):
     eng.synthesize(SEED)
     eng.set_sampling(T, top_p, seed)
     ids = shard.shard_of(a.seqs, rank, world)
-    # warm-up: short decodes of a sequence outside the measured set
-    warm = shard.prompts_for([a.seqs + rank], a.prompt_len, DIMS["vocab"], PROMPT_SEED)
+    # this rank's sequences decode as one in-GPU batch: its KV regions are
+    # reserved once, outside the timed region
+    eng.batch_reserve(max(1, len(ids)), a.prompt_len + a.new_tokens + a.k + 3)
+    # warm-up: short decodes of as many sequences outside the measured set
+    # (same batch size: the same kernels and GEMM tiles)
+    wid = list(range(a.seqs + rank * len(ids), a.seqs + (rank + 1) * len(ids))) or [a.seqs + rank]
+    warm = shard.prompts_for(wid, 64, DIMS["vocab"], PROMPT_SEED)
     for _ in range(max(a.warmup, 3)):
-        eng.spec_generate_batch(warm, 16, a.k, seq_ids=[a.seqs + rank])
+        eng.spec_generate_batch(warm, 16, a.k, seq_ids=wid)
 
     def barrier():
         if dist:
@@ -412,13 +420,15 @@ def run_sampled_batch(a):
     clocks.start()
     got_ids, toks, steps, secs = shard.run_shard(eng, ids, a.prompt_len, a.new_tokens, a.k, DIMS["vocab"],
                                                  PROMPT_SEED)
+    dec = eng.last_timing()[1] * 1e-6 if len(ids) else 0.0  # decode loops alone
+    launches = eng.last_launches() if len(ids) else 0
     torch.cuda.synchronize()
     barrier()
     clk = clocks.stop()
     if dist:
-        t = torch.tensor([secs], device="cuda")
+        t = torch.tensor([secs, dec], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        secs = float(t.item())
+        secs, dec = float(t[0].item()), float(t[1].item())
         full = shard.gather_tokens(dist, got_ids, toks, a.seqs)
     else:
         full = toks
@@ -440,9 +450,12 @@ def run_sampled_batch(a):
                                    f"{a.seqs} sequences x ({a.prompt_len} prompt + {a.new_tokens} new), "
                                    f"split over {world} rank(s), prefill included",
                        "parallelism": f"sequence sharding over {world} GPU(s), no collective",
-                       "step": "one sequence per rank (prefill + decode)"},
+                       "step": "each rank's share as one in-GPU batch (prefills + batched decode)"},
             "spec": {"speculative_steps": nsteps, "tokens_per_step": tokens / max(1, nsteps),
+                     "decode_only_tok_s": tokens / dec if dec > 0 else None,
+                     "batch_per_gpu": len(ids), "decode_s": dec, "prefill_s": secs - dec,
                      "stream_checksum": int(np.asarray(full, np.int64).sum())},
+            "gpu_launches": launches,
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)

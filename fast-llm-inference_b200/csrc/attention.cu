@@ -77,7 +77,11 @@ __global__ void __launch_bounds__(kAThreads) attention_kernel(const AttnParams p
     const int r0 = blockIdx.y * kARows;
     if (r0 >= M) return;
     const int nr = min(kARows, M - r0);
-    const int base = *p.slot_base;
+    // batched sequences: this CTA's sequence, its rows and its cache region
+    const int sb = blockIdx.z;
+    const int base = p.slot_base[sb * p.seq_state];
+    const int* btab = p.block_table + (sb * p.seq_slots) / kPageSize;
+    const size_t qrow0 = (size_t)sb * M + r0;
     const int ctx = base + M;
     const int hd = p.head_dim;
     const int hd2 = hd >> 1;
@@ -95,7 +99,7 @@ __global__ void __launch_bounds__(kAThreads) attention_kernel(const AttnParams p
 
     for (int i = threadIdx.x; i < nr * hd; i += kAThreads) {
         const int rr = i / hd, dd = i - rr * hd;
-        q_s[rr * hd + dd] = p.q[(size_t)(r0 + rr) * qd + (size_t)h * hd + dd];
+        q_s[rr * hd + dd] = p.q[(qrow0 + rr) * qd + (size_t)h * hd + dd];
     }
     if (threadIdx.x < kARows) {
         m_run[threadIdx.x] = -INFINITY;
@@ -118,7 +122,7 @@ __global__ void __launch_bounds__(kAThreads) attention_kernel(const AttnParams p
         for (int i = threadIdx.x; i < nt * hd2; i += kAThreads) {
             const int key = i / hd2, c = i - key * hd2;
             const int slot = j0 + key;
-            const int page = p.block_table[slot / kPageSize];
+            const int page = btab[slot / kPageSize];
             const size_t off = (((size_t)page * p.kv_heads + kvh) * kPageSize + (slot % kPageSize)) * hd2 + c;
             Ks[key * kstride + c] = reinterpret_cast<const uint32_t*>(p.kv.k)[off];
             Vs[key * hd2 + c] = reinterpret_cast<const uint32_t*>(p.kv.v)[off];
@@ -215,7 +219,7 @@ __global__ void __launch_bounds__(kAThreads) attention_kernel(const AttnParams p
         float o = 0.0f;
         for (int gg = 0; gg < G; gg++) o += red[(gg * kARows + rr) * hd + dd];
         o = __fdiv_rn(o, l_run[rr]);
-        const size_t idx = (size_t)(r0 + rr) * qd + (size_t)h * hd + dd;
+        const size_t idx = (qrow0 + rr) * qd + (size_t)h * hd + dd;
         p.out_q[idx] = (uint8_t)quant_u8(o);
         if (p.out_f) p.out_f[idx] = o;
     }
@@ -245,7 +249,9 @@ __global__ void __launch_bounds__(kDThreads) attention_split_kernel(const AttnPa
     const int M = p.dyn_M ? *p.dyn_M : p.M;
     const int nr = min(M, MR);
     const int h = blockIdx.x, sp = blockIdx.y;
-    const int base = *p.slot_base;
+    const int sb = blockIdx.z;  // batched sequence
+    const int base = p.slot_base[sb * p.seq_state];
+    const size_t qrow0 = (size_t)sb * M;
     const int ctx = base + M;
     const int nsplit = (ctx + kSplit - 1) / kSplit;
     if (sp >= nsplit || nr <= 0) return;
@@ -258,10 +264,10 @@ __global__ void __launch_bounds__(kDThreads) attention_split_kernel(const AttnPa
 
     for (int i = threadIdx.x; i < nr * hd; i += kDThreads) {
         const int rr = i / hd, dd = i - rr * hd;
-        q_s[rr][dd] = p.q[(size_t)rr * qd + (size_t)h * hd + dd];
+        q_s[rr][dd] = p.q[(qrow0 + rr) * qd + (size_t)h * hd + dd];
     }
     {   // the split is one page: contiguous [64][hd] halves for this kv head
-        const int page = p.block_table[sp];
+        const int page = p.block_table[(sb * p.seq_slots) / kPageSize + sp];
         const size_t base_off = (((size_t)page * p.kv_heads + kvh) * kPageSize) * hd2;
         const uint32_t* kg = reinterpret_cast<const uint32_t*>(p.kv.k) + base_off;
         const uint32_t* vg = reinterpret_cast<const uint32_t*>(p.kv.v) + base_off;
@@ -352,7 +358,8 @@ __global__ void __launch_bounds__(kDThreads) attention_split_kernel(const AttnPa
     __syncthreads();
     // unnormalised P.V: thread -> (dimension pair d2, row parity)
     const int pstride = hd + 2;  // per (h, split, row): [max, sum, o[hd]]
-    float* part = p.part + (((size_t)h * gridDim.y + sp) * MR) * pstride;
+    const int hs = sb * p.heads + h;  // (sequence, head) scratch index
+    float* part = p.part + (((size_t)hs * gridDim.y + sp) * MR) * pstride;
     if (threadIdx.x < 2 * hd2) {
         const int d2 = threadIdx.x % hd2, rb = threadIdx.x / hd2;
         float a0[(MR + 1) / 2], a1[(MR + 1) / 2];
@@ -386,11 +393,11 @@ __global__ void __launch_bounds__(kDThreads) attention_split_kernel(const AttnPa
     // last CTA of this head combines
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) ticket_s = atomicAdd(&p.counters[h], 1);
+    if (threadIdx.x == 0) ticket_s = atomicAdd(&p.counters[hs], 1);
     __syncthreads();
     if (ticket_s != nsplit - 1) return;
     __threadfence();
-    const float* ph = p.part + ((size_t)h * gridDim.y * MR) * pstride;
+    const float* ph = p.part + ((size_t)hs * gridDim.y * MR) * pstride;
     for (int i = threadIdx.x; i < nr * hd; i += kDThreads) {
         const int rr = i / hd, dd = i - rr * hd;
         float gm = -INFINITY;
@@ -405,11 +412,11 @@ __global__ void __launch_bounds__(kDThreads) attention_split_kernel(const AttnPa
             O = __fmaf_rn(__ldcg(q + 2 + dd), wgt, O);
         }
         const float o = __fdiv_rn(O, L);
-        const size_t idx = (size_t)rr * qd + (size_t)h * hd + dd;
+        const size_t idx = (qrow0 + rr) * qd + (size_t)h * hd + dd;
         p.out_q[idx] = (uint8_t)quant_u8(o);
         if (p.out_f) p.out_f[idx] = o;
     }
-    if (threadIdx.x == 0) p.counters[h] = 0;  // re-arm for the next launch
+    if (threadIdx.x == 0) p.counters[hs] = 0;  // re-arm for the next launch
 }
 
 size_t attention_smem() {
@@ -443,7 +450,7 @@ size_t attention_scratch_counters(int heads) { return (size_t)heads; }
 template <int MR>
 cudaError_t launch_split(const AttnParams& p, cudaStream_t s, bool pdl) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p.heads, (p.max_ctx + kSplit - 1) / kSplit);
+    cfg.gridDim = dim3(p.heads, (p.max_ctx + kSplit - 1) / kSplit, p.seqs > 1 ? p.seqs : 1);
     cfg.blockDim = dim3(kDThreads);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
@@ -457,6 +464,8 @@ cudaError_t launch_split(const AttnParams& p, cudaStream_t s, bool pdl) {
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl) {
     if (p.head_dim > kMaxHd || p.head_dim < 64 || p.head_dim % 2 != 0 || (p.group <= 0 && p.heads % p.kv_heads != 0))
         return cudaErrorInvalidValue;
+    // batched sequences: static rows, page-aligned regions, grid z <= 65535
+    if (p.seqs > 1 && (p.dyn_M || p.seq_slots % kPageSize != 0 || p.seqs > 65535)) return cudaErrorInvalidValue;
     if (p.M <= kMaxRows && p.part && p.counters) {
         // grid.y covers every page the context can reach; the partial layout
         // indexes (head, split) with gridDim.y, so max_ctx must be the one the
@@ -473,7 +482,7 @@ cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl) {
         if (e != cudaSuccess) return e;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p.heads, (p.M + kARows - 1) / kARows);
+    cfg.gridDim = dim3(p.heads, (p.M + kARows - 1) / kARows, p.seqs > 1 ? p.seqs : 1);
     cfg.blockDim = dim3(kAThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;

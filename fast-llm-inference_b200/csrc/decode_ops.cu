@@ -63,12 +63,13 @@ __global__ void embed_rows_kernel(const float* embed, int vocab, const int* tok,
     for (int i = threadIdx.x; i < d; i += blockDim.x) xr[i] = f ? __fadd_rn(f[i], e[i]) : e[i];
 }
 
-__global__ void draft_pick_kernel(StepBuffers b, int j) {
+__global__ void draft_pick_kernel(const StepBuffers b0, int j) {
     pdl_trigger();
     pdl_wait();
+    const StepBuffers b = seq_view(b0, blockIdx.x);
     SpecState* st = b.st;
     if (st->done) return;
-    const unsigned long long best = block_best(b.amax_part, b.nparts);
+    const unsigned long long best = block_best(b.amax_d, b.nparts);
     const int tok = argmax_key_index(best);
     const int n = st->n;
     if (threadIdx.x == 0) {
@@ -79,18 +80,19 @@ __global__ void draft_pick_kernel(StepBuffers b, int j) {
         }
     }
     if (j + 1 < st->K) {
-        const int g_row = (j == 0) ? st->last_row : 0;
-        const float* g = b.x_d + (size_t)g_row * b.d;
+        const int g_row = (j == 0 && !b.batch) ? st->last_row : 0;
+        const float* g = b.x_d1 + (size_t)g_row * b.d;
         const float* e = b.embed + (size_t)tok * b.d;
-        float* x0 = b.x_d;
+        float* x0 = b.x_d1;
         // g_row may be 0: element-wise in place is safe.
         for (int i = threadIdx.x; i < b.d; i += blockDim.x) x0[i] = __fadd_rn(g[i], e[i]);
     }
 }
 
-__global__ void verify_prep_kernel(StepBuffers b) {
+__global__ void verify_prep_kernel(const StepBuffers b0) {
     pdl_trigger();
     pdl_wait();
+    const StepBuffers b = seq_view(b0, blockIdx.y);
     SpecState* st = b.st;
     if (st->done) return;
     const int r = blockIdx.x;
@@ -105,9 +107,10 @@ __global__ void verify_prep_kernel(StepBuffers b) {
     for (int i = threadIdx.x; i < b.d; i += blockDim.x) xr[i] = e[i];
 }
 
-__global__ void accept_kernel(StepBuffers b, int K) {
+__global__ void accept_kernel(const StepBuffers b0, int K) {
     pdl_trigger();
     pdl_wait();
+    const StepBuffers b = seq_view(b0, blockIdx.x);
     SpecState* st = b.st;
     if (st->done) return;
     __shared__ int tgt[kMaxRows];
@@ -135,23 +138,44 @@ __global__ void accept_kernel(StepBuffers b, int K) {
     st->rows = a + 1;
     st->last_row = a;
     st->draft_base = n + 1;
-    for (int r = 0; r <= a; r++) st->draft_pos[r] = n + 1 + r;
+    for (int r = 0; r <= K; r++) st->draft_pos[r] = n + 1 + r;
     st->done = produced >= st->n_new ? 1 : 0;
+    batch_retire(b, st->done);
 }
 
-__global__ void catchup_prep_kernel(StepBuffers b) {
+__global__ void catchup_prep_kernel(const StepBuffers b0) {
     pdl_trigger();
     pdl_wait();
+    const StepBuffers b = seq_view(b0, blockIdx.y);
     SpecState* st = b.st;
     if (st->done) return;
     const int r = blockIdx.x;
-    if (r >= st->rows) return;
+    if (r >= st->rows) {
+        // batched catch-up passes run K + 1 rows for every sequence: rows past
+        // this sequence's accepted ones are zero (their outputs are unused,
+        // and the cache slots they write are rewritten before they are read)
+        if (b.batch) {
+            float* xr = b.x_d + (size_t)r * b.d;
+            for (int i = threadIdx.x; i < b.d; i += blockDim.x) xr[i] = 0.0f;
+        }
+        return;
+    }
     const int pos = st->draft_base + r;  // = n_old + 1 + r
     const int tok = b.seq[pos];
     const float* e = b.embed + (size_t)tok * b.d;
     const float* f = b.x_v + (size_t)r * b.d;
     float* xr = b.x_d + (size_t)r * b.d;
     for (int i = threadIdx.x; i < b.d; i += blockDim.x) xr[i] = __fadd_rn(f[i], e[i]);
+}
+
+// Batched: the catch-up's feature of each sequence's newest token.
+__global__ void gather_last_kernel(const StepBuffers b0) {
+    pdl_trigger();
+    pdl_wait();
+    const StepBuffers b = seq_view(b0, blockIdx.x);
+    if (b.st->done) return;
+    const float* src = b.x_d + (size_t)b.st->last_row * b.d;
+    for (int i = threadIdx.x; i < b.d; i += blockDim.x) b.x_d1[i] = src[i];
 }
 
 __global__ void argmax_rows_kernel(const unsigned long long* part, int nparts, int* out_tok,
@@ -206,19 +230,23 @@ cudaError_t launch_embed_rows(const float* embed, int vocab, const int* tok, con
 }
 
 cudaError_t launch_draft_pick(const StepBuffers& b, int j, cudaStream_t s, bool pdl) {
-    return launch_pdl(draft_pick_kernel, dim3(1), kT, s, pdl, b, j);
+    return launch_pdl(draft_pick_kernel, dim3(step_seqs(b)), kT, s, pdl, b, j);
 }
 
 cudaError_t launch_verify_prep(const StepBuffers& b, int K, cudaStream_t s, bool pdl) {
-    return launch_pdl(verify_prep_kernel, dim3(K + 1), kT, s, pdl, b);
+    return launch_pdl(verify_prep_kernel, dim3(K + 1, step_seqs(b)), kT, s, pdl, b);
 }
 
 cudaError_t launch_accept(const StepBuffers& b, int K, cudaStream_t s, bool pdl) {
-    return launch_pdl(accept_kernel, dim3(1), kT, s, pdl, b, K);
+    return launch_pdl(accept_kernel, dim3(step_seqs(b)), kT, s, pdl, b, K);
 }
 
 cudaError_t launch_catchup_prep(const StepBuffers& b, int K, cudaStream_t s, bool pdl) {
-    return launch_pdl(catchup_prep_kernel, dim3(K + 1), kT, s, pdl, b);
+    return launch_pdl(catchup_prep_kernel, dim3(K + 1, step_seqs(b)), kT, s, pdl, b);
+}
+
+cudaError_t launch_gather_last(const StepBuffers& b, cudaStream_t s, bool pdl) {
+    return launch_pdl(gather_last_kernel, dim3(step_seqs(b)), kT, s, pdl, b);
 }
 
 cudaError_t launch_argmax_rows(const unsigned long long* part, int nparts, int rows, int* out_tok,

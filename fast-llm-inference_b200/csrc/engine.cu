@@ -11,6 +11,7 @@
 //   GEMV down (EPI_RESID)           -> x += down
 // One speculative step is captured once as a CUDA graph whose kernels read
 // positions from the device-resident SpecState, and replayed.
+#include <stddef.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -50,6 +51,19 @@ struct Stack {
     std::vector<KvLayer> kv;
     int* block_table = nullptr;
     int pages = 0;
+};
+
+// The KV cache a pass reads and writes: one sequence's region, or an in-GPU
+// batch (rows of sequence b are rows [b seq_rows, (b + 1) seq_rows) of the
+// pass, its slots [b seq_slots, (b + 1) seq_slots), and its slot base and
+// positions in state records seq_state ints apart).
+struct KvView {
+    const KvLayer* kv = nullptr;  // [layers] (host array)
+    const int* block_table = nullptr;
+    int seqs = 1, seq_rows = 0, seq_state = 0, seq_slots = 0;
+    int max_ctx = 0;              // slots per sequence (attention grid)
+    float* attn_part = nullptr;   // split-K scratch for seqs sequences
+    int* attn_cnt = nullptr;
 };
 
 }  // namespace
@@ -142,9 +156,46 @@ struct fl_engine {
     unsigned char* samp_snap = nullptr;
     float* samp_trace = nullptr;  // [2 * kMaxRows, V] logits behind each draw (trace on)
     bool trace_on = false;
+    // In-GPU batch of independent sequences (fl_engine_batch_*): its own KV
+    // regions (bslots slots per sequence), per-sequence state and rows, and
+    // one step graph that advances every sequence
+    struct Batch {
+        int cap = 0, slots = 0;          // sequences held, KV slots per sequence
+        int n = 0, K = 0, P = 0;         // sequences, drafts per step, prompt length of the prefill
+        bool ready = false, samp = false, traced = false;
+        std::vector<KvLayer> kv_base, kv_draft;
+        int* block = nullptr;            // identity table over cap * slots / kPageSize pages
+        float* attn_part = nullptr;
+        int* attn_cnt = nullptr;
+        SpecState* st = nullptr;         // [cap]
+        SpecState* st_snap = nullptr;
+        int* seq = nullptr;              // [cap][slots] committed tokens
+        int* out = nullptr;              // [cap][slots] emitted tokens
+        int* acc = nullptr;              // [cap][slots] accepted drafts per step
+        BatchCtl* ctl = nullptr;
+        float* x_v = nullptr;            // [cap * kMaxRows, d] verify rows
+        float* x_dc = nullptr;           // [cap * kMaxRows, d] draft catch-up rows
+        float* x_d1 = nullptr;           // [cap, d] single-row draft inputs
+        float* x_d1_snap = nullptr;
+        float* logits = nullptr;         // [cap * kMaxRows, V]
+        unsigned long long* amax = nullptr;  // [cap * kMaxRows, nparts]
+        uint32_t* key = nullptr;         // [cap][2] Philox seed, sequence id
+        uint32_t* q = nullptr;           // [cap][kMaxDraft][V] (sampling)
+        uint32_t* p = nullptr;           // [cap][kMaxRows][V]
+        unsigned long long* m = nullptr; // [cap][kMaxDraft + kMaxRows]
+        unsigned long long* r = nullptr; // [cap][V]
+        uint32_t* q_snap = nullptr;      // [cap][V] draft weights of step 0
+        unsigned long long* m_snap = nullptr;  // [cap]
+        float* trace = nullptr;          // [cap][2 * kMaxRows][V] (trace on)
+        float* trace_snap = nullptr;     // [cap][V]
+        cudaGraphExec_t exec = nullptr;
+        int graph_kernels = 0;
+    } bt;
 };
 
 namespace {
+
+void batch_free(fl_engine* e);
 
 int alloc_linear(Linear& l, int N, int K, unsigned need, bool step_layout) {
     l.N = N;
@@ -343,8 +394,9 @@ int residual_linear(fl_engine* e, GemvParams g, float* x, int M, const int* dyn_
 // Runs M rows (M <= R; dyn_M bounds the live rows when set, M <= kMaxRows)
 // through a stack. slot_base / pos are device pointers.
 int run_stack(fl_engine* e, Stack& S, float* x, int M, const int* dyn_M, const int* slot_base, const int* pos,
-              const uint8_t* mask, const int* done, bool pdl) {
+              const uint8_t* mask, const int* done, bool pdl, const KvView* view = nullptr) {
     const int d = e->d, qd = e->qd, F = e->F;
+    const bool batched = view && view->seqs > 1;
     // Fused RMSNorm + quantization prologues need K % 128 == 0; otherwise a
     // separate act_quant launch produces xq.
     const bool fuse = (d % 128) == 0;
@@ -358,10 +410,15 @@ int run_stack(fl_engine* e, Stack& S, float* x, int M, const int* dyn_M, const i
             g.eps = e->c.norm_eps;
         }
         g.q_out = e->q;
-        g.kv = S.kv[l];
-        g.block_table = S.block_table;
+        g.kv = view ? view->kv[l] : S.kv[l];
+        g.block_table = view ? view->block_table : S.block_table;
         g.slot_base = slot_base;
         g.pos = pos;
+        if (batched) {
+            g.seq_rows = view->seq_rows;
+            g.seq_state = view->seq_state;
+            g.seq_slots = view->seq_slots;
+        }
         g.q_dim = qd;
         g.kv_dim = e->kd;
         g.head_dim = e->hd;
@@ -370,10 +427,15 @@ int run_stack(fl_engine* e, Stack& S, float* x, int M, const int* dyn_M, const i
         FL_CHECK(launch_chunks(g, EPI_QKV, M, dyn_M, e->s, pdl));
         AttnParams at = {};
         at.q = e->q;
-        at.kv = S.kv[l];
-        at.block_table = S.block_table;
+        at.kv = view ? view->kv[l] : S.kv[l];
+        at.block_table = view ? view->block_table : S.block_table;
         at.slot_base = slot_base;
-        at.M = M;
+        at.M = batched ? view->seq_rows : M;
+        if (batched) {
+            at.seqs = view->seqs;
+            at.seq_state = view->seq_state;
+            at.seq_slots = view->seq_slots;
+        }
         at.dyn_M = dyn_M;
         at.mask = mask;
         at.heads = e->H;
@@ -384,11 +446,11 @@ int run_stack(fl_engine* e, Stack& S, float* x, int M, const int* dyn_M, const i
             at.kv_head0 = e->tp.kv0;
             at.group = e->tp.group;
         }
-        at.max_ctx = e->c.max_seq_len;
+        at.max_ctx = view && view->max_ctx ? view->max_ctx : e->c.max_seq_len;
         at.out_q = e->aq;
         at.done = done;
-        at.part = e->attn_part;
-        at.counters = e->attn_cnt;
+        at.part = view && view->attn_part ? view->attn_part : e->attn_part;
+        at.counters = view && view->attn_cnt ? view->attn_cnt : e->attn_cnt;
         FL_CHECK_CUDA(launch_attention(at, e->s, pdl));
         g = gemv_base(W.o, e->aq, done);
         g.out = x;
@@ -414,7 +476,27 @@ int run_stack(fl_engine* e, Stack& S, float* x, int M, const int* dyn_M, const i
 
 // LM head over rows of x (M <= kMaxRows): logits [M, V] and argmax partials.
 // dyn_src_row (device) selects the first source row of x.
-int run_lm(fl_engine* e, const float* x, int M, const int* dyn_src_row, const int* done, bool pdl) {
+int run_lm(fl_engine* e, const float* x, int M, const int* dyn_src_row, const int* done, bool pdl,
+           float* logits = nullptr, unsigned long long* amax = nullptr) {
+    if (M > kMaxRows || logits) {
+        // rows in launches of up to kMaxRows (batched steps), into the given
+        // logits [M, V] and argmax partials [M, nparts]
+        if (e->tp_size > 1 || dyn_src_row || !logits || !amax || (e->d % 128) != 0)
+            return set_error(FL_E_UNSUPPORTED, "LM head: many-row passes need the fused prologue on one GPU");
+        GemvParams g = gemv_base(e->lm, e->xq, done);
+        g.x = x;
+        g.norm = 1;
+        g.eps = e->c.norm_eps;
+        g.out = logits;
+        g.ldo = e->V;
+        g.amax_part = amax;
+        for (int r0 = 0; r0 < M; r0 += kMaxRows) {
+            g.row0 = r0;
+            g.M = std::min(kMaxRows, M - r0);
+            FL_CHECK_CUDA(launch_gemv_auto(g, EPI_LOGITS, e->s, pdl));
+        }
+        return FL_OK;
+    }
     GemvParams g = gemv_base(e->lm, e->xq, done);
     if ((e->d % 128) == 0) {
         g.x = x;
@@ -463,7 +545,7 @@ const unsigned long long* amax_keys(const fl_engine* e) { return e->tp_size > 1 
 int amax_nparts(const fl_engine* e) { return e->tp_size > 1 ? 1 : e->nparts; }
 
 StepBuffers step_buffers(fl_engine* e) {
-    StepBuffers b;
+    StepBuffers b = {};
     b.st = e->st;
     b.seq = e->seq;
     b.out = e->out;
@@ -959,6 +1041,7 @@ FL_API void fl_engine_destroy(fl_engine_t* e) {
     cudaSetDevice(e->device);
     if (e->s) cudaStreamSynchronize(e->s);
     if (e->step_exec) cudaGraphExecDestroy(e->step_exec);
+    batch_free(e);
     free_stack(e->base);
     free_stack(e->draft);
     free_linear(e->lm);
@@ -1440,12 +1523,477 @@ FL_API int fl_engine_spec_generate(fl_engine_t* e, const int* prompt, int P, int
     return fl_engine_spec_decode(e, n_new, out, acc_hist, steps);
 }
 
+// ---------------------------------------------------------------------------
+// In-GPU batch of independent sequences. Every step runs each draft pass
+// over one row per sequence and the verify and draft catch-up passes over
+// K + 1 rows per sequence, so the weights stream once per pass for the whole
+// batch (the tcgen05 GEMM takes passes of more than 16 rows). Each sequence
+// keeps its own KV region, state record, token arrays and Philox key
+// (seed, sequence id); its decisions are those of the one-sequence step.
+// ---------------------------------------------------------------------------
+namespace {
+
+void batch_free(fl_engine* e) {
+    auto& B = e->bt;
+    if (B.exec) cudaGraphExecDestroy(B.exec);
+    for (auto* kv : {&B.kv_base, &B.kv_draft})
+        for (auto& l : *kv) {
+            cudaFree(l.k);
+            cudaFree(l.v);
+        }
+    void* bufs[] = {B.block, B.attn_part, B.attn_cnt, B.st, B.st_snap, B.seq, B.out, B.acc, B.ctl, B.x_v,
+                    B.x_dc, B.x_d1, B.x_d1_snap, B.logits, B.amax, B.key, B.q, B.p, B.m, B.r, B.q_snap,
+                    B.m_snap, B.trace, B.trace_snap};
+    for (void* p : bufs) cudaFree(p);
+    B = fl_engine::Batch();
+}
+
+// Device bytes one sequence of a batch holds with `slots` KV slots.
+size_t batch_bytes_per_seq(const fl_engine* e, int slots) {
+    const size_t kv = (size_t)(e->base.nl + e->draft.nl) * 2 * e->Hkv * e->hd * sizeof(__half) * slots;
+    const size_t rows = (size_t)kMaxRows * (3 * e->d + e->V + e->nparts * 2) * 4 + (size_t)e->d * 8;
+    const size_t toks = (size_t)3 * slots * sizeof(int);
+    const size_t attn = sizeof(float) * attention_scratch_floats(e->H, e->hd, slots);
+    return kv + rows + toks + attn + 2 * sizeof(SpecState);
+}
+
+int batch_alloc(fl_engine* e, int cap, int slots) {
+    batch_free(e);
+    auto& B = e->bt;
+    slots = (slots + kPageSize - 1) / kPageSize * kPageSize;
+    const size_t pages = (size_t)cap * (slots / kPageSize);
+    const size_t kvb = pages * e->Hkv * kPageSize * e->hd * sizeof(__half);
+    for (auto pr : {std::make_pair(&B.kv_base, e->base.nl), std::make_pair(&B.kv_draft, e->draft.nl)}) {
+        pr.first->assign(pr.second, KvLayer{nullptr, nullptr});
+        for (auto& l : *pr.first) {
+            FL_CHECK_CUDA(cudaMalloc(&l.k, kvb));
+            FL_CHECK_CUDA(cudaMalloc(&l.v, kvb));
+            FL_CHECK_CUDA(cudaMemsetAsync(l.k, 0, kvb, e->s));
+            FL_CHECK_CUDA(cudaMemsetAsync(l.v, 0, kvb, e->s));
+        }
+    }
+    const size_t d = e->d, V = e->V, rows = (size_t)cap * kMaxRows, cnt = attention_scratch_counters(e->H) * cap;
+    FL_CHECK_CUDA(cudaMalloc(&B.block, sizeof(int) * pages));
+    FL_CHECK_CUDA(cudaMalloc(&B.attn_part, sizeof(float) * attention_scratch_floats(e->H, e->hd, slots) * cap));
+    FL_CHECK_CUDA(cudaMalloc(&B.attn_cnt, sizeof(int) * cnt));
+    FL_CHECK_CUDA(cudaMemsetAsync(B.attn_cnt, 0, sizeof(int) * cnt, e->s));
+    FL_CHECK_CUDA(cudaMalloc(&B.st, sizeof(SpecState) * cap));
+    FL_CHECK_CUDA(cudaMalloc(&B.st_snap, sizeof(SpecState) * cap));
+    FL_CHECK_CUDA(cudaMalloc(&B.seq, sizeof(int) * cap * (size_t)slots));
+    FL_CHECK_CUDA(cudaMalloc(&B.out, sizeof(int) * cap * (size_t)slots));
+    FL_CHECK_CUDA(cudaMalloc(&B.acc, sizeof(int) * cap * (size_t)slots));
+    FL_CHECK_CUDA(cudaMalloc(&B.ctl, sizeof(BatchCtl)));
+    FL_CHECK_CUDA(cudaMalloc(&B.x_v, sizeof(float) * rows * d));
+    FL_CHECK_CUDA(cudaMalloc(&B.x_dc, sizeof(float) * rows * d));
+    FL_CHECK_CUDA(cudaMalloc(&B.x_d1, sizeof(float) * cap * d));
+    FL_CHECK_CUDA(cudaMalloc(&B.x_d1_snap, sizeof(float) * cap * d));
+    FL_CHECK_CUDA(cudaMalloc(&B.logits, sizeof(float) * rows * V));
+    FL_CHECK_CUDA(cudaMalloc(&B.amax, sizeof(unsigned long long) * rows * e->nparts));
+    FL_CHECK_CUDA(cudaMalloc(&B.key, sizeof(uint32_t) * 2 * cap));
+    std::vector<int> id(pages);
+    for (size_t i = 0; i < pages; i++) id[i] = (int)i;
+    FL_CHECK_CUDA(cudaMemcpy(B.block, id.data(), sizeof(int) * pages, cudaMemcpyHostToDevice));
+    B.cap = cap;
+    B.slots = slots;
+    return FL_OK;
+}
+
+int batch_alloc_sampling(fl_engine* e) {
+    auto& B = e->bt;
+    const size_t V = e->V, cap = B.cap;
+    if (!B.q) {
+        FL_CHECK_CUDA(cudaMalloc(&B.q, sizeof(uint32_t) * cap * kMaxDraft * V));
+        FL_CHECK_CUDA(cudaMalloc(&B.p, sizeof(uint32_t) * cap * kMaxRows * V));
+        FL_CHECK_CUDA(cudaMalloc(&B.m, sizeof(unsigned long long) * cap * (kMaxDraft + kMaxRows)));
+        FL_CHECK_CUDA(cudaMalloc(&B.r, sizeof(unsigned long long) * cap * V));
+        FL_CHECK_CUDA(cudaMalloc(&B.q_snap, sizeof(uint32_t) * cap * V));
+        FL_CHECK_CUDA(cudaMalloc(&B.m_snap, sizeof(unsigned long long) * cap));
+    }
+    if (B.traced && !B.trace_snap) {
+        FL_CHECK_CUDA(cudaMalloc(&B.trace, sizeof(float) * cap * 2 * kMaxRows * V));
+        FL_CHECK_CUDA(cudaMalloc(&B.trace_snap, sizeof(float) * cap * V));
+    }
+    return FL_OK;
+}
+
+StepBuffers batch_buffers(fl_engine* e) {
+    auto& B = e->bt;
+    StepBuffers b = {};
+    b.st = B.st;
+    b.seq = B.seq;
+    b.out = B.out;
+    b.acc_hist = B.acc;
+    b.embed = e->embed;
+    b.x_d = B.x_dc;
+    b.x_v = B.x_v;
+    b.amax_part = B.amax;
+    b.nparts = e->nparts;
+    b.d = e->d;
+    b.logits = B.logits;
+    b.V = e->V;
+    b.temp = e->samp_T;
+    b.top_p = e->samp_top_p;
+    b.key = B.key;
+    if (B.samp) {
+        b.qd = B.q;
+        b.qm = B.m;
+        b.pt = B.p;
+        b.pm = B.m + kMaxDraft;
+        b.resid = B.r;
+        b.trace = B.traced ? B.trace : nullptr;
+    }
+    b.batch = B.n;
+    b.rows_per = B.K + 1;
+    b.seq_cap = B.slots;
+    b.x_d1 = B.x_d1;
+    b.logits_d = B.logits;
+    b.amax_d = B.amax;
+    b.ctl = B.ctl;
+    return b;
+}
+
+// The batch's KV regions as seen by a pass of `rows` rows per sequence.
+KvView batch_view(fl_engine* e, bool base, int rows) {
+    auto& B = e->bt;
+    KvView v;
+    v.kv = base ? B.kv_base.data() : B.kv_draft.data();
+    v.block_table = B.block;
+    v.seqs = B.n;
+    v.seq_rows = rows;
+    v.seq_state = (int)(sizeof(SpecState) / sizeof(int));
+    v.seq_slots = B.slots;
+    v.max_ctx = B.slots;
+    v.attn_part = B.attn_part;
+    v.attn_cnt = B.attn_cnt;
+    return v;
+}
+
+// One batched speculative step (the rule of record_step, every sequence at once).
+int record_batch_step(fl_engine* e, bool pdl) {
+    auto& B = e->bt;
+    const int K = B.K, n = B.n;
+    const StepBuffers b = batch_buffers(e);
+    const int* done = &B.ctl->done;
+    KvView vd = batch_view(e, false, 1);
+    const KvView vb = batch_view(e, true, K + 1);
+    auto pick = [&](int j) {
+        return B.samp ? launch_sample_pick(b, j, e->s, pdl) : launch_draft_pick(b, j, e->s, pdl);
+    };
+    for (int j = 1; j < K; j++) {
+        FL_CHECK(run_stack(e, e->draft, B.x_d1, n, nullptr, &B.st->draft_base, B.st->draft_pos, nullptr, done, pdl, &vd));
+        FL_CHECK(run_lm(e, B.x_d1, n, nullptr, done, pdl, B.logits, B.amax));
+        FL_CHECK_CUDA(pick(j));
+    }
+    FL_CHECK_CUDA(launch_verify_prep(b, K, e->s, pdl));
+    FL_CHECK(run_stack(e, e->base, B.x_v, n * (K + 1), nullptr, &B.st->verify_base, B.st->verify_pos, nullptr, done,
+                       pdl, &vb));
+    FL_CHECK(run_lm(e, B.x_v, n * (K + 1), nullptr, done, pdl, B.logits, B.amax));
+    if (B.samp) {
+        FL_CHECK_CUDA(launch_target_dist(b, K, e->s, pdl));
+        FL_CHECK_CUDA(launch_accept_sampled(b, K, e->s, pdl));
+    } else {
+        FL_CHECK_CUDA(launch_accept(b, K, e->s, pdl));
+    }
+    FL_CHECK_CUDA(launch_catchup_prep(b, K, e->s, pdl));
+    vd.seq_rows = K + 1;
+    FL_CHECK(run_stack(e, e->draft, B.x_dc, n * (K + 1), nullptr, &B.st->draft_base, B.st->draft_pos, nullptr, done,
+                       pdl, &vd));
+    FL_CHECK_CUDA(launch_gather_last(b, e->s, pdl));
+    FL_CHECK(run_lm(e, B.x_d1, n, nullptr, done, pdl, B.logits, B.amax));
+    FL_CHECK_CUDA(pick(0));
+    return FL_OK;
+}
+
+int build_batch_graph(fl_engine* e) {
+    auto& B = e->bt;
+    if (B.exec) {
+        FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
+        cudaGraphExecDestroy(B.exec);
+        B.exec = nullptr;
+    }
+    cudaGraph_t g = nullptr;
+    FL_CHECK_CUDA(cudaStreamBeginCapture(e->s, cudaStreamCaptureModeThreadLocal));
+    const int rc = record_batch_step(e, true);
+    const cudaError_t ce = cudaStreamEndCapture(e->s, &g);
+    if (rc != FL_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    FL_CHECK_CUDA(ce);
+    size_t nn = 0;
+    cudaGraphGetNodes(g, nullptr, &nn);
+    std::vector<cudaGraphNode_t> nodes(nn);
+    cudaGraphGetNodes(g, nodes.data(), &nn);
+    int nk = 0;
+    for (auto nd : nodes) {
+        cudaGraphNodeType t;
+        if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) nk++;
+    }
+    B.graph_kernels = nk;
+    const cudaError_t ie = cudaGraphInstantiate(&B.exec, g, 0);
+    cudaGraphDestroy(g);
+    FL_CHECK_CUDA(ie);
+    return FL_OK;
+}
+
+// Strided copy of `rows` rows of `width` bytes (row pitches in bytes).
+cudaError_t copy_rows(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width, size_t rows,
+                      cudaMemcpyKind kind, cudaStream_t s) {
+    return cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, rows, kind, s);
+}
+
+}  // namespace
+
+FL_API int fl_engine_batch_reserve(fl_engine_t* e, int nseq, int max_ctx) {
+    FL_CHECK(check_ready(e, true));
+    if (e->tp_size > 1) return set_error(FL_E_UNSUPPORTED, "batch: a tensor-parallel engine decodes one sequence");
+    if (nseq <= 0 || max_ctx < 16 || nseq > 65535) return set_error(FL_E_INVAL, "batch_reserve: bad arguments");
+    FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
+    const int rc = batch_alloc(e, nseq, max_ctx);
+    if (rc != FL_OK) {
+        batch_free(e);
+        (void)cudaGetLastError();
+        return set_error(FL_E_NOMEM, "batch_reserve: device allocation failed");
+    }
+    FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
+    return FL_OK;
+}
+
+FL_API int fl_engine_batch_capacity(const fl_engine_t* e, int* nseq, int* slots) {
+    if (!e) return set_error(FL_E_INVAL, "engine is NULL");
+    if (nseq) *nseq = e->bt.cap;
+    if (slots) *slots = e->bt.slots;
+    return FL_OK;
+}
+
+FL_API int fl_engine_batch_prefill(fl_engine_t* e, const int* prompts, int P, int nseq, const unsigned* seq_ids, int K) {
+    FL_CHECK(check_ready(e, true));
+    auto& B = e->bt;
+    if (!prompts || P <= 0 || nseq <= 0 || K < 1 || K > kMaxDraft)
+        return set_error(FL_E_INVAL, "batch_prefill: bad arguments (1 <= K <= 7)");
+    if (nseq > B.cap) return set_error(FL_E_INVAL, "batch_prefill: more sequences than reserved");
+    if (P + K + 3 > B.slots || P + 2 > e->R || nseq * (K + 1) > e->R)
+        return set_error(FL_E_INVAL, "batch_prefill: prompt or batch too long for the reservation");
+    if (e->d % 128 != 0) return set_error(FL_E_UNSUPPORTED, "batch: the hidden size must be a multiple of 128");
+    B.ready = false;
+    B.n = nseq;
+    B.K = K;
+    B.P = P;
+    B.samp = e->samp;
+    B.traced = e->samp && e->trace_on;
+    if (B.samp) {
+        FL_CHECK(batch_alloc_sampling(e));
+        std::vector<uint32_t> key(2 * (size_t)nseq);
+        for (int s = 0; s < nseq; s++) {
+            key[2 * s] = e->samp_seed;
+            key[2 * s + 1] = seq_ids ? seq_ids[s] : (unsigned)s;
+        }
+        FL_CHECK_CUDA(cudaMemcpyAsync(B.key, key.data(), sizeof(uint32_t) * key.size(), cudaMemcpyHostToDevice, e->s));
+    }
+    const StepBuffers b = batch_buffers(e);
+    const size_t d = e->d, V = e->V;
+    const size_t region = (size_t)(B.slots / kPageSize) * e->Hkv * kPageSize * e->hd;  // halves per sequence
+    std::vector<KvLayer> rb(B.kv_base.size()), rd(B.kv_draft.size());
+    for (int s = 0; s < nseq; s++) {
+        // this sequence's KV region, addressed as a cache of its own
+        for (size_t l = 0; l < rb.size(); l++) rb[l] = {B.kv_base[l].k + s * region, B.kv_base[l].v + s * region};
+        for (size_t l = 0; l < rd.size(); l++) rd[l] = {B.kv_draft[l].k + s * region, B.kv_draft[l].v + s * region};
+        KvView vb, vd;
+        vb.kv = rb.data();
+        vd.kv = rd.data();
+        vb.block_table = vd.block_table = B.block;
+        int* sq = B.seq + (size_t)s * B.slots;
+        FL_CHECK_CUDA(cudaMemcpyAsync(sq, prompts + (size_t)s * P, sizeof(int) * P, cudaMemcpyHostToDevice, e->s));
+        FL_CHECK_CUDA(launch_embed_rows(e->embed, e->Vg, sq, nullptr, 0, e->x, e->d, P, nullptr, nullptr, e->s, false));
+        FL_CHECK(run_stack(e, e->base, e->x, P, nullptr, e->iota, e->iota, nullptr, nullptr, false, &vb));
+        // first token from the last prompt row (LM-head row s)
+        FL_CHECK(run_lm(e, e->x + (size_t)(P - 1) * d, 1, nullptr, nullptr, false, B.logits + s * V,
+                        B.amax + (size_t)s * e->nparts));
+        if (B.samp)
+            FL_CHECK_CUDA(launch_sample_first(b, P, e->s, s));
+        else
+            FL_CHECK_CUDA(launch_argmax_rows(B.amax + (size_t)s * e->nparts, e->nparts, 1, sq + P, nullptr, e->s));
+        // draft catch-up over positions 0..P: x_i = F_{i-1} + E[t_i]
+        FL_CHECK_CUDA(launch_embed_rows(e->embed, e->Vg, sq, e->x, 1, e->x2, e->d, P + 1, nullptr, nullptr, e->s, false));
+        FL_CHECK(run_stack(e, e->draft, e->x2, P + 1, nullptr, e->iota, e->iota, nullptr, nullptr, false, &vd));
+        FL_CHECK_CUDA(cudaMemcpyAsync(B.x_d1 + s * d, e->x2 + (size_t)P * d, sizeof(float) * d,
+                                      cudaMemcpyDeviceToDevice, e->s));
+        FL_CHECK_CUDA(cudaMemcpyAsync(B.out + (size_t)s * B.slots, sq + P, sizeof(int), cudaMemcpyDeviceToDevice, e->s));
+    }
+    std::vector<SpecState> h(nseq);
+    for (auto& x : h) {
+        x = SpecState{};
+        x.n = P;
+        x.produced = 1;
+        x.n_new = 1;
+        x.K = K;
+        x.max_acc = K;
+        x.one = 1;
+        x.rows = 1;
+    }
+    FL_CHECK_CUDA(cudaMemcpyAsync(B.st, h.data(), sizeof(SpecState) * nseq, cudaMemcpyHostToDevice, e->s));
+    const BatchCtl c0 = {nseq, 0};
+    FL_CHECK_CUDA(cudaMemcpyAsync(B.ctl, &c0, sizeof(c0), cudaMemcpyHostToDevice, e->s));
+    FL_CHECK(run_lm(e, B.x_d1, nseq, nullptr, nullptr, false, B.logits, B.amax));
+    if (B.samp)
+        FL_CHECK_CUDA(launch_sample_pick(b, 0, e->s, false));
+    else
+        FL_CHECK_CUDA(launch_draft_pick(b, 0, e->s, false));
+    // post-prefill state of every sequence (decodes start from it)
+    FL_CHECK_CUDA(cudaMemcpyAsync(B.st_snap, B.st, sizeof(SpecState) * nseq, cudaMemcpyDeviceToDevice, e->s));
+    FL_CHECK_CUDA(cudaMemcpyAsync(B.x_d1_snap, B.x_d1, sizeof(float) * d * nseq, cudaMemcpyDeviceToDevice, e->s));
+    if (B.samp) {
+        FL_CHECK_CUDA(copy_rows(B.q_snap, 4 * V, B.q, 4 * V * kMaxDraft, 4 * V, nseq, cudaMemcpyDeviceToDevice, e->s));
+        FL_CHECK_CUDA(copy_rows(B.m_snap, 8, B.m, 8 * (kMaxDraft + kMaxRows), 8, nseq, cudaMemcpyDeviceToDevice, e->s));
+        if (B.traced)
+            FL_CHECK_CUDA(copy_rows(B.trace_snap, 4 * V, B.trace, 4 * V * 2 * kMaxRows, 4 * V, nseq,
+                                    cudaMemcpyDeviceToDevice, e->s));
+    }
+    FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
+    if (take_device_error() != 0) return set_error(FL_E_TIMEOUT, "batch_prefill: a bounded device wait gave up");
+    FL_CHECK(build_batch_graph(e));
+    B.ready = true;
+    return FL_OK;
+}
+
+FL_API int fl_engine_batch_begin(fl_engine_t* e, int n_new) {
+    FL_CHECK(check_ready(e, true));
+    auto& B = e->bt;
+    if (!B.ready || !B.exec) return set_error(FL_E_STATE, "batch_decode: call fl_engine_batch_prefill first");
+    if (n_new <= 0 || B.P + n_new + B.K + 3 > B.slots) return set_error(FL_E_INVAL, "batch_decode: context too long");
+    const size_t V = e->V, d = e->d;
+    FL_CHECK_CUDA(cudaMemcpyAsync(B.st, B.st_snap, sizeof(SpecState) * B.n, cudaMemcpyDeviceToDevice, e->s));
+    FL_CHECK_CUDA(cudaMemcpyAsync(B.x_d1, B.x_d1_snap, sizeof(float) * d * B.n, cudaMemcpyDeviceToDevice, e->s));
+    if (B.samp) {
+        FL_CHECK_CUDA(copy_rows(B.q, 4 * V * kMaxDraft, B.q_snap, 4 * V, 4 * V, B.n, cudaMemcpyDeviceToDevice, e->s));
+        FL_CHECK_CUDA(copy_rows(B.m, 8 * (kMaxDraft + kMaxRows), B.m_snap, 8, 8, B.n, cudaMemcpyDeviceToDevice, e->s));
+        if (B.traced)
+            FL_CHECK_CUDA(copy_rows(B.trace, 4 * V * 2 * kMaxRows, B.trace_snap, 4 * V, 4 * V, B.n,
+                                    cudaMemcpyDeviceToDevice, e->s));
+    }
+    // n_new and done of every record (adjacent ints)
+    static_assert(offsetof(SpecState, done) == offsetof(SpecState, n_new) + sizeof(int), "n_new, done adjacent");
+    std::vector<int> patch(2 * (size_t)B.n);
+    for (int s = 0; s < B.n; s++) {
+        patch[2 * s] = n_new;
+        patch[2 * s + 1] = n_new <= 1 ? 1 : 0;
+    }
+    FL_CHECK_CUDA(copy_rows(&B.st->n_new, sizeof(SpecState), patch.data(), 2 * sizeof(int), 2 * sizeof(int), B.n,
+                            cudaMemcpyHostToDevice, e->s));
+    const BatchCtl c0 = {n_new <= 1 ? 0 : B.n, n_new <= 1 ? 1 : 0};
+    FL_CHECK_CUDA(cudaMemcpyAsync(B.ctl, &c0, sizeof(c0), cudaMemcpyHostToDevice, e->s));
+    FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
+    return FL_OK;
+}
+
+FL_API int fl_engine_batch_decode(fl_engine_t* e, int n_new, int* out, int* steps) {
+    FL_CHECK(fl_engine_batch_begin(e, n_new));
+    auto& B = e->bt;
+    const int K = B.K;
+    std::vector<SpecState> h(B.n);
+    FL_CHECK_CUDA(cudaEventRecord(e->ev[0], e->s));
+    long long launched = 0;
+    // every step emits at least one token per unfinished sequence and at
+    // most K + 1: launch the steps the slowest sequence needs at least, then
+    // check again
+    int chunk = (n_new - 1 + K) / (K + 1);
+    while (chunk > 0) {
+        for (int i = 0; i < chunk; i++) FL_CHECK_CUDA(cudaGraphLaunch(B.exec, e->s));
+        launched += chunk;
+        FL_CHECK_CUDA(cudaMemcpyAsync(h.data(), B.st, sizeof(SpecState) * B.n, cudaMemcpyDeviceToHost, e->s));
+        FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
+        if (take_device_error() != 0) return set_error(FL_E_TIMEOUT, "batch_decode: a bounded device wait gave up");
+        int rem = 0;
+        for (const auto& x : h) rem = std::max(rem, x.done ? 0 : x.n_new - x.produced);
+        if (rem > 0 && launched > n_new + 1) return set_error(FL_E_STATE, "batch_decode: no progress");
+        chunk = (rem + K) / (K + 1);
+    }
+    FL_CHECK_CUDA(cudaEventRecord(e->ev[1], e->s));
+    FL_CHECK_CUDA(cudaEventSynchronize(e->ev[1]));
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, e->ev[0], e->ev[1]);
+    e->t_total_us = ms * 1000.0;
+    e->last_launches = launched * B.graph_kernels;
+    if (out)
+        FL_CHECK_CUDA(cudaMemcpy2D(out, sizeof(int) * n_new, B.out, sizeof(int) * B.slots, sizeof(int) * n_new, B.n,
+                                   cudaMemcpyDeviceToHost));
+    long long total = 0;
+    for (int s = 0; s < B.n; s++) {
+        if (steps) steps[s] = h[s].steps;
+        total += h[s].steps;
+    }
+    return (int)std::min<long long>(total, INT_MAX);
+}
+
+FL_API int fl_engine_batch_trace(const fl_engine_t* e, int seq, float* logits, unsigned* qd, unsigned long long* qm,
+                                 unsigned* pt, unsigned long long* pm, int* drafted) {
+    if (!e) return set_error(FL_E_INVAL, "engine is NULL");
+    const auto& B = e->bt;
+    if (!B.ready || !B.traced) return set_error(FL_E_STATE, "batch_trace: prefill a sampled batch with the trace on");
+    if (seq < 0 || seq >= B.n) return set_error(FL_E_INVAL, "batch_trace: no such sequence");
+    FL_CHECK_CUDA(cudaSetDevice(e->device));
+    FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
+    const size_t V = e->V, s = seq;
+    if (logits)
+        FL_CHECK_CUDA(cudaMemcpy(logits, B.trace + s * 2 * kMaxRows * V, sizeof(float) * 2 * kMaxRows * V,
+                                 cudaMemcpyDeviceToHost));
+    if (qd) FL_CHECK_CUDA(cudaMemcpy(qd, B.q + s * kMaxDraft * V, sizeof(uint32_t) * kMaxDraft * V, cudaMemcpyDeviceToHost));
+    if (pt) FL_CHECK_CUDA(cudaMemcpy(pt, B.p + s * kMaxRows * V, sizeof(uint32_t) * kMaxRows * V, cudaMemcpyDeviceToHost));
+    const unsigned long long* m = B.m + s * (kMaxDraft + kMaxRows);
+    if (qm) FL_CHECK_CUDA(cudaMemcpy(qm, m, sizeof(unsigned long long) * kMaxDraft, cudaMemcpyDeviceToHost));
+    if (pm) FL_CHECK_CUDA(cudaMemcpy(pm, m + kMaxDraft, sizeof(unsigned long long) * kMaxRows, cudaMemcpyDeviceToHost));
+    if (drafted) {
+        SpecState h;
+        FL_CHECK_CUDA(cudaMemcpy(&h, B.st + s, sizeof(h), cudaMemcpyDeviceToHost));
+        memcpy(drafted, h.drafted, sizeof(int) * kMaxDraft);
+    }
+    return FL_OK;
+}
+
+// One step of the prefilled batch (after fl_engine_batch_begin); state[s] =
+// (n, produced, steps, a_last, done) of sequence s.
+FL_API int fl_engine_batch_step(fl_engine_t* e, int* state) {
+    FL_CHECK(check_ready(e, true));
+    auto& B = e->bt;
+    if (!B.ready || !B.exec) return set_error(FL_E_STATE, "batch_step: call fl_engine_batch_prefill first");
+    FL_CHECK_CUDA(cudaGraphLaunch(B.exec, e->s));
+    std::vector<SpecState> h(B.n);
+    FL_CHECK_CUDA(cudaMemcpyAsync(h.data(), B.st, sizeof(SpecState) * B.n, cudaMemcpyDeviceToHost, e->s));
+    FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
+    if (take_device_error() != 0) return set_error(FL_E_TIMEOUT, "batch_step: a bounded device wait gave up");
+    if (state)
+        for (int s = 0; s < B.n; s++) {
+            int* o = state + 5 * s;
+            o[0] = h[s].n;
+            o[1] = h[s].produced;
+            o[2] = h[s].steps;
+            o[3] = h[s].a_last;
+            o[4] = h[s].done;
+        }
+    return FL_OK;
+}
+
 FL_API int fl_engine_spec_generate_batch(fl_engine_t* e, const int* prompts, int P, int nseq, const unsigned* seq_ids,
                                          int n_new, int K, int* out, int* steps) {
     FL_CHECK(check_ready(e, true));
-    if (!prompts || !out || nseq <= 0 || P <= 0 || n_new <= 0) return set_error(FL_E_INVAL, "spec_generate_batch: bad arguments");
-    const float T = e->samp_T, top_p = e->samp_top_p;
-    const unsigned seed = e->samp_seed;
+    if (!prompts || !out || nseq <= 0 || P <= 0 || n_new <= 0 || K < 1 || K > kMaxDraft)
+        return set_error(FL_E_INVAL, "spec_generate_batch: bad arguments");
+    const int slots = P + n_new + K + 3;
+    auto& B = e->bt;
+    const int rows_cap = std::min(nseq, e->R / (K + 1));
+    if (B.cap < rows_cap || B.slots < slots) {
+        // as many sequences per batch as rows and (80 % of) free memory allow
+        // (an existing reservation that holds them all is kept)
+        size_t fr = 0, tot = 0;
+        FL_CHECK_CUDA(cudaMemGetInfo(&fr, &tot));
+        size_t free_now = fr;
+        if (B.cap) free_now += batch_bytes_per_seq(e, B.slots) * B.cap;
+        const int need_slots = std::max(slots, B.slots);
+        const long long by_mem = (long long)(free_now * 0.8 / batch_bytes_per_seq(e, need_slots));
+        const int cap = (int)std::min<long long>((long long)rows_cap, by_mem);
+        if (cap < 1) return set_error(FL_E_NOMEM, "spec_generate_batch: no room for one sequence");
+        if (cap > B.cap || B.slots < slots) FL_CHECK(fl_engine_batch_reserve(e, cap, need_slots));
+    }
     cudaEvent_t t0 = nullptr, t1 = nullptr;
     FL_CHECK_CUDA(cudaEventCreate(&t0));
     FL_CHECK_CUDA(cudaEventCreate(&t1));
@@ -1455,20 +2003,28 @@ FL_API int fl_engine_spec_generate_batch(fl_engine_t* e, const int* prompts, int
     } ev_guard{t0, t1};
     FL_CHECK_CUDA(cudaEventRecord(t0, e->s));
     long long total = 0;
+    std::vector<unsigned> ids(nseq);
+    for (int i = 0; i < nseq; i++) ids[i] = seq_ids ? seq_ids[i] : (unsigned)i;
+    std::vector<int> st(nseq);
+    double decode_us = 0.0;
+    for (int s0 = 0; s0 < nseq; s0 += B.cap) {
+        const int n = std::min(B.cap, nseq - s0);
+        FL_CHECK(fl_engine_batch_prefill(e, prompts + (size_t)s0 * P, P, n, ids.data() + s0, K));
+        const int rc = fl_engine_batch_decode(e, n_new, out + (size_t)s0 * n_new, st.data() + s0);
+        if (rc < 0) return rc;
+        decode_us += e->t_total_us;
+    }
     for (int i = 0; i < nseq; i++) {
-        // one sequence after another; each draws from its own Philox stream
-        if (T > 0.0f) FL_CHECK(fl_engine_set_sampling(e, T, top_p, seed, seq_ids ? seq_ids[i] : (unsigned)i));
-        int st = 0;
-        FL_CHECK(fl_engine_spec_generate(e, prompts + (size_t)i * P, P, n_new, K, -1, out + (size_t)i * n_new, nullptr,
-                                         &st));
-        if (steps) steps[i] = st;
-        total += st;
+        if (steps) steps[i] = st[i];
+        total += st[i];
     }
     FL_CHECK_CUDA(cudaEventRecord(t1, e->s));
     FL_CHECK_CUDA(cudaEventSynchronize(t1));
     float ms = 0.0f;
     cudaEventElapsedTime(&ms, t0, t1);
     e->t_total_us = ms * 1000.0;
+    e->t_verify_us = decode_us;  // the decode loops alone (prefills excluded)
+    e->t_draft_us = 0.0;
     return (int)std::min<long long>(total, INT_MAX);
 }
 

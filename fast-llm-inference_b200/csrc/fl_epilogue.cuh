@@ -9,6 +9,19 @@
 
 namespace fl {
 
+// Rotary position and cache slot of activation row r (batched rows: the
+// row's sequence record and KV region).
+__device__ __forceinline__ int row_pos(const GemvParams& p, int r) {
+    if (p.seq_rows <= 0) return p.pos[r];
+    const int b = r / p.seq_rows;
+    return p.pos[b * p.seq_state + (r - b * p.seq_rows)];
+}
+__device__ __forceinline__ int row_slot(const GemvParams& p, int r) {
+    if (p.seq_rows <= 0) return *p.slot_base + r;
+    const int b = r / p.seq_rows;
+    return b * p.seq_slots + p.slot_base[b * p.seq_state] + (r - b * p.seq_rows);
+}
+
 // Epilogue of one weight-row pair (n0, n0 + 1) for activation row r.
 template <int EPI>
 __device__ __forceinline__ void pair_epilogue(const GemvParams& p, int r, int n0, bool has1, float y0, float y1,
@@ -35,7 +48,7 @@ __device__ __forceinline__ void pair_epilogue(const GemvParams& p, int r, int n0
             // inference.c:165-173 adjacent-pair rotation at position pos[r]
             const int ii = (n0 < p.q_dim ? n0 : n0 - p.q_dim) % p.head_dim;
             const float freq = __fdiv_rn(1.0f, powf(p.theta, __fdiv_rn((float)ii, (float)p.head_dim)));
-            const float ang = __fmul_rn((float)p.pos[r], freq);
+            const float ang = __fmul_rn((float)row_pos(p, r), freq);
             float sn, cs;
             sincosf(ang, &sn, &cs);
             v0 = __fsub_rn(__fmul_rn(y0, cs), __fmul_rn(y1, sn));
@@ -49,7 +62,7 @@ __device__ __forceinline__ void pair_epilogue(const GemvParams& p, int r, int n0
             const int c = n0 - (is_k ? p.q_dim : qkd);
             const int h = c / p.head_dim;
             const int dd = c - h * p.head_dim;
-            const int slot = *p.slot_base + r;
+            const int slot = row_slot(p, r);
             const int page = p.block_table[slot / kPageSize];
             const size_t off = (((size_t)page * p.kv_heads + h) * kPageSize + (slot % kPageSize)) * p.head_dim + dd;
             *reinterpret_cast<__half2*>((is_k ? p.kv.k : p.kv.v) + off) = __floats2half2_rn(v0, v1);

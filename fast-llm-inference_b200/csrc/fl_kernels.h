@@ -53,6 +53,11 @@ struct GemvParams {
     const int* block_table;   // slot / kPageSize -> page
     const int* slot_base;     // device scalar: cache slot of activation row 0
     const int* pos;           // [rows] rotary positions
+    // Batched rows (seq_rows > 0): row r belongs to sequence b = r / seq_rows
+    // as its row i = r % seq_rows; its slot is b * seq_slots +
+    // slot_base[b * seq_state] + i and its position pos[b * seq_state + i]
+    // (seq_state = ints between the sequences' state records)
+    int seq_rows, seq_state, seq_slots;
     int q_dim, kv_dim, head_dim, kv_heads;
     float theta;
     // EPI_SWIGLU
@@ -146,8 +151,12 @@ struct AttnParams {
     KvLayer kv;
     const int* block_table;
     const int* slot_base;     // device scalar: slot of new row 0 (= prefix length)
-    int M;                    // new rows
+    int M;                    // new rows (per sequence when seqs > 1)
     const int* dyn_M;
+    // Batched sequences (grid z): sequence b owns rows [b M, (b + 1) M) of q
+    // and out, cache slots [b seq_slots, (b + 1) seq_slots) (seq_slots a
+    // multiple of the page size) and its prefix length slot_base[b * seq_state]
+    int seqs, seq_state, seq_slots;
     const uint8_t* mask;      // [M*M] visibility among new rows, NULL = causal
     int heads, kv_heads, head_dim;
     // KV head of local query head h: (q_head0 + h) / group - kv_head0; group 0
@@ -158,9 +167,10 @@ struct AttnParams {
     uint8_t* out_q;           // [rows, heads*head_dim] quantized output
     float* out_f;             // optional f32 output
     const int* done;
-    // Decode split-K scratch (M <= kMaxRows): per (head, split, row) partial
-    // max / sum / unnormalised output, and one arrival counter per head
-    // (zero between launches). Sizes from attention_scratch_*.
+    // Decode split-K scratch (M <= kMaxRows): per (sequence, head, split,
+    // row) partial max / sum / unnormalised output, and one arrival counter
+    // per (sequence, head) (zero between launches). Sizes per sequence from
+    // attention_scratch_*.
     float* part;
     int* counters;
 };

@@ -34,6 +34,13 @@ struct SpecState {
     int target[kMaxRows];   // base-model argmax of the verify rows
 };
 
+// Shared state of an in-GPU batch: sequences still decoding, and the flag
+// every kernel of a batched step tests (set once all sequences are done).
+struct BatchCtl {
+    int active;
+    int done;
+};
+
 struct StepBuffers {
     SpecState* st;
     int* seq;               // committed tokens
@@ -60,7 +67,61 @@ struct StepBuffers {
     // [2 * kMaxRows, V]: draft j at row j, verify row r at kMaxDraft + r,
     // the first token after the prefill at 2 * kMaxRows - 1
     float* trace;
+    // In-GPU batch of `batch` sequences (0: one sequence): the buffers above
+    // hold every sequence, and the control kernels take sequence s's slice
+    // (seq_view). Verify and
+    // catch-up rows (x_v, x_d, logits, amax_part) are rows_per per sequence;
+    // the single-row draft passes use x_d1 [sequences, d] and the LM-head
+    // rows s of logits_d / amax_d.
+    int batch;
+    int rows_per;
+    int seq_cap;            // ints per sequence in seq / out / acc_hist
+    float* x_d1;
+    const float* logits_d;
+    const unsigned long long* amax_d;
+    BatchCtl* ctl;
 };
+
+#ifdef __CUDACC__
+// Sequence s's view of a batched step's buffers (unchanged for one sequence).
+__device__ __forceinline__ StepBuffers seq_view(const StepBuffers& b0, int s) {
+    StepBuffers b = b0;
+    if (!b0.batch) {
+        b.x_d1 = b0.x_d;
+        b.logits_d = b0.logits;
+        b.amax_d = b0.amax_part;
+        return b;
+    }
+    const size_t rows = (size_t)s * b0.rows_per;
+    b.st = b0.st + s;
+    b.seq = b0.seq + (size_t)s * b0.seq_cap;
+    b.out = b0.out + (size_t)s * b0.seq_cap;
+    b.acc_hist = b0.acc_hist + (size_t)s * b0.seq_cap;
+    b.x_d = b0.x_d + rows * b0.d;
+    b.x_v = b0.x_v + rows * b0.d;
+    b.x_d1 = b0.x_d1 + (size_t)s * b0.d;
+    b.amax_part = b0.amax_part + rows * b0.nparts;
+    b.amax_d = b0.amax_d + (size_t)s * b0.nparts;
+    b.logits = b0.logits + rows * b0.V;
+    b.logits_d = b0.logits_d + (size_t)s * b0.V;
+    b.key = b0.key + 2 * s;
+    if (b0.qd) {
+        b.qd = b0.qd + (size_t)s * kMaxDraft * b0.V;
+        b.qm = b0.qm + (size_t)s * (kMaxDraft + kMaxRows);
+        b.pt = b0.pt + (size_t)s * kMaxRows * b0.V;
+        b.pm = b0.pm + (size_t)s * (kMaxDraft + kMaxRows);
+        b.resid = b0.resid + (size_t)s * b0.V;
+    }
+    if (b0.trace) b.trace = b0.trace + (size_t)s * 2 * kMaxRows * b0.V;
+    return b;
+}
+
+// Called once by the acceptance of a sequence that has just finished: the
+// last sequence of a batch to finish raises the batch's done flag.
+__device__ __forceinline__ void batch_retire(const StepBuffers& b, int finished) {
+    if (b.batch && finished && atomicSub(&b.ctl->active, 1) == 1) atomicExch(&b.ctl->done, 1);
+}
+#endif
 
 // x[r] = E[tok[r]] + (r >= shift ? feat[r - shift] : 0) for r < rows,
 // rows = dyn_rows ? *dyn_rows : rows_static; ids outside [0, vocab) read row 0.
@@ -71,7 +132,9 @@ cudaError_t launch_embed_rows(const float* embed, int vocab, const int* tok, con
 // Greedy pick of draft token j from the LM-head partials of row 0; writes
 // drafted[j] and, when j + 1 < K, the next single-row draft input
 // x_d[0] = g + E[drafted[j]] with g = x_d[g_row] (g_row = last_row when
-// j == 0, else 0) at slot/position n + j + 1.
+// j == 0, else 0) at slot/position n + j + 1. Batched: one CTA per sequence,
+// draft row s of the LM head, g = x_d1[s] (the catch-up's last feature is
+// gathered there first, launch_gather_last).
 cudaError_t launch_draft_pick(const StepBuffers& b, int j, cudaStream_t s, bool pdl);
 
 // Verify rows: x_v[r] = E[tok_r], tok_0 = seq[n], tok_r = drafted[r - 1],
@@ -90,7 +153,7 @@ cudaError_t launch_catchup_prep(const StepBuffers& b, int K, cudaStream_t s, boo
 // Stochastic mode (sample_ops.cu): first token after the prefill from logits
 // row 0; sampled draft pick j; nucleus distributions of the K + 1 verify rows;
 // rejection-sampling acceptance with the same state update as launch_accept.
-cudaError_t launch_sample_first(const StepBuffers& b, int P, cudaStream_t s);
+cudaError_t launch_sample_first(const StepBuffers& b, int P, cudaStream_t s, int seq = 0);
 cudaError_t launch_sample_pick(const StepBuffers& b, int j, cudaStream_t s, bool pdl);
 cudaError_t launch_target_dist(const StepBuffers& b, int K, cudaStream_t s, bool pdl);
 cudaError_t launch_accept_sampled(const StepBuffers& b, int K, cudaStream_t s, bool pdl);
@@ -102,6 +165,13 @@ cudaError_t launch_tp_local_best(const unsigned long long* part, int nparts, int
                                  cudaStream_t s);
 cudaError_t launch_tp_reduce_best(const unsigned long long* all, int size, int stride, int rows,
                                   unsigned long long* out, cudaStream_t s);
+
+// Sequences of a step: launches take one CTA (or one row of CTAs) each.
+inline int step_seqs(const StepBuffers& b) { return b.batch > 0 ? b.batch : 1; }
+
+// Batched: x_d1[s] = x_d[s * rows_per + last_row_s] (the draft catch-up's
+// feature of each sequence's newest token).
+cudaError_t launch_gather_last(const StepBuffers& b, cudaStream_t s, bool pdl);
 
 cudaError_t launch_argmax_rows(const unsigned long long* part, int nparts, int rows, int* out_tok,
                                float* out_val, cudaStream_t s);

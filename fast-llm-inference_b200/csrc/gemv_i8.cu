@@ -15,6 +15,7 @@
 // issued before griddepcontrol.wait so it overlaps the previous kernel.
 #include "fl_common.cuh"
 #include "fl_kernels.h"
+#include "fl_epilogue.cuh"
 #include "fl_layout.cuh"
 
 namespace fl {
@@ -259,7 +260,7 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const GemvParams p) {
                 const int i = (n0 < p.q_dim ? n0 : n0 - p.q_dim) % p.head_dim;
                 // inference.c:165-173 (theta from the model configuration)
                 const float freq = __fdiv_rn(1.0f, powf(p.theta, __fdiv_rn((float)i, (float)p.head_dim)));
-                const float ang = __fmul_rn((float)p.pos[r], freq);
+                const float ang = __fmul_rn((float)row_pos(p, r), freq);
                 float sn, cs;
                 sincosf(ang, &sn, &cs);
                 const float a = v0, b = v1;
@@ -274,7 +275,7 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const GemvParams p) {
                 const int c = n0 - (is_k ? p.q_dim : qkd);
                 const int h = c / p.head_dim;
                 const int dd = c - h * p.head_dim;
-                const int slot = *p.slot_base + r;
+                const int slot = row_slot(p, r);
                 const int page = p.block_table[slot / kPageSize];
                 const size_t off = (((size_t)page * p.kv_heads + h) * kPageSize + (slot % kPageSize)) *
                                        p.head_dim + dd;

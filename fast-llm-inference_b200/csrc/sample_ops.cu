@@ -226,33 +226,36 @@ __device__ __forceinline__ void trace_row(const StepBuffers& b, int row, const f
     for (int i = threadIdx.x; i < b.V; i += kST) t[i] = l[i];
 }
 
-__global__ void __launch_bounds__(kST) sample_first_kernel(StepBuffers b, int P) {
+__global__ void __launch_bounds__(kST) sample_first_kernel(const StepBuffers b0, int P, int s0) {
     __shared__ unsigned long long red[kSW];
-    trace_row(b, 2 * kMaxRows - 1, b.logits);
-    const unsigned long long M = nucleus(b.logits, b.V, b.temp, b.top_p, b.pt, red);
+    const StepBuffers b = seq_view(b0, s0 + blockIdx.x);
+    trace_row(b, 2 * kMaxRows - 1, b.logits_d);
+    const unsigned long long M = nucleus(b.logits_d, b.V, b.temp, b.top_p, b.pt, red);
     const int t = draw(b.pt, b.V, M, philox_u24(b.key[0], b.key[1], 0xFFFFFFFFu, (uint32_t)P, 2u));
     if (threadIdx.x == 0) b.seq[P] = t;
 }
 
-// Sampled draft token j from the draft LM-head logits (row 0); its weights
-// and mass are kept for the acceptance test. The rest as the greedy pick.
-__global__ void __launch_bounds__(kST) sample_pick_kernel(StepBuffers b, int j) {
+// Sampled draft token j from the draft LM-head logits (row 0; batched: row
+// s); its weights and mass are kept for the acceptance test. The rest as the
+// greedy pick.
+__global__ void __launch_bounds__(kST) sample_pick_kernel(const StepBuffers b0, int j) {
     __shared__ unsigned long long red[kSW];
     pdl_trigger();
     pdl_wait();
+    const StepBuffers b = seq_view(b0, blockIdx.x);
     SpecState* st = b.st;
     if (st->done) return;
     const int n = st->n;
     uint32_t* q = b.qd + (size_t)j * b.V;
-    trace_row(b, j, b.logits);
-    const unsigned long long M = nucleus(b.logits, b.V, b.temp, b.top_p, q, red);
+    trace_row(b, j, b.logits_d);
+    const unsigned long long M = nucleus(b.logits_d, b.V, b.temp, b.top_p, q, red);
     const int tok = draw(q, b.V, M, philox_u24(b.key[0], b.key[1], (uint32_t)st->steps, (uint32_t)(n + 1 + j), 0u));
     if (j + 1 < st->K) {
-        const int g_row = (j == 0) ? st->last_row : 0;
-        const float* g = b.x_d + (size_t)g_row * b.d;
+        const int g_row = (j == 0 && !b.batch) ? st->last_row : 0;
+        const float* g = b.x_d1 + (size_t)g_row * b.d;
         const float* e = b.embed + (size_t)tok * b.d;
         // g_row may be 0: element-wise in place is safe.
-        for (int i = threadIdx.x; i < b.d; i += blockDim.x) b.x_d[i] = __fadd_rn(g[i], e[i]);
+        for (int i = threadIdx.x; i < b.d; i += blockDim.x) b.x_d1[i] = __fadd_rn(g[i], e[i]);
     }
     if (threadIdx.x == 0) {
         b.qm[j] = M;
@@ -265,10 +268,11 @@ __global__ void __launch_bounds__(kST) sample_pick_kernel(StepBuffers b, int j) 
 }
 
 // Target weights of the K + 1 verify rows (one CTA per row).
-__global__ void __launch_bounds__(kST) target_dist_kernel(StepBuffers b) {
+__global__ void __launch_bounds__(kST) target_dist_kernel(const StepBuffers b0) {
     __shared__ unsigned long long red[kSW];
     pdl_trigger();
     pdl_wait();
+    const StepBuffers b = seq_view(b0, blockIdx.y);
     if (b.st->done) return;
     const int r = blockIdx.x;
     trace_row(b, kMaxDraft + r, b.logits + (size_t)r * b.V);
@@ -281,10 +285,11 @@ __global__ void __launch_bounds__(kST) target_dist_kernel(StepBuffers b) {
 // min(1, p(x) / q(x)); on rejection draw from the residual max(0, p - q), or
 // from p when it is empty; all accepted: bonus from p_K), then the same state
 // update as the greedy acceptance.
-__global__ void __launch_bounds__(kST) accept_sampled_kernel(StepBuffers b, int K) {
+__global__ void __launch_bounds__(kST) accept_sampled_kernel(const StepBuffers b0, int K) {
     __shared__ unsigned long long red[kSW];
     pdl_trigger();
     pdl_wait();
+    const StepBuffers b = seq_view(b0, blockIdx.x);
     SpecState* st = b.st;
     if (st->done) return;
     const int n = st->n;
@@ -334,14 +339,15 @@ __global__ void __launch_bounds__(kST) accept_sampled_kernel(StepBuffers b, int 
     st->rows = a + 1;
     st->last_row = a;
     st->draft_base = n + 1;
-    for (int r = 0; r <= a; r++) st->draft_pos[r] = n + 1 + r;
+    for (int r = 0; r <= K; r++) st->draft_pos[r] = n + 1 + r;
     st->done = produced >= st->n_new ? 1 : 0;
+    batch_retire(b, st->done);
 }
 
 template <typename... KArgs, typename... Args>
-cudaError_t launch_rows(void (*kern)(KArgs...), int grid, cudaStream_t s, bool pdl, Args... args) {
+cudaError_t launch_rows(void (*kern)(KArgs...), dim3 grid, cudaStream_t s, bool pdl, Args... args) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
+    cfg.gridDim = grid;
     cfg.blockDim = dim3(kST);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
@@ -354,17 +360,17 @@ cudaError_t launch_rows(void (*kern)(KArgs...), int grid, cudaStream_t s, bool p
 
 }  // namespace
 
-cudaError_t launch_sample_first(const StepBuffers& b, int P, cudaStream_t s) {
-    return launch_rows(sample_first_kernel, 1, s, false, b, P);
+cudaError_t launch_sample_first(const StepBuffers& b, int P, cudaStream_t s, int seq) {
+    return launch_rows(sample_first_kernel, dim3(1), s, false, b, P, seq);
 }
 cudaError_t launch_sample_pick(const StepBuffers& b, int j, cudaStream_t s, bool pdl) {
-    return launch_rows(sample_pick_kernel, 1, s, pdl, b, j);
+    return launch_rows(sample_pick_kernel, dim3(step_seqs(b)), s, pdl, b, j);
 }
 cudaError_t launch_target_dist(const StepBuffers& b, int K, cudaStream_t s, bool pdl) {
-    return launch_rows(target_dist_kernel, K + 1, s, pdl, b);
+    return launch_rows(target_dist_kernel, dim3(K + 1, step_seqs(b)), s, pdl, b);
 }
 cudaError_t launch_accept_sampled(const StepBuffers& b, int K, cudaStream_t s, bool pdl) {
-    return launch_rows(accept_sampled_kernel, 1, s, pdl, b, K);
+    return launch_rows(accept_sampled_kernel, dim3(step_seqs(b)), s, pdl, b, K);
 }
 
 }  // namespace fl

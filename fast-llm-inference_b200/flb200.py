@@ -135,6 +135,13 @@ _SIGS = {
     "fl_engine_spec_decode": (I, [VP, I, VP, VP, VP]),
     "fl_engine_set_sampling": (I, [VP, F, F, U32, U32]),
     "fl_engine_spec_generate_batch": (I, [VP, VP, I, I, VP, I, I, VP, VP]),
+    "fl_engine_batch_reserve": (I, [VP, I, I]),
+    "fl_engine_batch_capacity": (I, [VP, VP, VP]),
+    "fl_engine_batch_prefill": (I, [VP, VP, I, I, VP, I]),
+    "fl_engine_batch_begin": (I, [VP, I]),
+    "fl_engine_batch_decode": (I, [VP, I, VP, VP]),
+    "fl_engine_batch_step": (I, [VP, VP]),
+    "fl_engine_batch_trace": (I, [VP, I, VP, VP, VP, VP, VP, VP]),
     "fl_engine_get_sampling": (I, [VP, VP, VP, VP, VP]),
     "fl_engine_sample_trace_enable": (I, [VP, I]),
     "fl_engine_sample_trace": (I, [VP, VP, VP, VP, VP, VP, VP]),
@@ -380,9 +387,10 @@ class Engine:
         return self.spec_decode(n_new)
 
     def spec_generate_batch(self, prompts, n_new, k, seq_ids=None):
-        """Decodes independent sequences (rows of `prompts`) one after another
-        under the current rule; returns (tokens [nseq, n_new], steps [nseq],
-        device seconds of the whole call)."""
+        """Decodes independent sequences (rows of `prompts`) together on this
+        GPU (in-GPU batches as large as rows and memory allow) under the
+        current rule; returns (tokens [nseq, n_new], steps [nseq], device
+        seconds of the whole call, prefills included)."""
         pr = np.ascontiguousarray(prompts, np.int32)
         nseq, P = pr.shape
         ids = None if seq_ids is None else np.ascontiguousarray(seq_ids, np.uint32)
@@ -392,6 +400,52 @@ class Engine:
         if rc < 0:
             self.lib.check(rc, "spec_generate_batch")
         return out, steps, self.last_timing()[2] * 1e-6
+
+    def batch_reserve(self, nseq, max_ctx):
+        """KV regions and buffers for an in-GPU batch of nseq sequences of up
+        to max_ctx positions each."""
+        self.lib.check(self.lib.fl_engine_batch_reserve(self.h, nseq, max_ctx), "batch_reserve")
+
+    def batch_capacity(self):
+        n, s = C.c_int(), C.c_int()
+        self.lib.check(self.lib.fl_engine_batch_capacity(self.h, C.byref(n), C.byref(s)), "batch_capacity")
+        return n.value, s.value
+
+    def batch_prefill(self, prompts, k, seq_ids=None):
+        pr = np.ascontiguousarray(prompts, np.int32)
+        nseq, P = pr.shape
+        ids = None if seq_ids is None else np.ascontiguousarray(seq_ids, np.uint32)
+        self.lib.check(self.lib.fl_engine_batch_prefill(self.h, ptr(pr), P, nseq, ptr(ids), k), "batch_prefill")
+        self._bn = nseq
+
+    def batch_decode(self, n_new):
+        """Decodes the prefilled batch: (tokens [nseq, n_new], steps [nseq],
+        device seconds)."""
+        out = np.empty((self._bn, n_new), np.int32)
+        steps = np.empty(self._bn, np.int32)
+        rc = self.lib.fl_engine_batch_decode(self.h, n_new, ptr(out), ptr(steps))
+        if rc < 0:
+            self.lib.check(rc, "batch_decode")
+        return out, steps, self.last_timing()[2] * 1e-6
+
+    def batch_begin(self, n_new):
+        self.lib.check(self.lib.fl_engine_batch_begin(self.h, n_new), "batch_begin")
+
+    def batch_step(self):
+        """One step of every sequence: list of dict(n, produced, steps, accepted, done)."""
+        s = np.zeros((self._bn, 5), np.int32)
+        self.lib.check(self.lib.fl_engine_batch_step(self.h, ptr(s)), "batch_step")
+        return [dict(zip(("n", "produced", "steps", "accepted", "done"), (int(v) for v in r))) for r in s]
+
+    def batch_trace(self, seq):
+        """sample_trace() of sequence `seq` of a sampled batch."""
+        V = self.cfg["vocab_size"]
+        t = dict(logits=np.empty((16, V), np.float32), qd=np.empty((7, V), np.uint32), qm=np.empty(7, np.uint64),
+                 pt=np.empty((8, V), np.uint32), pm=np.empty(8, np.uint64), drafted=np.empty(7, np.int32))
+        self.lib.check(self.lib.fl_engine_batch_trace(self.h, int(seq), ptr(t["logits"]), ptr(t["qd"]), ptr(t["qm"]),
+                                                      ptr(t["pt"]), ptr(t["pm"]), ptr(t["drafted"])),
+                       "batch_trace")
+        return t
 
     def set_sampling(self, temperature, top_p=1.0, seed=0, seq_id=0):
         """temperature <= 0: greedy; > 0: Philox-keyed rejection sampling

@@ -220,13 +220,49 @@ int fl_engine_spec_generate(fl_engine_t* e, const int* prompt, int prompt_len,
 /* Independent sequences on one engine (one rank's share of a batch): for each
  * i < nseq, prompts[i * prompt_len ..] is decoded for n_new tokens with draft
  * length k into out[i * n_new ..], under the rule of fl_engine_set_sampling
- * with sequence id seq_ids[i] (i when seq_ids is NULL), so every sequence's
- * stream is the same wherever and alongside whatever it runs. steps[i]
- * (may be NULL) receives the speculative steps of sequence i. Returns the
- * total number of steps or a negative FL_E_* code; fl_engine_last_timing's
- * total_us is the device time of the whole call, prefills included. */
+ * with sequence id seq_ids[i] (i when seq_ids is NULL). The sequences are
+ * decoded together in in-GPU batches (fl_engine_batch_*) as large as the
+ * engine's rows (max_seq_len / (k + 1)) and 80 % of free device memory allow;
+ * a larger existing reservation is reused. Every decision of a sequence
+ * follows the rule with its own Philox key, whatever else shares its batch;
+ * batches of different sizes may run other kernels (GEMV chunks or the
+ * tcgen05 GEMM), whose logits differ in the last bits. steps[i] (may be
+ * NULL) receives the speculative steps of sequence i. Returns the total
+ * number of steps or a negative FL_E_* code; fl_engine_last_timing's
+ * total_us is the device time of the whole call, prefills included, and
+ * verify_us the decode loops alone. */
 int fl_engine_spec_generate_batch(fl_engine_t* e, const int* prompts, int prompt_len, int nseq,
                                   const unsigned* seq_ids, int n_new, int k, int* out, int* steps);
+
+/* In-GPU batch of independent sequences (one GPU; not tensor-parallel).
+ * Each sequence has its own KV region of max_ctx positions (rounded up to a
+ * page), state, tokens and Philox key; a step runs the k - 1 draft passes
+ * over one row per sequence, one verify pass over nseq x (k + 1) rows, the
+ * acceptance of every sequence, and the draft catch-up over nseq x (k + 1)
+ * rows (rows past a sequence's accepted ones are zero and unused), all in
+ * one CUDA graph. Passes of more than 16 rows run through the tcgen05 GEMM.
+ *
+ * reserve: allocates the regions and buffers for nseq sequences (frees a
+ * previous reservation). capacity: the reserved sequences and slots.
+ * prefill: prefills prompts[i * prompt_len ..] of sequence i < nseq
+ * (nseq <= reserved, nseq * (k + 1) <= max_seq_len) under the current
+ * rule with ids seq_ids (NULL: 0..nseq-1), draws every first token and the
+ * first draft, and records the step graph. begin: restores the
+ * post-prefill state for a decode of n_new tokens. decode: begin, then
+ * steps until every sequence has n_new tokens; out[i * n_new ..], steps[i];
+ * returns the total steps. step: one step after begin; state[5 i ..] =
+ * (n, produced, steps, accepted, done) of sequence i. trace: the
+ * fl_engine_sample_trace arrays of sequence seq (sampled prefill with the
+ * trace enabled). */
+int fl_engine_batch_reserve(fl_engine_t* e, int nseq, int max_ctx);
+int fl_engine_batch_capacity(const fl_engine_t* e, int* nseq, int* slots);
+int fl_engine_batch_prefill(fl_engine_t* e, const int* prompts, int prompt_len, int nseq,
+                            const unsigned* seq_ids, int k);
+int fl_engine_batch_begin(fl_engine_t* e, int n_new);
+int fl_engine_batch_decode(fl_engine_t* e, int n_new, int* out, int* steps);
+int fl_engine_batch_step(fl_engine_t* e, int* state);
+int fl_engine_batch_trace(const fl_engine_t* e, int seq, float* logits, unsigned* qd, unsigned long long* qm,
+                          unsigned* pt, unsigned long long* pm, int* drafted);
 
 /* Decoding rule of the next fl_engine_spec_prefill / spec_generate.
  * temperature <= 0: greedy (argmax drafts, exact-match acceptance; the

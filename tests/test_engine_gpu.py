@@ -290,6 +290,42 @@ def check_weights(orc, E_dev, M_dev, logits, T, top_p, what):
     return E, M
 
 
+def check_sampled_step(orc, u24, k, n_new, T, top_p, pre, t, before, after, out, acc_hist=None):
+    """Replays one sampled step of one sequence: `pre` = (logits, weights,
+    mass, token) of draft 0 (drawn by the previous step), `t` the trace after
+    the step, `before` / `after` its state; the emitted tokens are in `out`."""
+    n, s, produced = before["n"], before["steps"], before["produced"]
+    d_lg = [pre[0]] + [t["logits"][j] for j in range(1, k)]
+    d_q = [pre[1]] + [t["qd"][j] for j in range(1, k)]
+    d_m = [pre[2]] + [int(t["qm"][j]) for j in range(1, k)]
+    drafted = [pre[3]] + [int(t["drafted"][j]) for j in range(1, k)]
+    for j in range(k):
+        check_weights(orc, d_q[j], d_m[j], d_lg[j], T, top_p, f"step {s} draft {j}")
+        assert drafted[j] == orc.sample_pick(d_q[j], d_m[j], u24(s, n + 1 + j, 0)), f"step {s}: draft draw {j}"
+    pt, pm = t["pt"], [int(v) for v in t["pm"]]
+    for r in range(k + 1):
+        check_weights(orc, pt[r], pm[r], t["logits"][TARGET_ROW0 + r], T, top_p, f"step {s} target {r}")
+    a = 0
+    while True:
+        pos = n + 1 + a
+        if a == k:
+            last = orc.sample_pick(pt[k], pm[k], u24(s, pos, 2))
+            break
+        x = drafted[a]
+        if orc.sample_accept(u24(s, pos, 1), pt[a][x], pm[a], d_q[a][x], d_m[a]):
+            a += 1
+            continue
+        R, zr = orc.sample_residual(pt[a], pm[a], d_q[a], d_m[a])
+        last = orc.sample_pick(R, zr, u24(s, pos, 2)) if zr > 0 else orc.sample_pick(pt[a], pm[a], u24(s, pos, 2))
+        break
+    assert after["accepted"] == a, f"step {s}: accepted {after['accepted']} vs {a}"
+    if acc_hist is not None:
+        assert acc_hist[s] == a, f"step {s}: histogram"
+    assert after["n"] == n + a + 1
+    want = (drafted[:a] + [last])[: n_new - produced]
+    assert out[produced: produced + len(want)].tolist() == want, f"step {s}: emitted tokens"
+
+
 def replay_sampled(eng, orc, p, k, n_new, T, top_p, seed, seq_id=0):
     """Steps the device decode and replays every sampling decision; returns
     (tokens, accepted per step)."""
@@ -306,41 +342,49 @@ def replay_sampled(eng, orc, p, k, n_new, T, top_p, seed, seq_id=0):
     t = eng.sample_trace()
     state = dict(n=P, produced=1, steps=0, done=0)
     while not state["done"]:
-        n, s, produced = state["n"], state["steps"], state["produced"]
         pre = (t["logits"][0].copy(), t["qd"][0].copy(), int(t["qm"][0]), int(t["drafted"][0]))
-        state = eng.spec_step()
+        after = eng.spec_step()
         t = eng.sample_trace()
-        d_lg = [pre[0]] + [t["logits"][j] for j in range(1, k)]
-        d_q = [pre[1]] + [t["qd"][j] for j in range(1, k)]
-        d_m = [pre[2]] + [int(t["qm"][j]) for j in range(1, k)]
-        drafted = [pre[3]] + [int(t["drafted"][j]) for j in range(1, k)]
-        for j in range(k):
-            check_weights(orc, d_q[j], d_m[j], d_lg[j], T, top_p, f"step {s} draft {j}")
-            assert drafted[j] == orc.sample_pick(d_q[j], d_m[j], u24(s, n + 1 + j, 0)), f"step {s}: draft draw {j}"
-        pt, pm = t["pt"], [int(v) for v in t["pm"]]
-        for r in range(k + 1):
-            check_weights(orc, pt[r], pm[r], t["logits"][TARGET_ROW0 + r], T, top_p, f"step {s} target {r}")
-        a = 0
-        while True:
-            pos = n + 1 + a
-            if a == k:
-                last = orc.sample_pick(pt[k], pm[k], u24(s, pos, 2))
-                break
-            x = drafted[a]
-            if orc.sample_accept(u24(s, pos, 1), pt[a][x], pm[a], d_q[a][x], d_m[a]):
-                a += 1
-                continue
-            R, zr = orc.sample_residual(pt[a], pm[a], d_q[a], d_m[a])
-            last = orc.sample_pick(R, zr, u24(s, pos, 2)) if zr > 0 else orc.sample_pick(pt[a], pm[a], u24(s, pos, 2))
-            break
-        assert state["accepted"] == a and acc_hist[s] == a, f"step {s}: accepted {state['accepted']} vs {a}"
-        assert state["n"] == n + a + 1
-        want = (drafted[:a] + [last])[: n_new - produced]
-        assert out[produced: produced + len(want)].tolist() == want, f"step {s}: emitted tokens"
+        check_sampled_step(orc, u24, k, n_new, T, top_p, pre, t, state, after, out, acc_hist)
+        state = after
     assert state["produced"] == n_new and state["steps"] == len(acc_hist)
     eng.sample_trace_enable(False)
     eng.set_sampling(0.0)
     return out, acc_hist
+
+
+def replay_sampled_batch(eng, orc, prompts, k, n_new, T, top_p, seed, ids):
+    """replay_sampled for an in-GPU batch: every sequence's decisions, step
+    by step, with its own Philox key (seed, id)."""
+    nseq, P = prompts.shape
+    eng.set_sampling(T, top_p, seed)
+    eng.sample_trace_enable(True)
+    try:
+        eng.batch_prefill(prompts, k, ids)
+        out, steps, _ = eng.batch_decode(n_new)
+        u24s = [(lambda sid: (lambda st, pos, pu: orc.philox_u24(seed, sid, st, pos, pu)))(int(i)) for i in ids]
+        traces = [eng.batch_trace(s) for s in range(nseq)]
+        for s in range(nseq):
+            E, M = orc.sample_weights(traces[s]["logits"][FIRST_ROW], T, top_p)
+            assert out[s][0] == orc.sample_pick(E, M, u24s[s](0xFFFFFFFF, P, 2)), f"sequence {s}: first token"
+        eng.batch_begin(n_new)
+        traces = [eng.batch_trace(s) for s in range(nseq)]
+        states = [dict(n=P, produced=1, steps=0, done=0) for _ in range(nseq)]
+        while not all(st["done"] for st in states):
+            pres = [(t["logits"][0].copy(), t["qd"][0].copy(), int(t["qm"][0]), int(t["drafted"][0])) for t in traces]
+            after = eng.batch_step()
+            traces = [eng.batch_trace(s) for s in range(nseq)]
+            for s in range(nseq):
+                if states[s]["done"]:
+                    assert after[s]["steps"] == states[s]["steps"], f"sequence {s} stepped after finishing"
+                    continue
+                check_sampled_step(orc, u24s[s], k, n_new, T, top_p, pres[s], traces[s], states[s], after[s], out[s])
+            states = after
+        assert [st["steps"] for st in states] == steps.tolist()
+    finally:
+        eng.sample_trace_enable(False)
+        eng.set_sampling(0.0)
+    return out, steps
 
 
 @pytest.mark.parametrize("T,top_p", [(SAMPLE_T, SAMPLE_TOP_P), (1.5, 1.0), (0.3, 0.5)])
@@ -438,8 +482,12 @@ def test_speculative_generate_sampled_reference_api(gpu, orc):
 
 
 def test_sampled_batch_independent_of_sharding(small):
-    """A sequence's sampled stream depends only on its prompt and id: the batch
-    entry point, single decodes and any split of the ids give the same tokens."""
+    """A sequence's sampled stream depends only on its prompt and id, not on
+    its place in the batch or on the other sequences: reordered batches and
+    equal-size shards give the same tokens. (Batches of different sizes may
+    take other kernels for their passes -- GEMV chunks or the tcgen05 GEMM --
+    whose logits differ in the last bits, so only the rule is exact there:
+    test_sampled_batch_replays_on_oracle.)"""
     import shard
     dims, eng, om, embed = small
     ids = np.arange(4, dtype=np.uint32)
@@ -447,16 +495,70 @@ def test_sampled_batch_independent_of_sharding(small):
     try:
         eng.set_sampling(SAMPLE_T, SAMPLE_TOP_P, SAMPLE_SEED)
         all_toks, steps, secs = eng.spec_generate_batch(prompts, 20, 4, seq_ids=ids)
-        part, _, _ = eng.spec_generate_batch(prompts[2:], 20, 4, seq_ids=ids[2:])
-        singles = []
-        for i in ids:
-            eng.set_sampling(SAMPLE_T, SAMPLE_TOP_P, SAMPLE_SEED, int(i))
-            singles.append(eng.spec_generate(prompts[i], 20, 4)[0])
+        rev, _, _ = eng.spec_generate_batch(prompts[::-1], 20, 4, seq_ids=ids[::-1])
+        lo, _, _ = eng.spec_generate_batch(prompts[:2], 20, 4, seq_ids=ids[:2])
+        hi, _, _ = eng.spec_generate_batch(prompts[2:][::-1], 20, 4, seq_ids=ids[2:][::-1])
+        pair, _, _ = eng.spec_generate_batch(prompts[[1, 2]], 20, 4, seq_ids=ids[[1, 2]])
     finally:
         eng.set_sampling(0.0)
-    assert np.array_equal(all_toks, np.stack(singles))
-    assert np.array_equal(part, all_toks[2:])
+    assert np.array_equal(rev[::-1], all_toks)
+    assert np.array_equal(lo[1], pair[0]) and np.array_equal(hi[1], pair[1])
     assert len({tuple(r) for r in all_toks.tolist()}) == 4 and secs > 0 and steps.min() >= 1
+
+
+@pytest.mark.parametrize("nseq,k", [(3, 4), (5, 6)])
+def test_sampled_batch_replays_on_oracle(small, orc, nseq, k):
+    """Every decision of every sequence of a sampled in-GPU batch follows the
+    oracle's rule with that sequence's Philox key (3 x 5 verify rows through
+    GEMV chunks; 5 x 7 through the tcgen05 GEMM)."""
+    dims, eng, om, embed = small
+    ids = np.array([7, 3, 11, 0, 5][:nseq], np.uint32)
+    prompts = np.stack([prompt(60 + i, 12, dims["vocab"]) for i in range(nseq)])
+    eng.batch_reserve(nseq, 12 + 24 + k + 3)
+    out, steps = replay_sampled_batch(eng, orc, prompts, k, 24, SAMPLE_T, SAMPLE_TOP_P, SAMPLE_SEED, ids)
+    assert out.shape == (nseq, 24) and steps.min() >= 1
+
+
+@pytest.mark.parametrize("nseq,k", [(3, 4), (4, 5), (20, 4)])
+def test_batch_greedy_streams_match_oracle(small, nseq, k):
+    """An in-GPU batch decodes every sequence to the oracle's greedy stream:
+    3 x 5 verify rows (GEMV chunks), 4 x 6 and 20 x 5 (tcgen05 GEMM; 20
+    single-row draft passes through it too)."""
+    dims, eng, om, embed = small
+    prompts = np.stack([prompt(30 + i, 16, dims["vocab"]) for i in range(nseq)])
+    eng.batch_reserve(nseq, 16 + 40 + k + 3)
+    eng.batch_prefill(prompts, k)
+    toks, steps, secs = eng.batch_decode(40)
+    for i in range(nseq):
+        want, margins = om.greedy(prompts[i], 40)
+        assert_stream_matches(toks[i], want, margins)
+    assert steps.min() >= 1 and secs > 0
+    # decoding restarts from the post-prefill state
+    again, steps2, _ = eng.batch_decode(40)
+    assert np.array_equal(again, toks) and np.array_equal(steps2, steps)
+    short, _, _ = eng.batch_decode(9)
+    assert np.array_equal(short, toks[:, :9])
+
+
+def test_batch_step_api(small):
+    """fl_engine_batch_step advances every unfinished sequence by one step
+    and leaves finished ones alone."""
+    dims, eng, om, embed = small
+    prompts = np.stack([prompt(90 + i, 10, dims["vocab"]) for i in range(3)])
+    eng.batch_reserve(3, 64)
+    eng.batch_prefill(prompts, 3)
+    toks, steps, _ = eng.batch_decode(12)
+    eng.batch_begin(12)
+    n_steps = 0
+    while True:
+        st = eng.batch_step()
+        n_steps += 1
+        assert all(s["produced"] <= 12 or s["done"] for s in st)
+        if all(s["done"] for s in st):
+            break
+        assert n_steps <= 12
+    assert [s["steps"] for s in st] == steps.tolist()
+    assert n_steps == steps.max()
 
 
 def test_spec_medusa_stream_is_greedy(gpu, orc):
