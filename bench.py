@@ -285,11 +285,22 @@ def run_tp_medium(a):
     t0 = time.time()
     eng = flb200.Engine(lib, cfg, local, tp=tp)
     eng.synthesize(SEED)
-    prompt = np.random.default_rng(PROMPT_SEED).integers(0, MEDIUM["vocab_size"], a.prompt_len).astype(np.int32)
-    eng.spec_prefill(prompt, a.k)
+    B = max(1, a.batch)
+    rng = np.random.default_rng(PROMPT_SEED)
+    prompts = rng.integers(0, MEDIUM["vocab_size"], (B, a.prompt_len)).astype(np.int32)
+    if B == 1:
+        eng.spec_prefill(prompts[0], a.k)
+        decode = lambda: eng.spec_decode(a.new_tokens)
+    else:
+        # B independent sequences as one in-GPU batch on every rank
+        eng.batch_reserve(B, a.prompt_len + a.new_tokens + a.k + 3)
+        eng.batch_prefill(prompts, a.k)
+        def decode():
+            toks, steps, _ = eng.batch_decode(a.new_tokens)
+            return toks, np.zeros(int(steps.max()), np.int32)
     setup_s = time.time() - t0
     for _ in range(a.warmup):
-        eng.spec_decode(a.new_tokens)
+        decode()
     stream = torch.cuda.ExternalStream(eng.stream(), device=local)
     if dist:
         dist.barrier()
@@ -301,7 +312,7 @@ def run_tp_medium(a):
     e0.record(stream)
     steps_total, launches = 0, 0
     for _ in range(a.steps):
-        toks, acc = eng.spec_decode(a.new_tokens)
+        toks, acc = decode()
         steps_total += len(acc)
         launches += eng.last_launches()
     e1.record(stream)
@@ -314,12 +325,14 @@ def run_tp_medium(a):
         ms = float(t.item())
     if rank == 0:
         line = {
-            "metric": "Phi-3-medium spec-decode tok/s @bs1, tensor parallel", "value": a.steps * a.new_tokens / (ms / 1e3),
+            "metric": f"Phi-3-medium spec-decode tok/s @bs{B}, tensor parallel",
+            "value": B * a.steps * a.new_tokens / (ms / 1e3),
             "unit": "tok/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms / a.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8xs8->s32, f32",
             "data": "synthetic (seeded N(0,0.02) -> Q4_0 -> INT8 weights, uniform prompt ids)",
             "config": {"workload": f"phi3-medium int8 (40L d5120 40/10 heads x128 ffn17920 vocab32064) + 2-layer draft, "
-                                   f"greedy chain k={a.k}, bs1, prompt {a.prompt_len}, {a.new_tokens} new tokens per step",
+                                   f"greedy chain k={a.k}, batch {B}, prompt {a.prompt_len}, "
+                                   f"{a.new_tokens} new tokens per sequence per step",
                        "parallelism": f"tensor parallel x{world} (NCCL all-reduce after o and down)"},
             "spec": {"spec_steps_per_decode": steps_total / a.steps, "step_us": ms * 1e3 / max(1, steps_total)},
             "gpu_launches": int(launches), "clocks": clk, "setup_s": setup_s,
@@ -493,6 +506,7 @@ def main():
     ap.add_argument("--iters", type=int, default=10, help="sweeps for --microbench")
     ap.add_argument("--workload", default="spec-bs1", choices=["spec-bs1", "sampled-batch", "tp-medium", "medusa"])
     ap.add_argument("--seqs", type=int, default=64, help="sequences of --workload sampled-batch")
+    ap.add_argument("--batch", type=int, default=1, help="sequences decoded together by --workload tp-medium")
     a = ap.parse_args()
     if a.microbench:
         return run_microbench(a)

@@ -201,7 +201,7 @@ __global__ void tp_local_best_kernel(const unsigned long long* part, int nparts,
 
 __global__ void tp_reduce_best_kernel(const unsigned long long* all, int size, int stride, int rows,
                                       unsigned long long* out) {
-    const int r = threadIdx.x;
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= rows) return;
     unsigned long long m = 0ull;
     for (int s = 0; s < size; s++) m = all[(size_t)s * stride + r] > m ? all[(size_t)s * stride + r] : m;
@@ -218,7 +218,7 @@ cudaError_t launch_tp_local_best(const unsigned long long* part, int nparts, int
 
 cudaError_t launch_tp_reduce_best(const unsigned long long* all, int size, int stride, int rows,
                                   unsigned long long* out, cudaStream_t s) {
-    tp_reduce_best_kernel<<<1, 32, 0, s>>>(all, size, stride, rows, out);
+    tp_reduce_best_kernel<<<(rows + 127) / 128, 128, 0, s>>>(all, size, stride, rows, out);
     return cudaGetLastError();
 }
 

@@ -18,6 +18,7 @@
 
 #include <algorithm>
 #include <climits>
+#include <functional>
 #include <string>
 #include <vector>
 
@@ -137,9 +138,10 @@ struct fl_engine {
     void* tp_comm = nullptr;
     TpLayout tp = {};
     int Vg = 0;                                // embedding rows (the full vocabulary)
-    unsigned long long* tp_keys = nullptr;     // [kMaxRows] this rank's best LM-head key per row
-    unsigned long long* tp_all = nullptr;      // [tp_size][kMaxRows] gathered
-    unsigned long long* tp_best = nullptr;     // [kMaxRows] the argmax keys the control kernels read
+    int tp_rows = 0;                           // rows of the key buffers (kMaxRows; more for a batch)
+    unsigned long long* tp_keys = nullptr;     // [tp_rows] this rank's best LM-head key per row
+    unsigned long long* tp_all = nullptr;      // [tp_size][tp_rows] gathered
+    unsigned long long* tp_best = nullptr;     // [tp_rows] the argmax keys the control kernels read
     // fused all-reduce over NVLink peer memory for decode-sized passes: the o
     // and down GEMVs store partial rows into every rank's receive slots, a
     // small kernel sums them (tp_reduce_kernel); larger passes use NCCL
@@ -476,13 +478,24 @@ int run_stack(fl_engine* e, Stack& S, float* x, int M, const int* dyn_M, const i
 
 // LM head over rows of x (M <= kMaxRows): logits [M, V] and argmax partials.
 // dyn_src_row (device) selects the first source row of x.
+// Vocabulary-parallel LM head: every rank's best key per row (re-keyed to
+// the global index), all-gathered and reduced into tp_best[0, M).
+int tp_argmax(fl_engine* e, const unsigned long long* part, int M) {
+    if (M > e->tp_rows) return set_error(FL_E_INVAL, "tensor parallel: more LM-head rows than the key buffers hold");
+    FL_CHECK_CUDA(launch_tp_local_best(part, e->nparts, M, e->tp.v0, e->tp_keys, e->s));
+    FL_CHECK(tp_allgather_u64(e->tp_comm, e->tp_keys, e->tp_all, e->tp_rows, e->s));
+    FL_CHECK_CUDA(launch_tp_reduce_best(e->tp_all, e->tp_size, e->tp_rows, M, e->tp_best, e->s));
+    return FL_OK;
+}
+
 int run_lm(fl_engine* e, const float* x, int M, const int* dyn_src_row, const int* done, bool pdl,
            float* logits = nullptr, unsigned long long* amax = nullptr) {
     if (M > kMaxRows || logits) {
         // rows in launches of up to kMaxRows (batched steps), into the given
-        // logits [M, V] and argmax partials [M, nparts]
-        if (e->tp_size > 1 || dyn_src_row || !logits || !amax || (e->d % 128) != 0)
-            return set_error(FL_E_UNSUPPORTED, "LM head: many-row passes need the fused prologue on one GPU");
+        // logits [M, V] and argmax partials [M, nparts]; under tensor
+        // parallelism the keys of the rows end in tp_best[0, M)
+        if (dyn_src_row || !logits || !amax || (e->d % 128) != 0)
+            return set_error(FL_E_UNSUPPORTED, "LM head: many-row passes need the fused RMSNorm prologue");
         GemvParams g = gemv_base(e->lm, e->xq, done);
         g.x = x;
         g.norm = 1;
@@ -495,6 +508,7 @@ int run_lm(fl_engine* e, const float* x, int M, const int* dyn_src_row, const in
             g.M = std::min(kMaxRows, M - r0);
             FL_CHECK_CUDA(launch_gemv_auto(g, EPI_LOGITS, e->s, pdl));
         }
+        if (e->tp_size > 1) FL_CHECK(tp_argmax(e, amax, M));
         return FL_OK;
     }
     GemvParams g = gemv_base(e->lm, e->xq, done);
@@ -523,9 +537,7 @@ int run_lm(fl_engine* e, const float* x, int M, const int* dyn_src_row, const in
     FL_CHECK_CUDA(launch_gemv_auto(g, EPI_LOGITS, e->s, pdl));
     if (e->tp_size > 1) {
         // vocabulary-parallel head: each rank's winner (global index), all-gathered, reduced
-        FL_CHECK_CUDA(launch_tp_local_best(e->amax, e->nparts, M, e->tp.v0, e->tp_keys, e->s));
-        FL_CHECK(tp_allgather_u64(e->tp_comm, e->tp_keys, e->tp_all, kMaxRows, e->s));
-        FL_CHECK_CUDA(launch_tp_reduce_best(e->tp_all, e->tp_size, kMaxRows, M, e->tp_best, e->s));
+        FL_CHECK(tp_argmax(e, e->amax, M));
     }
     return FL_OK;
 }
@@ -965,6 +977,7 @@ static fl_engine_t* engine_create(const fl_model_config_t* cfg, int device, int 
     if (cudaStreamCreateWithFlags(&e->s, cudaStreamNonBlocking) != cudaSuccess) return fail(set_error(FL_E_CUDA, "stream"));
     if (tp_size > 1) {
         if (tp_comm_init(tp_rank, tp_size, tp_id, &e->tp_comm) != FL_OK) return fail(0);
+        e->tp_rows = kMaxRows;
         if (cudaMalloc(&e->tp_keys, sizeof(unsigned long long) * kMaxRows) != cudaSuccess ||
             cudaMalloc(&e->tp_all, sizeof(unsigned long long) * kMaxRows * tp_size) != cudaSuccess ||
             cudaMalloc(&e->tp_best, sizeof(unsigned long long) * kMaxRows) != cudaSuccess)
@@ -1626,8 +1639,8 @@ StepBuffers batch_buffers(fl_engine* e) {
     b.embed = e->embed;
     b.x_d = B.x_dc;
     b.x_v = B.x_v;
-    b.amax_part = B.amax;
-    b.nparts = e->nparts;
+    b.amax_part = e->tp_size > 1 ? e->tp_best : B.amax;  // tensor parallel: the reduced keys
+    b.nparts = amax_nparts(e);
     b.d = e->d;
     b.logits = B.logits;
     b.V = e->V;
@@ -1647,7 +1660,7 @@ StepBuffers batch_buffers(fl_engine* e) {
     b.seq_cap = B.slots;
     b.x_d1 = B.x_d1;
     b.logits_d = B.logits;
-    b.amax_d = B.amax;
+    b.amax_d = b.amax_part;
     b.ctl = B.ctl;
     return b;
 }
@@ -1746,9 +1759,29 @@ cudaError_t copy_rows(void* dst, size_t dpitch, const void* src, size_t spitch, 
 
 FL_API int fl_engine_batch_reserve(fl_engine_t* e, int nseq, int max_ctx) {
     FL_CHECK(check_ready(e, true));
-    if (e->tp_size > 1) return set_error(FL_E_UNSUPPORTED, "batch: a tensor-parallel engine decodes one sequence");
     if (nseq <= 0 || max_ctx < 16 || nseq > 65535) return set_error(FL_E_INVAL, "batch_reserve: bad arguments");
     FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
+    if (e->tp_size > 1 && e->tp_rows < nseq * kMaxRows) {
+        // vocabulary-parallel argmax keys for every LM-head row of a batched
+        // pass (every rank reserves the same batch, so the gathers match)
+        const size_t rows = (size_t)nseq * kMaxRows;
+        cudaFree(e->tp_keys);
+        cudaFree(e->tp_all);
+        cudaFree(e->tp_best);
+        e->tp_keys = e->tp_all = e->tp_best = nullptr;
+        e->tp_rows = 0;
+        e->spec_ready = 0;  // the one-sequence step graph holds the old buffers
+        if (e->step_exec) {
+            cudaGraphExecDestroy(e->step_exec);
+            e->step_exec = nullptr;
+        }
+        e->graph_K = -1;
+        if (cudaMalloc(&e->tp_keys, sizeof(unsigned long long) * rows) != cudaSuccess ||
+            cudaMalloc(&e->tp_all, sizeof(unsigned long long) * rows * e->tp_size) != cudaSuccess ||
+            cudaMalloc(&e->tp_best, sizeof(unsigned long long) * rows) != cudaSuccess)
+            return set_error(FL_E_NOMEM, "batch_reserve: tensor-parallel key buffers");
+        e->tp_rows = (int)rows;
+    }
     const int rc = batch_alloc(e, nseq, max_ctx);
     if (rc != FL_OK) {
         batch_free(e);
@@ -1811,6 +1844,8 @@ FL_API int fl_engine_batch_prefill(fl_engine_t* e, const int* prompts, int P, in
                         B.amax + (size_t)s * e->nparts));
         if (B.samp)
             FL_CHECK_CUDA(launch_sample_first(b, P, e->s, s));
+        else if (e->tp_size > 1)
+            FL_CHECK_CUDA(launch_argmax_rows(e->tp_best, 1, 1, sq + P, nullptr, e->s));
         else
             FL_CHECK_CUDA(launch_argmax_rows(B.amax + (size_t)s * e->nparts, e->nparts, 1, sq + P, nullptr, e->s));
         // draft catch-up over positions 0..P: x_i = F_{i-1} + E[t_i]
@@ -1981,7 +2016,10 @@ FL_API int fl_engine_spec_generate_batch(fl_engine_t* e, const int* prompts, int
     const int slots = P + n_new + K + 3;
     auto& B = e->bt;
     const int rows_cap = std::min(nseq, e->R / (K + 1));
-    if (B.cap < rows_cap || B.slots < slots) {
+    if (e->tp_size > 1 && (B.cap < 1 || B.slots < slots))
+        // every rank must run the same batches: no memory-dependent choice
+        return set_error(FL_E_STATE, "spec_generate_batch: reserve the batch (fl_engine_batch_reserve) on every rank first");
+    if (e->tp_size == 1 && (B.cap < rows_cap || B.slots < slots)) {
         // as many sequences per batch as rows and (80 % of) free memory allow
         // (an existing reservation that holds them all is kept)
         size_t fr = 0, tot = 0;
@@ -2644,6 +2682,173 @@ FL_API int fl_engine_spec_medusa_generate(fl_engine_t* e, const int* prompt, int
 #undef FL_SM
     cleanup();
     if (take_device_error() != 0) return set_error(FL_E_TIMEOUT, "spec_medusa_generate: a bounded device wait gave up");
+    return FL_OK;
+}
+
+// Static draft tree (EAGLE-style): the draft chain c_1..c_K plus, at every
+// depth j, the draft's next w - 1 candidates after c_j, all children of
+// c_{j-1} (c_0 = the newest committed token). Nodes in depth order: root,
+// then per depth [c_j, siblings]; 1 + K w nodes. One tree-masked verify pass,
+// greedy acceptance of the longest path whose tokens match the base argmax at
+// their parents (a sibling ends the path), KV compaction of the path and the
+// draft catch-up over it, as in fl_engine_spec_medusa_generate. Under tensor
+// parallelism each rank's top-w keys (value, global index) are all-gathered
+// and merged, so every rank builds the same tree.
+FL_API int fl_engine_spec_tree_generate(fl_engine_t* e, const int* prompt, int P, int n_new, int K, int width,
+                                        int* out, int* acc_hist, int* steps_out) {
+    FL_CHECK(check_ready(e, true));
+    const int Mt = 1 + K * width;
+    if (!prompt || !out || P <= 0 || n_new <= 0 || K < 1 || K > kMaxDraft || width < 1 || width > 32 ||
+        Mt > 256 || P + n_new + Mt + K + 2 > e->R)
+        return set_error(FL_E_INVAL, "spec_tree_generate: bad arguments or context too long");
+    const int d = e->d, G = e->tp_size;
+    cudaStream_t s = e->s;
+    int *mtok = nullptr, *mpos = nullptr, *mtarget = nullptr, *mpath = nullptr, *mchain = nullptr, *mcat = nullptr;
+    unsigned long long *mkeys = nullptr, *mall = nullptr;
+    KvLayer* dkv = nullptr;
+    auto cleanup = [&]() {
+        void* bufs[] = {mtok, mpos, mtarget, mpath, mchain, mcat, mkeys, mall, dkv};
+        for (void* p : bufs) cudaFree(p);
+    };
+    auto fail = [&](int rc) {
+        cleanup();
+        return rc;
+    };
+#define FL_ST_CUDA(expr)                                                     \
+    do {                                                                     \
+        cudaError_t fl_e_ = (expr);                                          \
+        if (fl_e_ != cudaSuccess) return fail(cuda_error(fl_e_, #expr));     \
+    } while (0)
+#define FL_ST(expr)                       \
+    do {                                  \
+        int fl_r_ = (expr);               \
+        if (fl_r_ != FL_OK) return fail(fl_r_); \
+    } while (0)
+    FL_ST_CUDA(cudaMalloc(&mtok, sizeof(int) * Mt));
+    FL_ST_CUDA(cudaMalloc(&mpos, sizeof(int) * Mt));
+    FL_ST_CUDA(cudaMalloc(&mtarget, sizeof(int) * Mt));
+    FL_ST_CUDA(cudaMalloc(&mpath, sizeof(int) * Mt));
+    FL_ST_CUDA(cudaMalloc(&mchain, sizeof(int) * kMaxRows));
+    FL_ST_CUDA(cudaMalloc(&mcat, sizeof(int) * Mt));
+    FL_ST_CUDA(cudaMalloc(&mkeys, sizeof(unsigned long long) * K * width));
+    FL_ST_CUDA(cudaMalloc(&mall, sizeof(unsigned long long) * K * width * G));
+    FL_ST_CUDA(cudaMalloc(&dkv, sizeof(KvLayer) * e->base.nl));
+    FL_ST_CUDA(cudaMemcpyAsync(dkv, e->base.kv.data(), sizeof(KvLayer) * e->base.nl, cudaMemcpyHostToDevice, s));
+    FL_ST(ensure_mask(e, Mt));
+
+    // prefill: base KV 0 .. P-1 and the first token; draft catch-up over 0 .. P
+    FL_ST(prefill_base(e, prompt, P));
+    FL_ST_CUDA(launch_embed_rows(e->embed, e->Vg, e->seq, e->x, 1, e->x2, d, P + 1, nullptr, nullptr, s, false));
+    FL_ST(run_stack(e, e->draft, e->x2, P + 1, nullptr, e->iota, e->iota, nullptr, nullptr, false));
+    FL_ST_CUDA(cudaMemcpyAsync(e->x_d, e->x2 + (size_t)P * d, sizeof(float) * d, cudaMemcpyDeviceToDevice, s));
+    int cur_tok = 0;
+    FL_ST_CUDA(cudaMemcpyAsync(&cur_tok, e->seq + P, sizeof(int), cudaMemcpyDeviceToHost, s));
+    FL_ST_CUDA(cudaStreamSynchronize(s));
+    int produced = 0, steps = 0, n = P;
+    out[produced++] = cur_tok;
+    std::vector<unsigned long long> keys((size_t)K * width * G);
+    std::vector<int> ntok(Mt), npar(Mt), ndep(Mt), hpos(Mt), target(Mt), path, cat;
+    std::vector<uint8_t> mask((size_t)Mt * Mt);
+    // static tree shape: parents, depths and the ancestor mask
+    npar[0] = -1;
+    ndep[0] = 0;
+    for (int j = 1; j <= K; j++)
+        for (int c2 = 0; c2 < width; c2++) {
+            const int i = 1 + (j - 1) * width + c2;
+            npar[i] = j == 1 ? 0 : 1 + (j - 2) * width;
+            ndep[i] = j;
+        }
+    for (int i = 0; i < Mt; i++) {
+        for (int j = 0; j < Mt; j++) mask[(size_t)i * Mt + j] = 0;
+        for (int j = i; j >= 0; j = npar[j]) mask[(size_t)i * Mt + j] = 1;
+    }
+    FL_ST_CUDA(cudaMemcpyAsync(e->mask, mask.data(), (size_t)Mt * Mt, cudaMemcpyHostToDevice, s));
+    FL_ST_CUDA(cudaEventRecord(e->ev[0], s));
+    while (produced < n_new) {
+        // draft chain from the draft state at position n (x_d row 0); each
+        // depth's top-w keys
+        for (int j = 0; j < K; j++) {
+            if (j > 0) {
+                FL_ST_CUDA(launch_embed_rows(e->embed, e->Vg, mchain + j - 1, e->x_d, 0, e->x_d, d, 1, nullptr, nullptr, s,
+                                             false));
+                FL_ST(run_stack(e, e->draft, e->x_d, 1, nullptr, e->iota + n + j, e->iota + n + j, nullptr, nullptr,
+                                false));
+            }
+            FL_ST(run_lm(e, e->x_d, 1, nullptr, nullptr, false));
+            FL_ST_CUDA(launch_argmax_rows(amax_keys(e), amax_nparts(e), 1, mchain + j, nullptr, s));
+            FL_ST_CUDA(launch_topk_keys(e->logits, 1, e->V, e->V, G > 1 ? e->tp.v0 : 0, width,
+                                        mkeys + (size_t)j * width, s));
+        }
+        if (G > 1) FL_ST(tp_allgather_u64(e->tp_comm, mkeys, mall, (size_t)K * width, s));
+        FL_ST_CUDA(cudaMemcpyAsync(keys.data(), G > 1 ? mall : mkeys, sizeof(unsigned long long) * keys.size(),
+                                   cudaMemcpyDeviceToHost, s));
+        FL_ST_CUDA(cudaStreamSynchronize(s));
+        ntok[0] = cur_tok;
+        for (int j = 0; j < K; j++) {
+            // merge the ranks' candidates of depth j + 1: the w largest keys
+            std::vector<unsigned long long> cand;
+            for (int r = 0; r < G; r++)
+                for (int c2 = 0; c2 < width; c2++) cand.push_back(keys[((size_t)r * K + j) * width + c2]);
+            std::sort(cand.begin(), cand.end(), std::greater<unsigned long long>());
+            for (int c2 = 0; c2 < width; c2++)
+                ntok[1 + j * width + c2] = 0x7fffffff - (int)(uint32_t)(cand[c2] & 0xffffffffu);
+        }
+        for (int i = 0; i < Mt; i++) hpos[i] = n + ndep[i];
+        FL_ST_CUDA(cudaMemcpyAsync(mtok, ntok.data(), sizeof(int) * Mt, cudaMemcpyHostToDevice, s));
+        FL_ST_CUDA(cudaMemcpyAsync(mpos, hpos.data(), sizeof(int) * Mt, cudaMemcpyHostToDevice, s));
+        FL_ST_CUDA(launch_embed_rows(e->embed, e->Vg, mtok, nullptr, 0, e->x, d, Mt, nullptr, nullptr, s, false));
+        FL_ST(run_stack(e, e->base, e->x, Mt, nullptr, e->iota + n, mpos, e->mask, nullptr, false));
+        for (int r0 = 0; r0 < Mt; r0 += kMaxRows) {
+            const int m = std::min(kMaxRows, Mt - r0);
+            FL_ST(run_lm(e, e->x + (size_t)r0 * d, m, nullptr, nullptr, false));
+            FL_ST_CUDA(launch_argmax_rows(amax_keys(e), amax_nparts(e), m, mtarget + r0, nullptr, s));
+        }
+        FL_ST_CUDA(cudaMemcpyAsync(target.data(), mtarget, sizeof(int) * Mt, cudaMemcpyDeviceToHost, s));
+        FL_ST_CUDA(cudaStreamSynchronize(s));
+        path.assign(1, 0);
+        int cur = 0;
+        for (;;) {
+            int nxt = -1;
+            for (int c2 = 1; c2 < Mt; c2++)
+                if (npar[c2] == cur && ntok[c2] == target[cur]) {
+                    nxt = c2;
+                    break;
+                }
+            if (nxt < 0) break;
+            path.push_back(nxt);
+            cur = nxt;
+        }
+        const int a = (int)path.size() - 1;
+        if (acc_hist) acc_hist[steps] = a;
+        steps++;
+        for (int j = 1; j <= a + 1 && produced < n_new; j++) out[produced++] = j <= a ? ntok[path[j]] : target[cur];
+        // draft catch-up over positions n+1 .. n+a+1: F of the path's tree rows + E[token]
+        cat.resize(a + 1);
+        for (int j = 0; j <= a; j++) cat[j] = j < a ? ntok[path[j + 1]] : target[cur];
+        FL_ST_CUDA(cudaMemcpyAsync(mcat, cat.data(), sizeof(int) * (a + 1), cudaMemcpyHostToDevice, s));
+        for (int j = 0; j <= a; j++)
+            FL_ST_CUDA(cudaMemcpyAsync(e->x2 + (size_t)j * d, e->x + (size_t)path[j] * d, sizeof(float) * d,
+                                       cudaMemcpyDeviceToDevice, s));
+        if (a > 0) {
+            FL_ST_CUDA(cudaMemcpyAsync(mpath, path.data(), sizeof(int) * (a + 1), cudaMemcpyHostToDevice, s));
+            FL_ST_CUDA(launch_kv_compact(dkv, e->base.nl, e->base.block_table, e->Hkv, e->hd, e->iota + n, mpath, a, s));
+        }
+        FL_ST_CUDA(launch_embed_rows(e->embed, e->Vg, mcat, e->x2, 0, e->x2, d, a + 1, nullptr, nullptr, s, false));
+        FL_ST(run_stack(e, e->draft, e->x2, a + 1, nullptr, e->iota + n + 1, e->iota + n + 1, nullptr, nullptr, false));
+        FL_ST_CUDA(cudaMemcpyAsync(e->x_d, e->x2 + (size_t)a * d, sizeof(float) * d, cudaMemcpyDeviceToDevice, s));
+        cur_tok = target[cur];
+        n += a + 1;
+    }
+    FL_ST_CUDA(cudaEventRecord(e->ev[1], s));
+    FL_ST_CUDA(cudaEventSynchronize(e->ev[1]));
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, e->ev[0], e->ev[1]);
+    e->t_total_us = ms * 1000.0;
+    if (steps_out) *steps_out = steps;
+#undef FL_ST_CUDA
+#undef FL_ST
+    cleanup();
+    if (take_device_error() != 0) return set_error(FL_E_TIMEOUT, "spec_tree_generate: a bounded device wait gave up");
     return FL_OK;
 }
 

@@ -186,6 +186,9 @@ cudaError_t launch_medusa_z(const float* x, const float* y, float* h, float* z, 
                             cudaStream_t s);
 cudaError_t launch_topk_rows(const float* logits, int rows, int V, int ld, const int* k, int kmax, int* tok,
                              float* prob, cudaStream_t s);
+// Top-w argmax keys of each row with global indices v0 + i (w <= 32).
+cudaError_t launch_topk_keys(const float* logits, int rows, int V, int ld, int v0, int w, unsigned long long* out,
+                             cudaStream_t s);
 cudaError_t launch_kv_compact(const KvLayer* layers, int n_layers, const int* block_table, int kv_heads, int head_dim,
                               const int* base, const int* src, int a, cudaStream_t s);
 

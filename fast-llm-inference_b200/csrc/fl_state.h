@@ -160,7 +160,7 @@ cudaError_t launch_accept_sampled(const StepBuffers& b, int K, cudaStream_t s, b
 
 // Tensor parallelism (decode_ops.cu): per-row best key of this rank's LM-head
 // partials with global indices; per-row maximum of the gathered keys
-// [size][stride] (rows <= 32).
+// [size][stride].
 cudaError_t launch_tp_local_best(const unsigned long long* part, int nparts, int rows, int v0, unsigned long long* out,
                                  cudaStream_t s);
 cudaError_t launch_tp_reduce_best(const unsigned long long* all, int size, int stride, int rows,

@@ -55,7 +55,10 @@ __device__ int g_gemm_error = 0;
 
 constexpr int kProdW = 4, kMma = 4, kRd0 = 5;
 // readout warps per TMEM lane quadrant (8 columns each at least), threads
-__host__ __device__ constexpr int rd_per_quad(int bn) { return bn >= 32 ? 4 : 2; }
+#ifndef FL_GEMM_COLS
+#define FL_GEMM_COLS 8
+#endif
+__host__ __device__ constexpr int rd_per_quad(int bn) { return bn / FL_GEMM_COLS > 1 ? bn / FL_GEMM_COLS : 1; }
 __host__ __device__ constexpr int gemm_threads(int bn) { return (kRd0 + 4 * rd_per_quad(bn)) * 32; }
 constexpr int kProdT = kProdW * 32;
 constexpr int kInFlight = 6;  // weight stages in flight per producer thread
@@ -169,6 +172,34 @@ __device__ __forceinline__ void tmem_ld8(uint32_t ta, uint32_t* v) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                  : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
                  : "r"(ta));
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t ta, uint32_t* v) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(ta));
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t ta, uint32_t* v) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(ta));
+}
+// The readout's load of `n` consecutive columns (n = 8, 16 or 32).
+template <int n>
+__device__ __forceinline__ void tmem_ld(uint32_t ta, uint32_t* v) {
+    if constexpr (n >= 32) {
+        tmem_ld32(ta, v);
+    } else if constexpr (n >= 16) {
+        tmem_ld16(ta, v);
+    } else {
+        tmem_ld8(ta, v);
+    }
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
@@ -318,6 +349,7 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
             return __ldg(reinterpret_cast<const uint2*>(g.sblk + tiled_s_off(N, geo.P, n, kg * 4)));
         };
         constexpr int kV = 2 * kCols;  // registers per half stage (two blocks)
+        constexpr int kLdW = kCols >= 32 ? 32 : (kCols >= 16 ? 16 : 8);  // columns per TMEM load
         uint32_t va[kV], vb[kV];
         // half stage h: blocks 2 (h & 1), 2 (h & 1) + 1 of stage h / 2
         auto ld_half = [&](int h, uint32_t* v) {
@@ -325,7 +357,7 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
 #pragma unroll
             for (int j = 0; j < 2; j++)
 #pragma unroll
-                for (int c = 0; c < kCols; c += 8) tmem_ld8(base + (uint32_t)(j * BN + c), v + j * kCols + c);
+                for (int c = 0; c < kCols; c += kLdW) tmem_ld<kLdW>(base + (uint32_t)(j * BN + c), v + j * kCols + c);
         };
         auto scale_add = [&](const uint32_t* v, float d) {
             const float nmd = __fmul_rn(-kMagic, d);  // exact: 3 * 2^22 * d

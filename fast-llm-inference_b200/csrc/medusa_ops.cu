@@ -98,6 +98,42 @@ __global__ void topk_rows_kernel(const float* logits, int V, int ld, const int* 
     }
 }
 
+// Top-w keys (value, global index v0 + i; argmax_key order: larger value
+// first, lower index on ties) of rows logits[row * ld ..] of V entries; best
+// first into out[row * w ..]. One CTA per row.
+__global__ void topk_keys_kernel(const float* logits, int V, int ld, int v0, int w, unsigned long long* out) {
+    __shared__ unsigned long long redk[kNT / 32];
+    __shared__ int taken[32];
+    const int row = blockIdx.x;
+    const float* lg = logits + (size_t)row * ld;
+    for (int j = 0; j < w; j++) {
+        unsigned long long best = 0ull;
+        for (int i = threadIdx.x; i < V; i += blockDim.x) {
+            bool used = false;
+            for (int q = 0; q < j; q++) used |= taken[q] == i;
+            if (!used) {
+                const unsigned long long key = argmax_key(lg[i], v0 + i);
+                best = key > best ? key : best;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long o2 = __shfl_xor_sync(0xffffffffu, best, o);
+            best = o2 > best ? o2 : best;
+        }
+        __syncthreads();
+        if ((threadIdx.x & 31) == 0) redk[threadIdx.x >> 5] = best;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            unsigned long long b = redk[0];
+            for (int q = 1; q < (int)(blockDim.x >> 5); q++) b = redk[q] > b ? redk[q] : b;
+            taken[j] = argmax_key_index(b) - v0;
+            out[(size_t)row * w + j] = b;
+        }
+        __syncthreads();
+    }
+}
+
 // Accepted path compaction: for j = 1 .. a in order, slot base + j takes the
 // K / V of slot base + src[j] (src[j] >= j, src increasing, so an earlier move
 // never overwrites a later source). CTA = (layer, stack of kv heads).
@@ -135,6 +171,13 @@ cudaError_t launch_topk_rows(const float* logits, int rows, int V, int ld, const
                              float* prob, cudaStream_t s) {
     if (kmax > 32) return cudaErrorInvalidValue;
     topk_rows_kernel<<<rows, kNT, 0, s>>>(logits, V, ld, k, kmax, tok, prob);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_topk_keys(const float* logits, int rows, int V, int ld, int v0, int w, unsigned long long* out,
+                             cudaStream_t s) {
+    if (w < 1 || w > 32 || w > V) return cudaErrorInvalidValue;
+    topk_keys_kernel<<<rows, kNT, 0, s>>>(logits, V, ld, v0, w, out);
     return cudaGetLastError();
 }
 

@@ -155,6 +155,7 @@ _SIGS = {
     "fl_engine_step_trace_stages": (I, [VP, VP]),
     "fl_engine_medusa_generate": (I, [VP, VP, I, I, VP, I, I, VP, VP, VP]),
     "fl_engine_spec_medusa_generate": (I, [VP, VP, I, I, I, VP, I, I, VP, VP, VP]),
+    "fl_engine_spec_tree_generate": (I, [VP, VP, I, I, I, I, VP, VP, VP]),
     "fl_engine_medusa_tree": (I, [VP, VP, I, VP, I, I, VP, VP, VP, VP]),
     "fl_engine_tree_verify": (I, [VP, VP, VP, VP, I, VP, VP]),
     "fl_engine_bind_medusa": (I, [VP, VP]),
@@ -528,6 +529,17 @@ class Engine:
         self.lib.check(self.lib.fl_engine_spec_medusa_generate(self.h, ptr(p), len(p), n_new, k, ptr(tk), len(tk),
                                                                max_nodes, ptr(o), ptr(acc), C.byref(steps)),
                        "spec_medusa_generate")
+        return o, acc[: steps.value]
+
+    def spec_tree_generate(self, prompt, n_new, k, width):
+        """Static draft tree (chain + top-width per depth), greedy:
+        (tokens, accepted count per step)."""
+        p = np.ascontiguousarray(prompt, np.int32)
+        o = np.empty(n_new, np.int32)
+        acc = np.zeros(n_new + 1, np.int32)
+        steps = C.c_int(0)
+        self.lib.check(self.lib.fl_engine_spec_tree_generate(self.h, ptr(p), len(p), n_new, k, width, ptr(o), ptr(acc),
+                                                             C.byref(steps)), "spec_tree_generate")
         return o, acc[: steps.value]
 
     def step_trace_stages(self):

@@ -360,6 +360,21 @@ int fl_engine_spec_medusa_generate(fl_engine_t* e, const int* prompt, int prompt
                                    const int* topk, int n_heads, int max_nodes, int* out, int* acc_hist,
                                    int* steps);
 
+/* Static draft tree (EAGLE-style), greedy: each step the draft drafts a
+ * chain of k tokens and, at every depth j, its next width - 1 candidates
+ * after the chain token (children of the chain token of depth j - 1); the
+ * 1 + k * width nodes are verified in one tree-masked base pass (passes of
+ * more than 16 rows through the tcgen05 GEMM), the longest path of the base
+ * model's greedy choices is accepted, its base KV compacted and the draft
+ * catches up over it. On a tensor-parallel engine every rank's top-width
+ * candidates (value, global index) are gathered and merged, so all ranks
+ * build the same tree; the output is the base model's greedy stream.
+ * Needs 1 + k * width <= 256 and prompt_len + n_new + 1 + k * width + k + 2
+ * <= max_seq_len. out[n_new]; acc_hist[steps] accepted per step (may be
+ * NULL); *steps (may be NULL). */
+int fl_engine_spec_tree_generate(fl_engine_t* e, const int* prompt, int prompt_len, int n_new, int k, int width,
+                                 int* out, int* acc_hist, int* steps);
+
 /* Step-level Medusa pieces (medusa_predict / medusa_build_tree /
  * medusa_verify_tree / medusa_decode_step run on these).
  * fl_engine_medusa_tree: the heads' candidate tree from a base feature F

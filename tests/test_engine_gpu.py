@@ -599,6 +599,33 @@ def test_spec_medusa_stream_is_greedy(gpu, orc):
     eng.close()
 
 
+@pytest.mark.parametrize("k,width", [(4, 8), (3, 4), (2, 1)])
+def test_spec_tree_stream_is_greedy(gpu, orc, small, k, width):
+    """Static draft tree (chain + top-width per depth; 33 nodes at k = 4,
+    width = 8, verified through the tcgen05 GEMM): the output is the base
+    model's greedy stream, on the small models and on a 16-token vocabulary
+    where paths through siblings are accepted often (KV compaction)."""
+    dims, eng, om, embed = small
+    p = prompt(12, 16, dims["vocab"])
+    got, acc = eng.spec_tree_generate(p, 40, k, width)
+    want, margins = om.greedy(p, 40)
+    assert_stream_matches(got, want, margins)
+    dims16 = dict(SMALL, vocab=16)
+    w, emb = make_weights(gpu, dims16, seed=5, draft_layers=1)
+    e16 = flb200.Engine(gpu, engine_cfg(dims16, draft_layers=1, max_seq_len=256))
+    load_engine(e16, w, emb)
+    p16 = prompt(13, 12, 16)
+    got, acc = e16.spec_tree_generate(p16, 60, k, width)
+    om16 = oracle_model(orc, dims16, w, emb, draft_layers=1)
+    want, margins = om16.greedy(p16, 60)
+    assert_stream_matches(got, want, margins)
+    chain, cacc = e16.spec_generate(p16, 60, k)
+    assert_stream_matches(chain, want, margins)
+    if width > 1:
+        assert acc.max() >= 2, acc.tolist()
+    e16.close()
+
+
 def test_medusa_step_api_matches_generate(gpu, orc):
     """The reference's step-level Medusa API on the engine's callback position
     (prefill with fl_cuda_base_forward, then medusa_decode_step /

@@ -50,10 +50,21 @@ def _rank(rank, size, uid, q):
         p = prompt(8, 16, TP_GQA["vocab"])
         toks, acc = eng.spec_generate(p, 24, 4)
         g = eng.greedy(p, 12)
+        # three sequences as one in-GPU batch (15 verify rows: NCCL sums;
+        # 3-row draft passes: the fused NVLink push)
+        eng.batch_reserve(3, 12 + 24 + 4 + 3)
+        eng.batch_prefill(_batch_prompts(prompt), 4)
+        bt, _, _ = eng.batch_decode(24)
+        # a 17-node draft tree (k = 4, width 4): merged top-4 across the ranks
+        tt, _ = eng.spec_tree_generate(p, 24, 4, 4)
         eng.close()
-        q.put((rank, toks.tolist(), acc.tolist(), g.tolist(), None))
+        q.put((rank, toks.tolist(), acc.tolist(), g.tolist(), bt.tolist(), tt.tolist(), None))
     except Exception as ex:  # reported to the parent
-        q.put((rank, None, None, None, repr(ex)))
+        q.put((rank, None, None, None, None, None, repr(ex)))
+
+
+def _batch_prompts(prompt):
+    return np.stack([prompt(70 + i, 12, TP_GQA["vocab"]) for i in range(3)])
 
 
 @pytest.mark.gpu
@@ -72,20 +83,28 @@ def test_two_rank_decode_matches_oracle(gpu, orc):
         p.start()
     res = {}
     for _ in range(2):
-        r, toks, acc, g, err = q.get(timeout=600)
+        r, toks, acc, g, bt, tt, err = q.get(timeout=600)
         assert err is None, f"rank {r}: {err}"
-        res[r] = (np.array(toks), np.array(acc), np.array(g))
+        res[r] = (np.array(toks), np.array(acc), np.array(g), np.array(bt), np.array(tt))
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
     assert np.array_equal(res[0][0], res[1][0]) and np.array_equal(res[0][2], res[1][2]), "ranks disagree"
+    assert np.array_equal(res[0][3], res[1][3]), "ranks disagree on the batch"
+    assert np.array_equal(res[0][4], res[1][4]), "ranks disagree on the tree decode"
     w, embed = make_weights(gpu, TP_GQA, seed=41)
     om = bind.OracleModel(orc, TP_GQA, embed, w, draft_layers=1)
     p = prompt(8, 16, TP_GQA["vocab"])
     want, _, margins = om.spec(p, 24, 4)
+    td = np.nonzero(res[0][4] != want)[0]
+    assert td.size == 0 or margins[td[0]] < 1e-2, f"tree decode diverges at {td[:1]}"
     got = res[0][0]
     diff = np.nonzero(got != want)[0]
     assert diff.size == 0 or margins[diff[0]] < 1e-2, f"diverges at {diff[:1]} (margin {margins[diff[0]]:.3g})"
     gw, gm = om.greedy(p, 12)
     gd = np.nonzero(res[0][2] != gw)[0]
     assert gd.size == 0 or gm[gd[0]] < 1e-2
+    for i, pb in enumerate(_batch_prompts(prompt)):
+        bw, bm = om.greedy(pb, 24)
+        bd = np.nonzero(res[0][3][i] != bw)[0]
+        assert bd.size == 0 or bm[bd[0]] < 1e-2, f"batch sequence {i} diverges at {bd[:1]}"
