@@ -288,7 +288,17 @@ def run_tp_medium(a):
     B = max(1, a.batch)
     rng = np.random.default_rng(PROMPT_SEED)
     prompts = rng.integers(0, MEDIUM["vocab_size"], (B, a.prompt_len)).astype(np.int32)
-    if B == 1:
+    tree_us = []
+    if a.tree > 0:
+        # static draft tree of 1 + k * width nodes (prefill inside each call,
+        # outside its device timing)
+        if B != 1:
+            raise SystemExit("--tree decodes one sequence (--batch 1)")
+        def decode():
+            toks, acc = eng.spec_tree_generate(prompts[0], a.new_tokens, a.k, a.tree)
+            tree_us.append(eng.last_timing()[2])
+            return toks, acc
+    elif B == 1:
         eng.spec_prefill(prompts[0], a.k)
         decode = lambda: eng.spec_decode(a.new_tokens)
     else:
@@ -319,6 +329,8 @@ def run_tp_medium(a):
     torch.cuda.synchronize()
     clk = clocks.stop()
     ms = e0.elapsed_time(e1)
+    if a.tree > 0:
+        ms = sum(tree_us[-a.steps:]) / 1e3  # the decode loops alone (prefills excluded)
     if dist:
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -331,7 +343,9 @@ def run_tp_medium(a):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8xs8->s32, f32",
             "data": "synthetic (seeded N(0,0.02) -> Q4_0 -> INT8 weights, uniform prompt ids)",
             "config": {"workload": f"phi3-medium int8 (40L d5120 40/10 heads x128 ffn17920 vocab32064) + 2-layer draft, "
-                                   f"greedy chain k={a.k}, batch {B}, prompt {a.prompt_len}, "
+                                   + (f"greedy draft tree k={a.k} x width {a.tree} ({1 + a.k * a.tree} nodes)"
+                                      if a.tree > 0 else f"greedy chain k={a.k}")
+                                   + f", batch {B}, prompt {a.prompt_len}, "
                                    f"{a.new_tokens} new tokens per sequence per step",
                        "parallelism": f"tensor parallel x{world} (NCCL all-reduce after o and down)"},
             "spec": {"spec_steps_per_decode": steps_total / a.steps, "step_us": ms * 1e3 / max(1, steps_total)},
@@ -507,6 +521,7 @@ def main():
     ap.add_argument("--workload", default="spec-bs1", choices=["spec-bs1", "sampled-batch", "tp-medium", "medusa"])
     ap.add_argument("--seqs", type=int, default=64, help="sequences of --workload sampled-batch")
     ap.add_argument("--batch", type=int, default=1, help="sequences decoded together by --workload tp-medium")
+    ap.add_argument("--tree", type=int, default=0, help="draft-tree width for --workload tp-medium (0: chain)")
     a = ap.parse_args()
     if a.microbench:
         return run_microbench(a)
