@@ -24,12 +24,13 @@
 //    hands its TMEM buffer (4 BN columns, one of 512 / (4 BN)) to the
 //    readout. Commits are slow enough (about half a microsecond apiece here)
 //    that one per block was the kernel's bottleneck.
-//  - warps 5 ..: readout, four per TMEM lane quadrant (two when BN = 16),
-//    each with 8 columns of its quadrant's 32 lanes. Per half stage (two
-//    blocks) it loads the s32 dots, releases a stage's TMEM buffer once both
-//    halves are in registers and, while the next half's load is in flight,
-//    turns each dot into the float
-//    12582912 + dot by an integer add of 0x4B400000 (exact: |dot| < 2^22).
+//  - warps 5 ..: readout, BN / 16 per TMEM lane quadrant, each with 16
+//    columns of its quadrant's 32 lanes (one 32x32b.x16 load per block: 3-8 %
+//    faster than 8-column warps, while 32-column warps are slower). Per half
+//    stage (two blocks) it loads the s32 dots, releases a stage's TMEM buffer
+//    once both halves are in registers and, while the next half's load is in
+//    flight, turns each dot into the float 12582912 + dot by an integer add
+//    of 0x4B400000 (exact: |dot| < 2^22).
 //    One fma with d and -12582912 d (exact) then yields exactly the rounded
 //    product (float)dot * d, which is added to the row's running sum in block
 //    order: the sum is bit-identical to the sequential reference order. Pairs
@@ -56,7 +57,7 @@ __device__ int g_gemm_error = 0;
 constexpr int kProdW = 4, kMma = 4, kRd0 = 5;
 // readout warps per TMEM lane quadrant (8 columns each at least), threads
 #ifndef FL_GEMM_COLS
-#define FL_GEMM_COLS 8
+#define FL_GEMM_COLS 16
 #endif
 __host__ __device__ constexpr int rd_per_quad(int bn) { return bn / FL_GEMM_COLS > 1 ? bn / FL_GEMM_COLS : 1; }
 __host__ __device__ constexpr int gemm_threads(int bn) { return (kRd0 + 4 * rd_per_quad(bn)) * 32; }
