@@ -118,14 +118,35 @@ __global__ void __launch_bounds__(kAThreads) attention_kernel(const AttnParams p
     for (int j0 = 0; j0 < ctx; j0 += kTile) {
         const int nt = min(kTile, ctx - j0);
         __syncthreads();  // previous tile fully consumed
-        // K and V tile: half2 words, consecutive threads -> consecutive words
-        for (int i = threadIdx.x; i < nt * hd2; i += kAThreads) {
-            const int key = i / hd2, c = i - key * hd2;
-            const int slot = j0 + key;
-            const int page = btab[slot / kPageSize];
-            const size_t off = (((size_t)page * p.kv_heads + kvh) * kPageSize + (slot % kPageSize)) * hd2 + c;
-            Ks[key * kstride + c] = reinterpret_cast<const uint32_t*>(p.kv.k)[off];
-            Vs[key * hd2 + c] = reinterpret_cast<const uint32_t*>(p.kv.v)[off];
+        // K and V tile, consecutive threads -> consecutive words: 16-byte
+        // loads (four half2 words), several in flight per thread, when a key
+        // row is a whole number of them; else one word at a time
+        if ((hd2 & 3) == 0) {
+            const int hd8 = hd2 >> 2;
+#pragma unroll 4
+            for (int i = threadIdx.x; i < nt * hd8; i += kAThreads) {
+                const int key = i / hd8, c = (i - key * hd8) * 4;
+                const int slot = j0 + key;
+                const int page = btab[slot / kPageSize];
+                const size_t off = (((size_t)page * p.kv_heads + kvh) * kPageSize + (slot % kPageSize)) * hd2 + c;
+                const uint4 k4 = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint32_t*>(p.kv.k) + off);
+                const uint4 v4 = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint32_t*>(p.kv.v) + off);
+                uint32_t* kd = Ks + key * kstride + c;
+                kd[0] = k4.x;
+                kd[1] = k4.y;
+                kd[2] = k4.z;
+                kd[3] = k4.w;
+                *reinterpret_cast<uint4*>(Vs + key * hd2 + c) = v4;
+            }
+        } else {
+            for (int i = threadIdx.x; i < nt * hd2; i += kAThreads) {
+                const int key = i / hd2, c = i - key * hd2;
+                const int slot = j0 + key;
+                const int page = btab[slot / kPageSize];
+                const size_t off = (((size_t)page * p.kv_heads + kvh) * kPageSize + (slot % kPageSize)) * hd2 + c;
+                Ks[key * kstride + c] = reinterpret_cast<const uint32_t*>(p.kv.k)[off];
+                Vs[key * hd2 + c] = reinterpret_cast<const uint32_t*>(p.kv.v)[off];
+            }
         }
         __syncthreads();
         // scores: one key per thread (kTile <= kAThreads)
