@@ -6,17 +6,22 @@
 //   C[m, n] = (sum over blocks b, in order, of (float)dot_b(m, n) * d[n, b]) / 127
 // with dot_b the exact int32 dot of 32 u8 activations and 32 s8 weights.
 //
-// One CTA computes a tile of 128 weight rows x BN (16 or 32) activation rows.
-//  - warps 0-3: producers. Per 128-byte K-group they copy the weight tile
-//    (128 rows x 128 B) with coalesced 16-byte cp.async (eight lanes per row;
-//    the tiled weight layout already stores each 128-byte group XOR-swizzled
-//    by row & 7, which is the 128-byte swizzle pattern the MMA descriptor
-//    expects, so the bytes move verbatim), and thread 0 loads the activation
-//    tile (BN rows x 128 B) by TMA with SWIZZLE_128B. Rows of the weight tile
-//    are separate 128-byte pieces of memory, which a TMA box would fetch one
-//    request at a time; the load/store unit keeps them in flight together.
-//    A stage is published (async-proxy fence, then mbarrier arrival) once
-//    its copies complete, six stages behind the newest.
+// A tile is 128 weight rows x BN (16 or 32) activation rows. The kernel is
+// persistent: one CTA per SM walks the tiles blockIdx.x, + gridDim.x, ...
+// (activation tiles fastest, so concurrent CTAs share weight tiles in L2),
+// and its stage counters run on across tiles, so the next tile's copies and
+// MMAs overlap this tile's readout and epilogue (per-tile CTAs spent about
+// 6 us per tile on start-up and drain).
+//  - warps 0-3: producers. Per 128-byte K-group thread 0 copies the weight
+//    tile (128 rows x 128 B; the tiled weight layout already stores each
+//    128-byte group XOR-swizzled by row & 7, which is the 128-byte swizzle
+//    pattern the MMA descriptor expects, so the bytes move verbatim) and the
+//    activation tile (BN rows x 128 B, SWIZZLE_128B) by TMA. Rows from
+//    FL_GEMM_TMA_ROWS on (128 by default: none) are copied instead with
+//    coalesced 16-byte cp.async by all producer threads, eight lanes per row;
+//    the full-tile TMA measured 2-3 % faster. A stage is published
+//    (async-proxy fence, then mbarrier arrival) once its copies complete, six
+//    stages behind the newest.
 //  - warp 4: allocates all 512 TMEM columns, then issues one
 //    tcgen05.mma.cta_group::1.kind::i8 (M = 128, N = BN, K = 32) per 32-element
 //    block into its own BN TMEM columns, and one tcgen05.commit per stage
@@ -63,7 +68,10 @@ __host__ __device__ constexpr int rd_per_quad(int bn) { return bn / FL_GEMM_COLS
 __host__ __device__ constexpr int gemm_threads(int bn) { return (kRd0 + 4 * rd_per_quad(bn)) * 32; }
 constexpr int kProdT = kProdW * 32;
 constexpr int kInFlight = 6;  // weight stages in flight per producer thread
-constexpr int kTmaRows = 64;  // weight-tile rows fetched by TMA (the rest by cp.async)
+#ifndef FL_GEMM_TMA_ROWS
+#define FL_GEMM_TMA_ROWS 128
+#endif
+constexpr int kTmaRows = FL_GEMM_TMA_ROWS;  // weight-tile rows fetched by TMA (the rest by cp.async)
 constexpr int kTileN = 128;                 // weight rows per tile (UMMA M)
 constexpr int kGroup = 128;                 // K bytes per stage (four 32-element blocks)
 constexpr int kABytes = kTileN * kGroup;    // 16 KB
@@ -207,6 +215,7 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 struct GemmGeo {
     int N, K, M, P;
     int stages, nbuf;
+    int mtiles, tiles;  // activation-row tiles; tiles = mtiles x weight-row tiles (m fastest)
 };
 
 // Two floats in one 64-bit register: sm_100 packed arithmetic (f32x2), each
@@ -244,8 +253,13 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int N = geo.N, K = geo.K, S = geo.stages, NB = geo.nbuf;
-    const int n0 = blockIdx.y * kTileN, m0 = blockIdx.x * BN;
     const int nkg = K / kGroup;
+    // persistent: this CTA takes tiles blockIdx.x, + gridDim.x, ...; the
+    // stage counters (smem slots, TMEM buffers, barrier phases) run on across
+    // its tiles, so the next tile's copies and MMAs overlap this tile's
+    // readout and epilogue
+    auto tile_n0 = [&](int tl) { return (tl / geo.mtiles) * kTileN; };
+    auto tile_m0 = [&](int tl) { return (tl % geo.mtiles) * BN; };
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; i++) {
@@ -271,19 +285,26 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
     if (warp < kProdW) {
         const int pt = threadIdx.x, prow = pt >> 3, pch = pt & 7;
         if (pt == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_a)) : "memory");
-        int kg = 0, pub = 0;  // stages issued / published
-        for (; kg < nkg; kg++) {
-            const int s = kg % S;
-            if (kg >= S && !warp_wait(&done[s], ((kg / S) - 1) & 1)) {
+        int gk = 0, pub = 0;  // stages issued / published (over this CTA's tiles)
+        bool stop = false;
+        for (int tl = blockIdx.x; tl < geo.tiles && !stop; tl += gridDim.x) {
+          const int n0 = tile_n0(tl), m0 = tile_m0(tl);
+          for (int kg = 0; kg < nkg; kg++, gk++) {
+            const int s = gk % S;
+            if (gk >= S && !warp_wait(&done[s], ((gk / S) - 1) & 1)) {
                 if (lane == 0) atomicOr(&bad_s, 1);
+                stop = true;
                 break;
             }
-            if (*(volatile int*)&bad_s) break;
+            if (*(volatile int*)&bad_s) {
+                stop = true;
+                break;
+            }
             uint8_t* st = smem + (size_t)s * kStage;
             const int kb = kg * kGroup;
             const int pan = kb / geo.P;
             if (pt == 0) {
-                // rows 0-63 of the weight tile by TMA, the activation tile by TMA
+                // weight rows [0, kTmaRows) and the activation tile by TMA
                 mb_expect(&full[s], kBBytes + kTmaRows * kGroup);
                 tma_2d(st, &tm_w, kb - pan * geo.P, pan * N + n0, &full[s]);
                 tma_2d(st + kABytes, &tm_a, kb, m0, &full[s]);
@@ -296,21 +317,24 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
                 cp_async16(st + row * kGroup + pch * 16, src + (size_t)(in ? n : 0) * geo.P, in ? 16u : 0u);
             }
             cp_async_commit();
-            if (kg - pub >= kInFlight - 1) {
+            if (gk - pub >= kInFlight - 1) {
                 cp_async_wait<kInFlight - 1>();
                 fence_async_smem();
                 mb_arrive(&full[pub % S]);
                 pub++;
             }
+          }
         }
         cp_async_wait<0>();
         fence_async_smem();
-        for (; pub < kg; pub++) mb_arrive(&full[pub % S]);
-        if (pt == 0) issued_s = kg;
+        for (; pub < gk; pub++) mb_arrive(&full[pub % S]);
+        if (pt == 0) issued_s = gk;
     } else if (warp == kMma) {
         if (lane == 0) {
+            const int my_tiles = blockIdx.x < geo.tiles ? (geo.tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+            const int total = my_tiles * nkg;
             int kg = 0;
-            for (; kg < nkg; kg++) {
+            for (; kg < total; kg++) {
                 const int s = kg % S;
                 if (!mb_wait(&full[s], (kg / S) & 1)) {
                     atomicOr(&bad_s, 1);
@@ -338,13 +362,11 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
         constexpr int kCols = BN / kWQ;
         static_assert(kCols % 8 == 0, "TMEM loads move 8 columns");
         const int c0 = part * kCols;
-        const int n = n0 + 32 * q + lane;
         const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0;
         unsigned long long acc2[kCols / 2];  // column pairs (2c, 2c + 1)
-#pragma unroll
-        for (int j = 0; j < kCols / 2; j++) acc2[j] = 0ull;
+        int n = 0, g0 = 0;  // this tile's weight row; global stage of its first K-group
+        bool live = false;
         // fp16 block scales of row n: four per K-group, prefetched one group ahead
-        const bool live = n < N;
         auto load_sc = [&](int kg) -> uint2 {
             if (!live || kg >= nkg) return make_uint2(0u, 0u);
             return __ldg(reinterpret_cast<const uint2*>(g.sblk + tiled_s_off(N, geo.P, n, kg * 4)));
@@ -352,9 +374,10 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
         constexpr int kV = 2 * kCols;  // registers per half stage (two blocks)
         constexpr int kLdW = kCols >= 32 ? 32 : (kCols >= 16 ? 16 : 8);  // columns per TMEM load
         uint32_t va[kV], vb[kV];
-        // half stage h: blocks 2 (h & 1), 2 (h & 1) + 1 of stage h / 2
+        // half stage h of the tile: blocks 2 (h & 1), 2 (h & 1) + 1 of its
+        // stage h / 2 (global stage g0 + h / 2)
         auto ld_half = [&](int h, uint32_t* v) {
-            const uint32_t base = tq + (uint32_t)(((h >> 1) % NB) * 4 * BN + (h & 1) * 2 * BN);
+            const uint32_t base = tq + (uint32_t)(((g0 + (h >> 1)) % NB) * 4 * BN + (h & 1) * 2 * BN);
 #pragma unroll
             for (int j = 0; j < 2; j++)
 #pragma unroll
@@ -376,8 +399,8 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
             const bool more = h + 1 < nh;
             if (more) {
                 if (((h + 1) & 1) == 0) {
-                    const int kg = (h + 1) >> 1;
-                    if (!warp_wait(&done[kg % S], (kg / S) & 1)) return false;
+                    const int gs = g0 + ((h + 1) >> 1);
+                    if (!warp_wait(&done[gs % S], (gs / S) & 1)) return false;
                     tc_fence_after();
                 }
                 ld_half(h + 1, nxt);
@@ -385,7 +408,7 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
             if (h & 1) {
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mb_arrive(&tempty[(h >> 1) % NB]);
+                if (lane == 0) mb_arrive(&tempty[(g0 + (h >> 1)) % NB]);
             }
             const __half2 hs = *reinterpret_cast<const __half2*>(&scw);
             scale_add(cur, __low2float(hs));
@@ -393,22 +416,27 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
             if (more) tmem_wait_ld();
             return true;
         };
-        bool bad = !warp_wait(&done[0], 0);
-        if (!bad) {
-            tc_fence_after();
-            ld_half(0, va);
-            tmem_wait_ld();
-        }
-        uint2 sc_next = load_sc(0);
-        for (int kg = 0; kg < nkg && !bad; kg++) {
-            const uint2 sc = sc_next;
-            sc_next = load_sc(kg + 1);
-            if (!step(2 * kg, va, vb, sc.x)) bad = true;
-            else if (!step(2 * kg + 1, vb, va, sc.y)) bad = true;
-        }
-        if (bad) {
-            if (lane == 0) atomicOr(&bad_s, 1);
-        } else {
+        bool bad = false;
+        for (int tl = blockIdx.x; tl < geo.tiles && !bad; tl += gridDim.x, g0 += nkg) {
+            const int m0 = tile_m0(tl);
+            n = tile_n0(tl) + 32 * q + lane;
+            live = n < N;
+#pragma unroll
+            for (int j = 0; j < kCols / 2; j++) acc2[j] = 0ull;
+            bad = !warp_wait(&done[g0 % S], (g0 / S) & 1);
+            if (!bad) {
+                tc_fence_after();
+                ld_half(0, va);
+                tmem_wait_ld();
+            }
+            uint2 sc_next = load_sc(0);
+            for (int kg = 0; kg < nkg && !bad; kg++) {
+                const uint2 sc = sc_next;
+                sc_next = load_sc(kg + 1);
+                if (!step(2 * kg, va, vb, sc.x)) bad = true;
+                else if (!step(2 * kg + 1, vb, va, sc.y)) bad = true;
+            }
+            if (bad) break;
 #pragma unroll
             for (int c = 0; c < kCols; c++) {
                 const uint32_t bits = (c & 1) ? (uint32_t)(acc2[c >> 1] >> 32) : (uint32_t)acc2[c >> 1];
@@ -418,6 +446,7 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
                 if ((lane & 1) == 0 && live && m < geo.M) pair_epilogue<EPI>(g, m, n, n + 1 < N, y, y1, nullptr);
             }
         }
+        if (bad && lane == 0) atomicOr(&bad_s, 1);
     }
     __syncthreads();
     if (bad_s) {
@@ -465,6 +494,18 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, u
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// SMs of the current device (the persistent grid).
+int gemm_sms() {
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (sms <= 0) sms = 148;
+    }
+    return sms;
+}
+
 template <int BN, int EPI>
 cudaError_t launch_bn(const CUtensorMap& tw, const CUtensorMap& ta, const GemvParams& g, int M, cudaStream_t s) {
     constexpr int stage = kABytes + BN * kGroup;
@@ -476,11 +517,14 @@ cudaError_t launch_bn(const CUtensorMap& tw, const CUtensorMap& ta, const GemvPa
     geo.stages = std::min(kMaxStagesG, (kSmemBudget - 1024) / stage);
     if (geo.stages < kInFlight + 1) return cudaErrorInvalidConfiguration;
     geo.nbuf = std::min(geo.stages, 512 / (4 * BN));  // TMEM stage buffers (no more than smem stages)
+    geo.mtiles = (M + BN - 1) / BN;
+    geo.tiles = geo.mtiles * ((g.N + kTileN - 1) / kTileN);
     const size_t smem = (size_t)geo.stages * stage + 1024;
     auto kern = gemm_i8_tc_kernel<BN, EPI>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    const dim3 grid((M + BN - 1) / BN, (g.N + kTileN - 1) / kTileN);
+    // one CTA per SM (all TMEM columns, most of shared memory), persistent
+    const dim3 grid(std::min(geo.tiles, gemm_sms()));
     kern<<<grid, gemm_threads(BN), smem, s>>>(tw, ta, g, geo);
     return cudaGetLastError();
 }
@@ -509,13 +553,7 @@ bool gemm_tc_supported(const GemvParams& g, int epi) {
 // BN (measured about 1 : 1.45 for 16 : 32 on B200). Narrow tiles also spread
 // small-N layers over more SMs (their weight tiles are then re-read from L2).
 int pick_bn(int M, int N) {
-    static int sms = 0;
-    if (!sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (sms <= 0) sms = 148;
-    }
+    const int sms = gemm_sms();
     const int ntiles = (N + kTileN - 1) / kTileN;
     const int cand[2] = {16, 32};
     const double cost[2] = {1.0, 1.45};
