@@ -1749,6 +1749,35 @@ int build_batch_graph(fl_engine* e) {
     return FL_OK;
 }
 
+// Tensor parallelism: argmax key buffers for at least `rows` LM-head rows.
+// Growing them drops the step graphs that hold the old buffers.
+int tp_ensure_rows(fl_engine* e, int rows) {
+    if (e->tp_size == 1 || e->tp_rows >= rows) return FL_OK;
+    FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
+    cudaFree(e->tp_keys);
+    cudaFree(e->tp_all);
+    cudaFree(e->tp_best);
+    e->tp_keys = e->tp_all = e->tp_best = nullptr;
+    e->tp_rows = 0;
+    e->spec_ready = 0;
+    if (e->step_exec) {
+        cudaGraphExecDestroy(e->step_exec);
+        e->step_exec = nullptr;
+    }
+    e->graph_K = -1;
+    if (e->bt.exec) {
+        cudaGraphExecDestroy(e->bt.exec);
+        e->bt.exec = nullptr;
+    }
+    e->bt.ready = false;
+    if (cudaMalloc(&e->tp_keys, sizeof(unsigned long long) * rows) != cudaSuccess ||
+        cudaMalloc(&e->tp_all, sizeof(unsigned long long) * rows * e->tp_size) != cudaSuccess ||
+        cudaMalloc(&e->tp_best, sizeof(unsigned long long) * rows) != cudaSuccess)
+        return set_error(FL_E_NOMEM, "tensor parallel: argmax key buffers");
+    e->tp_rows = rows;
+    return FL_OK;
+}
+
 // Strided copy of `rows` rows of `width` bytes (row pitches in bytes).
 cudaError_t copy_rows(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width, size_t rows,
                       cudaMemcpyKind kind, cudaStream_t s) {
@@ -1761,27 +1790,9 @@ FL_API int fl_engine_batch_reserve(fl_engine_t* e, int nseq, int max_ctx) {
     FL_CHECK(check_ready(e, true));
     if (nseq <= 0 || max_ctx < 16 || nseq > 65535) return set_error(FL_E_INVAL, "batch_reserve: bad arguments");
     FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
-    if (e->tp_size > 1 && e->tp_rows < nseq * kMaxRows) {
-        // vocabulary-parallel argmax keys for every LM-head row of a batched
-        // pass (every rank reserves the same batch, so the gathers match)
-        const size_t rows = (size_t)nseq * kMaxRows;
-        cudaFree(e->tp_keys);
-        cudaFree(e->tp_all);
-        cudaFree(e->tp_best);
-        e->tp_keys = e->tp_all = e->tp_best = nullptr;
-        e->tp_rows = 0;
-        e->spec_ready = 0;  // the one-sequence step graph holds the old buffers
-        if (e->step_exec) {
-            cudaGraphExecDestroy(e->step_exec);
-            e->step_exec = nullptr;
-        }
-        e->graph_K = -1;
-        if (cudaMalloc(&e->tp_keys, sizeof(unsigned long long) * rows) != cudaSuccess ||
-            cudaMalloc(&e->tp_all, sizeof(unsigned long long) * rows * e->tp_size) != cudaSuccess ||
-            cudaMalloc(&e->tp_best, sizeof(unsigned long long) * rows) != cudaSuccess)
-            return set_error(FL_E_NOMEM, "batch_reserve: tensor-parallel key buffers");
-        e->tp_rows = (int)rows;
-    }
+    // vocabulary-parallel argmax keys for every LM-head row of a batched
+    // pass (every rank reserves the same batch, so the gathers match)
+    FL_CHECK(tp_ensure_rows(e, nseq * kMaxRows));
     const int rc = batch_alloc(e, nseq, max_ctx);
     if (rc != FL_OK) {
         batch_free(e);
@@ -2850,6 +2861,267 @@ FL_API int fl_engine_spec_tree_generate(fl_engine_t* e, const int* prompt, int P
     cleanup();
     if (take_device_error() != 0) return set_error(FL_E_TIMEOUT, "spec_tree_generate: a bounded device wait gave up");
     return FL_OK;
+}
+
+// Static draft tree for an in-GPU batch (greedy): every step each sequence's
+// draft chain runs as one batched row per sequence, each depth's top-width
+// candidates form that sequence's tree (the shape of
+// fl_engine_spec_tree_generate, shared by all sequences), and the trees of
+// all sequences are verified in one tree-masked pass of nseq x (1 + k width)
+// rows over the sequences' own KV regions; then per sequence the accepted
+// path, its KV compaction, and one batched draft catch-up over k + 1 rows per
+// sequence (rows past its path zeroed and unused). On a tensor-parallel
+// engine the ranks' candidates are gathered and merged as in the
+// one-sequence tree. Needs fl_engine_batch_reserve(nseq, >= prompt_len + n_new
+// + 1 + k width + k + 3) on every rank.
+FL_API int fl_engine_batch_tree_generate(fl_engine_t* e, const int* prompts, int P, int nseq, int n_new, int K,
+                                         int width, int* out, int* steps_out) {
+    FL_CHECK(check_ready(e, true));
+    auto& B = e->bt;
+    const int Mt = 1 + K * width;
+    if (!prompts || !out || P <= 0 || nseq <= 0 || n_new <= 0 || K < 1 || K > kMaxDraft || width < 1 || width > 32 ||
+        Mt > 256)
+        return set_error(FL_E_INVAL, "batch_tree_generate: bad arguments");
+    if (nseq > B.cap || P + n_new + Mt + K + 3 > B.slots || nseq * Mt > e->R)
+        return set_error(FL_E_INVAL, "batch_tree_generate: batch or context larger than the reservation");
+    if (e->samp) return set_error(FL_E_UNSUPPORTED, "batch_tree_generate: the tree decode is greedy");
+    if (e->d % 128 != 0) return set_error(FL_E_UNSUPPORTED, "batch: the hidden size must be a multiple of 128");
+    const int d = e->d, G = e->tp_size, V = e->V, rows = nseq * Mt, cw = K * width;
+    const size_t npart = (size_t)e->nparts;
+    cudaStream_t s = e->s;
+    FL_CHECK(tp_ensure_rows(e, rows));
+    float* lg = nullptr;
+    unsigned long long *am = nullptr, *mkeys = nullptr, *mall = nullptr;
+    int *mtok = nullptr, *mvst = nullptr, *mdst = nullptr, *mcst = nullptr, *mtarget = nullptr, *mchain = nullptr,
+        *mpath = nullptr, *mbase = nullptr, *mcat = nullptr;
+    KvLayer* dkv = nullptr;
+    auto cleanup = [&]() {
+        void* bufs[] = {lg, am, mkeys, mall, mtok, mvst, mdst, mcst, mtarget, mchain, mpath, mbase, mcat, dkv};
+        for (void* p : bufs) cudaFree(p);
+    };
+    auto fail = [&](int rc) {
+        cleanup();
+        return rc;
+    };
+#define FL_BT_CUDA(expr)                                                     \
+    do {                                                                     \
+        cudaError_t fl_e_ = (expr);                                          \
+        if (fl_e_ != cudaSuccess) return fail(cuda_error(fl_e_, #expr));     \
+    } while (0)
+#define FL_BT(expr)                       \
+    do {                                  \
+        int fl_r_ = (expr);               \
+        if (fl_r_ != FL_OK) return fail(fl_r_); \
+    } while (0)
+    const int nlb = e->base.nl;
+    FL_BT_CUDA(cudaMalloc(&lg, sizeof(float) * (size_t)rows * V));
+    FL_BT_CUDA(cudaMalloc(&am, sizeof(unsigned long long) * (size_t)rows * npart));
+    FL_BT_CUDA(cudaMalloc(&mkeys, sizeof(unsigned long long) * (size_t)nseq * cw));
+    FL_BT_CUDA(cudaMalloc(&mall, sizeof(unsigned long long) * (size_t)nseq * cw * G));
+    FL_BT_CUDA(cudaMalloc(&mtok, sizeof(int) * rows));
+    FL_BT_CUDA(cudaMalloc(&mvst, sizeof(int) * (size_t)nseq * (Mt + 1)));
+    FL_BT_CUDA(cudaMalloc(&mdst, sizeof(int) * (size_t)K * nseq * 2));
+    FL_BT_CUDA(cudaMalloc(&mcst, sizeof(int) * (size_t)nseq * (K + 2)));
+    FL_BT_CUDA(cudaMalloc(&mtarget, sizeof(int) * rows));
+    FL_BT_CUDA(cudaMalloc(&mchain, sizeof(int) * (size_t)K * nseq));
+    FL_BT_CUDA(cudaMalloc(&mpath, sizeof(int) * rows));
+    FL_BT_CUDA(cudaMalloc(&mbase, sizeof(int) * nseq));
+    FL_BT_CUDA(cudaMalloc(&mcat, sizeof(int) * (size_t)nseq * (K + 1)));
+    FL_BT_CUDA(cudaMalloc(&dkv, sizeof(KvLayer) * (size_t)nseq * nlb));
+    // each sequence's base KV region as its own cache (compaction)
+    const size_t region = (size_t)(B.slots / kPageSize) * e->Hkv * kPageSize * e->hd;
+    std::vector<KvLayer> hkv((size_t)nseq * nlb);
+    for (int q = 0; q < nseq; q++)
+        for (int l = 0; l < nlb; l++)
+            hkv[(size_t)q * nlb + l] = {B.kv_base[l].k + q * region, B.kv_base[l].v + q * region};
+    FL_BT_CUDA(cudaMemcpyAsync(dkv, hkv.data(), sizeof(KvLayer) * hkv.size(), cudaMemcpyHostToDevice, s));
+    FL_BT(ensure_mask(e, Mt));
+    const unsigned long long* keys_lm = G > 1 ? e->tp_best : am;
+    const int np_lm = G > 1 ? 1 : e->nparts;
+    // prefill per sequence into its regions: base KV 0 .. P-1, the first
+    // (greedy) token, the draft catch-up over 0 .. P; x_d1[q] = the draft
+    // feature at position P
+    {
+        std::vector<KvLayer> rb(nlb), rd(e->draft.nl);
+        for (int q = 0; q < nseq; q++) {
+            for (int l = 0; l < nlb; l++) rb[l] = hkv[(size_t)q * nlb + l];
+            for (size_t l = 0; l < rd.size(); l++) rd[l] = {B.kv_draft[l].k + q * region, B.kv_draft[l].v + q * region};
+            KvView vb, vd;
+            vb.kv = rb.data();
+            vd.kv = rd.data();
+            vb.block_table = vd.block_table = B.block;
+            int* sq = B.seq + (size_t)q * B.slots;
+            FL_BT_CUDA(cudaMemcpyAsync(sq, prompts + (size_t)q * P, sizeof(int) * P, cudaMemcpyHostToDevice, s));
+            FL_BT_CUDA(launch_embed_rows(e->embed, e->Vg, sq, nullptr, 0, e->x, d, P, nullptr, nullptr, s, false));
+            FL_BT(run_stack(e, e->base, e->x, P, nullptr, e->iota, e->iota, nullptr, nullptr, false, &vb));
+            FL_BT(run_lm(e, e->x + (size_t)(P - 1) * d, 1, nullptr, nullptr, false, lg, am));
+            FL_BT_CUDA(launch_argmax_rows(keys_lm, np_lm, 1, sq + P, nullptr, s));
+            FL_BT_CUDA(launch_embed_rows(e->embed, e->Vg, sq, e->x, 1, e->x2, d, P + 1, nullptr, nullptr, s, false));
+            FL_BT(run_stack(e, e->draft, e->x2, P + 1, nullptr, e->iota, e->iota, nullptr, nullptr, false, &vd));
+            FL_BT_CUDA(cudaMemcpyAsync(B.x_d1 + (size_t)q * d, e->x2 + (size_t)P * d, sizeof(float) * d,
+                                       cudaMemcpyDeviceToDevice, s));
+        }
+    }
+    // static tree shape (as fl_engine_spec_tree_generate) and its mask
+    std::vector<int> npar(Mt), ndep(Mt);
+    npar[0] = -1;
+    ndep[0] = 0;
+    for (int j = 1; j <= K; j++)
+        for (int c2 = 0; c2 < width; c2++) {
+            const int i = 1 + (j - 1) * width + c2;
+            npar[i] = j == 1 ? 0 : 1 + (j - 2) * width;
+            ndep[i] = j;
+        }
+    std::vector<uint8_t> mask((size_t)Mt * Mt, 0);
+    for (int i = 0; i < Mt; i++)
+        for (int j = i; j >= 0; j = npar[j]) mask[(size_t)i * Mt + j] = 1;
+    FL_BT_CUDA(cudaMemcpyAsync(e->mask, mask.data(), (size_t)Mt * Mt, cudaMemcpyHostToDevice, s));
+    // views of the batch's KV regions for the three kinds of pass
+    auto view = [&](bool base, int seq_rows, int state) {
+        KvView v;
+        v.kv = base ? B.kv_base.data() : B.kv_draft.data();
+        v.block_table = B.block;
+        v.seqs = nseq;
+        v.seq_rows = seq_rows;
+        v.seq_state = state;
+        v.seq_slots = B.slots;
+        v.max_ctx = B.slots;
+        v.attn_part = B.attn_part;
+        v.attn_cnt = B.attn_cnt;
+        return v;
+    };
+    const KvView vdraft = view(false, 1, 2), vverify = view(true, Mt, Mt + 1), vcatch = view(false, K + 1, K + 2);
+    std::vector<int> n(nseq, P), produced(nseq, 1), steps(nseq, 0), cur_tok(nseq), target(rows), ntok(rows);
+    std::vector<int> hd_state((size_t)K * nseq * 2), hv_state((size_t)nseq * (Mt + 1)), hc_state((size_t)nseq * (K + 2));
+    std::vector<int> hpath(rows), hcat((size_t)nseq * (K + 1)), acc(nseq), last_row(nseq), live(nseq);
+    std::vector<unsigned long long> keys((size_t)nseq * cw * G);
+    FL_BT_CUDA(cudaMemcpy2DAsync(cur_tok.data(), sizeof(int), B.seq + P, sizeof(int) * B.slots, sizeof(int), nseq,
+                                 cudaMemcpyDeviceToHost, s));
+    FL_BT_CUDA(cudaStreamSynchronize(s));
+    for (int q = 0; q < nseq; q++) out[(size_t)q * n_new] = cur_tok[q];
+    FL_BT_CUDA(cudaEventRecord(e->ev[0], s));
+    auto active = [&]() {
+        for (int q = 0; q < nseq; q++)
+            if (produced[q] < n_new) return true;
+        return false;
+    };
+    while (active()) {
+        // draft chains: depth j of every sequence in one single-row pass
+        for (int j = 0; j < K; j++)
+            for (int q = 0; q < nseq; q++) {
+                hd_state[((size_t)j * nseq + q) * 2] = n[q] + j;
+                hd_state[((size_t)j * nseq + q) * 2 + 1] = n[q] + j;
+            }
+        FL_BT_CUDA(cudaMemcpyAsync(mdst, hd_state.data(), sizeof(int) * hd_state.size(), cudaMemcpyHostToDevice, s));
+        for (int j = 0; j < K; j++) {
+            if (j > 0) {
+                FL_BT_CUDA(launch_embed_rows(e->embed, e->Vg, mchain + (size_t)(j - 1) * nseq, B.x_d1, 0, B.x_d1, d,
+                                             nseq, nullptr, nullptr, s, false));
+                const int* st = mdst + (size_t)j * nseq * 2;
+                FL_BT(run_stack(e, e->draft, B.x_d1, nseq, nullptr, st, st + 1, nullptr, nullptr, false, &vdraft));
+            }
+            FL_BT(run_lm(e, B.x_d1, nseq, nullptr, nullptr, false, lg, am));
+            FL_BT_CUDA(launch_argmax_rows(keys_lm, np_lm, nseq, mchain + (size_t)j * nseq, nullptr, s));
+            FL_BT_CUDA(launch_topk_keys(lg, nseq, V, V, G > 1 ? e->tp.v0 : 0, width, mkeys + (size_t)j * nseq * width, s));
+        }
+        if (G > 1) FL_BT(tp_allgather_u64(e->tp_comm, mkeys, mall, (size_t)nseq * cw, s));
+        FL_BT_CUDA(cudaMemcpyAsync(keys.data(), G > 1 ? mall : mkeys, sizeof(unsigned long long) * keys.size(),
+                                   cudaMemcpyDeviceToHost, s));
+        FL_BT_CUDA(cudaStreamSynchronize(s));
+        // per sequence: merge the ranks' candidates of each depth into its tree
+        for (int q = 0; q < nseq; q++) {
+            int* tk = ntok.data() + (size_t)q * Mt;
+            tk[0] = cur_tok[q];
+            for (int j = 0; j < K; j++) {
+                std::vector<unsigned long long> cand;
+                for (int r = 0; r < G; r++)
+                    for (int c2 = 0; c2 < width; c2++)
+                        cand.push_back(keys[(((size_t)r * K + j) * nseq + q) * width + c2]);
+                std::sort(cand.begin(), cand.end(), std::greater<unsigned long long>());
+                for (int c2 = 0; c2 < width; c2++) tk[1 + j * width + c2] = 0x7fffffff - (int)(uint32_t)(cand[c2] & 0xffffffffu);
+            }
+            hv_state[(size_t)q * (Mt + 1)] = n[q];
+            for (int i = 0; i < Mt; i++) hv_state[(size_t)q * (Mt + 1) + 1 + i] = n[q] + ndep[i];
+        }
+        FL_BT_CUDA(cudaMemcpyAsync(mtok, ntok.data(), sizeof(int) * rows, cudaMemcpyHostToDevice, s));
+        FL_BT_CUDA(cudaMemcpyAsync(mvst, hv_state.data(), sizeof(int) * hv_state.size(), cudaMemcpyHostToDevice, s));
+        FL_BT_CUDA(launch_embed_rows(e->embed, e->Vg, mtok, nullptr, 0, e->x, d, rows, nullptr, nullptr, s, false));
+        FL_BT(run_stack(e, e->base, e->x, rows, nullptr, mvst, mvst + 1, e->mask, nullptr, false, &vverify));
+        FL_BT(run_lm(e, e->x, rows, nullptr, nullptr, false, lg, am));
+        FL_BT_CUDA(launch_argmax_rows(keys_lm, np_lm, rows, mtarget, nullptr, s));
+        FL_BT_CUDA(cudaMemcpyAsync(target.data(), mtarget, sizeof(int) * rows, cudaMemcpyDeviceToHost, s));
+        FL_BT_CUDA(cudaStreamSynchronize(s));
+        // per sequence: accepted path, emitted tokens, compaction, catch-up rows
+        FL_BT_CUDA(cudaMemsetAsync(B.x_dc, 0, sizeof(float) * (size_t)nseq * (K + 1) * d, s));
+        for (int q = 0; q < nseq; q++) {
+            const int* tk = ntok.data() + (size_t)q * Mt;
+            const int* tg = target.data() + (size_t)q * Mt;
+            int* path = hpath.data() + (size_t)q * Mt;
+            int len = 1, cur = 0;
+            path[0] = 0;
+            for (;;) {
+                int nxt = -1;
+                for (int c2 = 1; c2 < Mt; c2++)
+                    if (npar[c2] == cur && tk[c2] == tg[cur]) {
+                        nxt = c2;
+                        break;
+                    }
+                if (nxt < 0) break;
+                path[len++] = nxt;
+                cur = nxt;
+            }
+            const int a = len - 1;
+            live[q] = produced[q] < n_new;  // finished sequences stay where they are
+            acc[q] = live[q] ? a : 0;
+            last_row[q] = a;
+            int* cat = hcat.data() + (size_t)q * (K + 1);
+            for (int j = 0; j <= K; j++) cat[j] = j < a ? tk[path[j + 1]] : (j == a ? tg[cur] : 0);
+            hc_state[(size_t)q * (K + 2)] = n[q] + 1;
+            for (int j = 0; j <= K; j++) hc_state[(size_t)q * (K + 2) + 1 + j] = n[q] + 1 + j;
+            if (live[q]) {
+                for (int j = 1; j <= a + 1 && produced[q] < n_new; j++)
+                    out[(size_t)q * n_new + produced[q]++] = j <= a ? tk[path[j]] : tg[cur];
+                steps[q]++;
+            }
+            for (int j = 0; j <= a; j++)
+                FL_BT_CUDA(cudaMemcpyAsync(B.x_dc + ((size_t)q * (K + 1) + j) * d, e->x + ((size_t)q * Mt + path[j]) * d,
+                                           sizeof(float) * d, cudaMemcpyDeviceToDevice, s));
+            cur_tok[q] = tg[cur];
+        }
+        std::vector<int> hbase(nseq);
+        for (int q = 0; q < nseq; q++) hbase[q] = n[q];
+        FL_BT_CUDA(cudaMemcpyAsync(mbase, hbase.data(), sizeof(int) * nseq, cudaMemcpyHostToDevice, s));
+        FL_BT_CUDA(cudaMemcpyAsync(mpath, hpath.data(), sizeof(int) * rows, cudaMemcpyHostToDevice, s));
+        for (int q = 0; q < nseq; q++)
+            if (acc[q] > 0)
+                FL_BT_CUDA(launch_kv_compact(dkv + (size_t)q * nlb, nlb, B.block, e->Hkv, e->hd, mbase + q,
+                                             mpath + (size_t)q * Mt, acc[q], s));
+        FL_BT_CUDA(cudaMemcpyAsync(mcat, hcat.data(), sizeof(int) * hcat.size(), cudaMemcpyHostToDevice, s));
+        FL_BT_CUDA(cudaMemcpyAsync(mcst, hc_state.data(), sizeof(int) * hc_state.size(), cudaMemcpyHostToDevice, s));
+        FL_BT_CUDA(launch_embed_rows(e->embed, e->Vg, mcat, B.x_dc, 0, B.x_dc, d, nseq * (K + 1), nullptr, nullptr, s,
+                                     false));
+        FL_BT(run_stack(e, e->draft, B.x_dc, nseq * (K + 1), nullptr, mcst, mcst + 1, nullptr, nullptr, false, &vcatch));
+        for (int q = 0; q < nseq; q++) {
+            FL_BT_CUDA(cudaMemcpyAsync(B.x_d1 + (size_t)q * d, B.x_dc + ((size_t)q * (K + 1) + last_row[q]) * d,
+                                       sizeof(float) * d, cudaMemcpyDeviceToDevice, s));
+            if (live[q]) n[q] += acc[q] + 1;
+        }
+    }
+    FL_BT_CUDA(cudaEventRecord(e->ev[1], s));
+    FL_BT_CUDA(cudaEventSynchronize(e->ev[1]));
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, e->ev[0], e->ev[1]);
+    e->t_total_us = ms * 1000.0;
+    long long total = 0;
+    for (int q = 0; q < nseq; q++) {
+        if (steps_out) steps_out[q] = steps[q];
+        total += steps[q];
+    }
+#undef FL_BT_CUDA
+#undef FL_BT
+    cleanup();
+    if (take_device_error() != 0) return set_error(FL_E_TIMEOUT, "batch_tree_generate: a bounded device wait gave up");
+    return (int)std::min<long long>(total, INT_MAX);
 }
 
 // Medusa candidate tree from a base feature F (host [d]): the heads' per-head

@@ -156,6 +156,7 @@ _SIGS = {
     "fl_engine_medusa_generate": (I, [VP, VP, I, I, VP, I, I, VP, VP, VP]),
     "fl_engine_spec_medusa_generate": (I, [VP, VP, I, I, I, VP, I, I, VP, VP, VP]),
     "fl_engine_spec_tree_generate": (I, [VP, VP, I, I, I, I, VP, VP, VP]),
+    "fl_engine_batch_tree_generate": (I, [VP, VP, I, I, I, I, I, VP, VP]),
     "fl_engine_medusa_tree": (I, [VP, VP, I, VP, I, I, VP, VP, VP, VP]),
     "fl_engine_tree_verify": (I, [VP, VP, VP, VP, I, VP, VP]),
     "fl_engine_bind_medusa": (I, [VP, VP]),
@@ -541,6 +542,18 @@ class Engine:
         self.lib.check(self.lib.fl_engine_spec_tree_generate(self.h, ptr(p), len(p), n_new, k, width, ptr(o), ptr(acc),
                                                              C.byref(steps)), "spec_tree_generate")
         return o, acc[: steps.value]
+
+    def batch_tree_generate(self, prompts, n_new, k, width):
+        """Static draft tree for an in-GPU batch (after batch_reserve):
+        (tokens [nseq, n_new], steps [nseq], device seconds of the decode)."""
+        pr = np.ascontiguousarray(prompts, np.int32)
+        nseq, P = pr.shape
+        out = np.empty((nseq, n_new), np.int32)
+        steps = np.empty(nseq, np.int32)
+        rc = self.lib.fl_engine_batch_tree_generate(self.h, ptr(pr), P, nseq, n_new, k, width, ptr(out), ptr(steps))
+        if rc < 0:
+            self.lib.check(rc, "batch_tree_generate")
+        return out, steps, self.last_timing()[2] * 1e-6
 
     def step_trace_stages(self):
         """[64, 4] uint64 stage stamps of the phase FL_STEP_TRACE_PHASE names."""

@@ -375,6 +375,18 @@ int fl_engine_spec_medusa_generate(fl_engine_t* e, const int* prompt, int prompt
 int fl_engine_spec_tree_generate(fl_engine_t* e, const int* prompt, int prompt_len, int n_new, int k, int width,
                                  int* out, int* acc_hist, int* steps);
 
+/* The static draft tree for an in-GPU batch (greedy): nseq sequences
+ * (prompts[i * prompt_len ..]) each get the tree of fl_engine_spec_tree_generate
+ * every step; the draft chains run as batched single-row passes, the trees of
+ * all sequences are verified in one tree-masked pass of nseq * (1 + k * width)
+ * rows over their own KV regions, and the draft catch-up is batched too. On
+ * one GPU or tensor-parallel. Needs fl_engine_batch_reserve(e, >= nseq,
+ * >= prompt_len + n_new + 1 + k * width + k + 3) first (on every rank) and
+ * nseq * (1 + k * width) <= max_seq_len. out[i * n_new ..]; steps[i] (may be
+ * NULL). Returns the total steps or a negative FL_E_* code. */
+int fl_engine_batch_tree_generate(fl_engine_t* e, const int* prompts, int prompt_len, int nseq, int n_new, int k,
+                                  int width, int* out, int* steps);
+
 /* Step-level Medusa pieces (medusa_predict / medusa_build_tree /
  * medusa_verify_tree / medusa_decode_step run on these).
  * fl_engine_medusa_tree: the heads' candidate tree from a base feature F

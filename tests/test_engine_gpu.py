@@ -626,6 +626,36 @@ def test_spec_tree_stream_is_greedy(gpu, orc, small, k, width):
     e16.close()
 
 
+@pytest.mark.parametrize("nseq,k,width", [(3, 3, 4), (4, 4, 8), (1, 2, 2)])
+def test_batch_tree_streams_are_greedy(gpu, orc, small, nseq, k, width):
+    """Draft trees for an in-GPU batch (4 x 33 nodes at k = 4, width = 8,
+    132 verify rows): every sequence's output is the base model's greedy
+    stream; on a 16-token vocabulary paths through siblings are accepted."""
+    dims, eng, om, embed = small
+    prompts = np.stack([prompt(110 + i, 14, dims["vocab"]) for i in range(nseq)])
+    eng.batch_reserve(nseq, 14 + 32 + 1 + k * width + k + 3)
+    got, steps, secs = eng.batch_tree_generate(prompts, 32, k, width)
+    for i in range(nseq):
+        want, margins = om.greedy(prompts[i], 32)
+        assert_stream_matches(got[i], want, margins)
+    assert steps.min() >= 1 and secs > 0
+    dims16 = dict(SMALL, vocab=16)
+    w, emb = make_weights(gpu, dims16, seed=5, draft_layers=1)
+    e16 = flb200.Engine(gpu, engine_cfg(dims16, draft_layers=1, max_seq_len=256))
+    load_engine(e16, w, emb)
+    om16 = oracle_model(orc, dims16, w, emb, draft_layers=1)
+    p16 = np.stack([prompt(120 + i, 12, 16) for i in range(nseq)])
+    e16.batch_reserve(nseq, 12 + 48 + 1 + k * width + k + 3)
+    got, steps, _ = e16.batch_tree_generate(p16, 48, k, width)
+    for i in range(nseq):
+        want, margins = om16.greedy(p16[i], 48)
+        assert_stream_matches(got[i], want, margins)
+        one, acc = e16.spec_tree_generate(p16[i], 48, k, width)
+        assert_stream_matches(one, want, margins)
+    assert steps.max() < 47, steps.tolist()  # multi-token steps
+    e16.close()
+
+
 def test_medusa_step_api_matches_generate(gpu, orc):
     """The reference's step-level Medusa API on the engine's callback position
     (prefill with fl_cuda_base_forward, then medusa_decode_step /
