@@ -289,11 +289,17 @@ def run_tp_medium(a):
     rng = np.random.default_rng(PROMPT_SEED)
     prompts = rng.integers(0, MEDIUM["vocab_size"], (B, a.prompt_len)).astype(np.int32)
     tree_us = []
-    if a.tree > 0:
+    if a.tree > 0 and B > 1:
+        # a draft tree of 1 + k * width nodes for each of B sequences, all
+        # verified in one pass (prefills inside each call, outside its timing)
+        eng.batch_reserve(B, a.prompt_len + a.new_tokens + 1 + a.k * a.tree + a.k + 3)
+        def decode():
+            toks, steps, _ = eng.batch_tree_generate(prompts, a.new_tokens, a.k, a.tree)
+            tree_us.append(eng.last_timing()[2])
+            return toks, np.zeros(int(steps.max()), np.int32)
+    elif a.tree > 0:
         # static draft tree of 1 + k * width nodes (prefill inside each call,
         # outside its device timing)
-        if B != 1:
-            raise SystemExit("--tree decodes one sequence (--batch 1)")
         def decode():
             toks, acc = eng.spec_tree_generate(prompts[0], a.new_tokens, a.k, a.tree)
             tree_us.append(eng.last_timing()[2])

@@ -57,10 +57,13 @@ def _rank(rank, size, uid, q):
         bt, _, _ = eng.batch_decode(24)
         # a 17-node draft tree (k = 4, width 4): merged top-4 across the ranks
         tt, _ = eng.spec_tree_generate(p, 24, 4, 4)
+        # the same tree for each sequence of a batch of three
+        eng.batch_reserve(3, 12 + 24 + 1 + 4 * 4 + 4 + 3)
+        btt, _, _ = eng.batch_tree_generate(_batch_prompts(prompt), 24, 4, 4)
         eng.close()
-        q.put((rank, toks.tolist(), acc.tolist(), g.tolist(), bt.tolist(), tt.tolist(), None))
+        q.put((rank, toks.tolist(), acc.tolist(), g.tolist(), bt.tolist(), tt.tolist(), btt.tolist(), None))
     except Exception as ex:  # reported to the parent
-        q.put((rank, None, None, None, None, None, repr(ex)))
+        q.put((rank, None, None, None, None, None, None, repr(ex)))
 
 
 def _batch_prompts(prompt):
@@ -83,15 +86,16 @@ def test_two_rank_decode_matches_oracle(gpu, orc):
         p.start()
     res = {}
     for _ in range(2):
-        r, toks, acc, g, bt, tt, err = q.get(timeout=600)
+        r, toks, acc, g, bt, tt, btt, err = q.get(timeout=600)
         assert err is None, f"rank {r}: {err}"
-        res[r] = (np.array(toks), np.array(acc), np.array(g), np.array(bt), np.array(tt))
+        res[r] = (np.array(toks), np.array(acc), np.array(g), np.array(bt), np.array(tt), np.array(btt))
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
     assert np.array_equal(res[0][0], res[1][0]) and np.array_equal(res[0][2], res[1][2]), "ranks disagree"
     assert np.array_equal(res[0][3], res[1][3]), "ranks disagree on the batch"
     assert np.array_equal(res[0][4], res[1][4]), "ranks disagree on the tree decode"
+    assert np.array_equal(res[0][5], res[1][5]), "ranks disagree on the batched tree decode"
     w, embed = make_weights(gpu, TP_GQA, seed=41)
     om = bind.OracleModel(orc, TP_GQA, embed, w, draft_layers=1)
     p = prompt(8, 16, TP_GQA["vocab"])
@@ -108,3 +112,5 @@ def test_two_rank_decode_matches_oracle(gpu, orc):
         bw, bm = om.greedy(pb, 24)
         bd = np.nonzero(res[0][3][i] != bw)[0]
         assert bd.size == 0 or bm[bd[0]] < 1e-2, f"batch sequence {i} diverges at {bd[:1]}"
+        td = np.nonzero(res[0][5][i] != bw)[0]
+        assert td.size == 0 or bm[td[0]] < 1e-2, f"batched tree sequence {i} diverges at {td[:1]}"
