@@ -13,7 +13,7 @@ needed between timed iterations.
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
     python bench.py --workload sampled-batch [--seqs 64 --prompt-len 1024 --new-tokens 512 --k 6]
-    torchrun --nproc-per-node N bench.py --gpus N --workload tp-medium [--prompt-len 512]
+    torchrun --nproc-per-node N bench.py --gpus N --workload tp-medium [--prompt-len 512] [--batch 4] [--tree 8]
     python bench.py --workload medusa [--prompt-len 512 --new-tokens 256]
 
 One process per GPU (torchrun for N > 1); this path does not shard (batch 1),
@@ -35,7 +35,10 @@ default line.
 shaped base (40 layers, d 5120, 40 query / 10 KV heads x 128, SwiGLU 17920,
 vocab 32064) with a 2-layer draft of the same dims, greedy chain k = 4, bs1,
 sharded over the ranks (NCCL all-reduce after o and down); `value` = tokens/s
-of the one sequence (strong scaling), device-timed, max over ranks.
+of all sequences (strong scaling), device-timed, max over ranks. `--batch B`
+decodes B sequences as one in-GPU batch; `--tree W` verifies a static draft
+tree of 1 + k W nodes per step (with `--batch`, one tree per sequence, all
+in one pass; prefills outside the timing).
 
 --workload medusa is the Medusa configuration: the Phi-3-mini base with 4
 residual Medusa heads (3072 x 3072 INT8 each, shared LM head), per-head
