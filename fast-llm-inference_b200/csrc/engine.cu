@@ -2696,6 +2696,59 @@ FL_API int fl_engine_spec_medusa_generate(fl_engine_t* e, const int* prompt, int
     return FL_OK;
 }
 
+namespace {
+
+// Static draft-tree shape: node 0 is the root, then per depth j = 1 .. K the
+// chain node (first) and width - 1 siblings, all children of the chain node
+// of depth j - 1. mask[i * Mt + j] = 1 where node j is node i or one of its
+// ancestors.
+void draft_tree_shape(int K, int width, std::vector<int>& par, std::vector<int>& dep, std::vector<uint8_t>& mask) {
+    const int Mt = 1 + K * width;
+    par.assign(Mt, -1);
+    dep.assign(Mt, 0);
+    for (int j = 1; j <= K; j++)
+        for (int c2 = 0; c2 < width; c2++) {
+            const int i = 1 + (j - 1) * width + c2;
+            par[i] = j == 1 ? 0 : 1 + (j - 2) * width;
+            dep[i] = j;
+        }
+    mask.assign((size_t)Mt * Mt, 0);
+    for (int i = 0; i < Mt; i++)
+        for (int j = i; j >= 0; j = par[j]) mask[(size_t)i * Mt + j] = 1;
+}
+
+// Greedy tree acceptance: from the root, follow the child whose token is the
+// base model's choice at its parent (target[parent]) while there is one.
+// path[0] = 0 (the root); returns the accepted nodes (path length - 1).
+int accept_path(const int* tok, const int* par, const int* target, int M, std::vector<int>& path) {
+    path.assign(1, 0);
+    int cur = 0;
+    for (;;) {
+        int nxt = -1;
+        for (int c2 = 1; c2 < M; c2++)
+            if (par[c2] == cur && tok[c2] == target[cur]) {
+                nxt = c2;
+                break;
+            }
+        if (nxt < 0) break;
+        path.push_back(nxt);
+        cur = nxt;
+    }
+    return (int)path.size() - 1;
+}
+
+// The width best candidates of one depth from every rank's top-width keys
+// (value, global index; larger first): their token ids, best first.
+void merge_topw(const unsigned long long* keys, int ranks, size_t rank_stride, int width, int* tok) {
+    std::vector<unsigned long long> cand;
+    for (int r = 0; r < ranks; r++)
+        for (int c2 = 0; c2 < width; c2++) cand.push_back(keys[(size_t)r * rank_stride + c2]);
+    std::sort(cand.begin(), cand.end(), std::greater<unsigned long long>());
+    for (int c2 = 0; c2 < width; c2++) tok[c2] = 0x7fffffff - (int)(uint32_t)(cand[c2] & 0xffffffffu);
+}
+
+}  // namespace
+
 // Static draft tree (EAGLE-style): the draft chain c_1..c_K plus, at every
 // depth j, the draft's next w - 1 candidates after c_j, all children of
 // c_{j-1} (c_0 = the newest committed token). Nodes in depth order: root,
@@ -2758,21 +2811,9 @@ FL_API int fl_engine_spec_tree_generate(fl_engine_t* e, const int* prompt, int P
     int produced = 0, steps = 0, n = P;
     out[produced++] = cur_tok;
     std::vector<unsigned long long> keys((size_t)K * width * G);
-    std::vector<int> ntok(Mt), npar(Mt), ndep(Mt), hpos(Mt), target(Mt), path, cat;
-    std::vector<uint8_t> mask((size_t)Mt * Mt);
-    // static tree shape: parents, depths and the ancestor mask
-    npar[0] = -1;
-    ndep[0] = 0;
-    for (int j = 1; j <= K; j++)
-        for (int c2 = 0; c2 < width; c2++) {
-            const int i = 1 + (j - 1) * width + c2;
-            npar[i] = j == 1 ? 0 : 1 + (j - 2) * width;
-            ndep[i] = j;
-        }
-    for (int i = 0; i < Mt; i++) {
-        for (int j = 0; j < Mt; j++) mask[(size_t)i * Mt + j] = 0;
-        for (int j = i; j >= 0; j = npar[j]) mask[(size_t)i * Mt + j] = 1;
-    }
+    std::vector<int> ntok(Mt), npar, ndep, hpos(Mt), target(Mt), path, cat;
+    std::vector<uint8_t> mask;
+    draft_tree_shape(K, width, npar, ndep, mask);
     FL_ST_CUDA(cudaMemcpyAsync(e->mask, mask.data(), (size_t)Mt * Mt, cudaMemcpyHostToDevice, s));
     FL_ST_CUDA(cudaEventRecord(e->ev[0], s));
     while (produced < n_new) {
@@ -2795,15 +2836,8 @@ FL_API int fl_engine_spec_tree_generate(fl_engine_t* e, const int* prompt, int P
                                    cudaMemcpyDeviceToHost, s));
         FL_ST_CUDA(cudaStreamSynchronize(s));
         ntok[0] = cur_tok;
-        for (int j = 0; j < K; j++) {
-            // merge the ranks' candidates of depth j + 1: the w largest keys
-            std::vector<unsigned long long> cand;
-            for (int r = 0; r < G; r++)
-                for (int c2 = 0; c2 < width; c2++) cand.push_back(keys[((size_t)r * K + j) * width + c2]);
-            std::sort(cand.begin(), cand.end(), std::greater<unsigned long long>());
-            for (int c2 = 0; c2 < width; c2++)
-                ntok[1 + j * width + c2] = 0x7fffffff - (int)(uint32_t)(cand[c2] & 0xffffffffu);
-        }
+        for (int j = 0; j < K; j++)  // depth j + 1: the ranks' candidates merged
+            merge_topw(keys.data() + (size_t)j * width, G, (size_t)K * width, width, ntok.data() + 1 + j * width);
         for (int i = 0; i < Mt; i++) hpos[i] = n + ndep[i];
         FL_ST_CUDA(cudaMemcpyAsync(mtok, ntok.data(), sizeof(int) * Mt, cudaMemcpyHostToDevice, s));
         FL_ST_CUDA(cudaMemcpyAsync(mpos, hpos.data(), sizeof(int) * Mt, cudaMemcpyHostToDevice, s));
@@ -2816,20 +2850,8 @@ FL_API int fl_engine_spec_tree_generate(fl_engine_t* e, const int* prompt, int P
         }
         FL_ST_CUDA(cudaMemcpyAsync(target.data(), mtarget, sizeof(int) * Mt, cudaMemcpyDeviceToHost, s));
         FL_ST_CUDA(cudaStreamSynchronize(s));
-        path.assign(1, 0);
-        int cur = 0;
-        for (;;) {
-            int nxt = -1;
-            for (int c2 = 1; c2 < Mt; c2++)
-                if (npar[c2] == cur && ntok[c2] == target[cur]) {
-                    nxt = c2;
-                    break;
-                }
-            if (nxt < 0) break;
-            path.push_back(nxt);
-            cur = nxt;
-        }
-        const int a = (int)path.size() - 1;
+        const int a = accept_path(ntok.data(), npar.data(), target.data(), Mt, path);
+        const int cur = path[a];
         if (acc_hist) acc_hist[steps] = a;
         steps++;
         for (int j = 1; j <= a + 1 && produced < n_new; j++) out[produced++] = j <= a ? ntok[path[j]] : target[cur];
@@ -2963,18 +2985,9 @@ FL_API int fl_engine_batch_tree_generate(fl_engine_t* e, const int* prompts, int
         }
     }
     // static tree shape (as fl_engine_spec_tree_generate) and its mask
-    std::vector<int> npar(Mt), ndep(Mt);
-    npar[0] = -1;
-    ndep[0] = 0;
-    for (int j = 1; j <= K; j++)
-        for (int c2 = 0; c2 < width; c2++) {
-            const int i = 1 + (j - 1) * width + c2;
-            npar[i] = j == 1 ? 0 : 1 + (j - 2) * width;
-            ndep[i] = j;
-        }
-    std::vector<uint8_t> mask((size_t)Mt * Mt, 0);
-    for (int i = 0; i < Mt; i++)
-        for (int j = i; j >= 0; j = npar[j]) mask[(size_t)i * Mt + j] = 1;
+    std::vector<int> npar, ndep;
+    std::vector<uint8_t> mask;
+    draft_tree_shape(K, width, npar, ndep, mask);
     FL_BT_CUDA(cudaMemcpyAsync(e->mask, mask.data(), (size_t)Mt * Mt, cudaMemcpyHostToDevice, s));
     // views of the batch's KV regions for the three kinds of pass
     auto view = [&](bool base, int seq_rows, int state) {
@@ -2993,7 +3006,7 @@ FL_API int fl_engine_batch_tree_generate(fl_engine_t* e, const int* prompts, int
     const KvView vdraft = view(false, 1, 2), vverify = view(true, Mt, Mt + 1), vcatch = view(false, K + 1, K + 2);
     std::vector<int> n(nseq, P), produced(nseq, 1), steps(nseq, 0), cur_tok(nseq), target(rows), ntok(rows);
     std::vector<int> hd_state((size_t)K * nseq * 2), hv_state((size_t)nseq * (Mt + 1)), hc_state((size_t)nseq * (K + 2));
-    std::vector<int> hpath(rows), hcat((size_t)nseq * (K + 1)), acc(nseq), last_row(nseq), live(nseq);
+    std::vector<int> hpath(rows), hcat((size_t)nseq * (K + 1)), acc(nseq), last_row(nseq), live(nseq), pathv;
     std::vector<unsigned long long> keys((size_t)nseq * cw * G);
     FL_BT_CUDA(cudaMemcpy2DAsync(cur_tok.data(), sizeof(int), B.seq + P, sizeof(int) * B.slots, sizeof(int), nseq,
                                  cudaMemcpyDeviceToHost, s));
@@ -3032,14 +3045,9 @@ FL_API int fl_engine_batch_tree_generate(fl_engine_t* e, const int* prompts, int
         for (int q = 0; q < nseq; q++) {
             int* tk = ntok.data() + (size_t)q * Mt;
             tk[0] = cur_tok[q];
-            for (int j = 0; j < K; j++) {
-                std::vector<unsigned long long> cand;
-                for (int r = 0; r < G; r++)
-                    for (int c2 = 0; c2 < width; c2++)
-                        cand.push_back(keys[(((size_t)r * K + j) * nseq + q) * width + c2]);
-                std::sort(cand.begin(), cand.end(), std::greater<unsigned long long>());
-                for (int c2 = 0; c2 < width; c2++) tk[1 + j * width + c2] = 0x7fffffff - (int)(uint32_t)(cand[c2] & 0xffffffffu);
-            }
+            for (int j = 0; j < K; j++)
+                merge_topw(keys.data() + ((size_t)j * nseq + q) * width, G, (size_t)K * nseq * width, width,
+                           tk + 1 + j * width);
             hv_state[(size_t)q * (Mt + 1)] = n[q];
             for (int i = 0; i < Mt; i++) hv_state[(size_t)q * (Mt + 1) + 1 + i] = n[q] + ndep[i];
         }
@@ -3057,20 +3065,9 @@ FL_API int fl_engine_batch_tree_generate(fl_engine_t* e, const int* prompts, int
             const int* tk = ntok.data() + (size_t)q * Mt;
             const int* tg = target.data() + (size_t)q * Mt;
             int* path = hpath.data() + (size_t)q * Mt;
-            int len = 1, cur = 0;
-            path[0] = 0;
-            for (;;) {
-                int nxt = -1;
-                for (int c2 = 1; c2 < Mt; c2++)
-                    if (npar[c2] == cur && tk[c2] == tg[cur]) {
-                        nxt = c2;
-                        break;
-                    }
-                if (nxt < 0) break;
-                path[len++] = nxt;
-                cur = nxt;
-            }
-            const int a = len - 1;
+            const int a = accept_path(tk, npar.data(), tg, Mt, pathv);
+            const int cur = pathv[a];
+            std::copy(pathv.begin(), pathv.end(), path);
             live[q] = produced[q] < n_new;  // finished sequences stay where they are
             acc[q] = live[q] ? a : 0;
             last_row[q] = a;
