@@ -115,8 +115,11 @@ __global__ void __launch_bounds__(kAThreads) attention_kernel(const AttnParams p
 #pragma unroll
     for (int rr = 0; rr < kARows; rr++) { a0[rr] = 0.0f; a1[rr] = 0.0f; }
 
-    for (int j0 = 0; j0 < ctx; j0 += kTile) {
-        const int nt = min(kTile, ctx - j0);
+    // causal (no mask): keys after this CTA's last row are hidden from all
+    // its rows, so the loop stops there; a tree mask may expose any new slot
+    const int kend = p.mask ? ctx : min(ctx, base + r0 + nr);
+    for (int j0 = 0; j0 < kend; j0 += kTile) {
+        const int nt = min(kTile, kend - j0);
         __syncthreads();  // previous tile fully consumed
         // K and V tile, consecutive threads -> consecutive words: 16-byte
         // loads (four half2 words), several in flight per thread, when a key
