@@ -169,7 +169,7 @@ def cpu_decode_sample(w, embed, prompt, k, n_tokens, threads):
 
 
 def stream_parity(gpu, cpu, margins, tol=1e-2):
-    """BASELINE rule: identical streams, except from a position where the
+    """Parity rule: identical streams, except from a position where the
     oracle's relative top-2 logit margin is below the logit tolerance."""
     diff = np.nonzero(np.asarray(gpu) != np.asarray(cpu))[0]
     if diff.size == 0:

@@ -1,7 +1,7 @@
 """The whole decode path on the GPU against the oracle, on seeded small
 models (seconds of oracle time) and one full-size Phi-3-mini case.
 
-Tolerances (BASELINE parity rules): logits within 1e-2 relative to the row's
+Tolerances (the parity rules of the path): logits within 1e-2 relative to the row's
 largest |logit|; token streams identical except from a position where the
 oracle's top-2 logit margin is below 1e-2 of its top logit (a near-tie).
 """
