@@ -152,32 +152,40 @@ __global__ void __launch_bounds__(kAThreads) attention_kernel(const AttnParams p
             }
         }
         __syncthreads();
-        // scores: one key per thread (kTile <= kAThreads)
-        if (threadIdx.x < nt) {
-            const int j = j0 + threadIdx.x;
-            float acc[kARows];
+        // scores: thread -> key (tid % kTile) and half of the rows (tid / kTile);
+        // warps lie within one half, so the q reads are broadcasts
+        static_assert(kAThreads == 2 * kTile && kARows % 2 == 0, "two threads per key");
+        {
+            constexpr int kHalf = kARows / 2;
+            const int key = threadIdx.x & (kTile - 1);
+            const int rh = (threadIdx.x / kTile) * kHalf;
+            if (key < nt && rh < nr) {
+                const int j = j0 + key;
+                float acc[kHalf];
 #pragma unroll
-            for (int rr = 0; rr < kARows; rr++) acc[rr] = 0.0f;
-            const uint32_t* kr = Ks + threadIdx.x * kstride;
-            for (int e = 0; e < hd2; e++) {
-                const float2 kf = __half22float2(*reinterpret_cast<const __half2*>(&kr[e]));
+                for (int i = 0; i < kHalf; i++) acc[i] = 0.0f;
+                const uint32_t* kr = Ks + key * kstride;
+                for (int e = 0; e < hd2; e++) {
+                    const float2 kf = __half22float2(*reinterpret_cast<const __half2*>(&kr[e]));
 #pragma unroll
-                for (int rr = 0; rr < kARows; rr++) {
-                    if (rr < nr) {
-                        acc[rr] = __fmaf_rn(q_s[rr * hd + 2 * e], kf.x, acc[rr]);
-                        acc[rr] = __fmaf_rn(q_s[rr * hd + 2 * e + 1], kf.y, acc[rr]);
+                    for (int i = 0; i < kHalf; i++) {
+                        if (rh + i < nr) {
+                            acc[i] = __fmaf_rn(q_s[(rh + i) * hd + 2 * e], kf.x, acc[i]);
+                            acc[i] = __fmaf_rn(q_s[(rh + i) * hd + 2 * e + 1], kf.y, acc[i]);
+                        }
                     }
                 }
-            }
 #pragma unroll
-            for (int rr = 0; rr < kARows; rr++) {
-                if (rr < nr) {
-                    bool vis = true;
-                    if (j >= base) {
-                        const int jj = j - base, ii = r0 + rr;
-                        vis = p.mask ? (p.mask[(size_t)ii * M + jj] != 0) : (jj <= ii);
+                for (int i = 0; i < kHalf; i++) {
+                    const int rr = rh + i;
+                    if (rr < nr) {
+                        bool vis = true;
+                        if (j >= base) {
+                            const int jj = j - base, ii = r0 + rr;
+                            vis = p.mask ? (p.mask[(size_t)ii * M + jj] != 0) : (jj <= ii);
+                        }
+                        sc[rr * kTile + key] = vis ? __fmul_rn(acc[i], scale) : -INFINITY;
                     }
-                    sc[rr * kTile + threadIdx.x] = vis ? __fmul_rn(acc[rr], scale) : -INFINITY;
                 }
             }
         }
