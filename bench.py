@@ -75,22 +75,6 @@ def engine_cfg(max_seq_len):
                 rope_theta=DIMS["theta"], norm_eps=DIMS["eps"])
 
 
-def make_weights(lib):
-    """Host copies of every tensor (the oracle needs them too)."""
-    from flb200 import tensor_id
-    d, F = DIMS["d"], DIMS["ffn"]
-    qd = kd = DIMS["heads"] * DIMS["head_dim"]
-    shapes = [(qd, d), (kd, d), (kd, d), (d, qd), (F, d), (F, d), (d, F)]
-    w = {}
-    for s, nl in ((0, DIMS["layers"]), (1, DRAFT_LAYERS)):
-        for l in range(nl):
-            for p, (r, c) in enumerate(shapes):
-                w[(s, l, p)] = lib.synth_q4_0_i8(SEED, tensor_id(s, l, p), r, c)
-    w[(3, 0, 1)] = lib.synth_q4_0_i8(SEED, tensor_id(3, 0, 1), DIMS["vocab"], d)
-    embed = lib.synth_q4_0_f32(SEED, tensor_id(3, 0, 0), DIMS["vocab"], d)
-    return w, embed
-
-
 def step_bytes(k, ctx):
     """Algorithmic HBM bytes of one speculative step: k draft passes (4
     layers + LM head) and one verify pass (32 layers + LM head) of INT8
@@ -155,59 +139,115 @@ class Clocks:
                 "samples": len(sm)}
 
 
-def cpu_decode_sample(w, embed, prompt, k, n_tokens, threads):
-    """The oracle's speculative decode on the host cores; returns decode-loop
-    tokens/s (prefill excluded) and the tokens."""
+def tensor_id(stack, layer, proj):
+    """FL_TENSOR_ID of include/fl_cuda.h."""
+    return (stack << 24) | (layer << 8) | proj
+
+
+def workload_config(a, world):
+    """The `config` of both arms' lines (same workload, same keys)."""
+    return {"workload": f"phi3-mini int8 (32L d3072 ffn8192 vocab32064) + {DRAFT_LAYERS}-layer draft, "
+                        f"greedy chain k={a.k}, bs1, prompt {a.prompt_len}, {a.new_tokens} new tokens per step",
+            "parallelism": "replicas only" if world > 1 else "single GPU",
+            "l2": "inputs larger than L2 (6.4 GB of weights per speculative step)"}
+
+
+def oracle_weights(orc):
+    """Every tensor of the model from the oracle's restatement of the seeded
+    generator: the bits fl_engine_synthesize puts on the device, with no
+    product library loaded."""
+    d, F = DIMS["d"], DIMS["ffn"]
+    qd = kd = DIMS["heads"] * DIMS["head_dim"]
+    shapes = [(qd, d), (kd, d), (kd, d), (d, qd), (F, d), (F, d), (d, F)]
+    w = {}
+    for s_, nl in ((0, DIMS["layers"]), (1, DRAFT_LAYERS)):
+        for l in range(nl):
+            for p, (r, c) in enumerate(shapes):
+                w[(s_, l, p)] = orc.synth_q4_0_i8(SEED, tensor_id(s_, l, p), r, c)
+    w[(3, 0, 1)] = orc.synth_q4_0_i8(SEED, tensor_id(3, 0, 1), DIMS["vocab"], d)
+    embed = orc.synth_q4_0_f32(SEED, tensor_id(3, 0, 0), DIMS["vocab"], d)
+    return w, embed
+
+
+def reference_rows(w):
+    """Per-row-scale tensors for the reference's matmul_dequantized: the
+    same INT8 values in [-8, 7] (no pair-sum saturation) with one scale per
+    row, the row's first block scale times 16 (its epilogue divides by
+    127 * 16, dequantized_tensor.c:235-243). The reference's own loader
+    format ((q-8)*16, dequantized_tensor.c:27-58) saturates the pair sums
+    and collapses these random-init models into a stream that accepts every
+    draft, which would compare a different amount of work per token."""
+    out = {}
+    for key, (wq, dq) in w.items():
+        rs = dq[:, 0].view(np.float16).astype(np.float32) * 16.0
+        out[key] = (np.ascontiguousarray(wq), np.ascontiguousarray(rs))
+    return out
+
+
+def cpu_reference_decode(a, n_tokens, warmup, steps):
+    """The reference's CPU path on the host cores: the oracle's speculative
+    decode loop with every INT8 linear layer run by the reference's own
+    compiled matmul_dequantized (oracle/_ref/libref.so: dequantized_tensor.c
+    at the reference's flags, fast_llm/Makefile:5-6) on its per-row-scale
+    weight format; the other layer math is the oracle's restatement of
+    inference.c. Same weights (seeded generator restated by the oracle),
+    prompt and draft length as the GPU arm; no product library is loaded.
+    Returns a dict with the median decode-loop rate over `steps` decodes of
+    n_tokens (each after its own prefill, excluded from the rate)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    threads = os.cpu_count() or 1
     os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    import ctypes as C
     import bind
+    t0 = time.time()
     orc = bind.Oracle()
-    om = bind.OracleModel(orc, DIMS, embed, w, draft_layers=DRAFT_LAYERS)
-    toks, acc, margins = om.spec(prompt, n_tokens, k)
-    dec = orc.so.orc_last_decode_seconds()
-    return (n_tokens - 1) / dec, toks, acc, dec, margins
-
-
-def stream_parity(gpu, cpu, margins, tol=1e-2):
-    """Parity rule: identical streams, except from a position where the
-    oracle's relative top-2 logit margin is below the logit tolerance."""
-    diff = np.nonzero(np.asarray(gpu) != np.asarray(cpu))[0]
-    if diff.size == 0:
-        return {"identical": True, "checked": int(len(cpu))}
-    i = int(diff[0])
-    return {"identical": False, "first_divergence": i, "oracle_rel_margin": float(margins[i]),
-            "near_tie": bool(margins[i] < tol), "checked": int(len(cpu))}
+    try:
+        ref = bind.Ref()
+    except RuntimeError:
+        ref = None
+    w, embed = oracle_weights(orc)
+    if ref is not None:
+        orc.so.orc_set_ref_matmul(C.cast(ref.so.ref_matmul_dequantized, C.c_void_p))
+        om = bind.OracleModel(orc, DIMS, embed, w, draft_layers=DRAFT_LAYERS, ref_rows=reference_rows(w))
+    else:
+        om = bind.OracleModel(orc, DIMS, embed, w, draft_layers=DRAFT_LAYERS)
+    prompt = np.random.default_rng(PROMPT_SEED).integers(0, DIMS["vocab"], a.prompt_len).astype(np.int32)
+    setup_s = time.time() - t0
+    for _ in range(warmup):  # warms caches and threads: short decodes
+        om.spec(prompt, 8, a.k)
+    vals, hist = [], []
+    for _ in range(steps):
+        _, acc, _ = om.spec(prompt, n_tokens, a.k)
+        dec = orc.so.orc_last_decode_seconds()
+        vals.append(((n_tokens - 1) / dec, dec))
+        hist.append(acc)
+    orc.so.orc_set_ref_matmul(None)
+    acc_cat = np.concatenate(hist)
+    return {"value": float(statistics.median(x[0] for x in vals)),
+            "ms": float(statistics.median(x[1] for x in vals)) * 1000.0,
+            "kind": "reference" if ref is not None else "port", "cores": threads, "setup_s": setup_s,
+            "matmul": "reference matmul_dequantized (libref.so, reference flags), per-row-scale format"
+            if ref is not None else "oracle block matmul (libref.so absent)",
+            "accepted_hist": np.bincount(acc_cat, minlength=a.k + 1).tolist()}
 
 
 def run_reference(a, rank, world):
     if rank != 0:
         return 0
-    import flb200
-    lib = flb200.Lib()
-    threads = os.cpu_count() or 1
-    t0 = time.time()
-    w, embed = make_weights(lib)
-    prompt = np.random.default_rng(PROMPT_SEED).integers(0, DIMS["vocab"], a.prompt_len).astype(np.int32)
-    n = a.cpu_tokens
-    vals = []
-    for i in range(a.warmup + a.steps):
-        v, toks, acc, dec, _ = cpu_decode_sample(w, embed, prompt, a.k, n, threads)
-        if i >= a.warmup:
-            vals.append((v, dec))
-    v = float(statistics.median(x[0] for x in vals))
-    ms = float(statistics.median(x[1] for x in vals)) * 1000.0
+    r = cpu_reference_decode(a, a.new_tokens, a.warmup, a.steps)
     line = {
-        "metric": METRIC, "value": v, "unit": "tok/s", "impl": "reference", "n_gpus": world, "steps": a.steps,
-        "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "u8xs8->s32, f32", "data": "synthetic (seeded N(0,0.02) -> Q4_0 -> INT8 weights, uniform prompt)",
-        "config": {"workload": f"phi3-mini int8 + {DRAFT_LAYERS}-layer draft, greedy chain k={a.k}, bs1, prompt "
-                               f"{a.prompt_len}, {n} new tokens per step (bounded CPU sample)",
-                   "l2": "inputs larger than L2"},
-        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "port",
-                         "sample": f"decode loop of {n} tokens after a {a.prompt_len}-token prefill (prefill "
-                                   f"excluded); oracle restatement on the reference's arithmetic, OpenMP"},
-        "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "setup_s": time.time() - t0,
+        "metric": METRIC, "value": r["value"], "unit": "tok/s", "impl": "reference", "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": r["ms"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u8xs8->s32, f32",
+        "data": "synthetic (seeded N(0,0.02) -> Q4_0 -> INT8 weights, uniform prompt ids)",
+        "config": workload_config(a, world),
+        "cpu_baseline": {"value": r["value"], "unit": "tok/s", "cores": r["cores"], "kind": r["kind"],
+                         "sample": f"each step: one {a.new_tokens}-token speculative decode after the "
+                                   f"{a.prompt_len}-token prefill (prefill excluded from the rate; warm-up steps "
+                                   f"decode 8 tokens)",
+                         "matmul": r["matmul"], "accepted_hist": r["accepted_hist"]},
+        "e2e": {"value": r["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "setup_s": r["setup_s"],
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -563,15 +603,7 @@ def main():
     t_setup = time.time()
     max_seq = 512
     eng = flb200.Engine(lib, engine_cfg(max_seq), local)
-    keep_host = rank == 0 and world == 1 and not a.no_cpu_baseline
-    w = embed = None
-    if keep_host:
-        w, embed = make_weights(lib)
-        for (s, l, p), (wq, dq) in w.items():
-            eng.load_linear(s, l, p, wq, dq)
-        eng.load_embedding(embed)
-    else:
-        eng.synthesize(SEED)
+    eng.synthesize(SEED)  # the seeded generator on the device: the tensors the CPU arm generates
     prompt = np.random.default_rng(PROMPT_SEED).integers(0, DIMS["vocab"], a.prompt_len).astype(np.int32)
     eng.spec_prefill(prompt, a.k)
     setup_s = time.time() - t_setup
@@ -625,6 +657,8 @@ def main():
     us_qkv, by_qkv = eng.bench_linear(0, 0, a.k + 1, reps=5)
     us_o, by_o = eng.bench_linear(0, 1, a.k + 1, reps=5)
     us_d1, by_d1 = eng.bench_linear(1, 2, 1, reps=20)
+    us_att = eng.bench_attention(0, a.k + 1, ctx_mid, reps=20)
+    us_att1 = eng.bench_attention(1, 1, ctx_mid, reps=20)
     kern_gbs = by_gu / (us_gu * 1e-6) / 1e9
 
     # End to end through the reference-facing API: speculative_generate() with
@@ -654,12 +688,11 @@ def main():
     lib.draft_model_free(dm)
 
     cpu = None
-    if keep_host:
-        v, ctoks, cacc, dec, margins = cpu_decode_sample(w, embed, prompt, a.k, a.cpu_tokens, os.cpu_count() or 1)
-        cpu = {"value": v, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
-               "sample": f"oracle decode loop of {a.cpu_tokens} tokens after the same {a.prompt_len}-token "
-                         f"prefill (prefill excluded)",
-               "parity": stream_parity(toks[:a.cpu_tokens], ctoks, margins)}
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        r = cpu_reference_decode(a, a.cpu_tokens, 0, 1)
+        cpu = {"value": r["value"], "unit": "tok/s", "cores": r["cores"], "kind": r["kind"],
+               "sample": f"one {a.cpu_tokens}-token speculative decode after the same {a.prompt_len}-token prefill "
+                         f"(prefill excluded)", "matmul": r["matmul"]}
 
     if rank == 0:
         line = {
@@ -667,12 +700,9 @@ def main():
             "warmup": a.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "u8xs8->s32, f32",
             "data": "synthetic (seeded N(0,0.02) -> Q4_0 -> INT8 weights, uniform prompt ids)",
-            "config": {"workload": f"phi3-mini int8 (32L d3072 ffn8192 vocab32064) + {DRAFT_LAYERS}-layer draft, "
-                                   f"greedy chain k={a.k}, bs1, prompt {a.prompt_len}, {a.new_tokens} new tokens "
-                                   f"per step", "parallelism": "replicas only" if world > 1 else "single GPU",
-                       "l2": "inputs larger than L2 (6.4 GB of weights per speculative step)",
-                       "step_path": "one persistent tcgen05 kernel per step" if eng.step_kernel()
-                       else "multi-kernel CUDA graph per step"},
+            "config": workload_config(a, world),
+            "step_path": "one persistent tcgen05 kernel per step" if eng.step_kernel()
+            else "multi-kernel CUDA graph per step",
             "spec": {"spec_steps_per_decode": spec_steps, "mean_accepted": float(acc_cat.mean()),
                      "accepted_hist": np.bincount(acc_cat, minlength=a.k + 1).tolist(),
                      "step_us": step_us, "step_bytes": step_bytes(a.k, ctx_mid), "step_gbs": step_gbs,
@@ -688,7 +718,8 @@ def main():
                          "others": {"qkv_M5": [us_qkv, by_qkv / (us_qkv * 1e-6) / 1e9],
                                     "o_M5": [us_o, by_o / (us_o * 1e-6) / 1e9],
                                     "down_M5": [us_dn, by_dn / (us_dn * 1e-6) / 1e9],
-                                    "draft_gateup_M1": [us_d1, by_d1 / (us_d1 * 1e-6) / 1e9]}},
+                                    "draft_gateup_M1": [us_d1, by_d1 / (us_d1 * 1e-6) / 1e9],
+                                    "attention_M%d_us" % (a.k + 1): us_att, "draft_attention_M1_us": us_att1}},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_val, "unit": "tok/s", "h2d_bytes_per_step": int(ph.nbytes),
                     "d2h_bytes_per_step": int(out.nbytes), "api": "speculative_generate (prefill included)",

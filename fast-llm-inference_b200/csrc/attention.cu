@@ -451,6 +451,283 @@ __global__ void __launch_bounds__(kDThreads) attention_split_kernel(const AttnPa
     if (threadIdx.x == 0) p.counters[hs] = 0;  // re-arm for the next launch
 }
 
+// Decode attention (M <= 8 new rows) as one thread-block cluster of kCl
+// CTAs per (head, sequence). The live context [0, base + M) is cut into kCl
+// contiguous key ranges (read from the device at run time, so a graph
+// captured once serves every context length); CTA r of the cluster streams
+// its range in 32-key tiles (16-byte cp.async copies, two tiles in flight),
+// keeps an online softmax per row, and leaves (max, sum, unnormalised P.V)
+// in its shared memory. After a cluster barrier every CTA combines a slice
+// of the (row, dimension) outputs from all kCl CTAs' shared memory in rank
+// order (deterministic), normalises and quantizes. No global scratch, no
+// arrival counter, no launch-size dependence on max_ctx. Same arithmetic as
+// inference.c:193-247 up to float rounding.
+constexpr int kCl = 8;         // CTAs per head (portable cluster size)
+constexpr int kCTile = 32;     // keys per tile
+constexpr int kCThreads = 128;
+constexpr int kCRes = kMaxHd + 4;  // per row: max, sum, o[hd] (keeps the tile buffers 16-byte aligned)
+
+__device__ __forceinline__ void cp16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ uint32_t cl_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// Cluster-wide barrier (all threads of all CTAs), release / acquire.
+__device__ __forceinline__ void cl_sync() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// Load a float from CTA `rank`'s shared memory at the address of `p` in this CTA.
+__device__ __forceinline__ float ld_dsmem(const float* p, uint32_t rank) {
+    uint32_t a = (uint32_t)__cvta_generic_to_shared(p), ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra));
+    return v;
+}
+
+// Dynamic shared memory of attention_cluster_kernel<MR> for head_dim hd.
+__host__ __device__ inline size_t cluster_smem(int MR, int hd) {
+    const int hd2 = hd / 2;
+    return sizeof(float) * ((size_t)MR * kMaxHd + (size_t)MR * kCTile + (size_t)MR * kCRes) +
+           sizeof(uint32_t) * 2 * (size_t)kCTile * ((hd2 + 4) + hd2);
+}
+
+template <int MR>
+__global__ void __launch_bounds__(kCThreads) attention_cluster_kernel(const AttnParams p) {
+    extern __shared__ __align__(16) float csm[];
+    __shared__ float m_run[MR], l_run[MR], alpha_s[MR];
+    pdl_trigger();
+    pdl_wait();
+    // Both early exits are uniform over the grid, so no CTA of a cluster
+    // is left waiting at the cluster barriers below.
+    if (p.done && *p.done) return;
+    const int M = p.dyn_M ? *p.dyn_M : p.M;
+    const int nr = min(M, MR);
+    if (nr <= 0) return;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t rank = cl_rank();
+    const int h = blockIdx.x / kCl;
+    const int sb = blockIdx.z;  // batched sequence
+    const int base = p.slot_base[sb * p.seq_state];
+    const size_t qrow0 = (size_t)sb * M;
+    const int ctx = base + M;
+    const int hd = p.head_dim, hd2 = hd >> 1, hd8 = hd2 >> 2, kst = hd2 + 4;
+    const int kvh = kv_head_of(p, h);
+    const int qd = p.heads * hd;
+    const int* btab = p.block_table + (sb * p.seq_slots) / kPageSize;
+
+    float* q_s = csm;                                 // [MR][kMaxHd]
+    float* sc = q_s + MR * kMaxHd;                    // [MR][kCTile]
+    float* res = sc + MR * kCTile;                    // [MR][kCRes]
+    uint32_t* Ks = reinterpret_cast<uint32_t*>(res + MR * kCRes);  // [2][kCTile][kst] half2
+    uint32_t* Vs = Ks + 2 * kCTile * kst;                          // [2][kCTile][hd2] half2
+
+    int chunk = (ctx + kCl - 1) / kCl;
+    chunk = (chunk + 15) & ~15;
+    const int k0 = (int)rank * chunk;
+    const int k1 = min(ctx, k0 + chunk);
+    const int ntiles = k1 > k0 ? (k1 - k0 + kCTile - 1) / kCTile : 0;
+    const uint32_t* kg = reinterpret_cast<const uint32_t*>(p.kv.k);
+    const uint32_t* vg = reinterpret_cast<const uint32_t*>(p.kv.v);
+    auto load_tile = [&](int t) {
+        const int t0 = k0 + t * kCTile;
+        const int nt = min(kCTile, k1 - t0);
+        uint32_t* Kb = Ks + (t & 1) * kCTile * kst;
+        uint32_t* Vb = Vs + (t & 1) * kCTile * hd2;
+        for (int i = tid; i < nt * hd8; i += kCThreads) {
+            const int key = i / hd8, c = (i - key * hd8) * 4;
+            const int slot = t0 + key;
+            const size_t off =
+                (((size_t)btab[slot / kPageSize] * p.kv_heads + kvh) * kPageSize + (slot % kPageSize)) * hd2 + c;
+            cp16(Kb + key * kst + c, kg + off);
+            cp16(Vb + key * hd2 + c, vg + off);
+        }
+        cp_commit();
+    };
+    if (ntiles > 0) load_tile(0);
+
+    for (int i = tid; i < nr * hd; i += kCThreads) {
+        const int rr = i / hd, dd = i - rr * hd;
+        q_s[rr * kMaxHd + dd] = p.q[(qrow0 + rr) * qd + (size_t)h * hd + dd];
+    }
+    if (tid < MR) {
+        m_run[tid] = -INFINITY;
+        l_run[tid] = 0.0f;
+    }
+    const float scale = __fdiv_rn(1.0f, sqrtf((float)hd));
+    // P.V mapping: thread -> (dimension pair d2, row group g of G)
+    const int G = kCThreads / hd2;
+    const int d2 = tid % hd2, g = tid / hd2;
+    const bool pv = g < G;
+    constexpr int kPR = (MR + 1) / 2;  // rows per P.V thread (G >= 2: head_dim <= 128)
+    float a0[kPR], a1[kPR];
+#pragma unroll
+    for (int i = 0; i < kPR; i++) a0[i] = a1[i] = 0.0f;
+
+    for (int t = 0; t < ntiles; t++) {
+        if (t + 1 < ntiles) {
+            load_tile(t + 1);
+            cp_wait<1>();
+        } else {
+            cp_wait<0>();
+        }
+        __syncthreads();  // tile t (and, first time round, q_s / m_run) visible
+        const int t0 = k0 + t * kCTile;
+        const int nt = min(kCTile, k1 - t0);
+        const uint32_t* Kb = Ks + (t & 1) * kCTile * kst;
+        const uint32_t* Vb = Vs + (t & 1) * kCTile * hd2;
+        {   // scores: thread -> key (tid % 32), rows rq, rq + 4, ...
+            const int key = tid & (kCTile - 1), rq = tid / kCTile;
+            constexpr int kRQ = (MR + 3) / 4;
+            if (key < nt) {
+                float acc[kRQ];
+#pragma unroll
+                for (int i = 0; i < kRQ; i++) acc[i] = 0.0f;
+                const uint4* kr = reinterpret_cast<const uint4*>(Kb + key * kst);
+                for (int e4 = 0; e4 < hd8; e4++) {
+                    const uint4 kw = kr[e4];
+                    const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&kw.x));
+                    const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&kw.y));
+                    const float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&kw.z));
+                    const float2 f3 = __half22float2(*reinterpret_cast<const __half2*>(&kw.w));
+#pragma unroll
+                    for (int i = 0; i < kRQ; i++) {
+                        const int rr = rq + 4 * i;
+                        if (rr < nr) {
+                            const float4 qa = *reinterpret_cast<const float4*>(&q_s[rr * kMaxHd + 8 * e4]);
+                            const float4 qb = *reinterpret_cast<const float4*>(&q_s[rr * kMaxHd + 8 * e4 + 4]);
+                            float s = acc[i];
+                            s = __fmaf_rn(qa.x, f0.x, s);
+                            s = __fmaf_rn(qa.y, f0.y, s);
+                            s = __fmaf_rn(qa.z, f1.x, s);
+                            s = __fmaf_rn(qa.w, f1.y, s);
+                            s = __fmaf_rn(qb.x, f2.x, s);
+                            s = __fmaf_rn(qb.y, f2.y, s);
+                            s = __fmaf_rn(qb.z, f3.x, s);
+                            s = __fmaf_rn(qb.w, f3.y, s);
+                            acc[i] = s;
+                        }
+                    }
+                }
+                const int j = t0 + key;
+#pragma unroll
+                for (int i = 0; i < kRQ; i++) {
+                    const int rr = rq + 4 * i;
+                    if (rr < nr) {
+                        bool vis = true;
+                        if (j >= base) {
+                            const int jj = j - base;
+                            vis = p.mask ? (p.mask[(size_t)rr * M + jj] != 0) : (jj <= rr);
+                        }
+                        sc[rr * kCTile + key] = vis ? __fmul_rn(acc[i], scale) : -INFINITY;
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < kRQ; i++) {
+                    const int rr = rq + 4 * i;
+                    if (rr < nr) sc[rr * kCTile + key] = -INFINITY;
+                }
+            }
+        }
+        __syncthreads();
+        // online softmax: warp w -> rows w, w + 4; lane -> key
+        for (int rr = warp; rr < nr; rr += 4) {
+            const float s = sc[rr * kCTile + lane];
+            const float mx = warp_max(s);
+            const float m_old = m_run[rr];
+            const float m_new = fmaxf(m_old, mx);
+            const float e = (s == -INFINITY) ? 0.0f : expf(__fsub_rn(s, m_new));
+            sc[rr * kCTile + lane] = e;
+            const float sum = warp_sum(e);
+            if (lane == 0) {
+                const float al = (m_old == -INFINITY) ? 0.0f : expf(__fsub_rn(m_old, m_new));
+                alpha_s[rr] = al;
+                l_run[rr] = __fmaf_rn(l_run[rr], al, sum);
+                m_run[rr] = m_new;
+            }
+        }
+        __syncthreads();
+        if (pv) {
+#pragma unroll
+            for (int i = 0; i < kPR; i++) {
+                const int rr = g + G * i;
+                if (rr < nr) {
+                    a0[i] *= alpha_s[rr];
+                    a1[i] *= alpha_s[rr];
+                }
+            }
+            for (int tt = 0; tt < nt; tt++) {
+                const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&Vb[tt * hd2 + d2]));
+#pragma unroll
+                for (int i = 0; i < kPR; i++) {
+                    const int rr = g + G * i;
+                    if (rr < nr) {
+                        const float w = sc[rr * kCTile + tt];
+                        a0[i] = __fmaf_rn(w, v.x, a0[i]);
+                        a1[i] = __fmaf_rn(w, v.y, a1[i]);
+                    }
+                }
+            }
+        }
+        __syncthreads();  // this tile's buffers and scores are free again
+    }
+    // this CTA's partial result
+    if (pv) {
+#pragma unroll
+        for (int i = 0; i < kPR; i++) {
+            const int rr = g + G * i;
+            if (rr < nr) {
+                res[rr * kCRes + 2 + 2 * d2] = a0[i];
+                res[rr * kCRes + 3 + 2 * d2] = a1[i];
+            }
+        }
+    }
+    if (tid < nr) {
+        res[tid * kCRes] = m_run[tid];
+        res[tid * kCRes + 1] = l_run[tid];
+    }
+    cl_sync();
+    // combine: element i of [nr][hd] is handled by CTA i / kCThreads % kCl
+    for (int i = (int)rank * kCThreads + tid; i < nr * hd; i += kCl * kCThreads) {
+        const int rr = i / hd, dd = i - rr * hd;
+        // all remote loads issued before any is used: two round trips
+        float mv[kCl], lv[kCl], ov[kCl];
+#pragma unroll
+        for (int c = 0; c < kCl; c++) {
+            mv[c] = ld_dsmem(&res[rr * kCRes], (uint32_t)c);
+            lv[c] = ld_dsmem(&res[rr * kCRes + 1], (uint32_t)c);
+            ov[c] = ld_dsmem(&res[rr * kCRes + 2 + dd], (uint32_t)c);
+        }
+        float gm = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < kCl; c++) gm = fmaxf(gm, mv[c]);
+        float L = 0.0f, O = 0.0f;
+#pragma unroll
+        for (int c = 0; c < kCl; c++) {
+            if (mv[c] == -INFINITY) continue;
+            const float wgt = expf(__fsub_rn(mv[c], gm));
+            L = __fmaf_rn(lv[c], wgt, L);
+            O = __fmaf_rn(ov[c], wgt, O);
+        }
+        const float o = __fdiv_rn(O, L);
+        const size_t idx = (qrow0 + rr) * qd + (size_t)h * hd + dd;
+        p.out_q[idx] = (uint8_t)quant_u8(o);
+        if (p.out_f) p.out_f[idx] = o;
+    }
+    cl_sync();  // no CTA leaves while another still reads its shared memory
+}
+
 size_t attention_smem() {
     const size_t f = (size_t)kARows * kMaxHd + (size_t)kARows * kTile;
     const size_t kv = (size_t)kTile * (kMaxHd / 2 + 1) + (size_t)kTile * (kMaxHd / 2);
@@ -493,11 +770,49 @@ cudaError_t launch_split(const AttnParams& p, cudaStream_t s, bool pdl) {
     return cudaLaunchKernelEx(&cfg, attention_split_kernel<MR>, p);
 }
 
+template <int MR>
+cudaError_t launch_cluster(const AttnParams& p, cudaStream_t s, bool pdl) {
+    auto kern = attention_cluster_kernel<MR>;
+    const size_t smem = cluster_smem(MR, p.head_dim);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.heads * kCl, 1, p.seqs > 1 ? p.seqs : 1);
+    cfg.blockDim = dim3(kCThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kCl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+#ifndef FL_ATTN_CLUSTER
+#define FL_ATTN_CLUSTER 1
+#endif
+// Contexts up to this many slots take the cluster kernel (each CTA streams
+// at most a 256-key range); longer ones the page-split kernel.
+constexpr int kClusterMaxCtx = 2048;
+
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl) {
     if (p.head_dim > kMaxHd || p.head_dim < 64 || p.head_dim % 2 != 0 || (p.group <= 0 && p.heads % p.kv_heads != 0))
         return cudaErrorInvalidValue;
     // batched sequences: static rows, page-aligned regions, grid z <= 65535
     if (p.seqs > 1 && (p.dyn_M || p.seq_slots % kPageSize != 0 || p.seqs > 65535)) return cudaErrorInvalidValue;
+    if (FL_ATTN_CLUSTER && p.M <= kMaxRows && p.head_dim % 8 == 0 && p.max_ctx <= kClusterMaxCtx) {
+        if (p.M <= 1) return launch_cluster<1>(p, s, pdl);
+        if (p.M <= 2) return launch_cluster<2>(p, s, pdl);
+        if (p.M <= 4) return launch_cluster<4>(p, s, pdl);
+        return launch_cluster<8>(p, s, pdl);
+    }
     if (p.M <= kMaxRows && p.part && p.counters) {
         // grid.y covers every page the context can reach; the partial layout
         // indexes (head, split) with gridDim.y, so max_ctx must be the one the

@@ -1473,6 +1473,52 @@ FL_API int fl_engine_bench_linear(fl_engine_t* e, int stack, int kind, int M, in
     return FL_OK;
 }
 
+FL_API int fl_engine_bench_attention(fl_engine_t* e, int stack, int M, int ctx, int reps, double* us_per_launch) {
+    FL_CHECK(check_ready(e, stack == 1));
+    if (M < 1 || M > kMaxRows || ctx < M || ctx > e->c.max_seq_len || reps < 1)
+        return set_error(FL_E_INVAL, "bench_attention: bad arguments");
+    Stack& S = stack == 0 ? e->base : e->draft;
+    cudaGraph_t g = nullptr;
+    FL_CHECK_CUDA(cudaStreamBeginCapture(e->s, cudaStreamCaptureModeThreadLocal));
+    int rc = FL_OK;
+    for (int l = 0; l < S.nl && rc == FL_OK; l++) {
+        AttnParams at = {};
+        at.q = e->q;
+        at.kv = S.kv[l];
+        at.block_table = S.block_table;
+        at.slot_base = e->iota + (ctx - M);
+        at.M = M;
+        at.heads = e->H;
+        at.kv_heads = e->Hkv;
+        at.head_dim = e->hd;
+        at.max_ctx = e->c.max_seq_len;
+        at.out_q = e->aq;
+        at.part = e->attn_part;
+        at.counters = e->attn_cnt;
+        if (launch_attention(at, e->s, true) != cudaSuccess) rc = set_error(FL_E_CUDA, "bench_attention launch");
+    }
+    cudaError_t ce = cudaStreamEndCapture(e->s, &g);
+    if (rc != FL_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    FL_CHECK_CUDA(ce);
+    cudaGraphExec_t ex = nullptr;
+    ce = cudaGraphInstantiate(&ex, g, 0);
+    cudaGraphDestroy(g);
+    FL_CHECK_CUDA(ce);
+    FL_CHECK_CUDA(cudaGraphLaunch(ex, e->s));  // warm-up
+    FL_CHECK_CUDA(cudaEventRecord(e->ev[2], e->s));
+    for (int r = 0; r < reps; r++) FL_CHECK_CUDA(cudaGraphLaunch(ex, e->s));
+    FL_CHECK_CUDA(cudaEventRecord(e->ev[3], e->s));
+    FL_CHECK_CUDA(cudaEventSynchronize(e->ev[3]));
+    cudaGraphExecDestroy(ex);
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, e->ev[2], e->ev[3]);
+    if (us_per_launch) *us_per_launch = ms * 1000.0 / ((double)reps * S.nl);
+    return FL_OK;
+}
+
 // ---------------------------------------------------------------------------
 // Callback-level API: the engine as the reference's target_forward /
 // base_forward model, with an explicit base-cache position.

@@ -761,7 +761,9 @@ FL_API int fl_engine_batch_tree_generate(fl_engine_t* e, const int* prompts, int
     if (!prompts || !out || P <= 0 || nseq <= 0 || n_new <= 0 || K < 1 || K > kMaxDraft || width < 1 || width > 32 ||
         Mt > 256)
         return set_error(FL_E_INVAL, "batch_tree_generate: bad arguments");
-    if (nseq > B.cap || P + n_new + Mt + K + 3 > B.slots || nseq * Mt > e->R)
+    // the per-sequence prefill embeds P + 1 rows into the engine's R-row
+    // activation buffers, so the prompt is bounded by R as well as the slots
+    if (nseq > B.cap || P + n_new + Mt + K + 3 > B.slots || nseq * Mt > e->R || P + 2 > e->R)
         return set_error(FL_E_INVAL, "batch_tree_generate: batch or context larger than the reservation");
     if (e->samp) return set_error(FL_E_UNSUPPORTED, "batch_tree_generate: the tree decode is greedy");
     if (e->d % 128 != 0) return set_error(FL_E_UNSUPPORTED, "batch: the hidden size must be a multiple of 128");

@@ -163,6 +163,7 @@ _SIGS = {
     "fl_engine_draft_bound": (I, [VP, VP]),
     "fl_engine_note_draft": (None, [VP, VP]),
     "fl_engine_bench_linear": (I, [VP, I, I, I, I, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
+    "fl_engine_bench_attention": (I, [VP, I, I, I, I, C.POINTER(C.c_double)]),
     "fl_engine_position": (I, [VP]),
     "fl_engine_set_position": (I, [VP, I]),
     "fl_cuda_base_forward": (None, [VP, VP, I, VP, I]),
@@ -560,6 +561,12 @@ class Engine:
         t = np.zeros((64, 8), np.uint64)
         self.lib.fl_engine_step_trace_stages(self.h, ptr(t))
         return t
+
+    def bench_attention(self, stack, M, ctx, reps=10):
+        us = C.c_double()
+        self.lib.check(self.lib.fl_engine_bench_attention(self.h, stack, M, ctx, reps, C.byref(us)),
+                       "bench_attention")
+        return us.value
 
     def bench_linear(self, stack, kind, M, reps=10):
         us, by = C.c_double(), C.c_double()

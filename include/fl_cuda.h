@@ -95,9 +95,12 @@ int fl_cuda_block_dots_i8(const float* A, const dequantized_tensor_t* B, int32_t
  * HBM (KV page pools sized to the free memory). `stream` may be NULL only
  * after fl_cuda_init() created the library stream of the device. The first
  * call on a device resolves the scratch address (cudaGetSymbolAddress,
- * which may load the module); make it before any stream capture. Calls that
- * overlap in time (other streams or threads on the same device) race on
- * the one scratch; calls on one stream are ordered. */
+ * which may load the module); make it before any stream capture. The
+ * address is kept for the life of the process: after cudaDeviceReset of a
+ * device the kept address is stale, so this entry point must not be used on
+ * that device again. Calls that overlap in time (other streams or threads on
+ * the same device) race on the one scratch; calls on one stream are
+ * ordered. */
 #define FL_NOALLOC_SCRATCH_BYTES (1 << 20)
 int fl_cuda_block_dots_i8_noalloc(const float* A, const dequantized_tensor_t* B, int32_t* D,
                                   int M, int N, int K, void* stream);
@@ -418,6 +421,10 @@ void fl_engine_note_draft(fl_engine_t* e, const void* draft);
  * replayed reps times, and the algorithmic bytes of one launch. */
 int fl_engine_bench_linear(fl_engine_t* e, int stack, int kind, int M, int reps,
                            double* us_per_launch, double* bytes_per_launch);
+/* Device time per launch of the decode attention of every layer of a stack:
+ * M new rows over a context of ctx slots (the cache's current contents),
+ * captured back to back and replayed reps times. */
+int fl_engine_bench_attention(fl_engine_t* e, int stack, int M, int ctx, int reps, double* us_per_launch);
 
 /* Callback-level position of the base cache: tokens appended through
  * fl_cuda_target_forward / fl_cuda_base_forward land at this position.

@@ -32,7 +32,7 @@ class Dims(C.Structure):
 
 
 class Lin(C.Structure):
-    _fields_ = [("w", VP), ("s", VP), ("N", I), ("K", I), ("f32", VP)]
+    _fields_ = [("w", VP), ("s", VP), ("N", I), ("K", I), ("f32", VP), ("rs", VP)]
 
 
 class Layer(C.Structure):
@@ -108,6 +108,11 @@ class Oracle:
         s.orc_q4_0_quantize_i8.argtypes = [VP, I, VP, VP]
         s.orc_philox4x32_10.argtypes = [VP, VP, VP]
         s.orc_argmax.argtypes = [VP, I]
+        s.orc_synth_q4_0_i8.restype = I
+        s.orc_synth_q4_0_i8.argtypes = [C.c_uint64, C.c_uint32, I, I, C.c_float, VP, VP]
+        s.orc_synth_q4_0_f32.restype = I
+        s.orc_synth_q4_0_f32.argtypes = [C.c_uint64, C.c_uint32, I, I, C.c_float, VP]
+        s.orc_set_ref_matmul.argtypes = [VP]
         s.orc_last_decode_seconds.restype = C.c_double
 
     # ----------------------------------------------------------- primitives
@@ -167,6 +172,17 @@ class Oracle:
         self.so.orc_rope_vec(_p(v), heads, head_dim, pos, theta)
         return v
 
+    def synth_q4_0_i8(self, seed, tid, rows, cols, std=0.02):
+        w = np.empty((rows, cols), np.int8)
+        d = np.empty((rows, cols // 32), np.uint16)
+        assert self.so.orc_synth_q4_0_i8(seed, tid, rows, cols, std, _p(w), _p(d)) == 0
+        return w, d
+
+    def synth_q4_0_f32(self, seed, tid, rows, cols, std=0.02):
+        o = np.empty((rows, cols), np.float32)
+        assert self.so.orc_synth_q4_0_f32(seed, tid, rows, cols, std, _p(o)) == 0
+        return o
+
     def q4_0_i8(self, x):
         x = np.ascontiguousarray(x, np.float32)
         w = np.empty(x.size, np.int8)
@@ -223,7 +239,7 @@ class OracleModel:
     """Oracle model over numpy weights. `w` maps (stack, layer, proj) to
     (int8 [N,K], fp16 bits [N,K/32]); stack 3 proj 1 = LM head."""
 
-    def __init__(self, orc: Oracle, dims: dict, embed, w, draft_layers=0, n_medusa=0, f32=None):
+    def __init__(self, orc: Oracle, dims: dict, embed, w, draft_layers=0, n_medusa=0, f32=None, ref_rows=None):
         self.orc = orc
         self.keep = [embed]
         self.m = Model()
@@ -239,6 +255,14 @@ class OracleModel:
                 self.keep.append(a)
                 L.f32 = _p(a)
                 L.N, L.K = a.shape
+                return L
+            if ref_rows is not None and key in ref_rows:
+                # the reference's per-row-scale tensor, run by the installed
+                # reference matmul (orc_set_ref_matmul)
+                wr, rs = ref_rows[key]
+                self.keep += [wr, rs]
+                L.w, L.rs = _p(wr), _p(rs)
+                L.N, L.K = wr.shape
                 return L
             wq, dq = w[key]
             self.keep += [wq, dq]

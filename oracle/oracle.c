@@ -151,23 +151,59 @@ void orc_matmul_rowscale(const float* A, const int8_t* W, const float* scales,
     free(q);
 }
 
+/* Eight consecutive 32-element block dots in one vector (lane j = block j),
+ * each the maddubs + madd sum of block_dot32. */
+static inline __m256i block_dots8(const uint8_t* a, const int8_t* w) {
+    const __m256i one = _mm256_set1_epi16(1);
+    __m256i p[8];
+    for (int j = 0; j < 8; j++) {
+        const __m256i va = _mm256_loadu_si256((const __m256i*)(a + 32 * j));
+        const __m256i vw = _mm256_loadu_si256((const __m256i*)(w + 32 * j));
+        p[j] = _mm256_madd_epi16(_mm256_maddubs_epi16(va, vw), one);
+    }
+    const __m256i s01 = _mm256_hadd_epi32(p[0], p[1]), s23 = _mm256_hadd_epi32(p[2], p[3]);
+    const __m256i s45 = _mm256_hadd_epi32(p[4], p[5]), s67 = _mm256_hadd_epi32(p[6], p[7]);
+    const __m256i s0123 = _mm256_hadd_epi32(s01, s23), s4567 = _mm256_hadd_epi32(s45, s67);
+    /* s0123 = [b0 b1 b2 b3 (low halves) | b0 b1 b2 b3 (high halves)], same for 4..7 */
+    return _mm256_add_epi32(_mm256_permute2x128_si256(s0123, s4567, 0x20),
+                            _mm256_permute2x128_si256(s0123, s4567, 0x31));
+}
+
+/* Per block: t = (float)dot * scale (one rounding), acc = acc + t in block
+ * order (matmul_dequantized's per-row accumulation, one scale per block).
+ * Eight blocks' dots and products are formed in vectors; the adds stay
+ * sequential, so the result is that of the one-block-at-a-time loop. */
 static void matmul_block_q(const uint8_t* q, const int8_t* W, const uint16_t* S,
                            float* C, int M, int N, int K) {
     const int nb = K / 32;
-#pragma omp parallel for schedule(static)
-    for (int n = 0; n < N; n++) {
-        const int8_t* wr = W + (size_t)n * K;
-        const uint16_t* sr = S + (size_t)n * nb;
-        for (int m = 0; m < M; m++) {
-            const uint8_t* qa = q + (size_t)m * K;
-            float acc = 0.0f;
-            for (int b = 0; b < nb; b++) {
-                int32_t dot = block_dot32(qa + 32 * b, wr + 32 * b);
-                float t = (float)dot * orc_f16_to_f32(sr[b]);
-                acc = acc + t;
+#pragma omp parallel
+    {
+        float* sf = (float*)malloc(sizeof(float) * (size_t)nb);
+#pragma omp for schedule(static)
+        for (int n = 0; n < N; n++) {
+            const int8_t* wr = W + (size_t)n * K;
+            const uint16_t* sr = S + (size_t)n * nb;
+            for (int b = 0; b < nb; b++) sf[b] = orc_f16_to_f32(sr[b]);
+            for (int m = 0; m < M; m++) {
+                const uint8_t* qa = q + (size_t)m * K;
+                float acc = 0.0f;
+                int b = 0;
+                for (; b + 8 <= nb; b += 8) {
+                    const __m256 t8 = _mm256_mul_ps(_mm256_cvtepi32_ps(block_dots8(qa + 32 * b, wr + 32 * b)),
+                                                    _mm256_loadu_ps(sf + b));
+                    float t[8];
+                    _mm256_storeu_ps(t, t8);
+                    for (int j = 0; j < 8; j++) acc = acc + t[j];
+                }
+                for (; b < nb; b++) {
+                    int32_t dot = block_dot32(qa + 32 * b, wr + 32 * b);
+                    float t = (float)dot * sf[b];
+                    acc = acc + t;
+                }
+                C[(size_t)m * N + n] = acc / 127.0f;
             }
-            C[(size_t)m * N + n] = acc / 127.0f;
         }
+        free(sf);
     }
 }
 
@@ -291,6 +327,71 @@ void orc_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t ou
 }
 
 /* ------------------------------------------------------------------ */
+/* seeded synthetic weights (the library's generator, restated)        */
+/* ------------------------------------------------------------------ */
+
+static double unit_open(uint32_t x) { return ((double)(x >> 8) + 0.5) * (1.0 / 16777216.0); }
+
+/* Values [start, start + n) of a tensor's normal sequence (start % 4 == 0
+ * whenever cols % 32 == 0). */
+static void synth_normals(uint64_t seed, uint32_t tid, uint64_t start, int n, float std, float* out) {
+    const uint32_t key[2] = {(uint32_t)seed, (uint32_t)(seed >> 32)};
+    uint64_t g = start >> 2;
+    int off = (int)(start & 3), i = 0;
+    const double two_pi = 6.283185307179586476925;
+    while (i < n) {
+        const uint32_t ctr[4] = {(uint32_t)g, (uint32_t)(g >> 32), tid, 0x5EEDu};
+        uint32_t o[4];
+        orc_philox4x32_10(ctr, key, o);
+        double z[4];
+        for (int h = 0; h < 2; h++) {
+            const double r = sqrt(-2.0 * log(unit_open(o[2 * h])));
+            const double t = two_pi * unit_open(o[2 * h + 1]);
+            z[2 * h] = r * cos(t);
+            z[2 * h + 1] = r * sin(t);
+        }
+        for (int l = off; l < 4 && i < n; l++, i++) out[i] = (float)(z[l] * (double)std);
+        off = 0;
+        g++;
+    }
+}
+
+int orc_synth_q4_0_i8(uint64_t seed, uint32_t tensor_id, int rows, int cols, float std, int8_t* w, uint16_t* d) {
+    if (!w || !d || rows <= 0 || cols <= 0 || cols % 32 != 0) return -1;
+#pragma omp parallel
+    {
+        float* buf = (float*)malloc(sizeof(float) * (size_t)cols);
+#pragma omp for schedule(static)
+        for (int r = 0; r < rows; r++) {
+            synth_normals(seed, tensor_id, (uint64_t)r * cols, cols, std, buf);
+            orc_q4_0_quantize_i8(buf, cols, w + (size_t)r * cols, d + (size_t)r * (cols / 32));
+        }
+        free(buf);
+    }
+    return 0;
+}
+
+int orc_synth_q4_0_f32(uint64_t seed, uint32_t tensor_id, int rows, int cols, float std, float* out) {
+    if (!out || rows <= 0 || cols <= 0 || cols % 32 != 0) return -1;
+#pragma omp parallel
+    {
+        float* buf = (float*)malloc(sizeof(float) * (size_t)cols);
+        int8_t* w = (int8_t*)malloc((size_t)cols);
+        uint16_t* d = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)(cols / 32));
+#pragma omp for schedule(static)
+        for (int r = 0; r < rows; r++) {
+            synth_normals(seed, tensor_id, (uint64_t)r * cols, cols, std, buf);
+            orc_q4_0_quantize_i8(buf, cols, w, d);
+            for (int j = 0; j < cols; j++) out[(size_t)r * cols + j] = (float)w[j] * orc_f16_to_f32(d[j / 32]);
+        }
+        free(buf);
+        free(w);
+        free(d);
+    }
+    return 0;
+}
+
+/* ------------------------------------------------------------------ */
 /* model                                                               */
 /* ------------------------------------------------------------------ */
 
@@ -307,7 +408,14 @@ void orc_kv_free(orc_kv_t* kv) {
     kv->k = kv->v = NULL;
 }
 
+static orc_ref_matmul_fn g_ref_mm = NULL;
+void orc_set_ref_matmul(orc_ref_matmul_fn fn) { g_ref_mm = fn; }
+
 static void lin(const orc_lin_t* L, const float* x, float* y, int M) {
+    if (L->rs && g_ref_mm) {
+        g_ref_mm(x, L->w, L->rs, y, M, L->N, L->K);
+        return;
+    }
     if (L->f32) { /* inference.c:131-141 */
         for (int m = 0; m < M; m++)
             for (int o = 0; o < L->N; o++) {

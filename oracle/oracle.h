@@ -85,6 +85,19 @@ void orc_q4_0_quantize_i8(const float* x, int n, int8_t* w, uint16_t* d);
 /* Philox4x32-10 (Salmon et al., SC'11). */
 void orc_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t out[4]);
 
+/* The library's seeded synthetic weights (fl_synth_q4_0_i8 / _f32 of
+ * include/fl_cuda.h), restated so that CPU-only runs need no product code:
+ * N(0, std) from Philox4x32-10 (key = seed, counter = (element / 4, tensor
+ * id, 0x5EED)) and Box-Muller in double precision, quantized to Q4_0 blocks
+ * (orc_q4_0_quantize_i8), int8 q-8 plus fp16 scales; _f32 dequantizes. */
+int orc_synth_q4_0_i8(uint64_t seed, uint32_t tensor_id, int rows, int cols, float std, int8_t* w, uint16_t* d);
+int orc_synth_q4_0_f32(uint64_t seed, uint32_t tensor_id, int rows, int cols, float std, float* out);
+
+/* Installs (or, with NULL, removes) the reference matmul used by layers
+ * whose orc_lin_t.rs is set: fn(A, W, row_scales, C, M, N, K). */
+typedef void (*orc_ref_matmul_fn)(const float*, const int8_t*, const float*, float*, int, int, int);
+void orc_set_ref_matmul(orc_ref_matmul_fn fn);
+
 /* ---------------- model ---------------- */
 
 typedef struct {
@@ -100,6 +113,12 @@ typedef struct {
      * reference's f32 matvec (inference.c:131-141) instead of INT8; used to
      * pin the layer composition against the reference's model_forward. */
     const float* f32;
+    /* When non-NULL and a reference matmul is installed (orc_set_ref_matmul),
+     * the layer runs that function on `w` as the reference's per-row-scale
+     * tensor (dequantized_tensor.c:27-58 format: (q-8)*16, one scale per row
+     * rs[N]) -- the reference's own compiled CPU kernel, for timing it on the
+     * path; its arithmetic is the reference's, not the block-scaled rule. */
+    const float* rs;
 } orc_lin_t;
 
 typedef struct {

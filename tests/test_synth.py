@@ -74,3 +74,14 @@ def test_block_synthesis_is_a_slice(lib):
         assert np.array_equal(db, d[r0:r0 + nr, c0 // 32:(c0 + nc) // 32])
     wb = np.empty((4, 30), np.int8)
     assert lib.fl_synth_q4_0_i8_block(9, 77, rows, cols, 0, 4, 2, 30, 0.02, ptr(wb), ptr(wb)) != 0
+
+
+def test_oracle_generator_equals_library(lib, orc):
+    """The oracle's restatement of the seeded generator (used where no
+    product code may run, e.g. the CPU baseline) gives the library's bits."""
+    for seed, tid, rows, cols, std in ((1, tensor_id(0, 0, 0), 9, 3072, 0.02), (7, tensor_id(3, 0, 0), 5, 96, 50.0),
+                                       (2 ** 40 + 3, tensor_id(1, 2, 6), 3, 8192, 0.02)):
+        w, d = lib.synth_q4_0_i8(seed, tid, rows, cols, std)
+        w2, d2 = orc.synth_q4_0_i8(seed, tid, rows, cols, std)
+        assert np.array_equal(w, w2) and np.array_equal(d, d2)
+        assert np.array_equal(lib.synth_q4_0_f32(seed, tid, rows, cols, std), orc.synth_q4_0_f32(seed, tid, rows, cols, std))

@@ -6,8 +6,9 @@ after every other test; it must pass alone as well.
 - CPU: a call whose M * K exceeds the scratch fails with FL_E_INVAL before
   touching the device;
 - GPU: two calls in a row on one stream give exactly the integers of the
-  allocating entry point, in block and per-row tensor modes, up to a call
-  that fills the whole scratch.
+  allocating entry point and of the oracle's pair-saturated block dots, in
+  block and per-row tensor modes, up to a call that fills the whole scratch;
+  the same on a caller-created stream passed explicitly.
 """
 import ctypes as C
 
@@ -31,16 +32,16 @@ def test_oversize_rejected_without_device(lib):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("mode", ["block", "row"])
-def test_noalloc_matches_allocating_entry_point(gpu, mode):
+def test_noalloc_matches_allocating_entry_point(gpu, orc, mode):
     from test_gemv_gpu import Dev
     lib = gpu
     rng = np.random.default_rng(77)
     cases = [(5, 1100, 3072), (3, 333, 8192), (SCRATCH // 8192, 64, 8192)]  # the last fills the scratch
-    tensors, inputs = [], []
+    tensors, inputs, host = [], [], []
     for M, N, K in cases:
         if mode == "block":
-            w, d = lib.synth_q4_0_i8(17, 5000 + N + K, N, K)
-            t = block_tensor(w, d)
+            W, d = lib.synth_q4_0_i8(17, 5000 + N + K, N, K)
+            t = block_tensor(W, d)
         else:
             W = np.clip((rng.integers(0, 16, (N, K)) - 8) * 16, -128, 127).astype(np.int8)
             t = row_tensor(W, (rng.random(N) * 0.01 + 1e-4).astype(np.float32))
@@ -48,6 +49,7 @@ def test_noalloc_matches_allocating_entry_point(gpu, mode):
         A = rng.standard_normal((M, K)).astype(np.float32)
         tensors.append(t)
         inputs.append(Dev(lib, A.nbytes).put(A))
+        host.append((A, W))
     for i in range(0, len(cases), 2):
         pair = cases[i:i + 2]
         outs = []
@@ -64,3 +66,33 @@ def test_noalloc_matches_allocating_entry_point(gpu, mode):
                       "dots")
             want = dW.get(np.empty((M, N, K // 32), np.int32))
             assert np.array_equal(got, want), f"case {pair[j]} differs"
+            A, W = host[i + j]
+            assert np.array_equal(got, orc.block_dots(A, W)), f"case {pair[j]} differs from the oracle"
+
+
+@pytest.mark.gpu
+def test_noalloc_on_caller_stream(gpu, orc):
+    """The stream argument: two calls in a row on a stream the caller made,
+    read back after synchronising that stream, equal the oracle's dots."""
+    import torch
+    from test_gemv_gpu import Dev
+    lib = gpu
+    rng = np.random.default_rng(78)
+    s = torch.cuda.Stream()
+    M, N, K = 4, 700, 3072
+    W, d = lib.synth_q4_0_i8(19, 6000, N, K)
+    t = block_tensor(W, d)
+    lib.check(lib.fl_cuda_upload_tensor(C.byref(t)), "upload")
+    lib.check(lib.fl_cuda_sync(), "sync")
+    outs = []
+    for call in range(2):
+        A = rng.standard_normal((M, K)).astype(np.float32)
+        dA = Dev(lib, A.nbytes).put(A)
+        dD = Dev(lib, M * N * (K // 32) * 4)
+        lib.check(lib.fl_cuda_block_dots_i8_noalloc(dA.p, C.byref(t), dD.p, M, N, K, C.c_void_p(s.cuda_stream)),
+                  "noalloc on a caller stream")
+        outs.append((A, dA, dD))
+    s.synchronize()
+    for A, _, dD in outs:
+        got = dD.get(np.empty((M, N, K // 32), np.int32))
+        assert np.array_equal(got, orc.block_dots(A, W))
