@@ -453,13 +453,71 @@ def run_medusa(a):
     return 0
 
 
+SHARD_T, SHARD_TOP_P, SHARD_SEED = 0.8, 0.95, 1234
+
+
+def sharded_decode(a, dist, rank, nranks, local):
+    """Config 3's sequences decoded by ranks 0 .. nranks - 1 (each its share
+    as one in-GPU batch, no collective on the data path); ranks at or past
+    nranks only take part in the barriers. Returns (slowest rank's seconds
+    with prefills, slowest decode seconds, speculative steps, stream
+    checksum over all sequences, launches of this rank)."""
+    import torch
+    import flb200
+    import shard
+    lib = flb200.Lib()
+    lib.check(lib.fl_cuda_init(local), "init")
+    max_seq = ((a.prompt_len + a.new_tokens + a.k + 2 + 63) // 64) * 64
+    ids = shard.shard_of(a.seqs, rank, nranks) if rank < nranks else []
+    eng = None
+    if ids:
+        eng = flb200.Engine(lib, engine_cfg(max_seq), local)
+        eng.synthesize(SEED)
+        eng.set_sampling(SHARD_T, SHARD_TOP_P, SHARD_SEED)
+        # KV regions reserved once, outside the timed region; warm-up on as
+        # many other sequences (same batch size: the same kernels and tiles)
+        eng.batch_reserve(len(ids), a.prompt_len + a.new_tokens + a.k + 3)
+        wid = list(range(a.seqs + rank * len(ids), a.seqs + (rank + 1) * len(ids)))
+        warm = shard.prompts_for(wid, 64, DIMS["vocab"], PROMPT_SEED)
+        for _ in range(max(a.warmup, 3)):
+            eng.spec_generate_batch(warm, 16, a.k, seq_ids=wid)
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    barrier()
+    torch.cuda.synchronize()
+    secs = dec = 0.0
+    nsteps, launches, toks, got_ids = 0, 0, np.zeros((0, a.new_tokens), np.int32), []
+    if ids:
+        got_ids, toks, steps, secs = shard.run_shard(eng, ids, a.prompt_len, a.new_tokens, a.k, DIMS["vocab"],
+                                                     PROMPT_SEED)
+        dec = eng.last_timing()[1] * 1e-6  # decode loops alone
+        launches = eng.last_launches()
+        nsteps = int(steps.sum())
+    torch.cuda.synchronize()
+    barrier()
+    if dist:
+        t = torch.tensor([secs, dec], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        secs, dec = float(t[0].item()), float(t[1].item())
+        full = shard.gather_tokens(dist, list(got_ids), toks, a.seqs)
+        t = torch.tensor([nsteps], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t)
+        nsteps = int(t.item())
+    else:
+        full = toks
+    if eng:
+        eng.close()
+    return secs, dec, nsteps, int(np.asarray(full, np.int64).sum()), launches
+
+
 def run_sampled_batch(a):
     """Independent sampled sequences sharded across ranks (see the module
     docstring); one timed pass over each rank's share."""
     import datetime
     import torch
-    import flb200
-    import shard
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -468,78 +526,42 @@ def run_sampled_batch(a):
         import torch.distributed as dist
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
-    T, top_p, seed = 0.8, 0.95, 1234
-    lib = flb200.Lib()
-    lib.check(lib.fl_cuda_init(local), "init")
-    max_seq = ((a.prompt_len + a.new_tokens + a.k + 2 + 63) // 64) * 64
-    eng = flb200.Engine(lib, engine_cfg(max_seq), local)
-    eng.synthesize(SEED)
-    eng.set_sampling(T, top_p, seed)
-    ids = shard.shard_of(a.seqs, rank, world)
-    # this rank's sequences decode as one in-GPU batch: its KV regions are
-    # reserved once, outside the timed region
-    eng.batch_reserve(max(1, len(ids)), a.prompt_len + a.new_tokens + a.k + 3)
-    # warm-up: short decodes of as many sequences outside the measured set
-    # (same batch size: the same kernels and GEMM tiles)
-    wid = list(range(a.seqs + rank * len(ids), a.seqs + (rank + 1) * len(ids))) or [a.seqs + rank]
-    warm = shard.prompts_for(wid, 64, DIMS["vocab"], PROMPT_SEED)
-    for _ in range(max(a.warmup, 3)):
-        eng.spec_generate_batch(warm, 16, a.k, seq_ids=wid)
-
-    def barrier():
-        if dist:
-            dist.barrier()
-
     clocks = Clocks(local)
-    barrier()
-    torch.cuda.synchronize()
     clocks.start()
-    got_ids, toks, steps, secs = shard.run_shard(eng, ids, a.prompt_len, a.new_tokens, a.k, DIMS["vocab"],
-                                                 PROMPT_SEED)
-    dec = eng.last_timing()[1] * 1e-6 if len(ids) else 0.0  # decode loops alone
-    launches = eng.last_launches() if len(ids) else 0
-    torch.cuda.synchronize()
-    barrier()
+    secs, dec, nsteps, checksum, launches = sharded_decode(a, dist, rank, world, local)
     clk = clocks.stop()
-    if dist:
-        t = torch.tensor([secs, dec], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        secs, dec = float(t[0].item()), float(t[1].item())
-        full = shard.gather_tokens(dist, got_ids, toks, a.seqs)
-    else:
-        full = toks
     tokens = a.seqs * a.new_tokens
-    nsteps = int(steps.sum())
-    if dist:
-        t = torch.tensor([nsteps], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t)
-        nsteps = int(t.item())
     if rank == 0:
         line = {
             "metric": "sampled spec-decode tok/s, batch of independent sequences", "value": tokens / secs,
-            "unit": "tok/s", "n_gpus": world, "steps": len(ids), "warmup": max(a.warmup, 3),
-            "ms_per_step": secs * 1000.0 / max(1, len(ids)), "higher_is_better": True, "scaling": "strong",
+            "unit": "tok/s", "n_gpus": world, "steps": 1, "warmup": max(a.warmup, 3),
+            "ms_per_step": secs * 1000.0, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "u8xs8->s32, f32",
             "data": "synthetic (seeded N(0,0.02) -> Q4_0 -> INT8 weights, uniform prompt ids per sequence)",
-            "config": {"workload": f"phi3-mini int8 + {DRAFT_LAYERS}-layer draft, rejection sampling T={T} "
-                                   f"top-p={top_p} k={a.k}, Philox seed {seed} keyed by sequence id, "
+            "config": {"workload": f"phi3-mini int8 + {DRAFT_LAYERS}-layer draft, rejection sampling T={SHARD_T} "
+                                   f"top-p={SHARD_TOP_P} k={a.k}, Philox seed {SHARD_SEED} keyed by sequence id, "
                                    f"{a.seqs} sequences x ({a.prompt_len} prompt + {a.new_tokens} new), "
                                    f"split over {world} rank(s), prefill included",
                        "parallelism": f"sequence sharding over {world} GPU(s), no collective",
                        "step": "each rank's share as one in-GPU batch (prefills + batched decode)"},
             "spec": {"speculative_steps": nsteps, "tokens_per_step": tokens / max(1, nsteps),
                      "decode_only_tok_s": tokens / dec if dec > 0 else None,
-                     "batch_per_gpu": len(ids), "decode_s": dec, "prefill_s": secs - dec,
-                     "stream_checksum": int(np.asarray(full, np.int64).sum())},
+                     "batch_per_gpu": (a.seqs + world - 1) // world, "decode_s": dec, "prefill_s": secs - dec,
+                     "stream_checksum": checksum},
             "gpu_launches": launches,
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
-    eng.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+# Strong-scaling ceiling of config 3 from HBM bytes alone: every rank still
+# streams the replicated weights once per pass (about 7.47 GB), only the KV
+# reads shrink with the share (64 / g x 0.566 GB).
+SHARD_CEILING = {1: 1.0, 2: 1.71, 4: 2.64, 8: 3.64}
 
 
 def split_host_threads():
@@ -728,8 +750,25 @@ def main():
             "clocks": clk,
             "setup_s": setup_s,
         }
-        print(json.dumps(line), flush=True)
     eng.close()
+    if dist:
+        # The batch-1 path above does not shard (replicas only). Config 3 does:
+        # its 64 sampled sequences decoded by rank 0 alone, then split over all
+        # ranks with no collective on the data path (strong scaling, same run).
+        c3 = argparse.Namespace(seqs=64, prompt_len=1024, new_tokens=512, k=6, warmup=1)
+        one = sharded_decode(c3, dist, rank, 1, local)
+        many = sharded_decode(c3, dist, rank, world, local)
+        if rank == 0:
+            tok = c3.seqs * c3.new_tokens
+            line["sharded"] = {
+                "workload": "config 3: 64 independent sampled sequences (T 0.8, top-p 0.95, k 6, Philox seed 1234 "
+                            "by sequence id) x (1024 prompt + 512 new), prefills included",
+                "scaling": "strong", "tok_s_1gpu": tok / one[0], f"tok_s_{world}gpu": tok / many[0],
+                "speedup": one[0] / many[0], "hbm_ceiling_speedup": SHARD_CEILING.get(world),
+                "decode_only_speedup": one[1] / many[1] if many[1] > 0 else None,
+                "streams_identical": one[3] == many[3]}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()
         dist.destroy_process_group()

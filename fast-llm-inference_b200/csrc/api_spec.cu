@@ -14,6 +14,7 @@
 #include <vector>
 
 #include "fl_common.cuh"
+#include "fl_host_sample.h"
 #include "fl_runtime.h"
 #include "medusa.h"
 #include "speculative.h"
@@ -32,6 +33,7 @@ struct TreeImpl {
 struct CacheImpl {
     draft_kv_cache_t pub;
     int num_heads, head_dim;
+    int steps;  // speculative_decode_step calls with a host target (Philox step counter)
 };
 
 std::mutex g_bind_mu;
@@ -59,6 +61,23 @@ bool parse_synthetic(const char* path, uint64_t* seed) {
     *seed = v;
     return true;
 }
+
+// Seed of each draft / Medusa model's synthetic weights (0 when the model
+// never loaded any: its weights are then generated from seed 0 on first
+// use), and the device engines that run a draft or Medusa heads for host
+// targets (a caller's own target_forward / base_forward).
+std::map<const void*, uint64_t> g_seed;
+std::map<const void*, fl_engine_t*> g_host_eng;
+
+uint64_t synth_seed(const void* m) {
+    std::lock_guard<std::mutex> lk(g_bind_mu);
+    auto it = g_seed.find(m);
+    return it == g_seed.end() ? 0 : it->second;
+}
+
+// Head size of a draft / Medusa model given only its hidden size: 96 when it
+// divides (the Phi-3 shapes), else 128, else 64.
+int head_dim_for(int d) { return d % 96 == 0 ? 96 : d % 128 == 0 ? 128 : d % 64 == 0 ? 64 : 0; }
 
 void free_tensor_array(dequantized_tensor_t* arr, int n) {
     if (!arr) return;
@@ -135,6 +154,236 @@ int medusa_tree_settings(const medusa_model_t* m, const medusa_config_t* cfg, st
 int medusa_bind(fl_engine_t* e, medusa_model_t* m);
 fl_engine_t* medusa_engine(const medusa_model_t* m) { return bound(m); }
 
+// ------------------------------------------------------------------ host targets
+// Device engines for models whose target / base is a caller's host function:
+// no base layers, only the draft stack (or the Medusa heads) with the
+// embedding and the LM head, generated from the model's synthetic seed
+// (the LM head a loaded draft carries is used as it is). One engine per
+// model, on the current device, released with the model.
+
+void host_engine_release(const void* m) {
+    fl_engine_t* e = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_bind_mu);
+        auto it = g_host_eng.find(m);
+        if (it != g_host_eng.end()) {
+            e = it->second;
+            g_host_eng.erase(it);
+        }
+        g_seed.erase(m);
+    }
+    if (e) fl_engine_destroy(e);
+}
+
+static fl_engine_t* host_engine_get(const void* m) {
+    std::lock_guard<std::mutex> lk(g_bind_mu);
+    auto it = g_host_eng.find(m);
+    return it == g_host_eng.end() ? nullptr : it->second;
+}
+
+// Context capacity of the host-target engines (draft cache positions).
+constexpr int kHostCtx = 4096;
+
+static fl_engine_t* host_engine_new(int vocab, int d, int ffn, int draft_layers, int medusa_heads, uint64_t seed) {
+    const int hd = head_dim_for(d);
+    if (hd == 0) {
+        set_error(FL_E_UNSUPPORTED, "host target: hidden size must be a multiple of 64");
+        return nullptr;
+    }
+    fl_model_config_t c = {};
+    c.vocab_size = vocab;
+    c.hidden_size = d;
+    c.intermediate_size = ffn;
+    c.num_layers = 0;
+    c.num_heads = d / hd;
+    c.num_kv_heads = d / hd;
+    c.head_dim = hd;
+    c.draft_layers = draft_layers;
+    c.medusa_heads = medusa_heads;
+    c.max_seq_len = kHostCtx;
+    c.rope_theta = 10000.0f;
+    c.norm_eps = 1e-5f;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+    fl_engine_t* e = fl_engine_create(&c, dev);
+    if (!e) return nullptr;
+    std::vector<float> emb((size_t)vocab * d);
+    if (fl_synth_q4_0_f32(seed, FL_TENSOR_ID(3, 0, 0), vocab, d, 0.02f, emb.data()) != FL_OK ||
+        fl_engine_load_embedding(e, emb.data()) != FL_OK) {
+        fl_engine_destroy(e);
+        return nullptr;
+    }
+    return e;
+}
+
+// The draft's own engine (draft weights generated from seed 0 if the draft
+// never loaded any).
+static fl_engine_t* host_draft_engine(draft_model_t* dm) {
+    if (fl_engine_t* e = host_engine_get(dm)) return e;
+    if (!dm->w_q_proj[0].weights && draft_model_load(dm, "synthetic:0") != 0) return nullptr;
+    fl_engine_t* e = host_engine_new(dm->vocab_size, dm->hidden_size, dm->intermediate_size, dm->num_layers, 0,
+                                     synth_seed(dm));
+    if (!e) return nullptr;
+    if (load_draft_into(e, dm) != FL_OK || !fl_engine_ready(e)) {
+        fl_engine_destroy(e);
+        set_error(FL_E_STATE, "host target: draft weights incomplete");
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lk(g_bind_mu);
+    g_host_eng[dm] = e;
+    return e;
+}
+
+// The Medusa heads' own engine (heads generated from seed 0 if never
+// loaded; LM head from the heads' seed).
+fl_engine_t* host_medusa_engine(medusa_model_t* m) {
+    if (fl_engine_t* e = host_engine_get(m)) return e;
+    if ((!m->heads[0].weights || !m->heads[0].weights->weights) && medusa_model_load(m, "synthetic:0") != 0)
+        return nullptr;
+    const uint64_t seed = synth_seed(m);
+    fl_engine_t* e = host_engine_new(m->vocab_size, m->hidden_size, 32, 0, m->num_heads, seed);
+    if (!e) return nullptr;
+    dequantized_tensor_t lm = {};
+    unbind(m);
+    if (synth_tensor(&lm, seed, FL_TENSOR_ID(3, 0, 1), m->vocab_size, m->hidden_size) != FL_OK ||
+        fl_engine_load_linear(e, 3, 0, 1, lm.weights, lm.scales_f16, lm.rows, lm.cols) != FL_OK ||
+        medusa_bind(e, m) != FL_OK || !fl_engine_ready(e)) {
+        free(lm.weights);
+        free(lm.scales_f16);
+        fl_engine_destroy(e);
+        return nullptr;
+    }
+    free(lm.weights);
+    free(lm.scales_f16);
+    std::lock_guard<std::mutex> lk(g_bind_mu);
+    g_host_eng[m] = e;
+    return e;
+}
+
+// Sampling rule of a host-target decode (include/speculative.h): greedy
+// when temperature <= 0, else the library's integer rule at top-p 1 with
+// Philox key (seed 0, sequence 0).
+struct HostRule {
+    float T;
+    bool greedy() const { return !(T > 0.0f); }
+};
+
+// The token at position `pos` from target logits `row`: greedy argmax, or a
+// draw (purpose 2) at Philox step `step`.
+static int host_pick(const HostRule& r, const float* row, int V, uint32_t step, int pos) {
+    if (r.greedy()) return fl_host::argmax(row, V);
+    std::vector<uint32_t> E;
+    const uint64_t M = fl_host::weights(row, V, r.T, 1.0f, E);
+    return fl_host::pick(E, M, fl_host::u24(0u, 0u, step, (uint32_t)pos, 2u));
+}
+
+// Sequential verification of drafts d[0..K) against a host target whose
+// context ends just before `cur` (not yet fed): feeds cur, compares the
+// target's token at the next position with d[0], feeds d[0] if accepted,
+// and so on; a rejected draft is replaced by the target's token there, and
+// after K accepted drafts the target's next token follows (rejection
+// sampling with a greedy draft when sampling: d is kept with probability
+// p(d), otherwise the token is drawn from p without d). Only tokens that end
+// up in the output are ever fed. Appends the accepted drafts and the final
+// token to `emit` (at most `room`); returns the number of accepted drafts.
+static int host_verify(void* tm, void (*tf)(void*, const float*, float*, int), const HostRule& rule, int V, int cur,
+                       int pos, const int* d, int K, uint32_t step, int room, std::vector<int>& emit) {
+    std::vector<float> row(V);
+    std::vector<uint32_t> E;
+    int a = 0;
+    for (int j = 0; j <= K && (int)emit.size() < room; j++) {
+        const float f = (float)(j == 0 ? cur : d[j - 1]);
+        tf(tm, &f, row.data(), 1);
+        const int p = pos + 1 + j;  // position of the token being decided
+        if (j == K) {
+            emit.push_back(host_pick(rule, row.data(), V, step, p));
+            break;
+        }
+        int next;
+        bool keep;
+        if (rule.greedy()) {
+            next = fl_host::argmax(row.data(), V);
+            keep = next == d[j];
+        } else {
+            const uint64_t M = fl_host::weights(row.data(), V, rule.T, 1.0f, E);
+            const uint32_t U = fl_host::u24(0u, 0u, step, (uint32_t)p, 1u);
+            keep = (unsigned __int128)U * M < ((unsigned __int128)E[d[j]] << 24);
+            next = d[j];
+            if (!keep) {
+                const uint64_t rest = M - E[d[j]];
+                const uint32_t U2 = fl_host::u24(0u, 0u, step, (uint32_t)p, 2u);
+                next = rest > 0 ? fl_host::pick(E, rest, U2, d[j]) : fl_host::pick(E, M, U2);
+            }
+        }
+        emit.push_back(next);
+        if (!keep) break;
+        a++;
+    }
+    return a;
+}
+
+// speculative_generate with a host target_forward (see include/speculative.h).
+static int host_spec_generate(draft_model_t* dm, void* tm, void (*tf)(void*, const float*, float*, int),
+                              const float* prompt_hidden, int P, int* out, int n, const speculative_config_t* cfg) {
+    const int V = dm->vocab_size;
+    const int K = std::min(std::max(cfg->num_draft_tokens, 1), 7);
+    if (P + n + K + 2 > kHostCtx) {
+        set_error(FL_E_INVAL, "speculative_generate: prompt plus output longer than the host-target context");
+        return -1;
+    }
+    fl_engine_t* e = host_draft_engine(dm);
+    if (!e) return -1;
+    const HostRule rule{cfg->temperature};
+    std::vector<int> seq(P);
+    std::vector<float> in(P);
+    for (int i = 0; i < P; i++) {
+        const int t = (int)prompt_hidden[i];
+        seq[i] = t >= 0 && t < V ? t : 0;  // inference.c:420-426: ids outside the vocabulary embed as 0
+        in[i] = (float)seq[i];
+    }
+    std::vector<float> lg((size_t)P * V);
+    tf(tm, in.data(), lg.data(), P);
+    int produced = 0;
+    out[produced++] = seq.emplace_back(host_pick(rule, lg.data() + (size_t)(P - 1) * V, V, 0xFFFFFFFFu, P));
+    std::vector<int> d(K), emit;
+    int draft_len = 0;
+    for (uint32_t step = 0; produced < n; step++) {
+        const int L = (int)seq.size();
+        if (fl_engine_draft_lm(e, seq.data() + draft_len, L - draft_len, draft_len, K, d.data()) != FL_OK) return -1;
+        emit.clear();
+        const int a = host_verify(tm, tf, rule, V, seq.back(), L - 1, d.data(), K, step, n - produced, emit);
+        for (int t : emit) out[produced++] = seq.emplace_back(t);
+        draft_len = L + std::min(a, K - 1);
+    }
+    return produced;
+}
+
+// speculative_decode_step with a host target_forward: the draft's cache
+// holds the positions before `cache->cache_len`, where current_token goes.
+static int host_spec_step(draft_model_t* dm, draft_kv_cache_t* cache, void* tm,
+                          void (*tf)(void*, const float*, float*, int), int cur, int* out, int* num_out,
+                          const speculative_config_t* cfg) {
+    const int V = dm->vocab_size;
+    const int K = std::min(std::max(cfg->num_draft_tokens, 1), 7);
+    const int pos = cache->cache_len;
+    if (cur < 0 || cur >= V || pos + K + 2 > kHostCtx) return -1;
+    fl_engine_t* e = host_draft_engine(dm);
+    if (!e) return -1;
+    std::vector<int> d(K), emit;
+    if (fl_engine_draft_lm(e, &cur, 1, pos, K, d.data()) != FL_OK) return -1;
+    CacheImpl* ci = (CacheImpl*)cache;
+    const int a = host_verify(tm, tf, HostRule{cfg->temperature}, V, cur, pos, d.data(), K, (uint32_t)ci->steps,
+                              K + 1, emit);
+    ci->steps++;
+    int dummy = 0;
+    // keep the draft cache contiguous up to the last accepted draft
+    if (a == K && fl_engine_draft_lm(e, &d[K - 1], 1, pos + K, 1, &dummy) != FL_OK) return -1;
+    cache->cache_len = pos + a + 1;
+    for (size_t i = 0; i < emit.size(); i++) out[i] = emit[i];
+    *num_out = (int)emit.size();
+    return *num_out;
+}
+
 FL_API int fl_engine_bind_medusa(fl_engine_t* e, void* m) {
     if (!e || !m) return set_error(FL_E_INVAL, "bind_medusa: NULL");
     return medusa_bind(e, (medusa_model_t*)m);
@@ -197,12 +446,15 @@ FL_API int draft_model_load(draft_model_t* m, const char* path) {
         for (int p = 0; p < 7; p++)
             if (synth_tensor(&arrs[p][l], seed, FL_TENSOR_ID(1, l, p), shapes[p][0], shapes[p][1]) != FL_OK) return -1;
     if (synth_tensor(m->w_lm_head, seed, FL_TENSOR_ID(3, 0, 1), m->vocab_size, d) != FL_OK) return -1;
+    std::lock_guard<std::mutex> lk(g_bind_mu);
+    g_seed[m] = seed;
     return 0;
 }
 
 FL_API void draft_model_free(draft_model_t* m) {
     if (!m) return;
     unbind(m);
+    host_engine_release(m);
     free_tensor_array(m->w_q_proj, m->num_layers);
     free_tensor_array(m->w_k_proj, m->num_layers);
     free_tensor_array(m->w_v_proj, m->num_layers);
@@ -324,12 +576,11 @@ FL_API int speculative_decode_step(draft_model_t* draft, draft_kv_cache_t* draft
                                    void (*target_forward)(void*, const float*, float*, int),
                                    const float* current_hidden, int current_token, int* output_tokens,
                                    int* num_output, const speculative_config_t* config) {
-    if (!draft || !draft_cache || !target_model || !current_hidden || !output_tokens || !num_output || !config)
-        return -1;
-    if (target_forward != fl_cuda_target_forward) {
-        set_error(FL_E_UNSUPPORTED, "speculative_decode_step: target_forward must be fl_cuda_target_forward");
-        return -1;
-    }
+    if (!draft || !draft_cache || !target_forward || !output_tokens || !num_output || !config) return -1;
+    if (target_forward != fl_cuda_target_forward)
+        return host_spec_step(draft, draft_cache, target_model, target_forward, current_token, output_tokens,
+                              num_output, config);
+    if (!target_model || !current_hidden) return -1;
     fl_engine_t* e = (fl_engine_t*)target_model;
     if (!bound(draft) && fl_engine_bind_draft(e, draft) != FL_OK) return -1;
     const int K = config->num_draft_tokens;
@@ -360,12 +611,12 @@ FL_API int speculative_decode_step(draft_model_t* draft, draft_kv_cache_t* draft
 FL_API int speculative_generate(draft_model_t* draft, void* target_model,
                                 void (*target_forward)(void*, const float*, float*, int), const float* prompt_hidden,
                                 int prompt_len, int* output_tokens, int num_tokens, const speculative_config_t* config) {
-    if (!draft || !target_model || !prompt_hidden || !output_tokens || !config || prompt_len <= 0 || num_tokens <= 0)
+    if (!draft || !target_forward || !prompt_hidden || !output_tokens || !config || prompt_len <= 0 || num_tokens <= 0)
         return -1;
-    if (target_forward != fl_cuda_target_forward) {
-        set_error(FL_E_UNSUPPORTED, "speculative_generate: target_forward must be fl_cuda_target_forward");
-        return -1;
-    }
+    if (target_forward != fl_cuda_target_forward)
+        return host_spec_generate(draft, target_model, target_forward, prompt_hidden, prompt_len, output_tokens,
+                                  num_tokens, config);
+    if (!target_model) return -1;
     fl_engine_t* e = (fl_engine_t*)target_model;
     if (fl_engine_bind_draft(e, draft) != FL_OK) return -1;
     // temperature > 0: rejection sampling with the engine's top_p and Philox
@@ -415,12 +666,15 @@ FL_API int medusa_model_load(medusa_model_t* m, const char* path) {
         if (!m->heads[h].weights ||
             synth_tensor(m->heads[h].weights, seed, FL_TENSOR_ID(2, h, 0), m->hidden_size, m->hidden_size) != FL_OK)
             return -1;
+    std::lock_guard<std::mutex> lk(g_bind_mu);
+    g_seed[m] = seed;
     return 0;
 }
 
 FL_API void medusa_model_free(medusa_model_t* m) {
     if (!m) return;
     unbind(m);
+    host_engine_release(m);
     {
         std::lock_guard<std::mutex> lk(g_bind_mu);
         g_med_tree.erase(m);

@@ -766,7 +766,8 @@ static fl_engine_t* engine_create(const fl_model_config_t* cfg, int device, int 
     if (c.hidden_size <= 0 || c.num_heads <= 0 || c.num_kv_heads <= 0 || c.head_dim <= 0 ||
         c.num_heads % c.num_kv_heads != 0 || c.hidden_size % 32 != 0 || c.intermediate_size % 32 != 0 ||
         (c.num_heads * c.head_dim) % 32 != 0 || c.head_dim % 2 != 0 || c.head_dim > 128 ||
-        c.vocab_size <= 0 || c.num_layers <= 0 || c.max_seq_len < 16 || c.draft_layers < 0 || c.medusa_heads < 0) {
+        c.vocab_size <= 0 || c.num_layers < 0 || c.max_seq_len < 16 || c.draft_layers < 0 || c.medusa_heads < 0 ||
+        (c.num_layers == 0 && c.draft_layers == 0 && c.medusa_heads == 0)) {
         set_error(FL_E_INVAL, "fl_engine_create: unsupported model configuration");
         return nullptr;
     }

@@ -9,8 +9,13 @@
 // the barriers: it walks the same list and streams the weight stages of
 // every GEMV phase through one shared-memory ring, so the HBM stream keeps
 // running across layer and phase boundaries, attention and barriers
-// included. All waits (ring mbarriers, grid barrier) are bounded: on a
-// timeout the kernel records an error word, stops waiting and computing,
+// included. In a GEMV phase each consumer warp owns 16 weight rows of the
+// stage tile and runs mma.sync u8 x s8 -> s32 per 32-element block over
+// them for all activation rows, scaling and adding the blocks in order
+// (matmul_dequantized's order, bit-exact with the oracle), then applies the
+// layer epilogue to its own rows: no cross-warp reduction, no CTA barrier
+// inside a phase. All waits (ring mbarriers, grid barrier) are bounded: on
+// a timeout the kernel records an error word, stops waiting and computing,
 // still passes every barrier, and ends.
 #include <float.h>
 
@@ -23,11 +28,9 @@ namespace fl {
 namespace {
 
 constexpr int kCW = 8;                    // consumer warps (phase work, barriers)
-constexpr int kRW = 4;                    // of them, TMEM readout warps in GEMV phases
 constexpr int kCThreads = kCW * 32;
 constexpr int kProdWarp = kCW;            // TMA producer
-constexpr int kMmaWarp = kCW + 1;         // tcgen05.mma issuer, TMEM owner
-constexpr int kThr = (kCW + 2) * 32;
+constexpr int kThr = (kCW + 1) * 32;
 constexpr int kMaxSlots = 12;
 constexpr int kSmemLimit = 222 * 1024;    // + static shared memory <= 227 KB
 constexpr unsigned long long kWaitNs = 2000000000ull;  // every wait gives up after ~2 s
@@ -54,7 +57,6 @@ __device__ __forceinline__ bool cbar_or(bool v) {
         : "memory");
     return r != 0;
 }
-__device__ __forceinline__ void abar() { asm volatile("bar.sync 2, 128;" ::: "memory"); }  // warps 0-3
 
 __device__ __forceinline__ void mb_init(uint64_t* b, uint32_t n) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(b)), "r"(n) : "memory");
@@ -140,68 +142,65 @@ __device__ bool grid_sync(unsigned long long* ctr, unsigned long long target, in
 // ---------------------------------------------------------------- GEMV geometry
 // Weights are in the tiled layout with 128-byte panels (fl_layout.cuh): a
 // panel's rows are 128 contiguous bytes whose 16-byte chunks are XORed with
-// (row & 7), i.e. the tcgen05 SWIZZLE_128B K-major layout when a group of
-// 8 rows starts on a 1024-byte boundary. A ring stage is a tile of
-// kTileRows weight rows x kPPS panels, plus their fp16 block scales; the
-// MMA warp issues one tcgen05.mma kind::i8 (A = 128 weight rows s8,
-// B = the 8 activation rows u8, K = 32) per 32-element block into its own
-// group of 8 TMEM columns, and readout warp w takes TMEM lanes (rows)
-// 32w .. 32w + 31: it scales each block's s32 products by the row's block
-// scale and adds them in block order (matmul_dequantized's order).
+// (row & 7), so the eight rows of an ldmatrix read hit eight different bank
+// groups. A ring stage is a tile of kTileRows weight rows x kPPS panels plus
+// their fp16 block scales; consumer warp w takes tile rows 16w .. 16w + 15.
 constexpr int kP = 128;                         // panel bytes per row
 constexpr int kPPS = 2;                         // panels per stage
-constexpr int kTileRows = 128;                  // UMMA M
+constexpr int kTileRows = 128;                  // 8 warps x 16 rows
 constexpr int kKBS = kPPS * kP / 32;            // 32-element blocks per stage
 constexpr int kSlot = kPPS * (kTileRows * kP + kTileRows * (kP / 16));  // 34 KB
-constexpr int kCB = kKBS * 8;                   // TMEM columns per stage
-constexpr int kNB = 4;                          // TMEM stage buffers
-constexpr int kTmemCols = kNB * kCB;            // 256
-static_assert(kSlot % 1024 == 0, "stage slots keep the 1024-byte swizzle alignment");
+static_assert(kSlot % 1024 == 0, "stage slots keep 1024-byte alignment");
+static_assert(kTileRows == 16 * kCW, "one 16-row group per consumer warp");
 
 struct GGeo {
     int nps, row0, row1, ntiles, nstages;  // nps: stages per tile
+    int W;   // panels per stage
+    int rs;  // row spacing of a panel in a slot: tile rows rounded up to 16
 };
 
+// A CTA's rows are a contiguous run of 8-row units; tiles of up to kTileRows
+// rows. A stage holds W whole panels of the tile, W the widest divisor of
+// K / kP with W * rs <= kTileRows * kPPS, so a narrow CTA share still moves
+// about a slot's worth of bytes per stage.
 __host__ __device__ inline void gemv_geo(const GemvParams& g, int cta, int ncta, GGeo& o) {
-    o.nps = g.K / (kP * kPPS);
     const int nunits = g.N >> 3;
     const int u0 = (int)(((long long)nunits * cta) / ncta);
     const int u1 = (int)(((long long)nunits * (cta + 1)) / ncta);
     o.row0 = u0 * 8;
     o.row1 = u1 * 8;
-    o.ntiles = (o.row1 - o.row0 + kTileRows - 1) / kTileRows;
+    const int R = o.row1 - o.row0;
+    const int tr = R < kTileRows ? R : kTileRows;
+    o.rs = tr <= 16 ? 16 : (tr + 15) & ~15;
+    const int npan = g.K / kP;
+    o.W = kPPS;
+    for (int w = (kTileRows * kPPS) / o.rs; w > kPPS; w--)
+        if (npan % w == 0) {
+            o.W = w;
+            break;
+        }
+    o.nps = npan / o.W;
+    o.ntiles = (R + kTileRows - 1) / kTileRows;
     o.nstages = o.ntiles * o.nps;
 }
 
-// Shared-memory matrix descriptor (tcgen05): start, leading / stride byte
-// offsets, version 1, layout type (0 none, 2 128-byte swizzle).
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
-    uint64_t d = (uint64_t)((addr >> 4) & 0x3FFF);
-    d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
-    d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
-    d |= (uint64_t)1 << 46;
-    d |= (uint64_t)(layout & 7) << 61;
-    return d;
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
 }
 
-// D (s32, TMEM) = A (s8, 128 x 32) x B (u8, 32 x 8), not accumulated.
-__device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t da, uint64_t db) {
-    // instruction descriptor: D s32, A s8, B u8, both K-major, N = 8, M = 128
-    constexpr uint32_t idesc = (2u << 4) | (1u << 7) | (0u << 10) | (1u << 17) | (8u << 24);
+// D(16x8, s32) = A(16x32, u8, row) x B(32x8, s8, col); A rows 8-15 are zero,
+// so only the first two accumulator registers carry results.
+__device__ __forceinline__ void mma_u8s8(uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1, int& d0, int& d1) {
+    int c2, c3;
     asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(da), "l"(db), "r"(idesc), "r"(0)
-        : "memory");
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+        : "=r"(d0), "=r"(d1), "=r"(c2), "=r"(c3)
+        : "r"(a0), "r"(0), "r"(a2), "r"(0), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+    (void)c2;
+    (void)c3;
 }
-
-__device__ __forceinline__ void umma_commit(uint64_t* b) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(saddr(b))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
 // warp-uniform bounded wait: lane 0 waits, the result is broadcast
 __device__ __forceinline__ bool warp_wait(uint64_t* b, uint32_t par, int* err) {
@@ -276,168 +275,183 @@ __device__ void pair_epi(const GemvParams& p, int epi, int m, int n0, bool has1,
 struct Ring {
     uint8_t* base;
     uint64_t* full;    // TMA bytes landed
-    uint64_t* empty;   // slot free (readout warps)
-    uint64_t* mdone;   // [kNB] stage MMAs complete (tcgen05.commit)
-    uint64_t* tfree;   // [kNB] stage TMEM read (readout warps)
-    uint64_t* actrdy;  // activations of the phase written
-    uint32_t tmem;
+    uint64_t* empty;   // slot free (all consumer warps)
     int S, slot;
 };
 
 // The activation prologue out of line: its batched loads want registers
 // that the GEMV loops around it do not need at the same time.
-__device__ __noinline__ void step_prologue(uint8_t* act, const float* x, int K, int rows, int norm, float eps,
+#ifndef FL_STEP_PROLOGUE_CACHE
+#define FL_STEP_PROLOGUE_CACHE 1
+#endif
+__device__ __noinline__ void step_prologue(uint8_t* act, int ald, const float* x, int K, int rows, int norm, float eps,
                                            float* red, int tid) {
-    act_prologue_rows<kCThreads, kMaxRows, true, true>(act, 0, x, K, rows, norm, eps, red, tid, 1);
+    act_prologue_rows<kCThreads, kMaxRows, FL_STEP_PROLOGUE_CACHE != 0>(act, ald, x, K, rows, norm, eps, red, tid, 1);
 }
 
-// Consumer side of one GEMV phase (all 8 consumer warps: prologue; warps
-// 0..3: TMEM readout and epilogue). `s` is the global stage counter, `g`
-// the GEMV phase counter. With `skip` the protocol runs but no output is
-// written.
-template <int MR>
-__device__ void gemv_readout(const GemvParams& p, int epi, bool skip, const Ring& rg, int s, bool& bad, int* err,
-                             const GGeo& geo, int rows_m, unsigned long long* best_s, const EpiSmem& es,
-                             unsigned long long* tr, unsigned long long* str) {
+// Consumer side of one GEMV phase. The tile's rows form nrg = rs / 16
+// groups of 16; warp w takes group w % nrg and, of every stage, the 32-element
+// blocks kb with kb % wpr == w / nrg (wpr = 8 / nrg warps per group). Per
+// block one ldmatrix.x4 brings the group's 16 rows, two mma.sync form the
+// s32 dots against the activation rows (row-major in shared memory, row
+// stride ald), and each dot is turned into float exactly, scaled by its fp16
+// block scale and added. Lane (g, t) holds activation row g against weight
+// rows 2t, 2t + 1, 8 + 2t, 9 + 2t of its group. With one warp per group
+// (wide phases) the blocks are added in matmul_dequantized's order; with
+// several, their partial sums are added in warp order at the tile's end.
+// `s` is the global stage counter. With `skip` the protocol runs but no
+// output is written.
+__device__ void gemv_consume(const GemvParams& p, int epi, bool skip, const Ring& rg, int s, bool& bad, int* err,
+                             const GGeo& geo, int rows_m, const uint8_t* act, int ald, unsigned long long* best_s,
+                             const EpiSmem& es, float (*red)[32][4], unsigned long long* tr) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row = 32 * warp + lane;  // tile row = TMEM lane
+    const int g = lane >> 2, t = lane & 3;
+    const int lj = lane >> 3, lq = lane & 7;
+    const int nrg = geo.rs >> 4, wpr = kCW / nrg;
+    const int grp = warp % nrg, ks = warp / nrg;
+    const bool busy = ks < wpr;
+    const int lrow = 16 * grp + lq + 8 * (lj >> 1);  // this lane's ldmatrix row in the tile
+    const int nkb = geo.W * (kP / 32);               // blocks per stage
     const int nr = geo.row1 - geo.row0;
-    float acc[MR];
-#pragma unroll
-    for (int m = 0; m < MR; m++) acc[m] = 0.0f;
+    const bool arow = g < rows_m;
+    const uint8_t* arow_p = act + (size_t)g * ald;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     for (int i = 0; i < geo.nstages; i++, s++) {
-        const int sl = s % rg.S, buf = s % kNB;
+        const int sl = s % rg.S;
         const int tile = i / geo.nps, pp = i - tile * geo.nps;
         const int r = geo.row0 + tile * kTileRows;
         const int rows = min(kTileRows, geo.row1 - r);
-        if (bad) break;
-        if (!warp_wait(&rg.mdone[buf], (s / kNB) & 1, err)) {
-            bad = true;
-            break;
-        }
+        if (!bad && !warp_wait(&rg.full[sl], (s / rg.S) & 1, err)) bad = true;
         if (tr && threadIdx.x == 0 && i == 0) tr[5] = gtime();
-        if (str && i < 64 && threadIdx.x == 0) str[8 * i] = gtime();
-        tc_fence_after();
-        uint32_t v[kKBS * MR];
-        const uint32_t ta = rg.tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(buf * kCB);
+        if (!bad && busy && 16 * grp < rows) {
+            const uint8_t* st = rg.base + (size_t)sl * rg.slot;
+            const uint8_t* dsc = st + geo.W * geo.rs * kP;
+            const uint32_t sbase = saddr(st);
+            const int rb = 16 * grp + 2 * t;
+            auto block = [&](int kb) {
+                const int j = kb >> 2, kk = kb & 3;
+                const int chunk = 2 * kk + (lj & 1);
+                uint32_t b00, b01, b10, b11;
+                ldsm_x4(sbase + (uint32_t)(j * geo.rs * kP + lrow * kP + ((chunk ^ (lrow & 7)) << 4)), b00, b01, b10,
+                        b11);
+                uint32_t a0 = 0, a2 = 0;
+                if (arow) {
+                    const int kc = (pp * nkb + kb) * 32 + 4 * t;
+                    a0 = *reinterpret_cast<const uint32_t*>(arow_p + kc);
+                    a2 = *reinterpret_cast<const uint32_t*>(arow_p + kc + 16);
+                }
+                int d0, d1, d2, d3;
+                mma_u8s8(a0, a2, b00, b01, d0, d1);
+                mma_u8s8(a0, a2, b10, b11, d2, d3);
+                const __half* sc = reinterpret_cast<const __half*>(dsc + j * geo.rs * (kP / 16));
+                const float s0 = __half2float(sc[rb * 4 + kk]);
+                const float s1 = __half2float(sc[(rb + 1) * 4 + kk]);
+                const float s2 = __half2float(sc[(rb + 8) * 4 + kk]);
+                const float s3 = __half2float(sc[(rb + 9) * 4 + kk]);
+                acc[0] = __fadd_rn(acc[0], __fmul_rn(i2f_exact(d0), s0));
+                acc[1] = __fadd_rn(acc[1], __fmul_rn(i2f_exact(d1), s1));
+                acc[2] = __fadd_rn(acc[2], __fmul_rn(i2f_exact(d2), s2));
+                acc[3] = __fadd_rn(acc[3], __fmul_rn(i2f_exact(d3), s3));
+            };
+            if (wpr == 1 && nkb == kPPS * (kP / 32)) {
 #pragma unroll
-        for (int kb = 0; kb < kKBS; kb++) {
-            if (MR == 8) {
-                asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                             : "=r"(v[kb * MR + 0]), "=r"(v[kb * MR + 1]), "=r"(v[kb * MR + 2]), "=r"(v[kb * MR + 3]),
-                               "=r"(v[kb * MR + 4]), "=r"(v[kb * MR + 5]), "=r"(v[kb * MR + 6]), "=r"(v[kb * MR + 7])
-                             : "r"(ta + kb * 8));
+                for (int kb = 0; kb < kPPS * (kP / 32); kb++) block(kb);
             } else {
-                asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(v[kb * MR]) : "r"(ta + kb * 8));
+#pragma unroll 4
+                for (int kb = ks; kb < nkb; kb += wpr) block(kb);
             }
         }
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mb_arrive(&rg.tfree[buf]);
-        // the row's block scales; the slot is released right after
-        if (!warp_wait(&rg.full[sl], (s / rg.S) & 1, err)) {
-            bad = true;
-            break;
-        }
-        const uint8_t* dsc = rg.base + (size_t)sl * rg.slot + kPPS * kTileRows * kP;
-        uint2 sc[kPPS];
-#pragma unroll
-        for (int j = 0; j < kPPS; j++) sc[j] = *reinterpret_cast<const uint2*>(dsc + j * kTileRows * (kP / 16) + row * 8);
         __syncwarp();
         if (lane == 0) mb_arrive(&rg.empty[sl]);
-        if (str && i < 64 && threadIdx.x == 0) str[8 * i + 1] = gtime();
-#pragma unroll
-        for (int kb = 0; kb < kKBS; kb++) {
-            const uint32_t hw = (kb & 2) ? sc[kb / 4].y : sc[kb / 4].x;
-            const __half2 h2 = *reinterpret_cast<const __half2*>(&hw);
-            const float sk = (kb & 1) ? __high2float(h2) : __low2float(h2);
-#pragma unroll
-            for (int m = 0; m < MR; m++) acc[m] = __fadd_rn(acc[m], __fmul_rn(i2f_exact((int)v[kb * MR + m]), sk));
-        }
         if (pp == geo.nps - 1) {
-            // weight-row pairs (row, row + 1) for even rows: the odd row's
-            // values come from lane + 1
+            if (wpr > 1) {
+                // partial sums of the group's warps, added in warp order
 #pragma unroll
-            for (int m = 0; m < MR; m++) {
-                const float o = __shfl_down_sync(0xffffffffu, acc[m], 1);
-                if (!skip && !(lane & 1) && row < rows && m < rows_m)
-                    pair_epi(p, epi, m, r + row, true, __fdiv_rn(acc[m], 127.0f), __fdiv_rn(o, 127.0f), best_s, es,
-                             geo.row0, nr);
-                acc[m] = 0.0f;
+                for (int q = 0; q < 4; q++) red[warp][lane][q] = acc[q];
+                cbar();
+                if (ks == 0) {
+                    for (int k2 = 1; k2 < wpr; k2++)
+#pragma unroll
+                        for (int q = 0; q < 4; q++) acc[q] = __fadd_rn(acc[q], red[grp + nrg * k2][lane][q]);
+                }
             }
+            if (!bad && !skip && arow && ks == 0) {
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const int lr = 16 * grp + 8 * h + 2 * t;  // even row of the pair within the tile
+                    if (lr < rows)
+                        pair_epi(p, epi, g, r + lr, lr + 1 < rows, __fdiv_rn(acc[2 * h], 127.0f),
+                                 __fdiv_rn(acc[2 * h + 1], 127.0f), best_s, es, geo.row0, nr);
+                }
+            }
+            if (wpr > 1) cbar();  // red is free again
+            acc[0] = acc[1] = acc[2] = acc[3] = 0.0f;
         }
     }
 }
 
-__device__ void gemv_phase(const GemvParams& p, int epi, bool skip, const Ring& rg, int& s, int& g, bool& bad,
-                           int* err, uint8_t* act, unsigned long long* best_s, float* nred, EpiSmem& es,
-                           unsigned long long* tr, unsigned long long* str) {
+__device__ void gemv_phase(const GemvParams& p, int epi, bool skip, const Ring& rg, int& s, bool& bad, int* err,
+                           uint8_t* act, unsigned long long* best_s, float* nred, EpiSmem& es, float (*red)[32][4],
+                           unsigned long long* tr) {
     // tr (CTA 0 only, may be null): [3] prologue done, [5] first stage read
     GGeo geo;
     gemv_geo(p, blockIdx.x, gridDim.x, geo);
-    const int warp = threadIdx.x >> 5;
-    int rows_m = p.M;
-    if (p.dyn_M) rows_m = min(__ldcg(p.dyn_M) - p.row0, p.M);
-    rows_m = max(0, min(rows_m, kMaxRows));
+    // The phase's scalar inputs in one round of loads, then the epilogue
+    // inputs and the activations together; the QKV epilogue values ride in
+    // registers through the activation prologue and are stored after it.
+    const bool qkv = !skip && epi == EPI_QKV;
+    int dynm = p.M, sbase = 0, src0 = p.row0;
+    if (p.dyn_M) dynm = __ldcg(p.dyn_M);
+    if (qkv) sbase = __ldcg(p.slot_base);
+    if (p.x_row_dyn) src0 = __ldcg(p.x_row_dyn);
+    const int rows_m = max(0, min(min(dynm - p.row0, p.M), kMaxRows));
     const int K = p.K;
+    const int ald = K + 16;
     const int tid = threadIdx.x;
     const int nr = geo.row1 - geo.row0;
     if (tid < kMaxRows) best_s[tid] = 0ull;
-    // epilogue inputs, loaded in parallel before the activation prologue
-    if (!skip && epi == EPI_QKV) {
+    int e_pos = 0, e_page = 0, e_off = 0;
+    if (qkv) {
         if (tid < rows_m) {
             const int r = p.row0 + tid;
-            const int slot = __ldcg(p.slot_base) + r;
-            es.pos[tid] = __ldcg(p.pos + r);
-            es.page[tid] = p.block_table[slot / kPageSize];
-            es.off[tid] = slot % kPageSize;
+            const int slot = sbase + r;
+            e_pos = __ldcg(p.pos + r);
+            e_page = p.block_table[slot / kPageSize];
+            e_off = slot % kPageSize;
         }
         const int half = p.head_dim >> 1;
         if (tid >= 32 && tid < 32 + half) {
             const int i = tid - 32;
             es.freq[i] = __fdiv_rn(1.0f, powf(p.theta, __fdiv_rn((float)(2 * i), (float)p.head_dim)));
         }
-    } else if (!skip && epi == EPI_RESID) {
+    }
+    // activation rows, row-major with stride K + 16 (rows >= rows_m are
+    // never stored by the epilogue, so they need no clearing)
+    if (!skip && p.x && rows_m > 0) {
+        step_prologue(act, ald, p.x + (size_t)src0 * K, K, rows_m, p.norm, p.eps, nred, tid);
+    } else if (!skip && rows_m > 0) {
+        const int K16 = K >> 4;
+        const uint4* src = reinterpret_cast<const uint4*>(p.aq + (size_t)p.row0 * K);
+#pragma unroll 4
+        for (int i = tid; i < rows_m * K16; i += kCThreads) {
+            const int m = i / K16, c = i - m * K16;
+            *reinterpret_cast<uint4*>(act + (size_t)m * ald + (size_t)c * 16) = __ldcg(src + (size_t)m * K16 + c);
+        }
+    }
+    if (qkv && tid < rows_m) {
+        es.pos[tid] = e_pos;
+        es.page[tid] = e_page;
+        es.off[tid] = e_off;
+    }
+    if (!skip && epi == EPI_RESID) {
         for (int i = tid; i < rows_m * nr; i += kCThreads) {
             const int m = i / nr, j = i - m * nr;
             es.res[i] = __ldcg(p.out + (size_t)(p.row0 + m) * p.ldo + geo.row0 + j);
         }
     }
-    // activations in the core-matrix layout of 8 rows; rows >= rows_m zero
-    if (!skip && p.x && rows_m > 0) {
-        const int src0 = p.x_row_dyn ? __ldcg(p.x_row_dyn) : p.row0;
-        step_prologue(act, p.x + (size_t)src0 * K, K, rows_m, p.norm, p.eps, nred, tid);
-    } else if (!skip && rows_m > 0) {
-        const int K16 = K >> 4;
-        const uint4* src = reinterpret_cast<const uint4*>(p.aq + (size_t)p.row0 * K);
-        for (int i = tid; i < rows_m * K16; i += kCThreads) {
-            const int m = i / K16, c = i - m * K16;
-            *reinterpret_cast<uint4*>(act + (size_t)c * 128 + m * 16) = __ldcg(src + (size_t)m * K16 + c);
-        }
-    }
-    {
-        const int K16 = K >> 4;
-        const int zr = kMaxRows - rows_m;
-        for (int i = tid; i < zr * K16; i += kCThreads) {
-            const int m = rows_m + i / K16, c = i % K16;
-            *reinterpret_cast<uint4*>(act + (size_t)c * 128 + m * 16) = make_uint4(0u, 0u, 0u, 0u);
-        }
-    }
-    // generic-proxy writes -> visible to the tensor core's async proxy
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     cbar();
-    if (tid == 0) {
-        mb_arrive(rg.actrdy);
-        if (tr) tr[3] = gtime();
-    }
-    g++;
-    if (warp < kRW) {
-        if (rows_m <= 1)
-            gemv_readout<1>(p, epi, skip || rows_m == 0, rg, s, bad, err, geo, rows_m, best_s, es, tr, str);
-        else
-            gemv_readout<8>(p, epi, skip, rg, s, bad, err, geo, rows_m, best_s, es, tr, str);
-    }
+    if (tr && tid == 0) tr[3] = gtime();
+    gemv_consume(p, epi, skip || rows_m == 0, rg, s, bad, err, geo, rows_m, act, ald, best_s, es, red, tr);
     s += geo.nstages;
     if (epi == EPI_LOGITS) {
         cbar();
@@ -447,169 +461,204 @@ __device__ void gemv_phase(const GemvParams& p, int epi, bool skip, const Ring& 
 }
 
 // ---------------------------------------------------------------- attention
-constexpr int kSplit = 64;   // keys per unit (one KV page)
 constexpr int kHdMax = 128;
+constexpr int kAChunk = 64;  // keys per shared-memory chunk
 
-struct AttnSmem {
-    float q[kMaxRows][kHdMax];
-    uint32_t K[kSplit][kHdMax / 2 + 1];
-    uint32_t V[kSplit][kHdMax / 2];
-    float sc[kMaxRows][kSplit];
-    float ml[kMaxRows][2];
-    int ticket;
-};
+__device__ __forceinline__ void cp16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
-// One (head, page) unit of split-K decode attention, warps 0-3. Same rule
-// as attention.cu's attention_split_kernel (inference.c:193-247).
-__device__ void attn_unit(const AttnParams& p, int h, int sp, int nsplit_max, AttnSmem& sm) {
-    const int tid = threadIdx.x;  // 0..127
-    const int warp = tid >> 5, lane = tid & 31;
+// Shared memory of an attention phase (in the activation region): q rows,
+// one chunk of scores, two chunk buffers of K (rows padded by 4 words: the
+// 16-byte row reads of a warp hit distinct banks) and of V, running max /
+// sum / rescale per row.
+constexpr int kAKst = kHdMax / 2 + 4;
+constexpr size_t kAttnQ = 0;
+constexpr size_t kAttnSc = kAttnQ + sizeof(float) * kMaxRows * kHdMax;
+constexpr size_t kAttnK = kAttnSc + sizeof(float) * kMaxRows * kAChunk;
+constexpr size_t kAttnV = kAttnK + sizeof(uint32_t) * 2 * kAChunk * kAKst;
+constexpr size_t kAttnML = kAttnV + sizeof(uint32_t) * 2 * kAChunk * (kHdMax / 2);
+constexpr size_t kAttnBytes = kAttnML + sizeof(float) * 3 * kMaxRows;
+
+// Decode attention of one head for the phase's rows, by one CTA's 8
+// consumer warps: the keys [0, base + M) stream through shared memory in
+// chunks of kAChunk (16-byte cp.async copies, the next chunk in flight while
+// this one is used), an online softmax per row (running max and sum,
+// rescaled per chunk), then the normalised P.V is quantized for the o
+// projection. Same rule as attention.cu (inference.c:193-247): scores
+// q.k / sqrt(hd), causal among the new rows (or the tree mask).
+__device__ void attn_head(const AttnParams& p, int h, uint8_t* smem) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int M = p.dyn_M ? __ldcg(p.dyn_M) : p.M;
     const int nr = min(M, kMaxRows);
+    if (nr <= 0) return;  // uniform over the CTA
     const int base = __ldcg(p.slot_base);
     const int ctx = base + M;
-    const int nsplit = (ctx + kSplit - 1) / kSplit;
-    if (sp >= nsplit || nr <= 0) return;  // uniform over warps 0-3
-    const int hd = p.head_dim, hd2 = hd >> 1;
+    const int hd = p.head_dim, hd2 = hd >> 1, hd8 = hd2 >> 2, kst = hd2 + 4;
     const int kvh = h / (p.heads / p.kv_heads);
     const int qd = p.heads * hd;
-    const int j0 = sp * kSplit;
-    const int nt = min(kSplit, ctx - j0);
-    for (int i = tid; i < nr * hd; i += 128) {
-        const int rr = i / hd, dd = i - rr * hd;
-        sm.q[rr][dd] = __ldcg(p.q + (size_t)rr * qd + (size_t)h * hd + dd);
-    }
-    {
-        // the page of this head is nt * hd contiguous halves: 16-byte loads
-        const int page = p.block_table[sp];
-        const size_t off = (((size_t)page * p.kv_heads + kvh) * kPageSize) * hd2;
-        const uint4* kg = reinterpret_cast<const uint4*>(reinterpret_cast<const uint32_t*>(p.kv.k) + off);
-        const uint4* vg = reinterpret_cast<const uint4*>(reinterpret_cast<const uint32_t*>(p.kv.v) + off);
-        const int hd8 = hd2 >> 2;  // 16-byte chunks per key
-#pragma unroll 4
-        for (int i = tid; i < nt * hd8; i += 128) {
-            const uint4 kv4 = __ldcg(kg + i);
-            const uint4 vv4 = __ldcg(vg + i);
-            const int key = i / hd8, c = (i - key * hd8) * 4;
-            sm.K[key][c] = kv4.x;
-            sm.K[key][c + 1] = kv4.y;
-            sm.K[key][c + 2] = kv4.z;
-            sm.K[key][c + 3] = kv4.w;
-            *reinterpret_cast<uint4*>(&sm.V[key][c]) = vv4;
+    float* q_s = reinterpret_cast<float*>(smem + kAttnQ);
+    float* sc = reinterpret_cast<float*>(smem + kAttnSc);
+    uint32_t* Ks = reinterpret_cast<uint32_t*>(smem + kAttnK);
+    uint32_t* Vs = reinterpret_cast<uint32_t*>(smem + kAttnV);
+    float* m_run = reinterpret_cast<float*>(smem + kAttnML);
+    float* l_run = m_run + kMaxRows;
+    float* alpha = l_run + kMaxRows;
+    const uint32_t* kg = reinterpret_cast<const uint32_t*>(p.kv.k);
+    const uint32_t* vg = reinterpret_cast<const uint32_t*>(p.kv.v);
+    const int nchunks = (ctx + kAChunk - 1) / kAChunk;
+    auto load = [&](int c) {
+        const int k0 = c * kAChunk, nt = min(kAChunk, ctx - k0);
+        uint32_t* Kb = Ks + (c & 1) * kAChunk * kAKst;
+        uint32_t* Vb = Vs + (c & 1) * kAChunk * (kHdMax / 2);
+        for (int i = tid; i < nt * hd8; i += kCThreads) {
+            const int key = i / hd8, cc = (i - key * hd8) * 4;
+            const int slot = k0 + key;
+            const size_t off =
+                (((size_t)p.block_table[slot / kPageSize] * p.kv_heads + kvh) * kPageSize + (slot % kPageSize)) * hd2 +
+                cc;
+            cp16(Kb + key * kst + cc, kg + off);
+            cp16(Vb + key * hd2 + cc, vg + off);
         }
+        cp_commit();
+    };
+    load(0);
+    for (int i = tid; i < nr * hd; i += kCThreads) {
+        const int rr = i / hd, dd = i - rr * hd;
+        q_s[rr * kHdMax + dd] = __ldcg(p.q + (size_t)rr * qd + (size_t)h * hd + dd);
     }
-    abar();
+    if (tid < kMaxRows) {
+        m_run[tid] = -INFINITY;
+        l_run[tid] = 0.0f;
+    }
     const float scale = __fdiv_rn(1.0f, sqrtf((float)hd));
-    {
-        const int key = lane + 32 * (warp & 1);
-        const int rb = warp >> 1;
-        float acc[kMaxRows / 2];
+    // P.V: thread -> (dimension pair d2, row group g of G), rows g, g + G
+    const int G = kCThreads / hd2;
+    const int d2 = tid % hd2, g = tid / hd2;
+    const bool pv = g < G;
+    float a0[2] = {0.0f, 0.0f}, a1[2] = {0.0f, 0.0f};
+    for (int c = 0; c < nchunks; c++) {
+        if (c + 1 < nchunks) {
+            load(c + 1);
+            cp_wait<1>();
+        } else {
+            cp_wait<0>();
+        }
+        cbar();
+        const int k0 = c * kAChunk, nt = min(kAChunk, ctx - k0);
+        const uint32_t* Kb = Ks + (c & 1) * kAChunk * kAKst;
+        const uint32_t* Vb = Vs + (c & 1) * kAChunk * (kHdMax / 2);
+        {   // scores: thread -> key (tid % 64), rows rq, rq + 4
+            const int key = tid & (kAChunk - 1), rq = tid / kAChunk;
+            float acc[2] = {0.0f, 0.0f};
+            if (key < nt) {
+                const uint4* kr = reinterpret_cast<const uint4*>(Kb + key * kst);
+                for (int e4 = 0; e4 < hd8; e4++) {
+                    const uint4 kw = kr[e4];
+                    const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&kw.x));
+                    const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&kw.y));
+                    const float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&kw.z));
+                    const float2 f3 = __half22float2(*reinterpret_cast<const __half2*>(&kw.w));
 #pragma unroll
-        for (int i = 0; i < kMaxRows / 2; i++) acc[i] = 0.0f;
-        if (key < nt) {
-            for (int e = 0; e < hd2; e++) {
-                const float2 kf = __half22float2(*reinterpret_cast<const __half2*>(&sm.K[key][e]));
+                    for (int i = 0; i < 2; i++) {
+                        const int rr = rq + 4 * i;
+                        if (rr < nr) {
+                            const float4 qa = *reinterpret_cast<const float4*>(&q_s[rr * kHdMax + 8 * e4]);
+                            const float4 qb = *reinterpret_cast<const float4*>(&q_s[rr * kHdMax + 8 * e4 + 4]);
+                            float v = acc[i];
+                            v = __fmaf_rn(qa.x, f0.x, v);
+                            v = __fmaf_rn(qa.y, f0.y, v);
+                            v = __fmaf_rn(qa.z, f1.x, v);
+                            v = __fmaf_rn(qa.w, f1.y, v);
+                            v = __fmaf_rn(qb.x, f2.x, v);
+                            v = __fmaf_rn(qb.y, f2.y, v);
+                            v = __fmaf_rn(qb.z, f3.x, v);
+                            v = __fmaf_rn(qb.w, f3.y, v);
+                            acc[i] = v;
+                        }
+                    }
+                }
+            }
+            const int j = k0 + key;
 #pragma unroll
-                for (int i = 0; i < kMaxRows / 2; i++) {
-                    const int rr = rb + 2 * i;
+            for (int i = 0; i < 2; i++) {
+                const int rr = rq + 4 * i;
+                if (rr < nr) {
+                    bool vis = key < nt;
+                    if (vis && j >= base) {
+                        const int jj = j - base;
+                        vis = p.mask ? (p.mask[(size_t)rr * M + jj] != 0) : (jj <= rr);
+                    }
+                    sc[rr * kAChunk + key] = vis ? __fmul_rn(acc[i], scale) : -INFINITY;
+                }
+            }
+        }
+        cbar();
+        // online softmax: warp w -> row w; lane -> keys lane, lane + 32
+        if (warp < nr) {
+            const float s0 = sc[warp * kAChunk + lane], s1 = sc[warp * kAChunk + lane + 32];
+            const float mx = warp_max(fmaxf(s0, s1));
+            const float m_old = m_run[warp];
+            const float m_new = fmaxf(m_old, mx);
+            const float e0 = s0 == -INFINITY ? 0.0f : expf(__fsub_rn(s0, m_new));
+            const float e1 = s1 == -INFINITY ? 0.0f : expf(__fsub_rn(s1, m_new));
+            sc[warp * kAChunk + lane] = e0;
+            sc[warp * kAChunk + lane + 32] = e1;
+            const float sum = warp_sum(e0 + e1);
+            if (lane == 0) {
+                const float al = m_old == -INFINITY ? 0.0f : expf(__fsub_rn(m_old, m_new));
+                alpha[warp] = al;
+                l_run[warp] = __fmaf_rn(l_run[warp], al, sum);
+                m_run[warp] = m_new;
+            }
+        }
+        cbar();
+        if (pv) {
+#pragma unroll
+            for (int i = 0; i < 2; i++) {
+                const int rr = g + G * i;
+                if (rr < nr) {
+                    a0[i] *= alpha[rr];
+                    a1[i] *= alpha[rr];
+                }
+            }
+            for (int tt = 0; tt < nt; tt++) {
+                const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&Vb[tt * hd2 + d2]));
+#pragma unroll
+                for (int i = 0; i < 2; i++) {
+                    const int rr = g + G * i;
                     if (rr < nr) {
-                        const float2 qf = *reinterpret_cast<const float2*>(&sm.q[rr][2 * e]);
-                        acc[i] = __fmaf_rn(qf.x, kf.x, acc[i]);
-                        acc[i] = __fmaf_rn(qf.y, kf.y, acc[i]);
+                        const float w = sc[rr * kAChunk + tt];
+                        a0[i] = __fmaf_rn(w, v.x, a0[i]);
+                        a1[i] = __fmaf_rn(w, v.y, a1[i]);
                     }
                 }
             }
         }
-        const int j = j0 + key;
+        cbar();  // the chunk's buffers and scores are free again
+    }
+    if (pv) {
 #pragma unroll
-        for (int i = 0; i < kMaxRows / 2; i++) {
-            const int rr = rb + 2 * i;
+        for (int i = 0; i < 2; i++) {
+            const int rr = g + G * i;
             if (rr < nr) {
-                bool vis = key < nt;
-                if (vis && j >= base) {
-                    const int jj = j - base;
-                    vis = p.mask ? (p.mask[(size_t)rr * M + jj] != 0) : (jj <= rr);
-                }
-                sm.sc[rr][key] = vis ? __fmul_rn(acc[i], scale) : -INFINITY;
-            }
-        }
-    }
-    abar();
-    for (int rr = warp; rr < nr; rr += 4) {
-        const float s0 = sm.sc[rr][lane], s1 = sm.sc[rr][lane + 32];
-        const float mx = warp_max(fmaxf(s0, s1));
-        float e0 = 0.0f, e1 = 0.0f;
-        if (mx != -INFINITY) {
-            e0 = s0 == -INFINITY ? 0.0f : expf(__fsub_rn(s0, mx));
-            e1 = s1 == -INFINITY ? 0.0f : expf(__fsub_rn(s1, mx));
-        }
-        sm.sc[rr][lane] = e0;
-        sm.sc[rr][lane + 32] = e1;
-        const float sum = warp_sum(e0 + e1);
-        if (lane == 0) {
-            sm.ml[rr][0] = mx;
-            sm.ml[rr][1] = sum;
-        }
-    }
-    abar();
-    const int pstride = hd + 2;
-    float* part = p.part + (((size_t)h * nsplit_max + sp) * kMaxRows) * pstride;
-    if (tid < 2 * hd2) {
-        const int d2 = tid % hd2, rb = tid / hd2;
-        float a0[kMaxRows / 2], a1[kMaxRows / 2];
-#pragma unroll
-        for (int i = 0; i < kMaxRows / 2; i++) a0[i] = a1[i] = 0.0f;
-        for (int tt = 0; tt < nt; tt++) {
-            const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&sm.V[tt][d2]));
-#pragma unroll
-            for (int i = 0; i < kMaxRows / 2; i++) {
-                const int rr = rb + 2 * i;
-                if (rr < nr) {
-                    const float w = sm.sc[rr][tt];
-                    a0[i] = __fmaf_rn(w, v.x, a0[i]);
-                    a1[i] = __fmaf_rn(w, v.y, a1[i]);
+                const float inv_l = l_run[rr];
+                const float o0 = __fdiv_rn(a0[i], inv_l), o1 = __fdiv_rn(a1[i], inv_l);
+                const size_t idx = (size_t)rr * qd + (size_t)h * hd + 2 * d2;
+                p.out_q[idx] = (uint8_t)quant_u8(o0);
+                p.out_q[idx + 1] = (uint8_t)quant_u8(o1);
+                if (p.out_f) {
+                    p.out_f[idx] = o0;
+                    p.out_f[idx + 1] = o1;
                 }
             }
         }
-#pragma unroll
-        for (int i = 0; i < kMaxRows / 2; i++) {
-            const int rr = rb + 2 * i;
-            if (rr < nr) {
-                part[(size_t)rr * pstride + 2 + 2 * d2] = a0[i];
-                part[(size_t)rr * pstride + 3 + 2 * d2] = a1[i];
-            }
-        }
     }
-    if (tid < nr) {
-        part[(size_t)tid * pstride] = sm.ml[tid][0];
-        part[(size_t)tid * pstride + 1] = sm.ml[tid][1];
-    }
-    __threadfence();
-    abar();
-    if (tid == 0) sm.ticket = atomicAdd(&p.counters[h], 1);
-    abar();
-    if (sm.ticket != nsplit - 1) return;
-    __threadfence();
-    const float* ph = p.part + ((size_t)h * nsplit_max * kMaxRows) * pstride;
-    for (int i = tid; i < nr * hd; i += 128) {
-        const int rr = i / hd, dd = i - rr * hd;
-        float gm = -INFINITY;
-        for (int s2 = 0; s2 < nsplit; s2++) gm = fmaxf(gm, __ldcg(ph + ((size_t)s2 * kMaxRows + rr) * pstride));
-        float L = 0.0f, O = 0.0f;
-        for (int s2 = 0; s2 < nsplit; s2++) {
-            const float* q = ph + ((size_t)s2 * kMaxRows + rr) * pstride;
-            const float m = __ldcg(q);
-            if (m == -INFINITY) continue;
-            const float wgt = expf(__fsub_rn(m, gm));
-            L = __fmaf_rn(__ldcg(q + 1), wgt, L);
-            O = __fmaf_rn(__ldcg(q + 2 + dd), wgt, O);
-        }
-        const float o = __fdiv_rn(O, L);
-        const size_t idx = (size_t)rr * qd + (size_t)h * hd + dd;
-        p.out_q[idx] = (uint8_t)quant_u8(o);
-        if (p.out_f) p.out_f[idx] = o;
-    }
-    if (tid == 0) p.counters[h] = 0;
 }
 
 // ---------------------------------------------------------------- control (CTA 0, 256 threads)
@@ -710,15 +759,12 @@ __global__ void __launch_bounds__(kThr, 1) step_kernel(const StepParams p, int* 
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[kMaxSlots];
     __shared__ __align__(8) uint64_t empty[kMaxSlots];
-    __shared__ __align__(8) uint64_t mdone[kNB];
-    __shared__ __align__(8) uint64_t tfree[kNB];
-    __shared__ __align__(8) uint64_t actrdy;
-    __shared__ uint32_t tmem_base;
     __shared__ unsigned long long best_s[kMaxRows];
     __shared__ unsigned long long red8[kCW];
     __shared__ int tgt[kMaxRows];
     __shared__ int ok_s, skip_s;
     __shared__ float nred[kMaxRows * kCW];
+    __shared__ float red[kCW][32][4];  // per-warp partial sums of a tile (K split over warps)
     __shared__ EpiSmem es;
     // phase descriptors, double-buffered: phase ph + 1 is loaded into
     // registers at the start of phase ph and stored here at its end
@@ -726,7 +772,7 @@ __global__ void __launch_bounds__(kThr, 1) step_kernel(const StepParams p, int* 
     static_assert(sizeof(Phase) % sizeof(uint2) == 0, "Phase is copied in 8-byte words");
     __shared__ uint2 sph[2][kPW];
 
-    // uniform early exits, before any barrier or TMEM allocation
+    // uniform early exits, before any barrier
     if (__ldcg(p.done)) return;  // the whole decode already finished
     if ((saddr(smem) + p.region_bytes) & 1023) {
         if (threadIdx.x == 0) atomicOr(err, kErrRing);  // the swizzled ring needs 1024-byte alignment
@@ -737,32 +783,16 @@ __global__ void __launch_bounds__(kThr, 1) step_kernel(const StepParams p, int* 
     rg.base = smem + p.region_bytes;
     rg.full = full;
     rg.empty = empty;
-    rg.mdone = mdone;
-    rg.tfree = tfree;
-    rg.actrdy = &actrdy;
     rg.S = p.S;
     rg.slot = p.slot_bytes;
     if (threadIdx.x == 0) {
         for (int i = 0; i < p.S; i++) {
             mb_init(&full[i], 1);
-            mb_init(&empty[i], kRW);
+            mb_init(&empty[i], kCW);
         }
-        for (int i = 0; i < kNB; i++) {
-            mb_init(&mdone[i], 1);
-            mb_init(&tfree[i], kRW);
-        }
-        mb_init(&actrdy, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == kMmaWarp) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&tmem_base)),
-                     "n"(kTmemCols));
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-    }
-    tc_fence_before();
     __syncthreads();
-    tc_fence_after();
-    rg.tmem = tmem_base;
 
     if (warp == kProdWarp) {
         // ---------------- producer: every GEMV phase's stages, in order ----------------
@@ -786,12 +816,11 @@ __global__ void __launch_bounds__(kThr, 1) step_kernel(const StepParams p, int* 
                     const int r = geo.row0 + tile * kTileRows;
                     const int rows = min(kTileRows, geo.row1 - r);
                     uint8_t* dw = rg.base + (size_t)sl * p.slot_bytes;
-                    mb_expect(&full[sl], (uint32_t)(kPPS * rows * (kP + kP / 16)));
-#pragma unroll
-                    for (int j = 0; j < kPPS; j++) {
-                        const size_t pan = (size_t)(pp * kPPS + j);
-                        bulk(dw + j * kTileRows * kP, P->g.w + (pan * N + r) * kP, (uint32_t)(rows * kP), &full[sl]);
-                        bulk(dw + kPPS * kTileRows * kP + j * kTileRows * (kP / 16), sb + (pan * N + r) * (kP / 16),
+                    mb_expect(&full[sl], (uint32_t)(geo.W * rows * (kP + kP / 16)));
+                    for (int j = 0; j < geo.W; j++) {
+                        const size_t pan = (size_t)(pp * geo.W + j);
+                        bulk(dw + j * geo.rs * kP, P->g.w + (pan * N + r) * kP, (uint32_t)(rows * kP), &full[sl]);
+                        bulk(dw + geo.W * geo.rs * kP + j * geo.rs * (kP / 16), sb + (pan * N + r) * (kP / 16),
                              (uint32_t)(rows * (kP / 16)), &full[sl]);
                     }
                 }
@@ -800,58 +829,9 @@ __global__ void __launch_bounds__(kThr, 1) step_kernel(const StepParams p, int* 
             for (int t = s - p.S < 0 ? 0 : s - p.S; t < s; t++)
                 if (!mb_wait(&full[t % p.S], (t / p.S) & 1, err)) break;
         }
-    } else if (warp == kMmaWarp) {
-        // ---------------- MMA issuer: every GEMV phase's stages, in order ----------------
-        int s = 0, g = 0, issued = 0;
-        bool ok = true;
-        const uint32_t act_addr = saddr(smem);
-        for (int ph = 0; ph < p.nphases && ok; ph++) {
-            const Phase* P = p.phases + ph;
-            if (P->kind != PH_GEMV) continue;
-            GGeo geo;
-            gemv_geo(P->g, blockIdx.x, gridDim.x, geo);
-            unsigned long long* str =
-                p.trace && blockIdx.x == 0 && ph == p.trace_phase ? p.trace + kTr * p.nphases : nullptr;
-            if (!warp_wait(&actrdy, g & 1, err)) {
-                ok = false;
-                break;
-            }
-            g++;
-            for (int i = 0; i < geo.nstages; i++, s++) {
-                const int sl = s % p.S, buf = s % kNB;
-                const int pp = i % geo.nps;
-                if (!warp_wait(&full[sl], (s / p.S) & 1, err)) {
-                    ok = false;
-                    break;
-                }
-                if (s >= kNB && !warp_wait(&tfree[buf], ((s / kNB) - 1) & 1, err)) {
-                    ok = false;
-                    break;
-                }
-                if (str && i < 64 && lane == 0) str[8 * i + 4] = gtime();
-                tc_fence_after();
-                if (lane == 0) {
-                    const uint32_t wbase = saddr(rg.base + (size_t)sl * p.slot_bytes);
-#pragma unroll
-                    for (int kb = 0; kb < kKBS; kb++) {
-                        const int j = kb / (kP / 32), kk = kb % (kP / 32);
-                        const uint64_t da = smem_desc(wbase + j * kTileRows * kP + kk * 32, 16, 1024, 2);
-                        const uint64_t db = smem_desc(act_addr + (uint32_t)((pp * kKBS + kb) * 256), 128, 256, 0);
-                        umma_i8(rg.tmem + (uint32_t)(buf * kCB + kb * 8), da, db);
-                    }
-                    umma_commit(&mdone[buf]);
-                    if (str && i < 64) str[8 * i + 5] = gtime();
-                }
-                __syncwarp();
-                issued = s + 1;
-            }
-        }
-        // the MMAs in flight complete before TMEM is released
-        for (int t = issued - kNB < 0 ? 0 : issued - kNB; t < issued; t++)
-            if (!warp_wait(&mdone[t % kNB], (t / kNB) & 1, err)) break;
     } else {
         // ---------------- consumers ----------------
-        int s = 0, g = 0;
+        int s = 0;
         bool bad = false, skip = false;
         const uint2* gph = reinterpret_cast<const uint2*>(p.phases);
         if (threadIdx.x < kPW) sph[0][threadIdx.x] = __ldg(gph + threadIdx.x);
@@ -864,16 +844,12 @@ __global__ void __launch_bounds__(kThr, 1) step_kernel(const StepParams p, int* 
             const int kind = P.kind;
             if (p.trace && blockIdx.x == 0 && threadIdx.x == 0) p.trace[kTr * ph] = gtime();
             if (kind == PH_GEMV) {
-                gemv_phase(P.g, P.epi, skip || bad, rg, s, g, bad, err, smem, best_s, nred, es,
-                           p.trace && blockIdx.x == 0 ? p.trace + kTr * ph : nullptr,
-                           p.trace && blockIdx.x == 0 && ph == p.trace_phase ? p.trace + kTr * p.nphases : nullptr);
+                gemv_phase(P.g, P.epi, skip || bad, rg, s, bad, err, smem, best_s, nred, es, red,
+                           p.trace && blockIdx.x == 0 ? p.trace + kTr * ph : nullptr);
             } else if (kind == PH_ATTN) {
-                if (!skip && !bad && warp < 4) {
+                if (!skip && !bad) {
                     const AttnParams& a = P.a;
-                    const int nsm = (a.max_ctx + kSplit - 1) / kSplit;
-                    const int units = a.heads * nsm;
-                    for (int u = blockIdx.x; u < units; u += gridDim.x)
-                        attn_unit(a, u / nsm, u % nsm, nsm, *reinterpret_cast<AttnSmem*>(smem));
+                    for (int h = blockIdx.x; h < a.heads; h += gridDim.x) attn_head(a, h, smem);
                 }
             } else if (!skip && !bad && blockIdx.x == 0) {
                 control(kind, P.arg, p.sb, p.K, red8, tgt);
@@ -892,13 +868,6 @@ __global__ void __launch_bounds__(kThr, 1) step_kernel(const StepParams p, int* 
             }
         }
     }
-    // TMEM is released by its owner once every warp is done with it
-    tc_fence_before();
-    __syncthreads();
-    if (warp == kMmaWarp) {
-        tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(rg.tmem), "n"(kTmemCols));
-    }
 }
 
 int g_sms[16] = {0};
@@ -916,7 +885,7 @@ int step_grid() {
 }
 
 bool step_plan(const Phase* ph, int n, StepParams& sp, size_t* smem_bytes) {
-    int region = (int)sizeof(AttnSmem);
+    int region = (int)kAttnBytes;
     for (int i = 0; i < n; i++) {
         if (ph[i].kind != PH_GEMV) continue;
         const GemvParams& g = ph[i].g;
@@ -927,7 +896,7 @@ bool step_plan(const Phase* ph, int n, StepParams& sp, size_t* smem_bytes) {
             const int rows_cta = ((g.N / 8 + grid - 1) / grid) * 8;
             if (rows_cta * g.M > kResFloats) return false;
         }
-        region = region > kMaxRows * g.K ? region : kMaxRows * g.K;  // core-matrix activations
+        region = region > kMaxRows * (g.K + 16) ? region : kMaxRows * (g.K + 16);  // row-major activations
     }
     region = (region + 1023) & ~1023;
     const int avail = kSmemLimit - region;

@@ -24,6 +24,7 @@
 #include <mutex>
 
 #include "fl_common.cuh"
+#include "fl_kernels.h"
 #include "fl_runtime.h"
 #include "fl_tp.h"
 
@@ -134,5 +135,46 @@ FL_API int fl_tp_layout(const fl_model_config_t* cfg, int rank, int size, int* o
     FL_CHECK(tp_layout(cfg->num_heads, cfg->num_kv_heads, cfg->intermediate_size, cfg->vocab_size, rank, size, L));
     const int v[9] = {L.q0, L.nq, L.kv0, L.nkv, L.f0, L.nf, L.v0, L.nv, L.group};
     memcpy(out, v, sizeof(v));
+    return FL_OK;
+}
+
+// The failure path of the tensor-parallel reduction's bounded wait, on one
+// GPU: tp_reduce_kernel waits for arrival counters of a two-rank group that
+// no rank ever increments; after its limit (about two seconds of clock
+// cycles) it records the error word and returns without touching the
+// activations, and fl_cuda_sync reports FL_E_TIMEOUT. The context stays
+// usable. For tests of failure detection; no fault is involved.
+FL_API int fl_cuda_tp_wait_timeout_check(void) {
+    using namespace fl;
+    FL_CHECK(ensure_device());
+    cudaStream_t s = device_stream();
+    if (!s) return set_error(FL_E_NODEV, "no device");
+    float* x = nullptr;
+    unsigned long long* words = nullptr;  // [4] counters of two ranks (two parities), [1] sequence
+    int* arrived = nullptr;
+    FL_CHECK_CUDA(cudaMalloc(&x, sizeof(float) * 256));
+    FL_CHECK_CUDA(cudaMalloc(&words, sizeof(unsigned long long) * 5));
+    FL_CHECK_CUDA(cudaMalloc(&arrived, sizeof(int)));
+    FL_CHECK_CUDA(cudaMemsetAsync(x, 0, sizeof(float) * 256, s));
+    FL_CHECK_CUDA(cudaMemsetAsync(words, 0, sizeof(unsigned long long) * 5, s));
+    FL_CHECK_CUDA(cudaMemsetAsync(arrived, 0, sizeof(int), s));
+    TpReduceParams p = {};
+    p.x = x;
+    p.rows = 1;
+    p.d = 256;
+    p.recv = x;  // never read: the wait gives up first
+    p.cnt = words;
+    p.size = 2;
+    p.cap = 1;
+    p.seq = words + 4;
+    p.ctas_per_push = 1;
+    p.arrived = arrived;
+    const cudaError_t le = launch_tp_reduce(p, s, false);
+    const cudaError_t se = cudaStreamSynchronize(s);
+    cudaFree(x);
+    cudaFree(words);
+    cudaFree(arrived);
+    FL_CHECK_CUDA(le);
+    FL_CHECK_CUDA(se);
     return FL_OK;
 }

@@ -100,6 +100,10 @@ _SIGS = {
     "fl_cuda_init": (I, [I]),
     "fl_cuda_device_count": (I, [C.POINTER(I)]),
     "fl_cuda_sync": (I, []),
+    "fl_cuda_tp_wait_timeout_check": (I, []),
+    "fl_engine_draft_lm": (I, [VP, VP, I, I, I, VP]),
+    "fl_engine_lm_argmax": (I, [VP, VP, VP]),
+    "fl_engine_lm_logits": (I, [VP, VP, VP]),
     "fl_cuda_stream": (VP, []),
     "fl_cuda_malloc": (I, [C.POINTER(VP), SZ]),
     "fl_cuda_free": (I, [VP]),
@@ -184,6 +188,8 @@ _SIGS = {
     "draft_kv_cache_free": (None, [C.POINTER(DraftKV)]),
     "verify_tokens": (I, [VP, C.POINTER(DraftTree), VP, C.POINTER(I), C.POINTER(SpecConfig)]),
     "speculative_generate": (I, [C.POINTER(DraftModel), VP, VP, VP, I, VP, I, C.POINTER(SpecConfig)]),
+    "speculative_decode_step": (I, [C.POINTER(DraftModel), C.POINTER(DraftKV), VP, VP, VP, I, VP, VP,
+                                    C.POINTER(SpecConfig)]),
     "medusa_model_create": (VP, [I, I, I]),
     "medusa_model_load": (I, [VP, C.c_char_p]),
     "medusa_model_free": (None, [VP]),

@@ -85,6 +85,14 @@ int fl_cuda_gemv_i8(const uint8_t* Aq, const dequantized_tensor_t* B, float* C,
 int fl_cuda_block_dots_i8(const float* A, const dequantized_tensor_t* B, int32_t* D,
                           int M, int N, int K, void* stream);
 
+/* Failure detection, no counterpart in the reference: runs the
+ * tensor-parallel reduction kernel on the library stream against the arrival
+ * counters of a two-rank group that nobody increments. Its bounded wait gives
+ * up after about two seconds, records the device error word and returns; the
+ * following fl_cuda_sync() returns FL_E_TIMEOUT and clears the word, and the
+ * device stays usable. Returns FL_OK once the kernel has finished. */
+int fl_cuda_tp_wait_timeout_check(void);
+
 /* fl_cuda_block_dots_i8 without any allocation: no counterpart in the
  * reference. The quantized activations go to a fixed device scratch of
  * FL_NOALLOC_SCRATCH_BYTES in the library's static device memory (one per
@@ -155,7 +163,9 @@ typedef struct {
     int vocab_size;          /* 32064 for Phi-3-mini                     */
     int hidden_size;         /* d                                        */
     int intermediate_size;   /* SwiGLU width                             */
-    int num_layers;          /* base decoder layers                      */
+    int num_layers;          /* base decoder layers (0: an engine holding only
+                                a draft stack or Medusa heads, with the
+                                embedding and LM head, for host targets) */
     int num_heads;           /* query heads                              */
     int num_kv_heads;        /* key/value heads (GQA when < num_heads)   */
     int head_dim;
@@ -425,6 +435,23 @@ int fl_engine_bench_linear(fl_engine_t* e, int stack, int kind, int M, int reps,
  * M new rows over a context of ctx slots (the cache's current contents),
  * captured back to back and replayed reps times. */
 int fl_engine_bench_attention(fl_engine_t* e, int stack, int M, int ctx, int reps, double* us_per_launch);
+
+/* Host-target support (no counterpart in the reference): passes for an
+ * engine created with num_layers = 0, which holds only a draft stack or
+ * Medusa heads with the embedding and LM head, for callers whose target or
+ * base model is their own host function.
+ * fl_engine_draft_lm: the draft as a plain language model over token
+ * embeddings (input at position i is E[t_i]): the nrows tokens rows_tok at
+ * positions pos0 .. pos0 + nrows - 1 (not yet in the draft cache) in one
+ * pass, drafts[0] = the last row's LM-head argmax, then each draft token fed
+ * back at the next position; K tokens in drafts. The draft cache then holds
+ * the positions below pos0 + nrows + K - 1.
+ * fl_engine_lm_argmax / fl_engine_lm_logits: the LM head (final RMSNorm
+ * included) over one host feature row F [hidden]: its argmax (ties to the
+ * lowest index) or its logits [vocab] on the host. */
+int fl_engine_draft_lm(fl_engine_t* e, const int* rows_tok, int nrows, int pos0, int K, int* drafts);
+int fl_engine_lm_argmax(fl_engine_t* e, const float* F, int* tok);
+int fl_engine_lm_logits(fl_engine_t* e, const float* F, float* logits);
 
 /* Callback-level position of the base cache: tokens appended through
  * fl_cuda_target_forward / fl_cuda_base_forward land at this position.

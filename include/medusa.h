@@ -25,6 +25,21 @@
  * through the base model in one pass with a tree attention mask; the longest
  * root-to-leaf path whose every token equals the base model's greedy choice
  * at its parent is accepted, plus the base model's token after it.
+ *
+ * Bases. base_forward(model, tokens, len, hidden, hidden_size) appends the
+ * `len` tokens to the base's context and writes the last one's last-layer
+ * feature F [hidden_size]. fl_cuda_base_forward is that function for the
+ * device engine (model = fl_engine_t*), which verifies a whole tree in one
+ * tree-masked pass. Any other base_forward is the caller's own host function
+ * (model may be NULL): the heads and an LM head (the Medusa model's, from
+ * its synthetic seed; seed 0 heads if it never loaded any) run on a device
+ * engine of the Medusa model's own, and the tree is walked on the host --
+ * the current node's token is fed, the base's next token g (LM-head argmax
+ * of the returned F, or a draw at temperature > 0: top-p 1, Philox key
+ * (0, 0)) is emitted, and the walk goes on while g is a child of the node.
+ * The base is given only tokens that are part of the output, so it never
+ * rolls back; each emitted token costs one base_forward call.
+ * medusa_verify_tree needs the device engine (a tree carries no context).
  */
 #ifndef FL_MEDUSA_H
 #define FL_MEDUSA_H
@@ -115,11 +130,13 @@ int medusa_decode_step(void* base_model,
                        int current_token, int* output_tokens, int* num_output,
                        const medusa_config_t* config);
 
-/* base_model: an fl_engine_t* created with medusa_heads >= the heads used;
- * base_forward: fl_cuda_base_forward. Greedy acceptance only (temperature
- * <= 0). The heads' weights are loaded into the engine on the first call.
- * Prefill prompt_len float-encoded token ids, then Medusa steps until
- * num_tokens new tokens exist. Returns the count written or -1. */
+/* base_model: an fl_engine_t* created with medusa_heads >= the heads used
+ * and base_forward fl_cuda_base_forward (greedy acceptance only,
+ * temperature <= 0; the heads' weights are loaded into the engine on the
+ * first call), or the caller's own host base_forward (see "Bases";
+ * temperature > 0 draws). prompt_hidden holds prompt_len token ids as
+ * floats. Medusa steps run until num_tokens new tokens exist. Returns the
+ * count written or -1. */
 int medusa_generate(void* base_model,
                     void (*base_forward)(void*, const int*, int, float*, int),
                     medusa_model_t* medusa, const float* prompt_hidden,

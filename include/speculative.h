@@ -42,6 +42,32 @@
  * draft_model_t each point to an array of `num_layers` tensors (the
  * reference struct holds one set; a multi-layer draft needs one per layer).
  * w_lm_head points to the shared LM head.
+ *
+ * Targets. target_forward(model, input, output, len) appends the `len`
+ * token ids in `input` (floats, exact below 2^24) to the target's context
+ * and writes `len` rows of next-token logits [len, vocab] to `output`.
+ * fl_cuda_target_forward (fl_cuda.h) is that function for the device engine
+ * (model = fl_engine_t*); the library then verifies all K+1 rows of a step
+ * in one pass and rolls the engine's cache back to the accepted prefix.
+ * Any other target_forward is the caller's own host function with the same
+ * contract (model may be NULL); the library then
+ *   - runs the draft on a device engine of its own (no base layers: the
+ *     draft stack, the embedding and LM head from the draft's synthetic seed,
+ *     seed 0 weights if the draft never loaded any) as a plain language
+ *     model over token embeddings (no base features exist on the host),
+ *   - feeds the target only tokens that are already part of the output, one
+ *     per call during verification (the current token, then each accepted
+ *     draft), so a target that keeps per-position state never rolls back;
+ *     a step costs the target a+1 calls instead of one,
+ *   - decides with the rule above from the target's logits, drafts greedy:
+ *     greedy acceptance, or (temperature > 0) draft d kept with probability
+ *     p(d) (U * Mp < 2^24 * E_p(d)) and otherwise a draw from p without d,
+ *     at top-p 1 with Philox key (seed 0, sequence 0).
+ *
+ * Prompts. prompt_hidden holds prompt_len token ids as floats (not hidden
+ * vectors, which the reference's header implies): a device target must
+ * prefill its KV cache from tokens, and a host target receives the same ids.
+ * Ids outside [0, vocab) are read as 0 (inference.c:420-426).
  */
 #ifndef FL_SPECULATIVE_H
 #define FL_SPECULATIVE_H
@@ -135,18 +161,22 @@ int draft_tokens(draft_model_t* model, draft_kv_cache_t* cache,
  * model's logits for the K+1 verify rows, [(K+1), vocab] host floats, with
  * K = tree->num_tokens and vocab the one recorded in the tree by
  * draft_tokens. Greedy: accepted_tokens gets the accepted drafts followed by
- * the base model's next token; *num_accepted = number of accepted drafts.
- * Returns *num_accepted, or -1 on bad arguments. */
+ * the base model's next token -- up to K+1 entries, one more than the
+ * reference's "0 to K", so size it K+1; *num_accepted = number of accepted
+ * drafts. Returns *num_accepted, or -1 on bad arguments. */
 int verify_tokens(const float* target_hidden, const draft_tree_t* tree,
                   int* accepted_tokens, int* num_accepted,
                   const speculative_config_t* config);
 
 /* One draft + verify + accept step (reference speculative.h:146).
- * target_model must be an fl_engine_t* and target_forward must be
- * fl_cuda_target_forward (fl_cuda.h): the base model runs on the GPU.
- * current_hidden / current_token describe the next position as in
- * draft_tokens. Writes 1..K+1 tokens to output_tokens, sets *num_output and
- * returns it; -1 on error. */
+ * current_token is the newest output token (not yet given to the target).
+ * With fl_cuda_target_forward, target_model is the fl_engine_t* and
+ * current_hidden the base feature of the position before current_token (as
+ * in draft_tokens). With a host target_forward, current_hidden is unused
+ * and the draft's own cache holds the positions before
+ * draft_cache->cache_len, where current_token goes; cache_len advances past
+ * the emitted tokens. Writes 1..K+1 tokens to output_tokens, sets
+ * *num_output and returns it; -1 on error. */
 int speculative_decode_step(draft_model_t* draft, draft_kv_cache_t* draft_cache,
                             void* target_model,
                             void (*target_forward)(void* model, const float* input,
@@ -156,10 +186,10 @@ int speculative_decode_step(draft_model_t* draft, draft_kv_cache_t* draft_cache,
                             const speculative_config_t* config);
 
 /* Full loop (reference speculative.h:173). prompt_hidden holds the prompt's
- * prompt_len token ids as floats (exact below 2^24). The base model
- * (target_model, an fl_engine_t*) prefills them, then speculative steps run
- * until num_tokens new tokens exist. Returns the number written (num_tokens
- * on success), -1 on error. */
+ * prompt_len token ids as floats. The target (an fl_engine_t* with
+ * fl_cuda_target_forward, or the caller's host function, see "Targets")
+ * takes the prompt, then speculative steps run until num_tokens new tokens
+ * exist. Returns the number written (num_tokens on success), -1 on error. */
 int speculative_generate(draft_model_t* draft, void* target_model,
                          void (*target_forward)(void*, const float*, float*, int),
                          const float* prompt_hidden, int prompt_len,

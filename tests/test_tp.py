@@ -114,3 +114,28 @@ def test_two_rank_decode_matches_oracle(gpu, orc):
         assert bd.size == 0 or bm[bd[0]] < 1e-2, f"batch sequence {i} diverges at {bd[:1]}"
         td = np.nonzero(res[0][5][i] != bw)[0]
         assert td.size == 0 or bm[td[0]] < 1e-2, f"batched tree sequence {i} diverges at {td[:1]}"
+
+
+@pytest.mark.gpu
+def test_bounded_wait_reports_timeout(gpu):
+    """A device wait that runs out (arrival counters nobody increments)
+    ends the kernel, sets the error word, and fl_cuda_sync reports
+    FL_E_TIMEOUT once; the device stays usable afterwards."""
+    import time
+    FL_E_TIMEOUT = -5
+    t0 = time.time()
+    assert gpu.fl_cuda_tp_wait_timeout_check() == 0, gpu.err()
+    assert time.time() - t0 < 30
+    assert gpu.fl_cuda_sync() == FL_E_TIMEOUT
+    assert gpu.fl_cuda_sync() == 0
+    w, d = gpu.synth_q4_0_i8(3, 77, 64, 256)
+    from test_gemv_gpu import Dev
+    import ctypes as C
+    from flb200 import block_tensor
+    t = block_tensor(w, d)
+    assert gpu.fl_cuda_upload_tensor(C.byref(t)) == 0
+    A = np.ones((1, 256), np.float32)
+    dA = Dev(gpu, A.nbytes).put(A)
+    dO = Dev(gpu, 64 * 4)
+    assert gpu.fl_cuda_matmul_i8(dA.p, C.byref(t), dO.p, 1, 64, 256, None) == 0
+    assert gpu.fl_cuda_sync() == 0
