@@ -606,6 +606,18 @@ void merge_topw(const unsigned long long* keys, int ranks, size_t rank_stride, i
 
 }  // namespace
 
+// Host entry points of the tensor-parallel candidate merge (for tests of the
+// control flow without a GPU): a logit's orderable argmax key, and the merge
+// of the ranks' top-width keys into the width best tokens.
+FL_API unsigned long long fl_argmax_key(float v, int index) { return argmax_key(v, index); }
+
+FL_API int fl_tp_merge_topw(const unsigned long long* keys, int ranks, size_t rank_stride, int width, int* tok) {
+    if (!keys || !tok || ranks < 1 || width < 1 || rank_stride < (size_t)width)
+        return set_error(FL_E_INVAL, "tp_merge_topw: bad arguments");
+    merge_topw(keys, ranks, rank_stride, width, tok);
+    return FL_OK;
+}
+
 // Static draft tree (EAGLE-style): the draft chain c_1..c_K plus, at every
 // depth j, the draft's next w - 1 candidates after c_j, all children of
 // c_{j-1} (c_0 = the newest committed token). Nodes in depth order: root,

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
+#include <string.h>
 
 #define FL_API extern "C" __attribute__((visibility("default")))
 
@@ -288,12 +289,17 @@ __device__ __forceinline__ uint4 ld_stream16(const void* p) {
 
 // Orderable 64-bit key for a deterministic argmax: larger value wins, ties go
 // to the lower index (inference.c:104-111 keeps the first maximum).
-__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+__host__ __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+#ifdef __CUDA_ARCH__
     uint32_t b = __float_as_uint(v);
+#else
+    uint32_t b;
+    memcpy(&b, &v, sizeof(b));
+#endif
     b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
     return ((unsigned long long)b << 32) | (uint32_t)(0x7fffffff - idx);
 }
-__device__ __forceinline__ int argmax_key_index(unsigned long long k) {
+__host__ __device__ __forceinline__ int argmax_key_index(unsigned long long k) {
     return 0x7fffffff - (int)(uint32_t)(k & 0xffffffffu);
 }
 __device__ __forceinline__ float argmax_key_value(unsigned long long k) {

@@ -101,6 +101,8 @@ _SIGS = {
     "fl_cuda_device_count": (I, [C.POINTER(I)]),
     "fl_cuda_sync": (I, []),
     "fl_cuda_tp_wait_timeout_check": (I, []),
+    "fl_argmax_key": (C.c_uint64, [C.c_float, I]),
+    "fl_tp_merge_topw": (I, [VP, I, C.c_size_t, I, VP]),
     "fl_engine_draft_lm": (I, [VP, VP, I, I, I, VP]),
     "fl_engine_lm_argmax": (I, [VP, VP, VP]),
     "fl_engine_lm_logits": (I, [VP, VP, VP]),

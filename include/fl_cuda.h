@@ -197,6 +197,15 @@ int fl_tp_unique_id(unsigned char* id);
  * heads, first FFN feature, features, first vocabulary row, rows, Q heads per
  * KV head}. */
 int fl_tp_layout(const fl_model_config_t* cfg, int rank, int size, int* out);
+/* The orderable 64-bit key of a logit v at vocabulary index `index`
+ * (larger value wins, ties to the lower index: inference.c:104-111), as the
+ * LM-head epilogue builds it; the tensor-parallel argmax of a row is the
+ * largest key over the ranks' local best keys (global indices). */
+unsigned long long fl_argmax_key(float v, int index);
+/* Tensor-parallel draft-tree candidates: the `width` best tokens of one
+ * depth from every rank's top-width keys (keys[r * rank_stride + c], c <
+ * width, global indices), best first. Host code. */
+int fl_tp_merge_topw(const unsigned long long* keys, int ranks, size_t rank_stride, int width, int* tok);
 void fl_engine_destroy(fl_engine_t* e);
 
 /* Loads one INT8 linear from host arrays: stack/layer/proj as in

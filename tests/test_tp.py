@@ -1,6 +1,8 @@
 """Tensor parallelism: the shard layout (CPU) and a 2-rank decode on two GPUs
 (skipped with fewer) that must give identical streams on both ranks, equal
 to the oracle's under the near-tie rule."""
+import ctypes as C
+
 import numpy as np
 import pytest
 
@@ -139,3 +141,75 @@ def test_bounded_wait_reports_timeout(gpu):
     dO = Dev(gpu, 64 * 4)
     assert gpu.fl_cuda_matmul_i8(dA.p, C.byref(t), dO.p, 1, 64, 256, None) == 0
     assert gpu.fl_cuda_sync() == 0
+
+
+# ---------------------------------------------------------------------------
+# The tensor-parallel control flow on CPU (gloo, world size 2): every rank
+# holds its vocabulary slice of the LM-head logits (fl_tp_layout), forms its
+# local best keys (fl_argmax_key, global indices), the keys are all-gathered,
+# and the argmax (largest key) and the draft-tree candidates
+# (fl_tp_merge_topw) must equal those of the whole row on every rank.
+# ---------------------------------------------------------------------------
+
+def _tp_worker(rank, world, port, q):
+    import os
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        lib = flb200.Lib()
+        cfg = dict(vocab_size=1001, hidden_size=512, intermediate_size=1024, num_layers=2, num_heads=8,
+                   num_kv_heads=4, head_dim=64, draft_layers=1, medusa_heads=0, max_seq_len=64, rope_theta=1e4,
+                   norm_eps=1e-5)
+        lay = flb200.tp_layout(lib, cfg, rank, world)
+        v0, nv = lay["v0"], lay["nv"]
+        rows, width = 6, 8
+        rng = np.random.default_rng(99)
+        logits = rng.standard_normal((rows, 1001)).astype(np.float32)
+        logits[2, 17] = logits[2, 900] = logits[2].max() + 1.0  # a tie across the two slices
+        local = logits[:, v0:v0 + nv]
+        keys = np.zeros((rows, width), np.uint64)
+        for r in range(rows):
+            k = np.array([lib.fl_argmax_key(float(v), v0 + i) for i, v in enumerate(local[r])], np.uint64)
+            keys[r] = np.sort(k)[::-1][:width]
+        allk = [torch.zeros(rows * width, dtype=torch.int64) for _ in range(world)]
+        dist.all_gather(allk, torch.from_numpy(keys.view(np.int64).reshape(-1)))
+        gathered = np.stack([t.numpy().view(np.uint64).reshape(rows, width) for t in allk])  # [rank, row, w]
+        best = [0x7fffffff - (int(gathered[:, r, 0].max()) & 0xffffffff) for r in range(rows)]
+        top = []
+        for r in range(rows):
+            flat = np.ascontiguousarray(gathered[:, r, :].reshape(-1))
+            tok = np.zeros(width, np.int32)
+            assert lib.fl_tp_merge_topw(flat.ctypes.data_as(C.c_void_p), world, width, width,
+                                        tok.ctypes.data_as(C.c_void_p)) == 0
+            top.append(tok.tolist())
+        q.put((rank, best, top))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp_argmax_and_candidates_merge_gloo():
+    import multiprocessing
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = multiprocessing.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_tp_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=60) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    rng = np.random.default_rng(99)
+    logits = rng.standard_normal((6, 1001)).astype(np.float32)
+    logits[2, 17] = logits[2, 900] = logits[2].max() + 1.0
+    want_best = [int(np.argmax(r)) for r in logits]                    # first maximum wins
+    want_top = [np.lexsort((np.arange(1001), -r))[:8].tolist() for r in logits]  # value desc, index asc
+    for rank, best, top in res:
+        assert best == want_best, rank
+        assert top == want_top, rank
+    assert want_best[2] == 17
