@@ -21,6 +21,11 @@
 
 using namespace fl;
 
+// api_gguf.cu
+int gguf_load_draft(draft_model_t* m, const char* path);
+int gguf_load_medusa(medusa_model_t* m, const char* path);
+int gguf_load_embedding(const char* path, int vocab, int hidden, std::vector<float>& out);
+
 namespace {
 
 // Hidden extension of draft_tree_t: the vocabulary size recorded by
@@ -67,6 +72,7 @@ bool parse_synthetic(const char* path, uint64_t* seed) {
 // use), and the device engines that run a draft or Medusa heads for host
 // targets (a caller's own target_forward / base_forward).
 std::map<const void*, uint64_t> g_seed;
+std::map<const void*, std::string> g_gguf;  // model -> GGUF file it was loaded from
 std::map<const void*, fl_engine_t*> g_host_eng;
 
 uint64_t synth_seed(const void* m) {
@@ -171,8 +177,15 @@ void host_engine_release(const void* m) {
             g_host_eng.erase(it);
         }
         g_seed.erase(m);
+        g_gguf.erase(m);
     }
     if (e) fl_engine_destroy(e);
+}
+
+static std::string gguf_of(const void* m) {
+    std::lock_guard<std::mutex> lk(g_bind_mu);
+    auto it = g_gguf.find(m);
+    return it == g_gguf.end() ? std::string() : it->second;
 }
 
 static fl_engine_t* host_engine_get(const void* m) {
@@ -184,7 +197,8 @@ static fl_engine_t* host_engine_get(const void* m) {
 // Context capacity of the host-target engines (draft cache positions).
 constexpr int kHostCtx = 4096;
 
-static fl_engine_t* host_engine_new(int vocab, int d, int ffn, int draft_layers, int medusa_heads, uint64_t seed) {
+static fl_engine_t* host_engine_new(int vocab, int d, int ffn, int draft_layers, int medusa_heads, uint64_t seed,
+                                    const std::string& gguf) {
     const int hd = head_dim_for(d);
     if (hd == 0) {
         set_error(FL_E_UNSUPPORTED, "host target: hidden size must be a multiple of 64");
@@ -208,8 +222,9 @@ static fl_engine_t* host_engine_new(int vocab, int d, int ffn, int draft_layers,
     fl_engine_t* e = fl_engine_create(&c, dev);
     if (!e) return nullptr;
     std::vector<float> emb((size_t)vocab * d);
-    if (fl_synth_q4_0_f32(seed, FL_TENSOR_ID(3, 0, 0), vocab, d, 0.02f, emb.data()) != FL_OK ||
-        fl_engine_load_embedding(e, emb.data()) != FL_OK) {
+    const int erc = gguf.empty() ? fl_synth_q4_0_f32(seed, FL_TENSOR_ID(3, 0, 0), vocab, d, 0.02f, emb.data())
+                                 : gguf_load_embedding(gguf.c_str(), vocab, d, emb);
+    if (erc != FL_OK || fl_engine_load_embedding(e, emb.data()) != FL_OK) {
         fl_engine_destroy(e);
         return nullptr;
     }
@@ -222,7 +237,7 @@ static fl_engine_t* host_draft_engine(draft_model_t* dm) {
     if (fl_engine_t* e = host_engine_get(dm)) return e;
     if (!dm->w_q_proj[0].weights && draft_model_load(dm, "synthetic:0") != 0) return nullptr;
     fl_engine_t* e = host_engine_new(dm->vocab_size, dm->hidden_size, dm->intermediate_size, dm->num_layers, 0,
-                                     synth_seed(dm));
+                                     synth_seed(dm), gguf_of(dm));
     if (!e) return nullptr;
     if (load_draft_into(e, dm) != FL_OK || !fl_engine_ready(e)) {
         fl_engine_destroy(e);
@@ -241,7 +256,7 @@ fl_engine_t* host_medusa_engine(medusa_model_t* m) {
     if ((!m->heads[0].weights || !m->heads[0].weights->weights) && medusa_model_load(m, "synthetic:0") != 0)
         return nullptr;
     const uint64_t seed = synth_seed(m);
-    fl_engine_t* e = host_engine_new(m->vocab_size, m->hidden_size, 32, 0, m->num_heads, seed);
+    fl_engine_t* e = host_engine_new(m->vocab_size, m->hidden_size, 32, 0, m->num_heads, seed, gguf_of(m));
     if (!e) return nullptr;
     dequantized_tensor_t lm = {};
     unbind(m);
@@ -435,9 +450,12 @@ FL_API draft_model_t* draft_model_create(int num_layers, int hidden_size, int in
 
 FL_API int draft_model_load(draft_model_t* m, const char* path) {
     uint64_t seed = 0;
-    if (!m || !parse_synthetic(path, &seed)) {
-        set_error(FL_E_UNSUPPORTED, "draft_model_load: only \"synthetic:<seed>\" sources are supported");
-        return -1;
+    if (!m || !path) return -1;
+    if (!parse_synthetic(path, &seed)) {
+        if (gguf_load_draft(m, path) != FL_OK) return -1;
+        std::lock_guard<std::mutex> lk(g_bind_mu);
+        g_gguf[m] = path;
+        return 0;
     }
     const int d = m->hidden_size, F = m->intermediate_size;
     const int shapes[7][2] = {{d, d}, {d, d}, {d, d}, {d, d}, {F, d}, {F, d}, {d, F}};
@@ -658,9 +676,12 @@ FL_API medusa_model_t* medusa_model_create(int num_heads, int hidden_size, int v
 
 FL_API int medusa_model_load(medusa_model_t* m, const char* path) {
     uint64_t seed = 0;
-    if (!m || !parse_synthetic(path, &seed)) {
-        set_error(FL_E_UNSUPPORTED, "medusa_model_load: only \"synthetic:<seed>\" sources are supported");
-        return -1;
+    if (!m || !path) return -1;
+    if (!parse_synthetic(path, &seed)) {
+        if (gguf_load_medusa(m, path) != FL_OK) return -1;
+        std::lock_guard<std::mutex> lk(g_bind_mu);
+        g_gguf[m] = path;
+        return 0;
     }
     for (int h = 0; h < m->num_heads; h++)
         if (!m->heads[h].weights ||

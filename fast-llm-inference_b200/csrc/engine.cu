@@ -1010,6 +1010,16 @@ FL_API int fl_engine_load_embedding(fl_engine_t* e, const float* table) {
     return FL_OK;
 }
 
+// Whole-model widths (hidden, q_dim, kv_dim, ffn), not a rank's slice.
+FL_API int fl_engine_dims(const fl_engine_t* e, int* out) {
+    if (!e || !out) return set_error(FL_E_INVAL, "engine_dims: NULL");
+    out[0] = e->c.hidden_size;
+    out[1] = e->c.num_heads * e->c.head_dim;
+    out[2] = e->c.num_kv_heads * e->c.head_dim;
+    out[3] = e->c.intermediate_size;
+    return FL_OK;
+}
+
 FL_API int fl_engine_ready(const fl_engine_t* e) {
     if (!e || !e->embed_loaded || !linear_ready(e->lm)) return 0;
     if (!stack_ready(e->base) || !stack_ready(e->draft)) return 0;

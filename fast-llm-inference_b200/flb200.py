@@ -132,6 +132,8 @@ _SIGS = {
     "fl_engine_destroy": (None, [VP]),
     "fl_engine_load_linear": (I, [VP, I, I, I, VP, VP, I, I]),
     "fl_engine_load_embedding": (I, [VP, VP]),
+    "fl_engine_load_gguf": (I, [VP, I, C.c_char_p]),
+    "fl_engine_dims": (I, [VP, VP]),
     "fl_engine_synthesize": (I, [VP, U64]),
     "fl_engine_ready": (I, [VP]),
     "fl_engine_forward_rows": (I, [VP, I, VP, I, I, VP, VP, VP, VP]),

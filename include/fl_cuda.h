@@ -215,6 +215,17 @@ int fl_engine_load_linear(fl_engine_t* e, int stack, int layer, int proj,
                           const int8_t* w, const uint16_t* d, int rows, int cols);
 /* Token embedding table [vocab, d] f32. */
 int fl_engine_load_embedding(fl_engine_t* e, const float* table);
+/* Whole-model widths of the engine's configuration: out[0] hidden, [1] q_dim
+ * (heads x head_dim), [2] kv_dim, [3] ffn. */
+int fl_engine_dims(const fl_engine_t* e, int* out);
+/* Loads a GGUF file with Q4_0 weights (18-byte blocks, fp16 d; the nibble
+ * order of gguf_loader.c:147-161): blk.<l>.* weights into stack `stack`
+ * (0 base, 1 draft), output.weight as the LM head, token_embd as the
+ * embedding (Q4_0, F16 or F32). Each Q4_0 tensor is pre-dequantized once to
+ * INT8 q-8 plus its fp16 block scales and uploaded. Names as the reference
+ * loader (gguf_loader.c:307-342), fused attn_qkv and Phi-3's gate+up ffn_up
+ * split; norm weights are not applied (unit RMSNorm weights). */
+int fl_engine_load_gguf(fl_engine_t* e, int stack, const char* path);
 /* Generates and loads every tensor with fl_synth_* (std 0.02). */
 int fl_engine_synthesize(fl_engine_t* e, uint64_t seed);
 /* 1 when every tensor the configuration needs has been loaded. */
