@@ -169,35 +169,58 @@ def oracle_weights(orc):
     return w, embed
 
 
-def reference_rows(w):
-    """Per-row-scale tensors for the reference's matmul_dequantized: the
-    same INT8 values in [-8, 7] (no pair-sum saturation) with one scale per
-    row, the row's first block scale times 16 (its epilogue divides by
-    127 * 16, dequantized_tensor.c:235-243). The reference's own loader
-    format ((q-8)*16, dequantized_tensor.c:27-58) saturates the pair sums
-    and collapses these random-init models into a stream that accepts every
-    draft, which would compare a different amount of work per token."""
-    out = {}
-    for key, (wq, dq) in w.items():
-        rs = dq[:, 0].view(np.float16).astype(np.float32) * 16.0
-        out[key] = (np.ascontiguousarray(wq), np.ascontiguousarray(rs))
-    return out
+def kernel_comparison(orc, ref, reps=10):
+    """The gate/up projection at the verify width (16384 x 3072, 5 rows):
+    the oracle's packed block matmul (the arm's kernel) against the
+    reference's compiled matmul_dequantized on the per-row form of the same
+    INT8 values, median ms over `reps` calls each. Shows that the arm's
+    kernel runs at the reference kernel's speed."""
+    import ctypes as C
+    rng = np.random.default_rng(7)
+    M, N, K = 5, 16384, 3072
+    A = (rng.standard_normal((M, K)) * 0.5).astype(np.float32)
+    wq, dq = orc.synth_q4_0_i8(SEED, tensor_id(0, 0, 4), N, K)
+    wp, sp = np.empty_like(wq), np.empty(dq.shape, np.float32)
+    P = lambda x: x.ctypes.data_as(C.c_void_p)
+    orc.so.orc_pack_rows8(P(wq), P(dq), N, K, P(wp), P(sp))
+    out = np.empty((M, N), np.float32)
+
+    def med(f):
+        f()
+        ts = []
+        for _ in range(reps):
+            t = time.perf_counter()
+            f()
+            ts.append(time.perf_counter() - t)
+        return float(statistics.median(ts)) * 1e3
+
+    res = {"shape": f"{M}x{K} @ {N}x{K}",
+           "port_ms": med(lambda: orc.so.orc_matmul_packed(P(A), P(wp), P(sp), P(out), M, N, K))}
+    if ref is not None:
+        rs = np.ascontiguousarray(dq[:, 0].view(np.float16).astype(np.float32) * 16.0)
+        res["reference_matmul_dequantized_ms"] = med(
+            lambda: ref.so.ref_matmul_dequantized(P(A), P(wq), P(rs), P(out), M, N, K))
+    return res
 
 
 def cpu_reference_decode(a, n_tokens, warmup, steps):
-    """The reference's CPU path on the host cores: the oracle's speculative
-    decode loop with every INT8 linear layer run by the reference's own
-    compiled matmul_dequantized (oracle/_ref/libref.so: dequantized_tensor.c
-    at the reference's flags, fast_llm/Makefile:5-6) on its per-row-scale
-    weight format; the other layer math is the oracle's restatement of
-    inference.c. Same weights (seeded generator restated by the oracle),
-    prompt and draft length as the GPU arm; no product library is loaded.
-    Returns a dict with the median decode-loop rate over `steps` decodes of
-    n_tokens (each after its own prefill, excluded from the rate)."""
+    """The reference's CPU path on the host cores, restated by the oracle:
+    the speculative decode loop (draft chain, one verify pass of k + 1 rows,
+    greedy acceptance) over the layer math of inference.c and the INT8
+    matmul of dequantized_tensor.c (u8 activations, maddubs dots) in its
+    per-32-block-scale form, which is what the workload's weights need. The
+    reference's compiled matmul_dequantized has a per-row scale only; on
+    these weights it computes a different model, one whose stream accepts
+    every draft, so it would be timed on other work per token. The oracle's
+    kernel runs on weights repacked for 8-lane integer dots and matches the
+    reference kernel's speed (kernel_comparison, in the same run). Same
+    weights (the oracle's restatement of the seeded generator: no product
+    library is loaded), prompt and draft length as the GPU arm, all host
+    threads, and the same tokens. Returns the median decode-loop rate over
+    `steps` decodes of n_tokens (each after its own prefill, excluded)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     threads = os.cpu_count() or 1
     os.environ.setdefault("OMP_NUM_THREADS", str(threads))
-    import ctypes as C
     import bind
     t0 = time.time()
     orc = bind.Oracle()
@@ -206,29 +229,40 @@ def cpu_reference_decode(a, n_tokens, warmup, steps):
     except RuntimeError:
         ref = None
     w, embed = oracle_weights(orc)
-    if ref is not None:
-        orc.so.orc_set_ref_matmul(C.cast(ref.so.ref_matmul_dequantized, C.c_void_p))
-        om = bind.OracleModel(orc, DIMS, embed, w, draft_layers=DRAFT_LAYERS, ref_rows=reference_rows(w))
-    else:
-        om = bind.OracleModel(orc, DIMS, embed, w, draft_layers=DRAFT_LAYERS)
+    om = bind.OracleModel(orc, DIMS, embed, w, draft_layers=DRAFT_LAYERS, packed=True)
+    del w
     prompt = np.random.default_rng(PROMPT_SEED).integers(0, DIMS["vocab"], a.prompt_len).astype(np.int32)
     setup_s = time.time() - t0
+    kernels = kernel_comparison(orc, ref)
     for _ in range(warmup):  # warms caches and threads: short decodes
         om.spec(prompt, 8, a.k)
     vals, hist = [], []
     for _ in range(steps):
-        _, acc, _ = om.spec(prompt, n_tokens, a.k)
+        toks, acc, margins = om.spec(prompt, n_tokens, a.k)
         dec = orc.so.orc_last_decode_seconds()
         vals.append(((n_tokens - 1) / dec, dec))
         hist.append(acc)
-    orc.so.orc_set_ref_matmul(None)
     acc_cat = np.concatenate(hist)
     return {"value": float(statistics.median(x[0] for x in vals)),
             "ms": float(statistics.median(x[1] for x in vals)) * 1000.0,
-            "kind": "reference" if ref is not None else "port", "cores": threads, "setup_s": setup_s,
-            "matmul": "reference matmul_dequantized (libref.so, reference flags), per-row-scale format"
-            if ref is not None else "oracle block matmul (libref.so absent)",
+            "kind": "port", "cores": threads, "setup_s": setup_s,
+            "matmul": "oracle block matmul on 8-row packed weights (reference's u8 x s8 maddubs rule, "
+                      "per-32-block scales)",
+            "kernel_comparison": kernels, "tokens": toks, "margins": margins,
             "accepted_hist": np.bincount(acc_cat, minlength=a.k + 1).tolist()}
+
+
+def stream_check(cpu_toks, margins, gpu_toks):
+    """Greedy streams of the CPU arm and the GPU decode from the same prompt:
+    the identical prefix and, where they part, the CPU's relative top-2
+    margin there (a near-tie below 1e-2 is the allowed divergence)."""
+    n = min(len(cpu_toks), len(gpu_toks))
+    same = int(np.argmin(np.asarray(cpu_toks[:n]) == np.asarray(gpu_toks[:n]))) \
+        if not np.array_equal(cpu_toks[:n], gpu_toks[:n]) else n
+    out = {"tokens": n, "identical_prefix": same}
+    if same < n:
+        out["margin_at_divergence"] = float(margins[same])
+    return out
 
 
 def run_reference(a, rank, world):
@@ -245,7 +279,8 @@ def run_reference(a, rank, world):
                          "sample": f"each step: one {a.new_tokens}-token speculative decode after the "
                                    f"{a.prompt_len}-token prefill (prefill excluded from the rate; warm-up steps "
                                    f"decode 8 tokens)",
-                         "matmul": r["matmul"], "accepted_hist": r["accepted_hist"]},
+                         "matmul": r["matmul"], "kernel_comparison": r["kernel_comparison"],
+                         "accepted_hist": r["accepted_hist"]},
         "e2e": {"value": r["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "setup_s": r["setup_s"],
     }
@@ -714,7 +749,8 @@ def main():
         r = cpu_reference_decode(a, a.cpu_tokens, 0, 1)
         cpu = {"value": r["value"], "unit": "tok/s", "cores": r["cores"], "kind": r["kind"],
                "sample": f"one {a.cpu_tokens}-token speculative decode after the same {a.prompt_len}-token prefill "
-                         f"(prefill excluded)", "matmul": r["matmul"]}
+                         f"(prefill excluded)", "matmul": r["matmul"],
+               "stream_check": stream_check(r["tokens"], r["margins"], toks)}
 
     if rank == 0:
         line = {

@@ -93,8 +93,35 @@ __device__ __forceinline__ void mma_u8s8(uint32_t a0, uint32_t a2, uint32_t b0, 
         : "r"(a0), "r"(0), "r"(a2), "r"(0), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 
+// Epilogue of one weight-row pair, chosen at compile time (EPI >= 0) or at
+// run time (EPI < 0: one kernel body serves every layer projection, so the
+// launches of a layer share their instructions in the SM's caches).
+template <int EPI>
+__device__ __forceinline__ void pair_epi_any(int epi, const GemvParams& p, int r, int n0, bool has1, float y0,
+                                             float y1, unsigned long long* best_s) {
+    if constexpr (EPI >= 0) {
+        pair_epilogue<EPI>(p, r, n0, has1, y0, y1, best_s);
+    } else {
+        switch (epi) {
+            case EPI_STORE: pair_epilogue<EPI_STORE>(p, r, n0, has1, y0, y1, best_s); break;
+            case EPI_RESID: pair_epilogue<EPI_RESID>(p, r, n0, has1, y0, y1, best_s); break;
+            case EPI_QKV: pair_epilogue<EPI_QKV>(p, r, n0, has1, y0, y1, best_s); break;
+            case EPI_SWIGLU: pair_epilogue<EPI_SWIGLU>(p, r, n0, has1, y0, y1, best_s); break;
+            case EPI_LOGITS: pair_epilogue<EPI_LOGITS>(p, r, n0, has1, y0, y1, best_s); break;
+            case EPI_TP_PUSH: pair_epilogue<EPI_TP_PUSH>(p, r, n0, has1, y0, y1, best_s); break;
+            default: break;
+        }
+    }
+}
+
+#ifndef FL_GEMV_RT_EPI
+#define FL_GEMV_RT_EPI 0
+#endif
+
 template <int MMAX, int EPI, bool MMA>
-__global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const GemvParams p, const Geo geo) {
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const GemvParams p, const Geo geo,
+                                                                         const int epi_rt) {
+    const int epi = EPI >= 0 ? EPI : epi_rt;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full_bar[kMaxStages];
     __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
@@ -216,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const Ge
                 const float t1 = __fdiv_rn(warp_sum(f1), 127.0f);
                 f0 = f1 = 0.0f;
                 if (lane == 0 && lr < rows && rows_m > 0)
-                    pair_epilogue<EPI>(p, p.row0, r + lr, lr + 1 < rows, t0, t1, best_s);
+                    pair_epi_any<EPI>(epi, p, p.row0, r + lr, lr + 1 < rows, t0, t1, best_s);
             }
         }
     } else {
@@ -280,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const Ge
                             y0 += red[buf][w][src_lane][q0];
                             y1 += red[buf][w][src_lane][q0 + 1];
                         }
-                        pair_epilogue<EPI>(p, p.row0 + m, r + 2 * pr, 2 * pr + 1 < rows, __fdiv_rn(y0, 127.0f),
+                        pair_epi_any<EPI>(epi, p, p.row0 + m, r + 2 * pr, 2 * pr + 1 < rows, __fdiv_rn(y0, 127.0f),
                                            __fdiv_rn(y1, 127.0f), best_s);
                     }
                 }
@@ -289,12 +316,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const Ge
         }
     }
 
-    if (EPI == EPI_LOGITS) {
+    if (epi == EPI_LOGITS) {
         asm volatile("bar.sync 1, %0;" ::"n"(kCWarps * 32) : "memory");
         if (threadIdx.x < (unsigned)rows_m)
             p.amax_part[(size_t)(p.row0 + threadIdx.x) * gridDim.x + blockIdx.x] = best_s[threadIdx.x];
     }
-    if (EPI == EPI_TP_PUSH) {
+    if (epi == EPI_TP_PUSH) {
         // this CTA's rows are on every rank: publish (system-scope fence, then count)
         __threadfence_system();
         asm volatile("bar.sync 1, %0;" ::"n"(kCWarps * 32) : "memory");
@@ -371,7 +398,7 @@ int sm_count() {
 }
 
 template <int MMAX, int EPI, bool MMA>
-cudaError_t launch_t(const GemvParams& p, const Geo& geo, cudaStream_t s, bool pdl) {
+cudaError_t launch_t(const GemvParams& p, const Geo& geo, cudaStream_t s, bool pdl, int epi) {
     auto kern = gemv_tma_kernel<MMAX, EPI, MMA>;
     const size_t smem = (size_t)geo.act_bytes + (size_t)geo.S * slot_bytes(geo.P);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -386,15 +413,15 @@ cudaError_t launch_t(const GemvParams& p, const Geo& geo, cudaStream_t s, bool p
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, kern, p, geo);
+    return cudaLaunchKernelEx(&cfg, kern, p, geo, epi);
 }
 
 template <int EPI>
-cudaError_t launch_e(const GemvParams& p, const Geo& geo, cudaStream_t s, bool pdl) {
-    if (p.M <= 1) return launch_t<1, EPI, false>(p, geo, s, pdl);
-    if (p.M <= 2) return launch_t<2, EPI, true>(p, geo, s, pdl);
-    if (p.M <= 4) return launch_t<4, EPI, true>(p, geo, s, pdl);
-    return launch_t<8, EPI, true>(p, geo, s, pdl);
+cudaError_t launch_e(const GemvParams& p, const Geo& geo, cudaStream_t s, bool pdl, int epi) {
+    if (p.M <= 1) return launch_t<1, EPI, false>(p, geo, s, pdl, epi);
+    if (p.M <= 2) return launch_t<2, EPI, true>(p, geo, s, pdl, epi);
+    if (p.M <= 4) return launch_t<4, EPI, true>(p, geo, s, pdl, epi);
+    return launch_t<8, EPI, true>(p, geo, s, pdl, epi);
 }
 
 }  // namespace
@@ -424,15 +451,20 @@ cudaError_t launch_gemv_tma(const GemvParams& p, int epi, cudaStream_t s, bool p
     Geo geo;
     if (!make_geo(p.K, p.M, geo, p.P)) return cudaErrorInvalidValue;
     if (p.x && p.K % 128 != 0) return cudaErrorInvalidValue;
+    if (epi < EPI_STORE || epi > EPI_TP_PUSH || epi == EPI_DOTS) return cudaErrorInvalidValue;
+#if FL_GEMV_RT_EPI
+    return launch_e<-1>(p, geo, s, pdl, epi);
+#else
     switch (epi) {
-        case EPI_STORE: return launch_e<EPI_STORE>(p, geo, s, pdl);
-        case EPI_RESID: return launch_e<EPI_RESID>(p, geo, s, pdl);
-        case EPI_QKV: return launch_e<EPI_QKV>(p, geo, s, pdl);
-        case EPI_SWIGLU: return launch_e<EPI_SWIGLU>(p, geo, s, pdl);
-        case EPI_LOGITS: return launch_e<EPI_LOGITS>(p, geo, s, pdl);
-        case EPI_TP_PUSH: return launch_e<EPI_TP_PUSH>(p, geo, s, pdl);
+        case EPI_STORE: return launch_e<EPI_STORE>(p, geo, s, pdl, epi);
+        case EPI_RESID: return launch_e<EPI_RESID>(p, geo, s, pdl, epi);
+        case EPI_QKV: return launch_e<EPI_QKV>(p, geo, s, pdl, epi);
+        case EPI_SWIGLU: return launch_e<EPI_SWIGLU>(p, geo, s, pdl, epi);
+        case EPI_LOGITS: return launch_e<EPI_LOGITS>(p, geo, s, pdl, epi);
+        case EPI_TP_PUSH: return launch_e<EPI_TP_PUSH>(p, geo, s, pdl, epi);
         default: return cudaErrorInvalidValue;
     }
+#endif
 }
 
 cudaError_t launch_tp_reduce(const TpReduceParams& p, cudaStream_t s, bool pdl) {

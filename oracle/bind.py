@@ -32,7 +32,7 @@ class Dims(C.Structure):
 
 
 class Lin(C.Structure):
-    _fields_ = [("w", VP), ("s", VP), ("N", I), ("K", I), ("f32", VP), ("rs", VP)]
+    _fields_ = [("w", VP), ("s", VP), ("N", I), ("K", I), ("f32", VP), ("wp", VP), ("sp", VP)]
 
 
 class Layer(C.Structure):
@@ -112,7 +112,8 @@ class Oracle:
         s.orc_synth_q4_0_i8.argtypes = [C.c_uint64, C.c_uint32, I, I, C.c_float, VP, VP]
         s.orc_synth_q4_0_f32.restype = I
         s.orc_synth_q4_0_f32.argtypes = [C.c_uint64, C.c_uint32, I, I, C.c_float, VP]
-        s.orc_set_ref_matmul.argtypes = [VP]
+        s.orc_pack_rows8.argtypes = [VP, VP, I, I, VP, VP]
+        s.orc_matmul_packed.argtypes = [VP, VP, VP, VP, I, I, I]
         s.orc_last_decode_seconds.restype = C.c_double
 
     # ----------------------------------------------------------- primitives
@@ -138,6 +139,24 @@ class Oracle:
         N = W.shape[0]
         Cm = np.empty((M, N), np.float32)
         self.so.orc_matmul_block(_p(A), _p(W), _p(d), _p(Cm), M, N, K)
+        return Cm
+
+    def pack_rows8(self, W, d):
+        """orc_pack_rows8: (wp, sp), or None when W is not packable."""
+        W = np.ascontiguousarray(W, np.int8)
+        d = np.ascontiguousarray(d, np.uint16)
+        wp = np.empty_like(W)
+        sp = np.empty(d.shape, np.float32)
+        if self.so.orc_pack_rows8(_p(W), _p(d), W.shape[0], W.shape[1], _p(wp), _p(sp)) != 0:
+            return None
+        return wp, sp
+
+    def matmul_packed(self, A, wp, sp):
+        A = np.ascontiguousarray(A, np.float32)
+        M, K = A.shape
+        N = wp.shape[0]
+        Cm = np.empty((M, N), np.float32)
+        self.so.orc_matmul_packed(_p(A), _p(wp), _p(sp), _p(Cm), M, N, K)
         return Cm
 
     def block_dots(self, A, W):
@@ -239,7 +258,7 @@ class OracleModel:
     """Oracle model over numpy weights. `w` maps (stack, layer, proj) to
     (int8 [N,K], fp16 bits [N,K/32]); stack 3 proj 1 = LM head."""
 
-    def __init__(self, orc: Oracle, dims: dict, embed, w, draft_layers=0, n_medusa=0, f32=None, ref_rows=None):
+    def __init__(self, orc: Oracle, dims: dict, embed, w, draft_layers=0, n_medusa=0, f32=None, packed=False):
         self.orc = orc
         self.keep = [embed]
         self.m = Model()
@@ -256,14 +275,17 @@ class OracleModel:
                 L.f32 = _p(a)
                 L.N, L.K = a.shape
                 return L
-            if ref_rows is not None and key in ref_rows:
-                # the reference's per-row-scale tensor, run by the installed
-                # reference matmul (orc_set_ref_matmul)
-                wr, rs = ref_rows[key]
-                self.keep += [wr, rs]
-                L.w, L.rs = _p(wr), _p(rs)
-                L.N, L.K = wr.shape
-                return L
+            wq, dq = w[key]
+            if packed and wq.shape[0] % 8 == 0:
+                # weights repacked for 8-lane integer dots (orc_pack_rows8);
+                # same results, the reference kernel's speed
+                wp = np.empty_like(wq)
+                sp = np.empty(dq.shape, np.float32)
+                if orc.so.orc_pack_rows8(_p(wq), _p(dq), wq.shape[0], wq.shape[1], _p(wp), _p(sp)) == 0:
+                    self.keep += [wp, sp]
+                    L.wp, L.sp = _p(wp), _p(sp)
+                    L.N, L.K = wq.shape
+                    return L
             wq, dq = w[key]
             self.keep += [wq, dq]
             L.w, L.s = _p(wq), _p(dq)

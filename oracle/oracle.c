@@ -151,60 +151,142 @@ void orc_matmul_rowscale(const float* A, const int8_t* W, const float* scales,
     free(q);
 }
 
-/* Eight consecutive 32-element block dots in one vector (lane j = block j),
- * each the maddubs + madd sum of block_dot32. */
-static inline __m256i block_dots8(const uint8_t* a, const int8_t* w) {
+/* The block dots of eight weight rows (stride K) against one activation
+ * block, lane r = row r: the maddubs + madd sums of block_dot32. */
+static inline __m256i rows_dots8(const __m256i va, const __m256i* w) {
     const __m256i one = _mm256_set1_epi16(1);
     __m256i p[8];
-    for (int j = 0; j < 8; j++) {
-        const __m256i va = _mm256_loadu_si256((const __m256i*)(a + 32 * j));
-        const __m256i vw = _mm256_loadu_si256((const __m256i*)(w + 32 * j));
-        p[j] = _mm256_madd_epi16(_mm256_maddubs_epi16(va, vw), one);
-    }
+    for (int r = 0; r < 8; r++) p[r] = _mm256_madd_epi16(_mm256_maddubs_epi16(va, w[r]), one);
     const __m256i s01 = _mm256_hadd_epi32(p[0], p[1]), s23 = _mm256_hadd_epi32(p[2], p[3]);
     const __m256i s45 = _mm256_hadd_epi32(p[4], p[5]), s67 = _mm256_hadd_epi32(p[6], p[7]);
     const __m256i s0123 = _mm256_hadd_epi32(s01, s23), s4567 = _mm256_hadd_epi32(s45, s67);
-    /* s0123 = [b0 b1 b2 b3 (low halves) | b0 b1 b2 b3 (high halves)], same for 4..7 */
     return _mm256_add_epi32(_mm256_permute2x128_si256(s0123, s4567, 0x20),
                             _mm256_permute2x128_si256(s0123, s4567, 0x31));
 }
 
 /* Per block: t = (float)dot * scale (one rounding), acc = acc + t in block
- * order (matmul_dequantized's per-row accumulation, one scale per block).
- * Eight blocks' dots and products are formed in vectors; the adds stay
- * sequential, so the result is that of the one-block-at-a-time loop. */
+ * order (matmul_dequantized's per-row accumulation, one scale per block),
+ * C = acc / 127. Eight weight rows go through in the lanes of one vector and
+ * up to four activation rows share each weight load; every lane still adds
+ * its row's blocks one at a time in block order, so the result is that of
+ * the one-block-at-a-time loop. Rows past the last multiple of 8 take that
+ * loop directly. */
 static void matmul_block_q(const uint8_t* q, const int8_t* W, const uint16_t* S,
                            float* C, int M, int N, int K) {
     const int nb = K / 32;
+    const int N8 = N & ~7;
 #pragma omp parallel
     {
-        float* sf = (float*)malloc(sizeof(float) * (size_t)nb);
+        float* sf = (float*)malloc(sizeof(float) * (size_t)nb * 8);
 #pragma omp for schedule(static)
-        for (int n = 0; n < N; n++) {
+        for (int n = 0; n < N8; n += 8) {
+            for (int b = 0; b < nb; b++)
+                for (int r = 0; r < 8; r++) sf[b * 8 + r] = orc_f16_to_f32(S[(size_t)(n + r) * nb + b]);
             const int8_t* wr = W + (size_t)n * K;
-            const uint16_t* sr = S + (size_t)n * nb;
-            for (int b = 0; b < nb; b++) sf[b] = orc_f16_to_f32(sr[b]);
-            for (int m = 0; m < M; m++) {
-                const uint8_t* qa = q + (size_t)m * K;
-                float acc = 0.0f;
-                int b = 0;
-                for (; b + 8 <= nb; b += 8) {
-                    const __m256 t8 = _mm256_mul_ps(_mm256_cvtepi32_ps(block_dots8(qa + 32 * b, wr + 32 * b)),
-                                                    _mm256_loadu_ps(sf + b));
-                    float t[8];
-                    _mm256_storeu_ps(t, t8);
-                    for (int j = 0; j < 8; j++) acc = acc + t[j];
+            for (int m0 = 0; m0 < M; m0 += 4) {
+                const int mc = M - m0 < 4 ? M - m0 : 4;
+                __m256 acc[4] = {_mm256_setzero_ps(), _mm256_setzero_ps(), _mm256_setzero_ps(),
+                                 _mm256_setzero_ps()};
+                for (int b = 0; b < nb; b++) {
+                    __m256i w8[8];
+                    for (int r = 0; r < 8; r++)
+                        w8[r] = _mm256_loadu_si256((const __m256i*)(wr + (size_t)r * K + 32 * b));
+                    const __m256 sc = _mm256_loadu_ps(sf + 8 * b);
+                    for (int i = 0; i < mc; i++) {
+                        const __m256i va = _mm256_loadu_si256((const __m256i*)(q + (size_t)(m0 + i) * K + 32 * b));
+                        const __m256 t = _mm256_mul_ps(_mm256_cvtepi32_ps(rows_dots8(va, w8)), sc);
+                        acc[i] = _mm256_add_ps(acc[i], t);
+                    }
                 }
-                for (; b < nb; b++) {
-                    int32_t dot = block_dot32(qa + 32 * b, wr + 32 * b);
-                    float t = (float)dot * sf[b];
-                    acc = acc + t;
-                }
-                C[(size_t)m * N + n] = acc / 127.0f;
+                const __m256 d127 = _mm256_set1_ps(127.0f);
+                for (int i = 0; i < mc; i++)
+                    _mm256_storeu_ps(C + (size_t)(m0 + i) * N + n, _mm256_div_ps(acc[i], d127));
             }
         }
         free(sf);
     }
+    for (int n = N8; n < N; n++) {
+        const int8_t* wr = W + (size_t)n * K;
+        const uint16_t* sr = S + (size_t)n * nb;
+        for (int m = 0; m < M; m++) {
+            const uint8_t* qa = q + (size_t)m * K;
+            float acc = 0.0f;
+            for (int b = 0; b < nb; b++) {
+                const float t = (float)block_dot32(qa + 32 * b, wr + 32 * b) * orc_f16_to_f32(sr[b]);
+                acc = acc + t;
+            }
+            C[(size_t)m * N + n] = acc / 127.0f;
+        }
+    }
+}
+
+/* The same rule over weights packed for 8-lane integer dots: rows in groups
+ * of 8, and for each block of a group eight 32-byte chunks, chunk c holding
+ * 4 consecutive weights of each of the 8 rows (byte 4r + j = row r, column
+ * 32b + 4c + j). One maddubs of a chunk against 4 activation bytes repeated
+ * 8 times gives, in int16 lanes 2r and 2r+1, row r's two pair sums; the
+ * eight chunks of a block add up in int16 without overflow because every
+ * weight is in [-8, 7] (16 products of at most 255 * 8 = 2040), and one madd
+ * with ones then leaves row r's block dot in int32 lane r. Scales are packed
+ * the same way as f32 ([group][block][8]). Only the order of the integer
+ * adds differs from matmul_block_q, so every block dot, product and sum is
+ * the same. */
+int orc_pack_rows8(const int8_t* W, const uint16_t* S, int N, int K, int8_t* wp, float* sp) {
+    if (N % 8 || K % 32) return -1;
+    const int nb = K / 32;
+    for (size_t i = 0; i < (size_t)N * K; i++)
+        if (W[i] < -8 || W[i] > 7) return -1;
+#pragma omp parallel for schedule(static)
+    for (int g = 0; g < N / 8; g++)
+        for (int b = 0; b < nb; b++) {
+            int8_t* dst = wp + ((size_t)g * nb + b) * 256;
+            for (int c = 0; c < 8; c++)
+                for (int r = 0; r < 8; r++)
+                    for (int j = 0; j < 4; j++)
+                        dst[c * 32 + 4 * r + j] = W[(size_t)(8 * g + r) * K + 32 * b + 4 * c + j];
+            for (int r = 0; r < 8; r++)
+                sp[((size_t)g * nb + b) * 8 + r] = orc_f16_to_f32(S[(size_t)(8 * g + r) * nb + b]);
+        }
+    return 0;
+}
+
+static void matmul_packed_q(const uint8_t* q, const int8_t* wp, const float* sp, float* C, int M, int N, int K) {
+    const int nb = K / 32;
+    const __m256i one = _mm256_set1_epi16(1);
+    const __m256 d127 = _mm256_set1_ps(127.0f);
+#pragma omp parallel for schedule(static)
+    for (int g = 0; g < N / 8; g++) {
+        for (int m0 = 0; m0 < M; m0 += 4) {
+            const int mc = M - m0 < 4 ? M - m0 : 4;
+            __m256 acc[4] = {_mm256_setzero_ps(), _mm256_setzero_ps(), _mm256_setzero_ps(), _mm256_setzero_ps()};
+            for (int b = 0; b < nb; b++) {
+                const int8_t* wb = wp + ((size_t)g * nb + b) * 256;
+                __m256i w8[8];
+                for (int c = 0; c < 8; c++) w8[c] = _mm256_loadu_si256((const __m256i*)(wb + 32 * c));
+                const __m256 sc = _mm256_loadu_ps(sp + ((size_t)g * nb + b) * 8);
+                for (int i = 0; i < mc; i++) {
+                    const uint8_t* qa = q + (size_t)(m0 + i) * K + 32 * b;
+                    __m256i s16 = _mm256_setzero_si256();
+                    for (int c = 0; c < 8; c++) {
+                        int32_t a4;
+                        memcpy(&a4, qa + 4 * c, 4);
+                        s16 = _mm256_add_epi16(s16, _mm256_maddubs_epi16(_mm256_set1_epi32(a4), w8[c]));
+                    }
+                    const __m256 t = _mm256_mul_ps(_mm256_cvtepi32_ps(_mm256_madd_epi16(s16, one)), sc);
+                    acc[i] = _mm256_add_ps(acc[i], t);
+                }
+            }
+            for (int i = 0; i < mc; i++)
+                _mm256_storeu_ps(C + (size_t)(m0 + i) * N + 8 * g, _mm256_div_ps(acc[i], d127));
+        }
+    }
+}
+
+void orc_matmul_packed(const float* A, const int8_t* wp, const float* sp, float* C, int M, int N, int K) {
+    uint8_t* q = (uint8_t*)malloc((size_t)M * K);
+    for (int m = 0; m < M; m++) orc_quant_u8(A + (size_t)m * K, q + (size_t)m * K, K);
+    matmul_packed_q(q, wp, sp, C, M, N, K);
+    free(q);
 }
 
 void orc_matmul_block(const float* A, const int8_t* W, const uint16_t* scales,
@@ -408,12 +490,9 @@ void orc_kv_free(orc_kv_t* kv) {
     kv->k = kv->v = NULL;
 }
 
-static orc_ref_matmul_fn g_ref_mm = NULL;
-void orc_set_ref_matmul(orc_ref_matmul_fn fn) { g_ref_mm = fn; }
-
 static void lin(const orc_lin_t* L, const float* x, float* y, int M) {
-    if (L->rs && g_ref_mm) {
-        g_ref_mm(x, L->w, L->rs, y, M, L->N, L->K);
+    if (L->wp) {
+        orc_matmul_packed(x, L->wp, L->sp, y, M, L->N, L->K);
         return;
     }
     if (L->f32) { /* inference.c:131-141 */

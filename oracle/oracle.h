@@ -49,6 +49,12 @@ void orc_matmul_rowscale(const float* A, const int8_t* W, const float* scales,
 
 /* Block mode (weights [-8,7], fp16 scale per 32-block):
  * C[m,n] = (sum_b (float)dot_b * d_b, summed in block order) / 127.0f. */
+/* Packs [N, K] block-mode weights (all in [-8, 7], N % 8 == 0) and their
+ * fp16 scales for orc_matmul_packed: wp N*K bytes, sp N*K/32 floats.
+ * Returns -1 (nothing written past the check) when a condition fails. */
+int orc_pack_rows8(const int8_t* W, const uint16_t* S, int N, int K, int8_t* wp, float* sp);
+/* orc_matmul_block on packed weights; identical results. */
+void orc_matmul_packed(const float* A, const int8_t* wp, const float* sp, float* C, int M, int N, int K);
 void orc_matmul_block(const float* A, const int8_t* W, const uint16_t* scales,
                       float* C, int M, int N, int K);
 
@@ -93,11 +99,6 @@ void orc_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t ou
 int orc_synth_q4_0_i8(uint64_t seed, uint32_t tensor_id, int rows, int cols, float std, int8_t* w, uint16_t* d);
 int orc_synth_q4_0_f32(uint64_t seed, uint32_t tensor_id, int rows, int cols, float std, float* out);
 
-/* Installs (or, with NULL, removes) the reference matmul used by layers
- * whose orc_lin_t.rs is set: fn(A, W, row_scales, C, M, N, K). */
-typedef void (*orc_ref_matmul_fn)(const float*, const int8_t*, const float*, float*, int, int, int);
-void orc_set_ref_matmul(orc_ref_matmul_fn fn);
-
 /* ---------------- model ---------------- */
 
 typedef struct {
@@ -113,12 +114,11 @@ typedef struct {
      * reference's f32 matvec (inference.c:131-141) instead of INT8; used to
      * pin the layer composition against the reference's model_forward. */
     const float* f32;
-    /* When non-NULL and a reference matmul is installed (orc_set_ref_matmul),
-     * the layer runs that function on `w` as the reference's per-row-scale
-     * tensor (dequantized_tensor.c:27-58 format: (q-8)*16, one scale per row
-     * rs[N]) -- the reference's own compiled CPU kernel, for timing it on the
-     * path; its arithmetic is the reference's, not the block-scaled rule. */
-    const float* rs;
+    /* When non-NULL: `w` and `s` packed by orc_pack_rows8 (wp, sp); the
+     * layer then runs orc_matmul_packed, with results identical to the
+     * block matmul on w and s. */
+    const int8_t* wp;
+    const float* sp;
 } orc_lin_t;
 
 typedef struct {
