@@ -88,6 +88,22 @@ def step_bytes(k, ctx):
     return draft + verify
 
 
+def profiled_traffic(summary, m):
+    """dram__bytes_read.sum + dram__bytes_write.sum per launch of a kernel at
+    M = m, from the ncu summary committed under profiles/ (its line
+    `traffic_bytes_per_launch M=<m>: <bytes>`); None when absent."""
+    import re
+    try:
+        with open(os.path.join(ROOT, "profiles", summary)) as f:
+            for line in f:
+                r = re.match(r"\s*traffic_bytes_per_launch M=(\d+): (\d+)", line)
+                if r and int(r.group(1)) == m:
+                    return int(r.group(2))
+    except OSError:
+        pass
+    return None
+
+
 def measured_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -331,7 +347,8 @@ def run_microbench(a):
     us = e0.elapsed_time(e1) * 1000.0 / (a.iters * nt)
     byts = N * K * 17 / 16 + a.m * K * 4 + a.m * N * 4
     print(json.dumps({"microbench": a.microbench, "N": N, "K": K, "M": a.m, "launches": a.iters * nt,
-                      "us_per_launch": us, "GBps": byts / us / 1e3}), flush=True)
+                      "us_per_launch": us, "GBps": byts / us / 1e3, "TOPS": 2.0 * a.m * N * K / us / 1e6}),
+          flush=True)
     return 0
 
 
@@ -443,6 +460,33 @@ def run_tp_medium(a):
     return 0
 
 
+def run_profile_step(a):
+    """A small case of the config-0 decode for ncu captures: the full widths
+    (d 3072, 32 heads of 96, ffn 8192, vocab 32064) with 4 base and 2 draft
+    layers, a 64-token prompt and 12 new tokens (the same kernels, tiles and
+    launch shapes as the full model, about 1 GB on the device), then one
+    pass of each decode attention over the 4 layers at a 192-position
+    context. --step-kernel selects the one-kernel step."""
+    if a.step_kernel:
+        os.environ["FL_STEP_KERNEL"] = "1"
+    import flb200
+    lib = flb200.Lib()
+    lib.check(lib.fl_cuda_init(0), "init")
+    cfg = engine_cfg(256)
+    cfg["num_layers"], cfg["draft_layers"] = 4, 2
+    eng = flb200.Engine(lib, cfg, 0)
+    eng.synthesize(SEED)
+    prompt = np.random.default_rng(PROMPT_SEED).integers(0, DIMS["vocab"], 64).astype(np.int32)
+    eng.spec_prefill(prompt, a.k)
+    toks, acc = eng.spec_decode(12)
+    att = eng.bench_attention(0, a.k + 1, 192, reps=1)
+    att1 = eng.bench_attention(1, 1, 192, reps=1)
+    print(json.dumps({"profile_case": "phi3-mini widths, 4 + 2 layers", "step_kernel": bool(eng.step_kernel()),
+                      "spec_steps": len(acc), "attention_us": [att, att1]}), flush=True)
+    eng.close()
+    return 0
+
+
 def run_medusa(a):
     """Medusa heads on the Phi-3-mini base, bs1, one timed generate per step."""
     import torch
@@ -545,7 +589,8 @@ def sharded_decode(a, dist, rank, nranks, local):
         full = toks
     if eng:
         eng.close()
-    return secs, dec, nsteps, int(np.asarray(full, np.int64).sum()), launches
+    # gather_tokens gives the full set on rank 0 only
+    return secs, dec, nsteps, int(np.asarray(full, np.int64).sum()) if full is not None else 0, launches
 
 
 def run_sampled_batch(a):
@@ -624,7 +669,8 @@ def main():
                     help="one persistent tcgen05 kernel per speculative step (128-byte panels)")
     ap.add_argument("--m", type=int, default=5, help="activation rows for --microbench")
     ap.add_argument("--iters", type=int, default=10, help="sweeps for --microbench")
-    ap.add_argument("--workload", default="spec-bs1", choices=["spec-bs1", "sampled-batch", "tp-medium", "medusa"])
+    ap.add_argument("--workload", default="spec-bs1",
+                    choices=["spec-bs1", "sampled-batch", "tp-medium", "medusa", "profile-step"])
     ap.add_argument("--seqs", type=int, default=64, help="sequences of --workload sampled-batch")
     ap.add_argument("--batch", type=int, default=1, help="sequences decoded together by --workload tp-medium")
     ap.add_argument("--tree", type=int, default=0, help="draft-tree width for --workload tp-medium (0: chain)")
@@ -637,6 +683,8 @@ def main():
         return run_tp_medium(a)
     if a.workload == "medusa":
         return run_medusa(a)
+    if a.workload == "profile-step":
+        return run_profile_step(a)
     a.warmup = max(a.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -768,9 +816,9 @@ def main():
             "verify_step_us_est": 32 * (us_gu + us_dn + us_qkv + us_o),
             "roofline": {"bound": "hbm", "achieved": kern_gbs, "peak": peak, "unit": "GB/s",
                          "frac": kern_gbs / peak,
-                         # dram__bytes_read.sum + dram__bytes_write.sum of this kernel and shape (M = 5)
-                         # from one ncu --set full capture of bench.py --microbench gateup --m 5
-                         "traffic": 53616128 + 11264 if not eng.step_kernel() else None, "peak_kind": peak_kind,
+                         "traffic": None if eng.step_kernel() else profiled_traffic(
+                             "gemv_tma_gateup_16384x3072.md", a.k + 1),
+                         "peak_kind": peak_kind,
                          "kernel": "gemv_tma_kernel (verify gate/up, 16384x3072, M=%d)" % (a.k + 1),
                          "per_launch_us": us_gu, "bytes_per_launch": by_gu,
                          "others": {"qkv_M5": [us_qkv, by_qkv / (us_qkv * 1e-6) / 1e9],

@@ -12,24 +12,21 @@
 // and its stage counters run on across tiles, so the next tile's copies and
 // MMAs overlap this tile's readout and epilogue (per-tile CTAs spent about
 // 6 us per tile on start-up and drain).
-//  - warps 0-3: producers. Per 128-byte K-group thread 0 copies the weight
+//  - warp 0: producer. One thread copies, per 128-byte K-group, the weight
 //    tile (128 rows x 128 B; the tiled weight layout already stores each
 //    128-byte group XOR-swizzled by row & 7, which is the 128-byte swizzle
 //    pattern the MMA descriptor expects, so the bytes move verbatim) and the
-//    activation tile (BN rows x 128 B, SWIZZLE_128B) by TMA. Rows from
-//    FL_GEMM_TMA_ROWS on (128 by default: none) are copied instead with
-//    coalesced 16-byte cp.async by all producer threads, eight lanes per row;
-//    the full-tile TMA measured 2-3 % faster. A stage is published
-//    (async-proxy fence, then mbarrier arrival) once its copies complete, six
-//    stages behind the newest.
-//  - warp 4: allocates all 512 TMEM columns, then issues one
+//    activation tile (BN rows x 128 B, SWIZZLE_128B) by TMA into a ring of
+//    stages; a stage's barrier completes on the copies' byte count, and its
+//    slot is reused once the MMAs that read it have committed.
+//  - warp 1: allocates all 512 TMEM columns, then issues one
 //    tcgen05.mma.cta_group::1.kind::i8 (M = 128, N = BN, K = 32) per 32-element
 //    block into its own BN TMEM columns, and one tcgen05.commit per stage
 //    (four blocks): the commit both frees the stage's shared-memory slot and
 //    hands its TMEM buffer (4 BN columns, one of 512 / (4 BN)) to the
 //    readout. Commits are slow enough (about half a microsecond apiece here)
 //    that one per block was the kernel's bottleneck.
-//  - warps 5 ..: readout, BN / 16 per TMEM lane quadrant, each with 16
+//  - warps 2 ..: readout, BN / 16 per TMEM lane quadrant, each with 16
 //    columns of its quadrant's 32 lanes (one 32x32b.x16 load per block: 3-8 %
 //    faster than 8-column warps, while 32-column warps are slower). Per half
 //    stage (two blocks) it loads the s32 dots, releases a stage's TMEM buffer
@@ -59,19 +56,14 @@ namespace {
 
 __device__ int g_gemm_error = 0;
 
-constexpr int kProdW = 4, kMma = 4, kRd0 = 5;
+constexpr int kMma = 1, kRd0 = 2;  // warp 0 producer, warp 1 MMA, readout from warp 2
 // readout warps per TMEM lane quadrant (8 columns each at least), threads
 #ifndef FL_GEMM_COLS
 #define FL_GEMM_COLS 16
 #endif
 __host__ __device__ constexpr int rd_per_quad(int bn) { return bn / FL_GEMM_COLS > 1 ? bn / FL_GEMM_COLS : 1; }
 __host__ __device__ constexpr int gemm_threads(int bn) { return (kRd0 + 4 * rd_per_quad(bn)) * 32; }
-constexpr int kProdT = kProdW * 32;
-constexpr int kInFlight = 6;  // weight stages in flight per producer thread
-#ifndef FL_GEMM_TMA_ROWS
-#define FL_GEMM_TMA_ROWS 128
-#endif
-constexpr int kTmaRows = FL_GEMM_TMA_ROWS;  // weight-tile rows fetched by TMA (the rest by cp.async)
+constexpr int kMinStages = 4;
 constexpr int kTileN = 128;                 // weight rows per tile (UMMA M)
 constexpr int kGroup = 128;                 // K bytes per stage (four 32-element blocks)
 constexpr int kABytes = kTileN * kGroup;    // 16 KB
@@ -129,17 +121,6 @@ __device__ __forceinline__ bool warp_wait(uint64_t* b, uint32_t par) {
     return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-// 16-byte global -> shared copy through L2; src_bytes 0 fills zeros.
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t src_bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(saddr(dst)), "l"(src), "r"(src_bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* b) {
     asm volatile(
@@ -263,7 +244,7 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; i++) {
-            mb_init(&full[i], kProdT + 1);  // producer threads + the activation TMA
+            mb_init(&full[i], 1);  // the producer's expect_tx arrival; completes on the copied bytes
             mb_init(&done[i], 1);
         }
         for (int i = 0; i < NB; i++) mb_init(&tempty[i], kNRd);
@@ -282,53 +263,32 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
     tc_fence_after();
     const uint32_t tmem = tmem_base_s;
 
-    if (warp < kProdW) {
-        const int pt = threadIdx.x, prow = pt >> 3, pch = pt & 7;
-        if (pt == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_a)) : "memory");
-        int gk = 0, pub = 0;  // stages issued / published (over this CTA's tiles)
-        bool stop = false;
-        for (int tl = blockIdx.x; tl < geo.tiles && !stop; tl += gridDim.x) {
-          const int n0 = tile_n0(tl), m0 = tile_m0(tl);
-          for (int kg = 0; kg < nkg; kg++, gk++) {
-            const int s = gk % S;
-            if (gk >= S && !warp_wait(&done[s], ((gk / S) - 1) & 1)) {
-                if (lane == 0) atomicOr(&bad_s, 1);
-                stop = true;
-                break;
+    if (warp == 0) {
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_w)) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_a)) : "memory");
+            int gk = 0;  // stages issued over this CTA's tiles
+            bool stop = false;
+            for (int tl = blockIdx.x; tl < geo.tiles && !stop; tl += gridDim.x) {
+                const int n0 = tile_n0(tl), m0 = tile_m0(tl);
+                for (int kg = 0; kg < nkg; kg++, gk++) {
+                    const int s = gk % S;
+                    // the slot's previous stage must have been consumed by its MMAs
+                    if ((gk >= S && !mb_wait(&done[s], ((gk / S) - 1) & 1)) || *(volatile int*)&bad_s) {
+                        atomicOr(&bad_s, 1);
+                        stop = true;
+                        break;
+                    }
+                    uint8_t* st = smem + (size_t)s * kStage;
+                    const int kb = kg * kGroup;
+                    const int pan = kb / geo.P;
+                    mb_expect(&full[s], kBBytes + kABytes);
+                    tma_2d(st, &tm_w, kb - pan * geo.P, pan * N + n0, &full[s]);
+                    tma_2d(st + kABytes, &tm_a, kb, m0, &full[s]);
+                }
             }
-            if (*(volatile int*)&bad_s) {
-                stop = true;
-                break;
-            }
-            uint8_t* st = smem + (size_t)s * kStage;
-            const int kb = kg * kGroup;
-            const int pan = kb / geo.P;
-            if (pt == 0) {
-                // weight rows [0, kTmaRows) and the activation tile by TMA
-                mb_expect(&full[s], kBBytes + kTmaRows * kGroup);
-                tma_2d(st, &tm_w, kb - pan * geo.P, pan * N + n0, &full[s]);
-                tma_2d(st + kABytes, &tm_a, kb, m0, &full[s]);
-            }
-            const int8_t* src = g.w + (size_t)pan * N * geo.P + (kb - pan * geo.P) + pch * 16;
-#pragma unroll
-            for (int i = kTmaRows / 16; i < kTileN / 16; i++) {
-                const int row = prow + 16 * i, n = n0 + row;
-                const bool in = n < N;
-                cp_async16(st + row * kGroup + pch * 16, src + (size_t)(in ? n : 0) * geo.P, in ? 16u : 0u);
-            }
-            cp_async_commit();
-            if (gk - pub >= kInFlight - 1) {
-                cp_async_wait<kInFlight - 1>();
-                fence_async_smem();
-                mb_arrive(&full[pub % S]);
-                pub++;
-            }
-          }
+            issued_s = gk;
         }
-        cp_async_wait<0>();
-        fence_async_smem();
-        for (; pub < gk; pub++) mb_arrive(&full[pub % S]);
-        if (pt == 0) issued_s = gk;
     } else if (warp == kMma) {
         if (lane == 0) {
             const int my_tiles = blockIdx.x < geo.tiles ? (geo.tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
@@ -358,7 +318,7 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
         }
     } else {
         // readout warps: TMEM lanes of quadrant (warp % 4), 1 / kWQ of the columns
-        const int q = warp & 3, part = (warp - kRd0) >> 2;  // warps 5-12: quadrants 1, 2, 3, 0, 1, 2, 3, 0
+        const int q = warp & 3, part = (warp - kRd0) >> 2;  // warps 2-9: quadrants 2, 3, 0, 1, 2, 3, 0, 1
         constexpr int kCols = BN / kWQ;
         static_assert(kCols % 8 == 0, "TMEM loads move 8 columns");
         const int c0 = part * kCols;
@@ -450,10 +410,12 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
     }
     __syncthreads();
     if (bad_s) {
-        // drain: copies issued but not consumed, and the MMAs of the last commit
-        // (producer threads drained their own copies with cp.async.wait_group 0)
+        // drain: the MMAs of the last commit, then every stage copied but not
+        // consumed (its TMA writes land in this CTA's shared memory)
         if (warp == kMma && lane == 0 && last_commit_s >= 0)
             (void)mb_wait(&done[last_commit_s % S], (last_commit_s / S) & 1);
+        if (threadIdx.x == 0)
+            for (int g2 = consumed_s; g2 < issued_s; g2++) (void)mb_wait(&full[g2 % S], (g2 / S) & 1);
         __syncthreads();
     }
     if (warp == kMma) {
@@ -515,7 +477,7 @@ cudaError_t launch_bn(const CUtensorMap& tw, const CUtensorMap& ta, const GemvPa
     geo.M = M;
     geo.P = g.P;
     geo.stages = std::min(kMaxStagesG, (kSmemBudget - 1024) / stage);
-    if (geo.stages < kInFlight + 1) return cudaErrorInvalidConfiguration;
+    if (geo.stages < kMinStages) return cudaErrorInvalidConfiguration;
     geo.nbuf = std::min(geo.stages, 512 / (4 * BN));  // TMEM stage buffers (no more than smem stages)
     geo.mtiles = (M + BN - 1) / BN;
     geo.tiles = geo.mtiles * ((g.N + kTileN - 1) / kTileN);
@@ -578,7 +540,7 @@ cudaError_t launch_gemm_tc(const GemvParams& g, int epi, int M, cudaStream_t s) 
     const int BN = pick_bn(M, g.N);
     CUtensorMap tw, ta;
     const int npan = g.K / g.P;
-    if (!make_map(&tw, g.w, (uint64_t)g.P, (uint64_t)g.N * npan, (uint64_t)g.P, kTmaRows, false) ||
+    if (!make_map(&tw, g.w, (uint64_t)g.P, (uint64_t)g.N * npan, (uint64_t)g.P, kTileN, false) ||
         !make_map(&ta, g.aq, (uint64_t)g.K, (uint64_t)M, (uint64_t)g.K, (uint32_t)BN, true))
         return cudaErrorInvalidValue;
     switch (epi) {
