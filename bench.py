@@ -75,17 +75,30 @@ def engine_cfg(max_seq_len):
                 rope_theta=DIMS["theta"], norm_eps=DIMS["eps"])
 
 
-def step_bytes(k, ctx):
+def step_bytes(k, ctx, wbytes=1.0):
     """Algorithmic HBM bytes of one speculative step: k draft passes (4
-    layers + LM head) and one verify pass (32 layers + LM head) of INT8
-    weights with fp16 block scales, plus the fp16 KV read by attention."""
+    layers + LM head) and one verify pass (32 layers + LM head) of weights
+    (wbytes per weight: 1 INT8, 0.5 packed 4-bit) with fp16 block scales,
+    plus the fp16 KV read by attention."""
     d, F, V = DIMS["d"], DIMS["ffn"], DIMS["vocab"]
-    layer = (3 * d * d + d * d + 2 * F * d + d * F) * (1 + 1 / 16)
-    lm = V * d * (1 + 1 / 16)
+    layer = (3 * d * d + d * d + 2 * F * d + d * F) * (wbytes + 1 / 16)
+    lm = V * d * (wbytes + 1 / 16)
     kv_pos = 2 * d * 2  # K and V, fp16, one layer
     draft = k * (DRAFT_LAYERS * layer + lm + DRAFT_LAYERS * kv_pos * ctx)
     verify = DIMS["layers"] * layer + lm + DIMS["layers"] * kv_pos * ctx
     return draft + verify
+
+
+def medusa_step_bytes(rows, heads, ctx):
+    """Algorithmic HBM bytes of one Medusa tree step: the heads (one INT8
+    d x d linear each, their LM head pass over `heads` rows), one verify pass
+    over the tree's rows (32 layers, each weight read once; LM head in
+    ceil(rows / 8) eight-row passes) and the fp16 KV read by attention."""
+    d, F, V = DIMS["d"], DIMS["ffn"], DIMS["vocab"]
+    layer = (3 * d * d + d * d + 2 * F * d + d * F) * (1 + 1 / 16)
+    lm = V * d * (1 + 1 / 16)
+    kv = DIMS["layers"] * 2 * d * 2 * ctx
+    return heads * d * d * (1 + 1 / 16) + lm + DIMS["layers"] * layer + -(-rows // 8) * lm + kv
 
 
 def profiled_traffic(summary, m):
@@ -235,8 +248,7 @@ def cpu_reference_decode(a, n_tokens, warmup, steps):
     threads, and the same tokens. Returns the median decode-loop rate over
     `steps` decodes of n_tokens (each after its own prefill, excluded)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    threads = os.cpu_count() or 1
-    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
     import bind
     t0 = time.time()
     orc = bind.Oracle()
@@ -507,15 +519,20 @@ def run_medusa(a):
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    accs = []
+    accs, dec_us = [], []
     for _ in range(a.steps):
         toks, acc = eng.medusa_generate(prompt, a.new_tokens, topk, nodes)
         accs.append(acc)
+        dec_us.append(eng.last_timing()[2])  # the tree-step loop alone (after the prefill)
     e1.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
     ms = e0.elapsed_time(e1)
     acc_cat = np.concatenate(accs)
+    step_us = sum(dec_us) / max(1, len(acc_cat))
+    tree_bytes = medusa_step_bytes(nodes + 1, 4, a.prompt_len + a.new_tokens // 2)
+    tree_gbs = tree_bytes / (step_us * 1e-6) / 1e9
+    peak, peak_kind = measured_peaks()
     line = {
         "metric": "Phi-3-mini Medusa decode tok/s @bs1", "value": a.steps * a.new_tokens / (ms / 1e3), "unit": "tok/s",
         "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms / a.steps, "higher_is_better": True,
@@ -524,7 +541,11 @@ def run_medusa(a):
         "config": {"workload": f"phi3-mini int8 + 4 Medusa heads, top-k {topk}, {nodes}-node tree, bs1, "
                                f"prompt {a.prompt_len}, {a.new_tokens} new tokens per step (prefill included)"},
         "medusa": {"tree_steps_per_generate": len(acc_cat) / a.steps, "mean_accepted": float(acc_cat.mean()),
-                   "step_us": ms * 1e3 / max(1, len(acc_cat))},
+                   "step_us": step_us, "decode_tok_s": (a.new_tokens - 1) * len(dec_us) / (sum(dec_us) * 1e-6)},
+        "roofline": {"bound": "hbm", "achieved": tree_gbs, "peak": peak, "unit": "GB/s", "frac": tree_gbs / peak,
+                     "traffic": None, "peak_kind": peak_kind,
+                     "kernel": f"whole tree step ({nodes + 1} verify rows: tcgen05 GEMM, LM head in 8-row GEMVs)",
+                     "bytes_per_step": tree_bytes},
         "clocks": clk,
     }
     print(json.dumps(line), flush=True)
@@ -644,16 +665,21 @@ def run_sampled_batch(a):
 SHARD_CEILING = {1: 1.0, 2: 1.71, 4: 2.64, 8: 3.64}
 
 
-def split_host_threads():
-    """Ranks of one node share the host cores for the OpenMP weight
-    generator (set before the library, and its OpenMP runtime, load)."""
+def split_host_threads(impl):
+    """OpenMP threads of this process, set before the libraries (and their
+    OpenMP runtimes) load. The ranks of one node share the host cores for
+    the weight generator; the reference arm runs on rank 0 alone and takes
+    them all. torchrun exports OMP_NUM_THREADS=1 to every rank when the
+    variable is unset, so 1 counts as unset under it."""
     world = int(os.environ.get("LOCAL_WORLD_SIZE", os.environ.get("WORLD_SIZE", "1")))
-    if world > 1 and "OMP_NUM_THREADS" not in os.environ:
-        os.environ["OMP_NUM_THREADS"] = str(max(1, (os.cpu_count() or 1) // world))
+    cur = os.environ.get("OMP_NUM_THREADS")
+    if cur is not None and not (world > 1 and cur == "1"):
+        return
+    cores = os.cpu_count() or 1
+    os.environ["OMP_NUM_THREADS"] = str(cores if impl == "reference" else max(1, cores // world))
 
 
 def main():
-    split_host_threads()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
@@ -665,6 +691,8 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=16, help="tokens of the bounded CPU decode sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--microbench", choices=sorted(MICRO_SHAPES), help="time one GEMV shape in isolation")
+    ap.add_argument("--w4", action="store_true",
+                    help="decode passes stream packed 4-bit weights (fl_engine_set_weight_bits 4)")
     ap.add_argument("--step-kernel", action="store_true",
                     help="one persistent tcgen05 kernel per speculative step (128-byte panels)")
     ap.add_argument("--m", type=int, default=5, help="activation rows for --microbench")
@@ -675,6 +703,7 @@ def main():
     ap.add_argument("--batch", type=int, default=1, help="sequences decoded together by --workload tp-medium")
     ap.add_argument("--tree", type=int, default=0, help="draft-tree width for --workload tp-medium (0: chain)")
     a = ap.parse_args()
+    split_host_threads(a.impl)
     if a.microbench:
         return run_microbench(a)
     if a.workload == "sampled-batch":
@@ -709,6 +738,9 @@ def main():
     max_seq = 512
     eng = flb200.Engine(lib, engine_cfg(max_seq), local)
     eng.synthesize(SEED)  # the seeded generator on the device: the tensors the CPU arm generates
+    if a.w4:
+        eng.set_weight_bits(4)
+    wbytes = 0.5 if a.w4 else 1.0
     prompt = np.random.default_rng(PROMPT_SEED).integers(0, DIMS["vocab"], a.prompt_len).astype(np.int32)
     eng.spec_prefill(prompt, a.k)
     setup_s = time.time() - t_setup
@@ -753,7 +785,7 @@ def main():
     step_us = ms_per_step * 1000.0 / spec_steps
     ctx_mid = a.prompt_len + a.new_tokens // 2
     peak, peak_kind = measured_peaks()
-    step_gbs = step_bytes(a.k, ctx_mid) / (step_us * 1e-6) / 1e9
+    step_gbs = step_bytes(a.k, ctx_mid, wbytes) / (step_us * 1e-6) / 1e9
 
     # Dominant kernel: the verify pass's gate/up GEMV (M = k + 1), timed live
     # as captured back-to-back launches over all 32 layers (1.6 GB > L2).
@@ -806,17 +838,18 @@ def main():
             "warmup": a.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "u8xs8->s32, f32",
             "data": "synthetic (seeded N(0,0.02) -> Q4_0 -> INT8 weights, uniform prompt ids)",
-            "config": workload_config(a, world),
-            "step_path": "one persistent tcgen05 kernel per step" if eng.step_kernel()
+            "config": dict(workload_config(a, world),
+                           weights="packed 4-bit in the decode passes" if a.w4 else "INT8"),
+            "step_path": "one persistent cooperative kernel per step" if eng.step_kernel()
             else "multi-kernel CUDA graph per step",
             "spec": {"spec_steps_per_decode": spec_steps, "mean_accepted": float(acc_cat.mean()),
                      "accepted_hist": np.bincount(acc_cat, minlength=a.k + 1).tolist(),
-                     "step_us": step_us, "step_bytes": step_bytes(a.k, ctx_mid), "step_gbs": step_gbs,
+                     "step_us": step_us, "step_bytes": step_bytes(a.k, ctx_mid, wbytes), "step_gbs": step_gbs,
                      "step_frac_of_hbm": step_gbs / peak},
             "verify_step_us_est": 32 * (us_gu + us_dn + us_qkv + us_o),
             "roofline": {"bound": "hbm", "achieved": kern_gbs, "peak": peak, "unit": "GB/s",
                          "frac": kern_gbs / peak,
-                         "traffic": None if eng.step_kernel() else profiled_traffic(
+                         "traffic": None if eng.step_kernel() or a.w4 else profiled_traffic(
                              "gemv_tma_gateup_16384x3072.md", a.k + 1),
                          "peak_kind": peak_kind,
                          "kernel": "gemv_tma_kernel (verify gate/up, 16384x3072, M=%d)" % (a.k + 1),

@@ -54,8 +54,10 @@ int alloc_linear(Linear& l, int N, int K, unsigned need, bool step_layout) {
 void free_linear(Linear& l) {
     cudaFree(l.w);
     cudaFree(l.s);
+    cudaFree(l.w4);
     l.w = nullptr;
     l.s = nullptr;
+    l.w4 = nullptr;
 }
 
 int alloc_stack(fl_engine* e, Stack& S, int nl) {
@@ -123,6 +125,7 @@ GemvParams gemv_base(const Linear& l, const uint8_t* aq, const int* done) {
     GemvParams g = {};
     g.aq = aq;
     g.w = l.w;
+    g.w4 = l.w4;
     g.P = l.P;
     g.sblk = l.s;
     g.N = l.N;
@@ -1172,6 +1175,51 @@ int drop_step_graph(fl_engine* e) {
 }
 }  // namespace
 
+FL_API int fl_engine_set_weight_bits(fl_engine_t* e, int bits) {
+    if (!e) return set_error(FL_E_INVAL, "engine is NULL");
+    if (bits != 4 && bits != 8) return set_error(FL_E_INVAL, "set_weight_bits: 4 or 8");
+    FL_CHECK(check_ready(e, false));
+    FL_CHECK(drop_step_graph(e));
+    if (e->bt.exec) {
+        FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
+        cudaGraphExecDestroy(e->bt.exec);
+        e->bt.exec = nullptr;
+        e->bt.ready = false;
+    }
+    std::vector<Linear*> all;
+    for (Stack* S : {&e->base, &e->draft})
+        for (auto& W : S->L) all.insert(all.end(), {&W.qkv, &W.o, &W.gu, &W.down});
+    all.push_back(&e->lm);
+    for (auto& m : e->medusa) all.push_back(&m);
+    FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
+    for (Linear* l : all) {
+        cudaFree(l->w4);
+        l->w4 = nullptr;
+    }
+    if (bits == 8) return FL_OK;
+    int* bad = nullptr;
+    FL_CHECK_CUDA(cudaMalloc(&bad, sizeof(int)));
+    int rc = FL_OK;
+    cudaError_t ce = cudaMemsetAsync(bad, 0, sizeof(int), e->s);
+    for (Linear* l : all) {
+        if (ce != cudaSuccess || !l->w || !w4_supported(l->N, l->K, l->P)) continue;
+        ce = cudaMalloc(&l->w4, (size_t)l->N * l->K / 2);
+        if (ce == cudaSuccess) ce = launch_pack_w4(l->w, l->w4, l->N, l->K, l->P, bad, e->s);
+    }
+    int hbad = 0;
+    if (ce == cudaSuccess) ce = cudaMemcpyAsync(&hbad, bad, sizeof(int), cudaMemcpyDeviceToHost, e->s);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(e->s);
+    cudaFree(bad);
+    if (ce != cudaSuccess) rc = cuda_error(ce, "set_weight_bits");
+    else if (hbad) rc = set_error(FL_E_INVAL, "set_weight_bits: a weight lies outside [-8, 7]");
+    if (rc != FL_OK)
+        for (Linear* l : all) {
+            cudaFree(l->w4);
+            l->w4 = nullptr;
+        }
+    return rc;
+}
+
 FL_API int fl_engine_spec_prefill(fl_engine_t* e, const int* prompt, int P, int K, int max_acc) {
     FL_CHECK(check_ready(e, true));
     if (!prompt || P <= 0 || K < 1 || K > kMaxDraft || P + 2 > e->R)
@@ -1480,7 +1528,8 @@ FL_API int fl_engine_bench_linear(fl_engine_t* e, int stack, int kind, int M, in
     cudaEventElapsedTime(&ms, e->ev[2], e->ev[3]);
     if (us_per_launch) *us_per_launch = ms * 1000.0 / ((double)reps * S.nl);
     if (bytes_per_launch)
-        *bytes_per_launch = (double)l0->N * l0->K * (1.0 + 1.0 / 16.0) + (double)M * l0->K + 4.0 * M * l0->N;
+        *bytes_per_launch = (double)l0->N * l0->K * ((l0->w4 && M <= kGemmMinRows ? 0.5 : 1.0) + 1.0 / 16.0) +
+                            (double)M * l0->K + 4.0 * M * l0->N;
     return FL_OK;
 }
 
@@ -1754,18 +1803,25 @@ FL_API int fl_engine_medusa_generate(fl_engine_t* e, const int* prompt, int P, i
         max_nodes < 2 || max_nodes > 256 || P + n_new + max_nodes + 2 > e->R)
         return set_error(FL_E_INVAL, "medusa_generate: bad arguments, missing heads or context too long");
     int kmax = 1;
+    long long cand = 0, width = 1;
     for (int h = 0; h < H; h++) {
         if (topk[h] < 1 || topk[h] > 32) return set_error(FL_E_INVAL, "medusa_generate: top-k must be 1..32");
         kmax = std::max(kmax, topk[h]);
+        width *= topk[h];
+        cand += width;
+        if (cand > kMaxTreeCand)
+            return set_error(FL_E_INVAL, "medusa_generate: more than 1024 tree candidates (sum of top-k products)");
     }
+    const int M = 1 + std::min<int>(max_nodes - 1, (int)cand);  // tree nodes of every step
     const int d = e->d, V = e->V;
     cudaStream_t s = e->s;
     // device work buffers for this call
     float *mf = nullptr, *my = nullptr, *mz = nullptr, *mprob = nullptr;
     int *mk = nullptr, *mtt = nullptr, *mtok = nullptr, *mpos = nullptr, *mtarget = nullptr, *mpath = nullptr;
+    int *mpar = nullptr, *mdep = nullptr, *mrec = nullptr, *mroot = nullptr;
     KvLayer* dkv = nullptr;
     auto cleanup = [&]() {
-        void* bufs[] = {mf, my, mz, mprob, mk, mtt, mtok, mpos, mtarget, mpath, dkv};
+        void* bufs[] = {mf, my, mz, mprob, mk, mtt, mtok, mpos, mtarget, mpath, mpar, mdep, mrec, mroot, dkv};
         for (void* p : bufs) cudaFree(p);
     };
     auto fail = [&](int rc) {
@@ -1792,6 +1848,10 @@ FL_API int fl_engine_medusa_generate(fl_engine_t* e, const int* prompt, int P, i
     FL_MED_CUDA(cudaMalloc(&mpos, sizeof(int) * max_nodes));
     FL_MED_CUDA(cudaMalloc(&mtarget, sizeof(int) * max_nodes));
     FL_MED_CUDA(cudaMalloc(&mpath, sizeof(int) * max_nodes));
+    FL_MED_CUDA(cudaMalloc(&mpar, sizeof(int) * max_nodes));
+    FL_MED_CUDA(cudaMalloc(&mdep, sizeof(int) * max_nodes));
+    FL_MED_CUDA(cudaMalloc(&mrec, sizeof(int) * (max_nodes + 2)));
+    FL_MED_CUDA(cudaMalloc(&mroot, sizeof(int)));
     FL_MED_CUDA(cudaMalloc(&dkv, sizeof(KvLayer) * e->base.nl));
     FL_MED_CUDA(cudaMemcpyAsync(dkv, e->base.kv.data(), sizeof(KvLayer) * e->base.nl, cudaMemcpyHostToDevice, s));
     FL_MED_CUDA(cudaMemcpyAsync(mk, topk, sizeof(int) * H, cudaMemcpyHostToDevice, s));
@@ -1801,14 +1861,12 @@ FL_API int fl_engine_medusa_generate(fl_engine_t* e, const int* prompt, int P, i
     FL_MED(prefill_base(e, prompt, P));
     FL_MED_CUDA(cudaMemcpyAsync(mf, e->x + (size_t)(P - 1) * d, sizeof(float) * d, cudaMemcpyDeviceToDevice, s));
     int cur_tok = 0;
+    FL_MED_CUDA(cudaMemcpyAsync(mroot, e->seq + P, sizeof(int), cudaMemcpyDeviceToDevice, s));
     FL_MED_CUDA(cudaMemcpyAsync(&cur_tok, e->seq + P, sizeof(int), cudaMemcpyDeviceToHost, s));
     FL_MED_CUDA(cudaStreamSynchronize(s));
     int produced = 0, steps = 0, n = P;
     out[produced++] = cur_tok;
-    std::vector<int> htok((size_t)H * kmax), target(max_nodes), ntok, npar, ndep, path;
-    std::vector<float> hprob((size_t)H * kmax);
-    std::vector<int> hpos(max_nodes);
-    std::vector<uint8_t> mask((size_t)max_nodes * max_nodes);
+    std::vector<int> rec(M + 2);
     FL_MED_CUDA(cudaEventRecord(e->ev[0], s));
     while (produced < n_new) {
         // heads: h = RMSNorm(F), y_i = W_i h, z_i = h + SiLU(y_i), logits_i = LM(z_i)
@@ -1817,19 +1875,10 @@ FL_API int fl_engine_medusa_generate(fl_engine_t* e, const int* prompt, int P, i
         FL_MED_CUDA(launch_medusa_z(mf, my, nullptr, mz, d, H, e->c.norm_eps, s));
         FL_MED(gemv_rows(e, e->lm, mz, H, false, e->logits, V));
         FL_MED_CUDA(launch_topk_rows(e->logits, H, V, V, mk, kmax, mtt, mprob, s));
-        FL_MED_CUDA(cudaMemcpyAsync(htok.data(), mtt, sizeof(int) * htok.size(), cudaMemcpyDeviceToHost, s));
-        FL_MED_CUDA(cudaMemcpyAsync(hprob.data(), mprob, sizeof(float) * hprob.size(), cudaMemcpyDeviceToHost, s));
-        FL_MED_CUDA(cudaStreamSynchronize(s));
-        const int M = build_tree(cur_tok, H, topk, htok.data(), hprob.data(), kmax, max_nodes, ntok, npar, ndep);
-        for (int i = 0; i < M; i++) {
-            hpos[i] = n + ndep[i];
-            for (int j = 0; j < M; j++) mask[(size_t)i * M + j] = 0;
-            for (int j = i; j >= 0; j = npar[j]) mask[(size_t)i * M + j] = 1;
-        }
-        FL_MED_CUDA(cudaMemcpyAsync(mtok, ntok.data(), sizeof(int) * M, cudaMemcpyHostToDevice, s));
-        FL_MED_CUDA(cudaMemcpyAsync(mpos, hpos.data(), sizeof(int) * M, cudaMemcpyHostToDevice, s));
-        FL_MED_CUDA(cudaMemcpyAsync(e->mask, mask.data(), (size_t)M * M, cudaMemcpyHostToDevice, s));
-        // tree-masked verify: node i at slot n + i, rotary position n + depth
+        // candidate tree on the device: node i at slot n + i, rotary position n + depth
+        MedusaTreeParams tp = {mtt, mprob, mk, H, kmax, max_nodes, n, mroot, mtok, mpar, mdep, mpos, e->mask};
+        FL_MED_CUDA(launch_medusa_tree(tp, s));
+        // tree-masked verify
         FL_MED_CUDA(launch_embed_rows(e->embed, V, mtok, nullptr, 0, e->x, d, M, nullptr, nullptr, s, false));
         FL_MED(run_stack(e, e->base, e->x, M, nullptr, e->iota + n, mpos, e->mask, nullptr, false));
         for (int r0 = 0; r0 < M; r0 += kMaxRows) {
@@ -1837,32 +1886,19 @@ FL_API int fl_engine_medusa_generate(fl_engine_t* e, const int* prompt, int P, i
             FL_MED(run_lm(e, e->x + (size_t)r0 * d, m, nullptr, nullptr, false));
             FL_MED_CUDA(launch_argmax_rows(e->amax, e->nparts, m, mtarget + r0, nullptr, s));
         }
-        FL_MED_CUDA(cudaMemcpyAsync(target.data(), mtarget, sizeof(int) * M, cudaMemcpyDeviceToHost, s));
+        // longest path of the base model's greedy choices, its KV moved to
+        // consecutive slots, the next root and feature; one read-back per step
+        MedusaWalkParams wp = {mtok, mpar, mtarget, M, mpath, mrec, mroot, e->x, mf, d};
+        FL_MED_CUDA(launch_medusa_walk(wp, s));
+        FL_MED_CUDA(launch_kv_compact_dev(dkv, e->base.nl, e->base.block_table, e->Hkv, e->hd, e->iota + n, mpath,
+                                          mrec, s));
+        FL_MED_CUDA(cudaMemcpyAsync(rec.data(), mrec, sizeof(int) * (M + 2), cudaMemcpyDeviceToHost, s));
         FL_MED_CUDA(cudaStreamSynchronize(s));
-        // longest path of the base model's greedy choices
-        path.assign(1, 0);
-        int cur = 0;
-        for (;;) {
-            int nxt = -1;
-            for (int c2 = 1; c2 < M; c2++)
-                if (npar[c2] == cur && ntok[c2] == target[cur]) {
-                    nxt = c2;
-                    break;
-                }
-            if (nxt < 0) break;
-            path.push_back(nxt);
-            cur = nxt;
-        }
-        const int a = (int)path.size() - 1;
+        const int a = rec[0];
+        if (a < 0 || a >= M) return fail(set_error(FL_E_CUDA, "medusa_generate: bad accepted path"));
         if (acc_hist) acc_hist[steps] = a;
         steps++;
-        for (int j = 1; j <= a + 1 && produced < n_new; j++) out[produced++] = j <= a ? ntok[path[j]] : target[cur];
-        if (a > 0) {
-            FL_MED_CUDA(cudaMemcpyAsync(mpath, path.data(), sizeof(int) * (a + 1), cudaMemcpyHostToDevice, s));
-            FL_MED_CUDA(launch_kv_compact(dkv, e->base.nl, e->base.block_table, e->Hkv, e->hd, e->iota + n, mpath, a, s));
-        }
-        FL_MED_CUDA(cudaMemcpyAsync(mf, e->x + (size_t)cur * d, sizeof(float) * d, cudaMemcpyDeviceToDevice, s));
-        cur_tok = target[cur];
+        for (int j = 1; j <= a + 1 && produced < n_new; j++) out[produced++] = rec[1 + j];
         n += a + 1;
     }
     FL_MED_CUDA(cudaEventRecord(e->ev[1], s));

@@ -28,6 +28,7 @@ namespace fl_eng {
 struct Linear {
     int8_t* w = nullptr;
     __half* s = nullptr;
+    uint8_t* w4 = nullptr;  // packed 4-bit copy (w4.cu) read by the GEMV when the engine runs 4-bit weights
     int N = 0, K = 0;
     int P = 0;  // tiled-layout panel width (fl_layout.cuh), 0 = row-major
     unsigned need = 0, have = 0;  // bit masks of the source tensors loaded

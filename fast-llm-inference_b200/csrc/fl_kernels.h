@@ -29,6 +29,7 @@ struct KvLayer {
 struct GemvParams {
     const uint8_t* aq;        // [rows, K] quantized activations
     const int8_t* w;          // [N, K]: row-major (P == 0) or tiled (fl_layout.cuh)
+    const uint8_t* w4;        // if set: the same weights packed 4-bit (w4.cu); the TMA-ring GEMV reads these
     int P;                    // tiled-layout panel width; 0 = plain row-major
     const __half* sblk;       // [N, K/32] block scales (block mode)
     const float* srow;        // [N] per-row scales (per-row mode)
@@ -191,5 +192,53 @@ cudaError_t launch_topk_keys(const float* logits, int rows, int V, int ld, int v
                              cudaStream_t s);
 cudaError_t launch_kv_compact(const KvLayer* layers, int n_layers, const int* block_table, int kv_heads, int head_dim,
                               const int* base, const int* src, int a, cudaStream_t s);
+// The same compaction with the path length read on the device (*a_dev, at
+// most a_max).
+// Packed 4-bit copy (w4.cu) of tiled INT8 block-mode weights in [-8, 7]:
+// w4 gets N * K / 2 bytes; *bad (device) is set if a weight is out of range.
+bool w4_supported(int N, int K, int P);
+cudaError_t launch_pack_w4(const int8_t* w, uint8_t* w4, int N, int K, int P, int* bad, cudaStream_t s);
+
+cudaError_t launch_kv_compact_dev(const KvLayer* layers, int n_layers, const int* block_table, int kv_heads,
+                                  int head_dim, const int* base, const int* src, const int* a_dev, cudaStream_t s);
+
+// Medusa candidate tree on the device (one CTA): candidates in generation
+// order (head h's top-k under every depth-h candidate), score = product of
+// the path's probabilities from the first head on, kept by (score desc,
+// depth asc, generation asc) up to max_nodes - 1 below the root; node i's
+// token, parent, depth, rotary position n + depth and its ancestor mask row.
+struct MedusaTreeParams {
+    const int* tok;     // [H][kmax] per-head top-k tokens
+    const float* prob;  // [H][kmax] their probabilities
+    const int* topk;    // [H] (device)
+    int H, kmax, max_nodes, n;
+    const int* root;    // [1] root token (device)
+    int* ntok;          // [max_nodes]
+    int* npar;
+    int* ndep;
+    int* pos;
+    uint8_t* mask;      // [M][M], M = 1 + min(max_nodes - 1, candidates)
+};
+constexpr int kMaxTreeCand = 1024;
+cudaError_t launch_medusa_tree(const MedusaTreeParams& p, cudaStream_t s);
+
+// Longest path of the base model's greedy choices through a verified tree
+// (node c follows node cur when npar[c] == cur and ntok[c] == target[cur],
+// first such c): path[0 .. a] (node indices), rec = {a, last node, the a
+// accepted tokens, the base token after them}, *root = that token, and the
+// last node's feature row x[last] copied to f (d floats).
+struct MedusaWalkParams {
+    const int* ntok;
+    const int* npar;
+    const int* target;  // [M] base argmax per node
+    int M;
+    int* path;
+    int* rec;           // [M + 2]
+    int* root;
+    const float* x;     // [M][d] last-layer features of the tree rows
+    float* f;
+    int d;
+};
+cudaError_t launch_medusa_walk(const MedusaWalkParams& p, cudaStream_t s);
 
 }  // namespace fl

@@ -50,6 +50,17 @@ __host__ __device__ __forceinline__ size_t tiled_s_off(int N, int P, int n, int 
     return ((size_t)p * N + n) * (size_t)bpp + bb;
 }
 
+// 4-bit tiled layout (w4.cu): byte offset of the 16-byte chunk of 32-element
+// block b of row n; panels of P columns are P / 2 bytes per row, chunks
+// swizzled like the INT8 layout's.
+__host__ __device__ __forceinline__ size_t tiled_w4_off(int N, int P, int n, int b) {
+    const int bpp = P >> 5;
+    const int p = b / bpp;
+    const int bb = b - p * bpp;
+    const int phys = (bb & ~7) | ((bb & 7) ^ (n & 7));
+    return ((size_t)p * N + n) * (size_t)(P >> 1) + (size_t)phys * 16;
+}
+
 // Physical chunk of logical chunk cc (within a panel row) for row n.
 __host__ __device__ __forceinline__ int swz_chunk(int cc, int n) { return (cc & ~7) | ((cc & 7) ^ (n & 7)); }
 

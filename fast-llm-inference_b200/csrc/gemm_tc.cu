@@ -6,7 +6,7 @@
 //   C[m, n] = (sum over blocks b, in order, of (float)dot_b(m, n) * d[n, b]) / 127
 // with dot_b the exact int32 dot of 32 u8 activations and 32 s8 weights.
 //
-// A tile is 128 weight rows x BN (16 or 32) activation rows. The kernel is
+// A tile is 128 weight rows x BN (16, 32 or 64) activation rows. The kernel is
 // persistent: one CTA per SM walks the tiles blockIdx.x, + gridDim.x, ...
 // (activation tiles fastest, so concurrent CTAs share weight tiles in L2),
 // and its stage counters run on across tiles, so the next tile's copies and
@@ -71,7 +71,12 @@ constexpr int kMaxStagesG = 8;
 constexpr int kMaxBuf = 32;
 constexpr int kSmemBudget = 220 * 1024;
 constexpr unsigned long long kWaitNsG = 2000000000ull;
+#ifndef FL_GEMM_SUSPEND
+#define FL_GEMM_SUSPEND 0
+#endif
+#if FL_GEMM_SUSPEND
 constexpr uint32_t kSuspendNs = 1000000;  // try_wait suspend-time hint (a bound; completion wakes earlier)
+#endif
 constexpr uint32_t kMagicBits = 0x4B400000u;  // 12582912.0f
 constexpr float kMagic = 12582912.0f;
 
@@ -90,17 +95,26 @@ __device__ __forceinline__ void mb_arrive(uint64_t* b) {
 __device__ __forceinline__ void mb_expect(uint64_t* b, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(b)), "r"(bytes) : "memory");
 }
-// try_wait with a suspend-time hint: a thread whose phase has not completed
-// sleeps (up to the hint, woken when the phase completes) instead of spinning,
-// leaving the issue slots to the warps that do the work.
+// try_wait: with FL_GEMM_SUSPEND a suspend-time hint lets a thread whose
+// phase has not completed sleep (woken when the phase completes) instead of
+// polling; without it the instruction polls for its own short window.
 __device__ __forceinline__ bool mb_try(uint64_t* b, uint32_t par) {
     uint32_t ok;
+#if FL_GEMM_SUSPEND
     asm volatile(
         "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
         : "r"(saddr(b)), "r"(par), "r"(kSuspendNs)
         : "memory");
+#else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(saddr(b)), "r"(par)
+        : "memory");
+#endif
     return ok != 0;
 }
 // Bounded wait of one thread: the clock is read between suspended tries.
@@ -496,7 +510,8 @@ cudaError_t launch_epi(const CUtensorMap& tw, const CUtensorMap& ta, const GemvP
                        cudaStream_t s) {
     switch (BN) {
         case 16: return launch_bn<16, EPI>(tw, ta, g, M, s);
-        default: return launch_bn<32, EPI>(tw, ta, g, M, s);
+        case 32: return launch_bn<32, EPI>(tw, ta, g, M, s);
+        default: return launch_bn<64, EPI>(tw, ta, g, M, s);
     }
 }
 
@@ -509,23 +524,24 @@ bool gemm_tc_supported(const GemvParams& g, int epi) {
     return encode_fn() != nullptr;
 }
 
-// Tile width: the candidate (16 or 32 rows: a stage's TMEM buffer of 4 BN
-// columns, double-buffered by half stages, fits the readout registers) with
-// the least modelled time = waves x per-tile time; per-tile time grows with
-// BN (measured about 1 : 1.45 for 16 : 32 on B200). Narrow tiles also spread
-// small-N layers over more SMs (their weight tiles are then re-read from L2).
+// Tile width: the candidate (16, 32 or 64 activation rows) with the least
+// modelled time = waves x per-tile time. Measured per-tile times over
+// K = 3072 on B200 are about 27.6, 33.2 and 44.4 us for 16-, 32- and 64-row
+// tiles (22 + 0.35 BN): wider tiles read each weight tile once for more rows
+// and give it more readout warps, narrower ones spread small-N layers (the o
+// and down projections: 24 weight tiles) over more SMs.
+#ifndef FL_GEMM_MAX_BN
+#define FL_GEMM_MAX_BN 64
+#endif
 int pick_bn(int M, int N) {
     const int sms = gemm_sms();
     const int ntiles = (N + kTileN - 1) / kTileN;
-    const int cand[2] = {16, 32};
-    const double cost[2] = {1.0, 1.45};
-    int best = 32;
+    int best = 16;
     double best_t = 1e30;
-    for (int i = 0; i < 2; i++) {
-        const int bn = cand[i];
+    for (int bn = 16; bn <= FL_GEMM_MAX_BN; bn *= 2) {
         const int mt = (M + bn - 1) / bn;
         const int waves = (ntiles * mt + sms - 1) / sms;
-        const double t = waves * cost[i];
+        const double t = waves * (22.0 + 0.35 * bn);
         if (t < best_t - 1e-9) {
             best_t = t;
             best = bn;

@@ -47,24 +47,32 @@ constexpr int kSmemLimit = FL_TMA_SMEM_KB * 1024;
 constexpr int kCtasPerSm = FL_TMA_CTAS_PER_SM;
 
 struct Geo {
-    int P;         // panel width (bytes of a stage row)
+    int P;         // panel width (weights of a stage row)
     int npan;      // K / P
     int S;         // ring stages
     int act_ld;    // activation row stride in shared memory (K + 16)
-    int act_bytes; // shared bytes of the activation rows
+    int act_bytes; // shared bytes of the activation rows (and, 4-bit, their block sums)
+    int asum_off;  // 4-bit: byte offset of the int block sums [rows][K / 32]
 };
 
-__host__ __device__ inline size_t slot_bytes(int P) { return (size_t)kStageRows * P + (size_t)kStageRows * (P / 16); }
+// Bytes of a stage row's weights: P int8, or P / 2 packed 4-bit.
+__host__ __device__ inline int row_bytes(int P, bool w4) { return w4 ? P >> 1 : P; }
+__host__ __device__ inline size_t slot_bytes(int P, bool w4 = false) {
+    return (size_t)kStageRows * row_bytes(P, w4) + (size_t)kStageRows * (P / 16);
+}
 
 // P: the weights' panel width (0 = the default width for K).
-inline bool make_geo(int K, int mrows, Geo& g, int P = 0) {
+inline bool make_geo(int K, int mrows, Geo& g, int P = 0, bool w4 = false) {
     g.P = P ? P : panel_width(K);
     if (!g.P || g.P % 128 || K % g.P || mrows < 1 || mrows > kMaxRows) return false;
+    if (w4 && g.P % 256) return false;
     g.npan = K / g.P;
     g.act_ld = K + 16;
-    g.act_bytes = ((mrows * g.act_ld) + 127) & ~127;
+    g.asum_off = ((mrows * g.act_ld) + 127) & ~127;
+    const int mmax = mrows <= 1 ? 1 : (mrows <= 2 ? 2 : (mrows <= 4 ? 4 : 8));  // the kernel's row template
+    g.act_bytes = g.asum_off + (w4 ? ((mmax * (K / 32) * 4 + 127) & ~127) : 0);
     const long avail = (long)kSmemLimit - g.act_bytes - 256;
-    const int S = (int)(avail / (long)slot_bytes(g.P));
+    const int S = (int)(avail / (long)slot_bytes(g.P, w4));
     if (S < 2) return false;
     g.S = S > kMaxStages ? kMaxStages : S;
     return true;
@@ -114,7 +122,30 @@ __device__ __forceinline__ void pair_epi_any(int epi, const GemvParams& p, int r
     }
 }
 
-template <int MMAX, int EPI, bool MMA>
+// d = u8 . q over one block of packed 4-bit weights (a: 32 activation bytes,
+// w: the block's 16 bytes; q[j] low nibbles, q[j + 16] high nibbles).
+__device__ __forceinline__ int dot_w4(const uint4& a0, const uint4& a1, const uint4& w) {
+    const uint32_t m = 0x0F0F0F0Fu;
+    int d = (int)__dp4a(a0.x, w.x & m, 0u);
+    d = (int)__dp4a(a0.y, w.y & m, (unsigned)d);
+    d = (int)__dp4a(a0.z, w.z & m, (unsigned)d);
+    d = (int)__dp4a(a0.w, w.w & m, (unsigned)d);
+    d = (int)__dp4a(a1.x, (w.x >> 4) & m, (unsigned)d);
+    d = (int)__dp4a(a1.y, (w.y >> 4) & m, (unsigned)d);
+    d = (int)__dp4a(a1.z, (w.z >> 4) & m, (unsigned)d);
+    return (int)__dp4a(a1.w, (w.w >> 4) & m, (unsigned)d);
+}
+
+// D(16x8, s32) = A(16x32, u8, row) x B(32x8, u8, col) (4-bit weights as q).
+__device__ __forceinline__ void mma_u8u8(uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1, int& d0, int& d1) {
+    int c2, c3;
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+        : "=r"(d0), "=r"(d1), "=r"(c2), "=r"(c3)
+        : "r"(a0), "r"(0), "r"(a2), "r"(0), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+template <int MMAX, int EPI, bool MMA, bool W4>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const GemvParams p, const Geo geo,
                                                                          const int epi_rt) {
     const int epi = EPI >= 0 ? EPI : epi_rt;
@@ -134,8 +165,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const Ge
     const int row0 = u0 * 8, row1 = u1 * 8;
     const int ntiles = (row1 - row0 + kStageRows - 1) / kStageRows;
     const int total = ntiles * npan;
-    const size_t slot = slot_bytes(P);
+    const size_t slot = slot_bytes(P, W4);
+    const int wrb = row_bytes(P, W4);  // weight bytes of a stage row
     uint8_t* act = smem;
+    int* asum = reinterpret_cast<int*>(smem + geo.asum_off);  // 4-bit: [MMAX][K / 32]
     uint8_t* ring = smem + geo.act_bytes;
 
     if (threadIdx.x == 0) {
@@ -159,9 +192,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const Ge
             const int r = row0 + tile * kStageRows;
             const int rows = min(kStageRows, row1 - r);
             uint8_t* dw = ring + (size_t)sl * slot;
-            uint8_t* ds = dw + (size_t)kStageRows * P;
-            mbar_arrive_expect_tx(&full_bar[sl], (uint32_t)(rows * P + rows * (P / 16)));
-            bulk_g2s(dw, p.w + ((size_t)pan * N + r) * P, (uint32_t)(rows * P), &full_bar[sl]);
+            uint8_t* ds = dw + (size_t)kStageRows * wrb;
+            const uint8_t* wsrc = W4 ? p.w4 : reinterpret_cast<const uint8_t*>(p.w);
+            mbar_arrive_expect_tx(&full_bar[sl], (uint32_t)(rows * wrb + rows * (P / 16)));
+            bulk_g2s(dw, wsrc + ((size_t)pan * N + r) * wrb, (uint32_t)(rows * wrb), &full_bar[sl]);
             bulk_g2s(ds, sbase + ((size_t)pan * N + r) * (P / 16), (uint32_t)(rows * (P / 16)), &full_bar[sl]);
         };
         const int first = total < S ? total : S;
@@ -199,6 +233,30 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const Ge
         }
     }
     asm volatile("bar.sync 1, %0;" ::"n"(kCWarps * 32) : "memory");
+    if (W4) {
+        // per (row, block) sum of the u8 activations: the 4-bit dots are over
+        // q = w + 8, so each block's dot is d(q) - 8 * sum
+        const int nbk = K >> 5;
+        for (int i = threadIdx.x; i < MMAX * nbk; i += kCWarps * 32) {
+            const int m = i / nbk, b = i - m * nbk;
+            int t = 0;
+            if (m < rows_m) {
+                const uint4* a = reinterpret_cast<const uint4*>(act + (size_t)m * ald + (size_t)b * 32);
+                const uint4 x0 = a[0], x1 = a[1];
+                const uint32_t one = 0x01010101u;
+                t = (int)__dp4a(x0.x, one, 0u);
+                t = (int)__dp4a(x0.y, one, (unsigned)t);
+                t = (int)__dp4a(x0.z, one, (unsigned)t);
+                t = (int)__dp4a(x0.w, one, (unsigned)t);
+                t = (int)__dp4a(x1.x, one, (unsigned)t);
+                t = (int)__dp4a(x1.y, one, (unsigned)t);
+                t = (int)__dp4a(x1.z, one, (unsigned)t);
+                t = (int)__dp4a(x1.w, one, (unsigned)t);
+            }
+            asum[i] = t;
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(kCWarps * 32) : "memory");
+    }
 
     const int bpp = P >> 5;   // 32-element blocks per panel row
     bool bad = false;
@@ -218,10 +276,29 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const Ge
             if (!bad && lr < rows && rows_m > 0) {
                 const bool two = lr + 1 < rows;
                 const uint8_t* dw = ring + (size_t)sl * slot;
-                const __half* ds = reinterpret_cast<const __half*>(dw + (size_t)kStageRows * P);
+                const __half* ds = reinterpret_cast<const __half*>(dw + (size_t)kStageRows * wrb);
                 const int ra = lr, rb = two ? lr + 1 : lr;
-                const uint8_t* wa = dw + (size_t)ra * P;
-                const uint8_t* wb = dw + (size_t)rb * P;
+                const uint8_t* wa = dw + (size_t)ra * wrb;
+                const uint8_t* wb = dw + (size_t)rb * wrb;
+                if (W4) {
+                    for (int c = lane; c < bpp; c += 32) {  // one 16-byte chunk = one block
+                        const uint4 w0 = *reinterpret_cast<const uint4*>(wa + swz_chunk(c, r + ra) * 16);
+                        const uint4 w1 = *reinterpret_cast<const uint4*>(wb + swz_chunk(c, r + rb) * 16);
+                        const uint4* ap = reinterpret_cast<const uint4*>(act + (size_t)pan * P + (size_t)c * 32);
+                        const uint4 x0 = ap[0], x1 = ap[1];
+                        const int bsum = 8 * asum[pan * bpp + c];
+                        const int d0 = dot_w4(x0, x1, w0) - bsum, d1 = dot_w4(x0, x1, w1) - bsum;
+                        if (epi == EPI_DOTS) {
+                            const int nbk = K >> 5;
+                            int32_t* dd = p.dots + (size_t)p.row0 * N * nbk;
+                            dd[(size_t)(r + ra) * nbk + pan * bpp + c] = d0;
+                            if (two) dd[(size_t)(r + rb) * nbk + pan * bpp + c] = d1;
+                        } else {
+                            f0 = __fmaf_rn(i2f_exact(d0), __half2float(ds[ra * bpp + c]), f0);
+                            f1 = __fmaf_rn(i2f_exact(d1), __half2float(ds[rb * bpp + c]), f1);
+                        }
+                    }
+                } else {
                 for (int c = lane; c < cpp; c += 32) {  // logical chunk within the panel row
                     const uint4 w0 = *reinterpret_cast<const uint4*>(wa + swz_chunk(c, r + ra) * 16);
                     const uint4 w1 = *reinterpret_cast<const uint4*>(wb + swz_chunk(c, r + rb) * 16);
@@ -230,6 +307,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const Ge
                     const uint4 a = *reinterpret_cast<const uint4*>(act + (size_t)pan * P + (size_t)c * 16);
                     f0 = __fmaf_rn(i2f_exact(dot16(a, w0)), s0, f0);
                     f1 = __fmaf_rn(i2f_exact(dot16(a, w1)), s1, f1);
+                }
                 }
             }
             __syncwarp();
@@ -259,21 +337,56 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const Ge
             const int rows = min(kStageRows, row1 - r);
             if (!bad && !mbar_wait(&full_bar[sl], (i / S) & 1)) bad = true;
             const uint8_t* dw = ring + (size_t)sl * slot;
-            const __half* ds = reinterpret_cast<const __half*>(dw + (size_t)kStageRows * P);
+            const __half* ds = reinterpret_cast<const __half*>(dw + (size_t)kStageRows * wrb);
             const uint32_t wrow = smem_u32(dw + (size_t)lrow * P);
             const uint8_t* arow_p = act + (size_t)g * ald + (size_t)pan * P;
             for (int kb = kb0; kb < (bad ? kb0 : kb1); kb++) {
-                const int chunk = 2 * kb + (lj & 1);
                 uint32_t b00, b01, b10, b11;
-                ldmatrix_x4(wrow + swz_chunk(chunk, r + lrow) * 16, b00, b01, b10, b11);
+                if (W4) {
+                    // rows g and 8 + g of the tile, bytes 4t .. 4t + 3 of the block:
+                    // low nibbles are elements 4t .. 4t + 3, high ones 16 + 4t ..
+                    const uint32_t wa = *reinterpret_cast<const uint32_t*>(
+                        dw + (size_t)g * wrb + swz_chunk(kb, r + g) * 16 + 4 * t);
+                    const uint32_t wb = *reinterpret_cast<const uint32_t*>(
+                        dw + (size_t)(8 + g) * wrb + swz_chunk(kb, r + 8 + g) * 16 + 4 * t);
+                    b00 = wa & 0x0F0F0F0Fu;
+                    b01 = (wa >> 4) & 0x0F0F0F0Fu;
+                    b10 = wb & 0x0F0F0F0Fu;
+                    b11 = (wb >> 4) & 0x0F0F0F0Fu;
+                } else {
+                    const int chunk = 2 * kb + (lj & 1);
+                    ldmatrix_x4(wrow + swz_chunk(chunk, r + lrow) * 16, b00, b01, b10, b11);
+                }
                 uint32_t a0 = 0, a2 = 0;
                 if (arow) {
                     a0 = *reinterpret_cast<const uint32_t*>(arow_p + kb * 32 + 4 * t);
                     a2 = *reinterpret_cast<const uint32_t*>(arow_p + kb * 32 + 16 + 4 * t);
                 }
                 int d0, d1, d2, d3;
-                mma_u8s8(a0, a2, b00, b01, d0, d1);
-                mma_u8s8(a0, a2, b10, b11, d2, d3);
+                if (W4) {
+                    mma_u8u8(a0, a2, b00, b01, d0, d1);
+                    mma_u8u8(a0, a2, b10, b11, d2, d3);
+                    const int bsum = arow ? 8 * asum[g * (K >> 5) + pan * bpp + kb] : 0;
+                    d0 -= bsum;
+                    d1 -= bsum;
+                    d2 -= bsum;
+                    d3 -= bsum;
+                    if (epi == EPI_DOTS) {
+                        if (arow) {
+                            const int nbk = K >> 5;
+                            int32_t* dd = p.dots + ((size_t)(p.row0 + g) * N) * nbk + pan * bpp + kb;
+                            const int n0 = 2 * t, n1 = 8 + 2 * t;
+                            if (n0 < rows) dd[(size_t)(r + n0) * nbk] = d0;
+                            if (n0 + 1 < rows) dd[(size_t)(r + n0 + 1) * nbk] = d1;
+                            if (n1 < rows) dd[(size_t)(r + n1) * nbk] = d2;
+                            if (n1 + 1 < rows) dd[(size_t)(r + n1 + 1) * nbk] = d3;
+                        }
+                        continue;
+                    }
+                } else {
+                    mma_u8s8(a0, a2, b00, b01, d0, d1);
+                    mma_u8s8(a0, a2, b10, b11, d2, d3);
+                }
                 const float s0 = __half2float(ds[(2 * t) * bpp + kb]);
                 const float s1 = __half2float(ds[(2 * t + 1) * bpp + kb]);
                 const float s2 = __half2float(ds[(8 + 2 * t) * bpp + kb]);
@@ -393,10 +506,10 @@ int sm_count() {
     return n;
 }
 
-template <int MMAX, int EPI, bool MMA>
+template <int MMAX, int EPI, bool MMA, bool W4>
 cudaError_t launch_t(const GemvParams& p, const Geo& geo, cudaStream_t s, bool pdl, int epi) {
-    auto kern = gemv_tma_kernel<MMAX, EPI, MMA>;
-    const size_t smem = (size_t)geo.act_bytes + (size_t)geo.S * slot_bytes(geo.P);
+    auto kern = gemv_tma_kernel<MMAX, EPI, MMA, W4>;
+    const size_t smem = (size_t)geo.act_bytes + (size_t)geo.S * slot_bytes(geo.P, W4);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
@@ -414,10 +527,16 @@ cudaError_t launch_t(const GemvParams& p, const Geo& geo, cudaStream_t s, bool p
 
 template <int EPI>
 cudaError_t launch_e(const GemvParams& p, const Geo& geo, cudaStream_t s, bool pdl, int epi) {
-    if (p.M <= 1) return launch_t<1, EPI, false>(p, geo, s, pdl, epi);
-    if (p.M <= 2) return launch_t<2, EPI, true>(p, geo, s, pdl, epi);
-    if (p.M <= 4) return launch_t<4, EPI, true>(p, geo, s, pdl, epi);
-    return launch_t<8, EPI, true>(p, geo, s, pdl, epi);
+    if (p.w4) {
+        if (p.M <= 1) return launch_t<1, EPI, false, true>(p, geo, s, pdl, epi);
+        if (p.M <= 2) return launch_t<2, EPI, true, true>(p, geo, s, pdl, epi);
+        if (p.M <= 4) return launch_t<4, EPI, true, true>(p, geo, s, pdl, epi);
+        return launch_t<8, EPI, true, true>(p, geo, s, pdl, epi);
+    }
+    if (p.M <= 1) return launch_t<1, EPI, false, false>(p, geo, s, pdl, epi);
+    if (p.M <= 2) return launch_t<2, EPI, true, false>(p, geo, s, pdl, epi);
+    if (p.M <= 4) return launch_t<4, EPI, true, false>(p, geo, s, pdl, epi);
+    return launch_t<8, EPI, true, false>(p, geo, s, pdl, epi);
 }
 
 }  // namespace
@@ -445,9 +564,10 @@ bool tma_gemv_supported(int N, int K, int M) {
 cudaError_t launch_gemv_tma(const GemvParams& p, int epi, cudaStream_t s, bool pdl) {
     if (p.M <= 0 || p.M > kMaxRows || p.N % 8 != 0 || p.P == 0) return cudaErrorInvalidValue;
     Geo geo;
-    if (!make_geo(p.K, p.M, geo, p.P)) return cudaErrorInvalidValue;
+    if (!make_geo(p.K, p.M, geo, p.P, p.w4 != nullptr)) return cudaErrorInvalidValue;
     if (p.x && p.K % 128 != 0) return cudaErrorInvalidValue;
-    if (epi < EPI_STORE || epi > EPI_TP_PUSH || epi == EPI_DOTS) return cudaErrorInvalidValue;
+    // integer block dots only from 4-bit weights (the INT8 ones go through gemv_i8.cu)
+    if (epi < EPI_STORE || epi > EPI_TP_PUSH || (epi == EPI_DOTS && !p.w4)) return cudaErrorInvalidValue;
     // One kernel body per row count for every epilogue: the epilogue is
     // chosen at run time, so the launches of a layer run the same code and
     // find it in the SM's instruction caches (7 % faster per decode step than
@@ -472,9 +592,11 @@ cudaError_t launch_tp_reduce(const TpReduceParams& p, cudaStream_t s, bool pdl) 
 
 cudaError_t launch_gemv_auto(const GemvParams& p, int epi, cudaStream_t s, bool pdl) {
     Geo geo;
-    if (epi != EPI_DOTS && p.P != 0 && p.N % 8 == 0 && make_geo(p.K, p.M, geo, p.P))
-        return launch_gemv_tma(p, epi, s, pdl);
-    return launch_gemv(p, epi, false, false, s, pdl);
+    if (p.w4 && p.P != 0 && p.N % 8 == 0 && make_geo(p.K, p.M, geo, p.P, true)) return launch_gemv_tma(p, epi, s, pdl);
+    GemvParams q = p;  // the INT8 copy serves every other case
+    q.w4 = nullptr;
+    if (epi != EPI_DOTS && q.P != 0 && q.N % 8 == 0 && make_geo(q.K, q.M, geo, q.P)) return launch_gemv_tma(q, epi, s, pdl);
+    return launch_gemv(q, epi, false, false, s, pdl);
 }
 
 int gemv_auto_grid(int N, int K) { return tma_gemv_supported(N, K, kMaxRows) ? tma_gemv_grid() : gemv_grid(N); }

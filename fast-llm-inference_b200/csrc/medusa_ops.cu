@@ -138,9 +138,10 @@ __global__ void topk_keys_kernel(const float* logits, int V, int ld, int v0, int
 // K / V of slot base + src[j] (src[j] >= j, src increasing, so an earlier move
 // never overwrites a later source). CTA = (layer, stack of kv heads).
 __global__ void kv_compact_kernel(const KvLayer* layers, const int* block_table, int kv_heads, int head_dim,
-                                  const int* base_p, const int* src, int a) {
+                                  const int* base_p, const int* src, int a, const int* a_dev) {
     const KvLayer L = layers[blockIdx.x];
     const int base = *base_p;
+    if (a_dev) a = *a_dev;
     const int hd2 = head_dim >> 1;
     for (int j = 1; j <= a; j++) {
         const int s_slot = base + src[j], d_slot = base + j;
@@ -157,6 +158,124 @@ __global__ void kv_compact_kernel(const KvLayer* layers, const int* block_table,
         }
         __syncthreads();
     }
+}
+
+constexpr int kTreeThreads = 1024;
+
+// Candidate tree (the rule of engine.cu build_tree and of the oracle's
+// orc_medusa_tree): one thread per candidate computes its path score in the
+// same left-to-right product order, its rank under the total order (score
+// desc, depth asc, generation asc) by counting the candidates before it, and
+// the kept ones (rank < max_nodes - 1) become node rank + 1. A kept
+// candidate's parent ranks before it (its score is at least the child's and
+// its depth smaller), so it is kept too.
+__global__ void __launch_bounds__(kTreeThreads) medusa_tree_kernel(const MedusaTreeParams p) {
+    __shared__ float sc[kMaxTreeCand];
+    __shared__ int dep[kMaxTreeCand], par[kMaxTreeCand], tk[kMaxTreeCand], rk[kMaxTreeCand];
+    __shared__ int spar[256];
+    __shared__ int lstart[kMaxRows + 1], ltopk[kMaxRows];
+    __shared__ int total_s;
+    const int t = threadIdx.x;
+    if (t == 0) {
+        int width = 1, tot = 0;
+        for (int h = 0; h < p.H; h++) {
+            ltopk[h] = min(max(p.topk[h], 0), p.kmax);
+            lstart[h] = tot;
+            width *= ltopk[h];
+            if (tot + width > kMaxTreeCand) width = kMaxTreeCand - tot;  // bounded (the host checks the count)
+            tot += width;
+        }
+        lstart[p.H] = tot;
+        total_s = tot;
+    }
+    __syncthreads();
+    const int C = total_s;
+    for (int i = t; i < C; i += kTreeThreads) {
+        int h = 0;
+        while (i >= lstart[h + 1]) h++;
+        // per-level choice indices of the path, from this level up
+        int ks[kMaxRows];
+        int j = i - lstart[h];
+        for (int l = h; l >= 0; l--) {
+            ks[l] = ltopk[l] > 0 ? j % ltopk[l] : 0;
+            j = ltopk[l] > 0 ? j / ltopk[l] : 0;
+        }
+        float s = p.prob[ks[0]];
+        for (int l = 1; l <= h; l++) s = __fmul_rn(s, p.prob[l * p.kmax + ks[l]]);
+        sc[i] = s;
+        dep[i] = h + 1;
+        tk[i] = p.tok[h * p.kmax + ks[h]];
+        par[i] = h == 0 ? -1 : lstart[h - 1] + (i - lstart[h]) / ltopk[h];
+    }
+    __syncthreads();
+    for (int i = t; i < C; i += kTreeThreads) {
+        const float si = sc[i];
+        const int di = dep[i];
+        int r = 0;
+        for (int j = 0; j < C; j++) {
+            const float sj = sc[j];
+            r += (sj > si || (sj == si && (dep[j] < di || (dep[j] == di && j < i)))) ? 1 : 0;
+        }
+        rk[i] = r;
+    }
+    __syncthreads();
+    const int keep = min(p.max_nodes - 1, C);
+    const int M = keep + 1;
+    if (t == 0) {
+        p.ntok[0] = *p.root;
+        p.npar[0] = -1;
+        p.ndep[0] = 0;
+        p.pos[0] = p.n;
+        spar[0] = -1;
+    }
+    for (int i = t; i < C; i += kTreeThreads) {
+        const int r = rk[i];
+        if (r < keep) {
+            const int node = r + 1;
+            const int pn = par[i] < 0 ? 0 : rk[par[i]] + 1;
+            p.ntok[node] = tk[i];
+            p.npar[node] = pn;
+            p.ndep[node] = dep[i];
+            p.pos[node] = p.n + dep[i];
+            spar[node] = pn;
+        }
+    }
+    __syncthreads();
+    for (int i = t; i < M; i += kTreeThreads) {
+        uint8_t* row = p.mask + (size_t)i * M;
+        for (int j = 0; j < M; j++) row[j] = 0;
+        for (int j = i, g = 0; j >= 0 && g <= kMaxRows; j = spar[j], g++) row[j] = 1;
+    }
+}
+
+// Accepted path of a verified tree; thread 0 walks, then the CTA copies the
+// last node's feature row.
+__global__ void medusa_walk_kernel(const MedusaWalkParams p) {
+    __shared__ int last_s;
+    if (threadIdx.x == 0) {
+        int cur = 0, a = 0;
+        p.path[0] = 0;
+        for (;;) {
+            int nxt = -1;
+            for (int c = 1; c < p.M; c++)
+                if (p.npar[c] == cur && p.ntok[c] == p.target[cur]) {
+                    nxt = c;
+                    break;
+                }
+            if (nxt < 0) break;
+            p.path[++a] = nxt;
+            p.rec[1 + a] = p.ntok[nxt];
+            cur = nxt;
+        }
+        p.rec[0] = a;
+        p.rec[1] = cur;
+        p.rec[2 + a] = p.target[cur];
+        *p.root = p.target[cur];
+        last_s = cur;
+    }
+    __syncthreads();
+    const float* src = p.x + (size_t)last_s * p.d;
+    for (int i = threadIdx.x; i < p.d; i += blockDim.x) p.f[i] = src[i];
 }
 
 }  // namespace
@@ -184,7 +303,25 @@ cudaError_t launch_topk_keys(const float* logits, int rows, int V, int ld, int v
 cudaError_t launch_kv_compact(const KvLayer* layers, int n_layers, const int* block_table, int kv_heads, int head_dim,
                               const int* base, const int* src, int a, cudaStream_t s) {
     if (a <= 0) return cudaSuccess;
-    kv_compact_kernel<<<n_layers, kNT, 0, s>>>(layers, block_table, kv_heads, head_dim, base, src, a);
+    kv_compact_kernel<<<n_layers, kNT, 0, s>>>(layers, block_table, kv_heads, head_dim, base, src, a, nullptr);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_kv_compact_dev(const KvLayer* layers, int n_layers, const int* block_table, int kv_heads,
+                                  int head_dim, const int* base, const int* src, const int* a_dev, cudaStream_t s) {
+    kv_compact_kernel<<<n_layers, kNT, 0, s>>>(layers, block_table, kv_heads, head_dim, base, src, 0, a_dev);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_medusa_tree(const MedusaTreeParams& p, cudaStream_t s) {
+    if (p.H < 1 || p.H > kMaxRows || p.kmax < 1 || p.max_nodes < 1 || p.max_nodes > 256) return cudaErrorInvalidValue;
+    medusa_tree_kernel<<<1, kTreeThreads, 0, s>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_medusa_walk(const MedusaWalkParams& p, cudaStream_t s) {
+    if (p.M < 1 || p.M > 256 || p.d < 1) return cudaErrorInvalidValue;
+    medusa_walk_kernel<<<1, kNT, 0, s>>>(p);
     return cudaGetLastError();
 }
 

@@ -369,3 +369,94 @@ FL_API int fl_cuda_block_dots_i8(const float* A, const dequantized_tensor_t* B, 
     FL_CHECK(fl_cuda_act_quant(A, q, M, K, 0, 0.0f, s));
     return run_gemv_chunks(q, B, nullptr, D, M, N, K, s, EPI_DOTS);
 }
+
+FL_API int fl_cuda_block_dots_w4(const float* A, const dequantized_tensor_t* B, int32_t* D, int M, int N, int K,
+                                 void* stream) {
+    if (!A || !D || M <= 0 || M > kMaxRows || N <= 0 || K <= 0 || K % 32 != 0)
+        return set_error(FL_E_INVAL, "block_dots_w4: bad arguments (M <= 8)");
+    cudaStream_t s = stream ? (cudaStream_t)stream : device_stream();
+    GemvParams p = {};
+    FL_CHECK(tensor_params(B, N, K, p));
+    const DevTensor* d = (const DevTensor*)B->dev;
+    if (d->scale_block != 32 || !w4_supported(N, K, d->P))
+        return set_error(FL_E_INVAL, "block_dots_w4: needs a tiled block-mode tensor (cols a multiple of 256)");
+    uint8_t* q = nullptr;
+    FL_CHECK(scratch_q((size_t)M * K, &q));
+    FL_CHECK(fl_cuda_act_quant(A, q, M, K, 0, 0.0f, s));
+    uint8_t* w4 = nullptr;
+    int* bad = nullptr;
+    int hbad = 0, rc = FL_OK;
+    cudaError_t ce = cudaMalloc(&w4, (size_t)N * K / 2);
+    if (ce == cudaSuccess) ce = cudaMalloc(&bad, sizeof(int));
+    if (ce == cudaSuccess) ce = cudaMemsetAsync(bad, 0, sizeof(int), s);
+    if (ce == cudaSuccess) ce = launch_pack_w4(d->w, w4, N, K, d->P, bad, s);
+    if (ce == cudaSuccess) {
+        p.aq = q;
+        p.w4 = w4;
+        p.dots = D;
+        p.row0 = 0;
+        p.M = M;
+        ce = launch_gemv_tma(p, EPI_DOTS, s, false);
+    }
+    if (ce == cudaSuccess) ce = cudaMemcpyAsync(&hbad, bad, sizeof(int), cudaMemcpyDeviceToHost, s);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(s);
+    if (ce != cudaSuccess) rc = cuda_error(ce, "block_dots_w4");
+    else if (hbad) rc = set_error(FL_E_INVAL, "block_dots_w4: a weight lies outside [-8, 7]");
+    cudaFree(w4);
+    cudaFree(bad);
+    return rc;
+}
+
+FL_API int fl_cuda_medusa_tree(const int* tok, const float* prob, const int* topk, int H, int kmax, int max_nodes,
+                               int root, int n, int* out_tok, int* out_parent, int* out_depth, int* out_pos,
+                               uint8_t* out_mask) {
+    if (!tok || !prob || !topk || !out_tok || !out_parent || !out_depth || !out_pos || !out_mask || H < 1 ||
+        H > kMaxRows || kmax < 1 || kmax > 32 || max_nodes < 1 || max_nodes > 256)
+        return set_error(FL_E_INVAL, "medusa_tree: bad arguments");
+    long long cand = 0, width = 1;
+    for (int h = 0; h < H; h++) {
+        if (topk[h] < 1 || topk[h] > kmax) return set_error(FL_E_INVAL, "medusa_tree: top-k must be 1..kmax");
+        width *= topk[h];
+        cand += width;
+        if (cand > kMaxTreeCand) return set_error(FL_E_INVAL, "medusa_tree: more than 1024 candidates");
+    }
+    const int M = 1 + std::min<int>(max_nodes - 1, (int)cand);
+    cudaStream_t s = device_stream();
+    int *dtok = nullptr, *dk = nullptr, *droot = nullptr, *dout = nullptr;
+    float* dprob = nullptr;
+    uint8_t* dmask = nullptr;
+    int rc = FL_OK;
+    auto cuda_ok = [&](cudaError_t e, const char* what) {
+        if (e != cudaSuccess && rc == FL_OK) rc = cuda_error(e, what);
+        return rc == FL_OK;
+    };
+    do {
+        if (!cuda_ok(cudaMalloc(&dtok, sizeof(int) * (size_t)H * kmax), "medusa_tree: alloc") ||
+            !cuda_ok(cudaMalloc(&dprob, sizeof(float) * (size_t)H * kmax), "medusa_tree: alloc") ||
+            !cuda_ok(cudaMalloc(&dk, sizeof(int) * H), "medusa_tree: alloc") ||
+            !cuda_ok(cudaMalloc(&droot, sizeof(int)), "medusa_tree: alloc") ||
+            !cuda_ok(cudaMalloc(&dout, sizeof(int) * 4 * (size_t)max_nodes), "medusa_tree: alloc") ||
+            !cuda_ok(cudaMalloc(&dmask, (size_t)M * M), "medusa_tree: alloc"))
+            break;
+        if (!cuda_ok(cudaMemcpyAsync(dtok, tok, sizeof(int) * (size_t)H * kmax, cudaMemcpyHostToDevice, s), "up") ||
+            !cuda_ok(cudaMemcpyAsync(dprob, prob, sizeof(float) * (size_t)H * kmax, cudaMemcpyHostToDevice, s), "up") ||
+            !cuda_ok(cudaMemcpyAsync(dk, topk, sizeof(int) * H, cudaMemcpyHostToDevice, s), "up") ||
+            !cuda_ok(cudaMemcpyAsync(droot, &root, sizeof(int), cudaMemcpyHostToDevice, s), "up"))
+            break;
+        MedusaTreeParams p = {dtok, dprob, dk, H, kmax, max_nodes, n, droot,
+                              dout, dout + max_nodes, dout + 2 * max_nodes, dout + 3 * max_nodes, dmask};
+        if (!cuda_ok(launch_medusa_tree(p, s), "medusa_tree: launch")) break;
+        int* outs[4] = {out_tok, out_parent, out_depth, out_pos};
+        for (int i = 0; i < 4; i++)
+            if (!cuda_ok(cudaMemcpyAsync(outs[i], dout + (size_t)i * max_nodes, sizeof(int) * M,
+                                         cudaMemcpyDeviceToHost, s), "medusa_tree: read"))
+                break;
+        if (rc != FL_OK) break;
+        if (!cuda_ok(cudaMemcpyAsync(out_mask, dmask, (size_t)M * M, cudaMemcpyDeviceToHost, s), "medusa_tree: read"))
+            break;
+        cuda_ok(cudaStreamSynchronize(s), "medusa_tree: sync");
+    } while (0);
+    void* bufs[] = {dtok, dprob, dk, droot, dout, dmask};
+    for (void* b : bufs) cudaFree(b);
+    return rc == FL_OK ? M : rc;
+}

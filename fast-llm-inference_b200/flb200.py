@@ -101,6 +101,9 @@ _SIGS = {
     "fl_cuda_device_count": (I, [C.POINTER(I)]),
     "fl_cuda_sync": (I, []),
     "fl_cuda_tp_wait_timeout_check": (I, []),
+    "fl_cuda_medusa_tree": (I, [VP, VP, VP, I, I, I, I, I, VP, VP, VP, VP, VP]),
+    "fl_cuda_block_dots_w4": (I, [VP, C.POINTER(DequantizedTensor), VP, I, I, I, VP]),
+    "fl_engine_set_weight_bits": (I, [VP, I]),
     "fl_argmax_key": (C.c_uint64, [C.c_float, I]),
     "fl_tp_merge_topw": (I, [VP, I, C.c_size_t, I, VP]),
     "fl_engine_draft_lm": (I, [VP, VP, I, I, I, VP]),
@@ -362,6 +365,10 @@ class Engine:
 
     def load_embedding(self, e):
         self.lib.check(self.lib.fl_engine_load_embedding(self.h, ptr(e)), "load_embedding")
+
+    def set_weight_bits(self, bits):
+        """4: the GEMV passes stream a packed 4-bit copy; 8: INT8 only."""
+        self.lib.check(self.lib.fl_engine_set_weight_bits(self.h, bits), "set_weight_bits")
 
     def synthesize(self, seed):
         self.lib.check(self.lib.fl_engine_synthesize(self.h, seed), "synthesize")

@@ -85,6 +85,28 @@ int fl_cuda_gemv_i8(const uint8_t* Aq, const dequantized_tensor_t* B, float* C,
 int fl_cuda_block_dots_i8(const float* A, const dequantized_tensor_t* B, int32_t* D,
                           int M, int N, int K, void* stream);
 
+/* fl_cuda_block_dots_i8 through the packed 4-bit GEMV (no counterpart in
+ * the reference): B must be an uploaded block-mode tensor (scale_block 32)
+ * whose weights lie in [-8, 7], in the tiled layout (cols a multiple of 256).
+ * The weights are packed on the device for this call; D[M, N, K/32] gets the
+ * int32 block dots, which must equal fl_cuda_block_dots_i8's. M <= 8. */
+int fl_cuda_block_dots_w4(const float* A, const dequantized_tensor_t* B, int32_t* D, int M, int N, int K,
+                          void* stream);
+
+/* The Medusa candidate tree of one step, built on the device by the kernel
+ * fl_engine_medusa_generate uses (host buffers in and out; no counterpart in
+ * the reference, whose medusa_build_tree is declared at medusa.h:126-131
+ * without code). tok / prob: [H][kmax] per-head top-k tokens and
+ * probabilities (the first topk[h] of row h are used); root: the root token;
+ * n: the slot and rotary position of the root. Writes M = 1 + min(max_nodes -
+ * 1, candidates) nodes: tok, parent (-1 for the root), depth, pos = n +
+ * depth, and mask[M][M] (1 where column j is row i or one of its ancestors).
+ * Candidates (sum over h of topk[0] * ... * topk[h]) must be at most 1024.
+ * Returns M, or a negative FL_E_* code. */
+int fl_cuda_medusa_tree(const int* tok, const float* prob, const int* topk, int H, int kmax, int max_nodes,
+                        int root, int n, int* out_tok, int* out_parent, int* out_depth, int* out_pos,
+                        uint8_t* out_mask);
+
 /* Failure detection, no counterpart in the reference: runs the
  * tensor-parallel reduction kernel on the library stream against the arrival
  * counters of a two-rank group that nobody increments. Its bounded wait gives
@@ -226,6 +248,19 @@ int fl_engine_dims(const fl_engine_t* e, int* out);
  * loader (gguf_loader.c:307-342), fused attn_qkv and Phi-3's gate+up ffn_up
  * split; norm weights are not applied (unit RMSNorm weights). */
 int fl_engine_load_gguf(fl_engine_t* e, int stack, const char* path);
+/* Weight format read by the engine's GEMV passes (up to 16 rows: the decode
+ * chain, its draft passes and the LM head), no counterpart in the reference.
+ * bits = 4: every loaded block-mode tensor is packed once more, on the
+ * device, two weights per byte (its values are Q4_0 nibbles minus 8, so the
+ * packing is lossless) and those passes stream the packed copy: about half
+ * the weight bytes per decode step; every int32 block dot is the same as
+ * with INT8 weights (the 4-bit dot is taken over q = w + 8 and 8 x the
+ * block's activation sum is subtracted). Passes of more than 16 rows (the
+ * tcgen05 GEMM) keep reading the INT8 copy. bits = 8 frees the packed copy.
+ * Needs every tensor loaded; drops the captured step and batch graphs (the
+ * next prefill records them again). FL_E_INVAL if a weight lies outside
+ * [-8, 7]. */
+int fl_engine_set_weight_bits(fl_engine_t* e, int bits);
 /* Generates and loads every tensor with fl_synth_* (std 0.02). */
 int fl_engine_synthesize(fl_engine_t* e, uint64_t seed);
 /* 1 when every tensor the configuration needs has been loaded. */

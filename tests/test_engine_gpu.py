@@ -207,6 +207,58 @@ def test_phi3_mini_full_size_spec(gpu, orc):
 MEDUSA_TOPK = [10, 5, 3, 2]
 
 
+def device_tree(lib, root, topk, tok, prob, max_nodes, n):
+    """fl_cuda_medusa_tree: (tokens, parents, depths, positions, mask)."""
+    tk = np.ascontiguousarray(topk, np.int32)
+    t = np.ascontiguousarray(tok, np.int32)
+    pr = np.ascontiguousarray(prob, np.float32)
+    outs = [np.full(max_nodes, -7, np.int32) for _ in range(4)]
+    mask = np.zeros(max_nodes * max_nodes, np.uint8)
+    M = lib.fl_cuda_medusa_tree(flb200.ptr(t), flb200.ptr(pr), flb200.ptr(tk), len(tk), t.shape[1], max_nodes, root,
+                                n, *[flb200.ptr(o) for o in outs], flb200.ptr(mask))
+    assert M > 0, lib.err()
+    return [o[:M] for o in outs] + [mask[:M * M].reshape(M, M)]
+
+
+@pytest.mark.parametrize("topk,max_nodes,ties", [([10, 5, 3, 2], 64, False), ([10, 5, 3, 2], 64, True),
+                                                 ([4, 4, 4, 4], 256, True), ([3, 2], 5, False),
+                                                 ([8, 8, 8], 200, False)])
+def test_device_tree_matches_oracle(gpu, topk, max_nodes, ties, orc):
+    """The device tree builder (the one medusa_generate runs every step)
+    against the oracle's, node for node: tokens, parents, depths, rotary
+    positions and the ancestor mask, with equal scores (ties broken by depth,
+    then generation order) when `ties`."""
+    import bind
+    rng = np.random.default_rng(sum(topk) + max_nodes)
+    kmax = max(topk)
+    tok = rng.integers(0, 32064, (len(topk), kmax)).astype(np.int32)
+    prob = np.sort(rng.random((len(topk), kmax)).astype(np.float32), axis=1)[:, ::-1].copy()
+    if ties:
+        prob = np.round(prob * 4) / 4  # many equal probabilities and products
+        prob[:, 0] = 1.0
+    t, par, dep, pos, mask = device_tree(gpu, 77, topk, tok, prob, max_nodes, 300)
+    wt, wpar, wdep, _ = bind.medusa_tree(orc, 77, topk, tok, prob, max_nodes)
+    assert np.array_equal(t, wt) and np.array_equal(par, wpar) and np.array_equal(dep, wdep)
+    assert np.array_equal(pos, 300 + wdep)
+    want = np.zeros_like(mask)
+    for i in range(len(wt)):
+        j = i
+        while j >= 0:
+            want[i, j] = 1
+            j = wpar[j]
+    assert np.array_equal(mask, want)
+
+
+def test_device_tree_rejects_too_many_candidates(gpu):
+    tok = np.zeros((3, 32), np.int32)
+    prob = np.ones((3, 32), np.float32)
+    t = np.zeros(64, np.int32)
+    m = np.zeros(64 * 64, np.uint8)
+    rc = gpu.fl_cuda_medusa_tree(flb200.ptr(tok), flb200.ptr(prob), flb200.ptr(np.array([32, 32, 2], np.int32)), 3,
+                                 32, 64, 0, 0, *[flb200.ptr(t)] * 4, flb200.ptr(m))
+    assert rc < 0
+
+
 def test_medusa_stream_matches_oracle(gpu, orc):
     """Medusa on the device (heads, top-k, tree, tree-masked verify, path
     acceptance, KV compaction) against the oracle; 16-token vocabulary so
