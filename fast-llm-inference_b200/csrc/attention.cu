@@ -462,7 +462,10 @@ __global__ void __launch_bounds__(kDThreads) attention_split_kernel(const AttnPa
 // order (deterministic), normalises and quantizes. No global scratch, no
 // arrival counter, no launch-size dependence on max_ctx. Same arithmetic as
 // inference.c:193-247 up to float rounding.
-constexpr int kCl = 8;         // CTAs per head (portable cluster size)
+#ifndef FL_ATTN_CL
+#define FL_ATTN_CL 8
+#endif
+constexpr int kCl = FL_ATTN_CL;  // CTAs per head (portable cluster size: at most 8)
 constexpr int kCTile = 32;     // keys per tile
 constexpr int kCThreads = 128;
 constexpr int kCRes = kMaxHd + 4;  // per row: max, sum, o[hd] (keeps the tile buffers 16-byte aligned)
