@@ -145,6 +145,20 @@ __device__ __forceinline__ void mma_u8u8(uint32_t a0, uint32_t a2, uint32_t b0, 
         : "r"(a0), "r"(0), "r"(a2), "r"(0), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 
+// D(16x8, s32) = A(16x32, s8, row: 16 weight rows) x B(32x8, u8, col: 8
+// activation rows): one instruction covers a 16-row tile for every row.
+__device__ __forceinline__ void mma_s8u8(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1, int& d0, int& d1, int& d2, int& d3) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+        : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+#ifndef FL_GEMV_SWAP
+#define FL_GEMV_SWAP 0
+#endif
+
 template <int MMAX, int EPI, bool MMA, bool W4>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const GemvParams p, const Geo geo,
                                                                          const int epi_rt) {
@@ -165,6 +179,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const Ge
     const int row0 = u0 * 8, row1 = u1 * 8;
     const int ntiles = (row1 - row0 + kStageRows - 1) / kStageRows;
     const int total = ntiles * npan;
+    constexpr bool kSwap = FL_GEMV_SWAP && !W4;  // INT8 tiles: weights as the MMA's A operand
     const size_t slot = slot_bytes(P, W4);
     const int wrb = row_bytes(P, W4);  // weight bytes of a stage row
     uint8_t* act = smem;
@@ -383,6 +398,17 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const Ge
                         }
                         continue;
                     }
+                } else if (kSwap) {
+                    // weights as A (rows g and g + 8), activations as B
+                    // (columns 2t, 2t + 1): d0, d1 = row g; d2, d3 = row g + 8
+                    mma_s8u8(b00, b10, b01, b11, a0, a2, d0, d1, d2, d3);
+                    const float sg = __half2float(ds[g * bpp + kb]);
+                    const float sg8 = __half2float(ds[(8 + g) * bpp + kb]);
+                    acc[0] = __fmaf_rn(i2f_exact(d0), sg, acc[0]);
+                    acc[1] = __fmaf_rn(i2f_exact(d1), sg, acc[1]);
+                    acc[2] = __fmaf_rn(i2f_exact(d2), sg8, acc[2]);
+                    acc[3] = __fmaf_rn(i2f_exact(d3), sg8, acc[3]);
+                    continue;
                 } else {
                     mma_u8s8(a0, a2, b00, b01, d0, d1);
                     mma_u8s8(a0, a2, b10, b11, d2, d3);
@@ -408,13 +434,19 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const Ge
                 if (tid < 64) {
                     const int pr = tid & 7, m = tid >> 3;  // row pair pr of the tile, activation row m
                     if (m < rows_m && 2 * pr < rows) {
-                        const int src_lane = 4 * m + (pr & 3);
-                        const int q0 = (pr >> 2) * 2;
+                        // (weight row n, activation row m) of the tile lives in lane
+                        // 4m + (n % 8) / 2, slot 2 (n / 8) + n % 2 (activations as A),
+                        // or in lane 4 (n % 8) + m / 2, slot 2 (n / 8) + m % 2 (weights as A)
+                        const int n0 = 2 * pr, n1 = 2 * pr + 1;
+                        const int l0 = kSwap ? 4 * (n0 & 7) + (m >> 1) : 4 * m + ((n0 & 7) >> 1);
+                        const int l1 = kSwap ? 4 * (n1 & 7) + (m >> 1) : 4 * m + ((n1 & 7) >> 1);
+                        const int q0 = kSwap ? 2 * (n0 >> 3) + (m & 1) : 2 * (n0 >> 3) + (n0 & 1);
+                        const int q1 = kSwap ? 2 * (n1 >> 3) + (m & 1) : 2 * (n1 >> 3) + (n1 & 1);
                         float y0 = 0.0f, y1 = 0.0f;
 #pragma unroll
                         for (int w = 0; w < kCWarps; w++) {
-                            y0 += red[buf][w][src_lane][q0];
-                            y1 += red[buf][w][src_lane][q0 + 1];
+                            y0 += red[buf][w][l0][q0];
+                            y1 += red[buf][w][l1][q1];
                         }
                         pair_epi_any<EPI>(epi, p, p.row0 + m, r + 2 * pr, 2 * pr + 1 < rows, __fdiv_rn(y0, 127.0f),
                                            __fdiv_rn(y1, 127.0f), best_s);

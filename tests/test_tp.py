@@ -38,8 +38,9 @@ def test_layout_rejects_bad_splits(lib):
 TP_GQA = dict(vocab=1024, d=512, ffn=1024, layers=2, heads=12, kv_heads=3, head_dim=64, theta=10000.0, eps=1e-5)
 
 
-def _rank(rank, size, uid, q):
+def _rank(rank, size, uid, q, fused="0"):
     import sys, os
+    os.environ["FL_TP_FUSED"] = fused
     sys.path[:0] = [os.path.dirname(__file__), os.path.join(os.path.dirname(__file__), "..", "fast-llm-inference_b200")]
     import flb200 as F
     from _model import engine_cfg, load_engine, make_weights, prompt
@@ -73,7 +74,11 @@ def _batch_prompts(prompt):
 
 
 @pytest.mark.gpu
-def test_two_rank_decode_matches_oracle(gpu, orc):
+@pytest.mark.parametrize("fused", ["0", "1"])
+def test_two_rank_decode_matches_oracle(gpu, orc, fused):
+    """Two tensor-parallel ranks (one process per GPU) against the oracle,
+    with the decode-sized all-reduces on NCCL (the default) or on the fused
+    NVLink push (FL_TP_FUSED=1)."""
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
@@ -83,7 +88,7 @@ def test_two_rank_decode_matches_oracle(gpu, orc):
     uid = flb200.tp_unique_id(gpu)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, 2, uid, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, uid, q, fused)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
