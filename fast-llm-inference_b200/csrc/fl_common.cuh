@@ -98,6 +98,30 @@ __device__ __forceinline__ float warp_max(float v) {
 // Exact float of an int with |v| < 2^22 using full-rate integer and float
 // adds (the int->float conversion instruction runs at a fraction of the FMA
 // rate): 0x4B400000 is 1.5 * 2^23, whose ulp is 1.
+// Two floats in one 64-bit register and the sm_100 packed f32x2 arithmetic:
+// each lane is rounded exactly like the scalar fma.rn / add.rn.
+__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
+    return ((unsigned long long)__float_as_uint(hi) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b,
+                                                     unsigned long long c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+// i2f_exact of two ints (|v| < 2^22) as a packed pair.
+__device__ __forceinline__ unsigned long long i2f2_exact(int lo, int hi) {
+    const unsigned long long b = ((unsigned long long)(uint32_t)(hi + 0x4B400000) << 32) | (uint32_t)(lo + 0x4B400000);
+    return f2_add(b, f2_pack(-12582912.0f, -12582912.0f));
+}
+__device__ __forceinline__ float f2_lo(unsigned long long v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float f2_hi(unsigned long long v) { return __uint_as_float((uint32_t)(v >> 32)); }
+
 __device__ __forceinline__ float i2f_exact(int v) {
     return __fsub_rn(__int_as_float(v + 0x4B400000), 12582912.0f);
 }

@@ -331,6 +331,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const Ge
         const int g = lane >> 2, t = lane & 3;
         const int kb0 = (warp * bpp) / kCWarps, kb1 = ((warp + 1) * bpp) / kCWarps;
         float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        unsigned long long acc01 = 0ull, acc23 = 0ull;  // weights as A: (row g, row g + 8) x (col 2t, 2t + 1)
         int buf = 0;
         // ldmatrix row address of this lane: matrix j = lane / 8, row q = lane % 8
         const int lj = lane >> 3, lq = lane & 7;
@@ -395,10 +396,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const Ge
                     mma_s8u8(b00, b10, b01, b11, a0, a2, d0, d1, d2, d3);
                     const float sg = __half2float(ds[g * bpp + kb]);
                     const float sg8 = __half2float(ds[(8 + g) * bpp + kb]);
-                    acc[0] = __fmaf_rn(i2f_exact(d0), sg, acc[0]);
-                    acc[1] = __fmaf_rn(i2f_exact(d1), sg, acc[1]);
-                    acc[2] = __fmaf_rn(i2f_exact(d2), sg8, acc[2]);
-                    acc[3] = __fmaf_rn(i2f_exact(d3), sg8, acc[3]);
+                    // the scalar fma(i2f_exact(d), s, acc) of each column, two at a time
+                    acc01 = f2_fma(i2f2_exact(d0, d1), f2_pack(sg, sg), acc01);
+                    acc23 = f2_fma(i2f2_exact(d2, d3), f2_pack(sg8, sg8), acc23);
                     continue;
                 }
                 const float s0 = __half2float(ds[(2 * t) * bpp + kb]);
@@ -415,6 +415,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const Ge
             if (pan == npan - 1) {
                 // reduce the warps' block slices of this 16-row tile, then epilogue
 #pragma unroll
+                if (kSwap) {
+                    acc[0] = f2_lo(acc01);
+                    acc[1] = f2_hi(acc01);
+                    acc[2] = f2_lo(acc23);
+                    acc[3] = f2_hi(acc23);
+                    acc01 = acc23 = 0ull;
+                }
                 for (int q = 0; q < 4; q++) red[buf][warp][lane][q] = acc[q];
                 acc[0] = acc[1] = acc[2] = acc[3] = 0.0f;
                 asm volatile("bar.sync 1, %0;" ::"n"(kCWarps * 32) : "memory");
