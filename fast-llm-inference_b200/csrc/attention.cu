@@ -468,6 +468,9 @@ __global__ void __launch_bounds__(kDThreads) attention_split_kernel(const AttnPa
 constexpr int kCl = FL_ATTN_CL;  // CTAs per head (portable cluster size: at most 8)
 constexpr int kCTile = 32;     // keys per tile
 constexpr int kCThreads = 128;
+// a tile's key is a lane, its rows w, w + 4 belong to warp w in both the
+// score and the softmax phase
+static_assert(kCTile == 32 && kCThreads == 128, "cluster attention: one key per lane, four warps");
 constexpr int kCRes = kMaxHd + 4;  // per row: max, sum, o[hd] (keeps the tile buffers 16-byte aligned)
 
 __device__ __forceinline__ void cp16(void* dst, const void* src) {
@@ -643,7 +646,9 @@ __global__ void __launch_bounds__(kCThreads) attention_cluster_kernel(const Attn
                 }
             }
         }
-        __syncthreads();
+        // the scores of rows w, w + 4 were written by warp w's lanes (key =
+        // lane), which are the ones that read them next
+        __syncwarp();
         // online softmax: warp w -> rows w, w + 4; lane -> key
         for (int rr = warp; rr < nr; rr += 4) {
             const float s = sc[rr * kCTile + lane];

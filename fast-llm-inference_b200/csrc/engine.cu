@@ -902,7 +902,7 @@ FL_API void fl_engine_destroy(fl_engine_t* e) {
     free_linear(e->lm);
     for (auto& m : e->medusa) free_linear(m);
     void* bufs[] = {e->embed, e->x, e->x2, e->xq, e->q, e->aq, e->hq, e->logits, e->amax, e->x_v, e->x_d,
-                    e->iota, e->tok, e->mask, e->st, e->st_snap, e->xd0_snap, e->seq, e->out, e->acc,
+                    e->iota, e->tok, e->mask, e->med_arena, e->st, e->st_snap, e->xd0_snap, e->seq, e->out, e->acc,
                     e->last_feat, e->attn_part, e->attn_cnt, e->step_bar, e->d_phases, e->d_trace,
                     e->samp_q, e->samp_p, e->samp_r, e->samp_trace, e->samp_snap, e->samp_m, e->samp_key,
                     e->tp_keys, e->tp_all, e->tp_best, e->tp_recv_ptrs, e->tp_cnt_ptrs, e->tp_seq, e->tp_arrived};
@@ -1818,19 +1818,14 @@ FL_API int fl_engine_medusa_generate(fl_engine_t* e, const int* prompt, int P, i
     const int M = 1 + std::min<int>(max_nodes - 1, (int)cand);  // tree nodes of every step
     const int d = e->d, V = e->V;
     cudaStream_t s = e->s;
-    // device work buffers for this call
+    // device work buffers: carved from the engine's Medusa arena (allocated
+    // once, grown only when a call needs more), so a call makes no cudaMalloc
+    // or cudaFree of its own
     float *mf = nullptr, *my = nullptr, *mz = nullptr, *mprob = nullptr;
     int *mk = nullptr, *mtt = nullptr, *mtok = nullptr, *mpos = nullptr, *mtarget = nullptr, *mpath = nullptr;
     int *mpar = nullptr, *mdep = nullptr, *mrec = nullptr, *mroot = nullptr;
     KvLayer* dkv = nullptr;
-    auto cleanup = [&]() {
-        void* bufs[] = {mf, my, mz, mprob, mk, mtt, mtok, mpos, mtarget, mpath, mpar, mdep, mrec, mroot, dkv};
-        for (void* p : bufs) cudaFree(p);
-    };
-    auto fail = [&](int rc) {
-        cleanup();
-        return rc;
-    };
+    auto fail = [&](int rc) { return rc; };
 #define FL_MED_CUDA(expr)                                                    \
     do {                                                                     \
         cudaError_t fl_e_ = (expr);                                          \
@@ -1841,21 +1836,31 @@ FL_API int fl_engine_medusa_generate(fl_engine_t* e, const int* prompt, int P, i
         int fl_r_ = (expr);               \
         if (fl_r_ != FL_OK) return fail(fl_r_); \
     } while (0)
-    FL_MED_CUDA(cudaMalloc(&mf, sizeof(float) * d));
-    FL_MED_CUDA(cudaMalloc(&my, sizeof(float) * (size_t)H * d));
-    FL_MED_CUDA(cudaMalloc(&mz, sizeof(float) * (size_t)H * d));
-    FL_MED_CUDA(cudaMalloc(&mprob, sizeof(float) * (size_t)H * kmax));
-    FL_MED_CUDA(cudaMalloc(&mk, sizeof(int) * H));
-    FL_MED_CUDA(cudaMalloc(&mtt, sizeof(int) * (size_t)H * kmax));
-    FL_MED_CUDA(cudaMalloc(&mtok, sizeof(int) * max_nodes));
-    FL_MED_CUDA(cudaMalloc(&mpos, sizeof(int) * max_nodes));
-    FL_MED_CUDA(cudaMalloc(&mtarget, sizeof(int) * max_nodes));
-    FL_MED_CUDA(cudaMalloc(&mpath, sizeof(int) * max_nodes));
-    FL_MED_CUDA(cudaMalloc(&mpar, sizeof(int) * max_nodes));
-    FL_MED_CUDA(cudaMalloc(&mdep, sizeof(int) * max_nodes));
-    FL_MED_CUDA(cudaMalloc(&mrec, sizeof(int) * (max_nodes + 2)));
-    FL_MED_CUDA(cudaMalloc(&mroot, sizeof(int)));
-    FL_MED_CUDA(cudaMalloc(&dkv, sizeof(KvLayer) * e->base.nl));
+    {
+        const size_t sizes[] = {sizeof(float) * d, sizeof(float) * (size_t)H * d, sizeof(float) * (size_t)H * d,
+                                sizeof(float) * (size_t)H * kmax, sizeof(int) * H, sizeof(int) * (size_t)H * kmax,
+                                sizeof(int) * max_nodes, sizeof(int) * max_nodes, sizeof(int) * max_nodes,
+                                sizeof(int) * max_nodes, sizeof(int) * max_nodes, sizeof(int) * max_nodes,
+                                sizeof(int) * (max_nodes + 2), sizeof(int), sizeof(KvLayer) * e->base.nl};
+        void** ptrs[] = {(void**)&mf, (void**)&my, (void**)&mz, (void**)&mprob, (void**)&mk, (void**)&mtt,
+                         (void**)&mtok, (void**)&mpos, (void**)&mtarget, (void**)&mpath, (void**)&mpar,
+                         (void**)&mdep, (void**)&mrec, (void**)&mroot, (void**)&dkv};
+        size_t total = 0;
+        for (size_t sz : sizes) total += (sz + 255) & ~(size_t)255;
+        if (e->med_arena_cap < total) {
+            FL_MED_CUDA(cudaStreamSynchronize(s));
+            cudaFree(e->med_arena);
+            e->med_arena = nullptr;
+            e->med_arena_cap = 0;
+            FL_MED_CUDA(cudaMalloc(&e->med_arena, total));
+            e->med_arena_cap = total;
+        }
+        size_t off = 0;
+        for (size_t i = 0; i < sizeof(sizes) / sizeof(sizes[0]); i++) {
+            *ptrs[i] = e->med_arena + off;
+            off += (sizes[i] + 255) & ~(size_t)255;
+        }
+    }
     FL_MED_CUDA(cudaMemcpyAsync(dkv, e->base.kv.data(), sizeof(KvLayer) * e->base.nl, cudaMemcpyHostToDevice, s));
     FL_MED_CUDA(cudaMemcpyAsync(mk, topk, sizeof(int) * H, cudaMemcpyHostToDevice, s));
     FL_MED(ensure_mask(e, max_nodes));
@@ -1912,7 +1917,6 @@ FL_API int fl_engine_medusa_generate(fl_engine_t* e, const int* prompt, int P, i
     if (steps_out) *steps_out = steps;
 #undef FL_MED_CUDA
 #undef FL_MED
-    cleanup();
     if (take_device_error() != 0) return set_error(FL_E_TIMEOUT, "medusa_generate: a bounded device wait gave up");
     return FL_OK;
 }

@@ -91,6 +91,10 @@ struct fl_engine {
     int* tok = nullptr;      // [R]
     uint8_t* mask = nullptr; // [R * R] bounded by kMaxRows^2 for tests
     int mask_cap = 0;
+    // work buffers of fl_engine_medusa_generate, kept across calls (grown
+    // when a call needs more, freed with the engine)
+    uint8_t* med_arena = nullptr;
+    size_t med_arena_cap = 0;
     // speculative state
     SpecState* st = nullptr;
     SpecState* st_snap = nullptr;
