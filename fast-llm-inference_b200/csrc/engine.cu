@@ -389,6 +389,25 @@ int ensure_mask(fl_engine* e, int M) {
     return FL_OK;
 }
 
+int carve_work(fl_engine* e, void** const* ptrs, const size_t* sizes, int n) {
+    size_t total = 0;
+    for (int i = 0; i < n; i++) total += (sizes[i] + 255) & ~(size_t)255;
+    if (e->work_arena_cap < total) {
+        FL_CHECK_CUDA(cudaStreamSynchronize(e->s));
+        cudaFree(e->work_arena);
+        e->work_arena = nullptr;
+        e->work_arena_cap = 0;
+        FL_CHECK_CUDA(cudaMalloc(&e->work_arena, total));
+        e->work_arena_cap = total;
+    }
+    size_t off = 0;
+    for (int i = 0; i < n; i++) {
+        *ptrs[i] = e->work_arena + off;
+        off += (sizes[i] + 255) & ~(size_t)255;
+    }
+    return FL_OK;
+}
+
 // Argmax keys of the last LM-head pass: the GEMV's per-CTA partials, or under
 // tensor parallelism the all-rank maximum (one key per row).
 const unsigned long long* amax_keys(const fl_engine* e) { return e->tp_size > 1 ? e->tp_best : e->amax; }
@@ -902,7 +921,7 @@ FL_API void fl_engine_destroy(fl_engine_t* e) {
     free_linear(e->lm);
     for (auto& m : e->medusa) free_linear(m);
     void* bufs[] = {e->embed, e->x, e->x2, e->xq, e->q, e->aq, e->hq, e->logits, e->amax, e->x_v, e->x_d,
-                    e->iota, e->tok, e->mask, e->med_arena, e->st, e->st_snap, e->xd0_snap, e->seq, e->out, e->acc,
+                    e->iota, e->tok, e->mask, e->work_arena, e->st, e->st_snap, e->xd0_snap, e->seq, e->out, e->acc,
                     e->last_feat, e->attn_part, e->attn_cnt, e->step_bar, e->d_phases, e->d_trace,
                     e->samp_q, e->samp_p, e->samp_r, e->samp_trace, e->samp_snap, e->samp_m, e->samp_key,
                     e->tp_keys, e->tp_all, e->tp_best, e->tp_recv_ptrs, e->tp_cnt_ptrs, e->tp_seq, e->tp_arrived};
@@ -1818,7 +1837,7 @@ FL_API int fl_engine_medusa_generate(fl_engine_t* e, const int* prompt, int P, i
     const int M = 1 + std::min<int>(max_nodes - 1, (int)cand);  // tree nodes of every step
     const int d = e->d, V = e->V;
     cudaStream_t s = e->s;
-    // device work buffers: carved from the engine's Medusa arena (allocated
+    // device work buffers: carved from the engine's work arena (allocated
     // once, grown only when a call needs more), so a call makes no cudaMalloc
     // or cudaFree of its own
     float *mf = nullptr, *my = nullptr, *mz = nullptr, *mprob = nullptr;
@@ -1845,21 +1864,7 @@ FL_API int fl_engine_medusa_generate(fl_engine_t* e, const int* prompt, int P, i
         void** ptrs[] = {(void**)&mf, (void**)&my, (void**)&mz, (void**)&mprob, (void**)&mk, (void**)&mtt,
                          (void**)&mtok, (void**)&mpos, (void**)&mtarget, (void**)&mpath, (void**)&mpar,
                          (void**)&mdep, (void**)&mrec, (void**)&mroot, (void**)&dkv};
-        size_t total = 0;
-        for (size_t sz : sizes) total += (sz + 255) & ~(size_t)255;
-        if (e->med_arena_cap < total) {
-            FL_MED_CUDA(cudaStreamSynchronize(s));
-            cudaFree(e->med_arena);
-            e->med_arena = nullptr;
-            e->med_arena_cap = 0;
-            FL_MED_CUDA(cudaMalloc(&e->med_arena, total));
-            e->med_arena_cap = total;
-        }
-        size_t off = 0;
-        for (size_t i = 0; i < sizeof(sizes) / sizeof(sizes[0]); i++) {
-            *ptrs[i] = e->med_arena + off;
-            off += (sizes[i] + 255) & ~(size_t)255;
-        }
+        FL_MED(carve_work(e, ptrs, sizes, (int)(sizeof(sizes) / sizeof(sizes[0]))));
     }
     FL_MED_CUDA(cudaMemcpyAsync(dkv, e->base.kv.data(), sizeof(KvLayer) * e->base.nl, cudaMemcpyHostToDevice, s));
     FL_MED_CUDA(cudaMemcpyAsync(mk, topk, sizeof(int) * H, cudaMemcpyHostToDevice, s));

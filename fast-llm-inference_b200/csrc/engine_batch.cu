@@ -639,10 +639,7 @@ FL_API int fl_engine_spec_tree_generate(fl_engine_t* e, const int* prompt, int P
     int *mtok = nullptr, *mpos = nullptr, *mtarget = nullptr, *mpath = nullptr, *mchain = nullptr, *mcat = nullptr;
     unsigned long long *mkeys = nullptr, *mall = nullptr;
     KvLayer* dkv = nullptr;
-    auto cleanup = [&]() {
-        void* bufs[] = {mtok, mpos, mtarget, mpath, mchain, mcat, mkeys, mall, dkv};
-        for (void* p : bufs) cudaFree(p);
-    };
+    auto cleanup = [&]() {};  // the work buffers belong to the engine's arena
     auto fail = [&](int rc) {
         cleanup();
         return rc;
@@ -657,15 +654,14 @@ FL_API int fl_engine_spec_tree_generate(fl_engine_t* e, const int* prompt, int P
         int fl_r_ = (expr);               \
         if (fl_r_ != FL_OK) return fail(fl_r_); \
     } while (0)
-    FL_ST_CUDA(cudaMalloc(&mtok, sizeof(int) * Mt));
-    FL_ST_CUDA(cudaMalloc(&mpos, sizeof(int) * Mt));
-    FL_ST_CUDA(cudaMalloc(&mtarget, sizeof(int) * Mt));
-    FL_ST_CUDA(cudaMalloc(&mpath, sizeof(int) * Mt));
-    FL_ST_CUDA(cudaMalloc(&mchain, sizeof(int) * kMaxRows));
-    FL_ST_CUDA(cudaMalloc(&mcat, sizeof(int) * Mt));
-    FL_ST_CUDA(cudaMalloc(&mkeys, sizeof(unsigned long long) * K * width));
-    FL_ST_CUDA(cudaMalloc(&mall, sizeof(unsigned long long) * K * width * G));
-    FL_ST_CUDA(cudaMalloc(&dkv, sizeof(KvLayer) * e->base.nl));
+    {
+        const size_t sizes[] = {sizeof(int) * Mt, sizeof(int) * Mt, sizeof(int) * Mt, sizeof(int) * Mt,
+                                sizeof(int) * kMaxRows, sizeof(int) * Mt, sizeof(unsigned long long) * K * width,
+                                sizeof(unsigned long long) * K * width * G, sizeof(KvLayer) * e->base.nl};
+        void** ptrs[] = {(void**)&mtok, (void**)&mpos, (void**)&mtarget, (void**)&mpath, (void**)&mchain,
+                         (void**)&mcat, (void**)&mkeys, (void**)&mall, (void**)&dkv};
+        FL_ST(carve_work(e, ptrs, sizes, 9));
+    }
     FL_ST_CUDA(cudaMemcpyAsync(dkv, e->base.kv.data(), sizeof(KvLayer) * e->base.nl, cudaMemcpyHostToDevice, s));
     FL_ST(ensure_mask(e, Mt));
 
@@ -788,10 +784,7 @@ FL_API int fl_engine_batch_tree_generate(fl_engine_t* e, const int* prompts, int
     int *mtok = nullptr, *mvst = nullptr, *mdst = nullptr, *mcst = nullptr, *mtarget = nullptr, *mchain = nullptr,
         *mpath = nullptr, *mbase = nullptr, *mcat = nullptr;
     KvLayer* dkv = nullptr;
-    auto cleanup = [&]() {
-        void* bufs[] = {lg, am, mkeys, mall, mtok, mvst, mdst, mcst, mtarget, mchain, mpath, mbase, mcat, dkv};
-        for (void* p : bufs) cudaFree(p);
-    };
+    auto cleanup = [&]() {};  // the work buffers belong to the engine's arena
     auto fail = [&](int rc) {
         cleanup();
         return rc;
@@ -807,20 +800,19 @@ FL_API int fl_engine_batch_tree_generate(fl_engine_t* e, const int* prompts, int
         if (fl_r_ != FL_OK) return fail(fl_r_); \
     } while (0)
     const int nlb = e->base.nl;
-    FL_BT_CUDA(cudaMalloc(&lg, sizeof(float) * (size_t)rows * V));
-    FL_BT_CUDA(cudaMalloc(&am, sizeof(unsigned long long) * (size_t)rows * npart));
-    FL_BT_CUDA(cudaMalloc(&mkeys, sizeof(unsigned long long) * (size_t)nseq * cw));
-    FL_BT_CUDA(cudaMalloc(&mall, sizeof(unsigned long long) * (size_t)nseq * cw * G));
-    FL_BT_CUDA(cudaMalloc(&mtok, sizeof(int) * rows));
-    FL_BT_CUDA(cudaMalloc(&mvst, sizeof(int) * (size_t)nseq * (Mt + 1)));
-    FL_BT_CUDA(cudaMalloc(&mdst, sizeof(int) * (size_t)K * nseq * 2));
-    FL_BT_CUDA(cudaMalloc(&mcst, sizeof(int) * (size_t)nseq * (K + 2)));
-    FL_BT_CUDA(cudaMalloc(&mtarget, sizeof(int) * rows));
-    FL_BT_CUDA(cudaMalloc(&mchain, sizeof(int) * (size_t)K * nseq));
-    FL_BT_CUDA(cudaMalloc(&mpath, sizeof(int) * rows));
-    FL_BT_CUDA(cudaMalloc(&mbase, sizeof(int) * nseq));
-    FL_BT_CUDA(cudaMalloc(&mcat, sizeof(int) * (size_t)nseq * (K + 1)));
-    FL_BT_CUDA(cudaMalloc(&dkv, sizeof(KvLayer) * (size_t)nseq * nlb));
+    {
+        const size_t sizes[] = {sizeof(float) * (size_t)rows * V, sizeof(unsigned long long) * (size_t)rows * npart,
+                                sizeof(unsigned long long) * (size_t)nseq * cw,
+                                sizeof(unsigned long long) * (size_t)nseq * cw * G, sizeof(int) * rows,
+                                sizeof(int) * (size_t)nseq * (Mt + 1), sizeof(int) * (size_t)K * nseq * 2,
+                                sizeof(int) * (size_t)nseq * (K + 2), sizeof(int) * rows, sizeof(int) * (size_t)K * nseq,
+                                sizeof(int) * rows, sizeof(int) * nseq, sizeof(int) * (size_t)nseq * (K + 1),
+                                sizeof(KvLayer) * (size_t)nseq * nlb};
+        void** ptrs[] = {(void**)&lg, (void**)&am, (void**)&mkeys, (void**)&mall, (void**)&mtok, (void**)&mvst,
+                         (void**)&mdst, (void**)&mcst, (void**)&mtarget, (void**)&mchain, (void**)&mpath,
+                         (void**)&mbase, (void**)&mcat, (void**)&dkv};
+        FL_BT(carve_work(e, ptrs, sizes, 14));
+    }
     // each sequence's base KV region as its own cache (compaction)
     const size_t region = (size_t)(B.slots / kPageSize) * e->Hkv * kPageSize * e->hd;
     std::vector<KvLayer> hkv((size_t)nseq * nlb);

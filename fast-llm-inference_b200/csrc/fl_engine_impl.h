@@ -91,10 +91,11 @@ struct fl_engine {
     int* tok = nullptr;      // [R]
     uint8_t* mask = nullptr; // [R * R] bounded by kMaxRows^2 for tests
     int mask_cap = 0;
-    // work buffers of fl_engine_medusa_generate, kept across calls (grown
-    // when a call needs more, freed with the engine)
-    uint8_t* med_arena = nullptr;
-    size_t med_arena_cap = 0;
+    // per-call work buffers of the Medusa and draft-tree loops, carved from
+    // one arena kept across calls (grown when a call needs more, freed with
+    // the engine; carve_work)
+    uint8_t* work_arena = nullptr;
+    size_t work_arena_cap = 0;
     // speculative state
     SpecState* st = nullptr;
     SpecState* st_snap = nullptr;
@@ -197,6 +198,10 @@ struct fl_engine {
 namespace fl_eng {
 
 int check_ready(fl_engine* e, bool need_draft);
+// Points ptrs[i] at sizes[i] bytes (256-byte aligned) of the engine's work
+// arena, growing it after a stream synchronisation when the call needs more.
+// One user at a time: the buffers stay valid until the next carve_work.
+int carve_work(fl_engine* e, void** const* ptrs, const size_t* sizes, int n);
 // Runs M rows through a stack (the layer chain of engine.cu); view: the KV
 // regions of an in-GPU batch, or of one sequence of it.
 int run_stack(fl_engine* e, Stack& S, float* x, int M, const int* dyn_M, const int* slot_base, const int* pos,
