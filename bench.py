@@ -530,7 +530,7 @@ def run_medusa(a):
     ms = e0.elapsed_time(e1)
     acc_cat = np.concatenate(accs)
     step_us = sum(dec_us) / max(1, len(acc_cat))
-    tree_bytes = medusa_step_bytes(nodes + 1, 4, a.prompt_len + a.new_tokens // 2)
+    tree_bytes = medusa_step_bytes(nodes, 4, a.prompt_len + a.new_tokens // 2)  # the root is one of the nodes
     tree_gbs = tree_bytes / (step_us * 1e-6) / 1e9
     peak, peak_kind = measured_peaks()
     line = {
@@ -544,7 +544,7 @@ def run_medusa(a):
                    "step_us": step_us, "decode_tok_s": (a.new_tokens - 1) * len(dec_us) / (sum(dec_us) * 1e-6)},
         "roofline": {"bound": "hbm", "achieved": tree_gbs, "peak": peak, "unit": "GB/s", "frac": tree_gbs / peak,
                      "traffic": None, "peak_kind": peak_kind,
-                     "kernel": f"whole tree step ({nodes + 1} verify rows: tcgen05 GEMM, LM head in 8-row GEMVs)",
+                     "kernel": f"whole tree step ({nodes} verify rows: tcgen05 GEMM, LM head in 8-row GEMVs)",
                      "bytes_per_step": tree_bytes},
         "clocks": clk,
     }
