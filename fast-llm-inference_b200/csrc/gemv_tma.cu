@@ -337,6 +337,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const Ge
         const int lj = lane >> 3, lq = lane & 7;
         const int lrow = lq + 8 * (lj >> 1);
         const bool arow = g < rows_m;
+        // byte offsets of this lane's ldmatrix row chunk for the four blocks of
+        // a 128-byte swizzle group (chunk 2j + (lj & 1), rows at r + lrow with
+        // r a multiple of 16)
+        uint32_t goff[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) goff[j] = (uint32_t)(((2 * j + (lj & 1)) ^ (lrow & 7)) << 4);
         for (int i = 0; i < total; i++) {
             const int sl = i % S;
             const int tile = i / npan, pan = i - tile * npan;
@@ -347,6 +353,38 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const Ge
             const __half* ds = reinterpret_cast<const __half*>(dw + (size_t)kStageRows * wrb);
             const uint32_t wrow = smem_u32(dw + (size_t)lrow * P);
             const uint8_t* arow_p = act + (size_t)g * ald + (size_t)pan * P;
+            if (kSwap && (bpp & 31) == 0) {
+                // Panels of a multiple of 1024 weights: every warp's block range
+                // is whole groups of four blocks, i.e. whole 128-byte swizzle
+                // groups; the four chunk offsets of a group are fixed per lane
+                // (tile rows start at multiples of 16, so row & 7 = lane's row
+                // & 7) and the fp16 scales of a group are one 8-byte load per
+                // weight row. Same blocks in the same order as the loop below.
+                for (int kg = kb0; kg < (bad ? kb0 : kb1); kg += 4) {
+                    const uint32_t gbase = wrow + (uint32_t)((kg >> 2) << 7);
+                    const uint2 sgv = *reinterpret_cast<const uint2*>(ds + g * bpp + kg);
+                    const uint2 sg8v = *reinterpret_cast<const uint2*>(ds + (8 + g) * bpp + kg);
+                    const uint32_t sgw[4] = {sgv.x, sgv.x >> 16, sgv.y, sgv.y >> 16};
+                    const uint32_t sg8w[4] = {sg8v.x, sg8v.x >> 16, sg8v.y, sg8v.y >> 16};
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const int kb = kg + j;
+                        uint32_t b00, b01, b10, b11;
+                        ldmatrix_x4(gbase + goff[j], b00, b01, b10, b11);
+                        uint32_t a0 = 0, a2 = 0;
+                        if (arow) {
+                            a0 = *reinterpret_cast<const uint32_t*>(arow_p + kb * 32 + 4 * t);
+                            a2 = *reinterpret_cast<const uint32_t*>(arow_p + kb * 32 + 16 + 4 * t);
+                        }
+                        int d0, d1, d2, d3;
+                        mma_s8u8(b00, b10, b01, b11, a0, a2, d0, d1, d2, d3);
+                        const float sg = __half2float(__ushort_as_half((unsigned short)(sgw[j] & 0xFFFFu)));
+                        const float sg8 = __half2float(__ushort_as_half((unsigned short)(sg8w[j] & 0xFFFFu)));
+                        acc01 = f2_fma(i2f2_exact(d0, d1), f2_pack(sg, sg), acc01);
+                        acc23 = f2_fma(i2f2_exact(d2, d3), f2_pack(sg8, sg8), acc23);
+                    }
+                }
+            } else
             for (int kb = kb0; kb < (bad ? kb0 : kb1); kb++) {
                 uint32_t b00, b01, b10, b11;
                 if (W4) {
@@ -414,7 +452,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const Ge
             if (lane == 0) mbar_arrive(&empty_bar[sl]);
             if (pan == npan - 1) {
                 // reduce the warps' block slices of this 16-row tile, then epilogue
-#pragma unroll
                 if (kSwap) {
                     acc[0] = f2_lo(acc01);
                     acc[1] = f2_hi(acc01);
@@ -422,6 +459,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const Ge
                     acc[3] = f2_hi(acc23);
                     acc01 = acc23 = 0ull;
                 }
+#pragma unroll
                 for (int q = 0; q < 4; q++) red[buf][warp][lane][q] = acc[q];
                 acc[0] = acc[1] = acc[2] = acc[3] = 0.0f;
                 asm volatile("bar.sync 1, %0;" ::"n"(kCWarps * 32) : "memory");
