@@ -36,13 +36,16 @@ constexpr int kThreads = (kCWarps + 1) * 32; // + producer warp
 constexpr int kStageRows = 16;
 constexpr int kMaxStages = 8;
 #ifndef FL_TMA_SMEM_KB
-#define FL_TMA_SMEM_KB 216
+#define FL_TMA_SMEM_KB 208
 #endif
 #ifndef FL_TMA_CTAS_PER_SM
 #define FL_TMA_CTAS_PER_SM 1
 #endif
-// Dynamic shared memory budget per CTA: 227 KB per block minus the static
-// reduction buffers and barriers (~8.5 KB) when one CTA owns the SM.
+// Dynamic shared memory budget per CTA (activation rows + ring), with the
+// static reduction buffers and barriers (~8.7 KB) on top. 208 KB keeps every
+// launch at or below 216 KB in all, which leaves a profiler room to run the
+// kernel (the one-row down projection, 221 KB at a 216 KB budget, failed to
+// launch under ncu); the decode step measured the same at 208 and 216 KB.
 constexpr int kSmemLimit = FL_TMA_SMEM_KB * 1024;
 constexpr int kCtasPerSm = FL_TMA_CTAS_PER_SM;
 
