@@ -727,7 +727,9 @@ __global__ void __launch_bounds__(kCThreads) attention_cluster_kernel(const Attn
                 }
             }
         }
-        __syncthreads();  // this tile's buffers and scores are free again
+        // this tile's buffers and scores are free again before the next tile;
+        // after the last one the partials go to `res`, which nothing here reads
+        if (t + 1 < ntiles) __syncthreads();
     }
     // this CTA's partial result
     if (pv) {
