@@ -29,10 +29,10 @@
 //  - warps 2 ..: readout, BN / 16 per TMEM lane quadrant, each with 16
 //    columns of its quadrant's 32 lanes (one 32x32b.x16 load per block: 3-8 %
 //    faster than 8-column warps, while 32-column warps are slower). Per half
-//    stage (two blocks) it loads the s32 dots, releases a stage's TMEM buffer
-//    once both halves are in registers and, while the next half's load is in
-//    flight, turns each dot into the float 12582912 + dot by an integer add
-//    of 0x4B400000 (exact: |dot| < 2^22).
+//    stage (two blocks) it loads the s32 dots, writes its columns of a
+//    stage's TMEM buffer back to 0x4B400000 and releases the buffer once both
+//    halves are in registers; the MMAs accumulate onto that value, so each
+//    loaded word is already the float 12582912 + dot (exact: |dot| < 2^22).
 //    One fma with d and -12582912 d (exact) then yields exactly the rounded
 //    product (float)dot * d, which is added to the row's running sum in block
 //    order: the sum is bit-identical to the sequential reference order. Pairs
@@ -78,6 +78,13 @@ constexpr unsigned long long kWaitNsG = 2000000000ull;
 constexpr uint32_t kSuspendNs = 1000000;  // try_wait suspend-time hint (a bound; completion wakes earlier)
 #endif
 constexpr uint32_t kMagicBits = 0x4B400000u;  // 12582912.0f
+// FL_GEMM_BIAS: the readout writes the bias 0x4B400000 back into a TMEM stage
+// buffer before releasing it and the MMAs accumulate onto it, so the dots
+// leave TMEM already as the bits of 12582912 + dot (no integer add per value).
+// 1-6 % less time per launch at 64 and 448 rows (B200), same results.
+#ifndef FL_GEMM_BIAS
+#define FL_GEMM_BIAS 1
+#endif
 constexpr float kMagic = 12582912.0f;
 
 __device__ __forceinline__ uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -162,7 +169,7 @@ __device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t da, uint64_t d
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(da), "l"(db), "r"(idesc), "r"(0)
+        "l"(da), "l"(db), "r"(idesc), "r"(FL_GEMM_BIAS ? 1 : 0)
         : "memory");
 }
 __device__ __forceinline__ void umma_commit(uint64_t* b) {
@@ -315,7 +322,8 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
                     break;
                 }
                 const int t = kg % NB;
-                if (kg >= NB && !mb_wait(&tempty[t], ((kg / NB) - 1) & 1)) {
+                // with the bias, phase 0 of every buffer is the readout's initial fill
+                if ((FL_GEMM_BIAS || kg >= NB) && !mb_wait(&tempty[t], ((kg / NB) - (FL_GEMM_BIAS ? 0 : 1)) & 1)) {
                     atomicOr(&bad_s, 1);
                     break;
                 }
@@ -363,8 +371,29 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
             const unsigned long long n2 = pk2(__float_as_uint(nmd), __float_as_uint(nmd));
 #pragma unroll
             for (int c = 0; c < kCols / 2; c++)
-                acc2[c] = add2(acc2[c], fma2(pk2(v[2 * c] + kMagicBits, v[2 * c + 1] + kMagicBits), d2, n2));
+                acc2[c] = add2(acc2[c], FL_GEMM_BIAS ? fma2(pk2(v[2 * c], v[2 * c + 1]), d2, n2)
+                                                     : fma2(pk2(v[2 * c] + kMagicBits, v[2 * c + 1] + kMagicBits), d2, n2));
         };
+#if FL_GEMM_BIAS
+        // this warp's columns of a stage buffer back to the bias (four
+        // columns per store keep the register footprint small)
+        auto fill = [&](int buf) {
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+#pragma unroll
+                for (int c = 0; c < kCols; c += 4)
+                    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %1, %1, %1};" ::"r"(
+                                     tq + (uint32_t)(buf * 4 * BN + j * BN + c)),
+                                 "r"(kMagicBits)
+                                 : "memory");
+        };
+        for (int b = 0; b < NB; b++) fill(b);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0)
+            for (int b = 0; b < NB; b++) mb_arrive(&tempty[b]);
+#endif
         const int nh = 2 * nkg;
         // one half stage: start the next half's load (waiting for its stage's
         // MMAs when it opens a stage), free a stage's TMEM buffer once both its
@@ -380,6 +409,10 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
                 ld_half(h + 1, nxt);
             }
             if (h & 1) {
+#if FL_GEMM_BIAS
+                fill((g0 + (h >> 1)) % NB);
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+#endif
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mb_arrive(&tempty[(g0 + (h >> 1)) % NB]);
