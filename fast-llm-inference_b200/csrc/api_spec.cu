@@ -81,6 +81,15 @@ uint64_t synth_seed(const void* m) {
     return it == g_seed.end() ? 0 : it->second;
 }
 
+// True (with the seed) when the model's weights came from "synthetic:<seed>".
+bool synth_seed_of(const void* m, uint64_t* seed) {
+    std::lock_guard<std::mutex> lk(g_bind_mu);
+    auto it = g_seed.find(m);
+    if (it == g_seed.end()) return false;
+    *seed = it->second;
+    return true;
+}
+
 // Head size of a draft / Medusa model given only its hidden size: 96 when it
 // divides (the Phi-3 shapes), else 128, else 64.
 int head_dim_for(int d) { return d % 96 == 0 ? 96 : d % 128 == 0 ? 128 : d % 64 == 0 ? 64 : 0; }
@@ -112,16 +121,37 @@ int synth_tensor(dequantized_tensor_t* t, uint64_t seed, uint32_t id, int rows, 
     return fl_synth_q4_0_i8(seed, id, rows, cols, 0.02f, t->weights, t->scales_f16);
 }
 
-// Pushes a draft model's host tensors into the engine's draft stack.
+// Pushes a draft model's host tensors into the engine's draft stack. The
+// draft's layers share the engine's head layout, so a synthetic draft
+// (whose host q/k/v/o tensors have the speculative.h shapes [d, d]) bound
+// to an engine with grouped-query heads or q_dim != d gets those four
+// projections generated again from the same seed and tensor ids at the
+// engine's shapes: q [q_dim, d], k and v [kv_dim, d], o [d, q_dim]. Loaded
+// (GGUF or caller-filled) tensors go in as they are, and a shape the engine
+// does not take is an error from fl_engine_load_linear.
 int load_draft_into(fl_engine_t* e, const draft_model_t* dm) {
     const dequantized_tensor_t* arrs[7] = {dm->w_q_proj, dm->w_k_proj, dm->w_v_proj, dm->w_o_proj,
                                            dm->w_gate, dm->w_up, dm->w_down};
+    int dims[4];
+    FL_CHECK(fl_engine_dims(e, dims));
+    const int want[4][2] = {{dims[1], dims[0]}, {dims[2], dims[0]}, {dims[2], dims[0]}, {dims[0], dims[1]}};
+    uint64_t seed = 0;
+    const bool synth = synth_seed_of(dm, &seed);
     for (int l = 0; l < dm->num_layers; l++)
         for (int p = 0; p < 7; p++) {
             const dequantized_tensor_t* t = arrs[p] ? &arrs[p][l] : nullptr;
             if (!t || !t->weights) continue;  // keep what the engine holds
             if (t->scale_block != 32 || !t->scales_f16)
                 return set_error(FL_E_UNSUPPORTED, "draft tensors must be in block mode (scale_block 32)");
+            if (synth && p < 4 && (t->rows != want[p][0] || t->cols != want[p][1])) {
+                dequantized_tensor_t r = {};
+                int rc = synth_tensor(&r, seed, FL_TENSOR_ID(1, l, p), want[p][0], want[p][1]);
+                if (rc == FL_OK) rc = fl_engine_load_linear(e, 1, l, p, r.weights, r.scales_f16, r.rows, r.cols);
+                free(r.weights);
+                free(r.scales_f16);
+                FL_CHECK(rc);
+                continue;
+            }
             FL_CHECK(fl_engine_load_linear(e, 1, l, p, t->weights, t->scales_f16, t->rows, t->cols));
         }
     const dequantized_tensor_t* lm = dm->w_lm_head;

@@ -163,12 +163,14 @@ def test_max_accepted_cap(small):
     assert_stream_matches(got, want, margins)
 
 
-def test_speculative_generate_reference_api(gpu, orc):
+@pytest.mark.parametrize("dims", [SMALL, SMALL_GQA], ids=["mha", "gqa"])
+def test_speculative_generate_reference_api(gpu, orc, dims):
     """speculative_generate() through the reference signature: draft_model_t
     loaded with draft_model_load("synthetic:SEED"), target = the engine,
-    prompt ids passed as floats."""
+    prompt ids passed as floats. With grouped-query heads the synthetic
+    draft's host k/v tensors are [d, d] while the engine's draft layers take
+    [kv_dim, d]: binding generates them again at the engine's shapes."""
     import ctypes as C
-    dims = SMALL
     seed = 31
     w, embed = make_weights(gpu, dims, seed=seed)
     eng = flb200.Engine(gpu, engine_cfg(dims, draft_layers=1))
