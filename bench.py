@@ -15,6 +15,7 @@ needed between timed iterations.
     python bench.py --workload sampled-batch [--seqs 64 --prompt-len 1024 --new-tokens 512 --k 6]
     torchrun --nproc-per-node N bench.py --gpus N --workload tp-medium [--prompt-len 512] [--batch 4] [--tree 8]
     python bench.py --workload medusa [--prompt-len 512 --new-tokens 256]
+    python bench.py --workload step-breakdown [--steps 3 --warmup 1]
 
 One process per GPU (torchrun for N > 1); this path does not shard (batch 1),
 so N GPUs run N independent replicas and `value` sums their tokens/s.
@@ -472,6 +473,56 @@ def run_tp_medium(a):
     return 0
 
 
+def run_step_breakdown(a):
+    """Where the config-0 speculative step goes, from whole-step device times
+    of engines that differ only in layer counts and k (every launch of each
+    step runs; nothing is skipped): the Phi-3-mini widths with (base, draft,
+    k) = (32, 4, 4), (16, 4, 4), (32, 2, 4), (32, 4, 2), 128-token prompt,
+    128 new tokens, zero acceptance on random weights. A verify layer is the
+    difference of the first two over 16 layers; a draft layer's cost per step
+    (its catch-up pass and k - 1 chain passes) the difference of the first
+    and third over 2; the rest (LM heads, picks, control kernels) what
+    remains of the full step. One JSON line."""
+    import torch
+    import flb200
+    lib = flb200.Lib()
+    lib.check(lib.fl_cuda_init(0), "init")
+    prompt = np.random.default_rng(PROMPT_SEED).integers(0, DIMS["vocab"], 128).astype(np.int32)
+    cases = [(32, 4, 4), (16, 4, 4), (32, 2, 4), (32, 4, 2)]
+    us = {}
+    for L, D, k in cases:
+        cfg = engine_cfg(512)
+        cfg["num_layers"], cfg["draft_layers"] = L, D
+        eng = flb200.Engine(lib, cfg, 0)
+        eng.synthesize(SEED)
+        stream = torch.cuda.ExternalStream(eng.stream())
+        times = []
+        for r in range(max(a.warmup, 1) + a.steps):
+            eng.spec_prefill(prompt, k)
+            torch.cuda.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            toks, acc = eng.spec_decode(128)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            if r >= max(a.warmup, 1):
+                times.append(e0.elapsed_time(e1) * 1e3 / len(acc))
+        us[(L, D, k)] = statistics.median(times)
+        eng.close()
+    full = us[(32, 4, 4)]
+    verify_layer = (full - us[(16, 4, 4)]) / 16
+    draft_layer = (full - us[(32, 2, 4)]) / 2
+    line = {"workload": "step-breakdown: phi3-mini widths, 128-token prompt, 128 new tokens, zero acceptance",
+            "step_us": {f"L{L}_D{D}_k{k}": v for (L, D, k), v in us.items()},
+            "verify_layer_us": verify_layer, "verify_layers_us": 32 * verify_layer,
+            "draft_layer_per_step_us": draft_layer, "draft_layer_pass_us": draft_layer / 4,
+            "draft_us": 4 * draft_layer, "rest_us": full - 32 * verify_layer - 4 * draft_layer,
+            "k4_minus_k2_us": full - us[(32, 4, 2)]}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_profile_step(a):
     """A small case of the config-0 decode for ncu captures: the full widths
     (d 3072, 32 heads of 96, ffn 8192, vocab 32064) with 4 base and 2 draft
@@ -698,7 +749,7 @@ def main():
     ap.add_argument("--m", type=int, default=5, help="activation rows for --microbench")
     ap.add_argument("--iters", type=int, default=10, help="sweeps for --microbench")
     ap.add_argument("--workload", default="spec-bs1",
-                    choices=["spec-bs1", "sampled-batch", "tp-medium", "medusa", "profile-step"])
+                    choices=["spec-bs1", "sampled-batch", "tp-medium", "medusa", "profile-step", "step-breakdown"])
     ap.add_argument("--seqs", type=int, default=64, help="sequences of --workload sampled-batch")
     ap.add_argument("--batch", type=int, default=1, help="sequences decoded together by --workload tp-medium")
     ap.add_argument("--tree", type=int, default=0, help="draft-tree width for --workload tp-medium (0: chain)")
@@ -714,6 +765,8 @@ def main():
         return run_medusa(a)
     if a.workload == "profile-step":
         return run_profile_step(a)
+    if a.workload == "step-breakdown":
+        return run_step_breakdown(a)
     a.warmup = max(a.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

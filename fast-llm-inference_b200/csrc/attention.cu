@@ -582,13 +582,15 @@ __global__ void __launch_bounds__(kCThreads) attention_cluster_kernel(const Attn
         if (pre) cp_wait<0>();
         return;
     }
-    const int M = p.dyn_M ? *p.dyn_M : p.M;
+    // Read again through L2: the values read before the wait may sit in L1
+    // from before the launch that wrote them finished.
+    const int M = p.dyn_M ? __ldcg(p.dyn_M) : p.M;
     const int nr = min(M, MR);
     if (nr <= 0) {
         if (pre) cp_wait<0>();
         return;
     }
-    const int base = p.slot_base[sb * p.seq_state];
+    const int base = __ldcg(p.slot_base + sb * p.seq_state);
     const size_t qrow0 = (size_t)sb * M;
     const int ctx = base + M;
     int k0, k1;
