@@ -2,7 +2,10 @@
 // picks, verify-row preparation and acceptance (sm_100a). They move a few KB
 // and exist so that a whole draft + verify step runs on the device without a
 // host round trip.
+#include <algorithm>
+
 #include "fl_common.cuh"
+#include "fl_epilogue.cuh"
 #include "fl_state.h"
 
 namespace fl {
@@ -227,6 +230,25 @@ cudaError_t launch_embed_rows(const float* embed, int vocab, const int* tok, con
                               const int* done, cudaStream_t s, bool pdl) {
     return launch_pdl(embed_rows_kernel, dim3(rows_static), kT, s, pdl, embed, vocab, tok, feat, shift, x,
                       d, rows_static, dyn_rows, done);
+}
+
+__global__ void rope_table_kernel(float2* tab, int rows, int head_dim, float theta) {
+    const int h2 = head_dim >> 1;
+    const size_t n = (size_t)rows * h2;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int pos = (int)(i / h2), j = (int)(i - (size_t)pos * h2);
+        float sn, cs;
+        rope_angle(pos, 2 * j, head_dim, theta, &sn, &cs);
+        tab[i] = make_float2(cs, sn);
+    }
+}
+
+cudaError_t launch_rope_table(float2* tab, int rows, int head_dim, float theta, cudaStream_t s) {
+    if (!tab || rows <= 0 || head_dim <= 0 || head_dim % 2) return cudaErrorInvalidValue;
+    const size_t n = (size_t)rows * (head_dim / 2);
+    const int blocks = (int)std::min<size_t>((n + 255) / 256, 4096);
+    rope_table_kernel<<<blocks, 256, 0, s>>>(tab, rows, head_dim, theta);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_draft_pick(const StepBuffers& b, int j, cudaStream_t s, bool pdl) {

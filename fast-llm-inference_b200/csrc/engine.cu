@@ -134,6 +134,10 @@ GemvParams gemv_base(const Linear& l, const uint8_t* aq, const int* done) {
     return g;
 }
 
+#ifndef FL_ROPE_TABLE
+#define FL_ROPE_TABLE 1
+#endif
+
 // Many static rows (more than two GEMV launches' worth) go through the
 // tcgen05 GEMM (weights read once); the fused RMSNorm prologue then runs as
 // its own quantization pass.
@@ -264,6 +268,8 @@ int run_stack(fl_engine* e, Stack& S, float* x, int M, const int* dyn_M, const i
         g.head_dim = e->hd;
         g.kv_heads = e->Hkv;
         g.theta = e->c.rope_theta;
+        g.rope = e->rope;
+        g.rope_rows = e->rope_rows;
         FL_CHECK(launch_chunks(g, EPI_QKV, M, dyn_M, e->s, pdl));
         AttnParams at = {};
         at.q = e->q;
@@ -883,6 +889,16 @@ static fl_engine_t* engine_create(const fl_model_config_t* cfg, int device, int 
               cudaMemset(e->step_bar, 0, sizeof(unsigned) * 4) == cudaSuccess &&
               cudaMemset(e->attn_cnt, 0, sizeof(int) * attention_scratch_counters(e->H)) == cudaSuccess;
     if (!ok) return fail(set_error(FL_E_NOMEM, "fl_engine_create: device allocation failed"));
+#if FL_ROPE_TABLE
+    // Rotary (cos, sin) per context position and frequency, read by the QKV
+    // epilogues instead of a powf and a sincosf per output pair (same values).
+    e->rope_rows = c.max_seq_len + kMaxTreeCand;
+    if (cudaMalloc(&e->rope, sizeof(float2) * (size_t)e->rope_rows * (e->hd / 2)) != cudaSuccess)
+        return fail(set_error(FL_E_NOMEM, "fl_engine_create: rotary table"));
+    if (launch_rope_table(e->rope, e->rope_rows, e->hd, c.rope_theta, e->s) != cudaSuccess ||
+        cudaStreamSynchronize(e->s) != cudaSuccess)
+        return fail(set_error(FL_E_CUDA, "fl_engine_create: rotary table"));
+#endif
     std::vector<int> io(R + 16);
     for (size_t i = 0; i < io.size(); i++) io[i] = (int)i;
     if (cudaMemcpy(e->iota, io.data(), sizeof(int) * io.size(), cudaMemcpyHostToDevice) != cudaSuccess)
@@ -922,7 +938,7 @@ FL_API void fl_engine_destroy(fl_engine_t* e) {
     for (auto& m : e->medusa) free_linear(m);
     void* bufs[] = {e->embed, e->x, e->x2, e->xq, e->q, e->aq, e->hq, e->logits, e->amax, e->x_v, e->x_d,
                     e->iota, e->tok, e->mask, e->work_arena, e->st, e->st_snap, e->xd0_snap, e->seq, e->out, e->acc,
-                    e->last_feat, e->attn_part, e->attn_cnt, e->step_bar, e->d_phases, e->d_trace,
+                    e->last_feat, e->attn_part, e->attn_cnt, e->rope, e->step_bar, e->d_phases, e->d_trace,
                     e->samp_q, e->samp_p, e->samp_r, e->samp_trace, e->samp_snap, e->samp_m, e->samp_key,
                     e->tp_keys, e->tp_all, e->tp_best, e->tp_recv_ptrs, e->tp_cnt_ptrs, e->tp_seq, e->tp_arrived};
     for (void* p : bufs) cudaFree(p);

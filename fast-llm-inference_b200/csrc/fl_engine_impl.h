@@ -119,6 +119,8 @@ struct fl_engine {
     bool step_layout = false;      // weights in 128-byte panels for the tcgen05 step kernel
     float* attn_part = nullptr;   // decode attention split-K scratch
     int* attn_cnt = nullptr;      // per-head arrival counters (zero at rest)
+    float2* rope = nullptr;       // rotary (cos, sin) table [rope_rows][hd / 2]
+    int rope_rows = 0;
     int graph_kernels = 0;        // kernel nodes in the step graph
     long long last_launches = 0;  // kernels launched by the last decode
     const void* bound_draft = nullptr;

@@ -22,6 +22,13 @@ __device__ __forceinline__ int row_slot(const GemvParams& p, int r) {
     return b * p.seq_slots + p.slot_base[b * p.seq_state] + (r - b * p.seq_rows);
 }
 
+// sin and cos of the rotary angle of position pos and even dimension ii:
+// pos x theta^(-ii / head_dim) (inference.c:165-173).
+__device__ __forceinline__ void rope_angle(int pos, int ii, int head_dim, float theta, float* sn, float* cs) {
+    const float freq = __fdiv_rn(1.0f, powf(theta, __fdiv_rn((float)ii, (float)head_dim)));
+    sincosf(__fmul_rn((float)pos, freq), sn, cs);
+}
+
 // Epilogue of one weight-row pair (n0, n0 + 1) for activation row r.
 template <int EPI>
 __device__ __forceinline__ void pair_epilogue(const GemvParams& p, int r, int n0, bool has1, float y0, float y1,
@@ -47,10 +54,15 @@ __device__ __forceinline__ void pair_epilogue(const GemvParams& p, int r, int n0
         if (n0 < qkd) {
             // inference.c:165-173 adjacent-pair rotation at position pos[r]
             const int ii = (n0 < p.q_dim ? n0 : n0 - p.q_dim) % p.head_dim;
-            const float freq = __fdiv_rn(1.0f, powf(p.theta, __fdiv_rn((float)ii, (float)p.head_dim)));
-            const float ang = __fmul_rn((float)row_pos(p, r), freq);
+            const int pos = row_pos(p, r);
             float sn, cs;
-            sincosf(ang, &sn, &cs);
+            if (p.rope && pos < p.rope_rows) {
+                const float2 t = p.rope[(size_t)pos * (p.head_dim >> 1) + (ii >> 1)];
+                cs = t.x;
+                sn = t.y;
+            } else {
+                rope_angle(pos, ii, p.head_dim, p.theta, &sn, &cs);
+            }
             v0 = __fsub_rn(__fmul_rn(y0, cs), __fmul_rn(y1, sn));
             v1 = __fadd_rn(__fmul_rn(y0, sn), __fmul_rn(y1, cs));
         }

@@ -61,6 +61,11 @@ struct GemvParams {
     int seq_rows, seq_state, seq_slots;
     int q_dim, kv_dim, head_dim, kv_heads;
     float theta;
+    // Optional rotary table [rope_rows][head_dim / 2] of (cos, sin) of
+    // position x frequency (launch_rope_table; the values the epilogue would
+    // compute); rows at or past rope_rows are computed in the epilogue.
+    const float2* rope;
+    int rope_rows;
     // EPI_SWIGLU
     uint8_t* hq;              // [rows, F]
     int F;
@@ -176,6 +181,9 @@ struct AttnParams {
     int* counters;
 };
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl);
+// Fills tab[pos][i] = (cos, sin) of pos x theta^(-2i / head_dim) for pos <
+// rows, i < head_dim / 2, with the epilogue's own arithmetic (decode_ops.cu).
+cudaError_t launch_rope_table(float2* tab, int rows, int head_dim, float theta, cudaStream_t s);
 size_t attention_scratch_floats(int heads, int head_dim, int max_ctx);
 size_t attention_scratch_counters(int heads);
 
