@@ -30,6 +30,27 @@ __device__ __forceinline__ void pdl_wait() {
 // saturation to int16 and to [0, 255] -- net effect: clamp to [0, 255] with
 // out-of-range values mapping to 0.
 // ---------------------------------------------------------------------------
+// y / 127 rounded to nearest even, as the reference's epilogue divides
+// (dequantized_tensor.c:204-247), without a division instruction sequence:
+// q0 = RN(y * r) with r = RN(1 / 127), one fused residual correction
+// (Markstein's method for division by a constant: e = y - q0 * 127 is exact,
+// q = RN(q0 + e * r)) and y's sign on a zero result. Equal to the correctly
+// rounded quotient for every finite float y (all 2^32 inputs checked on the
+// host; tests/test_div127.py checks whole binades).
+#ifndef FL_DIV127_FMA
+#define FL_DIV127_FMA 1
+#endif
+__device__ __forceinline__ float div127(float y) {
+#if FL_DIV127_FMA
+    const float r = 1.0f / 127.0f;
+    const float q0 = __fmul_rn(y, r);
+    const float e = __fmaf_rn(-q0, 127.0f, y);
+    return copysignf(__fmaf_rn(e, r, q0), y);
+#else
+    return __fdiv_rn(y, 127.0f);
+#endif
+}
+
 __device__ __forceinline__ uint32_t quant_u8(float x) {
     float v = __fmaf_rn(x, 127.0f, 128.0f);
     if (!(v > -2147483648.0f && v < 2147483648.0f)) return 0u;

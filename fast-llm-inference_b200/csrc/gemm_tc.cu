@@ -447,7 +447,7 @@ __global__ void __launch_bounds__(gemm_threads(BN), 1)
 #pragma unroll
             for (int c = 0; c < kCols; c++) {
                 const uint32_t bits = (c & 1) ? (uint32_t)(acc2[c >> 1] >> 32) : (uint32_t)acc2[c >> 1];
-                const float y = __fdiv_rn(__uint_as_float(bits), 127.0f);
+                const float y = div127(__uint_as_float(bits));
                 const float y1 = __shfl_xor_sync(0xffffffffu, y, 1);
                 const int m = m0 + c0 + c;
                 if ((lane & 1) == 0 && live && m < geo.M) pair_epilogue<EPI>(g, m, n, n + 1 < N, y, y1, nullptr);

@@ -217,8 +217,8 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const GemvParams p) {
                 t0 = __fmul_rn(__fmul_rn((float)s0, p.srow[active ? n0 : 0]), 1.0f / 2032.0f);
                 t1 = __fmul_rn(__fmul_rn((float)s1, p.srow[active ? n1 : 0]), 1.0f / 2032.0f);
             } else {
-                t0 = __fdiv_rn(warp_sum(f0[m]), 127.0f);
-                t1 = __fdiv_rn(warp_sum(f1[m]), 127.0f);
+                t0 = div127(warp_sum(f0[m]));
+                t1 = div127(warp_sum(f1[m]));
             }
             if (m == m_own) y_own = sel ? t1 : t0;
             if (m == lane) { ypair0 = t0; ypair1 = t1; }

@@ -322,8 +322,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const Ge
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty_bar[sl]);
             if (pan == npan - 1) {
-                const float t0 = __fdiv_rn(warp_sum(f0), 127.0f);
-                const float t1 = __fdiv_rn(warp_sum(f1), 127.0f);
+                const float t0 = div127(warp_sum(f0));
+                const float t1 = div127(warp_sum(f1));
                 f0 = f1 = 0.0f;
                 if (lane == 0 && lr < rows && rows_m > 0)
                     pair_epi_any<EPI>(epi, p, p.row0, r + lr, lr + 1 < rows, t0, t1, best_s);
@@ -484,8 +484,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_tma_kernel(const Ge
                             y0 += red[buf][w][l0][q0];
                             y1 += red[buf][w][l1][q1];
                         }
-                        pair_epi_any<EPI>(epi, p, p.row0 + m, r + 2 * pr, 2 * pr + 1 < rows, __fdiv_rn(y0, 127.0f),
-                                           __fdiv_rn(y1, 127.0f), best_s);
+                        pair_epi_any<EPI>(epi, p, p.row0 + m, r + 2 * pr, 2 * pr + 1 < rows, div127(y0),
+                                           div127(y1), best_s);
                     }
                 }
                 buf ^= 1;

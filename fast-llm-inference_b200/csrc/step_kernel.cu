@@ -380,8 +380,8 @@ __device__ void gemv_consume(const GemvParams& p, int epi, bool skip, const Ring
                 for (int h = 0; h < 2; h++) {
                     const int lr = 16 * grp + 8 * h + 2 * t;  // even row of the pair within the tile
                     if (lr < rows)
-                        pair_epi(p, epi, g, r + lr, lr + 1 < rows, __fdiv_rn(acc[2 * h], 127.0f),
-                                 __fdiv_rn(acc[2 * h + 1], 127.0f), best_s, es, geo.row0, nr);
+                        pair_epi(p, epi, g, r + lr, lr + 1 < rows, div127(acc[2 * h]),
+                                 div127(acc[2 * h + 1]), best_s, es, geo.row0, nr);
                 }
             }
             if (wpr > 1) cbar();  // red is free again
