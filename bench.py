@@ -899,7 +899,9 @@ def main():
                      "accepted_hist": np.bincount(acc_cat, minlength=a.k + 1).tolist(),
                      "step_us": step_us, "step_bytes": step_bytes(a.k, ctx_mid, wbytes), "step_gbs": step_gbs,
                      "step_frac_of_hbm": step_gbs / peak},
-            "verify_step_us_est": 32 * (us_gu + us_dn + us_qkv + us_o),
+            # the 32 layers' four verify GEMVs, each timed in a chain of its own
+            # launches (inside the step they cost more: --workload step-breakdown)
+            "verify_gemvs_us_isolated": 32 * (us_gu + us_dn + us_qkv + us_o),
             "roofline": {"bound": "hbm", "achieved": kern_gbs, "peak": peak, "unit": "GB/s",
                          "frac": kern_gbs / peak,
                          "traffic": None if eng.step_kernel() or a.w4 else profiled_traffic(
